@@ -1,0 +1,474 @@
+"""Benchmark of the token-mixing hot path on B200 (BASELINE config 5 by default).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+Default workload "qwen35_hybrid_decode": one decode step of a Qwen3.5-like
+24-layer token-mixer stack -- 18 Gated DeltaNet layers (16 heads, d_k = d_v = 128, fp32 state) and 6
+gated full-attention layers (8 Q / 2 KV heads, head_dim 256, bf16 KV cache, sigmoid output gate and
+SubLN) in the engine's order (3 DeltaNet, 1 attention) x 6 -- for a decode batch of 256 sequences at
+context 32768 (every sequence appends its token at row 32767 and attends over all 32768 rows).
+Inputs are seeded synthetic tensors with the config's shapes and distributions (no model files).
+Under torchrun the batch is split across ranks (256/N sequences each): fixed total work, "strong".
+
+One JSON line on rank 0:
+  value        tokens/s of the whole job, device-timed (CUDA events, max over ranks), inputs resident
+  e2e          the same metric through the host-pointer C ABI calls (pinned host inputs copied in and
+               outputs read back every layer of every step), wall-clock, max over ranks
+  roofline     the dominant kernel (decode attention) against the measured HBM copy bandwidth
+  cpu_baseline the reference's own C code on this box's host cores (rank 0, N=1), bounded sample
+`--impl reference` times the reference's C code alone on the same workload (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# ---------------------------------------------------------------------------------------------------
+# workload constants
+# ---------------------------------------------------------------------------------------------------
+N_LAYERS = 24
+LAYER_TYPES = ["D", "D", "D", "A"] * 6  # Qwen3.5 layout: full attention every 4th layer
+DN_H, DN_D = 16, 128
+AT_HQ, AT_HKV, AT_D = 8, 2, 256
+CTX = 32768
+BATCH = 256
+METRIC = "attn+DeltaNet tokens/s (24-layer Qwen3.5-like token-mixer decode step)"
+UNIT = "tokens/s"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------------
+
+class CudaArray:
+    """A raw device allocation presented to torch through __cuda_array_interface__ (no copy)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": typestr,
+                                         "version": 3, "strides": None}
+
+
+class Hybrid:
+    """Device-resident state and per-layer inputs of the config-5 decode step for `B` sequences."""
+
+    def __init__(self, pkg, ctx, torch, B, seed):
+        self.pkg, self.ctx, self.torch, self.B = pkg, ctx, torch, B
+        dev = torch.device("cuda", torch.cuda.current_device())
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        n_att = LAYER_TYPES.count("A")
+        n_dn = LAYER_TYPES.count("D")
+        self.kv = pkg.KVCache(ctx, n_att, B, CTX, AT_HKV, AT_D, pkg.BF16)
+        self.dn = pkg.DeltaState(ctx, n_dn, B, DN_H, DN_D, DN_D)
+        # KV cache ~ N(0,1) bf16, S ~ N(0, 0.02) fp32, filled in place through the library's pointers
+        for l in range(n_att):
+            for p in self.kv.layer_ptrs(l):
+                t = torch.as_tensor(CudaArray(p, (B * CTX * AT_HKV * AT_D,), "<i2"), device=dev)
+                t.view(torch.bfloat16).normal_(generator=gen)
+        for l in range(n_dn):
+            s, _ = self.dn.layer_ptrs(l)
+            torch.as_tensor(CudaArray(s, (B * DN_H * DN_D * DN_D,), "<f4"), device=dev).normal_(0, 0.02,
+                                                                                              generator=gen)
+        # per-layer inputs, distributions of BASELINE configs 3 / 5
+        def nrm(*shape):
+            return torch.randn(*shape, device=dev, generator=gen)
+        self.dn_in = []
+        for l in range(n_dn):
+            qk = nrm(2, B, DN_H, DN_D)
+            qk = qk / torch.sqrt((qk * qk).sum(-1, keepdim=True) + 1e-12)
+            self.dn_in.append(dict(q=qk[0].contiguous(), k=qk[1].contiguous(), v=nrm(B, DN_H * DN_D),
+                                   beta=torch.sigmoid(nrm(B, DN_H)),
+                                   g=-torch.nn.functional.softplus(nrm(B, DN_H))))
+        self.at_in = []
+        for l in range(n_att):
+            self.at_in.append(dict(q=nrm(B, AT_HQ * AT_D), gate=nrm(B, AT_HQ * AT_D), k=nrm(B, AT_HKV * AT_D),
+                                   v=nrm(B, AT_HKV * AT_D)))
+        self.sub_norm = 1.0 + 0.1 * nrm(AT_HQ * AT_D)
+        self.pos = torch.full((B,), CTX - 1, dtype=torch.int32, device=dev)
+        self.out = torch.empty(B, AT_HQ * AT_D, device=dev)
+        self.dn_out = torch.empty(B, DN_H * DN_D, device=dev)
+        self.scale = 1.0 / math.sqrt(AT_D)
+        self.q_scale = 1.0 / math.sqrt(DN_D)
+
+    def step(self, att_events=None):
+        """One decode step through the `_dev` entry points, asynchronously on the context's stream."""
+        a = d = 0
+        for typ in LAYER_TYPES:
+            if typ == "D":
+                x = self.dn_in[d]
+                self.dn.step_dev(d, x["q"].data_ptr(), x["k"].data_ptr(), x["v"].data_ptr(), x["beta"].data_ptr(),
+                                 x["g"].data_ptr(), self.q_scale, self.dn_out.data_ptr())
+                d += 1
+            else:
+                x = self.at_in[a]
+                self.kv.append_dev(a, self.pos.data_ptr(), x["k"].data_ptr(), x["v"].data_ptr())
+                if att_events is not None:
+                    att_events[a][0].record()
+                self.kv.attend_decode_dev(a, x["q"].data_ptr(), self.pos.data_ptr(), CTX - 1, AT_HQ, self.scale,
+                                          self.out.data_ptr(), gate_dev=x["gate"].data_ptr(),
+                                          subln=self.pkg.SUBLN_WEIGHT, sub_norm_dev=self.sub_norm.data_ptr())
+                if att_events is not None:
+                    att_events[a][1].record()
+                a += 1
+
+
+class HybridHost:
+    """Pinned host inputs / outputs for the end-to-end (host-pointer ABI) measurement."""
+
+    def __init__(self, torch, B, seed):
+        rng = np.random.default_rng(seed)
+
+        def pinned(a):
+            t = torch.from_numpy(np.ascontiguousarray(a, np.float32)).pin_memory()
+            return t, t.numpy()
+
+        qk = rng.standard_normal((2, B, DN_H, DN_D)).astype(np.float32)
+        qk /= np.sqrt((qk * qk).sum(-1, keepdims=True) + 1e-12)
+        self._keep = []
+        arrs = dict(q=qk[0].reshape(B, -1), k=qk[1].reshape(B, -1),
+                    v=rng.standard_normal((B, DN_H * DN_D)),
+                    beta=1 / (1 + np.exp(-rng.standard_normal((B, DN_H)))),
+                    g=-np.log1p(np.exp(rng.standard_normal((B, DN_H)))),
+                    aq=rng.standard_normal((B, AT_HQ * AT_D)), gate=rng.standard_normal((B, AT_HQ * AT_D)),
+                    ak=rng.standard_normal((B, AT_HKV * AT_D)), av=rng.standard_normal((B, AT_HKV * AT_D)),
+                    sub_norm=1 + 0.1 * rng.standard_normal(AT_HQ * AT_D))
+        self.h = {}
+        for n, a in arrs.items():
+            t, v = pinned(a)
+            self._keep.append(t)
+            self.h[n] = v
+        tpos = torch.from_numpy(np.full(B, CTX - 1, np.int32)).pin_memory()
+        self._keep.append(tpos)
+        self.pos = tpos.numpy()
+        self.h2d = 0
+        self.d2h = 0
+        for typ in LAYER_TYPES:
+            if typ == "D":
+                self.h2d += sum(self.h[n].nbytes for n in ("q", "k", "v", "beta", "g"))
+                self.d2h += B * DN_H * DN_D * 4
+            else:
+                self.h2d += sum(self.h[n].nbytes for n in ("ak", "av", "aq", "gate", "sub_norm")) + 2 * self.pos.nbytes
+                self.d2h += B * AT_HQ * AT_D * 4
+
+    def step(self, hy: Hybrid):
+        a = d = 0
+        h = self.h
+        for typ in LAYER_TYPES:
+            if typ == "D":
+                hy.dn.step(d, h["q"], h["k"], h["v"], h["beta"], h["g"], hy.q_scale)
+                d += 1
+            else:
+                hy.kv.append(a, self.pos, h["ak"], h["av"])
+                hy.kv.attend_decode(a, h["aq"], self.pos, AT_HQ, hy.scale, gate=h["gate"],
+                                    subln=hy.pkg.SUBLN_WEIGHT, sub_norm=h["sub_norm"])
+                a += 1
+
+
+def attn_layer_bytes(B):
+    """Algorithmic HBM bytes of one decode-attention launch: the K and V rows read once, q and gate read,
+    out written (fp32)."""
+    kv = 2 * B * CTX * AT_HKV * AT_D * 2
+    io = 3 * B * AT_HQ * AT_D * 4
+    return kv + io
+
+
+def deltanet_layer_bytes(B):
+    return 2 * B * DN_H * DN_D * DN_D * 4 + 4 * B * DN_H * DN_D * 4 + 2 * B * DN_H * 4
+
+
+def run_ours(args, torch, dist, rank, world, local_rank):
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    torch.cuda.set_device(local_rank)
+    B = BATCH // world
+    ctx = pkg.Context(local_rank)
+    stream = torch.cuda.current_stream()
+    ctx.set_stream(stream.cuda_stream)
+    hy = Hybrid(pkg, ctx, torch, B, seed=1234 + rank)
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        hy.step()
+    torch.cuda.synchronize()
+    ctx.synchronize()
+
+    n_att = LAYER_TYPES.count("A")
+    att_ev = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(n_att)]
+              for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local_rank)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    launches0 = ctx.launch_count
+    start.record()
+    for s in range(args.steps):
+        hy.step(att_ev[s])
+    end.record()
+    torch.cuda.synchronize()
+    launches = ctx.launch_count - launches0
+    clk = clocks.stop()
+    ctx.synchronize()  # surfaces any device-side error word
+    if dist:
+        dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    att_ms = float(np.mean([e[0].elapsed_time(e[1]) for st in att_ev for e in st]))
+    ms_all = ms
+    if dist:
+        t = torch.tensor([ms, att_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_all, att_ms = float(t[0]), float(t[1])
+
+    # end to end through the host-pointer ABI (pinned host buffers, H2D + D2H inside every call)
+    ctx.set_stream(None)
+    host = HybridHost(torch, B, seed=99 + rank)
+    host.step(hy)  # warm
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        host.step(hy)
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+
+    if rank != 0:
+        return None
+    hbm, _, src = peaks()
+    bytes_att = attn_layer_bytes(B)
+    achieved = bytes_att / (att_ms * 1e-3) / 1e9
+    step_bytes = n_att * bytes_att + LAYER_TYPES.count("D") * deltanet_layer_bytes(B)
+    line = {
+        "metric": METRIC, "value": BATCH / (ms_all * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_all, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 math; bf16 KV, fp32 DeltaNet state", "data": "synthetic (seeded)",
+        "config": {"workload": "qwen35_hybrid_decode (BASELINE configs[4])", "global_batch": BATCH, "ctx": CTX,
+                   "layers": "18 DeltaNet (16h, d128, fp32 S) + 6 gated attention (8q/2kv, hd256, bf16 KV)",
+                   "per_gpu_batch": B, "parallelism": f"batch-sharded x{world}, no collective",
+                   "l2": "inputs larger than L2 (17.2 GB KV per attention layer, 268 MB S per DeltaNet layer)",
+                   "step_hbm_bytes": step_bytes},
+        "e2e": {"value": BATCH / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": host.h2d, "d2h_bytes_per_step": host.d2h,
+                "path": "host-pointer C ABI (eif_cuda_kv_append / eif_cuda_attend_decode / eif_cuda_deltanet_step)"},
+        "roofline": {"kernel": "decode attention (split-K kernel + chunk combine), one attention layer",
+                     "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": src, "algorithmic_bytes_per_launch": bytes_att, "ms_per_launch": att_ms,
+                     "traffic": None},
+        "step_hbm_frac": step_bytes / (ms_all * 1e-3) / 1e9 / (hbm * world),
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    return line
+
+
+# ---------------------------------------------------------------------------------------------------
+# the reference's C code on the host cores
+# ---------------------------------------------------------------------------------------------------
+
+def cpu_reference(n_seq_rounds, threads=None, per_round_cap_s=None):
+    """Time the reference's own deltanet_core x 18 and fullatt_attend x 6 (fp32 KV at ctx 32768, the only
+    KV dtype of its Qwen3.5 engine) for one decode step of independent sequences, one sequence per host
+    thread (the reference has no batch dimension; a batch is a loop over engine states).
+    Returns (tokens_per_s, cores, kind, sample description)."""
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as orc
+
+    kind = "reference" if orc.ref_available() else "port"
+    ncpu = threads or len(os.sched_getaffinity(0))
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:
+        avail = 64 << 30
+    kv_bytes = 6 * 2 * CTX * AT_HKV * AT_D * 4
+    workers = max(1, min(ncpu, int(avail * 0.5 // (kv_bytes + (20 << 20)))))
+    rng = np.random.default_rng(77)
+    block = rng.standard_normal((4096, AT_HKV * AT_D)).astype(np.float32)
+    conv_dim = 3 * DN_H * DN_D
+    w = dict(conv_w=(rng.standard_normal((conv_dim, 4)) * 0.5).astype(np.float32),
+             dt_bias=rng.standard_normal(DN_H).astype(np.float32),
+             A_log=(0.5 * rng.standard_normal(DN_H)).astype(np.float32),
+             norm_w=(1 + 0.1 * rng.standard_normal(DN_D)).astype(np.float32))
+    x = dict(qkv=rng.standard_normal(conv_dim).astype(np.float32), z=rng.standard_normal(DN_H * DN_D).astype(
+        np.float32), b=rng.standard_normal(DN_H).astype(np.float32), a=rng.standard_normal(DN_H).astype(np.float32),
+             q=rng.standard_normal(AT_HQ * AT_D).astype(np.float32),
+             gate=rng.standard_normal(AT_HQ * AT_D).astype(np.float32),
+             sub_norm=(1 + 0.1 * rng.standard_normal(AT_HQ * AT_D)).astype(np.float32))
+
+    class Seq:
+        def __init__(self):
+            self.kc = [np.tile(block, (CTX // 4096, 1)) for _ in range(6)]
+            self.vc = [np.tile(block[::-1].copy(), (CTX // 4096, 1)) for _ in range(6)]
+            self.S = [(0.02 * block.ravel()[:DN_H * DN_D * DN_D].reshape(DN_H, DN_D, DN_D)).copy() for _ in range(18)]
+            self.conv = [np.zeros((conv_dim, 4), np.float32) for _ in range(18)]
+
+        def step(self):
+            a = d = 0
+            for typ in LAYER_TYPES:
+                if typ == "D":
+                    if kind == "reference":
+                        orc.deltanet_core(x["qkv"], x["z"], x["b"], x["a"], self.conv[d], self.S[d], lib=orc.ref(), **w)
+                    else:
+                        orc.deltanet_core(x["qkv"], x["z"], x["b"], x["a"], self.conv[d], self.S[d], **w)
+                    d += 1
+                else:
+                    if kind == "reference":
+                        orc.ref_fullatt_attend(x["q"], x["gate"], self.kc[a], self.vc[a], x["sub_norm"], 0, CTX - 1,
+                                               AT_HQ, AT_HKV, AT_D)
+                    else:
+                        o = orc.attend_decode(x["q"], self.kc[a], self.vc[a], CTX - 1, AT_HQ, AT_HKV, AT_D,
+                                              1 / 16.0, gate=x["gate"])
+                        orc.subln(o, x["sub_norm"], 2)
+                    a += 1
+
+    if kind == "reference":
+        orc.ref().ref_set_threads(1)
+    seqs = [Seq() for _ in range(workers)]
+    pool = ThreadPoolExecutor(max_workers=workers)
+    list(pool.map(lambda s: s.step(), seqs))  # warm (page in)
+    times = []
+    for _ in range(n_seq_rounds):
+        t0 = time.perf_counter()
+        list(pool.map(lambda s: s.step(), seqs))
+        times.append(time.perf_counter() - t0)
+        if per_round_cap_s and sum(times) > per_round_cap_s:
+            break
+    pool.shutdown()
+    t = float(np.median(times))
+    sample = (f"{workers} sequences x 1 decode step through the 24 mixers at ctx {CTX} (fp32 KV), one sequence "
+              f"per host thread, median of {len(times)} rounds of {t:.3f} s; x{BATCH // workers if workers else 0} "
+              f"rounds would cover the batch of {BATCH}")
+    return workers / t, workers, kind, sample, t
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    warm = max(0, args.warmup)
+    tps, cores, kind, sample, t = cpu_reference(max(1, args.steps) + warm, per_round_cap_s=240)
+    return {"metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": BATCH / tps * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)", "impl": "reference",
+            "config": {"workload": "qwen35_hybrid_decode (BASELINE configs[4])", "global_batch": BATCH, "ctx": CTX,
+                       "kv_dtype": "f32 (the reference's only Qwen3.5 KV dtype)"},
+            "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
+            "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line:
+            print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+        torch.cuda.set_device(local_rank)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist = tdist
+    line = run_ours(args, torch, dist, rank, world, local_rank)
+    if line is not None and world == 1 and not args.no_cpu_baseline:
+        tps, cores, kind, sample, _ = cpu_reference(3, per_round_cap_s=30)
+        line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample}
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

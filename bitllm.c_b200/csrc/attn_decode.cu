@@ -1,0 +1,295 @@
+// attn_decode.cu -- split-K GQA decode attention over the KV cache.
+//
+// Reference: the head loop of fullatt_attend (src/eif_qwen35.c:741-771) and the inline tinyllm
+// decode attention (src/eif_tinyllm.c:555-656): for every query head h (kv head h / (Hq/Hkv)),
+// scores s_t = scale * q.k_t for t <= pos, softmax, o = sum_t p_t v_t; then the Qwen3.5 epilogue
+// o *= sigmoid(gate) and SubLN (src/eif_qwen35.c:773-789).
+//
+// Work split: one unit = (sequence b, kv head); the unit's key range [0, pos[b]] is cut into
+// `nchunk` chunks, one CTA per (chunk, unit).  A CTA serves ALL G = Hq/Hkv query heads of its kv
+// head, so every K/V byte is read from HBM once.  Each CTA leaves an unnormalised partial
+// (running max m, sum l, o[G][D]) in scratch; attn_decode_combine merges the chunks of a sequence
+// with a log-sum-exp rescale, applies the gate and the SubLN of the whole row and writes out.
+//
+// This file holds the SIMT kernel (fp32 or bf16 cache, fp32 arithmetic): lanes own keys for the
+// scores and own head-dim slices for P.V.  It is the exact-parity path for fp32 caches.
+#include <math.h>
+
+#include "internal.h"
+#include "common.cuh"
+
+namespace {
+
+constexpr int kDecodeThreads = 128;
+constexpr int kDecodeWarps = kDecodeThreads / 32;
+
+template <typename KT, int D, int G>
+__global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
+    const KT *__restrict__ Kc, const KT *__restrict__ Vc, const float *__restrict__ q, const int *__restrict__ pos,
+    int max_seq, int Hkv, int chunk, int nchunk, float scale, float *__restrict__ part_o,
+    float2 *__restrict__ part_ml, unsigned *__restrict__ dev_err) {
+    constexpr int DL = D / 32;  // head-dim elements per lane in P.V
+    static_assert(D % 32 == 0 && (DL == 2 || DL == 4 || DL == 8), "head_dim 64/128/256");
+    constexpr int KV_VEC = (sizeof(KT) == 4) ? 4 : 8;  // elements per K load
+
+    const int c = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int Hq = Hkv * G;
+
+    __shared__ float sq[G][D];
+    __shared__ float wm[kDecodeWarps][G], wl[kDecodeWarps][G];
+    __shared__ float wacc[kDecodeWarps][G][D];
+
+    int p = pos[b];
+    if (p < 0 || p >= max_seq) {
+        if (threadIdx.x == 0 && c == 0 && kvh == 0) atomicOr(dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
+        p = -1;  // no keys: the partial is empty and the combine writes zeros
+    }
+    const int L = p + 1;
+    const int t_begin = c * chunk;
+    const int t_end = min(L, t_begin + chunk);
+
+    for (int i = threadIdx.x; i < G * D; i += kDecodeThreads)
+        sq[i / D][i % D] = q[(size_t)b * Hq * D + (size_t)kvh * G * D + i];
+    __syncthreads();
+
+    float m[G], l[G], acc[G][DL];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+#pragma unroll
+        for (int i = 0; i < DL; ++i) acc[h][i] = 0.f;
+    }
+
+    const size_t row_stride = (size_t)Hkv * D;
+    const KT *Kb = Kc + ((size_t)b * max_seq * Hkv + kvh) * D;
+    const KT *Vb = Vc + ((size_t)b * max_seq * Hkv + kvh) * D;
+
+    for (int t0 = t_begin + warp * 32; t0 < t_end; t0 += kDecodeWarps * 32) {
+        const int t = t0 + lane;
+        const bool valid = t < t_end;
+        float s[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) s[h] = 0.f;
+        if (valid) {
+            const KT *kr = Kb + (size_t)t * row_stride;
+#pragma unroll 4
+            for (int d = 0; d < D; d += KV_VEC) {
+                float kv[KV_VEC];
+                KvLoad<KT, KV_VEC>::load(kr + d, kv);
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+#pragma unroll
+                    for (int j = 0; j < KV_VEC; ++j) s[h] += sq[h][d + j] * kv[j];
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            const float sc = valid ? s[h] * scale : -INFINITY;
+            const float m_new = fmaxf(m[h], warp_max(sc));
+            const float corr = expf(m[h] - m_new);  // 0 on the first block (m = -inf)
+            const float pr = valid ? expf(sc - m_new) : 0.f;
+            l[h] = l[h] * corr + warp_sum(pr);
+#pragma unroll
+            for (int i = 0; i < DL; ++i) acc[h][i] *= corr;
+            m[h] = m_new;
+            s[h] = pr;
+        }
+        const int nvalid = min(32, t_end - t0);
+        for (int j = 0; j < nvalid; ++j) {
+            float vv[DL];
+            KvLoad<KT, DL>::load(Vb + (size_t)(t0 + j) * row_stride + lane * DL, vv);
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                const float pj = __shfl_sync(0xffffffffu, s[h], j);
+#pragma unroll
+                for (int i = 0; i < DL; ++i) acc[h][i] += pj * vv[i];
+            }
+        }
+    }
+
+    // merge the warps of the CTA
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        if (lane == 0) {
+            wm[warp][h] = m[h];
+            wl[warp][h] = l[h];
+        }
+#pragma unroll
+        for (int i = 0; i < DL; ++i) wacc[warp][h][lane * DL + i] = acc[h][i];
+    }
+    __syncthreads();
+    const size_t unit = (size_t)b * Hkv + kvh;
+    for (int i = threadIdx.x; i < G * D; i += kDecodeThreads) {
+        const int h = i / D, d = i % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kDecodeWarps; ++w) M = fmaxf(M, wm[w][h]);
+        float O = 0.f, Ls = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kDecodeWarps; ++w) {
+                const float f = expf(wm[w][h] - M);
+                O += wacc[w][h][d] * f;
+                Ls += wl[w][h] * f;
+            }
+        }
+        part_o[((unit * nchunk + c) * G + h) * D + d] = O;
+        if (d == 0) part_ml[(unit * nchunk + c) * G + h] = make_float2(M, Ls);
+    }
+}
+
+// One CTA per sequence: merge the chunk partials of every head, gate, SubLN over the whole row.
+__global__ void __launch_bounds__(256) attn_decode_combine_kernel(
+    const float *__restrict__ part_o, const float2 *__restrict__ part_ml, int Hq, int Hkv, int D, int nchunk,
+    const float *__restrict__ gate, int subln, const float *__restrict__ sub_norm, float *__restrict__ out) {
+    extern __shared__ float smem[];
+    const int b = blockIdx.x;
+    const int G = Hq / Hkv;
+    const int row = Hq * D;
+    float *w = smem;             // [Hq][nchunk] chunk weights e^{m_c - M} / L
+    float *rowbuf = smem + Hq * nchunk;  // [Hq*D]
+    __shared__ float red[32];
+
+    for (int hc = threadIdx.x; hc < Hq; hc += blockDim.x) {
+        const int kvh = hc / G, g = hc % G;
+        const size_t base = ((size_t)b * Hkv + kvh) * nchunk;
+        float M = -INFINITY;
+        for (int c = 0; c < nchunk; ++c) M = fmaxf(M, part_ml[(base + c) * G + g].x);
+        float Ls = 0.f;
+        if (M != -INFINITY)
+            for (int c = 0; c < nchunk; ++c) {
+                const float2 ml = part_ml[(base + c) * G + g];
+                Ls += ml.y * expf(ml.x - M);
+            }
+        for (int c = 0; c < nchunk; ++c) {
+            const float2 ml = part_ml[(base + c) * G + g];
+            w[hc * nchunk + c] = (M == -INFINITY || Ls == 0.f) ? 0.f : expf(ml.x - M) / Ls;
+        }
+    }
+    __syncthreads();
+
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < row; i += blockDim.x) {
+        const int h = i / D, d = i % D;
+        const int kvh = h / G, g = h % G;
+        const size_t base = ((size_t)b * Hkv + kvh) * nchunk;
+        float o = 0.f;
+        for (int c = 0; c < nchunk; ++c) o += part_o[((base + c) * G + g) * D + d] * w[h * nchunk + c];
+        if (gate) o *= 1.0f / (1.0f + expf(-gate[(size_t)b * row + i]));
+        rowbuf[i] = o;
+        ss += o * o;
+    }
+    if (subln != EIF_CUDA_SUBLN_NONE) {
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+            t = warp_sum(t);
+            if (threadIdx.x == 0) red[0] = t;
+        }
+        __syncthreads();
+        const float inv = 1.0f / sqrtf(red[0] / row + 1e-6f);
+        for (int i = threadIdx.x; i < row; i += blockDim.x) {
+            float o = rowbuf[i] * inv;
+            if (subln == EIF_CUDA_SUBLN_WEIGHT) o *= sub_norm[i];
+            out[(size_t)b * row + i] = o;
+        }
+    } else {
+        for (int i = threadIdx.x; i < row; i += blockDim.x) out[(size_t)b * row + i] = rowbuf[i];
+    }
+}
+
+struct Split {
+    int nchunk, chunk;
+};
+
+Split choose_split(const DecodeArgs &a, int sm_count) {
+    const int units = a.B * a.Hkv;
+    const int L = a.max_len > 0 ? a.max_len : 1;
+    // aim at >= 4 CTAs per SM, chunks of at least 64 keys
+    int want = (4 * sm_count + units - 1) / units;
+    int max_chunks = (L + 63) / 64;
+    int nchunk = want < max_chunks ? want : max_chunks;
+    if (nchunk < 1) nchunk = 1;
+    int chunk = (L + nchunk - 1) / nchunk;
+    nchunk = (L + chunk - 1) / chunk;
+    return {nchunk, chunk};
+}
+
+template <typename KT, int D, int G>
+cudaError_t launch_simt(cudaStream_t st, const DecodeArgs &a, const Split &sp, float *part_o, float2 *part_ml) {
+    dim3 grid(sp.nchunk, a.Hkv, a.B);
+    attn_decode_simt_kernel<KT, D, G><<<grid, kDecodeThreads, 0, st>>>(
+        static_cast<const KT *>(a.K), static_cast<const KT *>(a.V), a.q, a.pos, a.max_seq, a.Hkv, sp.chunk,
+        sp.nchunk, a.scale, part_o, part_ml, a.dev_err);
+    return cudaGetLastError();
+}
+
+template <typename KT, int D>
+cudaError_t dispatch_g(cudaStream_t st, const DecodeArgs &a, const Split &sp, float *po, float2 *pml, bool *ok) {
+    switch (a.Hq / a.Hkv) {
+        case 1: return launch_simt<KT, D, 1>(st, a, sp, po, pml);
+        case 2: return launch_simt<KT, D, 2>(st, a, sp, po, pml);
+        case 3: return launch_simt<KT, D, 3>(st, a, sp, po, pml);
+        case 4: return launch_simt<KT, D, 4>(st, a, sp, po, pml);
+        case 5: return launch_simt<KT, D, 5>(st, a, sp, po, pml);
+        case 6: return launch_simt<KT, D, 6>(st, a, sp, po, pml);
+        case 7: return launch_simt<KT, D, 7>(st, a, sp, po, pml);
+        case 8: return launch_simt<KT, D, 8>(st, a, sp, po, pml);
+        default: *ok = false; return cudaSuccess;
+    }
+}
+
+template <typename KT>
+cudaError_t dispatch_d(cudaStream_t st, const DecodeArgs &a, const Split &sp, float *po, float2 *pml, bool *ok) {
+    switch (a.D) {
+        case 64: return dispatch_g<KT, 64>(st, a, sp, po, pml, ok);
+        case 128: return dispatch_g<KT, 128>(st, a, sp, po, pml, ok);
+        case 256: return dispatch_g<KT, 256>(st, a, sp, po, pml, ok);
+        default: *ok = false; return cudaSuccess;
+    }
+}
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace
+
+size_t decode_workspace_bytes(const DecodeArgs &a, int sm_count) {
+    const Split sp = choose_split(a, sm_count);
+    const size_t units = (size_t)a.B * a.Hkv;
+    const int G = a.Hq / a.Hkv;
+    return align256(units * sp.nchunk * G * a.D * sizeof(float)) + align256(units * sp.nchunk * G * sizeof(float2));
+}
+
+cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws, size_t ws_bytes, int sm_count,
+                                 bool *supported, int *n_launches) {
+    *supported = true;
+    *n_launches = 0;
+    const Split sp = choose_split(a, sm_count);
+    const size_t units = (size_t)a.B * a.Hkv;
+    const int G = a.Hq / a.Hkv;
+    const size_t o_bytes = align256(units * sp.nchunk * G * a.D * sizeof(float));
+    if (o_bytes + align256(units * sp.nchunk * G * sizeof(float2)) > ws_bytes) return cudaErrorInvalidValue;
+    float *part_o = static_cast<float *>(ws);
+    float2 *part_ml = reinterpret_cast<float2 *>(static_cast<char *>(ws) + o_bytes);
+    cudaError_t e;
+    if (a.dtype == EIF_CUDA_F32)
+        e = dispatch_d<float>(st, a, sp, part_o, part_ml, supported);
+    else
+        e = dispatch_d<__nv_bfloat16>(st, a, sp, part_o, part_ml, supported);
+    if (!*supported || e != cudaSuccess) return e;
+    ++*n_launches;
+    const size_t smem = ((size_t)a.Hq * sp.nchunk + (size_t)a.Hq * a.D) * sizeof(float);
+    if (smem > 48 * 1024) {
+        e = cudaFuncSetAttribute(attn_decode_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    attn_decode_combine_kernel<<<a.B, 256, smem, st>>>(part_o, part_ml, a.Hq, a.Hkv, a.D, sp.nchunk, a.gate,
+                                                         a.subln, a.sub_norm, a.out);
+    ++*n_launches;
+    return cudaGetLastError();
+}

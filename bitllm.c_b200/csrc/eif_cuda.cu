@@ -1,0 +1,649 @@
+// eif_cuda.cu -- the C ABI of include/eif_cuda.h: contexts, device mirrors of the engine's KV cache
+// and DeltaNet state, argument checking, host<->device staging and kernel dispatch.
+//
+// Every entry point validates its arguments on the host before anything is launched and returns an
+// eif_status_t (include/eif_status.h:8-19 in bitllm.c); there is no CPU fallback.  Host-pointer
+// entry points wait with a deadline (EIF_STATUS_TIMEOUT) instead of blocking forever.
+#include <errno.h>
+#include <sched.h>
+#include <stdarg.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+#include <unistd.h>
+
+#include <algorithm>
+
+#include "internal.h"
+
+#define EIF_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+eif_status_t fail(eif_cuda_ctx_t *ctx, eif_status_t st, const char *fmt, ...) {
+    if (ctx) {
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(ctx->err, sizeof ctx->err, fmt, ap);
+        va_end(ap);
+    }
+    return st;
+}
+
+eif_status_t cuda_fail(eif_cuda_ctx_t *ctx, cudaError_t e, const char *what) {
+    const eif_status_t st = (e == cudaErrorMemoryAllocation) ? EIF_STATUS_OUT_OF_MEMORY : EIF_STATUS_ERROR;
+    return fail(ctx, st, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(call)                                                      \
+    do {                                                              \
+        cudaError_t _e = (call);                                      \
+        if (_e != cudaSuccess) return cuda_fail(ctx, _e, #call);      \
+    } while (0)
+
+bool no_cuda_env() {
+    const char *e = getenv("BITLLM_NO_CUDA");
+    return e && *e && strcmp(e, "0") != 0;
+}
+
+// Makes ctx->device current for the scope and restores the caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(const eif_cuda_ctx_t *ctx) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != ctx->device) ok = cudaSetDevice(ctx->device) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+double now_ms() {
+    timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec * 1e3 + ts.tv_nsec * 1e-6;
+}
+
+size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Grow a device buffer; waits for the stream first because queued work may still use the old one.
+eif_status_t ensure_buffer(eif_cuda_ctx_t *ctx, void **buf, size_t *cap, size_t bytes) {
+    if (bytes <= *cap) return EIF_STATUS_OK;
+    CK(cudaStreamSynchronize(ctx->stream));
+    if (*buf) CK(cudaFree(*buf));
+    *buf = nullptr;
+    *cap = 0;
+    const size_t want = std::max(bytes, (size_t)1 << 20);
+    CK(cudaMalloc(buf, want));
+    *cap = want;
+    return EIF_STATUS_OK;
+}
+
+// Wait for the context's stream with the deadline, then report any device-side error word.
+eif_status_t wait_stream(eif_cuda_ctx_t *ctx) {
+    *ctx->host_err = 0;
+    cudaError_t e = cudaMemcpyAsync(ctx->host_err, ctx->dev_err, sizeof(unsigned), cudaMemcpyDeviceToHost,
+                                    ctx->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(ctx->done, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "queue completion event");
+    const double t0 = now_ms();
+    int spins = 0;
+    for (;;) {
+        e = cudaEventQuery(ctx->done);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) return cuda_fail(ctx, e, "device work failed");
+        if (ctx->timeout_ms > 0 && now_ms() - t0 > ctx->timeout_ms)
+            return fail(ctx, EIF_STATUS_TIMEOUT, "device work did not finish within %d ms", ctx->timeout_ms);
+        if (++spins < 2000)
+            sched_yield();
+        else
+            usleep(50);
+    }
+    const unsigned derr = *ctx->host_err;
+    if (derr) {
+        CK(cudaMemsetAsync(ctx->dev_err, 0, sizeof(unsigned), ctx->stream));
+        if (derr & EIF_DEVERR_POS_RANGE)
+            return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "a kernel saw pos outside [0, max_seq_len)");
+        if (derr & EIF_DEVERR_WAIT_LIMIT)
+            return fail(ctx, EIF_STATUS_TIMEOUT, "a kernel pipeline wait ran out of iterations");
+        return fail(ctx, EIF_STATUS_INTERNAL_ERROR, "device error word 0x%x", derr);
+    }
+    return EIF_STATUS_OK;
+}
+
+// Carve consecutive 256-byte aligned slices out of the staging buffer.
+struct Carver {
+    size_t off = 0;
+    size_t take(size_t bytes) {
+        const size_t o = off;
+        off += a256(bytes);
+        return o;
+    }
+};
+
+}  // namespace
+
+// =================================================================================================
+// Context
+// =================================================================================================
+
+EIF_API int eif_cuda_device_count(void) {
+    if (no_cuda_env()) return 0;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+EIF_API eif_status_t eif_cuda_init(eif_cuda_ctx_t **out, int device) {
+    if (!out) return EIF_STATUS_INVALID_ARGUMENT;
+    *out = nullptr;
+    if (no_cuda_env()) return EIF_STATUS_NOT_SUPPORTED;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return EIF_STATUS_NOT_SUPPORTED;
+    }
+    if (device < 0 || device >= n) return EIF_STATUS_NOT_SUPPORTED;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return EIF_STATUS_NOT_SUPPORTED;
+    if (prop.major != 10 || prop.minor != 0) return EIF_STATUS_NOT_SUPPORTED;  // built for sm_100a only
+
+    eif_cuda_ctx_t *ctx = new eif_cuda_ctx_t();
+    ctx->device = device;
+    ctx->sm_count = prop.multiProcessorCount;
+    ctx->cc_major = prop.major;
+    ctx->cc_minor = prop.minor;
+    DeviceGuard g(ctx);
+    cudaError_t e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->dev_err, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(ctx->dev_err, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMallocHost(&ctx->host_err, sizeof(unsigned));
+    if (e != cudaSuccess) {
+        eif_cuda_free(ctx);
+        return e == cudaErrorMemoryAllocation ? EIF_STATUS_OUT_OF_MEMORY : EIF_STATUS_ERROR;
+    }
+    ctx->stream = ctx->own_stream;
+    *out = ctx;
+    return EIF_STATUS_OK;
+}
+
+EIF_API void eif_cuda_free(eif_cuda_ctx_t *ctx) {
+    if (!ctx) return;
+    {
+        DeviceGuard g(ctx);
+        if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
+        if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
+        if (ctx->ws) cudaFree(ctx->ws);
+        if (ctx->stage) cudaFree(ctx->stage);
+        if (ctx->dev_err) cudaFree(ctx->dev_err);
+        if (ctx->host_err) cudaFreeHost(ctx->host_err);
+        if (ctx->done) cudaEventDestroy(ctx->done);
+        if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    }
+    delete ctx;
+}
+
+EIF_API const char *eif_cuda_last_error(const eif_cuda_ctx_t *ctx) { return ctx ? ctx->err : "no context"; }
+
+EIF_API eif_status_t eif_cuda_set_stream(eif_cuda_ctx_t *ctx, void *stream) {
+    if (!ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+    return EIF_STATUS_OK;
+}
+
+EIF_API void *eif_cuda_get_stream(const eif_cuda_ctx_t *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+EIF_API eif_status_t eif_cuda_set_timeout(eif_cuda_ctx_t *ctx, int timeout_ms) {
+    if (!ctx || timeout_ms < 0) return EIF_STATUS_INVALID_ARGUMENT;
+    ctx->timeout_ms = timeout_ms;
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_synchronize(eif_cuda_ctx_t *ctx) {
+    if (!ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    DeviceGuard g(ctx);
+    return wait_stream(ctx);
+}
+
+EIF_API uint64_t eif_cuda_launch_count(const eif_cuda_ctx_t *ctx) { return ctx ? ctx->launches : 0; }
+
+// =================================================================================================
+// KV cache
+// =================================================================================================
+
+static size_t dtype_size(eif_cuda_dtype_t t) { return t == EIF_CUDA_BF16 ? 2 : 4; }
+
+EIF_API eif_status_t eif_cuda_kv_alloc(eif_cuda_ctx_t *ctx, int n_layers, int batch, int max_seq_len,
+                                       int n_kv_heads, int head_dim, eif_cuda_dtype_t dtype, eif_cuda_kv_t **out) {
+    if (!ctx || !out) return EIF_STATUS_INVALID_ARGUMENT;
+    *out = nullptr;
+    if (n_layers <= 0 || batch <= 0 || max_seq_len <= 0 || n_kv_heads <= 0 || head_dim <= 0 || head_dim % 8)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "kv_alloc: bad shape");
+    if (dtype != EIF_CUDA_F32 && dtype != EIF_CUDA_BF16)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "kv_alloc: dtype must be F32 or BF16");
+    DeviceGuard g(ctx);
+    eif_cuda_kv_t *kv = new eif_cuda_kv_t();
+    kv->ctx = ctx;
+    kv->n_layers = n_layers;
+    kv->batch = batch;
+    kv->max_seq = max_seq_len;
+    kv->n_kv = n_kv_heads;
+    kv->hd = head_dim;
+    kv->dtype = dtype;
+    kv->layer_elems = (size_t)batch * max_seq_len * n_kv_heads * head_dim;
+    kv->k = (void **)calloc(n_layers, sizeof(void *));
+    kv->v = (void **)calloc(n_layers, sizeof(void *));
+    const size_t bytes = kv->layer_elems * dtype_size(dtype);
+    for (int l = 0; l < n_layers; ++l) {
+        cudaError_t e = cudaMalloc(&kv->k[l], bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&kv->v[l], bytes);
+        if (e == cudaSuccess) e = cudaMemsetAsync(kv->k[l], 0, bytes, ctx->stream);
+        if (e == cudaSuccess) e = cudaMemsetAsync(kv->v[l], 0, bytes, ctx->stream);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            eif_cuda_kv_free(kv);
+            return fail(ctx, EIF_STATUS_OUT_OF_MEMORY, "kv_alloc: %s (layer %d, %zu bytes each)",
+                        cudaGetErrorString(e), l, bytes);
+        }
+    }
+    eif_status_t st = wait_stream(ctx);
+    if (st != EIF_STATUS_OK) {
+        eif_cuda_kv_free(kv);
+        return st;
+    }
+    *out = kv;
+    return EIF_STATUS_OK;
+}
+
+EIF_API void eif_cuda_kv_free(eif_cuda_kv_t *kv) {
+    if (!kv) return;
+    {
+        DeviceGuard g(kv->ctx);
+        cudaStreamSynchronize(kv->ctx->stream);
+        for (int l = 0; l < kv->n_layers; ++l) {
+            if (kv->k && kv->k[l]) cudaFree(kv->k[l]);
+            if (kv->v && kv->v[l]) cudaFree(kv->v[l]);
+        }
+    }
+    free(kv->k);
+    free(kv->v);
+    delete kv;
+}
+
+EIF_API eif_status_t eif_cuda_kv_reset(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv) {
+    if (!ctx || !kv || kv->ctx != ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    DeviceGuard g(ctx);
+    const size_t bytes = kv->layer_elems * dtype_size(kv->dtype);
+    for (int l = 0; l < kv->n_layers; ++l) {
+        CK(cudaMemsetAsync(kv->k[l], 0, bytes, ctx->stream));
+        CK(cudaMemsetAsync(kv->v[l], 0, bytes, ctx->stream));
+    }
+    return wait_stream(ctx);
+}
+
+static eif_status_t kv_rows_check(eif_cuda_ctx_t *ctx, const eif_cuda_kv_t *kv, int layer, int seq, int row0,
+                                  int n_rows) {
+    if (!ctx || !kv || kv->ctx != ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= kv->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    if (seq < 0 || seq >= kv->batch) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "seq %d out of range", seq);
+    if (row0 < 0 || n_rows < 0 || row0 + n_rows > kv->max_seq)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rows [%d, %d) outside [0, %d)", row0, row0 + n_rows,
+                    kv->max_seq);
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_kv_upload(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int seq, int row0,
+                                        int n_rows, const float *k_rows, const float *v_rows) {
+    eif_status_t st = kv_rows_check(ctx, kv, layer, seq, row0, n_rows);
+    if (st != EIF_STATUS_OK) return st;
+    if (!k_rows || !v_rows) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "kv_upload: NULL rows");
+    if (n_rows == 0) return EIF_STATUS_OK;
+    DeviceGuard g(ctx);
+    const size_t kv_dim = (size_t)kv->n_kv * kv->hd;
+    const size_t n = (size_t)n_rows * kv_dim;
+    const size_t off = ((size_t)seq * kv->max_seq + row0) * kv_dim;
+    if (kv->dtype == EIF_CUDA_F32) {
+        CK(cudaMemcpyAsync(static_cast<float *>(kv->k[layer]) + off, k_rows, n * 4, cudaMemcpyHostToDevice,
+                           ctx->stream));
+        CK(cudaMemcpyAsync(static_cast<float *>(kv->v[layer]) + off, v_rows, n * 4, cudaMemcpyHostToDevice,
+                           ctx->stream));
+    } else {
+        st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, 2 * a256(n * 4));
+        if (st != EIF_STATUS_OK) return st;
+        float *sk = static_cast<float *>(ctx->stage);
+        float *sv = reinterpret_cast<float *>(static_cast<char *>(ctx->stage) + a256(n * 4));
+        CK(cudaMemcpyAsync(sk, k_rows, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        CK(cudaMemcpyAsync(sv, v_rows, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        CK(launch_f32_to_bf16(ctx->stream, sk, static_cast<__nv_bfloat16 *>(kv->k[layer]) + off, n));
+        CK(launch_f32_to_bf16(ctx->stream, sv, static_cast<__nv_bfloat16 *>(kv->v[layer]) + off, n));
+        ctx->launches += 2;
+    }
+    return wait_stream(ctx);
+}
+
+EIF_API eif_status_t eif_cuda_kv_download(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int seq, int row0,
+                                          int n_rows, float *k_rows, float *v_rows) {
+    eif_status_t st = kv_rows_check(ctx, kv, layer, seq, row0, n_rows);
+    if (st != EIF_STATUS_OK) return st;
+    if (!k_rows || !v_rows) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "kv_download: NULL rows");
+    if (n_rows == 0) return EIF_STATUS_OK;
+    DeviceGuard g(ctx);
+    const size_t kv_dim = (size_t)kv->n_kv * kv->hd;
+    const size_t n = (size_t)n_rows * kv_dim;
+    const size_t off = ((size_t)seq * kv->max_seq + row0) * kv_dim;
+    if (kv->dtype == EIF_CUDA_F32) {
+        CK(cudaMemcpyAsync(k_rows, static_cast<float *>(kv->k[layer]) + off, n * 4, cudaMemcpyDeviceToHost,
+                           ctx->stream));
+        CK(cudaMemcpyAsync(v_rows, static_cast<float *>(kv->v[layer]) + off, n * 4, cudaMemcpyDeviceToHost,
+                           ctx->stream));
+    } else {
+        st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, 2 * a256(n * 4));
+        if (st != EIF_STATUS_OK) return st;
+        float *sk = static_cast<float *>(ctx->stage);
+        float *sv = reinterpret_cast<float *>(static_cast<char *>(ctx->stage) + a256(n * 4));
+        CK(launch_bf16_to_f32(ctx->stream, static_cast<__nv_bfloat16 *>(kv->k[layer]) + off, sk, n));
+        CK(launch_bf16_to_f32(ctx->stream, static_cast<__nv_bfloat16 *>(kv->v[layer]) + off, sv, n));
+        ctx->launches += 2;
+        CK(cudaMemcpyAsync(k_rows, sk, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        CK(cudaMemcpyAsync(v_rows, sv, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    }
+    return wait_stream(ctx);
+}
+
+EIF_API eif_status_t eif_cuda_kv_layer_ptrs(const eif_cuda_kv_t *kv, int layer, void **k_dev, void **v_dev) {
+    if (!kv || layer < 0 || layer >= kv->n_layers) return EIF_STATUS_INVALID_ARGUMENT;
+    if (k_dev) *k_dev = kv->k[layer];
+    if (v_dev) *v_dev = kv->v[layer];
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t kv_append_impl(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const int *pos_dev,
+                                   const float *k_dev, const float *v_dev) {
+    CK(launch_kv_append(ctx->stream, kv->k[layer], kv->v[layer], kv->dtype, pos_dev, k_dev, v_dev, kv->batch,
+                        kv->max_seq, kv->n_kv * kv->hd, ctx->dev_err));
+    ctx->launches += 1;
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_kv_append_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const int *pos_dev,
+                                            const float *k_dev, const float *v_dev) {
+    if (!ctx || !kv || kv->ctx != ctx || !pos_dev || !k_dev || !v_dev) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= kv->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    DeviceGuard g(ctx);
+    return kv_append_impl(ctx, kv, layer, pos_dev, k_dev, v_dev);
+}
+
+EIF_API eif_status_t eif_cuda_kv_append(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const int *pos,
+                                        const float *k, const float *v) {
+    if (!ctx || !kv || kv->ctx != ctx || !pos || !k || !v) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= kv->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    for (int b = 0; b < kv->batch; ++b)
+        if (pos[b] < 0 || pos[b] >= kv->max_seq)
+            return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "pos[%d] = %d outside [0, %d)", b, pos[b], kv->max_seq);
+    DeviceGuard g(ctx);
+    const size_t n = (size_t)kv->batch * kv->n_kv * kv->hd;
+    Carver cv;
+    const size_t o_k = cv.take(n * 4), o_v = cv.take(n * 4), o_p = cv.take((size_t)kv->batch * 4);
+    eif_status_t st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (st != EIF_STATUS_OK) return st;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_k, k, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_v, v, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_p, pos, (size_t)kv->batch * 4, cudaMemcpyHostToDevice, ctx->stream));
+    st = kv_append_impl(ctx, kv, layer, reinterpret_cast<int *>(s + o_p), reinterpret_cast<float *>(s + o_k),
+                        reinterpret_cast<float *>(s + o_v));
+    if (st != EIF_STATUS_OK) return st;
+    return wait_stream(ctx);
+}
+
+// =================================================================================================
+// Decode attention
+// =================================================================================================
+
+static eif_status_t decode_check(eif_cuda_ctx_t *ctx, const eif_cuda_kv_t *kv, int layer, int n_heads,
+                                 eif_cuda_subln_t subln) {
+    if (!ctx || !kv || kv->ctx != ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= kv->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    if (n_heads <= 0 || n_heads % kv->n_kv)
+        return fail(ctx, EIF_STATUS_SHAPE_MISMATCH, "n_heads %d is not a multiple of n_kv_heads %d", n_heads, kv->n_kv);
+    if (subln != EIF_CUDA_SUBLN_NONE && subln != EIF_CUDA_SUBLN_RMS && subln != EIF_CUDA_SUBLN_WEIGHT)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "bad subln mode %d", (int)subln);
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t decode_run(eif_cuda_ctx_t *ctx, DecodeArgs &a) {
+    const size_t ws = decode_workspace_bytes(a, ctx->sm_count);
+    eif_status_t st = ensure_buffer(ctx, &ctx->ws, &ctx->ws_bytes, ws);
+    if (st != EIF_STATUS_OK) return st;
+    bool ok = true;
+    int nl = 0;
+    cudaError_t e = launch_attend_decode(ctx->stream, a, ctx->ws, ctx->ws_bytes, ctx->sm_count, &ok, &nl);
+    ctx->launches += nl;
+    if (!ok)
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "decode attention: head_dim %d / group %d not supported", a.D,
+                    a.Hq / a.Hkv);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "attend_decode launch");
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_attend_decode_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
+                                                const float *q_dev, const int *pos_dev, int max_pos, int n_heads,
+                                                float scale, const float *gate_dev, eif_cuda_subln_t subln,
+                                                const float *sub_norm_dev, float *out_dev) {
+    eif_status_t st = decode_check(ctx, kv, layer, n_heads, subln);
+    if (st != EIF_STATUS_OK) return st;
+    if (!q_dev || !pos_dev || !out_dev || (subln == EIF_CUDA_SUBLN_WEIGHT && !sub_norm_dev))
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "attend_decode_dev: NULL pointer");
+    if (max_pos < 0 || max_pos >= kv->max_seq)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "max_pos %d outside [0, %d)", max_pos, kv->max_seq);
+    DeviceGuard g(ctx);
+    DecodeArgs a{kv->k[layer], kv->v[layer], kv->dtype, q_dev, pos_dev, kv->batch, n_heads, kv->n_kv, kv->hd,
+                 kv->max_seq, max_pos + 1, scale, gate_dev, (int)subln, sub_norm_dev, out_dev, ctx->dev_err};
+    return decode_run(ctx, a);
+}
+
+EIF_API eif_status_t eif_cuda_attend_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
+                                            const int *pos, int n_heads, float scale, const float *gate,
+                                            eif_cuda_subln_t subln, const float *sub_norm, float *out) {
+    eif_status_t st = decode_check(ctx, kv, layer, n_heads, subln);
+    if (st != EIF_STATUS_OK) return st;
+    if (!q || !pos || !out || (subln == EIF_CUDA_SUBLN_WEIGHT && !sub_norm))
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "attend_decode: NULL pointer");
+    int max_pos = 0;
+    for (int b = 0; b < kv->batch; ++b) {
+        if (pos[b] < 0 || pos[b] >= kv->max_seq)
+            return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "pos[%d] = %d outside [0, %d)", b, pos[b], kv->max_seq);
+        max_pos = std::max(max_pos, pos[b]);
+    }
+    DeviceGuard g(ctx);
+    const size_t row = (size_t)n_heads * kv->hd;
+    const size_t nq = (size_t)kv->batch * row;
+    Carver cv;
+    const size_t o_q = cv.take(nq * 4), o_o = cv.take(nq * 4), o_p = cv.take((size_t)kv->batch * 4);
+    const size_t o_g = gate ? cv.take(nq * 4) : 0;
+    const size_t o_n = (subln == EIF_CUDA_SUBLN_WEIGHT) ? cv.take(row * 4) : 0;
+    st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (st != EIF_STATUS_OK) return st;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_q, q, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_p, pos, (size_t)kv->batch * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (gate) CK(cudaMemcpyAsync(s + o_g, gate, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (subln == EIF_CUDA_SUBLN_WEIGHT)
+        CK(cudaMemcpyAsync(s + o_n, sub_norm, row * 4, cudaMemcpyHostToDevice, ctx->stream));
+    DecodeArgs a{kv->k[layer], kv->v[layer], kv->dtype, reinterpret_cast<float *>(s + o_q),
+                 reinterpret_cast<int *>(s + o_p), kv->batch, n_heads, kv->n_kv, kv->hd, kv->max_seq, max_pos + 1,
+                 scale, gate ? reinterpret_cast<float *>(s + o_g) : nullptr, (int)subln,
+                 subln == EIF_CUDA_SUBLN_WEIGHT ? reinterpret_cast<float *>(s + o_n) : nullptr,
+                 reinterpret_cast<float *>(s + o_o), ctx->dev_err};
+    st = decode_run(ctx, a);
+    if (st != EIF_STATUS_OK) return st;
+    CK(cudaMemcpyAsync(out, s + o_o, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// =================================================================================================
+// DeltaNet state
+// =================================================================================================
+
+EIF_API eif_status_t eif_cuda_delta_alloc(eif_cuda_ctx_t *ctx, int n_layers, int batch, int n_heads, int d_k,
+                                          int d_v, int conv_k, eif_cuda_delta_t **out) {
+    if (!ctx || !out) return EIF_STATUS_INVALID_ARGUMENT;
+    *out = nullptr;
+    if (n_layers <= 0 || batch <= 0 || n_heads <= 0 || d_k <= 0 || d_v <= 0 || conv_k < 0 || d_k % 4 || d_v % 4)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "delta_alloc: bad shape");
+    DeviceGuard g(ctx);
+    eif_cuda_delta_t *st = new eif_cuda_delta_t();
+    st->ctx = ctx;
+    st->n_layers = n_layers;
+    st->batch = batch;
+    st->H = n_heads;
+    st->dk = d_k;
+    st->dv = d_v;
+    st->conv_k = conv_k;
+    st->conv_dim = 2 * n_heads * d_k + n_heads * d_v;
+    st->S = (float **)calloc(n_layers, sizeof(float *));
+    st->conv = (float **)calloc(n_layers, sizeof(float *));
+    const size_t s_bytes = (size_t)batch * n_heads * d_k * d_v * 4;
+    const size_t c_bytes = (size_t)batch * st->conv_dim * conv_k * 4;
+    for (int l = 0; l < n_layers; ++l) {
+        cudaError_t e = cudaMalloc(&st->S[l], s_bytes);
+        if (e == cudaSuccess) e = cudaMemsetAsync(st->S[l], 0, s_bytes, ctx->stream);
+        if (e == cudaSuccess && c_bytes) e = cudaMalloc(&st->conv[l], c_bytes);
+        if (e == cudaSuccess && c_bytes) e = cudaMemsetAsync(st->conv[l], 0, c_bytes, ctx->stream);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            eif_cuda_delta_free(st);
+            return fail(ctx, EIF_STATUS_OUT_OF_MEMORY, "delta_alloc: %s (layer %d)", cudaGetErrorString(e), l);
+        }
+    }
+    eif_status_t rs = wait_stream(ctx);
+    if (rs != EIF_STATUS_OK) {
+        eif_cuda_delta_free(st);
+        return rs;
+    }
+    *out = st;
+    return EIF_STATUS_OK;
+}
+
+EIF_API void eif_cuda_delta_free(eif_cuda_delta_t *st) {
+    if (!st) return;
+    {
+        DeviceGuard g(st->ctx);
+        cudaStreamSynchronize(st->ctx->stream);
+        for (int l = 0; l < st->n_layers; ++l) {
+            if (st->S && st->S[l]) cudaFree(st->S[l]);
+            if (st->conv && st->conv[l]) cudaFree(st->conv[l]);
+        }
+    }
+    free(st->S);
+    free(st->conv);
+    delete st;
+}
+
+EIF_API eif_status_t eif_cuda_delta_reset(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st) {
+    if (!ctx || !st || st->ctx != ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    DeviceGuard g(ctx);
+    const size_t s_bytes = (size_t)st->batch * st->H * st->dk * st->dv * 4;
+    const size_t c_bytes = (size_t)st->batch * st->conv_dim * st->conv_k * 4;
+    for (int l = 0; l < st->n_layers; ++l) {
+        CK(cudaMemsetAsync(st->S[l], 0, s_bytes, ctx->stream));
+        if (c_bytes) CK(cudaMemsetAsync(st->conv[l], 0, c_bytes, ctx->stream));
+    }
+    return wait_stream(ctx);
+}
+
+static eif_status_t delta_seq_check(eif_cuda_ctx_t *ctx, const eif_cuda_delta_t *st, int layer, int seq) {
+    if (!ctx || !st || st->ctx != ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= st->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    if (seq < 0 || seq >= st->batch) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "seq %d out of range", seq);
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_delta_upload(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, int seq,
+                                           const float *S, const float *conv_state) {
+    eif_status_t rs = delta_seq_check(ctx, st, layer, seq);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (conv_state && !st->conv_k) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "state has no conv window");
+    DeviceGuard g(ctx);
+    const size_t s_n = (size_t)st->H * st->dk * st->dv, c_n = (size_t)st->conv_dim * st->conv_k;
+    if (S) CK(cudaMemcpyAsync(st->S[layer] + seq * s_n, S, s_n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (conv_state)
+        CK(cudaMemcpyAsync(st->conv[layer] + seq * c_n, conv_state, c_n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    return wait_stream(ctx);
+}
+
+EIF_API eif_status_t eif_cuda_delta_download(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, int seq,
+                                             float *S, float *conv_state) {
+    eif_status_t rs = delta_seq_check(ctx, st, layer, seq);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (conv_state && !st->conv_k) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "state has no conv window");
+    DeviceGuard g(ctx);
+    const size_t s_n = (size_t)st->H * st->dk * st->dv, c_n = (size_t)st->conv_dim * st->conv_k;
+    if (S) CK(cudaMemcpyAsync(S, st->S[layer] + seq * s_n, s_n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    if (conv_state)
+        CK(cudaMemcpyAsync(conv_state, st->conv[layer] + seq * c_n, c_n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+EIF_API eif_status_t eif_cuda_delta_layer_ptrs(const eif_cuda_delta_t *st, int layer, float **S_dev,
+                                               float **conv_dev) {
+    if (!st || layer < 0 || layer >= st->n_layers) return EIF_STATUS_INVALID_ARGUMENT;
+    if (S_dev) *S_dev = st->S[layer];
+    if (conv_dev) *conv_dev = st->conv[layer];
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t rule_run(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *q, const float *k,
+                             const float *v, const float *beta, const float *g, float q_scale, float *o) {
+    bool ok = true;
+    cudaError_t e = launch_delta_rule(ctx->stream, st->S[layer], q, k, v, beta, g, q_scale, o, st->batch, st->H,
+                                      st->dk, st->dv, ctx->sm_count, &ok);
+    if (!ok)
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "deltanet_step: d_k %d / d_v %d not supported", st->dk, st->dv);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "deltanet_step launch");
+    ctx->launches += 1;
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_deltanet_step_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer,
+                                                const float *q_dev, const float *k_dev, const float *v_dev,
+                                                const float *beta_dev, const float *g_dev, float q_scale,
+                                                float *o_dev) {
+    if (!ctx || !st || st->ctx != ctx || !q_dev || !k_dev || !v_dev || !beta_dev || !g_dev || !o_dev)
+        return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= st->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    DeviceGuard gd(ctx);
+    return rule_run(ctx, st, layer, q_dev, k_dev, v_dev, beta_dev, g_dev, q_scale, o_dev);
+}
+
+EIF_API eif_status_t eif_cuda_deltanet_step(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *q,
+                                            const float *k, const float *v, const float *beta, const float *g,
+                                            float q_scale, float *o) {
+    if (!ctx || !st || st->ctx != ctx || !q || !k || !v || !beta || !g || !o) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= st->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    DeviceGuard gd(ctx);
+    const size_t nqk = (size_t)st->batch * st->H * st->dk, nv = (size_t)st->batch * st->H * st->dv;
+    const size_t nh = (size_t)st->batch * st->H;
+    Carver cv;
+    const size_t o_q = cv.take(nqk * 4), o_k = cv.take(nqk * 4), o_v = cv.take(nv * 4), o_o = cv.take(nv * 4);
+    const size_t o_b = cv.take(nh * 4), o_g = cv.take(nh * 4);
+    eif_status_t rs = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (rs != EIF_STATUS_OK) return rs;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_q, q, nqk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_k, k, nqk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_v, v, nv * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_b, beta, nh * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_g, g, nh * 4, cudaMemcpyHostToDevice, ctx->stream));
+    rs = rule_run(ctx, st, layer, reinterpret_cast<float *>(s + o_q), reinterpret_cast<float *>(s + o_k),
+                  reinterpret_cast<float *>(s + o_v), reinterpret_cast<float *>(s + o_b),
+                  reinterpret_cast<float *>(s + o_g), q_scale, reinterpret_cast<float *>(s + o_o));
+    if (rs != EIF_STATUS_OK) return rs;
+    CK(cudaMemcpyAsync(o, s + o_o, nv * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}

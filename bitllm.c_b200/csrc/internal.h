@@ -1,0 +1,83 @@
+// internal.h -- shared between the .cu files of libeif_cuda.so (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/eif_cuda.h"
+
+// Device-side error word bits (set by kernels, read back by eif_cuda_synchronize / host entry points).
+enum : unsigned {
+    EIF_DEVERR_POS_RANGE = 1u,   // a pos[] value outside [0, max_seq_len)
+    EIF_DEVERR_WAIT_LIMIT = 2u,  // a bounded pipeline wait ran out of iterations
+};
+
+struct eif_cuda_ctx {
+    int device = -1;
+    int sm_count = 0;
+    int cc_major = 0, cc_minor = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t done = nullptr;
+    int timeout_ms = 120000;
+    uint64_t launches = 0;
+    char err[512] = {0};
+    // device scratch (split-K partials etc.), grown on demand
+    void *ws = nullptr;
+    size_t ws_bytes = 0;
+    // device staging for the host-pointer entry points, grown on demand
+    void *stage = nullptr;
+    size_t stage_bytes = 0;
+    // device error word
+    unsigned *dev_err = nullptr;
+    // pinned host copy of the error word
+    unsigned *host_err = nullptr;
+};
+
+struct eif_cuda_kv {
+    eif_cuda_ctx_t *ctx = nullptr;
+    int n_layers = 0, batch = 0, max_seq = 0, n_kv = 0, hd = 0;
+    eif_cuda_dtype_t dtype = EIF_CUDA_F32;
+    size_t layer_elems = 0;  // batch * max_seq * n_kv * hd
+    void **k = nullptr;      // [n_layers] device pointers
+    void **v = nullptr;
+};
+
+struct eif_cuda_delta {
+    eif_cuda_ctx_t *ctx = nullptr;
+    int n_layers = 0, batch = 0, H = 0, dk = 0, dv = 0, conv_k = 0, conv_dim = 0;
+    float **S = nullptr;     // [n_layers] -> [batch][H][dk][dv]
+    float **conv = nullptr;  // [n_layers] -> [batch][conv_dim][conv_k] (nullptr when conv_k == 0)
+};
+
+// ---- launchers (return cudaError_t of the launch) ----
+cudaError_t launch_delta_rule(cudaStream_t st, float *S, const float *q, const float *k, const float *v,
+                              const float *beta, const float *g, float q_scale, float *o, int B, int H, int dk,
+                              int dv, int sm_count, bool *supported);
+
+struct DecodeArgs {
+    const void *K;
+    const void *V;
+    eif_cuda_dtype_t dtype;
+    const float *q;
+    const int *pos;
+    int B, Hq, Hkv, D, max_seq;
+    int max_len;  // upper bound of pos[b] + 1
+    float scale;
+    const float *gate;
+    int subln;
+    const float *sub_norm;
+    float *out;
+    unsigned *dev_err;
+};
+// Workspace bytes needed by launch_attend_decode for these args and the chosen split.
+size_t decode_workspace_bytes(const DecodeArgs &a, int sm_count);
+cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws, size_t ws_bytes, int sm_count,
+                                 bool *supported, int *n_launches);
+
+cudaError_t launch_kv_append(cudaStream_t st, void *K, void *V, eif_cuda_dtype_t dtype, const int *pos,
+                             const float *k, const float *v, int B, int max_seq, int kv_dim, unsigned *dev_err);
+cudaError_t launch_f32_to_bf16(cudaStream_t st, const float *src, __nv_bfloat16 *dst, size_t n);
+cudaError_t launch_bf16_to_f32(cudaStream_t st, const __nv_bfloat16 *src, float *dst, size_t n);

@@ -1,0 +1,297 @@
+"""ctypes binding of include/eif_cuda.h (the C ABI of libeif_cuda.so).
+
+This is the host-side mirror a Python caller uses; a C99 engine calls the same entry points
+directly.  Host arrays are numpy float32/int32; `_dev` methods take raw device
+addresses (ints), e.g. torch's tensor.data_ptr(), and run asynchronously on the context's stream.
+
+Errors come back as EifCudaError carrying the eif_status_t code and the library's message; there is
+no CPU fallback, and a missing library raises at import time of lib().
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libeif_cuda.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "eif_cuda.h")
+
+# eif_status_t (include/eif_status.h:8-19 of bitllm.c)
+STATUS = {0: "OK", -1: "ERROR", -2: "INVALID_ARGUMENT", -3: "OUT_OF_MEMORY", -4: "NOT_IMPLEMENTED",
+          -5: "NOT_SUPPORTED", -6: "TIMEOUT", -7: "INTERNAL_ERROR", -8: "INVALID_LAYER", -9: "SHAPE_MISMATCH"}
+F32, BF16 = 0, 1
+SUBLN_NONE, SUBLN_RMS, SUBLN_WEIGHT = 0, 1, 2
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_F = ctypes.c_float
+_lib = None
+
+
+class EifCudaError(RuntimeError):
+    def __init__(self, status: int, where: str, message: str = ""):
+        self.status = status
+        self.name = STATUS.get(status, str(status))
+        super().__init__(f"{where}: EIF_STATUS_{self.name}" + (f" ({message})" if message else ""))
+
+
+def header_functions() -> list[str]:
+    """Names of every function the C header declares."""
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(eif_cuda_\w+)\s*\(", src)))
+
+
+def lib() -> ctypes.CDLL:
+    """Load libeif_cuda.so (built by bitllm.c_b200/build.py); raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise FileNotFoundError(f"{LIB_PATH} not built: run python bitllm.c_b200/build.py")
+    L = ctypes.CDLL(LIB_PATH)
+    sig = {
+        "eif_cuda_device_count": (_I, []),
+        "eif_cuda_init": (_I, [ctypes.POINTER(_P), _I]),
+        "eif_cuda_free": (None, [_P]),
+        "eif_cuda_last_error": (ctypes.c_char_p, [_P]),
+        "eif_cuda_set_stream": (_I, [_P, _P]),
+        "eif_cuda_get_stream": (_P, [_P]),
+        "eif_cuda_set_timeout": (_I, [_P, _I]),
+        "eif_cuda_synchronize": (_I, [_P]),
+        "eif_cuda_launch_count": (ctypes.c_uint64, [_P]),
+        "eif_cuda_kv_alloc": (_I, [_P, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
+        "eif_cuda_kv_free": (None, [_P]),
+        "eif_cuda_kv_reset": (_I, [_P, _P]),
+        "eif_cuda_kv_upload": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
+        "eif_cuda_kv_download": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
+        "eif_cuda_kv_layer_ptrs": (_I, [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
+        "eif_cuda_kv_append": (_I, [_P, _P, _I, _P, _P, _P]),
+        "eif_cuda_kv_append_dev": (_I, [_P, _P, _I, _P, _P, _P]),
+        "eif_cuda_attend_decode": (_I, [_P, _P, _I, _P, _P, _I, _F, _P, _I, _P, _P]),
+        "eif_cuda_attend_decode_dev": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _P, _I, _P, _P]),
+        "eif_cuda_delta_alloc": (_I, [_P, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
+        "eif_cuda_delta_free": (None, [_P]),
+        "eif_cuda_delta_reset": (_I, [_P, _P]),
+        "eif_cuda_delta_upload": (_I, [_P, _P, _I, _I, _P, _P]),
+        "eif_cuda_delta_download": (_I, [_P, _P, _I, _I, _P, _P]),
+        "eif_cuda_delta_layer_ptrs": (_I, [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
+        "eif_cuda_deltanet_step": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _F, _P]),
+        "eif_cuda_deltanet_step_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _F, _P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _ptr(a):
+    """Host numpy array -> void* (None passes NULL)."""
+    if a is None:
+        return None
+    return a.ctypes.data_as(_P)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _i32(a):
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+def device_count() -> int:
+    return lib().eif_cuda_device_count()
+
+
+class Context:
+    """One device, one stream (eif_cuda_ctx_t).  Not thread-safe, like the engine's eif_gpu context."""
+
+    def __init__(self, device: int = 0):
+        self._h = _P()
+        st = lib().eif_cuda_init(ctypes.byref(self._h), int(device))
+        if st != 0:
+            raise EifCudaError(st, f"eif_cuda_init(device={device})")
+        self.device = device
+
+    @property
+    def handle(self):
+        return self._h
+
+    def check(self, st: int, where: str):
+        if st != 0:
+            msg = lib().eif_cuda_last_error(self._h)
+            raise EifCudaError(st, where, msg.decode() if msg else "")
+
+    def close(self):
+        if self._h:
+            lib().eif_cuda_free(self._h)
+            self._h = _P()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_handle: int | None):
+        self.check(lib().eif_cuda_set_stream(self._h, stream_handle), "set_stream")
+
+    @property
+    def stream(self) -> int:
+        return lib().eif_cuda_get_stream(self._h) or 0
+
+    def set_timeout(self, ms: int):
+        self.check(lib().eif_cuda_set_timeout(self._h, int(ms)), "set_timeout")
+
+    def synchronize(self):
+        self.check(lib().eif_cuda_synchronize(self._h), "synchronize")
+
+    @property
+    def launch_count(self) -> int:
+        return int(lib().eif_cuda_launch_count(self._h))
+
+    @property
+    def last_error(self) -> str:
+        m = lib().eif_cuda_last_error(self._h)
+        return m.decode() if m else ""
+
+
+class KVCache:
+    """Device KV cache (eif_cuda_kv_t): per layer [batch][max_seq_len][n_kv_heads][head_dim]."""
+
+    def __init__(self, ctx: Context, n_layers: int, batch: int, max_seq_len: int, n_kv_heads: int, head_dim: int,
+                 dtype: int = F32):
+        self.ctx = ctx
+        self.n_layers, self.batch, self.max_seq_len = n_layers, batch, max_seq_len
+        self.n_kv_heads, self.head_dim, self.dtype = n_kv_heads, head_dim, dtype
+        self._h = _P()
+        ctx.check(lib().eif_cuda_kv_alloc(ctx.handle, n_layers, batch, max_seq_len, n_kv_heads, head_dim, dtype,
+                                          ctypes.byref(self._h)), "kv_alloc")
+
+    @property
+    def kv_dim(self):
+        return self.n_kv_heads * self.head_dim
+
+    def free(self):
+        if self._h:
+            lib().eif_cuda_kv_free(self._h)
+            self._h = _P()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def reset(self):
+        self.ctx.check(lib().eif_cuda_kv_reset(self.ctx.handle, self._h), "kv_reset")
+
+    def upload(self, layer: int, seq: int, row0: int, k_rows, v_rows):
+        k, v = _f32(k_rows), _f32(v_rows)
+        n = k.size // self.kv_dim
+        self.ctx.check(lib().eif_cuda_kv_upload(self.ctx.handle, self._h, layer, seq, row0, n, _ptr(k), _ptr(v)),
+                       "kv_upload")
+
+    def download(self, layer: int, seq: int, row0: int, n_rows: int):
+        k = np.zeros((n_rows, self.kv_dim), np.float32)
+        v = np.zeros((n_rows, self.kv_dim), np.float32)
+        self.ctx.check(lib().eif_cuda_kv_download(self.ctx.handle, self._h, layer, seq, row0, n_rows, _ptr(k),
+                                                  _ptr(v)), "kv_download")
+        return k, v
+
+    def layer_ptrs(self, layer: int):
+        k, v = _P(), _P()
+        self.ctx.check(lib().eif_cuda_kv_layer_ptrs(self._h, layer, ctypes.byref(k), ctypes.byref(v)),
+                       "kv_layer_ptrs")
+        return k.value, v.value
+
+    def append(self, layer: int, pos, k, v):
+        p, kk, vv = _i32(pos), _f32(k), _f32(v)
+        self.ctx.check(lib().eif_cuda_kv_append(self.ctx.handle, self._h, layer, _ptr(p), _ptr(kk), _ptr(vv)),
+                       "kv_append")
+
+    def append_dev(self, layer: int, pos_dev: int, k_dev: int, v_dev: int):
+        self.ctx.check(lib().eif_cuda_kv_append_dev(self.ctx.handle, self._h, layer, pos_dev, k_dev, v_dev),
+                       "kv_append_dev")
+
+    def attend_decode(self, layer: int, q, pos, n_heads: int, scale: float, gate=None, subln: int = SUBLN_NONE,
+                      sub_norm=None):
+        """q [batch][n_heads*head_dim] fp32 -> out [batch][n_heads*head_dim] fp32."""
+        qq, pp = _f32(q), _i32(pos)
+        gg = _f32(gate) if gate is not None else None
+        nn = _f32(sub_norm) if sub_norm is not None else None
+        out = np.zeros((self.batch, n_heads * self.head_dim), np.float32)
+        self.ctx.check(lib().eif_cuda_attend_decode(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(pp), n_heads,
+                                                    float(scale), _ptr(gg), int(subln), _ptr(nn), _ptr(out)),
+                       "attend_decode")
+        return out
+
+    def attend_decode_dev(self, layer: int, q_dev: int, pos_dev: int, max_pos: int, n_heads: int, scale: float,
+                          out_dev: int, gate_dev: int | None = None, subln: int = SUBLN_NONE,
+                          sub_norm_dev: int | None = None):
+        self.ctx.check(lib().eif_cuda_attend_decode_dev(self.ctx.handle, self._h, layer, q_dev, pos_dev, int(max_pos),
+                                                        n_heads, float(scale), gate_dev, int(subln), sub_norm_dev,
+                                                        out_dev), "attend_decode_dev")
+
+
+class DeltaState:
+    """Device DeltaNet states (eif_cuda_delta_t): per layer S [batch][H][d_k][d_v] and conv windows."""
+
+    def __init__(self, ctx: Context, n_layers: int, batch: int, n_heads: int, d_k: int, d_v: int, conv_k: int = 0):
+        self.ctx = ctx
+        self.n_layers, self.batch, self.H, self.dk, self.dv, self.conv_k = n_layers, batch, n_heads, d_k, d_v, conv_k
+        self.conv_dim = 2 * n_heads * d_k + n_heads * d_v
+        self._h = _P()
+        ctx.check(lib().eif_cuda_delta_alloc(ctx.handle, n_layers, batch, n_heads, d_k, d_v, conv_k,
+                                             ctypes.byref(self._h)), "delta_alloc")
+
+    def free(self):
+        if self._h:
+            lib().eif_cuda_delta_free(self._h)
+            self._h = _P()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def reset(self):
+        self.ctx.check(lib().eif_cuda_delta_reset(self.ctx.handle, self._h), "delta_reset")
+
+    def upload(self, layer: int, seq: int, S=None, conv_state=None):
+        s = _f32(S) if S is not None else None
+        c = _f32(conv_state) if conv_state is not None else None
+        self.ctx.check(lib().eif_cuda_delta_upload(self.ctx.handle, self._h, layer, seq, _ptr(s), _ptr(c)),
+                       "delta_upload")
+
+    def download(self, layer: int, seq: int):
+        S = np.zeros((self.H, self.dk, self.dv), np.float32)
+        c = np.zeros((self.conv_dim, self.conv_k), np.float32) if self.conv_k else None
+        self.ctx.check(lib().eif_cuda_delta_download(self.ctx.handle, self._h, layer, seq, _ptr(S), _ptr(c)),
+                       "delta_download")
+        return S, c
+
+    def layer_ptrs(self, layer: int):
+        s, c = _P(), _P()
+        self.ctx.check(lib().eif_cuda_delta_layer_ptrs(self._h, layer, ctypes.byref(s), ctypes.byref(c)),
+                       "delta_layer_ptrs")
+        return s.value, c.value
+
+    def step(self, layer: int, q, k, v, beta, g, q_scale: float):
+        """One token of the delta rule for every sequence: returns o [batch][H*d_v]."""
+        qq, kk, vv, bb, gg = _f32(q), _f32(k), _f32(v), _f32(beta), _f32(g)
+        o = np.zeros((self.batch, self.H * self.dv), np.float32)
+        self.ctx.check(lib().eif_cuda_deltanet_step(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv),
+                                                    _ptr(bb), _ptr(gg), float(q_scale), _ptr(o)), "deltanet_step")
+        return o
+
+    def step_dev(self, layer: int, q_dev, k_dev, v_dev, beta_dev, g_dev, q_scale: float, o_dev):
+        self.ctx.check(lib().eif_cuda_deltanet_step_dev(self.ctx.handle, self._h, layer, q_dev, k_dev, v_dev,
+                                                        beta_dev, g_dev, float(q_scale), o_dev), "deltanet_step_dev")

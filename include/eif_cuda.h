@@ -1,0 +1,185 @@
+/*
+ * eif_cuda.h -- B200 (sm_100a) token-mixing hot path of bitllm.c behind a C99 ABI.
+ *
+ * The engine keeps its C99 host code; the GQA attention over the KV cache and the Gated DeltaNet
+ * state update run on the GPU through these entry points.  The header sits next to the engine's
+ * eif_gpu.h and follows its conventions (include/eif_gpu.h:31-61 in bitllm.c): an opaque context,
+ * one command stream per context, a context is not thread-safe.  Unlike eif_gpu there is no CPU
+ * fallback: every failure comes back as an eif_status_t and the caller decides.
+ *
+ * Device mirrors keep the engine's layouts unchanged:
+ *   KV cache   per layer, per sequence: [max_seq_len][n_kv_heads * head_dim], row t holds the
+ *              rotated key / value of position t (qwen35_attn_state_t, include/eif_qwen35.h:204-208;
+ *              tinyllm key_cache/value_cache, src/eif_tinyllm.c:415-418), fp32 or bf16.
+ *   DeltaNet   per layer, per sequence: S [n_v_heads][d_k][d_v] fp32, d_v contiguous, and the
+ *              conv window [conv_dim][conv_k] fp32 (qwen35_delta_state_t, include/eif_qwen35.h:199-202).
+ *   Sequences of one batch are stacked: sequence b of layer l starts at b * (one sequence's size).
+ *
+ * Pointer conventions: arguments are HOST pointers unless the entry point's name ends in `_dev`,
+ * in which case they are device pointers and the call is asynchronous on the context's stream.
+ * Host entry points copy their inputs in, run, copy the outputs back and wait (with the context's
+ * timeout) before returning.  Reference paths (file:line) are relative to the bitllm.c root.
+ */
+#ifndef EIF_CUDA_H
+#define EIF_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+/* Status codes: the engine's own eif_status_t (include/eif_status.h:8-19).  When the engine's header
+ * is reachable it is used as is; otherwise the same enumerators are declared here under the same
+ * include guard, so either header may come first. */
+#if defined(__has_include)
+#if __has_include("eif_status.h")
+#include "eif_status.h"
+#endif
+#endif
+#ifndef EIF_STATUS_H
+#define EIF_STATUS_H
+typedef enum {
+    EIF_STATUS_OK = 0,
+    EIF_STATUS_ERROR = -1,
+    EIF_STATUS_INVALID_ARGUMENT = -2,
+    EIF_STATUS_OUT_OF_MEMORY = -3,
+    EIF_STATUS_NOT_IMPLEMENTED = -4,
+    EIF_STATUS_NOT_SUPPORTED = -5,
+    EIF_STATUS_TIMEOUT = -6,
+    EIF_STATUS_INTERNAL_ERROR = -7,
+    EIF_STATUS_INVALID_LAYER = -8,
+    EIF_STATUS_SHAPE_MISMATCH = -9
+} eif_status_t;
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct eif_cuda_ctx eif_cuda_ctx_t;      /* one device, one stream; not thread-safe */
+typedef struct eif_cuda_kv eif_cuda_kv_t;        /* device KV cache of n_layers x batch sequences */
+typedef struct eif_cuda_delta eif_cuda_delta_t;  /* device DeltaNet states of n_layers x batch sequences */
+
+typedef enum { EIF_CUDA_F32 = 0, EIF_CUDA_BF16 = 1 } eif_cuda_dtype_t;
+
+/* SubLN applied after the attention output gate (src/eif_qwen35.c:779-789). */
+typedef enum {
+    EIF_CUDA_SUBLN_NONE = 0,  /* plain_linear: copy (also the tinyllm path, which has no SubLN) */
+    EIF_CUDA_SUBLN_RMS = 1,   /* !plain_linear without a sub_norm weight: x * rsqrt(mean(x^2) + 1e-6) */
+    EIF_CUDA_SUBLN_WEIGHT = 2 /* x * rsqrt(mean(x^2) + 1e-6) * sub_norm */
+} eif_cuda_subln_t;
+
+/* ---------------------------------------------------------------------------------------------
+ * Context  (replaces eif_gpu_init / eif_gpu_shutdown for this path, include/eif_gpu.h:44-50)
+ * ------------------------------------------------------------------------------------------- */
+
+/* Number of visible CUDA devices (0 without a driver or with BITLLM_NO_CUDA=1). */
+int eif_cuda_device_count(void);
+
+/* Create a context on `device`.  Returns EIF_STATUS_NOT_SUPPORTED when there is no device, the device
+ * is not sm_100 (B200) or BITLLM_NO_CUDA=1 is set. */
+eif_status_t eif_cuda_init(eif_cuda_ctx_t **ctx, int device);
+void eif_cuda_free(eif_cuda_ctx_t *ctx);
+
+/* Message of the last failure on this context ("" if none).  Valid until the next call. */
+const char *eif_cuda_last_error(const eif_cuda_ctx_t *ctx);
+
+/* Stream used by `_dev` calls: a cudaStream_t passed as void* (NULL = the context's own stream). */
+eif_status_t eif_cuda_set_stream(eif_cuda_ctx_t *ctx, void *stream);
+void *eif_cuda_get_stream(const eif_cuda_ctx_t *ctx);
+
+/* Host waits poll the stream until done or `timeout_ms` elapses (EIF_STATUS_TIMEOUT); 0 = no limit. */
+eif_status_t eif_cuda_set_timeout(eif_cuda_ctx_t *ctx, int timeout_ms);
+eif_status_t eif_cuda_synchronize(eif_cuda_ctx_t *ctx);
+
+/* Number of kernels this context has launched since it was created (instrumentation). */
+uint64_t eif_cuda_launch_count(const eif_cuda_ctx_t *ctx);
+
+/* ---------------------------------------------------------------------------------------------
+ * KV cache mirror  (qwen35_attn_state_t, include/eif_qwen35.h:204-208; tinyllm_state_t key/value
+ * caches, src/eif_tinyllm.c:131-134).  The reference keeps fp32 only (Qwen3.5) or fp32/INT8
+ * (tinyllm); bf16 is the B200 storage type for long contexts.
+ * ------------------------------------------------------------------------------------------- */
+
+eif_status_t eif_cuda_kv_alloc(eif_cuda_ctx_t *ctx, int n_layers, int batch, int max_seq_len, int n_kv_heads,
+                               int head_dim, eif_cuda_dtype_t dtype, eif_cuda_kv_t **kv);
+void eif_cuda_kv_free(eif_cuda_kv_t *kv);
+
+/* Zero every row of every layer (the KV part of qwen35_reset, src/eif_qwen35.c:1483-1497). */
+eif_status_t eif_cuda_kv_reset(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv);
+
+/* Copy rows [row0, row0+n_rows) of (layer, seq) from / to host fp32 arrays [n_rows][n_kv_heads*head_dim].
+ * A bf16 cache converts on the device (round to nearest even) and widens on download. */
+eif_status_t eif_cuda_kv_upload(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int seq, int row0, int n_rows,
+                                const float *k_rows, const float *v_rows);
+eif_status_t eif_cuda_kv_download(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int seq, int row0,
+                                  int n_rows, float *k_rows, float *v_rows);
+
+/* Device base pointers of one layer: [batch][max_seq_len][n_kv_heads][head_dim] of the cache dtype. */
+eif_status_t eif_cuda_kv_layer_ptrs(const eif_cuda_kv_t *kv, int layer, void **k_dev, void **v_dev);
+
+/* Append the new token's rotated k / v ([batch][n_kv_heads*head_dim] fp32) at row pos[b] of every
+ * sequence -- the memcpy into the cache at src/eif_qwen35.c:734-736 and src/eif_tinyllm.c:417-418. */
+eif_status_t eif_cuda_kv_append(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const int *pos, const float *k,
+                                const float *v);
+eif_status_t eif_cuda_kv_append_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const int *pos_dev,
+                                    const float *k_dev, const float *v_dev);
+
+/* ---------------------------------------------------------------------------------------------
+ * Decode attention: one new query token per sequence over cache rows [0, pos[b]].
+ * Replaces the head loop of fullatt_attend (src/eif_qwen35.c:741-790) and the inline tinyllm decode
+ * attention (src/eif_tinyllm.c:555-656):
+ *   q        [batch][n_heads * head_dim] fp32, rotated (kv head of q head h = h / (n_heads/n_kv_heads))
+ *   scale    score multiplier (1/sqrt(head_dim) in both engines)
+ *   gate     NULL, or [batch][n_heads*head_dim]: out *= sigmoid(gate)  (src/eif_qwen35.c:773-777)
+ *   subln    SubLN of the whole gated output row (src/eif_qwen35.c:779-789); sub_norm [n_heads*head_dim]
+ *            is read only for EIF_CUDA_SUBLN_WEIGHT
+ *   out      [batch][n_heads * head_dim] fp32
+ * pos[b] must satisfy 0 <= pos[b] < max_seq_len (the bound tinyllm_forward enforces,
+ * src/eif_tinyllm.c:387-389); violations return EIF_STATUS_INVALID_ARGUMENT before any launch.
+ * ------------------------------------------------------------------------------------------- */
+eif_status_t eif_cuda_attend_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
+                                    const int *pos, int n_heads, float scale, const float *gate,
+                                    eif_cuda_subln_t subln, const float *sub_norm, float *out);
+/* Device-pointer variant; max_pos is an upper bound of pos_dev[] (used to size the split over the KV
+ * length: rows beyond a sequence's own pos are never read). */
+eif_status_t eif_cuda_attend_decode_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_dev,
+                                        const int *pos_dev, int max_pos, int n_heads, float scale,
+                                        const float *gate_dev, eif_cuda_subln_t subln, const float *sub_norm_dev,
+                                        float *out_dev);
+
+/* ---------------------------------------------------------------------------------------------
+ * Gated DeltaNet state mirror (qwen35_delta_state_t, include/eif_qwen35.h:199-202)
+ * ------------------------------------------------------------------------------------------- */
+
+/* n_heads = lin_n_v_heads = lin_n_k_heads (deltanet_core indexes q/k by the v head,
+ * src/eif_qwen35.c:601-605).  conv_k may be 0 when only the delta rule is used. */
+eif_status_t eif_cuda_delta_alloc(eif_cuda_ctx_t *ctx, int n_layers, int batch, int n_heads, int d_k, int d_v,
+                                  int conv_k, eif_cuda_delta_t **st);
+void eif_cuda_delta_free(eif_cuda_delta_t *st);
+/* Zero S and the conv windows (the DeltaNet part of qwen35_reset, src/eif_qwen35.c:1483-1497). */
+eif_status_t eif_cuda_delta_reset(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st);
+/* Copy one sequence's S [n_heads][d_k][d_v] and / or conv window [conv_dim][conv_k] (either may be NULL). */
+eif_status_t eif_cuda_delta_upload(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, int seq, const float *S,
+                                   const float *conv_state);
+eif_status_t eif_cuda_delta_download(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, int seq, float *S,
+                                     float *conv_state);
+/* Device base pointers of one layer: S [batch][n_heads][d_k][d_v], conv [batch][conv_dim][conv_k]. */
+eif_status_t eif_cuda_delta_layer_ptrs(const eif_cuda_delta_t *st, int layer, float **S_dev, float **conv_dev);
+
+/*
+ * Delta rule of one token for every sequence and head (src/eif_qwen35.c:594-639), in the reference's
+ * order: S <- exp(g) S; e = S^T k; S <- S + beta k (v - e)^T; o = S^T (q_scale q).
+ *   q, k [batch][n_heads*d_k] (L2-normalised by the caller as at src/eif_qwen35.c:579-585)
+ *   v, o [batch][n_heads*d_v]; beta, g [batch][n_heads]
+ */
+eif_status_t eif_cuda_deltanet_step(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *q,
+                                    const float *k, const float *v, const float *beta, const float *g,
+                                    float q_scale, float *o);
+eif_status_t eif_cuda_deltanet_step_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *q_dev,
+                                        const float *k_dev, const float *v_dev, const float *beta_dev,
+                                        const float *g_dev, float q_scale, float *o_dev);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EIF_CUDA_H */

@@ -1,0 +1,185 @@
+"""ctypes front-end to the CPU checker (TEST INFRASTRUCTURE ONLY).
+
+Two libraries live under oracle/:
+  * liboracle.so           -- oracle.c, the C restatement ("port") of the reference hot path;
+  * _ref/libbitllm_ref.so  -- the reference's own src/eif_qwen35.c compiled from its sources
+                              (built only where the reference tree is present).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import this module; the
+product (libeif_cuda.so and its Python host mirror) never does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libbitllm_ref.so")
+
+_F = ctypes.POINTER(ctypes.c_float)
+_port = None
+_ref = None
+
+
+def build(ref: bool = False) -> None:
+    """Compile the port (and, when asked and the reference tree exists, the reference shim)."""
+    targets = ["all"]
+    if ref:
+        targets.append("ref")
+    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+
+
+def _fp(a):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"], "oracle buffers are contiguous float32"
+    return a.ctypes.data_as(_F)
+
+
+def port():
+    """The C restatement (liboracle.so), built on first use if missing."""
+    global _port
+    if _port is None:
+        if not os.path.exists(PORT_SO):
+            build(ref=False)
+        _port = ctypes.CDLL(PORT_SO)
+        i, f = ctypes.c_int, ctypes.c_float
+        _port.orc_deltanet_rule.argtypes = [_F, _F, _F, _F, _F, _F, f, _F, i, i, i]
+        _port.orc_deltanet_core.argtypes = [_F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, i, i, i, i]
+        _port.orc_attend_decode.argtypes = [_F, _F, _F, i, i, i, i, f, _F, _F]
+        _port.orc_subln.argtypes = [_F, _F, i, i]
+        _port.orc_attend_prefill.argtypes = [_F, _F, _F, i, i, i, i, i, f, _F]
+        _port.orc_rope_table.argtypes = [i, i, f, _F, _F]
+        _port.orc_rope_apply.argtypes = [_F, i, i, _F, _F, i]
+        _port.orc_rope_partial.argtypes = [_F, i, i, i]
+        _port.orc_fullatt_prep.argtypes = [_F, _F, _F, _F, _F, _F, _F, _F, _F, i, i, i, i]
+        _port.orc_round_bf16.argtypes = [_F, ctypes.c_size_t]
+    return _port
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref():
+    """The reference's own code (oracle/_ref/libbitllm_ref.so); raises if it was not built."""
+    global _ref
+    if _ref is None:
+        if not os.path.exists(REF_SO):
+            raise FileNotFoundError("oracle/_ref/libbitllm_ref.so not built (needs the reference tree)")
+        _ref = ctypes.CDLL(REF_SO)
+        i = ctypes.c_int
+        _ref.ref_deltanet_core.argtypes = [_F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, i, i, i, i]
+        _ref.ref_fullatt_prep.argtypes = [_F, _F, _F, _F, _F, _F, _F, _F, _F, i, i, i, i]
+        _ref.ref_fullatt_attend.argtypes = [_F, _F, _F, _F, _F, _F, i, i, i, i, i]
+        _ref.ref_omp_threads.restype = i
+        _ref.ref_set_threads.argtypes = [i]
+    return _ref
+
+
+def c32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# ------------------------------------------------------------------------------------------------
+# Port wrappers (numpy in, numpy out; inputs are not modified unless stated)
+# ------------------------------------------------------------------------------------------------
+
+def deltanet_rule(S, q, k, v, beta, g, q_scale):
+    """One token, one sequence: S [H,dk,dv] is updated IN PLACE; returns o [H*dv]."""
+    H, dk, dv = S.shape
+    o = np.zeros(H * dv, np.float32)
+    port().orc_deltanet_rule(_fp(S), _fp(c32(q)), _fp(c32(k)), _fp(c32(v)), _fp(c32(beta)), _fp(c32(g)),
+                             float(q_scale), _fp(o), H, dk, dv)
+    return o
+
+
+def deltanet_core(qkv_raw, z, b_raw, a_raw, conv_state, S, conv_w, dt_bias, A_log, norm_w, lib=None):
+    """deltanet_core on one token; conv_state and S are updated IN PLACE; returns out [H*dv].
+
+    lib=None uses the port; lib=ref() runs the reference's own function."""
+    H, dk, dv = S.shape
+    conv_k = conv_state.shape[-1]
+    qkv = c32(qkv_raw).copy()
+    out = np.zeros(H * dv, np.float32)
+    args = (_fp(qkv), _fp(c32(z).copy()), _fp(c32(b_raw).copy()), _fp(c32(a_raw).copy()), _fp(conv_state), _fp(S),
+            _fp(c32(conv_w)), _fp(c32(dt_bias)), _fp(c32(A_log)), _fp(c32(norm_w)), _fp(out), H, dk, dv, conv_k)
+    if lib is None:
+        port().orc_deltanet_core(*args)
+    else:
+        lib.ref_deltanet_core(*args)
+    return out
+
+
+def attend_decode(q, k_cache, v_cache, pos, nh, nkv, hd, scale, gate=None):
+    out = np.zeros(nh * hd, np.float32)
+    port().orc_attend_decode(_fp(c32(q)), _fp(c32(k_cache)), _fp(c32(v_cache)), int(pos), nh, nkv, hd, float(scale),
+                             _fp(c32(gate)) if gate is not None else None, _fp(out))
+    return out
+
+
+def subln(x, sub_norm, mode):
+    y = c32(x).copy()
+    port().orc_subln(_fp(y), _fp(c32(sub_norm)) if sub_norm is not None else None, int(mode), y.size)
+    return y
+
+
+def attend_prefill(q, k_cache, v_cache, n_tok, start_pos, nh, nkv, hd, scale):
+    out = np.zeros((n_tok, nh * hd), np.float32)
+    port().orc_attend_prefill(_fp(c32(q)), _fp(c32(k_cache)), _fp(c32(v_cache)), n_tok, start_pos, nh, nkv, hd,
+                              float(scale), _fp(out))
+    return out
+
+
+def rope_table(pos, hd, theta):
+    c = np.zeros(hd // 2, np.float32)
+    s = np.zeros(hd // 2, np.float32)
+    port().orc_rope_table(int(pos), hd, float(theta), _fp(c), _fp(s))
+    return c, s
+
+
+def rope_apply(x, n_heads, hd, pos, theta, interleaved=False):
+    """tinyllm RoPE of x [n_heads*hd] at pos (returns a rotated copy)."""
+    c, s = rope_table(pos, hd, theta)
+    y = c32(x).copy()
+    port().orc_rope_apply(_fp(y), n_heads, hd, _fp(c), _fp(s), int(bool(interleaved)))
+    return y
+
+
+def rope_partial(x, pos, n_heads, hd):
+    y = c32(x).copy()
+    port().orc_rope_partial(_fp(y), int(pos), n_heads, hd)
+    return y
+
+
+def fullatt_prep(qg, k, v, q_norm, k_norm, k_cache, v_cache, pos, nh, nkv, hd, lib=None):
+    """Returns (q, gate, k_rotated); writes cache row pos IN PLACE."""
+    q = np.zeros(nh * hd, np.float32)
+    gate = np.zeros(nh * hd, np.float32)
+    kk = c32(k).copy()
+    args = (_fp(c32(qg)), _fp(kk), _fp(c32(v)), _fp(q), _fp(gate), _fp(c32(q_norm)), _fp(c32(k_norm)),
+            _fp(k_cache), _fp(v_cache), int(pos), nh, nkv, hd)
+    if lib is None:
+        port().orc_fullatt_prep(*args)
+    else:
+        lib.ref_fullatt_prep(*args)
+    return q, gate, kk
+
+
+def ref_fullatt_attend(q, gate, k_cache, v_cache, sub_norm, plain_linear, pos, nh, nkv, hd):
+    """The reference's fullatt_attend (needs oracle/_ref)."""
+    o = np.zeros(nh * hd, np.float32)
+    ref().ref_fullatt_attend(_fp(c32(q)), _fp(c32(gate)), _fp(o), _fp(k_cache), _fp(v_cache),
+                             _fp(c32(sub_norm)) if sub_norm is not None else None, int(plain_linear), int(pos),
+                             nh, nkv, hd)
+    return o
+
+
+def round_bf16(x):
+    y = c32(x).copy()
+    port().orc_round_bf16(_fp(y), y.size)
+    return y

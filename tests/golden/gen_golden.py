@@ -1,0 +1,134 @@
+"""Generate the golden fixtures of the hot path from the REFERENCE's own code.
+
+Run in a container that holds the reference tree (the fixtures are committed; the GPU box never
+runs this script):
+
+    make -C oracle all ref            # builds oracle/_ref/libbitllm_ref.so from the reference sources
+    python tests/golden/gen_golden.py
+
+Every fixture stores its seeded inputs and the outputs of the reference function named in it, so
+the tests can check both the C restatement (oracle/oracle.c) and the CUDA kernels against the
+reference without the reference being present.
+
+  deltanet_core_*.npz   deltanet_core          src/eif_qwen35.c:546-656  (several tokens in a row)
+  fullatt_prep.npz      fullatt_prep           src/eif_qwen35.c:699-737
+  fullatt_attend.npz    fullatt_attend         src/eif_qwen35.c:741-790  (gate + SubLN, and plain)
+  decode_cfg1.npz       fullatt_attend, gate=+100 (sigmoid == 1.0f), plain: the ungated GQA core at
+                        the Qwen2.5-0.5B decode shape of BASELINE config 1, RoPE (NeoX, theta 1e6)
+                        applied by the tinyllm restatement before the cache is filled
+  prefill_small.npz     fullatt_attend per token with the causal bound pos = start_pos + i, which is
+                        what tinyllm_forward_batch_embeddings (src/eif_tinyllm.c:1158-1268) computes
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "..", ".."))
+from oracle import oracle as orc  # noqa: E402
+
+GATE_ONE = 100.0  # 1/(1+expf(-100)) rounds to exactly 1.0f
+
+
+def gen_deltanet_core(name, seed, H, dk, dv, conv_k, n_steps):
+    rng = np.random.default_rng(seed)
+    conv_dim = 2 * H * dk + H * dv
+    S0 = (rng.standard_normal((H, dk, dv)) * 0.02).astype(np.float32)
+    conv0 = rng.standard_normal((conv_dim, conv_k)).astype(np.float32)
+    conv_w = (rng.standard_normal((conv_dim, conv_k)) * 0.5).astype(np.float32)
+    dt_bias = rng.standard_normal(H).astype(np.float32)
+    A_log = (rng.standard_normal(H) * 0.5).astype(np.float32)
+    norm_w = (1.0 + 0.1 * rng.standard_normal(dv)).astype(np.float32)
+    qkv = rng.standard_normal((n_steps, conv_dim)).astype(np.float32)
+    z = rng.standard_normal((n_steps, H * dv)).astype(np.float32)
+    b = rng.standard_normal((n_steps, H)).astype(np.float32)
+    a = rng.standard_normal((n_steps, H)).astype(np.float32)
+    S = S0.copy()
+    conv = conv0.copy()
+    outs = []
+    lib = orc.ref()
+    for t in range(n_steps):
+        outs.append(orc.deltanet_core(qkv[t], z[t], b[t], a[t], conv, S, conv_w, dt_bias, A_log, norm_w, lib=lib))
+    np.savez(os.path.join(HERE, name), S0=S0, conv0=conv0, conv_w=conv_w, dt_bias=dt_bias, A_log=A_log,
+             norm_w=norm_w, qkv=qkv, z=z, b=b, a=a, out=np.stack(outs), S_final=S, conv_final=conv,
+             meta=np.array([H, dk, dv, conv_k, n_steps], np.int32))
+
+
+def gen_fullatt_prep(seed, nh, nkv, hd, max_seq, pos):
+    rng = np.random.default_rng(seed)
+    kv_dim = nkv * hd
+    qg = rng.standard_normal(nh * 2 * hd).astype(np.float32)
+    k = rng.standard_normal(kv_dim).astype(np.float32)
+    v = rng.standard_normal(kv_dim).astype(np.float32)
+    q_norm = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    k_norm = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kc = np.zeros((max_seq, kv_dim), np.float32)
+    vc = np.zeros((max_seq, kv_dim), np.float32)
+    q, gate, k_rot = orc.fullatt_prep(qg, k, v, q_norm, k_norm, kc, vc, pos, nh, nkv, hd, lib=orc.ref())
+    np.savez(os.path.join(HERE, "fullatt_prep.npz"), qg=qg, k=k, v=v, q_norm=q_norm, k_norm=k_norm, q=q,
+             gate=gate, k_rot=k_rot, k_row=kc[pos], v_row=vc[pos], meta=np.array([nh, nkv, hd, pos], np.int32))
+
+
+def gen_fullatt_attend(seed, nh, nkv, hd, n_rows, pos):
+    rng = np.random.default_rng(seed)
+    kv_dim = nkv * hd
+    kc = rng.standard_normal((n_rows, kv_dim)).astype(np.float32)
+    vc = rng.standard_normal((n_rows, kv_dim)).astype(np.float32)
+    q = rng.standard_normal(nh * hd).astype(np.float32)
+    gate = rng.standard_normal(nh * hd).astype(np.float32)
+    sub_norm = (1.0 + 0.1 * rng.standard_normal(nh * hd)).astype(np.float32)
+    out_subln = orc.ref_fullatt_attend(q, gate, kc, vc, sub_norm, 0, pos, nh, nkv, hd)
+    out_rms = orc.ref_fullatt_attend(q, gate, kc, vc, None, 0, pos, nh, nkv, hd)
+    out_plain = orc.ref_fullatt_attend(q, gate, kc, vc, None, 1, pos, nh, nkv, hd)
+    np.savez(os.path.join(HERE, "fullatt_attend.npz"), k_cache=kc, v_cache=vc, q=q, gate=gate, sub_norm=sub_norm,
+             out_subln=out_subln, out_rms=out_rms, out_plain=out_plain, meta=np.array([nh, nkv, hd, pos], np.int32))
+
+
+def gen_decode_cfg1(seed):
+    """B1, 14 Q / 2 KV heads, hd 64, KV length 512, fp32, NeoX RoPE theta 1e6."""
+    nh, nkv, hd, T, theta = 14, 2, 64, 512, 1e6
+    rng = np.random.default_rng(seed)
+    kv_dim = nkv * hd
+    k_raw = rng.standard_normal((T, kv_dim)).astype(np.float32)
+    vc = rng.standard_normal((T, kv_dim)).astype(np.float32)
+    q_raw = rng.standard_normal(nh * hd).astype(np.float32)
+    kc = np.stack([orc.rope_apply(k_raw[t], nkv, hd, t, theta) for t in range(T)])
+    q = orc.rope_apply(q_raw, nh, hd, T - 1, theta)
+    gate = np.full(nh * hd, GATE_ONE, np.float32)
+    out = orc.ref_fullatt_attend(q, gate, kc, vc, None, 1, T - 1, nh, nkv, hd)
+    np.savez(os.path.join(HERE, "decode_cfg1.npz"), q=q, k_cache=kc, v_cache=vc, out=out,
+             meta=np.array([nh, nkv, hd, T - 1], np.int32))
+
+
+def gen_prefill_small(seed, nh, nkv, hd, n_tok, start_pos):
+    rng = np.random.default_rng(seed)
+    kv_dim = nkv * hd
+    rows = start_pos + n_tok
+    kc = rng.standard_normal((rows, kv_dim)).astype(np.float32)
+    vc = rng.standard_normal((rows, kv_dim)).astype(np.float32)
+    q = rng.standard_normal((n_tok, nh * hd)).astype(np.float32)
+    gate = np.full(nh * hd, GATE_ONE, np.float32)
+    out = np.stack([orc.ref_fullatt_attend(q[i], gate, kc, vc, None, 1, start_pos + i, nh, nkv, hd)
+                    for i in range(n_tok)])
+    np.savez(os.path.join(HERE, "prefill_small.npz"), q=q, k_cache=kc, v_cache=vc, out=out,
+             meta=np.array([nh, nkv, hd, n_tok, start_pos], np.int32))
+
+
+def main():
+    orc.build(ref=True)
+    gen_deltanet_core("deltanet_core_h2d128.npz", 1001, H=2, dk=128, dv=128, conv_k=4, n_steps=6)
+    gen_deltanet_core("deltanet_core_h3d64.npz", 1002, H=3, dk=64, dv=64, conv_k=4, n_steps=5)
+    gen_fullatt_prep(1003, nh=8, nkv=2, hd=256, max_seq=16, pos=11)
+    gen_fullatt_attend(1004, nh=8, nkv=2, hd=256, n_rows=40, pos=37)
+    gen_decode_cfg1(1005)
+    gen_prefill_small(1006, nh=6, nkv=2, hd=64, n_tok=24, start_pos=8)
+    for f in sorted(os.listdir(HERE)):
+        if f.endswith(".npz"):
+            print(f"{f:32s} {os.path.getsize(os.path.join(HERE, f)):>9d} B")
+
+
+if __name__ == "__main__":
+    main()

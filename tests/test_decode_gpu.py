@@ -1,0 +1,159 @@
+"""Decode attention through the C ABI against the reference (golden fixtures) and the C restatement.
+
+Tolerance: rel-L2 <= 1e-5 for fp32 caches (the north-star bound for the fp32 decode path).  bf16
+caches are compared with the fp32 oracle run on the same bf16-rounded rows, also at 1e-5: the
+kernels accumulate in fp32, so only the storage is narrower."""
+import numpy as np
+import pytest
+
+from conftest import golden, rel_l2
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def _fill(pkg, ctx, kc, vc, dtype, max_seq=None):
+    B, T, kvd = kc.shape
+    return kc, vc
+
+
+def make_cache(pkg, ctx, orc, rng, B, T, nkv, hd, dtype, max_seq=None):
+    max_seq = max_seq or T
+    kv = pkg.KVCache(ctx, 1, B, max_seq, nkv, hd, dtype)
+    kc = rng.standard_normal((B, T, nkv * hd)).astype(np.float32)
+    vc = rng.standard_normal((B, T, nkv * hd)).astype(np.float32)
+    if dtype == pkg.BF16:
+        kc = orc.round_bf16(kc).reshape(kc.shape)
+        vc = orc.round_bf16(vc).reshape(vc.shape)
+    for b in range(B):
+        kv.upload(0, b, 0, kc[b], vc[b])
+    return kv, kc, vc
+
+
+def test_golden_cfg1(pkg, ctx):
+    """BASELINE config 1 (Qwen2.5-0.5B decode shape) against the reference's fullatt_attend."""
+    d = golden("decode_cfg1.npz")
+    nh, nkv, hd, pos = (int(x) for x in d["meta"])
+    kv = pkg.KVCache(ctx, 1, 1, pos + 1, nkv, hd, pkg.F32)
+    kv.upload(0, 0, 0, d["k_cache"], d["v_cache"])
+    out = kv.attend_decode(0, d["q"][None], np.array([pos]), nh, 1.0 / np.sqrt(hd))
+    assert rel_l2(out[0], d["out"]) <= TOL
+
+
+def test_golden_fullatt_gate_subln(pkg, ctx):
+    d = golden("fullatt_attend.npz")
+    nh, nkv, hd, pos = (int(x) for x in d["meta"])
+    kv = pkg.KVCache(ctx, 1, 1, d["k_cache"].shape[0], nkv, hd, pkg.F32)
+    kv.upload(0, 0, 0, d["k_cache"], d["v_cache"])
+    scale = np.float32(1.0) / np.sqrt(np.float32(hd))
+    for mode, key, w in [(pkg.SUBLN_NONE, "out_plain", None), (pkg.SUBLN_RMS, "out_rms", None),
+                         (pkg.SUBLN_WEIGHT, "out_subln", d["sub_norm"])]:
+        out = kv.attend_decode(0, d["q"][None], np.array([pos]), nh, scale, gate=d["gate"][None], subln=mode,
+                               sub_norm=w)
+        assert rel_l2(out[0], d[key]) <= TOL, key
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("hd,nh,nkv", [(64, 14, 2), (64, 9, 3), (128, 12, 2), (128, 16, 2), (256, 8, 2),
+                                       (64, 32, 32), (128, 40, 8), (256, 10, 2)])
+def test_random_ragged(pkg, ctx, orc, dtype, hd, nh, nkv):
+    """Ragged pos across the batch (including 0 and max_seq-1); all group sizes 1..8."""
+    rng = np.random.default_rng(hd * 1000 + nh * 10 + nkv)
+    dt = pkg.F32 if dtype == "f32" else pkg.BF16
+    B, T = 4, 333
+    kv, kc, vc = make_cache(pkg, ctx, orc, rng, B, T, nkv, hd, dt)
+    q = rng.standard_normal((B, nh * hd)).astype(np.float32)
+    pos = np.array([T - 1, 0, 64, 129], np.int32)
+    scale = 1.0 / np.sqrt(hd)
+    out = kv.attend_decode(0, q, pos, nh, scale)
+    for b in range(B):
+        ref = orc.attend_decode(q[b], kc[b], vc[b], pos[b], nh, nkv, hd, scale)
+        assert rel_l2(out[b], ref) <= TOL, (b, pos[b])
+
+
+def test_pos0_copies_v(pkg, ctx, orc):
+    """Known answer (reference tests/test_gguf_gqa_layout.c:105): at pos 0 the output is v_0 of the group."""
+    rng = np.random.default_rng(5)
+    nh, nkv, hd = 4, 2, 64
+    kv, kc, vc = make_cache(pkg, ctx, orc, rng, 2, 8, nkv, hd, pkg.F32)
+    out = kv.attend_decode(0, rng.standard_normal((2, nh * hd)), np.array([0, 0]), nh, 0.125)
+    for b in range(2):
+        for h in range(nh):
+            kvh = h // (nh // nkv)
+            np.testing.assert_allclose(out[b, h * hd:(h + 1) * hd], vc[b, 0, kvh * hd:(kvh + 1) * hd], rtol=0,
+                                       atol=1e-6)
+
+
+def test_long_context_bf16_gate(pkg, ctx, orc):
+    """Qwen3.5 attention shape at a long context with the sigmoid gate (sampled sequences of a batch)."""
+    rng = np.random.default_rng(9)
+    nh, nkv, hd, T, B = 8, 2, 256, 8192, 3
+    kv, kc, vc = make_cache(pkg, ctx, orc, rng, B, T, nkv, hd, pkg.BF16)
+    q = rng.standard_normal((B, nh * hd)).astype(np.float32)
+    gate = rng.standard_normal((B, nh * hd)).astype(np.float32)
+    pos = np.array([T - 1, T - 1000, 4097], np.int32)
+    out = kv.attend_decode(0, q, pos, nh, 1 / 16.0, gate=gate)
+    for b in range(B):
+        ref = orc.attend_decode(q[b], kc[b], vc[b], pos[b], nh, nkv, hd, 1 / 16.0, gate=gate[b])
+        assert rel_l2(out[b], ref) <= TOL
+
+
+def test_append_then_attend(pkg, ctx, orc):
+    """kv_append writes row pos[b]; attention then sees it (the engine's prep -> attend order)."""
+    rng = np.random.default_rng(10)
+    nh, nkv, hd, T, B = 8, 2, 128, 40, 3
+    for dt in (pkg.F32, pkg.BF16):
+        kv, kc, vc = make_cache(pkg, ctx, orc, rng, B, T, nkv, hd, dt)
+        pos = np.array([5, 39, 17], np.int32)
+        knew = rng.standard_normal((B, nkv * hd)).astype(np.float32)
+        vnew = rng.standard_normal((B, nkv * hd)).astype(np.float32)
+        kv.append(0, pos, knew, vnew)
+        if dt == pkg.BF16:
+            knew = orc.round_bf16(knew).reshape(knew.shape)
+            vnew = orc.round_bf16(vnew).reshape(vnew.shape)
+        for b in range(B):
+            kc[b, pos[b]] = knew[b]
+            vc[b, pos[b]] = vnew[b]
+            kd, vd = kv.download(0, b, 0, T)
+            assert np.array_equal(kd, kc[b]) and np.array_equal(vd, vc[b])
+        q = rng.standard_normal((B, nh * hd)).astype(np.float32)
+        out = kv.attend_decode(0, q, pos, nh, 0.1)
+        for b in range(B):
+            assert rel_l2(out[b], orc.attend_decode(q[b], kc[b], vc[b], pos[b], nh, nkv, hd, 0.1)) <= TOL
+
+
+def test_bad_arguments(pkg, ctx):
+    kv = pkg.KVCache(ctx, 2, 2, 16, 2, 64, pkg.F32)
+    q = np.zeros((2, 4 * 64), np.float32)
+    with pytest.raises(pkg.EifCudaError) as e:
+        kv.attend_decode(0, q, np.array([3, 16]), 4, 0.1)  # pos == max_seq_len
+    assert e.value.name == "INVALID_ARGUMENT"
+    with pytest.raises(pkg.EifCudaError) as e:
+        kv.attend_decode(0, np.zeros((2, 3 * 64), np.float32), np.array([1, 1]), 3, 0.1)
+    assert e.value.name == "SHAPE_MISMATCH"
+    with pytest.raises(pkg.EifCudaError) as e:
+        kv.attend_decode(2, q, np.array([1, 1]), 4, 0.1)
+    assert e.value.name == "INVALID_LAYER"
+    with pytest.raises(pkg.EifCudaError) as e:
+        kv.append(0, np.array([0, -1]), np.zeros((2, 128), np.float32), np.zeros((2, 128), np.float32))
+    assert e.value.name == "INVALID_ARGUMENT"
+    # the context stays usable after refusals
+    out = kv.attend_decode(0, q, np.array([0, 15]), 4, 0.1)
+    assert np.all(np.isfinite(out))
+
+
+def test_device_pos_out_of_range_reported(pkg, ctx):
+    """A device-side pos outside the cache is caught by the kernels' bounds check, skipped, and reported
+    as INVALID_ARGUMENT at the next synchronize (nothing out of bounds is read or written)."""
+    import torch
+    kv = pkg.KVCache(ctx, 1, 2, 16, 2, 64, pkg.F32)
+    q = torch.zeros((2, 4 * 64), device="cuda")
+    out = torch.zeros_like(q)
+    pos = torch.tensor([3, 99], dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    kv.attend_decode_dev(0, q.data_ptr(), pos.data_ptr(), 15, 4, 0.1, out.data_ptr())
+    with pytest.raises(pkg.EifCudaError) as e:
+        ctx.synchronize()
+    assert e.value.name == "INVALID_ARGUMENT"
+    ctx.synchronize()  # error word cleared
+    assert torch.all(out[1] == 0)

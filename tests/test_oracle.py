@@ -1,0 +1,107 @@
+"""The CPU checker (oracle/oracle.c) against the reference's own outputs.
+
+The fixtures under tests/golden/ were produced by the reference's src/eif_qwen35.c compiled from its
+sources (tests/golden/gen_golden.py); where that build is present (oracle/_ref/) the restatement is
+also compared with it on fresh seeded inputs.  No GPU needed."""
+import numpy as np
+import pytest
+
+from conftest import golden, rel_l2
+
+
+@pytest.mark.parametrize("name", ["deltanet_core_h2d128.npz", "deltanet_core_h3d64.npz"])
+def test_deltanet_core_golden(orc, name):
+    d = golden(name)
+    H, dk, dv, ck, n = (int(x) for x in d["meta"])
+    S, conv = d["S0"].copy(), d["conv0"].copy()
+    outs = [orc.deltanet_core(d["qkv"][t], d["z"][t], d["b"][t], d["a"][t], conv, S, d["conv_w"], d["dt_bias"],
+                              d["A_log"], d["norm_w"]) for t in range(n)]
+    assert rel_l2(np.stack(outs), d["out"]) < 1e-6
+    assert rel_l2(S, d["S_final"]) < 1e-6
+    assert rel_l2(conv, d["conv_final"]) < 1e-6
+
+
+def test_decode_cfg1_golden(orc):
+    d = golden("decode_cfg1.npz")
+    nh, nkv, hd, pos = (int(x) for x in d["meta"])
+    o = orc.attend_decode(d["q"], d["k_cache"], d["v_cache"], pos, nh, nkv, hd, 1.0 / np.sqrt(hd))
+    assert rel_l2(o, d["out"]) < 1e-6
+
+
+def test_fullatt_attend_golden(orc):
+    d = golden("fullatt_attend.npz")
+    nh, nkv, hd, pos = (int(x) for x in d["meta"])
+    scale = np.float32(1.0) / np.sqrt(np.float32(hd))
+    o = orc.attend_decode(d["q"], d["k_cache"], d["v_cache"], pos, nh, nkv, hd, scale, gate=d["gate"])
+    assert rel_l2(o, d["out_plain"]) < 1e-6
+    assert rel_l2(orc.subln(o, None, 1), d["out_rms"]) < 1e-6
+    assert rel_l2(orc.subln(o, d["sub_norm"], 2), d["out_subln"]) < 1e-6
+
+
+def test_prefill_golden(orc):
+    d = golden("prefill_small.npz")
+    nh, nkv, hd, n, sp = (int(x) for x in d["meta"])
+    o = orc.attend_prefill(d["q"], d["k_cache"], d["v_cache"], n, sp, nh, nkv, hd, 1.0 / np.sqrt(hd))
+    assert rel_l2(o, d["out"]) < 1e-6
+
+
+def test_fullatt_prep_golden(orc):
+    d = golden("fullatt_prep.npz")
+    nh, nkv, hd, pos = (int(x) for x in d["meta"])
+    kc = np.zeros((16, nkv * hd), np.float32)
+    vc = np.zeros_like(kc)
+    q, g, kr = orc.fullatt_prep(d["qg"], d["k"], d["v"], d["q_norm"], d["k_norm"], kc, vc, pos, nh, nkv, hd)
+    assert rel_l2(q, d["q"]) < 1e-6 and rel_l2(g, d["gate"]) == 0.0
+    assert rel_l2(kr, d["k_rot"]) < 1e-6 and rel_l2(kc[pos], d["k_row"]) < 1e-6
+    assert np.array_equal(vc[pos], d["v_row"])
+
+
+def test_pos0_attention_copies_v(orc):
+    """Known answer of the reference's tests/test_gguf_gqa_layout.c:105: at pos 0 attention returns v_0
+    of each query head's kv group (GQA mapping h -> h / (nh/nkv))."""
+    rng = np.random.default_rng(3)
+    nh, nkv, hd = 4, 2, 16
+    kc = rng.standard_normal((1, nkv * hd)).astype(np.float32)
+    vc = rng.standard_normal((1, nkv * hd)).astype(np.float32)
+    o = orc.attend_decode(rng.standard_normal(nh * hd), kc, vc, 0, nh, nkv, hd, 0.25)
+    for h in range(nh):
+        kvh = h // (nh // nkv)
+        assert np.allclose(o[h * hd:(h + 1) * hd], vc[0, kvh * hd:(kvh + 1) * hd], rtol=0, atol=1e-6)
+
+
+ref_only = pytest.mark.skipif("not __import__('oracle.oracle', fromlist=['x']).ref_available()",
+                              reason="reference build (oracle/_ref) absent")
+
+
+@ref_only
+def test_port_vs_reference_deltanet_random(orc):
+    rng = np.random.default_rng(11)
+    for H, dk, ck in [(16, 128, 4), (1, 32, 3)]:
+        conv_dim = 3 * H * dk
+        args = dict(conv_w=(rng.standard_normal((conv_dim, ck)) * 0.5).astype(np.float32),
+                    dt_bias=rng.standard_normal(H).astype(np.float32),
+                    A_log=rng.standard_normal(H).astype(np.float32) * 0.5,
+                    norm_w=(1 + 0.1 * rng.standard_normal(dk)).astype(np.float32))
+        S1 = (rng.standard_normal((H, dk, dk)) * 0.02).astype(np.float32)
+        c1 = rng.standard_normal((conv_dim, ck)).astype(np.float32)
+        S2, c2 = S1.copy(), c1.copy()
+        for _ in range(3):
+            x = [rng.standard_normal(n).astype(np.float32) for n in (conv_dim, H * dk, H, H)]
+            o1 = orc.deltanet_core(*x, c1, S1, **args)
+            o2 = orc.deltanet_core(*x, c2, S2, **args, lib=orc.ref())
+            assert rel_l2(o1, o2) < 1e-6
+        assert rel_l2(S1, S2) < 1e-6
+
+
+@ref_only
+def test_port_vs_reference_attend_random(orc):
+    rng = np.random.default_rng(12)
+    for nh, nkv, hd, T in [(14, 2, 64, 300), (8, 2, 256, 64), (9, 3, 128, 17), (4, 4, 64, 1)]:
+        kc = rng.standard_normal((T, nkv * hd)).astype(np.float32)
+        vc = rng.standard_normal((T, nkv * hd)).astype(np.float32)
+        q = rng.standard_normal(nh * hd).astype(np.float32)
+        gate = rng.standard_normal(nh * hd).astype(np.float32)
+        scale = np.float32(1.0) / np.sqrt(np.float32(hd))
+        o = orc.attend_decode(q, kc, vc, T - 1, nh, nkv, hd, scale, gate=gate)
+        r = orc.ref_fullatt_attend(q, gate, kc, vc, None, 1, T - 1, nh, nkv, hd)
+        assert rel_l2(o, r) < 1e-6
