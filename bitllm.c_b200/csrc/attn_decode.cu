@@ -205,9 +205,39 @@ __global__ void __launch_bounds__(256) attn_decode_combine_kernel(
 
 struct Split {
     int nchunk, chunk;
+    bool tc;
 };
 
+bool use_tc(const DecodeArgs &a) {
+    return a.dtype == EIF_CUDA_BF16 && a.tmk && a.tmv && !a.force_simt && decode_tc_supported(a.D, a.Hq / a.Hkv);
+}
+
+// Tensor-core path: persistent CTAs (one per SM) take items round-robin, so pick the chunk count that
+// minimises the busiest CTA's tiles plus the partials it writes and the combine reads back.
+Split choose_split_tc(const DecodeArgs &a, int sm_count) {
+    const long units = (long)a.B * a.Hkv;
+    const long tpu = (a.max_len + 63) / 64;  // 64-key tiles per unit
+    const double tile_bytes = 64.0 * a.D * 2 * 2;
+    const double part_bytes = 2.0 * (a.Hq / a.Hkv) * a.D * 4;
+    int best = 1;
+    double best_cost = 1e300;
+    for (int nc = 1; nc <= 64 && nc <= tpu; ++nc) {
+        const long ct = (tpu + nc - 1) / nc;
+        const long ncu = (tpu + ct - 1) / ct;  // chunks actually used
+        const long items = units * ncu;
+        const long per_cta = (items + sm_count - 1) / sm_count;
+        const double cost = per_cta * ct * tile_bytes + per_cta * part_bytes;
+        if (cost < best_cost * 0.999) {
+            best_cost = cost;
+            best = (int)ncu;
+        }
+    }
+    const int chunk_tiles = (int)((tpu + best - 1) / best);
+    return {best, chunk_tiles * 64, true};
+}
+
 Split choose_split(const DecodeArgs &a, int sm_count) {
+    if (use_tc(a)) return choose_split_tc(a, sm_count);
     const int units = a.B * a.Hkv;
     const int L = a.max_len > 0 ? a.max_len : 1;
     // aim at >= 4 CTAs per SM, chunks of at least 64 keys
@@ -217,7 +247,7 @@ Split choose_split(const DecodeArgs &a, int sm_count) {
     if (nchunk < 1) nchunk = 1;
     int chunk = (L + nchunk - 1) / nchunk;
     nchunk = (L + chunk - 1) / chunk;
-    return {nchunk, chunk};
+    return {nchunk, chunk, false};
 }
 
 template <typename KT, int D, int G>
@@ -277,7 +307,9 @@ cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws,
     float *part_o = static_cast<float *>(ws);
     float2 *part_ml = reinterpret_cast<float2 *>(static_cast<char *>(ws) + o_bytes);
     cudaError_t e;
-    if (a.dtype == EIF_CUDA_F32)
+    if (sp.tc)
+        e = launch_attend_decode_tc(st, *a.tmk, *a.tmv, a, sp.nchunk, sp.chunk, part_o, part_ml, sm_count);
+    else if (a.dtype == EIF_CUDA_F32)
         e = dispatch_d<float>(st, a, sp, part_o, part_ml, supported);
     else
         e = dispatch_d<__nv_bfloat16>(st, a, sp, part_o, part_ml, supported);

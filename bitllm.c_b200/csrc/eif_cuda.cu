@@ -112,6 +112,46 @@ eif_status_t wait_stream(eif_cuda_ctx_t *ctx) {
     return EIF_STATUS_OK;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link dependency on libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// TMA descriptor of one bf16 cache array [batch*max_seq][n_kv][hd] as a 3-D tensor (hd, n_kv, rows),
+// boxes of 64 dims x 1 head x 64 rows with the 128-byte swizzle the decode kernel's ldmatrix expects.
+bool make_kv_tensor_map(CUtensorMap *map, void *base, const eif_cuda_kv_t *kv) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc || kv->hd % 64) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)kv->hd, (cuuint64_t)kv->n_kv, (cuuint64_t)kv->batch * kv->max_seq};
+    const cuuint64_t strides[2] = {(cuuint64_t)kv->hd * 2, (cuuint64_t)kv->n_kv * kv->hd * 2};
+    const cuuint32_t box[3] = {64, 1, 64};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool env_flag(const char *name) {
+    const char *e = getenv(name);
+    return e && *e && strcmp(e, "0") != 0;
+}
+
 // Carve consecutive 256-byte aligned slices out of the staging buffer.
 struct Carver {
     size_t off = 0;
@@ -238,6 +278,9 @@ EIF_API eif_status_t eif_cuda_kv_alloc(eif_cuda_ctx_t *ctx, int n_layers, int ba
     kv->layer_elems = (size_t)batch * max_seq_len * n_kv_heads * head_dim;
     kv->k = (void **)calloc(n_layers, sizeof(void *));
     kv->v = (void **)calloc(n_layers, sizeof(void *));
+    kv->tmk = static_cast<CUtensorMap *>(aligned_alloc(64, sizeof(CUtensorMap) * n_layers));
+    kv->tmv = static_cast<CUtensorMap *>(aligned_alloc(64, sizeof(CUtensorMap) * n_layers));
+    kv->tm_ready = (bool *)calloc(n_layers, sizeof(bool));
     const size_t bytes = kv->layer_elems * dtype_size(dtype);
     for (int l = 0; l < n_layers; ++l) {
         cudaError_t e = cudaMalloc(&kv->k[l], bytes);
@@ -272,6 +315,9 @@ EIF_API void eif_cuda_kv_free(eif_cuda_kv_t *kv) {
     }
     free(kv->k);
     free(kv->v);
+    free(kv->tmk);
+    free(kv->tmv);
+    free(kv->tm_ready);
     delete kv;
 }
 
@@ -416,7 +462,18 @@ static eif_status_t decode_check(eif_cuda_ctx_t *ctx, const eif_cuda_kv_t *kv, i
     return EIF_STATUS_OK;
 }
 
-static eif_status_t decode_run(eif_cuda_ctx_t *ctx, DecodeArgs &a) {
+static eif_status_t decode_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, DecodeArgs &a) {
+    if (kv->dtype == EIF_CUDA_BF16) {
+        if (!kv->tm_ready[layer]) {
+            kv->tm_ready[layer] = make_kv_tensor_map(&kv->tmk[layer], kv->k[layer], kv) &&
+                                  make_kv_tensor_map(&kv->tmv[layer], kv->v[layer], kv);
+        }
+        if (kv->tm_ready[layer]) {
+            a.tmk = &kv->tmk[layer];
+            a.tmv = &kv->tmv[layer];
+        }
+    }
+    a.force_simt = env_flag("BITLLM_DECODE_SIMT");
     const size_t ws = decode_workspace_bytes(a, ctx->sm_count);
     eif_status_t st = ensure_buffer(ctx, &ctx->ws, &ctx->ws_bytes, ws);
     if (st != EIF_STATUS_OK) return st;
@@ -444,7 +501,7 @@ EIF_API eif_status_t eif_cuda_attend_decode_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv
     DeviceGuard g(ctx);
     DecodeArgs a{kv->k[layer], kv->v[layer], kv->dtype, q_dev, pos_dev, kv->batch, n_heads, kv->n_kv, kv->hd,
                  kv->max_seq, max_pos + 1, scale, gate_dev, (int)subln, sub_norm_dev, out_dev, ctx->dev_err};
-    return decode_run(ctx, a);
+    return decode_run(ctx, kv, layer, a);
 }
 
 EIF_API eif_status_t eif_cuda_attend_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
@@ -480,7 +537,7 @@ EIF_API eif_status_t eif_cuda_attend_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *
                  scale, gate ? reinterpret_cast<float *>(s + o_g) : nullptr, (int)subln,
                  subln == EIF_CUDA_SUBLN_WEIGHT ? reinterpret_cast<float *>(s + o_n) : nullptr,
                  reinterpret_cast<float *>(s + o_o), ctx->dev_err};
-    st = decode_run(ctx, a);
+    st = decode_run(ctx, kv, layer, a);
     if (st != EIF_STATUS_OK) return st;
     CK(cudaMemcpyAsync(out, s + o_o, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return wait_stream(ctx);

@@ -1,6 +1,7 @@
 // internal.h -- shared between the .cu files of libeif_cuda.so (not part of the C ABI).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -43,6 +44,10 @@ struct eif_cuda_kv {
     size_t layer_elems = 0;  // batch * max_seq * n_kv * hd
     void **k = nullptr;      // [n_layers] device pointers
     void **v = nullptr;
+    // TMA descriptors of the bf16 layers (64-key x 64-dim boxes, 128-byte swizzle), made on first use
+    CUtensorMap *tmk = nullptr;
+    CUtensorMap *tmv = nullptr;
+    bool *tm_ready = nullptr;
 };
 
 struct eif_cuda_delta {
@@ -71,7 +76,16 @@ struct DecodeArgs {
     const float *sub_norm;
     float *out;
     unsigned *dev_err;
+    const CUtensorMap *tmk = nullptr;  // bf16 caches: TMA descriptors of K / V (nullptr -> SIMT kernel)
+    const CUtensorMap *tmv = nullptr;
+    bool force_simt = false;
 };
+
+// Tensor-core decode path (attn_decode_tc.cu).
+bool decode_tc_supported(int D, int G);
+cudaError_t launch_attend_decode_tc(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
+                                    const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,
+                                    float2 *part_ml, int sm_count);
 // Workspace bytes needed by launch_attend_decode for these args and the chosen split.
 size_t decode_workspace_bytes(const DecodeArgs &a, int sm_count);
 cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws, size_t ws_bytes, int sm_count,

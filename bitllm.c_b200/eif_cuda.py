@@ -12,6 +12,7 @@ from __future__ import annotations
 import ctypes
 import os
 import re
+import weakref
 
 import numpy as np
 
@@ -118,6 +119,8 @@ class Context:
         if st != 0:
             raise EifCudaError(st, f"eif_cuda_init(device={device})")
         self.device = device
+        # device objects made on this context; they must be freed before the context itself
+        self._children = weakref.WeakSet()
 
     @property
     def handle(self):
@@ -130,8 +133,14 @@ class Context:
 
     def close(self):
         if self._h:
+            for c in list(self._children):
+                c.free()
             lib().eif_cuda_free(self._h)
             self._h = _P()
+
+    @property
+    def alive(self) -> bool:
+        return bool(self._h)
 
     def __del__(self):
         try:
@@ -173,15 +182,16 @@ class KVCache:
         self._h = _P()
         ctx.check(lib().eif_cuda_kv_alloc(ctx.handle, n_layers, batch, max_seq_len, n_kv_heads, head_dim, dtype,
                                           ctypes.byref(self._h)), "kv_alloc")
+        ctx._children.add(self)
 
     @property
     def kv_dim(self):
         return self.n_kv_heads * self.head_dim
 
     def free(self):
-        if self._h:
+        if self._h and self.ctx.alive:
             lib().eif_cuda_kv_free(self._h)
-            self._h = _P()
+        self._h = _P()
 
     def __del__(self):
         try:
@@ -250,11 +260,12 @@ class DeltaState:
         self._h = _P()
         ctx.check(lib().eif_cuda_delta_alloc(ctx.handle, n_layers, batch, n_heads, d_k, d_v, conv_k,
                                              ctypes.byref(self._h)), "delta_alloc")
+        ctx._children.add(self)
 
     def free(self):
-        if self._h:
+        if self._h and self.ctx.alive:
             lib().eif_cuda_delta_free(self._h)
-            self._h = _P()
+        self._h = _P()
 
     def __del__(self):
         try:

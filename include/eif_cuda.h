@@ -77,6 +77,7 @@ int eif_cuda_device_count(void);
 /* Create a context on `device`.  Returns EIF_STATUS_NOT_SUPPORTED when there is no device, the device
  * is not sm_100 (B200) or BITLLM_NO_CUDA=1 is set. */
 eif_status_t eif_cuda_init(eif_cuda_ctx_t **ctx, int device);
+/* Free every KV cache and DeltaNet state made on the context before the context itself. */
 void eif_cuda_free(eif_cuda_ctx_t *ctx);
 
 /* Message of the last failure on this context ("" if none).  Valid until the next call. */

@@ -12,11 +12,6 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-5
 
 
-def _fill(pkg, ctx, kc, vc, dtype, max_seq=None):
-    B, T, kvd = kc.shape
-    return kc, vc
-
-
 def make_cache(pkg, ctx, orc, rng, B, T, nkv, hd, dtype, max_seq=None):
     max_seq = max_seq or T
     kv = pkg.KVCache(ctx, 1, B, max_seq, nkv, hd, dtype)
@@ -69,6 +64,45 @@ def test_random_ragged(pkg, ctx, orc, dtype, hd, nh, nkv):
     for b in range(B):
         ref = orc.attend_decode(q[b], kc[b], vc[b], pos[b], nh, nkv, hd, scale)
         assert rel_l2(out[b], ref) <= TOL, (b, pos[b])
+
+
+@pytest.mark.parametrize("hd,nh,nkv", [(256, 8, 2), (128, 14, 2), (64, 16, 2)])
+def test_bf16_tensor_core_and_simt_paths_agree(pkg, ctx, orc, monkeypatch, hd, nh, nkv):
+    """The bf16 cache runs on the TMA + tensor-core kernel; BITLLM_DECODE_SIMT=1 selects the SIMT kernel.
+    Both must match the oracle on the same bf16 rows (many items per persistent CTA, ragged tails)."""
+    rng = np.random.default_rng(hd + nh)
+    B, T = 5, 1500
+    kv, kc, vc = make_cache(pkg, ctx, orc, rng, B, T, nkv, hd, pkg.BF16)
+    q = rng.standard_normal((B, nh * hd)).astype(np.float32)
+    gate = rng.standard_normal((B, nh * hd)).astype(np.float32)
+    pos = np.array([T - 1, 1, 63, 64, 1000], np.int32)
+    scale = 1.0 / np.sqrt(hd)
+    out_tc = kv.attend_decode(0, q, pos, nh, scale, gate=gate, subln=pkg.SUBLN_RMS)
+    monkeypatch.setenv("BITLLM_DECODE_SIMT", "1")
+    out_simt = kv.attend_decode(0, q, pos, nh, scale, gate=gate, subln=pkg.SUBLN_RMS)
+    for b in range(B):
+        ref = orc.subln(orc.attend_decode(q[b], kc[b], vc[b], pos[b], nh, nkv, hd, scale, gate=gate[b]), None, 1)
+        assert rel_l2(out_tc[b], ref) <= TOL, ("tc", b)
+        assert rel_l2(out_simt[b], ref) <= TOL, ("simt", b)
+
+
+def test_rows_past_pos_are_never_used(pkg, ctx, orc):
+    """Rows after pos[b] hold non-finite garbage: the output must not depend on them (the reference reads
+    only rows 0..pos, src/eif_qwen35.c:757-770)."""
+    rng = np.random.default_rng(21)
+    nh, nkv, hd, T, B = 8, 2, 256, 300, 2
+    for dt in (pkg.BF16, pkg.F32):
+        kv, kc, vc = make_cache(pkg, ctx, orc, rng, B, T, nkv, hd, dt)
+        pos = np.array([100, 37], np.int32)
+        for b in range(B):
+            junk = np.full((T - pos[b] - 1, nkv * hd), np.nan, np.float32)
+            junk[::2] = np.inf
+            kv.upload(0, b, int(pos[b]) + 1, junk, -junk)
+        q = rng.standard_normal((B, nh * hd)).astype(np.float32)
+        out = kv.attend_decode(0, q, pos, nh, 0.0625)
+        assert np.all(np.isfinite(out))
+        for b in range(B):
+            assert rel_l2(out[b], orc.attend_decode(q[b], kc[b], vc[b], pos[b], nh, nkv, hd, 0.0625)) <= TOL
 
 
 def test_pos0_copies_v(pkg, ctx, orc):
