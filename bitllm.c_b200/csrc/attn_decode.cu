@@ -208,6 +208,15 @@ struct Split {
     bool tc;
 };
 
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Scratch bytes of the chunk partials: o [units][nchunk][G][D] and (m, l) [units][nchunk][G].
+size_t partials_bytes(const DecodeArgs &a, int nchunk) {
+    const size_t units = (size_t)a.B * a.Hkv;
+    const size_t G = (size_t)(a.Hq / a.Hkv);
+    return align256(units * nchunk * G * a.D * sizeof(float)) + align256(units * nchunk * G * sizeof(float2));
+}
+
 bool use_tc(const DecodeArgs &a) {
     return a.dtype == EIF_CUDA_BF16 && a.tmk && a.tmv && !a.force_simt && decode_tc_supported(a.D, a.Hq / a.Hkv);
 }
@@ -225,6 +234,7 @@ Split choose_split_tc(const DecodeArgs &a, int sm_count) {
         const long ct = (tpu + nc - 1) / nc;
         const long ncu = (tpu + ct - 1) / ct;  // chunks actually used
         const long items = units * ncu;
+        if (a.max_ws_bytes && ncu > 1 && partials_bytes(a, (int)ncu) > a.max_ws_bytes) break;
         const long per_cta = (items + sm_count - 1) / sm_count;
         const double cost = per_cta * ct * tile_bytes + per_cta * part_bytes;
         if (cost < best_cost * 0.999) {
@@ -245,6 +255,8 @@ Split choose_split(const DecodeArgs &a, int sm_count) {
     int max_chunks = (L + 63) / 64;
     int nchunk = want < max_chunks ? want : max_chunks;
     if (nchunk < 1) nchunk = 1;
+    if (a.max_ws_bytes)
+        while (nchunk > 1 && partials_bytes(a, nchunk) > a.max_ws_bytes) --nchunk;
     int chunk = (L + nchunk - 1) / nchunk;
     nchunk = (L + chunk - 1) / chunk;
     return {nchunk, chunk, false};
@@ -283,8 +295,6 @@ cudaError_t dispatch_d(cudaStream_t st, const DecodeArgs &a, const Split &sp, fl
         default: *ok = false; return cudaSuccess;
     }
 }
-
-size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace
 

@@ -462,7 +462,7 @@ static eif_status_t decode_check(eif_cuda_ctx_t *ctx, const eif_cuda_kv_t *kv, i
     return EIF_STATUS_OK;
 }
 
-static eif_status_t decode_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, DecodeArgs &a) {
+void decode_prepare(eif_cuda_kv_t *kv, int layer, DecodeArgs &a) {
     if (kv->dtype == EIF_CUDA_BF16) {
         if (!kv->tm_ready[layer]) {
             kv->tm_ready[layer] = make_kv_tensor_map(&kv->tmk[layer], kv->k[layer], kv) &&
@@ -474,6 +474,10 @@ static eif_status_t decode_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer
         }
     }
     a.force_simt = env_flag("BITLLM_DECODE_SIMT");
+}
+
+static eif_status_t decode_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, DecodeArgs &a) {
+    decode_prepare(kv, layer, a);
     const size_t ws = decode_workspace_bytes(a, ctx->sm_count);
     eif_status_t st = ensure_buffer(ctx, &ctx->ws, &ctx->ws_bytes, ws);
     if (st != EIF_STATUS_OK) return st;

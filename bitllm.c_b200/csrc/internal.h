@@ -79,7 +79,11 @@ struct DecodeArgs {
     const CUtensorMap *tmk = nullptr;  // bf16 caches: TMA descriptors of K / V (nullptr -> SIMT kernel)
     const CUtensorMap *tmv = nullptr;
     bool force_simt = false;
+    size_t max_ws_bytes = 0;  // 0: the split may use any amount of scratch; else it must fit in this many bytes
 };
+
+// Fills the TMA descriptors (made on first use per layer) and the kernel choice of `a` (eif_cuda.cu).
+void decode_prepare(eif_cuda_kv_t *kv, int layer, DecodeArgs &a);
 
 // Tensor-core decode path (attn_decode_tc.cu).
 bool decode_tc_supported(int D, int G);

@@ -74,6 +74,7 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_kv_append_dev": (_I, [_P, _P, _I, _P, _P, _P]),
         "eif_cuda_attend_decode": (_I, [_P, _P, _I, _P, _P, _I, _F, _P, _I, _P, _P]),
         "eif_cuda_attend_decode_dev": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _P, _I, _P, _P]),
+        "eif_cuda_attend_decode_noalloc_dev": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _P, _I, _P, _P]),
         "eif_cuda_delta_alloc": (_I, [_P, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
         "eif_cuda_delta_free": (None, [_P]),
         "eif_cuda_delta_reset": (_I, [_P, _P]),

@@ -147,6 +147,18 @@ eif_status_t eif_cuda_attend_decode_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, 
                                         const float *gate_dev, eif_cuda_subln_t subln, const float *sub_norm_dev,
                                         float *out_dev);
 
+/* Same computation and arguments as eif_cuda_attend_decode_dev, for callers that may not allocate device
+ * memory after start-up (an engine whose device memory is all reserved up front, or one running under a
+ * fixed memory budget).  No counterpart in the reference.  It calls no cudaMalloc / cudaFree: the split-K
+ * partials go to one 16 MiB array compiled into the library (reserved on every GPU that loads it, until
+ * exit); shapes whose partials do not fit even unsplit return EIF_STATUS_INVALID_ARGUMENT.  The first call
+ * on a device looks the array's address up, so make it before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race and must be serialised by the caller. */
+eif_status_t eif_cuda_attend_decode_noalloc_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
+                                                const float *q_dev, const int *pos_dev, int max_pos, int n_heads,
+                                                float scale, const float *gate_dev, eif_cuda_subln_t subln,
+                                                const float *sub_norm_dev, float *out_dev);
+
 /* ---------------------------------------------------------------------------------------------
  * Gated DeltaNet state mirror (qwen35_delta_state_t, include/eif_qwen35.h:199-202)
  * ------------------------------------------------------------------------------------------- */
