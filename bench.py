@@ -435,8 +435,134 @@ def run_reference(args, rank):
             "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+PF_B, PF_S, PF_HQ, PF_HKV, PF_D = 8, 4096, 12, 2, 128
+
+
+def prefill_flops(B, S):
+    """Causal QK^T + PV FLOPs: 2 * B * Hq * D * S * (S + 1)."""
+    return 2.0 * B * PF_HQ * PF_D * S * (S + 1)
+
+
+def cpu_prefill_reference(seconds=20.0):
+    """The reference's fullatt_attend per token (Qwen3.5 prefill_chunk's parallel loop over tokens,
+    src/eif_qwen35.c:1122-1133; gate = +100 -> sigmoid 1, plain), one sequence of the config, tokens
+    spread over the causal range, one token per host thread; scaled by FLOPs to the whole config."""
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as orc
+    ncpu = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(5)
+    kc = rng.standard_normal((PF_S, PF_HKV * PF_D)).astype(np.float32)
+    vc = rng.standard_normal((PF_S, PF_HKV * PF_D)).astype(np.float32)
+    q = rng.standard_normal(PF_HQ * PF_D).astype(np.float32)
+    gate = np.full(PF_HQ * PF_D, 100.0, np.float32)
+    kind = "reference" if orc.ref_available() else "port"
+
+    def one(t):
+        if kind == "reference":
+            orc.ref_fullatt_attend(q, gate, kc, vc, None, 1, t, PF_HQ, PF_HKV, PF_D)
+        else:
+            orc.attend_decode(q, kc, vc, t, PF_HQ, PF_HKV, PF_D, 0.0884)
+        return t
+
+    positions = list(range(PF_S - 1, -1, -PF_S // 256))
+    pool = ThreadPoolExecutor(max_workers=ncpu)
+    done, t0 = [], time.perf_counter()
+    for i in range(0, len(positions), ncpu):
+        done += list(pool.map(one, positions[i:i + ncpu]))
+        if time.perf_counter() - t0 > seconds:
+            break
+    el = time.perf_counter() - t0
+    pool.shutdown()
+    flops_done = sum(4.0 * PF_HQ * PF_D * (t + 1) for t in done)
+    tps = PF_B * PF_S / (el * prefill_flops(PF_B, PF_S) / flops_done)
+    return tps, ncpu, kind, (f"{len(done)} of the {PF_S} query tokens of one sequence (positions spread over the "
+                             f"causal range), one token per host thread, {el:.1f} s; scaled by FLOPs to {PF_B} x {PF_S}")
+
+
+def run_prefill(args, torch, dist, rank, world, local_rank):
+    """causal prefill, batch 8 x 4096 tokens, 12 q / 2 kv heads, head_dim 128, bf16."""
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    torch.cuda.set_device(local_rank)
+    B = max(1, PF_B // world)
+    ctx = pkg.Context(local_rank)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11 + rank)
+    kv = pkg.KVCache(ctx, 1, B, PF_S, PF_HKV, PF_D, pkg.BF16)
+    for p in kv.layer_ptrs(0):
+        torch.as_tensor(CudaArray(p, (B * PF_S * PF_HKV * PF_D,), "<i2"), device=dev).view(torch.bfloat16).normal_(
+            generator=gen)
+    q = torch.randn(B, PF_S, PF_HQ * PF_D, device=dev, generator=gen).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(PF_D)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2: evicts q / K / V between launches
+    for _ in range(args.warmup):
+        kv.attend_prefill_dev(0, q.data_ptr(), PF_S, 0, PF_HQ, scale, out.data_ptr())
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(args.steps)]
+    clocks = ClockSampler(local_rank)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    l0 = ctx.launch_count
+    for s in range(args.steps):
+        flush.zero_()
+        ev[s][0].record()
+        kv.attend_prefill_dev(0, q.data_ptr(), PF_S, 0, PF_HQ, scale, out.data_ptr())
+        ev[s][1].record()
+    torch.cuda.synchronize()
+    launches = ctx.launch_count - l0
+    clk = clocks.stop()
+    ctx.synchronize()
+    ms = float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    # e2e through the host-pointer ABI: fp32 q from pinned host memory, fp32 output read back
+    qh = torch.randn(B, PF_S, PF_HQ * PF_D, generator=torch.Generator().manual_seed(3)).pin_memory().numpy()
+    ctx.set_stream(None)
+    kv.attend_prefill(0, qh, PF_S, 0, PF_HQ, scale)
+    t0 = time.perf_counter()
+    for _ in range(max(1, args.steps // 4)):
+        kv.attend_prefill(0, qh, PF_S, 0, PF_HQ, scale)
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / max(1, args.steps // 4)
+    if rank != 0:
+        return None
+    _, tflops_peak, src = peaks()
+    flops = prefill_flops(B, PF_S)
+    ach = flops / (ms * 1e-3) / 1e12
+    GB = B * world
+    line = {"metric": "causal prefill attention tokens/s (BASELINE configs[1])", "value": GB * PF_S / (ms * 1e-3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16 in, fp32 accumulate, bf16 out", "data": "synthetic (seeded)",
+            "config": {"workload": "gqa_causal_prefill (BASELINE configs[1])", "global_batch": GB, "seq_len": PF_S,
+                       "heads": "12 q / 2 kv", "head_dim": PF_D, "l2": "256 MiB flush between launches"},
+            "e2e": {"value": B * PF_S / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": qh.nbytes, "d2h_bytes_per_step": qh.nbytes,
+                    "path": "host-pointer C ABI eif_cuda_attend_prefill (fp32 in/out)"},
+            "roofline": {"kernel": "attn_prefill_tc_kernel", "bound": "tensor", "achieved": ach,
+                         "peak": tflops_peak, "unit": "TFLOP/s", "frac": ach / tflops_peak, "peak_source": src,
+                         "algorithmic_flops_per_launch": flops, "traffic": None},
+            "gpu_launches": launches, "clocks": clk}
+    if world == 1 and not args.no_cpu_baseline:
+        tps, cores, kind, sample = cpu_prefill_reference()
+        line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", default="hybrid", choices=["hybrid", "prefill"],
+                    help="hybrid = BASELINE configs[4] (the headline); prefill = configs[1]")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -467,6 +593,14 @@ def main():
         torch.cuda.set_device(local_rank)
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         dist = tdist
+    if args.workload == "prefill":
+        line = run_prefill(args, torch, dist, rank, world, local_rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     line = run_ours(args, torch, dist, rank, world, local_rank)
     if line is not None and world == 1 and not args.no_cpu_baseline:
         tps, cores, kind, sample, _ = cpu_reference(3, per_round_cap_s=30)

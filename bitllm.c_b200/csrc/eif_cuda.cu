@@ -548,6 +548,87 @@ EIF_API eif_status_t eif_cuda_attend_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *
 }
 
 // =================================================================================================
+// Causal prefill attention
+// =================================================================================================
+
+static eif_status_t prefill_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int n_tok, int start_pos,
+                                  int n_heads) {
+    if (!ctx || !kv || kv->ctx != ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= kv->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    if (n_heads <= 0 || n_heads % kv->n_kv)
+        return fail(ctx, EIF_STATUS_SHAPE_MISMATCH, "n_heads %d is not a multiple of n_kv_heads %d", n_heads, kv->n_kv);
+    if (n_tok < 1 || start_pos < 0 || start_pos + n_tok > kv->max_seq)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rows [%d, %d) outside the cache [0, %d)", start_pos,
+                    start_pos + n_tok, kv->max_seq);
+    if (kv->dtype != EIF_CUDA_BF16 || !prefill_tc_supported(kv->hd))
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "prefill attention needs a bf16 cache with head_dim 128");
+    if ((size_t)kv->batch * n_tok > 0x7fffffffull) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "too many rows");
+    return EIF_STATUS_OK;
+}
+
+// TMA descriptor of the queries [B*n_tok][Hq][hd] bf16: boxes of 64 dims x 1 head x 128 tokens.
+static bool make_q_tensor_map(CUtensorMap *map, const void *q, int rows, int Hq, int hd) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)Hq, (cuuint64_t)rows};
+    const cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)Hq * hd * 2};
+    const cuuint32_t box[3] = {64, 1, 128};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(q), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static eif_status_t prefill_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const void *q_dev, int n_tok,
+                                int start_pos, int n_heads, float scale, void *out_dev) {
+    if ((reinterpret_cast<uintptr_t>(q_dev) | reinterpret_cast<uintptr_t>(out_dev)) & 15)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "prefill: q and out must be 16-byte aligned");
+    DecodeArgs probe{};
+    decode_prepare(kv, layer, probe);  // makes the layer's K / V tensor maps
+    if (!probe.tmk || !probe.tmv) return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "prefill: no TMA descriptors");
+    alignas(64) CUtensorMap tq;
+    if (!make_q_tensor_map(&tq, q_dev, kv->batch * n_tok, n_heads, kv->hd))
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "prefill: cannot describe q for TMA");
+    CK(launch_attend_prefill_tc(ctx->stream, tq, *probe.tmk, *probe.tmv, kv->batch, n_tok, start_pos, n_heads,
+                                kv->n_kv, kv->max_seq, scale, static_cast<__nv_bfloat16 *>(out_dev), ctx->dev_err));
+    ctx->launches += 1;
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_attend_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
+                                                 const void *q_dev, int n_tok, int start_pos, int n_heads,
+                                                 float scale, void *out_dev) {
+    eif_status_t st = prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st != EIF_STATUS_OK) return st;
+    if (!q_dev || !out_dev) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "attend_prefill_dev: NULL pointer");
+    DeviceGuard g(ctx);
+    return prefill_run(ctx, kv, layer, q_dev, n_tok, start_pos, n_heads, scale, out_dev);
+}
+
+EIF_API eif_status_t eif_cuda_attend_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
+                                             int n_tok, int start_pos, int n_heads, float scale, float *out) {
+    eif_status_t st = prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st != EIF_STATUS_OK) return st;
+    if (!q || !out) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "attend_prefill: NULL pointer");
+    DeviceGuard g(ctx);
+    const size_t n = (size_t)kv->batch * n_tok * n_heads * kv->hd;
+    Carver cv;
+    const size_t o_f = cv.take(n * 4), o_q = cv.take(n * 2), o_o = cv.take(n * 2);
+    st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (st != EIF_STATUS_OK) return st;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_f, q, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(launch_f32_to_bf16(ctx->stream, reinterpret_cast<float *>(s + o_f), reinterpret_cast<__nv_bfloat16 *>(s + o_q), n));
+    ctx->launches += 1;
+    st = prefill_run(ctx, kv, layer, s + o_q, n_tok, start_pos, n_heads, scale, s + o_o);
+    if (st != EIF_STATUS_OK) return st;
+    CK(launch_bf16_to_f32(ctx->stream, reinterpret_cast<__nv_bfloat16 *>(s + o_o), reinterpret_cast<float *>(s + o_f), n));
+    ctx->launches += 1;
+    CK(cudaMemcpyAsync(out, s + o_f, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// =================================================================================================
 // DeltaNet state
 // =================================================================================================
 

@@ -82,6 +82,12 @@ struct DecodeArgs {
     size_t max_ws_bytes = 0;  // 0: the split may use any amount of scratch; else it must fit in this many bytes
 };
 
+// Causal prefill attention on tcgen05 (attn_prefill_tc.cu).
+bool prefill_tc_supported(int D);
+cudaError_t launch_attend_prefill_tc(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
+                                     const CUtensorMap &tv, int B, int n_tok, int start_pos, int Hq, int Hkv,
+                                     int max_seq, float scale, __nv_bfloat16 *out, unsigned *dev_err);
+
 // Fills the TMA descriptors (made on first use per layer) and the kernel choice of `a` (eif_cuda.cu).
 void decode_prepare(eif_cuda_kv_t *kv, int layer, DecodeArgs &a);
 

@@ -75,6 +75,8 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_attend_decode": (_I, [_P, _P, _I, _P, _P, _I, _F, _P, _I, _P, _P]),
         "eif_cuda_attend_decode_dev": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _P, _I, _P, _P]),
         "eif_cuda_attend_decode_noalloc_dev": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _P, _I, _P, _P]),
+        "eif_cuda_attend_prefill": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P]),
+        "eif_cuda_attend_prefill_dev": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P]),
         "eif_cuda_delta_alloc": (_I, [_P, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
         "eif_cuda_delta_free": (None, [_P]),
         "eif_cuda_delta_reset": (_I, [_P, _P]),
@@ -242,6 +244,20 @@ class KVCache:
                                                     float(scale), _ptr(gg), int(subln), _ptr(nn), _ptr(out)),
                        "attend_decode")
         return out
+
+    def attend_prefill(self, layer: int, q, n_tok: int, start_pos: int, n_heads: int, scale: float):
+        """Causal prefill: q [batch][n_tok][n_heads*head_dim] fp32 -> out of the same shape (fp32)."""
+        qq = _f32(q)
+        out = np.zeros((self.batch, n_tok, n_heads * self.head_dim), np.float32)
+        self.ctx.check(lib().eif_cuda_attend_prefill(self.ctx.handle, self._h, layer, _ptr(qq), n_tok, start_pos,
+                                                     n_heads, float(scale), _ptr(out)), "attend_prefill")
+        return out
+
+    def attend_prefill_dev(self, layer: int, q_dev: int, n_tok: int, start_pos: int, n_heads: int, scale: float,
+                           out_dev: int):
+        """bf16 device arrays [batch][n_tok][n_heads*head_dim]; asynchronous on the context's stream."""
+        self.ctx.check(lib().eif_cuda_attend_prefill_dev(self.ctx.handle, self._h, layer, q_dev, n_tok, start_pos,
+                                                         n_heads, float(scale), out_dev), "attend_prefill_dev")
 
     def attend_decode_dev(self, layer: int, q_dev: int, pos_dev: int, max_pos: int, n_heads: int, scale: float,
                           out_dev: int, gate_dev: int | None = None, subln: int = SUBLN_NONE,

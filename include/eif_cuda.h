@@ -147,6 +147,21 @@ eif_status_t eif_cuda_attend_decode_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, 
                                         const float *gate_dev, eif_cuda_subln_t subln, const float *sub_norm_dev,
                                         float *out_dev);
 
+/* ---------------------------------------------------------------------------------------------
+ * Causal prefill attention: n_tok new tokens per sequence at positions start_pos .. start_pos+n_tok-1,
+ * token i attending to cache rows 0 .. start_pos+i.  Replaces the batched prefill attention of
+ * tinyllm_forward_batch_embeddings (src/eif_tinyllm.c:1158-1268) and the per-token fullatt_attend of
+ * Qwen3.5's prefill_chunk (src/eif_qwen35.c:1122-1133, without gate / SubLN).  The chunk's k / v rows must
+ * already be in the cache (kv_upload, kv_append).  Needs a bf16 cache with head_dim 128.
+ *   q   [batch][n_tok][n_heads*head_dim], out the same shape
+ * _dev: bf16 device arrays (16-byte aligned), asynchronous.  Host variant: fp32 host arrays (rounded to
+ * bf16 on the device, the output widened back).
+ * ------------------------------------------------------------------------------------------- */
+eif_status_t eif_cuda_attend_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q, int n_tok,
+                                     int start_pos, int n_heads, float scale, float *out);
+eif_status_t eif_cuda_attend_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const void *q_dev,
+                                         int n_tok, int start_pos, int n_heads, float scale, void *out_dev);
+
 /* Same computation and arguments as eif_cuda_attend_decode_dev, for callers that may not allocate device
  * memory after start-up (an engine whose device memory is all reserved up front, or one running under a
  * fixed memory budget).  No counterpart in the reference.  It calls no cudaMalloc / cudaFree: the split-K

@@ -1,0 +1,94 @@
+"""Causal prefill attention (tcgen05 + TMEM + TMA) through the C ABI against the C restatement of the
+reference's batched prefill loop (src/eif_tinyllm.c:1158-1268), pinned to the reference's
+fullatt_attend by tests/golden/prefill_small.npz.
+
+Inputs are drawn in fp32 and rounded to bf16 (the kernel's input type); the oracle runs in fp32 on the
+same rounded values.  Tolerance for the bf16-in / fp32-accumulate prefill path: rel-L2 <= 1e-2 and
+max-abs <= 2e-2."""
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+REL, ABS = 1e-2, 2e-2
+
+
+def bf16(orc, a):
+    return orc.round_bf16(a).reshape(a.shape)
+
+
+def setup(pkg, ctx, orc, rng, B, rows, max_seq, nkv, hd=128):
+    kv = pkg.KVCache(ctx, 1, B, max_seq, nkv, hd, pkg.BF16)
+    kc = bf16(orc, rng.standard_normal((B, rows, nkv * hd)).astype(np.float32))
+    vc = bf16(orc, rng.standard_normal((B, rows, nkv * hd)).astype(np.float32))
+    for b in range(B):
+        kv.upload(0, b, 0, kc[b], vc[b])
+    return kv, kc, vc
+
+
+@pytest.mark.parametrize("B,n_tok,start_pos,nh,nkv", [(2, 300, 0, 12, 2), (1, 128, 0, 4, 4), (3, 130, 200, 8, 2),
+                                                      (2, 1, 77, 12, 2), (1, 257, 3, 6, 1)])
+def test_prefill_vs_oracle(pkg, ctx, orc, B, n_tok, start_pos, nh, nkv):
+    rng = np.random.default_rng(n_tok * 7 + start_pos)
+    hd = 128
+    rows = start_pos + n_tok
+    kv, kc, vc = setup(pkg, ctx, orc, rng, B, rows, rows + 5, nkv)
+    q = bf16(orc, rng.standard_normal((B, n_tok, nh * hd)).astype(np.float32))
+    scale = 1.0 / np.sqrt(hd)
+    out = kv.attend_prefill(0, q, n_tok, start_pos, nh, scale)
+    for b in range(B):
+        ref = orc.attend_prefill(q[b], kc[b], vc[b], n_tok, start_pos, nh, nkv, hd, scale)
+        assert rel_l2(out[b], ref) <= REL
+        assert np.max(np.abs(out[b] - ref)) <= ABS
+
+
+def test_config2_full_size_sampled(pkg, ctx, orc):
+    """BASELINE config 2 at full size (8 x 4096 tokens, 12 q / 2 kv heads, head_dim 128, causal) on the GPU;
+    64 sampled tokens across sequences and the causal range are recomputed by the oracle."""
+    rng = np.random.default_rng(2)
+    B, S, nh, nkv, hd = 8, 4096, 12, 2, 128
+    kv, kc, vc = setup(pkg, ctx, orc, rng, B, S, S, nkv)
+    q = bf16(orc, rng.standard_normal((B, S, nh * hd)).astype(np.float32))
+    scale = 1.0 / np.sqrt(hd)
+    out = kv.attend_prefill(0, q, S, 0, nh, scale)
+    assert np.all(np.isfinite(out))
+    picks = [(b, t) for b in range(B) for t in (0, 1, 127, 128, 129, 2047, 4094, 4095)]
+    got, want = [], []
+    for b, t in picks:
+        want.append(orc.attend_prefill(q[b, t:t + 1], kc[b], vc[b], 1, t, nh, nkv, hd, scale)[0])
+        got.append(out[b, t])
+    got, want = np.array(got), np.array(want)
+    assert rel_l2(got, want) <= REL
+    assert np.max(np.abs(got - want)) <= ABS
+
+
+def test_prefill_is_causal(pkg, ctx, orc):
+    """Rows after a token never influence it: rewriting cache rows >= 300 (with non-finite values past
+    start_pos + n_tok) leaves tokens < 300 bit-identical."""
+    rng = np.random.default_rng(4)
+    B, n_tok, nh, nkv, hd = 1, 600, 8, 2, 128
+    kv, kc, vc = setup(pkg, ctx, orc, rng, B, n_tok, n_tok + 64, nkv)
+    q = bf16(orc, rng.standard_normal((B, n_tok, nh * hd)).astype(np.float32))
+    a = kv.attend_prefill(0, q, n_tok, 0, nh, 0.0884)
+    junk = rng.standard_normal((n_tok - 300, nkv * hd)).astype(np.float32) * 50
+    kv.upload(0, 0, 300, junk, -junk)
+    tail = np.full((64, nkv * hd), np.nan, np.float32)
+    kv.upload(0, 0, n_tok, tail, tail)
+    b2 = kv.attend_prefill(0, q, n_tok, 0, nh, 0.0884)
+    assert np.array_equal(a[0, :300], b2[0, :300])
+    assert np.all(np.isfinite(b2))
+
+
+def test_prefill_bad_arguments(pkg, ctx):
+    kv32 = pkg.KVCache(ctx, 1, 1, 64, 2, 128, pkg.F32)
+    with pytest.raises(pkg.EifCudaError) as e:
+        kv32.attend_prefill(0, np.zeros((1, 4, 256), np.float32), 4, 0, 2, 0.1)
+    assert e.value.name == "NOT_SUPPORTED"
+    kv = pkg.KVCache(ctx, 1, 1, 64, 2, 128, pkg.BF16)
+    with pytest.raises(pkg.EifCudaError) as e:
+        kv.attend_prefill(0, np.zeros((1, 8, 256), np.float32), 8, 60, 2, 0.1)
+    assert e.value.name == "INVALID_ARGUMENT"
+    with pytest.raises(pkg.EifCudaError) as e:
+        kv.attend_prefill(0, np.zeros((1, 8, 384), np.float32), 8, 0, 3, 0.1)
+    assert e.value.name == "SHAPE_MISMATCH"
