@@ -44,6 +44,39 @@ struct PrefillParams {
     unsigned *dev_err;
 };
 
+// Tile max of scale * s over 32 columns of one row (columns past `lim` masked when MASK).
+template <bool MASK>
+__device__ __forceinline__ void chunk_max(const float (&x)[32], float scale, int lim, float &mt) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+        float v0 = x[i] * scale, v1 = x[i + 1] * scale;
+        if (MASK) {
+            if (i > lim) v0 = -INFINITY;
+            if (i + 1 > lim) v1 = -INFINITY;
+        }
+        mt = fmax3(mt, v0, v1);
+    }
+}
+
+// p = 2^(scale * s - m_use) over 32 columns: packed running sum, bf16 pairs into pk[16].
+template <bool MASK>
+__device__ __forceinline__ void chunk_exp(const float (&x)[32], float scale, float m_use, int lim,
+                                          unsigned long long &sum2, uint32_t (&pk)[16]) {
+    const unsigned long long sc2 = f2_pack(scale, scale), nm2 = f2_pack(-m_use, -m_use);
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+        float v0, v1;
+        f2_unpack(ffma2(f2_pack(x[i], x[i + 1]), sc2, nm2), v0, v1);
+        if (MASK) {
+            if (i > lim) v0 = -INFINITY;
+            if (i + 1 > lim) v1 = -INFINITY;
+        }
+        const float e0 = fast_exp2(v0), e1 = fast_exp2(v1);
+        sum2 = fadd2(sum2, f2_pack(e0, e1));
+        pk[i / 2] = pack_bf16x2(e0, e1);
+    }
+}
+
 // barrier slots (each 8 bytes) in the barrier area
 enum {
     BAR_Q = 0,
@@ -142,35 +175,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
         constexpr uint32_t idesc_qk = umma_idesc_bf16(BM, BN, false, false);
         constexpr uint32_t idesc_pv = umma_idesc_bf16(BM, HD, false, true);
         bool ok = mbar_wait(bar(BAR_Q), 0, p.dev_err);
+        // issue order per step j: S_A(j), PV_A(j-1), S_B(j), PV_B(j-1) -- each tile's PV follows its own S,
+        // so neither softmax warpgroup waits on the other's progress
         for (int j = 0; ok && j <= nkv_all; ++j) {
-            if (j < nkv_all) {
-                const int s = j & 1;
-                if (!mbar_wait(bar(BAR_KFULL + s), (j >> 1) & 1, p.dev_err)) { ok = false; break; }
-                const uint32_t kb = sbase + OFF_K + s * TILE;
-                for (int t = 0; t < 2; ++t) {
-                    if (j >= nkv[t]) continue;
-                    if (!mbar_wait(bar(BAR_SFREE + t), (j & 1) ^ 1, p.dev_err)) { ok = false; break; }
-                    tc_fence_after();
-                    if (lane == 0) {
-                        const uint32_t qb = sbase + t * TILE;
-#pragma unroll
-                        for (int kk = 0; kk < HD / 16; ++kk) {
-                            const uint32_t off = (kk >> 2) * (TILE / 2) + (kk & 3) * 32;
-                            umma_bf16_ss(tmem + t * BN, umma_desc_sw128(qb + off, 16, 1024),
-                                         umma_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0);
-                        }
-                        umma_commit(bar(BAR_SFULL + t));
-                    }
-                    __syncwarp();
-                }
-                if (!ok) break;
-                if (lane == 0) umma_commit(bar(BAR_KEMPTY + s));
-                __syncwarp();
-            }
+            const int s = j & 1, jj = j - 1;
+            if (j < nkv_all && !mbar_wait(bar(BAR_KFULL + s), (j >> 1) & 1, p.dev_err)) { ok = false; break; }
             if (j >= 1) {
-                const int jj = j - 1;
                 if (!mbar_wait(bar(BAR_VFULL), jj & 1, p.dev_err)) { ok = false; break; }
-                const int first_bad = kv_end - jj * BN;  // keys of this tile at or past kv_end
+                const int first_bad = kv_end - jj * BN;  // keys of tile jj at or past kv_end
                 if (first_bad < BN) {
                     // their p is 0, but 0 * (a non-finite stale row) would be NaN: zero those V rows
                     for (int r = max(first_bad, 0); r < BN; ++r)
@@ -181,8 +193,24 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     fence_proxy_async_smem();
                     __syncwarp();
                 }
-                for (int t = 0; t < 2; ++t) {
-                    if (jj >= nkv[t]) continue;
+            }
+            for (int t = 0; t < 2; ++t) {
+                if (j < nkv[t]) {
+                    if (!mbar_wait(bar(BAR_SFREE + t), (j & 1) ^ 1, p.dev_err)) { ok = false; break; }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t qb = sbase + t * TILE, kb = sbase + OFF_K + s * TILE;
+#pragma unroll
+                        for (int kk = 0; kk < HD / 16; ++kk) {
+                            const uint32_t off = (kk >> 2) * (TILE / 2) + (kk & 3) * 32;
+                            umma_bf16_ss(tmem + t * BN, umma_desc_sw128(qb + off, 16, 1024),
+                                         umma_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0);
+                        }
+                        umma_commit(bar(BAR_SFULL + t));
+                    }
+                    __syncwarp();
+                }
+                if (j >= 1 && jj < nkv[t]) {
                     if (!mbar_wait(bar(BAR_PFULL + t), jj & 1, p.dev_err)) { ok = false; break; }
                     tc_fence_after();
                     if (lane == 0) {
@@ -198,10 +226,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     }
                     __syncwarp();
                 }
-                if (!ok) break;
-                if (lane == 0) umma_commit(bar(BAR_VEMPTY));
-                __syncwarp();
             }
+            if (!ok) break;
+            if (lane == 0) {
+                if (j < nkv_all) umma_commit(bar(BAR_KEMPTY + s));
+                if (j >= 1) umma_commit(bar(BAR_VEMPTY));
+            }
+            __syncwarp();
         }
     } else if (warp < 8) {
         // ------------------------------------------------------------------ softmax warps (tile A: 0-3, B: 4-7)
@@ -218,57 +249,31 @@ __global__ void __launch_bounds__(kPThreads, 1)
             tc_fence_after();
             const int kbase = j * BN;
             const bool diag = kbase + BN - 1 > p.start_pos + q0[t];
-            // pass 1: exponentiate 32-column chunks against the running max m and track the tile max;
-            // the row keeps m as its reference while the tile max stays within 2^8 of it
-            const float m_ref = m == -INFINITY ? 0.f : m;
-            float mt = -INFINITY, sum = 0.f;
-            uint32_t pk[BN / 2];
+            const int lim = qpos - kbase;  // diagonal tiles: columns past lim are masked
+            // pass 1: the tile max of scale * s (two packed ALU ops per pair, no exponentials)
+            float mt = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
-                float x[32];
+            for (int c = 0; c < BN / 32; c += 2) {
+                float x[32], y[32];
                 tmem_ld32(s_col + c * 32, x);
+                tmem_ld32(s_col + c * 32 + 32, y);
                 tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    float v0 = x[i] * p.scale_log2, v1 = x[i + 1] * p.scale_log2;
-                    if (diag && kbase + c * 32 + i > qpos) v0 = -INFINITY;
-                    if (diag && kbase + c * 32 + i + 1 > qpos) v1 = -INFINITY;
-                    mt = fmaxf(mt, fmaxf(v0, v1));
-                    const float e0 = fast_exp2(v0 - m_ref), e1 = fast_exp2(v1 - m_ref);
-                    sum += e0 + e1;
-                    pk[c * 16 + i / 2] = pack_bf16x2(e0, e1);
+                if (diag) {
+                    chunk_max<true>(x, p.scale_log2, lim - c * 32, mt);
+                    chunk_max<true>(y, p.scale_log2, lim - c * 32 - 32, mt);
+                } else {
+                    chunk_max<false>(x, p.scale_log2, 0, mt);
+                    chunk_max<false>(y, p.scale_log2, 0, mt);
                 }
             }
-            const bool grow = mt > m + kRescaleLog2;  // always on a row's first unmasked tile (m = -inf)
-            if (__any_sync(0xffffffffu, grow)) {
-                // pass 2, rows whose max grew: exponentiate against the tile max instead
-                const float m_use = mt;
-                float sum2 = 0.f;
-#pragma unroll
-                for (int c = 0; c < BN / 32; ++c) {
-                    float x[32];
-                    tmem_ld32(s_col + c * 32, x);
-                    tmem_wait_ld();
-                    if (grow) {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 2) {
-                            float v0 = x[i] * p.scale_log2, v1 = x[i + 1] * p.scale_log2;
-                            if (diag && kbase + c * 32 + i > qpos) v0 = -INFINITY;
-                            if (diag && kbase + c * 32 + i + 1 > qpos) v1 = -INFINITY;
-                            const float e0 = fast_exp2(v0 - m_use), e1 = fast_exp2(v1 - m_use);
-                            sum2 += e0 + e1;
-                            pk[c * 16 + i / 2] = pack_bf16x2(e0, e1);
-                        }
-                    }
-                }
-                if (grow) sum = sum2;
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(BAR_SFREE + t));
+            // the row keeps its reference max while the tile max stays within 2^8 of it (then every
+            // p <= 256); the first unmasked tile of a row always moves it (m = -inf)
+            const bool grow = m == -INFINITY ? mt > -INFINITY : mt > m + kRescaleLog2;
             const float m_new = grow ? mt : m;
-            const float corr = grow ? fast_exp2(m - m_new) : 1.f;
+            const float m_use = m_new == -INFINITY ? 0.f : m_new;
+            const float corr = grow ? fast_exp2(m - m_use) : 1.f;
             if (j > 0) {
+                // PV(j-1) must be done: it reads the P buffer and accumulates into O
                 if (!mbar_wait(bar(BAR_PEMPTY + t), (j - 1) & 1, p.dev_err)) { ok = false; break; }
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, grow)) {
@@ -284,13 +289,37 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     tmem_wait_st();
                 }
             }
-            // P row -> smem, K-major 128-byte swizzle (the A operand layout of the PV MMA)
+            // pass 2: p = 2^(scale*s - m_use) -> running sum, bf16 P row into smem (K-major 128-byte
+            // swizzle, the A operand layout of the PV MMA), 32 columns at a time
+            unsigned long long sum2 = 0;
+            auto exp_store = [&](const float(&x)[32], int c) {
+                uint32_t pk[16];
+                if (diag)
+                    chunk_exp<true>(x, p.scale_log2, m_use, lim - c * 32, sum2, pk);
+                else
+                    chunk_exp<false>(x, p.scale_log2, m_use, 0, sum2, pk);
 #pragma unroll
-            for (int uu = 0; uu < BN / 8; ++uu) {
-                const int chunk = uu >> 3, ui = uu & 7;
-                *reinterpret_cast<uint4 *>(prow + chunk * (TILE / 2) + ((ui ^ (r & 7)) << 4)) =
-                    make_uint4(pk[uu * 4], pk[uu * 4 + 1], pk[uu * 4 + 2], pk[uu * 4 + 3]);
+                for (int u4 = 0; u4 < 4; ++u4) {
+                    const int uu = c * 4 + u4, chunk = uu >> 3, ui = uu & 7;
+                    *reinterpret_cast<uint4 *>(prow + chunk * (TILE / 2) + ((ui ^ (r & 7)) << 4)) =
+                        make_uint4(pk[u4 * 4], pk[u4 * 4 + 1], pk[u4 * 4 + 2], pk[u4 * 4 + 3]);
+                }
+            };
+#pragma unroll
+            for (int c = 0; c < BN / 32; c += 2) {
+                float x[32], y[32];
+                tmem_ld32(s_col + c * 32, x);
+                tmem_ld32(s_col + c * 32 + 32, y);
+                tmem_wait_ld();
+                exp_store(x, c);
+                exp_store(y, c + 1);
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(BAR_SFREE + t));
+            float s0, s1;
+            f2_unpack(sum2, s0, s1);
+            const float sum = s0 + s1;
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
