@@ -7,19 +7,23 @@
 //
 // One CTA = two 128-row query tiles (A, B) of one (sequence, query head) sharing every K / V tile;
 // 10 warps, warp-specialised:
-//   warp 8      TMA producer: both Q tiles once, then K (two stages) and V (one stage) tiles of 128
-//               keys into 128-byte-swizzled smem (no multicast);
-//   warp 9      MMA issuer, one thread: S_A(j) = Q_A K_j^T, S_B(j) = Q_B K_j^T (tcgen05.mma kind::f16,
-//               M = N = 128, bf16 in, fp32 accumulate in TMEM), then O_A += P_A(j-1) V_{j-1} and
-//               O_B += P_B(j-1) V_{j-1}; completions go to mbarriers through tcgen05.commit;
-//   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: thread r owns query row r; it reads
-//               its S row with tcgen05.ld, masks diagonal tiles, runs the online softmax in base 2,
-//               writes P (bf16) into swizzled smem as the A operand of the next MMA, and rescales its
-//               O row in TMEM only when its running max grew by more than 2^8 (until then the stale
-//               max keeps every p <= 256: the same result, fewer TMEM round trips); at the end
-//               O / l -> bf16 -> global.
-// While one softmax warpgroup works, the tensor cores run the other tile's products.
-// TMEM: S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512).
+//   warp 8      TMA producer: both Q tiles once, then K and V tiles of 128 keys into double-buffered
+//               128-byte-swizzled smem rings (no multicast);
+//   warp 9      MMA issuer, one thread, per key tile j and query tile t in turn:
+//                 O_t += P_t(j-1) V_{j-1}   tcgen05.mma, A = P from TMEM, B = V from smem
+//                 S_t(j) = Q_t K_j^T        tcgen05.mma, A and B from smem
+//               (M = N = 128, bf16 in, fp32 accumulate in TMEM), completions signalled to mbarriers
+//               with tcgen05.commit.  tcgen05.mma ops execute in issue order, so S_t(j) may overwrite
+//               the TMEM columns that held P_t(j-1);
+//   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: thread r owns query row r.  Pass 1
+//               reads its S row with tcgen05.ld and takes the (causally masked) row max; the row keeps
+//               its reference max while a tile's max stays within 2^8 of it (every p <= 256: the same
+//               result, and O is rescaled in TMEM only when the max really moves); pass 2 computes
+//               p = 2^(scale*s - m) with packed f32x2 arithmetic and writes P as bf16 pairs into the
+//               first 64 columns of its own S buffer with tcgen05.st; at the end O / l -> bf16 -> global.
+// The two tiles ping-pong: while one warpgroup runs its softmax the tensor cores run the other
+// tile's PV and S.  P never touches shared memory, so each PV product reads only V from smem.
+// TMEM: S_A (and P_A) [0,128), S_B (P_B) [128,256), O_A [256,384), O_B [384,512).
 // Work order: the longest causal rows first, so the tail is short tiles.
 #include <math.h>
 
@@ -31,8 +35,8 @@ namespace {
 
 constexpr int BM = 128, BN = 128, HD = 128;
 constexpr int kPThreads = 320;
-constexpr int TILE = BM * HD * 2;  // 32 KB: one Q, P, K or V tile (two 64-column swizzled boxes)
-constexpr int OFF_PA = 2 * TILE, OFF_K = 4 * TILE, OFF_V = 6 * TILE, OFF_BAR = 7 * TILE;  // Q_A 0, Q_B TILE, P_B 3*TILE
+constexpr int TILE = BM * HD * 2;  // 32 KB: one Q, K or V tile (two 64-column swizzled boxes)
+constexpr int OFF_Q = 0, OFF_K = 2 * TILE, OFF_V = 4 * TILE, OFF_BAR = 6 * TILE;  // Q_A, Q_B | K[2] | V[2]
 constexpr int kPSmem = OFF_BAR + 256 + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
@@ -61,7 +65,7 @@ __device__ __forceinline__ void chunk_max(const float (&x)[32], float scale, int
 // p = 2^(scale * s - m_use) over 32 columns: packed running sum, bf16 pairs into pk[16].
 template <bool MASK>
 __device__ __forceinline__ void chunk_exp(const float (&x)[32], float scale, float m_use, int lim,
-                                          unsigned long long &sum2, uint32_t (&pk)[16]) {
+                                          unsigned long long &sum2, uint32_t *pk) {
     const unsigned long long sc2 = f2_pack(scale, scale), nm2 = f2_pack(-m_use, -m_use);
 #pragma unroll
     for (int i = 0; i < 32; i += 2) {
@@ -80,14 +84,13 @@ __device__ __forceinline__ void chunk_exp(const float (&x)[32], float scale, flo
 // barrier slots (each 8 bytes) in the barrier area
 enum {
     BAR_Q = 0,
-    BAR_KFULL = 1,   // 2
+    BAR_KFULL = 1,   // 2 stages
     BAR_KEMPTY = 3,  // 2
-    BAR_VFULL = 5,
-    BAR_VEMPTY = 6,
-    BAR_SFULL = 7,   // per tile (A, B)
-    BAR_SFREE = 9,   // per tile
+    BAR_VFULL = 5,   // 2
+    BAR_VEMPTY = 7,  // 2
+    BAR_SFULL = 9,   // per tile (A, B)
     BAR_PFULL = 11,  // per tile
-    BAR_PEMPTY = 13, // per tile (PV of that tile done)
+    BAR_PEMPTY = 13, // per tile: PV of that tile done
     BAR_COUNT = 15
 };
 
@@ -122,13 +125,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
         for (int s = 0; s < 2; ++s) {
             mbar_init(bar(BAR_KFULL + s), 1);
             mbar_init(bar(BAR_KEMPTY + s), 1);
+            mbar_init(bar(BAR_VFULL + s), 1);
+            mbar_init(bar(BAR_VEMPTY + s), 1);
             mbar_init(bar(BAR_SFULL + s), 1);
-            mbar_init(bar(BAR_SFREE + s), 4);
             mbar_init(bar(BAR_PFULL + s), 4);
             mbar_init(bar(BAR_PEMPTY + s), 1);
         }
-        mbar_init(bar(BAR_VFULL), 1);
-        mbar_init(bar(BAR_VEMPTY), 1);
         fence_barrier_init();
     }
     if (warp == 9) {
@@ -150,24 +152,25 @@ __global__ void __launch_bounds__(kPThreads, 1)
             mbar_arrive_expect_tx(bar(BAR_Q), nq * TILE);
             for (int t = 0; t < nq; ++t)
                 for (int d = 0; d < 2; ++d)
-                    tma_load_3d(sbase + t * TILE + d * (TILE / 2), &tmQ, d * 64, h, b * p.n_tok + q0[t], bar(BAR_Q));
+                    tma_load_3d(sbase + OFF_Q + t * TILE + d * (TILE / 2), &tmQ, d * 64, h, b * p.n_tok + q0[t],
+                                bar(BAR_Q));
             for (int j = 0; j < nkv_all; ++j) {
                 const int s = j & 1;
+                const uint32_t par = ((j >> 1) & 1) ^ 1;
                 const int row = b * p.max_seq + j * BN;
-                if (!mbar_wait(bar(BAR_KEMPTY + s), ((j >> 1) & 1) ^ 1, p.dev_err)) break;
+                if (!mbar_wait(bar(BAR_KEMPTY + s), par, p.dev_err)) break;
                 mbar_arrive_expect_tx(bar(BAR_KFULL + s), TILE);
-                const uint32_t kdst = sbase + OFF_K + s * TILE;
+                const uint32_t kdst = sbase + OFF_K + s * TILE, vdst = sbase + OFF_V + s * TILE;
                 for (int d = 0; d < 2; ++d)
                     for (int hf = 0; hf < 2; ++hf)
                         tma_load_3d(kdst + d * (TILE / 2) + hf * (TILE / 4), &tmK, d * 64, kvh, row + hf * 64,
                                     bar(BAR_KFULL + s));
-                if (!mbar_wait(bar(BAR_VEMPTY), (j & 1) ^ 1, p.dev_err)) break;
-                mbar_arrive_expect_tx(bar(BAR_VFULL), TILE);
-                const uint32_t vdst = sbase + OFF_V;
+                if (!mbar_wait(bar(BAR_VEMPTY + s), par, p.dev_err)) break;
+                mbar_arrive_expect_tx(bar(BAR_VFULL + s), TILE);
                 for (int d = 0; d < 2; ++d)
                     for (int hf = 0; hf < 2; ++hf)
                         tma_load_3d(vdst + d * (TILE / 2) + hf * (TILE / 4), &tmV, d * 64, kvh, row + hf * 64,
-                                    bar(BAR_VFULL));
+                                    bar(BAR_VFULL + s));
             }
         }
     } else if (warp == 9) {
@@ -175,31 +178,44 @@ __global__ void __launch_bounds__(kPThreads, 1)
         constexpr uint32_t idesc_qk = umma_idesc_bf16(BM, BN, false, false);
         constexpr uint32_t idesc_pv = umma_idesc_bf16(BM, HD, false, true);
         bool ok = mbar_wait(bar(BAR_Q), 0, p.dev_err);
-        // issue order per step j: S_A(j), PV_A(j-1), S_B(j), PV_B(j-1) -- each tile's PV follows its own S,
-        // so neither softmax warpgroup waits on the other's progress
         for (int j = 0; ok && j <= nkv_all; ++j) {
-            const int s = j & 1, jj = j - 1;
-            if (j < nkv_all && !mbar_wait(bar(BAR_KFULL + s), (j >> 1) & 1, p.dev_err)) { ok = false; break; }
+            const int jj = j - 1;
+            const int s = j & 1, sv = jj & 1;
             if (j >= 1) {
-                if (!mbar_wait(bar(BAR_VFULL), jj & 1, p.dev_err)) { ok = false; break; }
+                if (!mbar_wait(bar(BAR_VFULL + sv), (jj >> 1) & 1, p.dev_err)) { ok = false; break; }
                 const int first_bad = kv_end - jj * BN;  // keys of tile jj at or past kv_end
                 if (first_bad < BN) {
                     // their p is 0, but 0 * (a non-finite stale row) would be NaN: zero those V rows
                     for (int r = max(first_bad, 0); r < BN; ++r)
                         for (int d = 0; d < 2; ++d)
                             if (lane < 8)
-                                reinterpret_cast<uint4 *>(smem + OFF_V + d * (TILE / 2) + r * 128)[lane] =
+                                reinterpret_cast<uint4 *>(smem + OFF_V + sv * TILE + d * (TILE / 2) + r * 128)[lane] =
                                     make_uint4(0, 0, 0, 0);
                     fence_proxy_async_smem();
                     __syncwarp();
                 }
             }
+            if (j < nkv_all && !mbar_wait(bar(BAR_KFULL + s), (j >> 1) & 1, p.dev_err)) { ok = false; break; }
             for (int t = 0; t < 2; ++t) {
-                if (j < nkv[t]) {
-                    if (!mbar_wait(bar(BAR_SFREE + t), (j & 1) ^ 1, p.dev_err)) { ok = false; break; }
+                if (j >= 1 && jj < nkv[t]) {
+                    // O_t += P_t(jj) V_jj once the softmax has written P_t(jj) into TMEM
+                    if (!mbar_wait(bar(BAR_PFULL + t), jj & 1, p.dev_err)) { ok = false; break; }
                     tc_fence_after();
                     if (lane == 0) {
-                        const uint32_t qb = sbase + t * TILE, kb = sbase + OFF_K + s * TILE;
+                        const uint32_t vb = sbase + OFF_V + sv * TILE;
+#pragma unroll
+                        for (int kk = 0; kk < BN / 16; ++kk)
+                            umma_bf16_ts(tmem + (2 + t) * BN, tmem + t * BN + kk * 8,
+                                         umma_desc_sw128(vb + kk * 2048, TILE / 2, 1024), idesc_pv,
+                                         (jj > 0 || kk > 0));
+                        umma_commit(bar(BAR_PEMPTY + t));
+                    }
+                    __syncwarp();
+                }
+                if (j < nkv[t]) {
+                    // S_t(j) = Q_t K_j^T (issued after PV_t(j-1), which read the same TMEM columns)
+                    if (lane == 0) {
+                        const uint32_t qb = sbase + OFF_Q + t * TILE, kb = sbase + OFF_K + s * TILE;
 #pragma unroll
                         for (int kk = 0; kk < HD / 16; ++kk) {
                             const uint32_t off = (kk >> 2) * (TILE / 2) + (kk & 3) * 32;
@@ -210,38 +226,21 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     }
                     __syncwarp();
                 }
-                if (j >= 1 && jj < nkv[t]) {
-                    if (!mbar_wait(bar(BAR_PFULL + t), jj & 1, p.dev_err)) { ok = false; break; }
-                    tc_fence_after();
-                    if (lane == 0) {
-                        const uint32_t pb = sbase + OFF_PA + t * TILE, vb = sbase + OFF_V;
-#pragma unroll
-                        for (int kk = 0; kk < BN / 16; ++kk) {
-                            const uint32_t aoff = (kk >> 2) * (TILE / 2) + (kk & 3) * 32;
-                            umma_bf16_ss(tmem + (2 + t) * BN, umma_desc_sw128(pb + aoff, 16, 1024),
-                                         umma_desc_sw128(vb + kk * 2048, TILE / 2, 1024), idesc_pv,
-                                         (jj > 0 || kk > 0));
-                        }
-                        umma_commit(bar(BAR_PEMPTY + t));
-                    }
-                    __syncwarp();
-                }
             }
             if (!ok) break;
             if (lane == 0) {
                 if (j < nkv_all) umma_commit(bar(BAR_KEMPTY + s));
-                if (j >= 1) umma_commit(bar(BAR_VEMPTY));
+                if (j >= 1) umma_commit(bar(BAR_VEMPTY + sv));
             }
             __syncwarp();
         }
-    } else if (warp < 8) {
+    } else {
         // ------------------------------------------------------------------ softmax warps (tile A: 0-3, B: 4-7)
         const int t = warp >> 2;
         const int r = threadIdx.x & 127;  // query row of the tile == TMEM lane
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t s_col = tmem + lane_base + t * BN, o_col = tmem + lane_base + (2 + t) * BN;
         const int qpos = p.start_pos + q0[t] + r;
-        uint8_t *prow = smem + OFF_PA + t * TILE + r * 128;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nkv[t]; ++j) {
@@ -250,7 +249,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             const int kbase = j * BN;
             const bool diag = kbase + BN - 1 > p.start_pos + q0[t];
             const int lim = qpos - kbase;  // diagonal tiles: columns past lim are masked
-            // pass 1: the tile max of scale * s (two packed ALU ops per pair, no exponentials)
+            // pass 1: the tile max of scale * s
             float mt = -INFINITY;
 #pragma unroll
             for (int c = 0; c < BN / 32; c += 2) {
@@ -266,14 +265,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     chunk_max<false>(y, p.scale_log2, 0, mt);
                 }
             }
-            // the row keeps its reference max while the tile max stays within 2^8 of it (then every
-            // p <= 256); the first unmasked tile of a row always moves it (m = -inf)
+            // the row keeps its reference max while the tile max stays within 2^8 of it; the first
+            // unmasked tile of a row always moves it (m = -inf)
             const bool grow = m == -INFINITY ? mt > -INFINITY : mt > m + kRescaleLog2;
             const float m_new = grow ? mt : m;
             const float m_use = m_new == -INFINITY ? 0.f : m_new;
             const float corr = grow ? fast_exp2(m - m_use) : 1.f;
             if (j > 0) {
-                // PV(j-1) must be done: it reads the P buffer and accumulates into O
+                // PV_t(j-1) has finished (it precedes S_t(j) in the tensor pipe); O may be rescaled
                 if (!mbar_wait(bar(BAR_PEMPTY + t), (j - 1) & 1, p.dev_err)) { ok = false; break; }
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, grow)) {
@@ -289,42 +288,31 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     tmem_wait_st();
                 }
             }
-            // pass 2: p = 2^(scale*s - m_use) -> running sum, bf16 P row into smem (K-major 128-byte
-            // swizzle, the A operand layout of the PV MMA), 32 columns at a time
+            // pass 2: p = 2^(scale*s - m_use), running sum, bf16 P into TMEM columns [0, 64) of S
             unsigned long long sum2 = 0;
-            auto exp_store = [&](const float(&x)[32], int c) {
-                uint32_t pk[16];
-                if (diag)
-                    chunk_exp<true>(x, p.scale_log2, m_use, lim - c * 32, sum2, pk);
-                else
-                    chunk_exp<false>(x, p.scale_log2, m_use, 0, sum2, pk);
-#pragma unroll
-                for (int u4 = 0; u4 < 4; ++u4) {
-                    const int uu = c * 4 + u4, chunk = uu >> 3, ui = uu & 7;
-                    *reinterpret_cast<uint4 *>(prow + chunk * (TILE / 2) + ((ui ^ (r & 7)) << 4)) =
-                        make_uint4(pk[u4 * 4], pk[u4 * 4 + 1], pk[u4 * 4 + 2], pk[u4 * 4 + 3]);
-                }
-            };
 #pragma unroll
             for (int c = 0; c < BN / 32; c += 2) {
                 float x[32], y[32];
                 tmem_ld32(s_col + c * 32, x);
                 tmem_ld32(s_col + c * 32 + 32, y);
                 tmem_wait_ld();
-                exp_store(x, c);
-                exp_store(y, c + 1);
+                uint32_t pk[32];
+                if (diag) {
+                    chunk_exp<true>(x, p.scale_log2, m_use, lim - c * 32, sum2, pk);
+                    chunk_exp<true>(y, p.scale_log2, m_use, lim - c * 32 - 32, sum2, pk + 16);
+                } else {
+                    chunk_exp<false>(x, p.scale_log2, m_use, 0, sum2, pk);
+                    chunk_exp<false>(y, p.scale_log2, m_use, 0, sum2, pk + 16);
+                }
+                tmem_st32u(s_col + (c / 2) * 32, pk);  // columns already read (S keys 0-63 / 64-127)
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(BAR_SFREE + t));
-            float s0, s1;
-            f2_unpack(sum2, s0, s1);
-            const float sum = s0 + s1;
-            fence_proxy_async_smem();
+            tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(BAR_PFULL + t));
-            l = l * corr + sum;
+            float s0, s1;
+            f2_unpack(sum2, s0, s1);
+            l = l * corr + (s0 + s1);
             m = m_new;
         }
         if (ok && nkv[t] > 0 && mbar_wait(bar(BAR_PEMPTY + t), (nkv[t] - 1) & 1, p.dev_err)) {
