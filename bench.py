@@ -40,6 +40,8 @@ sys.path.insert(0, ROOT)
 N_LAYERS = 24
 LAYER_TYPES = ["D", "D", "D", "A"] * 6  # Qwen3.5 layout: full attention every 4th layer
 DN_H, DN_D = 16, 128
+CONV_K = 4
+DN_CONV = 3 * DN_H * DN_D  # conv channels: q, k, v
 AT_HQ, AT_HKV, AT_D = 8, 2, 256
 CTX = 32768
 BATCH = 256
@@ -117,10 +119,30 @@ class CudaArray:
                                          "version": 3, "strides": None}
 
 
-class Hybrid:
-    """Device-resident state and per-layer inputs of the config-5 decode step for `B` sequences."""
+class Weights:
+    """Random-init mixer weights of the stack (seeded; the same on every rank): per DeltaNet layer
+    conv_w, dt_bias, A_log, norm_w; per attention layer q_norm, k_norm, sub_norm."""
 
-    def __init__(self, pkg, ctx, torch, B, seed):
+    def __init__(self, seed=4242):
+        rng = np.random.default_rng(seed)
+        self.dn = [dict(conv_w=(0.5 * rng.standard_normal((DN_CONV, CONV_K))).astype(np.float32),
+                        dt_bias=rng.standard_normal(DN_H).astype(np.float32),
+                        A_log=(0.5 * rng.standard_normal(DN_H)).astype(np.float32),
+                        norm_w=(1 + 0.1 * rng.standard_normal(DN_D)).astype(np.float32))
+                   for _ in range(LAYER_TYPES.count("D"))]
+        self.at = [dict(q_norm=(1 + 0.1 * rng.standard_normal(AT_D)).astype(np.float32),
+                        k_norm=(1 + 0.1 * rng.standard_normal(AT_D)).astype(np.float32),
+                        sub_norm=(1 + 0.1 * rng.standard_normal(AT_HQ * AT_D)).astype(np.float32))
+                   for _ in range(LAYER_TYPES.count("A"))]
+
+
+class Hybrid:
+    """Device-resident state and per-layer inputs of the config-5 decode step for `B` sequences: every
+    DeltaNet layer is the engine's whole deltanet_core (conv window, norms, gates, rule, gated RMSNorm),
+    every attention layer fullatt_prep (norms, partial RoPE, KV append) + fullatt_attend (GQA over the
+    cache, sigmoid gate, SubLN)."""
+
+    def __init__(self, pkg, ctx, torch, B, seed, weights):
         self.pkg, self.ctx, self.torch, self.B = pkg, ctx, torch, B
         dev = torch.device("cuda", torch.cuda.current_device())
         gen = torch.Generator(device=dev)
@@ -128,36 +150,36 @@ class Hybrid:
         n_att = LAYER_TYPES.count("A")
         n_dn = LAYER_TYPES.count("D")
         self.kv = pkg.KVCache(ctx, n_att, B, CTX, AT_HKV, AT_D, pkg.BF16)
-        self.dn = pkg.DeltaState(ctx, n_dn, B, DN_H, DN_D, DN_D)
-        # KV cache ~ N(0,1) bf16, S ~ N(0, 0.02) fp32, filled in place through the library's pointers
+        self.dn = pkg.DeltaState(ctx, n_dn, B, DN_H, DN_D, DN_D, CONV_K)
+        for l, w in enumerate(weights.dn):
+            self.dn.set_weights(l, **w)
+        for l, w in enumerate(weights.at):
+            self.kv.set_norms(l, w["q_norm"], w["k_norm"])
+        # KV cache ~ N(0,1) bf16, S ~ N(0, 0.02), conv windows ~ N(0,1), filled through the library's pointers
         for l in range(n_att):
             for p in self.kv.layer_ptrs(l):
                 t = torch.as_tensor(CudaArray(p, (B * CTX * AT_HKV * AT_D,), "<i2"), device=dev)
                 t.view(torch.bfloat16).normal_(generator=gen)
         for l in range(n_dn):
-            s, _ = self.dn.layer_ptrs(l)
+            s, c = self.dn.layer_ptrs(l)
             torch.as_tensor(CudaArray(s, (B * DN_H * DN_D * DN_D,), "<f4"), device=dev).normal_(0, 0.02,
                                                                                               generator=gen)
-        # per-layer inputs, distributions of BASELINE configs 3 / 5
+            torch.as_tensor(CudaArray(c, (B * DN_CONV * CONV_K,), "<f4"), device=dev).normal_(generator=gen)
+
         def nrm(*shape):
             return torch.randn(*shape, device=dev, generator=gen)
-        self.dn_in = []
-        for l in range(n_dn):
-            qk = nrm(2, B, DN_H, DN_D)
-            qk = qk / torch.sqrt((qk * qk).sum(-1, keepdim=True) + 1e-12)
-            self.dn_in.append(dict(q=qk[0].contiguous(), k=qk[1].contiguous(), v=nrm(B, DN_H * DN_D),
-                                   beta=torch.sigmoid(nrm(B, DN_H)),
-                                   g=-torch.nn.functional.softplus(nrm(B, DN_H))))
-        self.at_in = []
-        for l in range(n_att):
-            self.at_in.append(dict(q=nrm(B, AT_HQ * AT_D), gate=nrm(B, AT_HQ * AT_D), k=nrm(B, AT_HKV * AT_D),
-                                   v=nrm(B, AT_HKV * AT_D)))
-        self.sub_norm = 1.0 + 0.1 * nrm(AT_HQ * AT_D)
+        # per-layer projection outputs (the mixers' inputs), N(0,1)
+        self.dn_in = [dict(qkv=nrm(B, DN_CONV), z=nrm(B, DN_H * DN_D), b=nrm(B, DN_H), a=nrm(B, DN_H))
+                      for _ in range(n_dn)]
+        self.at_in = [dict(qg=nrm(B, AT_HQ * 2 * AT_D), k=nrm(B, AT_HKV * AT_D), v=nrm(B, AT_HKV * AT_D))
+                      for _ in range(n_att)]
+        self.sub_norm = [torch.from_numpy(w["sub_norm"]).to(dev) for w in weights.at]
         self.pos = torch.full((B,), CTX - 1, dtype=torch.int32, device=dev)
+        self.q = torch.empty(B, AT_HQ * AT_D, device=dev)
+        self.gate = torch.empty(B, AT_HQ * AT_D, device=dev)
         self.out = torch.empty(B, AT_HQ * AT_D, device=dev)
         self.dn_out = torch.empty(B, DN_H * DN_D, device=dev)
         self.scale = 1.0 / math.sqrt(AT_D)
-        self.q_scale = 1.0 / math.sqrt(DN_D)
 
     def step(self, att_events=None):
         """One decode step through the `_dev` entry points, asynchronously on the context's stream."""
@@ -165,17 +187,18 @@ class Hybrid:
         for typ in LAYER_TYPES:
             if typ == "D":
                 x = self.dn_in[d]
-                self.dn.step_dev(d, x["q"].data_ptr(), x["k"].data_ptr(), x["v"].data_ptr(), x["beta"].data_ptr(),
-                                 x["g"].data_ptr(), self.q_scale, self.dn_out.data_ptr())
+                self.dn.core_dev(d, x["qkv"].data_ptr(), x["z"].data_ptr(), x["b"].data_ptr(), x["a"].data_ptr(),
+                                 self.dn_out.data_ptr())
                 d += 1
             else:
                 x = self.at_in[a]
-                self.kv.append_dev(a, self.pos.data_ptr(), x["k"].data_ptr(), x["v"].data_ptr())
+                self.kv.fullatt_prep_dev(a, x["qg"].data_ptr(), x["k"].data_ptr(), x["v"].data_ptr(),
+                                         self.pos.data_ptr(), AT_HQ, self.q.data_ptr(), self.gate.data_ptr())
                 if att_events is not None:
                     att_events[a][0].record()
-                self.kv.attend_decode_dev(a, x["q"].data_ptr(), self.pos.data_ptr(), CTX - 1, AT_HQ, self.scale,
-                                          self.out.data_ptr(), gate_dev=x["gate"].data_ptr(),
-                                          subln=self.pkg.SUBLN_WEIGHT, sub_norm_dev=self.sub_norm.data_ptr())
+                self.kv.attend_decode_dev(a, self.q.data_ptr(), self.pos.data_ptr(), CTX - 1, AT_HQ, self.scale,
+                                          self.out.data_ptr(), gate_dev=self.gate.data_ptr(),
+                                          subln=self.pkg.SUBLN_WEIGHT, sub_norm_dev=self.sub_norm[a].data_ptr())
                 if att_events is not None:
                     att_events[a][1].record()
                 a += 1
@@ -184,39 +207,34 @@ class Hybrid:
 class HybridHost:
     """Pinned host inputs / outputs for the end-to-end (host-pointer ABI) measurement."""
 
-    def __init__(self, torch, B, seed):
+    def __init__(self, torch, B, seed, weights):
         rng = np.random.default_rng(seed)
-
-        def pinned(a):
-            t = torch.from_numpy(np.ascontiguousarray(a, np.float32)).pin_memory()
-            return t, t.numpy()
-
-        qk = rng.standard_normal((2, B, DN_H, DN_D)).astype(np.float32)
-        qk /= np.sqrt((qk * qk).sum(-1, keepdims=True) + 1e-12)
         self._keep = []
-        arrs = dict(q=qk[0].reshape(B, -1), k=qk[1].reshape(B, -1),
-                    v=rng.standard_normal((B, DN_H * DN_D)),
-                    beta=1 / (1 + np.exp(-rng.standard_normal((B, DN_H)))),
-                    g=-np.log1p(np.exp(rng.standard_normal((B, DN_H)))),
-                    aq=rng.standard_normal((B, AT_HQ * AT_D)), gate=rng.standard_normal((B, AT_HQ * AT_D)),
-                    ak=rng.standard_normal((B, AT_HKV * AT_D)), av=rng.standard_normal((B, AT_HKV * AT_D)),
-                    sub_norm=1 + 0.1 * rng.standard_normal(AT_HQ * AT_D))
-        self.h = {}
-        for n, a in arrs.items():
-            t, v = pinned(a)
+
+        def pinned(a, dtype=np.float32):
+            t = torch.from_numpy(np.ascontiguousarray(a, dtype)).pin_memory()
             self._keep.append(t)
-            self.h[n] = v
-        tpos = torch.from_numpy(np.full(B, CTX - 1, np.int32)).pin_memory()
-        self._keep.append(tpos)
-        self.pos = tpos.numpy()
+            return t.numpy()
+
+        self.h = dict(qkv=pinned(rng.standard_normal((B, DN_CONV))), z=pinned(rng.standard_normal((B, DN_H * DN_D))),
+                      b=pinned(rng.standard_normal((B, DN_H))), a=pinned(rng.standard_normal((B, DN_H))),
+                      qg=pinned(rng.standard_normal((B, AT_HQ * 2 * AT_D))),
+                      k=pinned(rng.standard_normal((B, AT_HKV * AT_D))),
+                      v=pinned(rng.standard_normal((B, AT_HKV * AT_D))))
+        self.sub_norm = [pinned(w["sub_norm"]) for w in weights.at]
+        self.pos = pinned(np.full(B, CTX - 1), np.int32)
+        h = self.h
         self.h2d = 0
         self.d2h = 0
         for typ in LAYER_TYPES:
             if typ == "D":
-                self.h2d += sum(self.h[n].nbytes for n in ("q", "k", "v", "beta", "g"))
+                self.h2d += h["qkv"].nbytes + h["z"].nbytes + h["b"].nbytes + h["a"].nbytes
                 self.d2h += B * DN_H * DN_D * 4
             else:
-                self.h2d += sum(self.h[n].nbytes for n in ("ak", "av", "aq", "gate", "sub_norm")) + 2 * self.pos.nbytes
+                # fullatt_prep: qg, k, v, pos in; q, gate out -- attend: q, gate, pos, sub_norm in; out out
+                self.h2d += h["qg"].nbytes + h["k"].nbytes + h["v"].nbytes + self.pos.nbytes
+                self.d2h += 2 * B * AT_HQ * AT_D * 4
+                self.h2d += 2 * B * AT_HQ * AT_D * 4 + self.pos.nbytes + self.sub_norm[0].nbytes
                 self.d2h += B * AT_HQ * AT_D * 4
 
     def step(self, hy: Hybrid):
@@ -224,12 +242,12 @@ class HybridHost:
         h = self.h
         for typ in LAYER_TYPES:
             if typ == "D":
-                hy.dn.step(d, h["q"], h["k"], h["v"], h["beta"], h["g"], hy.q_scale)
+                hy.dn.core(d, h["qkv"], h["z"], h["b"], h["a"])
                 d += 1
             else:
-                hy.kv.append(a, self.pos, h["ak"], h["av"])
-                hy.kv.attend_decode(a, h["aq"], self.pos, AT_HQ, hy.scale, gate=h["gate"],
-                                    subln=hy.pkg.SUBLN_WEIGHT, sub_norm=h["sub_norm"])
+                q, g = hy.kv.fullatt_prep(a, h["qg"], h["k"], h["v"], self.pos, AT_HQ)
+                hy.kv.attend_decode(a, q, self.pos, AT_HQ, hy.scale, gate=g, subln=hy.pkg.SUBLN_WEIGHT,
+                                    sub_norm=self.sub_norm[a])
                 a += 1
 
 
@@ -242,7 +260,11 @@ def attn_layer_bytes(B):
 
 
 def deltanet_layer_bytes(B):
-    return 2 * B * DN_H * DN_D * DN_D * 4 + 4 * B * DN_H * DN_D * 4 + 2 * B * DN_H * 4
+    """Algorithmic HBM bytes of one deltanet_core launch: S and the conv windows read + written, the
+    projection outputs (qkv, z, b, a) read, the mixer output written."""
+    state = 2 * B * DN_H * DN_D * DN_D * 4 + 2 * B * DN_CONV * CONV_K * 4
+    io = B * (DN_CONV + DN_H * DN_D + 2 * DN_H + DN_H * DN_D) * 4
+    return state + io
 
 
 def run_ours(args, torch, dist, rank, world, local_rank):
@@ -256,7 +278,8 @@ def run_ours(args, torch, dist, rank, world, local_rank):
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
-    hy = Hybrid(pkg, ctx, torch, B, seed=1234 + rank)
+    weights = Weights()
+    hy = Hybrid(pkg, ctx, torch, B, seed=1234 + rank, weights=weights)
     torch.cuda.synchronize()
 
     for _ in range(args.warmup):
@@ -296,7 +319,7 @@ def run_ours(args, torch, dist, rank, world, local_rank):
     e2e = None
     if not args.no_e2e:
         ctx.set_stream(None)
-        host = HybridHost(torch, B, seed=99 + rank)
+        host = HybridHost(torch, B, seed=99 + rank, weights=weights)
         host.step(hy)  # warm
         if dist:
             dist.barrier()
@@ -344,7 +367,7 @@ def run_ours(args, torch, dist, rank, world, local_rank):
 # ---------------------------------------------------------------------------------------------------
 
 def cpu_reference(n_seq_rounds, threads=None, per_round_cap_s=None):
-    """Time the reference's own deltanet_core x 18 and fullatt_attend x 6 (fp32 KV at ctx 32768, the only
+    """Time the reference's own deltanet_core x 18 and fullatt_prep + fullatt_attend x 6 (fp32 KV at ctx 32768, the only
     KV dtype of its Qwen3.5 engine) for one decode step of independent sequences, one sequence per host
     thread (the reference has no batch dimension; a batch is a loop over engine states).
     Returns (tokens_per_s, cores, kind, sample description)."""
@@ -364,41 +387,39 @@ def cpu_reference(n_seq_rounds, threads=None, per_round_cap_s=None):
     workers = max(1, min(ncpu, int(avail * 0.5 // (kv_bytes + (20 << 20)))))
     rng = np.random.default_rng(77)
     block = rng.standard_normal((4096, AT_HKV * AT_D)).astype(np.float32)
-    conv_dim = 3 * DN_H * DN_D
-    w = dict(conv_w=(rng.standard_normal((conv_dim, 4)) * 0.5).astype(np.float32),
-             dt_bias=rng.standard_normal(DN_H).astype(np.float32),
-             A_log=(0.5 * rng.standard_normal(DN_H)).astype(np.float32),
-             norm_w=(1 + 0.1 * rng.standard_normal(DN_D)).astype(np.float32))
-    x = dict(qkv=rng.standard_normal(conv_dim).astype(np.float32), z=rng.standard_normal(DN_H * DN_D).astype(
+    W = Weights()
+    x = dict(qkv=rng.standard_normal(DN_CONV).astype(np.float32), z=rng.standard_normal(DN_H * DN_D).astype(
         np.float32), b=rng.standard_normal(DN_H).astype(np.float32), a=rng.standard_normal(DN_H).astype(np.float32),
-             q=rng.standard_normal(AT_HQ * AT_D).astype(np.float32),
-             gate=rng.standard_normal(AT_HQ * AT_D).astype(np.float32),
-             sub_norm=(1 + 0.1 * rng.standard_normal(AT_HQ * AT_D)).astype(np.float32))
+             qg=rng.standard_normal(AT_HQ * 2 * AT_D).astype(np.float32),
+             k=rng.standard_normal(AT_HKV * AT_D).astype(np.float32),
+             v=rng.standard_normal(AT_HKV * AT_D).astype(np.float32))
+    lib = orc.ref() if kind == "reference" else None
 
     class Seq:
         def __init__(self):
             self.kc = [np.tile(block, (CTX // 4096, 1)) for _ in range(6)]
             self.vc = [np.tile(block[::-1].copy(), (CTX // 4096, 1)) for _ in range(6)]
             self.S = [(0.02 * block.ravel()[:DN_H * DN_D * DN_D].reshape(DN_H, DN_D, DN_D)).copy() for _ in range(18)]
-            self.conv = [np.zeros((conv_dim, 4), np.float32) for _ in range(18)]
+            self.conv = [np.zeros((DN_CONV, CONV_K), np.float32) for _ in range(18)]
 
         def step(self):
+            # each mixer exactly as the engine calls it: deltanet_core; fullatt_prep then fullatt_attend
             a = d = 0
             for typ in LAYER_TYPES:
                 if typ == "D":
-                    if kind == "reference":
-                        orc.deltanet_core(x["qkv"], x["z"], x["b"], x["a"], self.conv[d], self.S[d], lib=orc.ref(), **w)
-                    else:
-                        orc.deltanet_core(x["qkv"], x["z"], x["b"], x["a"], self.conv[d], self.S[d], **w)
+                    orc.deltanet_core(x["qkv"], x["z"], x["b"], x["a"], self.conv[d], self.S[d], lib=lib, **W.dn[d])
                     d += 1
                 else:
+                    w = W.at[a]
+                    q, g, _ = orc.fullatt_prep(x["qg"], x["k"], x["v"], w["q_norm"], w["k_norm"], self.kc[a],
+                                               self.vc[a], CTX - 1, AT_HQ, AT_HKV, AT_D, lib=lib)
                     if kind == "reference":
-                        orc.ref_fullatt_attend(x["q"], x["gate"], self.kc[a], self.vc[a], x["sub_norm"], 0, CTX - 1,
-                                               AT_HQ, AT_HKV, AT_D)
+                        orc.ref_fullatt_attend(q, g, self.kc[a], self.vc[a], w["sub_norm"], 0, CTX - 1, AT_HQ,
+                                               AT_HKV, AT_D)
                     else:
-                        o = orc.attend_decode(x["q"], self.kc[a], self.vc[a], CTX - 1, AT_HQ, AT_HKV, AT_D,
-                                              1 / 16.0, gate=x["gate"])
-                        orc.subln(o, x["sub_norm"], 2)
+                        o = orc.attend_decode(q, self.kc[a], self.vc[a], CTX - 1, AT_HQ, AT_HKV, AT_D, 1 / 16.0,
+                                              gate=g)
+                        orc.subln(o, w["sub_norm"], 2)
                     a += 1
 
     if kind == "reference":

@@ -5,6 +5,7 @@
 // eif_status_t (include/eif_status.h:8-19 in bitllm.c); there is no CPU fallback.  Host-pointer
 // entry points wait with a deadline (EIF_STATUS_TIMEOUT) instead of blocking forever.
 #include <errno.h>
+#include <math.h>
 #include <sched.h>
 #include <stdarg.h>
 #include <stdlib.h>
@@ -281,6 +282,8 @@ EIF_API eif_status_t eif_cuda_kv_alloc(eif_cuda_ctx_t *ctx, int n_layers, int ba
     kv->tmk = static_cast<CUtensorMap *>(aligned_alloc(64, sizeof(CUtensorMap) * n_layers));
     kv->tmv = static_cast<CUtensorMap *>(aligned_alloc(64, sizeof(CUtensorMap) * n_layers));
     kv->tm_ready = (bool *)calloc(n_layers, sizeof(bool));
+    kv->q_norm = (float **)calloc(n_layers, sizeof(float *));
+    kv->k_norm = (float **)calloc(n_layers, sizeof(float *));
     const size_t bytes = kv->layer_elems * dtype_size(dtype);
     for (int l = 0; l < n_layers; ++l) {
         cudaError_t e = cudaMalloc(&kv->k[l], bytes);
@@ -311,6 +314,7 @@ EIF_API void eif_cuda_kv_free(eif_cuda_kv_t *kv) {
         for (int l = 0; l < kv->n_layers; ++l) {
             if (kv->k && kv->k[l]) cudaFree(kv->k[l]);
             if (kv->v && kv->v[l]) cudaFree(kv->v[l]);
+            if (kv->q_norm && kv->q_norm[l]) cudaFree(kv->q_norm[l]);
         }
     }
     free(kv->k);
@@ -318,6 +322,12 @@ EIF_API void eif_cuda_kv_free(eif_cuda_kv_t *kv) {
     free(kv->tmk);
     free(kv->tmv);
     free(kv->tm_ready);
+    if (kv->rope_cos) {
+        DeviceGuard g(kv->ctx);
+        cudaFree(kv->rope_cos);
+    }
+    free(kv->q_norm);
+    free(kv->k_norm);
     delete kv;
 }
 
@@ -650,6 +660,7 @@ EIF_API eif_status_t eif_cuda_delta_alloc(eif_cuda_ctx_t *ctx, int n_layers, int
     st->conv_dim = 2 * n_heads * d_k + n_heads * d_v;
     st->S = (float **)calloc(n_layers, sizeof(float *));
     st->conv = (float **)calloc(n_layers, sizeof(float *));
+    st->weights = (float **)calloc(n_layers, sizeof(float *));
     const size_t s_bytes = (size_t)batch * n_heads * d_k * d_v * 4;
     const size_t c_bytes = (size_t)batch * st->conv_dim * conv_k * 4;
     for (int l = 0; l < n_layers; ++l) {
@@ -680,10 +691,12 @@ EIF_API void eif_cuda_delta_free(eif_cuda_delta_t *st) {
         for (int l = 0; l < st->n_layers; ++l) {
             if (st->S && st->S[l]) cudaFree(st->S[l]);
             if (st->conv && st->conv[l]) cudaFree(st->conv[l]);
+            if (st->weights && st->weights[l]) cudaFree(st->weights[l]);
         }
     }
     free(st->S);
     free(st->conv);
+    free(st->weights);
     delete st;
 }
 
@@ -787,5 +800,200 @@ EIF_API eif_status_t eif_cuda_deltanet_step(eif_cuda_ctx_t *ctx, eif_cuda_delta_
                   reinterpret_cast<float *>(s + o_g), q_scale, reinterpret_cast<float *>(s + o_o));
     if (rs != EIF_STATUS_OK) return rs;
     CK(cudaMemcpyAsync(o, s + o_o, nv * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// =================================================================================================
+// Whole DeltaNet mixer (deltanet_core)
+// =================================================================================================
+
+EIF_API eif_status_t eif_cuda_delta_set_weights(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer,
+                                                const float *conv_w, const float *dt_bias, const float *A_log,
+                                                const float *norm_w) {
+    if (!ctx || !st || st->ctx != ctx || !conv_w || !dt_bias || !A_log || !norm_w) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= st->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    if (st->conv_k < 1) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "state was allocated without a conv window");
+    DeviceGuard g(ctx);
+    const size_t ncw = (size_t)st->conv_dim * st->conv_k, n = ncw + 2 * st->H + st->dv;
+    if (!st->weights[layer]) CK(cudaMalloc(&st->weights[layer], n * 4));
+    // a_exp = expf(A_log) on the host, exactly as the engine's loader does (src/eif_qwen35.c:1362)
+    float *a_exp = (float *)malloc(sizeof(float) * st->H);
+    for (int h = 0; h < st->H; ++h) a_exp[h] = expf(A_log[h]);
+    float *w = st->weights[layer];
+    cudaError_t e = cudaMemcpyAsync(w, conv_w, ncw * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(w + ncw, dt_bias, st->H * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(w + ncw + st->H, a_exp, st->H * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(w + ncw + 2 * st->H, norm_w, st->dv * 4, cudaMemcpyHostToDevice, ctx->stream);
+    eif_status_t rs = e == cudaSuccess ? wait_stream(ctx) : cuda_fail(ctx, e, "delta_set_weights");
+    free(a_exp);
+    return rs;
+}
+
+static eif_status_t core_check(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer) {
+    if (!ctx || !st || st->ctx != ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= st->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    if (!st->weights[layer]) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "layer %d has no weights (delta_set_weights)", layer);
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t core_run(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *qkv, const float *z,
+                             const float *b_raw, const float *a_raw, float *out) {
+    const size_t ncw = (size_t)st->conv_dim * st->conv_k;
+    const float *w = st->weights[layer];
+    DeltaCoreArgs a{st->S[layer], st->conv[layer], qkv, z, b_raw, a_raw, w, w + ncw, w + ncw + st->H,
+                    w + ncw + 2 * st->H, out, st->batch, st->H, st->dk, st->dv, st->conv_k};
+    bool ok = true;
+    cudaError_t e = launch_deltanet_core(ctx->stream, a, &ok);
+    if (!ok) return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "deltanet_core: d_k %d / d_v %d not supported", st->dk, st->dv);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "deltanet_core launch");
+    ctx->launches += 1;
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_deltanet_core_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer,
+                                                const float *qkv_dev, const float *z_dev, const float *b_dev,
+                                                const float *a_dev, float *out_dev) {
+    eif_status_t rs = core_check(ctx, st, layer);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!qkv_dev || !z_dev || !b_dev || !a_dev || !out_dev)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "deltanet_core_dev: NULL pointer");
+    DeviceGuard g(ctx);
+    return core_run(ctx, st, layer, qkv_dev, z_dev, b_dev, a_dev, out_dev);
+}
+
+EIF_API eif_status_t eif_cuda_deltanet_core(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *qkv,
+                                            const float *z, const float *b_raw, const float *a_raw, float *out) {
+    eif_status_t rs = core_check(ctx, st, layer);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!qkv || !z || !b_raw || !a_raw || !out) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "deltanet_core: NULL pointer");
+    DeviceGuard g(ctx);
+    const size_t B = st->batch, nq = B * st->conv_dim, nz = B * st->H * st->dv, nh = B * st->H;
+    Carver cv;
+    const size_t o_q = cv.take(nq * 4), o_z = cv.take(nz * 4), o_b = cv.take(nh * 4), o_a = cv.take(nh * 4),
+                 o_o = cv.take(nz * 4);
+    rs = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (rs != EIF_STATUS_OK) return rs;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_q, qkv, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_z, z, nz * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_b, b_raw, nh * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_a, a_raw, nh * 4, cudaMemcpyHostToDevice, ctx->stream));
+    rs = core_run(ctx, st, layer, reinterpret_cast<float *>(s + o_q), reinterpret_cast<float *>(s + o_z),
+                  reinterpret_cast<float *>(s + o_b), reinterpret_cast<float *>(s + o_a),
+                  reinterpret_cast<float *>(s + o_o));
+    if (rs != EIF_STATUS_OK) return rs;
+    CK(cudaMemcpyAsync(out, s + o_o, nz * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// =================================================================================================
+// Qwen3.5 attention prep (fullatt_prep)
+// =================================================================================================
+
+EIF_API eif_status_t eif_cuda_kv_set_norms(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_norm,
+                                           const float *k_norm) {
+    if (!ctx || !kv || kv->ctx != ctx || !q_norm || !k_norm) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= kv->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    DeviceGuard g(ctx);
+    if (!kv->q_norm[layer]) {
+        CK(cudaMalloc(&kv->q_norm[layer], 2 * (size_t)kv->hd * 4));
+        kv->k_norm[layer] = kv->q_norm[layer] + kv->hd;
+    }
+    CK(cudaMemcpyAsync(kv->q_norm[layer], q_norm, kv->hd * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(kv->k_norm[layer], k_norm, kv->hd * 4, cudaMemcpyHostToDevice, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// cos / sin of rope_partial (src/eif_qwen35.c:502-535) for every cache row, by the reference's formula:
+// n_rot = head_dim * 0.25, inv_freq_i = 1 / powf(1e7, 2i / n_rot), angle = pos * inv_freq_i.
+static eif_status_t ensure_rope_table(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv) {
+    if (kv->rope_cos) return EIF_STATUS_OK;
+    const int n_rot = (int)(kv->hd * 0.25f), half = n_rot / 2;
+    if (half < 1) return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "head_dim %d too small for partial RoPE", kv->hd);
+    const size_t n = (size_t)kv->max_seq * half;
+    float *hc = (float *)malloc(2 * n * sizeof(float));
+    if (!hc) return fail(ctx, EIF_STATUS_OUT_OF_MEMORY, "rope table");
+    float inv[128];
+    for (int i = 0; i < half && i < 128; ++i) inv[i] = 1.0f / powf(10000000.0f, 2.0f * i / (float)n_rot);
+    for (int pos = 0; pos < kv->max_seq; ++pos)
+        for (int i = 0; i < half; ++i) {
+            const float theta = pos * inv[i];
+            hc[(size_t)pos * half + i] = cosf(theta);
+            hc[n + (size_t)pos * half + i] = sinf(theta);
+        }
+    float *d = nullptr;
+    cudaError_t e = cudaMalloc(&d, 2 * n * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemcpy(d, hc, 2 * n * sizeof(float), cudaMemcpyHostToDevice);
+    free(hc);
+    if (e != cudaSuccess) {
+        if (d) cudaFree(d);
+        return cuda_fail(ctx, e, "rope table");
+    }
+    kv->rope_cos = d;
+    kv->rope_sin = d + n;
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t prep_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int n_heads) {
+    if (!ctx || !kv || kv->ctx != ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= kv->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    if (n_heads <= 0 || n_heads % kv->n_kv)
+        return fail(ctx, EIF_STATUS_SHAPE_MISMATCH, "n_heads %d is not a multiple of n_kv_heads %d", n_heads, kv->n_kv);
+    if (!kv->q_norm[layer]) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "layer %d has no q/k norms (kv_set_norms)", layer);
+    if (kv->hd > 1024) return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "head_dim %d", kv->hd);
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t prep_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg, const float *k,
+                             const float *v, const int *pos, int n_heads, float *q_out, float *gate_out) {
+    eif_status_t rs = ensure_rope_table(ctx, kv);
+    if (rs != EIF_STATUS_OK) return rs;
+    AttnPrepArgs a{qg, k, v, kv->q_norm[layer], kv->k_norm[layer], kv->rope_cos, kv->rope_sin, pos, kv->k[layer],
+                   kv->v[layer], kv->dtype, q_out, gate_out, kv->batch, n_heads, kv->n_kv, kv->hd,
+                   (int)(kv->hd * 0.25f), kv->max_seq, ctx->dev_err};
+    CK(launch_fullatt_prep(ctx->stream, a));
+    ctx->launches += 1;
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_fullatt_prep_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg_dev,
+                                               const float *k_dev, const float *v_dev, const int *pos_dev,
+                                               int n_heads, float *q_out_dev, float *gate_out_dev) {
+    eif_status_t rs = prep_check(ctx, kv, layer, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!qg_dev || !k_dev || !v_dev || !pos_dev || !q_out_dev || !gate_out_dev)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "fullatt_prep_dev: NULL pointer");
+    DeviceGuard g(ctx);
+    return prep_run(ctx, kv, layer, qg_dev, k_dev, v_dev, pos_dev, n_heads, q_out_dev, gate_out_dev);
+}
+
+EIF_API eif_status_t eif_cuda_fullatt_prep(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg,
+                                           const float *k, const float *v, const int *pos, int n_heads,
+                                           float *q_out, float *gate_out) {
+    eif_status_t rs = prep_check(ctx, kv, layer, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!qg || !k || !v || !pos || !q_out || !gate_out)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "fullatt_prep: NULL pointer");
+    for (int b = 0; b < kv->batch; ++b)
+        if (pos[b] < 0 || pos[b] >= kv->max_seq)
+            return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "pos[%d] = %d outside [0, %d)", b, pos[b], kv->max_seq);
+    DeviceGuard g(ctx);
+    const size_t B = kv->batch, nq = B * n_heads * kv->hd, nk = B * kv->n_kv * kv->hd;
+    Carver cv;
+    const size_t o_qg = cv.take(2 * nq * 4), o_k = cv.take(nk * 4), o_v = cv.take(nk * 4), o_p = cv.take(B * 4),
+                 o_q = cv.take(nq * 4), o_g = cv.take(nq * 4);
+    rs = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (rs != EIF_STATUS_OK) return rs;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_qg, qg, 2 * nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_k, k, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_v, v, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_p, pos, B * 4, cudaMemcpyHostToDevice, ctx->stream));
+    rs = prep_run(ctx, kv, layer, reinterpret_cast<float *>(s + o_qg), reinterpret_cast<float *>(s + o_k),
+                  reinterpret_cast<float *>(s + o_v), reinterpret_cast<int *>(s + o_p), n_heads,
+                  reinterpret_cast<float *>(s + o_q), reinterpret_cast<float *>(s + o_g));
+    if (rs != EIF_STATUS_OK) return rs;
+    CK(cudaMemcpyAsync(q_out, s + o_q, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaMemcpyAsync(gate_out, s + o_g, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return wait_stream(ctx);
 }

@@ -48,6 +48,9 @@ struct eif_cuda_kv {
     CUtensorMap *tmk = nullptr;
     CUtensorMap *tmv = nullptr;
     bool *tm_ready = nullptr;
+    // Qwen3.5 attention prep: per-layer q_norm / k_norm [hd] and the partial-RoPE cos / sin table
+    float **q_norm = nullptr, **k_norm = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr;  // [max_seq][hd/8], theta 1e7 (made on first use)
 };
 
 struct eif_cuda_delta {
@@ -55,6 +58,9 @@ struct eif_cuda_delta {
     int n_layers = 0, batch = 0, H = 0, dk = 0, dv = 0, conv_k = 0, conv_dim = 0;
     float **S = nullptr;     // [n_layers] -> [batch][H][dk][dv]
     float **conv = nullptr;  // [n_layers] -> [batch][conv_dim][conv_k] (nullptr when conv_k == 0)
+    // per-layer weights of deltanet_core, uploaded by eif_cuda_delta_set_weights: one device block
+    // [conv_dim*conv_k | H dt_bias | H exp(A_log) | dv norm_w]
+    float **weights = nullptr;
 };
 
 // ---- launchers (return cudaError_t of the launch) ----
@@ -81,6 +87,29 @@ struct DecodeArgs {
     bool force_simt = false;
     size_t max_ws_bytes = 0;  // 0: the split may use any amount of scratch; else it must fit in this many bytes
 };
+
+// Fused per-token mixer bodies (mixer_fused.cu).
+struct DeltaCoreArgs {
+    float *S, *conv;  // layer state [B][H][dk][dv], conv windows [B][conv_dim][conv_k]
+    const float *qkv, *z, *b_raw, *a_raw;  // [B][conv_dim], [B][H*dv], [B][H], [B][H]
+    const float *conv_w, *dt_bias, *a_exp, *norm_w;  // layer weights: [conv_dim][conv_k], [H], [H], [dv]
+    float *out;  // [B][H*dv]
+    int B, H, dk, dv, conv_k;
+};
+cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *supported);
+
+struct AttnPrepArgs {
+    const float *qg, *k, *v;  // [B][nh][2*hd], [B][nkv*hd], [B][nkv*hd]
+    const float *q_norm, *k_norm;  // [hd]
+    const float *rope_cos, *rope_sin;  // [max_seq][n_rot/2]
+    const int *pos;  // [B]
+    void *Kc, *Vc;   // layer cache
+    eif_cuda_dtype_t dtype;
+    float *q_out, *gate_out;  // [B][nh*hd]
+    int B, nh, nkv, hd, n_rot, max_seq;
+    unsigned *dev_err;
+};
+cudaError_t launch_fullatt_prep(cudaStream_t st, const AttnPrepArgs &a);
 
 // Causal prefill attention on tcgen05 (attn_prefill_tc.cu).
 bool prefill_tc_supported(int D);

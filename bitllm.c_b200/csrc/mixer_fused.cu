@@ -1,0 +1,224 @@
+// mixer_fused.cu -- the whole per-token Qwen3.5 token-mixer bodies as single kernels.
+//
+// deltanet_core_kernel: deltanet_core (src/eif_qwen35.c:546-656) for one token of every sequence:
+//   causal conv1d over the sliding window + SiLU (:560-572), per-head L2 norm of q and k, q scaled by
+//   1/sqrt(d_k) (:579-585), beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias) (:587-592), the
+//   delta rule (:594-639) and the gated RMSNorm o * rsqrt(mean(o^2) + 1e-6) * norm_w * silu(z)
+//   (:642-653).  One CTA per (sequence, head): it owns that head's q, k and v conv channels (so every
+//   conv-window row is updated by exactly one CTA) and all d_v columns of S (so the RMSNorm of the
+//   head's output row closes inside the CTA).  S makes one trip HBM -> registers -> HBM.
+//
+// fullatt_prep_kernel: fullatt_prep (src/eif_qwen35.c:699-737) for one token of every sequence:
+//   split the interleaved [q | gate] heads, RMSNorm q and k per head with q_norm / k_norm (eps 1e-6),
+//   rotate the first head_dim/4 dims of q and k (half-split pairs, theta 1e7: rope_partial,
+//   :502-535) with a cos / sin table computed on the host by the reference's formula, and write k, v
+//   into cache row pos[b].
+#include <math.h>
+
+#include "internal.h"
+#include "common.cuh"
+
+namespace {
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+template <int DK, int DV, int THREADS>
+__global__ void __launch_bounds__(THREADS) deltanet_core_kernel(const DeltaCoreArgs a) {
+    constexpr int LPR = DV / 4;        // threads per S row (float4 each)
+    constexpr int RP = THREADS / LPR;  // rows per pass
+    constexpr int NP = DK / RP;        // passes
+    constexpr int NW = THREADS / 32;
+    static_assert(LPR <= 32 && 32 % LPR == 0 && DK % RP == 0, "tile shape");
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int H = a.H;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lc = tid % LPR, rg = tid / LPR;
+    const size_t bh = (size_t)b * H + h;
+    const int key_dim = H * DK, conv_dim = 2 * key_dim + H * DV;
+
+    __shared__ float sq[DK], sk[DK], sv[DV];
+    __shared__ float red[NW];
+    __shared__ float4 cred[NW][LPR];
+    __shared__ float gates[2];
+
+    float *Sh = a.S + bh * DK * DV;
+    const int col0 = lc * 4;
+    float4 s[NP];
+#pragma unroll
+    for (int p = 0; p < NP; ++p) s[p] = __ldcs(reinterpret_cast<const float4 *>(Sh + (size_t)(rg + p * RP) * DV + col0));
+
+    // causal conv1d + SiLU on this head's channels: q [h*DK, +DK), k [key_dim + h*DK, +DK), v [2*key_dim + h*DV, +DV)
+    const int ck = a.conv_k;
+    for (int i = tid; i < 2 * DK + DV; i += THREADS) {
+        const int c = i < DK ? h * DK + i : (i < 2 * DK ? key_dim + h * DK + (i - DK) : 2 * key_dim + h * DV + (i - 2 * DK));
+        float *row = a.conv + ((size_t)b * conv_dim + c) * ck;
+        const float *w = a.conv_w + (size_t)c * ck;
+        const float xin = a.qkv[(size_t)b * conv_dim + c];
+        float acc = 0.f;
+        for (int j = 0; j < ck - 1; ++j) {
+            const float v = row[j + 1];
+            row[j] = v;
+            acc += v * w[j];
+        }
+        row[ck - 1] = xin;
+        acc += xin * w[ck - 1];
+        const float y = silu_f(acc);
+        if (i < DK) sq[i] = y;
+        else if (i < 2 * DK) sk[i - DK] = y;
+        else sv[i - 2 * DK] = y;
+    }
+    if (tid == 0) {
+        gates[0] = 1.0f / (1.0f + expf(-a.b_raw[bh]));
+        const float x = a.a_raw[bh] + a.dt_bias[h];
+        gates[1] = -a.a_exp[h] * logf(1.0f + expf(x));
+    }
+    __syncthreads();
+
+    auto block_sum = [&](float x) -> float {
+        x = warp_sum(x);
+        if (lane == 0) red[warp] = x;
+        __syncthreads();
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) t += red[w];
+        __syncthreads();
+        return t;
+    };
+    // L2 norms (eps 1e-12 inside the root), q also scaled by 1/sqrt(d_k)
+    float pq = 0.f, pk = 0.f;
+    for (int i = tid; i < DK; i += THREADS) {
+        pq += sq[i] * sq[i];
+        pk += sk[i] * sk[i];
+    }
+    const float ssq = block_sum(pq), ssk = block_sum(pk);
+    const float iq = 1.0f / sqrtf(ssq + 1e-12f), ik = 1.0f / sqrtf(ssk + 1e-12f);
+    const float q_scale = 1.0f / sqrtf((float)DK);
+    for (int i = tid; i < DK; i += THREADS) {
+        sq[i] = sq[i] * iq * q_scale;
+        sk[i] = sk[i] * ik;
+    }
+    __syncthreads();
+
+    auto colsum = [&](float4 x) -> float4 {
+#pragma unroll
+        for (int off = LPR; off < 32; off <<= 1) x = f4_add(x, f4_shfl_xor(x, off));
+        if (lane < LPR) cred[warp][lc] = x;
+        __syncthreads();
+        float4 t = cred[0][lc];
+#pragma unroll
+        for (int w = 1; w < NW; ++w) t = f4_add(t, cred[w][lc]);
+        __syncthreads();
+        return t;
+    };
+
+    const float decay = expf(gates[1]), bet = gates[0];
+    float4 e = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+        const float ki = sk[rg + p * RP];
+        s[p].x *= decay; s[p].y *= decay; s[p].z *= decay; s[p].w *= decay;
+        e.x += s[p].x * ki; e.y += s[p].y * ki; e.z += s[p].z * ki; e.w += s[p].w * ki;
+    }
+    e = colsum(e);
+    const float4 vv = make_float4(sv[col0], sv[col0 + 1], sv[col0 + 2], sv[col0 + 3]);
+    const float4 dlt = make_float4(vv.x - e.x, vv.y - e.y, vv.z - e.z, vv.w - e.w);
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+        const int i = rg + p * RP;
+        const float ki = bet * sk[i];
+        s[p].x += ki * dlt.x; s[p].y += ki * dlt.y; s[p].z += ki * dlt.z; s[p].w += ki * dlt.w;
+        __stcs(reinterpret_cast<float4 *>(Sh + (size_t)i * DV + col0), s[p]);
+        const float qi = sq[i];
+        o.x += s[p].x * qi; o.y += s[p].y * qi; o.z += s[p].z * qi; o.w += s[p].w * qi;
+    }
+    o = colsum(o);
+    // gated RMSNorm over the head's d_v outputs (threads of row group 0 hold the whole row)
+    float pss = rg == 0 ? o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w : 0.f;
+    const float ss = block_sum(pss);
+    if (rg == 0) {
+        const float rms = 1.0f / sqrtf(ss / DV + 1e-6f);
+        const float *z = a.z + bh * DV + col0;
+        const float *nw = a.norm_w + col0;
+        float4 y;
+        y.x = o.x * rms * nw[0] * silu_f(z[0]);
+        y.y = o.y * rms * nw[1] * silu_f(z[1]);
+        y.z = o.z * rms * nw[2] * silu_f(z[2]);
+        y.w = o.w * rms * nw[3] * silu_f(z[3]);
+        *reinterpret_cast<float4 *>(a.out + bh * DV + col0) = y;
+    }
+}
+
+// One CTA per sequence.
+__global__ void __launch_bounds__(256) fullatt_prep_kernel(const AttnPrepArgs a) {
+    const int b = blockIdx.x;
+    const int hd = a.hd, nh = a.nh, nkv = a.nkv, n_rot = a.n_rot, half = n_rot / 2;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int p = a.pos[b];
+    const bool pos_ok = p >= 0 && p < a.max_seq;
+    if (!pos_ok && tid == 0) atomicOr(a.dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
+    const float *cs = a.rope_cos + (size_t)(pos_ok ? p : 0) * half;
+    const float *sn = a.rope_sin + (size_t)(pos_ok ? p : 0) * half;
+    // one warp per head: q heads then k heads
+    for (int hh = warp; hh < nh + nkv; hh += nw) {
+        const bool isq = hh < nh;
+        const int hi = isq ? hh : hh - nh;
+        const float *src = isq ? a.qg + ((size_t)b * nh + hi) * 2 * hd : a.k + ((size_t)b * nkv + hi) * hd;
+        const float *wn = isq ? a.q_norm : a.k_norm;
+        float ss = 0.f;
+        for (int i = lane; i < hd; i += 32) ss += src[i] * src[i];
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / hd + 1e-6f);
+        float *dst = isq ? a.q_out + ((size_t)b * nh + hi) * hd : nullptr;
+        for (int i = lane; i < hd; i += 32) {
+            float y = src[i] * inv * wn[i];
+            if (i < n_rot) {
+                // rotated pair (i, i + half) within the first n_rot dims
+                const int j = i < half ? i : i - half;
+                const float x0 = src[j] * inv * wn[j], x1 = src[j + half] * inv * wn[j + half];
+                y = i < half ? x0 * cs[j] - x1 * sn[j] : x0 * sn[j] + x1 * cs[j];
+            }
+            if (isq) {
+                dst[i] = y;
+            } else if (pos_ok) {
+                const size_t row = (((size_t)b * a.max_seq + p) * nkv + hi) * hd + i;
+                if (a.dtype == EIF_CUDA_F32)
+                    static_cast<float *>(a.Kc)[row] = y;
+                else
+                    static_cast<__nv_bfloat16 *>(a.Kc)[row] = __float2bfloat16_rn(y);
+            }
+        }
+        if (isq)
+            for (int i = lane; i < hd; i += 32) a.gate_out[((size_t)b * nh + hi) * hd + i] = src[hd + i];
+    }
+    if (pos_ok)
+        for (int i = tid; i < nkv * hd; i += blockDim.x) {
+            const size_t row = ((size_t)b * a.max_seq + p) * nkv * hd + i;
+            const float v = a.v[(size_t)b * nkv * hd + i];
+            if (a.dtype == EIF_CUDA_F32)
+                static_cast<float *>(a.Vc)[row] = v;
+            else
+                static_cast<__nv_bfloat16 *>(a.Vc)[row] = __float2bfloat16_rn(v);
+        }
+}
+
+}  // namespace
+
+cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *supported) {
+    *supported = true;
+    const dim3 grid(a.H, a.B);
+    if (a.dk == 128 && a.dv == 128)
+        deltanet_core_kernel<128, 128, 256><<<grid, 256, 0, st>>>(a);
+    else if (a.dk == 64 && a.dv == 64)
+        deltanet_core_kernel<64, 64, 128><<<grid, 128, 0, st>>>(a);
+    else {
+        *supported = false;
+        return cudaSuccess;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fullatt_prep(cudaStream_t st, const AttnPrepArgs &a) {
+    fullatt_prep_kernel<<<a.B, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}

@@ -85,6 +85,12 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_delta_layer_ptrs": (_I, [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
         "eif_cuda_deltanet_step": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _F, _P]),
         "eif_cuda_deltanet_step_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _F, _P]),
+        "eif_cuda_delta_set_weights": (_I, [_P, _P, _I, _P, _P, _P, _P]),
+        "eif_cuda_deltanet_core": (_I, [_P, _P, _I, _P, _P, _P, _P, _P]),
+        "eif_cuda_deltanet_core_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _P]),
+        "eif_cuda_kv_set_norms": (_I, [_P, _P, _I, _P, _P]),
+        "eif_cuda_fullatt_prep": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P, _P]),
+        "eif_cuda_fullatt_prep_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -245,6 +251,25 @@ class KVCache:
                        "attend_decode")
         return out
 
+    def set_norms(self, layer: int, q_norm, k_norm):
+        """Per-layer q_norm / k_norm [head_dim] of the Qwen3.5 attention prep."""
+        qn, kn = _f32(q_norm), _f32(k_norm)
+        self.ctx.check(lib().eif_cuda_kv_set_norms(self.ctx.handle, self._h, layer, _ptr(qn), _ptr(kn)), "kv_set_norms")
+
+    def fullatt_prep(self, layer: int, qg, k, v, pos, n_heads: int):
+        """fullatt_prep for one token per sequence: returns (q, gate) [batch][n_heads*head_dim]; writes k, v
+        (normed and rotated k) into cache row pos[b]."""
+        qq, kk, vv, pp = _f32(qg), _f32(k), _f32(v), _i32(pos)
+        q = np.zeros((self.batch, n_heads * self.head_dim), np.float32)
+        g = np.zeros_like(q)
+        self.ctx.check(lib().eif_cuda_fullatt_prep(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv),
+                                                   _ptr(pp), n_heads, _ptr(q), _ptr(g)), "fullatt_prep")
+        return q, g
+
+    def fullatt_prep_dev(self, layer: int, qg_dev, k_dev, v_dev, pos_dev, n_heads: int, q_out_dev, gate_out_dev):
+        self.ctx.check(lib().eif_cuda_fullatt_prep_dev(self.ctx.handle, self._h, layer, qg_dev, k_dev, v_dev, pos_dev,
+                                                       n_heads, q_out_dev, gate_out_dev), "fullatt_prep_dev")
+
     def attend_prefill(self, layer: int, q, n_tok: int, start_pos: int, n_heads: int, scale: float):
         """Causal prefill: q [batch][n_tok][n_heads*head_dim] fp32 -> out of the same shape (fp32)."""
         qq = _f32(q)
@@ -319,6 +344,24 @@ class DeltaState:
         self.ctx.check(lib().eif_cuda_deltanet_step(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv),
                                                     _ptr(bb), _ptr(gg), float(q_scale), _ptr(o)), "deltanet_step")
         return o
+
+    def set_weights(self, layer: int, conv_w, dt_bias, A_log, norm_w):
+        """Per-layer weights of deltanet_core: conv_w [conv_dim][conv_k], dt_bias [H], A_log [H], norm_w [d_v]."""
+        a = [_f32(x) for x in (conv_w, dt_bias, A_log, norm_w)]
+        self.ctx.check(lib().eif_cuda_delta_set_weights(self.ctx.handle, self._h, layer, *[_ptr(x) for x in a]),
+                       "delta_set_weights")
+
+    def core(self, layer: int, qkv, z, b_raw, a_raw):
+        """deltanet_core for one token of every sequence: returns out [batch][H*d_v]."""
+        a = [_f32(x) for x in (qkv, z, b_raw, a_raw)]
+        out = np.zeros((self.batch, self.H * self.dv), np.float32)
+        self.ctx.check(lib().eif_cuda_deltanet_core(self.ctx.handle, self._h, layer, *[_ptr(x) for x in a], _ptr(out)),
+                       "deltanet_core")
+        return out
+
+    def core_dev(self, layer: int, qkv_dev, z_dev, b_dev, a_dev, out_dev):
+        self.ctx.check(lib().eif_cuda_deltanet_core_dev(self.ctx.handle, self._h, layer, qkv_dev, z_dev, b_dev, a_dev,
+                                                        out_dev), "deltanet_core_dev")
 
     def step_dev(self, layer: int, q_dev, k_dev, v_dev, beta_dev, g_dev, q_scale: float, o_dev):
         self.ctx.check(lib().eif_cuda_deltanet_step_dev(self.ctx.handle, self._h, layer, q_dev, k_dev, v_dev,

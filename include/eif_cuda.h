@@ -206,6 +206,39 @@ eif_status_t eif_cuda_deltanet_step_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *s
                                         const float *k_dev, const float *v_dev, const float *beta_dev,
                                         const float *g_dev, float q_scale, float *o_dev);
 
+/*
+ * The whole DeltaNet mixer of one token per sequence after the input projections: deltanet_core
+ * (src/eif_qwen35.c:546-656) -- causal conv1d over the window + SiLU, q/k L2 norm, q *= 1/sqrt(d_k),
+ * beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias), the delta rule, gated RMSNorm.
+ * The layer's weights come first (eif_cuda_delta_set_weights); the state needs conv_k > 0.
+ *   qkv [batch][2*H*d_k + H*d_v] (the qkv projection, conv input), z [batch][H*d_v],
+ *   b_raw, a_raw [batch][H] (proj_b / proj_a outputs), out [batch][H*d_v] (input of out_proj)
+ * Supported: d_k = d_v = 128 (Qwen3.5) or 64.
+ */
+eif_status_t eif_cuda_delta_set_weights(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer,
+                                        const float *conv_w /*[conv_dim][conv_k]*/, const float *dt_bias /*[H]*/,
+                                        const float *A_log /*[H]*/, const float *norm_w /*[d_v]*/);
+eif_status_t eif_cuda_deltanet_core(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *qkv,
+                                    const float *z, const float *b_raw, const float *a_raw, float *out);
+eif_status_t eif_cuda_deltanet_core_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *qkv_dev,
+                                        const float *z_dev, const float *b_dev, const float *a_dev, float *out_dev);
+
+/*
+ * Qwen3.5 attention prep of one token per sequence: fullatt_prep (src/eif_qwen35.c:699-737) -- split the
+ * interleaved [q | gate] heads, RMSNorm q and k per head with the layer's q_norm / k_norm (eps 1e-6),
+ * partial RoPE on the first head_dim/4 dims (theta 1e7, rope_partial :502-535; the cos / sin table is
+ * computed once on the host by the reference's formula), and write k, v into cache row pos[b].
+ *   qg [batch][n_heads][2*head_dim], k, v [batch][n_kv*head_dim], pos [batch]
+ *   q_out, gate_out [batch][n_heads*head_dim] (the inputs of eif_cuda_attend_decode)
+ */
+eif_status_t eif_cuda_kv_set_norms(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_norm,
+                                   const float *k_norm);
+eif_status_t eif_cuda_fullatt_prep(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg, const float *k,
+                                   const float *v, const int *pos, int n_heads, float *q_out, float *gate_out);
+eif_status_t eif_cuda_fullatt_prep_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg_dev,
+                                       const float *k_dev, const float *v_dev, const int *pos_dev, int n_heads,
+                                       float *q_out_dev, float *gate_out_dev);
+
 #ifdef __cplusplus
 }
 #endif

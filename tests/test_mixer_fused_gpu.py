@@ -1,0 +1,110 @@
+"""The whole Qwen3.5 mixer bodies through the C ABI: deltanet_core (src/eif_qwen35.c:546-656) and
+fullatt_prep (src/eif_qwen35.c:699-737) -> attend (gate + SubLN), against the reference's own outputs
+(tests/golden/*.npz, recorded from the compiled reference) and the C restatement.  fp32 paths:
+rel-L2 <= 1e-5."""
+import numpy as np
+import pytest
+
+from conftest import golden, rel_l2
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+@pytest.mark.parametrize("name", ["deltanet_core_h2d128.npz", "deltanet_core_h3d64.npz"])
+def test_deltanet_core_golden(pkg, ctx, name):
+    """Consecutive tokens through the reference's deltanet_core (conv window, norms, gates, rule, gated
+    RMSNorm); the same tokens through eif_cuda_deltanet_core, state carried on the device."""
+    d = golden(name)
+    H, dk, dv, ck, n = (int(x) for x in d["meta"])
+    st = pkg.DeltaState(ctx, 1, 1, H, dk, dv, ck)
+    st.set_weights(0, d["conv_w"], d["dt_bias"], d["A_log"], d["norm_w"])
+    st.upload(0, 0, S=d["S0"], conv_state=d["conv0"])
+    outs = [st.core(0, d["qkv"][t][None], d["z"][t][None], d["b"][t][None], d["a"][t][None])[0] for t in range(n)]
+    assert rel_l2(np.stack(outs), d["out"]) <= TOL
+    S, conv = st.download(0, 0)
+    assert rel_l2(S, d["S_final"]) <= TOL
+    assert rel_l2(conv, d["conv_final"]) <= TOL
+
+
+def test_deltanet_core_batched_vs_port(pkg, ctx, orc):
+    """Qwen3.5-0.8B mixer shape (16 heads, d 128, conv 4) for a batch of 5 sequences, 4 tokens."""
+    rng = np.random.default_rng(77)
+    B, H, d, ck = 5, 16, 128, 4
+    conv_dim = 3 * H * d
+    w = dict(conv_w=(rng.standard_normal((conv_dim, ck)) * 0.5).astype(np.float32),
+             dt_bias=rng.standard_normal(H).astype(np.float32), A_log=(0.5 * rng.standard_normal(H)).astype(np.float32),
+             norm_w=(1 + 0.1 * rng.standard_normal(d)).astype(np.float32))
+    st = pkg.DeltaState(ctx, 2, B, H, d, d, ck)
+    st.set_weights(1, **w)
+    S = (0.02 * rng.standard_normal((B, H, d, d))).astype(np.float32)
+    conv = rng.standard_normal((B, conv_dim, ck)).astype(np.float32)
+    for b in range(B):
+        st.upload(1, b, S=S[b], conv_state=conv[b])
+    for t in range(4):
+        qkv = rng.standard_normal((B, conv_dim)).astype(np.float32)
+        z = rng.standard_normal((B, H * d)).astype(np.float32)
+        bb = rng.standard_normal((B, H)).astype(np.float32)
+        aa = rng.standard_normal((B, H)).astype(np.float32)
+        out = st.core(1, qkv, z, bb, aa)
+        for b in range(B):
+            ref = orc.deltanet_core(qkv[b], z[b], bb[b], aa[b], conv[b], S[b], **w)
+            assert rel_l2(out[b], ref) <= TOL, (t, b)
+    for b in range(B):
+        Sg, cg = st.download(1, b)
+        assert rel_l2(Sg, S[b]) <= TOL and rel_l2(cg, conv[b]) <= TOL
+
+
+def test_deltanet_core_needs_weights(pkg, ctx):
+    st = pkg.DeltaState(ctx, 1, 1, 2, 128, 128, 4)
+    z = np.zeros((1, 256), np.float32)
+    with pytest.raises(pkg.EifCudaError) as e:
+        st.core(0, np.zeros((1, 768), np.float32), z, np.zeros((1, 2), np.float32), np.zeros((1, 2), np.float32))
+    assert e.value.name == "INVALID_ARGUMENT"
+
+
+def test_fullatt_prep_golden(pkg, ctx):
+    """The reference's fullatt_prep at pos 11: q, gate, and the cache rows it writes."""
+    d = golden("fullatt_prep.npz")
+    nh, nkv, hd, pos = (int(x) for x in d["meta"])
+    kv = pkg.KVCache(ctx, 1, 1, 16, nkv, hd, pkg.F32)
+    kv.set_norms(0, d["q_norm"], d["k_norm"])
+    q, g = kv.fullatt_prep(0, d["qg"][None], d["k"][None], d["v"][None], np.array([pos]), nh)
+    assert rel_l2(q[0], d["q"]) <= TOL
+    assert np.array_equal(g[0], d["gate"])
+    kd, vd = kv.download(0, 0, pos, 1)
+    assert rel_l2(kd[0], d["k_row"]) <= TOL
+    assert np.array_equal(vd[0], d["v_row"])
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_qwen35_attention_layer_chain(pkg, ctx, orc, dtype):
+    """Several decode steps of a Qwen3.5 full-attention layer for a batch with ragged positions:
+    fullatt_prep (norms, partial RoPE, append) then attend with the sigmoid gate and SubLN, against the
+    restatement of fullatt_prep + fullatt_attend."""
+    rng = np.random.default_rng(88)
+    B, nh, nkv, hd, T = 3, 8, 2, 256, 48
+    dt = pkg.F32 if dtype == "f32" else pkg.BF16
+    kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, dt)
+    qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    sub = (1 + 0.1 * rng.standard_normal(nh * hd)).astype(np.float32)
+    kv.set_norms(0, qn, kn)
+    kc = np.zeros((B, T, nkv * hd), np.float32)
+    vc = np.zeros_like(kc)
+    pos = np.array([0, 5, 20], np.int32)
+    for step in range(6):
+        qg = rng.standard_normal((B, nh * 2 * hd)).astype(np.float32)
+        k = rng.standard_normal((B, nkv * hd)).astype(np.float32)
+        v = rng.standard_normal((B, nkv * hd)).astype(np.float32)
+        q, g = kv.fullatt_prep(0, qg, k, v, pos, nh)
+        out = kv.attend_decode(0, q, pos, nh, 1.0 / 16, gate=g, subln=pkg.SUBLN_WEIGHT, sub_norm=sub)
+        for b in range(B):
+            rq, rg, _ = orc.fullatt_prep(qg[b], k[b], v[b], qn, kn, kc[b], vc[b], pos[b], nh, nkv, hd)
+            if dt == pkg.BF16:
+                kc[b, pos[b]] = orc.round_bf16(kc[b, pos[b]])
+                vc[b, pos[b]] = orc.round_bf16(vc[b, pos[b]])
+            assert rel_l2(q[b], rq) <= TOL and np.array_equal(g[b], rg)
+            ref = orc.subln(orc.attend_decode(rq, kc[b], vc[b], pos[b], nh, nkv, hd, 1.0 / 16, gate=rg), sub, 2)
+            assert rel_l2(out[b], ref) <= TOL, (step, b)
+        pos = pos + 1
