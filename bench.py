@@ -580,10 +580,91 @@ def run_prefill(args, torch, dist, rank, world, local_rank):
     return line
 
 
+CK_B, CK_T, CK_H, CK_D = 4, 8192, 16, 128
+
+
+def run_chunked(args, torch, dist, rank, world, local_rank):
+    """chunked DeltaNet prefill, batch 4 x 8192 tokens, 16 heads, d 128, bf16 q/k/v,
+    zero initial state (reset before every timed launch, outside the events)."""
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    torch.cuda.set_device(local_rank)
+    B = max(1, CK_B // world)
+    ctx = pkg.Context(local_rank)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(21 + rank)
+    qk = torch.randn(2, B, CK_T, CK_H, CK_D, device=dev, generator=gen)
+    qk = (qk / torch.sqrt((qk * qk).sum(-1, keepdim=True) + 1e-12)).to(torch.bfloat16)
+    q, k = qk[0].contiguous(), qk[1].contiguous()
+    v = torch.randn(B, CK_T, CK_H, CK_D, device=dev, generator=gen).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(B, CK_T, CK_H, device=dev, generator=gen))
+    g = -torch.nn.functional.softplus(torch.randn(B, CK_T, CK_H, device=dev, generator=gen))
+    o = torch.empty_like(v)
+    st = pkg.DeltaState(ctx, 1, B, CK_H, CK_D, CK_D)
+    s_ptr, _ = st.layer_ptrs(0)
+    S = torch.as_tensor(CudaArray(s_ptr, (B * CK_H * CK_D * CK_D,), "<f4"), device=dev)
+    qs = 1.0 / math.sqrt(CK_D)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def launch():
+        st.prefill_dev(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(), g.data_ptr(), CK_T, qs,
+                       o.data_ptr())
+
+    for _ in range(args.warmup):
+        S.zero_()
+        launch()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(args.steps)]
+    clocks = ClockSampler(local_rank)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    l0 = ctx.launch_count
+    for s in range(args.steps):
+        S.zero_()
+        flush.zero_()
+        ev[s][0].record()
+        launch()
+        ev[s][1].record()
+    torch.cuda.synchronize()
+    launches = ctx.launch_count - l0
+    clk = clocks.stop()
+    ctx.synchronize()
+    ms = float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    if rank != 0:
+        return None
+    hbm, _, src = peaks()
+    GB = B * world
+    bytes_alg = GB * CK_T * CK_H * (3 * CK_D * 2 + 2 * 4 + CK_D * 2) + 2 * GB * CK_H * CK_D * CK_D * 4
+    ach = bytes_alg / (ms * 1e-3) / 1e9
+    flops_rec = 4.0 * CK_D * CK_D * GB * CK_T * CK_H
+    return {"metric": "chunked DeltaNet prefill tokens/s (BASELINE configs[3])", "value": GB * CK_T / (ms * 1e-3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16 q/k/v/o, fp32 state and accumulate", "data": "synthetic (seeded)",
+            "config": {"workload": "deltanet_chunked_prefill (BASELINE configs[3])", "global_batch": GB,
+                       "seq_len": CK_T, "heads": CK_H, "head_dim": CK_D, "chunk": 64,
+                       "l2": "256 MiB flush between launches"},
+            "roofline": {"kernel": "deltanet_chunked_kernel", "bound": "hbm", "achieved": ach, "peak": hbm,
+                         "unit": "GB/s", "frac": ach / hbm, "peak_source": src, "algorithmic_bytes_per_launch":
+                             bytes_alg, "recurrent_equivalent_tflops": flops_rec / (ms * 1e-3) / 1e12,
+                         "traffic": None},
+            "gpu_launches": launches, "clocks": clk}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", default="hybrid", choices=["hybrid", "prefill"],
-                    help="hybrid = BASELINE configs[4] (the headline); prefill = configs[1]")
+    ap.add_argument("--workload", default="hybrid", choices=["hybrid", "prefill", "chunked"],
+                    help="hybrid = BASELINE configs[4] (the headline); prefill = configs[1]; chunked = configs[3]")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -614,8 +695,9 @@ def main():
         torch.cuda.set_device(local_rank)
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         dist = tdist
-    if args.workload == "prefill":
-        line = run_prefill(args, torch, dist, rank, world, local_rank)
+    if args.workload in ("prefill", "chunked"):
+        run = run_prefill if args.workload == "prefill" else run_chunked
+        line = run(args, torch, dist, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)
         if dist:

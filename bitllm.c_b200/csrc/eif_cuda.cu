@@ -887,6 +887,95 @@ EIF_API eif_status_t eif_cuda_deltanet_core(eif_cuda_ctx_t *ctx, eif_cuda_delta_
 }
 
 // =================================================================================================
+// Chunked DeltaNet prefill
+// =================================================================================================
+
+// TMA descriptor of a token-major bf16 array [rows][H][d] as (d, H, rows), boxes of 64 x 1 x 64.
+static bool make_tok_tensor_map(CUtensorMap *map, const void *base, int rows, int H, int d) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)H, (cuuint64_t)rows};
+    const cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)H * d * 2};
+    const cuuint32_t box[3] = {64, 1, 64};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static eif_status_t chunked_check(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, int n_tok) {
+    if (!ctx || !st || st->ctx != ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= st->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    if (n_tok < 1) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "n_tok %d", n_tok);
+    if (!deltanet_chunked_supported(st->dk, st->dv))
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "chunked prefill: d_k %d / d_v %d not supported", st->dk, st->dv);
+    if ((size_t)st->batch * n_tok > 0x7fffffffull) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "too many rows");
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t chunked_run(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const void *q, const void *k,
+                                const void *v, const float *beta, const float *g, int n_tok, float q_scale, void *o) {
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+         reinterpret_cast<uintptr_t>(o)) & 15)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "chunked prefill: q, k, v, o must be 16-byte aligned");
+    alignas(64) CUtensorMap tq, tk, tv;
+    const int rows = st->batch * n_tok;
+    if (!make_tok_tensor_map(&tq, q, rows, st->H, st->dk) || !make_tok_tensor_map(&tk, k, rows, st->H, st->dk) ||
+        !make_tok_tensor_map(&tv, v, rows, st->H, st->dv))
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "chunked prefill: cannot describe q / k / v for TMA");
+    CK(launch_deltanet_chunked(ctx->stream, tq, tk, tv, beta, g, static_cast<__nv_bfloat16 *>(o), st->S[layer],
+                               st->batch, n_tok, st->H, st->dv, q_scale, ctx->dev_err));
+    ctx->launches += 1;
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_deltanet_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer,
+                                                   const void *q_dev, const void *k_dev, const void *v_dev,
+                                                   const float *beta_dev, const float *g_dev, int n_tok, float q_scale,
+                                                   void *o_dev) {
+    eif_status_t rs = chunked_check(ctx, st, layer, n_tok);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!q_dev || !k_dev || !v_dev || !beta_dev || !g_dev || !o_dev)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "deltanet_prefill_dev: NULL pointer");
+    DeviceGuard gd(ctx);
+    return chunked_run(ctx, st, layer, q_dev, k_dev, v_dev, beta_dev, g_dev, n_tok, q_scale, o_dev);
+}
+
+EIF_API eif_status_t eif_cuda_deltanet_prefill(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *q,
+                                               const float *k, const float *v, const float *beta, const float *g,
+                                               int n_tok, float q_scale, float *o) {
+    eif_status_t rs = chunked_check(ctx, st, layer, n_tok);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!q || !k || !v || !beta || !g || !o) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "deltanet_prefill: NULL pointer");
+    DeviceGuard gd(ctx);
+    const size_t rows = (size_t)st->batch * n_tok, nqk = rows * st->H * st->dk, nv = rows * st->H * st->dv,
+                 nh = rows * st->H;
+    Carver cv;
+    const size_t o_f = cv.take(std::max(nqk, nv) * 4), o_q = cv.take(nqk * 2), o_k = cv.take(nqk * 2),
+                 o_v = cv.take(nv * 2), o_o = cv.take(nv * 2), o_b = cv.take(nh * 4), o_g = cv.take(nh * 4);
+    rs = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (rs != EIF_STATUS_OK) return rs;
+    char *s = static_cast<char *>(ctx->stage);
+    float *f = reinterpret_cast<float *>(s + o_f);
+    CK(cudaMemcpyAsync(f, q, nqk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(launch_f32_to_bf16(ctx->stream, f, reinterpret_cast<__nv_bfloat16 *>(s + o_q), nqk));
+    CK(cudaMemcpyAsync(f, k, nqk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(launch_f32_to_bf16(ctx->stream, f, reinterpret_cast<__nv_bfloat16 *>(s + o_k), nqk));
+    CK(cudaMemcpyAsync(f, v, nv * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(launch_f32_to_bf16(ctx->stream, f, reinterpret_cast<__nv_bfloat16 *>(s + o_v), nv));
+    CK(cudaMemcpyAsync(s + o_b, beta, nh * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_g, g, nh * 4, cudaMemcpyHostToDevice, ctx->stream));
+    ctx->launches += 3;
+    rs = chunked_run(ctx, st, layer, s + o_q, s + o_k, s + o_v, reinterpret_cast<float *>(s + o_b),
+                     reinterpret_cast<float *>(s + o_g), n_tok, q_scale, s + o_o);
+    if (rs != EIF_STATUS_OK) return rs;
+    CK(launch_bf16_to_f32(ctx->stream, reinterpret_cast<__nv_bfloat16 *>(s + o_o), f, nv));
+    ctx->launches += 1;
+    CK(cudaMemcpyAsync(o, f, nv * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// =================================================================================================
 // Qwen3.5 attention prep (fullatt_prep)
 // =================================================================================================
 

@@ -111,6 +111,12 @@ struct AttnPrepArgs {
 };
 cudaError_t launch_fullatt_prep(cudaStream_t st, const AttnPrepArgs &a);
 
+// Chunked (WY / UT) DeltaNet prefill (deltanet_chunked.cu).
+bool deltanet_chunked_supported(int dk, int dv);
+cudaError_t launch_deltanet_chunked(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
+                                    const CUtensorMap &tv, const float *beta, const float *g, __nv_bfloat16 *o,
+                                    float *S, int B, int T, int H, int dv, float q_scale, unsigned *dev_err);
+
 // Causal prefill attention on tcgen05 (attn_prefill_tc.cu).
 bool prefill_tc_supported(int D);
 cudaError_t launch_attend_prefill_tc(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,

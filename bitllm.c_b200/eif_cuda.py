@@ -88,6 +88,8 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_delta_set_weights": (_I, [_P, _P, _I, _P, _P, _P, _P]),
         "eif_cuda_deltanet_core": (_I, [_P, _P, _I, _P, _P, _P, _P, _P]),
         "eif_cuda_deltanet_core_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _P]),
+        "eif_cuda_deltanet_prefill": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _I, _F, _P]),
+        "eif_cuda_deltanet_prefill_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _I, _F, _P]),
         "eif_cuda_kv_set_norms": (_I, [_P, _P, _I, _P, _P]),
         "eif_cuda_fullatt_prep": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P, _P]),
         "eif_cuda_fullatt_prep_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P, _P]),
@@ -362,6 +364,22 @@ class DeltaState:
     def core_dev(self, layer: int, qkv_dev, z_dev, b_dev, a_dev, out_dev):
         self.ctx.check(lib().eif_cuda_deltanet_core_dev(self.ctx.handle, self._h, layer, qkv_dev, z_dev, b_dev, a_dev,
                                                         out_dev), "deltanet_core_dev")
+
+    def prefill(self, layer: int, q, k, v, beta, g, q_scale: float):
+        """Chunked prefill of n_tok tokens per sequence (fp32 host arrays; q, k [batch][n_tok][H][d_k],
+        v [batch][n_tok][H][d_v], beta, g [batch][n_tok][H]); returns o [batch][n_tok][H][d_v]."""
+        qq, kk, vv, bb, gg = (_f32(x) for x in (q, k, v, beta, g))
+        n_tok = qq.shape[1]
+        o = np.zeros((self.batch, n_tok, self.H, self.dv), np.float32)
+        self.ctx.check(lib().eif_cuda_deltanet_prefill(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv),
+                                                       _ptr(bb), _ptr(gg), n_tok, float(q_scale), _ptr(o)),
+                       "deltanet_prefill")
+        return o
+
+    def prefill_dev(self, layer: int, q_dev, k_dev, v_dev, beta_dev, g_dev, n_tok: int, q_scale: float, o_dev):
+        self.ctx.check(lib().eif_cuda_deltanet_prefill_dev(self.ctx.handle, self._h, layer, q_dev, k_dev, v_dev,
+                                                           beta_dev, g_dev, n_tok, float(q_scale), o_dev),
+                       "deltanet_prefill_dev")
 
     def step_dev(self, layer: int, q_dev, k_dev, v_dev, beta_dev, g_dev, q_scale: float, o_dev):
         self.ctx.check(lib().eif_cuda_deltanet_step_dev(self.ctx.handle, self._h, layer, q_dev, k_dev, v_dev,

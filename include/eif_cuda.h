@@ -224,6 +224,22 @@ eif_status_t eif_cuda_deltanet_core_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *s
                                         const float *z_dev, const float *b_dev, const float *a_dev, float *out_dev);
 
 /*
+ * DeltaNet prefill of n_tok tokens per sequence in the chunked WY / UT form (64-token chunks, the chunk
+ * products on tensor cores, fp32 state carried across chunks), starting from and updating the layer's S.
+ * Algebraically the token-by-token rule the engine runs in prefill_chunk (src/eif_qwen35.c:1104-1106
+ * calling :594-639 per token); q and k are L2-normalised by the caller, q is multiplied by q_scale.
+ *   q, k [batch][n_tok][H][d_k], v, o [batch][n_tok][H][d_v]; beta, g [batch][n_tok][H] (decay = exp(g))
+ * _dev: bf16 q / k / v / o (16-byte aligned), fp32 beta / g, asynchronous.  Host variant: fp32 arrays.
+ * Supported: d_k = 128, d_v a multiple of 64 up to 256.
+ */
+eif_status_t eif_cuda_deltanet_prefill(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *q,
+                                       const float *k, const float *v, const float *beta, const float *g, int n_tok,
+                                       float q_scale, float *o);
+eif_status_t eif_cuda_deltanet_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const void *q_dev,
+                                           const void *k_dev, const void *v_dev, const float *beta_dev,
+                                           const float *g_dev, int n_tok, float q_scale, void *o_dev);
+
+/*
  * Qwen3.5 attention prep of one token per sequence: fullatt_prep (src/eif_qwen35.c:699-737) -- split the
  * interleaved [q | gate] heads, RMSNorm q and k per head with the layer's q_norm / k_norm (eps 1e-6),
  * partial RoPE on the first head_dim/4 dims (theta 1e7, rope_partial :502-535; the cos / sin table is
