@@ -918,14 +918,22 @@ static eif_status_t chunked_run(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int l
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
          reinterpret_cast<uintptr_t>(o)) & 15)
         return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "chunked prefill: q, k, v, o must be 16-byte aligned");
-    alignas(64) CUtensorMap tq, tk, tv;
+    // scratch: the per-chunk T = (I + A)^-1 matrices, bf16 [batch][H][chunk][64][64]
+    const size_t ws = deltanet_chunked_workspace(st->batch, n_tok, st->H);
+    eif_status_t rs = ensure_buffer(ctx, &ctx->ws, &ctx->ws_bytes, ws);
+    if (rs != EIF_STATUS_OK) return rs;
+    alignas(64) CUtensorMap tq, tk, tv, tt;
     const int rows = st->batch * n_tok;
+    const int t_rows = (int)(ws / 128);  // 64 bf16 per row
     if (!make_tok_tensor_map(&tq, q, rows, st->H, st->dk) || !make_tok_tensor_map(&tk, k, rows, st->H, st->dk) ||
-        !make_tok_tensor_map(&tv, v, rows, st->H, st->dv))
+        !make_tok_tensor_map(&tv, v, rows, st->H, st->dv) || !make_tok_tensor_map(&tt, ctx->ws, t_rows, 1, 64))
         return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "chunked prefill: cannot describe q / k / v for TMA");
-    CK(launch_deltanet_chunked(ctx->stream, tq, tk, tv, beta, g, static_cast<__nv_bfloat16 *>(o), st->S[layer],
-                               st->batch, n_tok, st->H, st->dv, q_scale, ctx->dev_err));
-    ctx->launches += 1;
+    int nl = 0;
+    const cudaError_t e = launch_deltanet_chunked(ctx->stream, tq, tk, tv, tt, ctx->ws, beta, g,
+                                                  static_cast<__nv_bfloat16 *>(o), st->S[layer], st->batch, n_tok,
+                                                  st->H, st->dv, q_scale, ctx->dev_err, &nl);
+    ctx->launches += nl;
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "deltanet_chunked launch");
     return EIF_STATUS_OK;
 }
 

@@ -113,9 +113,12 @@ cudaError_t launch_fullatt_prep(cudaStream_t st, const AttnPrepArgs &a);
 
 // Chunked (WY / UT) DeltaNet prefill (deltanet_chunked.cu).
 bool deltanet_chunked_supported(int dk, int dv);
+// Scratch bytes of the per-chunk T matrices (bf16 64 x 64 per sequence, head and chunk).
+size_t deltanet_chunked_workspace(int B, int T, int H);
 cudaError_t launch_deltanet_chunked(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
-                                    const CUtensorMap &tv, const float *beta, const float *g, __nv_bfloat16 *o,
-                                    float *S, int B, int T, int H, int dv, float q_scale, unsigned *dev_err);
+                                    const CUtensorMap &tv, const CUtensorMap &tt, void *t_ws, const float *beta,
+                                    const float *g, __nv_bfloat16 *o, float *S, int B, int T, int H, int dv,
+                                    float q_scale, unsigned *dev_err, int *n_launches);
 
 // Causal prefill attention on tcgen05 (attn_prefill_tc.cu).
 bool prefill_tc_supported(int D);
