@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     using C = TcCfg<D, NB>;
     constexpr int NS = C::NS, HS = C::HS, MT = D / 16;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *smem = smem_align1024(smem_raw);
     float *ow = reinterpret_cast<float *>(smem + NS * C::STAGE);   // [4][HS][D]
     float *mw = ow + kConsumers * HS * D;                          // [4][HS]
     float *lw = mw + kConsumers * HS;                              // [4][HS]

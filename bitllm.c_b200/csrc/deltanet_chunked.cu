@@ -14,13 +14,14 @@
 // Two kernels:
 //   chunk_solve_kernel   one CTA per (sequence, head, chunk), all in parallel: K K^T on the tensor cores,
 //                        A, then T = (I + A)^-1 in fp32 by blocked forward substitution (16 x 16 diagonal
-//                        blocks per warp, three block levels); T is written as bf16 [64 x 64] per chunk.
+//                        blocks per warp, three block levels); writes T diag(-b e^G) and T diag(b) as bf16
+//                        [64 x 64] each, and G, per chunk.
 //   deltanet_chunked_kernel  one CTA per (sequence, head, 64-column slice of d_v): the columns of S
 //                        evolve independently (column j of u depends on column j of S only), so slices
-//                        need no communication.  It walks the chunks in order with the fp32 state in
-//                        registers (mma accumulator layout, warps 0-3); TMA brings the next chunk's q / k
-//                        / v / T tiles (128-byte swizzle, no multicast) during the current one; every
-//                        product runs on the tensor cores (mma.m16n8k16, bf16 in, fp32 accumulate).
+//                        need no communication.  Every chunk product runs on tcgen05 (bf16 operands in
+//                        shared memory, fp32 accumulators in tensor memory); the fp32 state stays in
+//                        registers; TMA brings q / k / v / T two chunks ahead (128-byte swizzle, no
+//                        multicast).  Warp roles are described above the kernel.
 #include <math.h>
 
 #include "internal.h"
@@ -71,20 +72,23 @@ constexpr int kSolveThreads = 128;
 constexpr int SOL_K = 0;                      // bf16 64 x 128 K tile (TMA)
 constexpr int SOL_A = C * DK * 2;             // fp32 [64][FP] A
 constexpr int SOL_T = SOL_A + C * FP * 4;     // fp32 [64][FP] T
-constexpr int SOL_VEC = SOL_T + C * FP * 4;   // G[64], beta[64]
-constexpr int SOL_BAR = SOL_VEC + 2 * C * 4;
+constexpr int SOL_VEC = SOL_T + C * FP * 4;   // G[64], beta[64], -beta e^G [64]
+constexpr int SOL_BAR = SOL_VEC + 3 * C * 4;
 constexpr int kSolveSmem = SOL_BAR + 16 + 1024;
 
+// Outputs per (sequence, head, chunk): Tout [128][64] bf16 = T diag(-b e^G) ; T diag(b) (the A operands
+// of W and U' in the state kernel, with the minus sign of U = U' - W S folded in) and Gout [64] fp32 = G.
 __global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                     const float *__restrict__ beta,
                                                                     const float *__restrict__ g,
-                                                                    __nv_bfloat16 *__restrict__ Tout, int T, int H,
+                                                                    __nv_bfloat16 *__restrict__ Tout,
+                                                                    float *__restrict__ Gout, int T, int H,
                                                                     unsigned *dev_err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *sm = smem_align1024(smem_raw);
     const uint32_t sb = smem_u32(sm);
     float *Af = reinterpret_cast<float *>(sm + SOL_A), *Tf = reinterpret_cast<float *>(sm + SOL_T);
-    float *Gv = reinterpret_cast<float *>(sm + SOL_VEC), *Bv = Gv + C;
+    float *Gv = reinterpret_cast<float *>(sm + SOL_VEC), *Bv = Gv + C, *Xv = Gv + 2 * C;
     const uint32_t bar = smem_u32(sm + SOL_BAR);
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z, n_chunks = gridDim.x;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
@@ -101,6 +105,7 @@ __global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid
     load_chunk_gates(beta, g, b, h, H, T, c * C, Gv, Bv);
     const bool ok = mbar_wait(bar, 0, dev_err);
     if (!__syncthreads_and(ok)) return;
+    if (tid < C) Xv[tid] = -Bv[tid] * expf(Gv[tid]);  // read after the solve's barriers
 
     // K K^T: warp w owns rows 16w..16w+15; A_ij = b_i e^{G_i - G_j} k_i.k_j for j < i
     {
@@ -171,40 +176,78 @@ __global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid
         }
         __syncthreads();
     }
-    // T (lower, upper zeroed) -> bf16 rows of 64 for the state kernel's TMA
-    __nv_bfloat16 *dst = Tout + (((size_t)b * H + h) * n_chunks + c) * C * C;
+    // T diag(-b e^G) ; T diag(b) (T lower triangular) -> bf16 rows of 64 for the state kernel's TMA; G
+    const size_t chunk_ix = ((size_t)b * H + h) * n_chunks + c;
+    __nv_bfloat16 *dst = Tout + chunk_ix * 2 * C * C;
     for (int e = tid; e < C * C / 8; e += kSolveThreads) {
         const int i = e >> 3, j0 = (e & 7) * 8;
-        uint32_t w[4];
+        uint32_t w1[4], w2[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const int j = j0 + 2 * q;
-            w[q] = pack_bf16x2(j <= i ? Tf[i * FP + j] : 0.f, j + 1 <= i ? Tf[i * FP + j + 1] : 0.f);
+            const float t0 = j <= i ? Tf[i * FP + j] : 0.f, t1 = j + 1 <= i ? Tf[i * FP + j + 1] : 0.f;
+            w1[q] = pack_bf16x2(t0 * Xv[j], t1 * Xv[j + 1]);
+            w2[q] = pack_bf16x2(t0 * Bv[j], t1 * Bv[j + 1]);
         }
-        *reinterpret_cast<uint4 *>(dst + i * C + j0) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(dst + i * C + j0) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+        *reinterpret_cast<uint4 *>(dst + C * C + i * C + j0) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
     }
+    if (tid < C) Gout[chunk_ix * C + tid] = Gv[tid];
 }
 
 // ==================================================================================================
-// Kernel B: the chunk products and the state recurrence
+// Kernel B: the chunk products on tcgen05 and the state recurrence
 // ==================================================================================================
-constexpr int kThreads = 256;
-// stage: Q (2 boxes), K (2 boxes), V slice (1 box), T (1 box)
-constexpr int STG_Q = 0, STG_K = C * DK * 2, STG_V = 2 * C * DK * 2, STG_T = STG_V + C * DS * 2,
-              STG_BYTES = STG_T + C * C * 2;
-constexpr int OFF_STG = 0;                                   // two stages
-constexpr int OFF_QKM = 2 * STG_BYTES;                       // bf16 64 x 64: q_scale e^{G_i-G_j} Q K^T (j <= i)
-constexpr int OFF_X = OFF_QKM + C * C * 2;                   // bf16 64 x 192: [b e^G K | b V]
-constexpr int OFF_KT = OFF_X + C * (DK + DS) * 2;            // bf16 64 x 128: e^{G_C - G} K
-constexpr int OFF_W = OFF_KT + C * DK * 2;                   // bf16 64 x 128: W
-constexpr int OFF_U = OFF_W + C * DK * 2;                    // bf16 64 x 64: U
-constexpr int OFF_SB = OFF_U + C * DS * 2;                   // bf16 128 x 64: S (bf16 copy)
-constexpr int OFF_VEC = OFF_SB + DK * DS * 2;                // fp32: G[64], beta[64], eG[64], eGC[64]
-constexpr int OFF_BAR = OFF_VEC + 4 * C * 4;
-constexpr int kSmem = OFF_BAR + 64 + 1024;
+// Products of chunk c (M = 128 TMEM lanes, fp32 accumulators; "lanes 0-63" are the chunk's tokens):
+//   Dq  = [Q ; *] K^T                         lanes 0-63: Q K^T                      (prep)
+//   Dp[:, 0:128]   = [T1 ; T2] K              lanes 0-63: -W                          (prep)
+//   Dp[:, 128:192] = [T2 ; 0] V               lanes 0-63: U'                          (prep)
+//   Dp[:, 128:192] += [-W ; Q~] S             lanes 0-63: U = U' - W S, lanes 64-127: Q~ S
+//   Dp[:, 128:192] += [* ; QKm] U             lanes 64-127: O (lanes 0-63 are dead by then)
+//   Ds  = Kt^T U                              S_next = e^{G_C} S + Ds
+// with T1 = T diag(-b e^G), T2 = T diag(b) (from chunk_solve_kernel), Q~ = q_scale e^G Q,
+// Kt = e^{G_C - G} K and QKm = q_scale e^{G_i - G_j} Q K^T (j <= i); "*" rows only reach dead lanes.
+// Roles (352 threads):
+//   warps 0-3  state: thread r owns row r of the fp32 state slice (64 columns, registers) and TMEM
+//              lane r; warps 0-1 turn Dp into U (bf16), all four form the next S (bf16 copy for the
+//              MMA), warps 2-3 store O.
+//   warps 4-7  prep, one chunk ahead of the state: QKm and -W (from TMEM, warps 4-5, which own lanes
+//              0-63); Q~ and Kt (bf16x2 products from the TMA stage, warps 6-7).
+//   warp 8     MMA issuer of the state chain; owns the TMEM allocation.
+//   warp 9     MMA issuer of the prep products (Dq, Dp).
+//   warp 10    TMA producer (two stages); its lanes also copy the chunk's G into the stage.
+// Every wait is a bounded mbarrier wait; the prep warps agree on aborting through a barrier reduction.
+constexpr int kThreads = 352;
+// one stage: [Q box0 | K box0 | Q box1 | K box1] 32 KB, V 8 KB, T1 8 KB, T2 8 KB, zeros 8 KB, G 256 B
+constexpr int SL_V = 32768, SL_T1 = 40960, SL_T2 = 49152, SL_Z = 57344, SL_G = 65536, SLOT = 66560;
+constexpr int STAGE_TX = 57344;               // bytes TMA brings per stage
+constexpr int OFF_WQ = 2 * SLOT;              // [-W box0 | Q~ box0 | -W box1 | Q~ box1]: A of the S product
+constexpr int OFF_QKM = OFF_WQ + 32768;       // QKm; the 8 KB before it stand in as the dead A rows 0-63
+constexpr int OFF_KT = OFF_QKM + 8192;        // Kt, 2 boxes
+constexpr int OFF_SB = OFF_KT + 16384;        // S slice, bf16 [128 key rows][64 columns]
+constexpr int OFF_U = OFF_SB + 16384;         // U, bf16 [64 tokens][64 columns]
+constexpr int OFF_VEC = OFF_U + 8192;         // bf16x2 pairs q_scale e^G, e^{G_C - G}; fp32 e^{g} [64 each]; e^{G_C} ring [4]
+constexpr int OFF_BAR = OFF_VEC + 1024;
+constexpr int kSmem = OFF_BAR + 256 + 1024;
+constexpr int TM_DS = 384, TM_DQ = 448, kTmemCols = 512;  // Dp of slot s at columns 192 s
+
+enum {
+    B_FULL = 0,      // [2] stage landed (TMA tx + G copied)
+    B_EMPTY = 2,     // [2] stage consumed (prep MMAs + 128 prep threads)
+    B_QDONE = 4,     // Dq ready
+    B_DQFREE = 5,    // Dq read (warps 4-5)
+    B_PDONE = 6,     // [2] Dp of the slot ready (a ring: the prep issuer may run a chunk ahead of the reader)
+    B_DPFREE = 8,    // [2] O of the slot read (warps 2-3)
+    B_PREP = 10,     // [2] -W, Q~, QKm, Kt and the gates of the chunk written (prep)
+    B_M1 = 12,       // S product done: U in TMEM; -W / Q~ free
+    B_UREADY = 13,   // U written (warps 0-1)
+    B_M23 = 14,      // O and Ds done; U, QKm, Kt free
+    B_SREADY = 15,   // next S written (state)
+    B_COUNT = 16
+};
 
 struct ChunkArgs {
-    const float *beta, *g;  // [B][T][H]
+    const float *G;         // [B][H][n_chunks][64] cumulative log decays (chunk_solve_kernel)
     __nv_bfloat16 *o;       // [B][T][H][dv]
     float *S;               // layer state [B][H][DK][dv]
     int B, T, H, dv, n_chunks;
@@ -212,305 +255,366 @@ struct ChunkArgs {
     unsigned *dev_err;
 };
 
+__device__ __forceinline__ uint32_t swz(int row, int u) { return (uint32_t)(row * 128 + ((u ^ (row & 7)) << 4)); }
+
+// 8 bf16 times a bf16 scale given as a duplicated pair
+__device__ __forceinline__ uint4 scale8(uint4 v, uint32_t f2) {
+    return make_uint4(bf16x2_mul(v.x, f2), bf16x2_mul(v.y, f2), bf16x2_mul(v.z, f2), bf16x2_mul(v.w, f2));
+}
+
+// 64 fp32 values -> one 128-byte swizzled bf16 row (times `f`)
+__device__ __forceinline__ void store_row64(uint8_t *box, int row, const float *v, float f) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<uint4 *>(box + swz(row, u)) =
+            make_uint4(pack_bf16x2(v[8 * u] * f, v[8 * u + 1] * f), pack_bf16x2(v[8 * u + 2] * f, v[8 * u + 3] * f),
+                       pack_bf16x2(v[8 * u + 4] * f, v[8 * u + 5] * f), pack_bf16x2(v[8 * u + 6] * f, v[8 * u + 7] * f));
+}
+
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+    tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(v));
+    tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     deltanet_chunked_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmT,
                             const ChunkArgs p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *sm = smem_align1024(smem_raw);
     const uint32_t sb = smem_u32(sm);
-    float *Gv = reinterpret_cast<float *>(sm + OFF_VEC), *Bv = Gv + C, *eG = Gv + 2 * C, *eGC = Gv + 3 * C;
+    uint32_t *fq2 = reinterpret_cast<uint32_t *>(sm + OFF_VEC), *fk2 = fq2 + C;
+    float *decv = reinterpret_cast<float *>(fq2 + 2 * C), *dCv = decv + C;
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
+    auto bar = [&](int i) { return smem_u32(bars + i); };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + B_COUNT);
 
     const int slice = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
-    const int mi = lane >> 3, r8 = lane & 7;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n_chunks = p.n_chunks;
     const size_t bh = (size_t)b * p.H + h;
 
     if (tid == 0) {
-        mbar_init(smem_u32(bars), 1);
-        mbar_init(smem_u32(bars + 1), 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(bar(B_FULL + s), 2);
+            mbar_init(bar(B_EMPTY + s), 1 + 128);
+            mbar_init(bar(B_DPFREE + s), 64);
+            mbar_init(bar(B_PREP + s), 128);
+        }
+        mbar_init(bar(B_QDONE), 1);
+        mbar_init(bar(B_DQFREE), 64);
+        mbar_init(bar(B_PDONE), 1);
+        mbar_init(bar(B_PDONE + 1), 1);
+        mbar_init(bar(B_M1), 1);
+        mbar_init(bar(B_UREADY), 64);
+        mbar_init(bar(B_M23), 1);
+        mbar_init(bar(B_SREADY), 128);
         fence_barrier_init();
     }
-
-    // ---- initial state: warps 0-3 hold S rows [32w, 32w+32) x 64 columns in accumulator layout
-    float S[2][8][4];
-    float *Sg = p.S + bh * DK * p.dv + slice * DS;
-    if (warp < 4) {
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
-                const int row = warp * 32 + mt * 16 + g8, col = nt * 8 + 2 * t4;
-                S[mt][nt][0] = Sg[(size_t)row * p.dv + col];
-                S[mt][nt][1] = Sg[(size_t)row * p.dv + col + 1];
-                S[mt][nt][2] = Sg[(size_t)(row + 8) * p.dv + col];
-                S[mt][nt][3] = Sg[(size_t)(row + 8) * p.dv + col + 1];
-                *reinterpret_cast<uint32_t *>(sm + OFF_SB + sw(DK, row, col)) = pack_bf16x2(S[mt][nt][0], S[mt][nt][1]);
-                *reinterpret_cast<uint32_t *>(sm + OFF_SB + sw(DK, row + 8, col)) =
-                    pack_bf16x2(S[mt][nt][2], S[mt][nt][3]);
-            }
+    // zero rows 64-127 of the [T2 ; 0] operand of both stages (TMA never writes them)
+    for (int e = tid; e < 2 * 512; e += kThreads)
+        reinterpret_cast<uint4 *>(sm + (e >> 9) * SLOT + SL_Z)[e & 511] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+    if (warp == 8) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
     }
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
 
-    auto issue = [&](int c) {  // TMA for chunk c into stage c & 1 (thread 0)
-        const int s = c & 1;
-        const uint32_t bar = smem_u32(bars + s), base = sb + OFF_STG + s * STG_BYTES;
-        const int row = b * p.T + c * C;
-        mbar_arrive_expect_tx(bar, STG_BYTES);
-        for (int d = 0; d < 2; ++d) {
-            tma_load_3d(base + STG_Q + d * C * 128, &tmQ, d * 64, h, row, bar);
-            tma_load_3d(base + STG_K + d * C * 128, &tmK, d * 64, h, row, bar);
+    if (warp < 4) {
+        // ------------------------------------------------------------------ state
+        const int r = tid;
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        float S[64];
+        float *Sg = p.S + (bh * DK + r) * p.dv + slice * DS;
+#pragma unroll
+        for (int j = 0; j < 64; j += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(Sg + j);
+            S[j] = v.x;
+            S[j + 1] = v.y;
+            S[j + 2] = v.z;
+            S[j + 3] = v.w;
         }
-        tma_load_3d(base + STG_V, &tmV, slice * DS, h, row, bar);
-        tma_load_3d(base + STG_T, &tmT, 0, 0, (int)(bh * n_chunks + c) * C, bar);
-    };
-    if (tid == 0) {
-        prefetch_tmap(&tmQ);
-        prefetch_tmap(&tmK);
-        prefetch_tmap(&tmV);
-        prefetch_tmap(&tmT);
-        issue(0);
-    }
-
-    float Up[8][4];  // U' tiles of warps 0-3 (rows 16w..16w+15, all 64 columns)
-    bool ok = true;
-    for (int c = 0; c < n_chunks; ++c) {
-        const int s = c & 1;
-        const int t0 = c * C;
-        const uint32_t stg = sb + OFF_STG + s * STG_BYTES;
-        uint8_t *stgp = sm + OFF_STG + s * STG_BYTES;
-        if (tid == 0 && c + 1 < n_chunks) {
+        store_row64(sm + OFF_SB, r, S, 1.f);
+        fence_proxy_async_smem();
+        mbar_arrive(bar(B_SREADY));
+        bool ok = true;
+        for (int c = 0; c < n_chunks; ++c) {
+            const int slot = c & 1;
+            const uint32_t dcol = tmem + lane_off + slot * 192 + 128;
+            if (!mbar_wait(bar(B_PREP + slot), (c >> 1) & 1, p.dev_err)) { ok = false; break; }
+            const float dC = dCv[c & 3];
+            if (warp < 2) {
+                if (!mbar_wait(bar(B_M1), c & 1, p.dev_err)) { ok = false; break; }
+                tc_fence_after();
+                float u[64];
+                tmem_ld64(dcol, u);
+                tmem_wait_ld();
+                store_row64(sm + OFF_U, r, u, 1.f);
+                fence_proxy_async_smem();
+                tc_fence_before();
+                mbar_arrive(bar(B_UREADY));
+            }
+            if (!mbar_wait(bar(B_M23), c & 1, p.dev_err)) { ok = false; break; }
+            tc_fence_after();
+            {
+                float d[64];
+                tmem_ld64(tmem + lane_off + TM_DS, d);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 64; ++j) S[j] = fmaf(dC, S[j], d[j]);
+            }
+            store_row64(sm + OFF_SB, r, S, 1.f);
             fence_proxy_async_smem();
-            issue(c + 1);
-        }
-        // ---- P0: beta, g, cumulative log decay
-        load_chunk_gates(p.beta, p.g, b, h, p.H, p.T, t0, Gv, Bv);
-        ok = mbar_wait(smem_u32(bars + s), (c >> 1) & 1, p.dev_err);
-        if (!__syncthreads_and(ok)) {  // CTA-uniform: every thread leaves the loop together
-            ok = false;
-            break;
-        }
-        if (tid < C) {
-            eG[tid] = expf(Gv[tid]);
-            eGC[tid] = expf(Gv[C - 1] - Gv[tid]);
-        }
-
-        // ---- P1: Q K^T -> q_scale e^{G_i - G_j} (j <= i) as bf16; warp w: rows 16(w&3).., columns 32(w>>2)..
-        {
-            const int mt = warp & 3, n0 = (warp >> 2) * 32;
-            float acc[4][4];
+            if (warp >= 2) {
+                float o[64];
+                tmem_ld64(dcol, o);
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(bar(B_SREADY));
+                mbar_arrive(bar(B_DPFREE + slot));
+                const int t = c * C + r - 64;
+                if (t < p.T) {
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.o + (((size_t)b * p.T + t) * p.H + h) * p.dv + slice * DS);
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-#pragma unroll
-            for (int ks = 0; ks < DK / 16; ++ks) {
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4(stg + STG_Q + sw(C, mt * 16 + (mi & 1) * 8 + r8, ks * 16 + (mi >> 1) * 8), a0, a1, a2, a3);
-#pragma unroll
-                for (int np = 0; np < 2; ++np) {
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4(stg + STG_K + sw(C, n0 + np * 16 + (mi >> 1) * 8 + r8, ks * 16 + (mi & 1) * 8), b0, b1, b2,
-                            b3);
-                    mma_bf16_16816(acc[2 * np], a0, a1, a2, a3, b0, b1);
-                    mma_bf16_16816(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
-                }
-            }
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-                for (int hr = 0; hr < 2; ++hr) {
-                    const int i = mt * 16 + g8 + hr * 8, j = n0 + nt * 8 + 2 * t4;
-                    const float v0 = j <= i ? p.q_scale * expf(Gv[i] - Gv[j]) * acc[nt][2 * hr] : 0.f;
-                    const float v1 = j + 1 <= i ? p.q_scale * expf(Gv[i] - Gv[j + 1]) * acc[nt][2 * hr + 1] : 0.f;
-                    *reinterpret_cast<uint32_t *>(sm + OFF_QKM + sw(C, i, j)) = pack_bf16x2(v0, v1);
-                }
-        }
-        __syncthreads();  // eG / eGC ready
-
-        // ---- P2: X = [b e^G K | b V], Kt = e^{G_C - G} K (bf16, swizzled)
-        for (int e = tid; e < C * (DK / 8); e += kThreads) {  // 16-byte units of K rows
-            const int j = e >> 4, u = e & 15;
-            const uint4 kv = *reinterpret_cast<const uint4 *>(stgp + STG_K + sw(C, j, u * 8));
-            const float fx = Bv[j] * eG[j], fk = eGC[j];
-            uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w}, xo[4], ko[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float lo = bf16lo_to_f32(w[q]), hi = bf16hi_to_f32(w[q]);
-                xo[q] = pack_bf16x2(lo * fx, hi * fx);
-                ko[q] = pack_bf16x2(lo * fk, hi * fk);
-            }
-            *reinterpret_cast<uint4 *>(sm + OFF_X + sw(C, j, u * 8)) = make_uint4(xo[0], xo[1], xo[2], xo[3]);
-            *reinterpret_cast<uint4 *>(sm + OFF_KT + sw(C, j, u * 8)) = make_uint4(ko[0], ko[1], ko[2], ko[3]);
-        }
-        for (int e = tid; e < C * (DS / 8); e += kThreads) {  // 16-byte units of the V slice
-            const int j = e >> 3, u = e & 7;
-            const uint4 vv = *reinterpret_cast<const uint4 *>(stgp + STG_V + sw(C, j, u * 8));
-            const float fb = Bv[j];
-            uint32_t w[4] = {vv.x, vv.y, vv.z, vv.w}, xo[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) xo[q] = pack_bf16x2(bf16lo_to_f32(w[q]) * fb, bf16hi_to_f32(w[q]) * fb);
-            *reinterpret_cast<uint4 *>(sm + OFF_X + sw(C, j, DK + u * 8)) = make_uint4(xo[0], xo[1], xo[2], xo[3]);
-        }
-        __syncthreads();
-
-        // ---- P3: [W | U'] = T X.  warps 0-3: m-tile w, W cols 0-63 and U'; warps 4-7: W cols 64-127
-        {
-            const int mt = warp & 3;
-            const int wc0 = warp < 4 ? 0 : 64;
-            float wacc[8][4];
-#pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
-                wacc[nt][0] = wacc[nt][1] = wacc[nt][2] = wacc[nt][3] = 0.f;
-                Up[nt][0] = Up[nt][1] = Up[nt][2] = Up[nt][3] = 0.f;
-            }
-#pragma unroll
-            for (int ks = 0; ks < C / 16; ++ks) {
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4(stg + STG_T + sw(C, mt * 16 + (mi & 1) * 8 + r8, ks * 16 + (mi >> 1) * 8), a0, a1, a2, a3);
-#pragma unroll
-                for (int np = 0; np < 4; ++np) {
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4_t(sb + OFF_X + sw(C, ks * 16 + (mi & 1) * 8 + r8, wc0 + np * 16 + (mi >> 1) * 8), b0, b1, b2,
-                              b3);
-                    mma_bf16_16816(wacc[2 * np], a0, a1, a2, a3, b0, b1);
-                    mma_bf16_16816(wacc[2 * np + 1], a0, a1, a2, a3, b2, b3);
-                    if (warp < 4) {
-                        ldsm_x4_t(sb + OFF_X + sw(C, ks * 16 + (mi & 1) * 8 + r8, DK + np * 16 + (mi >> 1) * 8), b0,
-                                  b1, b2, b3);
-                        mma_bf16_16816(Up[2 * np], a0, a1, a2, a3, b0, b1);
-                        mma_bf16_16816(Up[2 * np + 1], a0, a1, a2, a3, b2, b3);
-                    }
-                }
-            }
-#pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
-                const int row = mt * 16 + g8, col = wc0 + nt * 8 + 2 * t4;
-                *reinterpret_cast<uint32_t *>(sm + OFF_W + sw(C, row, col)) = pack_bf16x2(wacc[nt][0], wacc[nt][1]);
-                *reinterpret_cast<uint32_t *>(sm + OFF_W + sw(C, row + 8, col)) = pack_bf16x2(wacc[nt][2], wacc[nt][3]);
-            }
-        }
-        __syncthreads();
-
-        // ---- P4: warps 0-3: U = U' - W S (m-tile w) -> bf16; warps 4-7: Q S (m-tile w-4), kept in registers
-        float qs[8][4];
-        {
-            const int mt = warp & 3;
-            const uint32_t abase = warp < 4 ? sb + OFF_W : stg + STG_Q;
-            float acc[8][4];
-#pragma unroll
-            for (int nt = 0; nt < 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-#pragma unroll
-            for (int ks = 0; ks < DK / 16; ++ks) {
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4(abase + sw(C, mt * 16 + (mi & 1) * 8 + r8, ks * 16 + (mi >> 1) * 8), a0, a1, a2, a3);
-#pragma unroll
-                for (int np = 0; np < 4; ++np) {
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4_t(sb + OFF_SB + sw(DK, ks * 16 + (mi & 1) * 8 + r8, np * 16 + (mi >> 1) * 8), b0, b1, b2, b3);
-                    mma_bf16_16816(acc[2 * np], a0, a1, a2, a3, b0, b1);
-                    mma_bf16_16816(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
-                }
-            }
-            if (warp < 4) {
-#pragma unroll
-                for (int nt = 0; nt < 8; ++nt) {
-                    const int row = mt * 16 + g8, col = nt * 8 + 2 * t4;
-                    *reinterpret_cast<uint32_t *>(sm + OFF_U + sw(C, row, col)) =
-                        pack_bf16x2(Up[nt][0] - acc[nt][0], Up[nt][1] - acc[nt][1]);
-                    *reinterpret_cast<uint32_t *>(sm + OFF_U + sw(C, row + 8, col)) =
-                        pack_bf16x2(Up[nt][2] - acc[nt][2], Up[nt][3] - acc[nt][3]);
+                    for (int u = 0; u < 8; ++u)
+                        dst[u] = make_uint4(pack_bf16x2(o[8 * u], o[8 * u + 1]), pack_bf16x2(o[8 * u + 2], o[8 * u + 3]),
+                                            pack_bf16x2(o[8 * u + 4], o[8 * u + 5]),
+                                            pack_bf16x2(o[8 * u + 6], o[8 * u + 7]));
                 }
             } else {
-#pragma unroll
-                for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) qs[nt][q] = acc[nt][q];
+                tc_fence_before();
+                mbar_arrive(bar(B_SREADY));
             }
         }
-        __syncthreads();
-
-        // ---- P5: warps 4-7: O = q_scale e^G Q S + QKm U -> bf16 out; warps 0-3: S = e^{G_C} S + Kt^T U
-        if (warp >= 4) {
-            const int mt = warp & 3;
-            float acc[8][4];
+        if (ok) {
 #pragma unroll
-            for (int nt = 0; nt < 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-#pragma unroll
-            for (int ks = 0; ks < C / 16; ++ks) {
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4(sb + OFF_QKM + sw(C, mt * 16 + (mi & 1) * 8 + r8, ks * 16 + (mi >> 1) * 8), a0, a1, a2, a3);
-#pragma unroll
-                for (int np = 0; np < 4; ++np) {
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4_t(sb + OFF_U + sw(C, ks * 16 + (mi & 1) * 8 + r8, np * 16 + (mi >> 1) * 8), b0, b1, b2, b3);
-                    mma_bf16_16816(acc[2 * np], a0, a1, a2, a3, b0, b1);
-                    mma_bf16_16816(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
+            for (int j = 0; j < 64; j += 4) *reinterpret_cast<float4 *>(Sg + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+        }
+    } else if (warp < 8) {
+        // ------------------------------------------------------------------ prep
+        const int pt = tid - 128, pw = warp - 4;
+        const uint32_t lane_off = (uint32_t)(pw * 32) << 16;
+        for (int c = 0; c < n_chunks; ++c) {
+            const int s = c & 1;
+            uint8_t *stg = sm + s * SLOT;
+            const float *Gst = reinterpret_cast<const float *>(stg + SL_G);
+            bool ok = mbar_wait(bar(B_FULL + s), (c >> 1) & 1, p.dev_err);
+            if (pt < C) {  // per-token scales as duplicated bf16 pairs, per-token decays e^{g}, and e^{G_C}
+                const float G = ok ? Gst[pt] : 0.f, GC = ok ? Gst[C - 1] : 0.f;
+                const float Gp = ok && pt > 0 ? Gst[pt - 1] : 0.f;
+                const uint32_t q1 = pack_bf16x2(p.q_scale * expf(G), 0.f) & 0xffffu;
+                const uint32_t k1 = pack_bf16x2(expf(GC - G), 0.f) & 0xffffu;
+                fq2[pt] = q1 | (q1 << 16);
+                fk2[pt] = k1 | (k1 << 16);
+                decv[pt] = expf(G - Gp);
+                if (pt == 0) dCv[c & 3] = expf(GC);
+            }
+            named_bar_sync(1, 128);
+            if (pw < 2) {
+                const int i = pt;
+                // QKm row i from Dq
+                if (ok) ok = mbar_wait(bar(B_QDONE), c & 1, p.dev_err);
+                float a[64];
+                if (ok) {
+                    tc_fence_after();
+                    tmem_ld64(tmem + lane_off + TM_DQ, a);
+                    tmem_wait_ld();
                 }
-            }
-            const int r0 = mt * 16 + g8;
-            const float f0 = p.q_scale * eG[r0], f1 = p.q_scale * eG[r0 + 8];
+                tc_fence_before();
+                mbar_arrive(bar(B_DQFREE));
+                {
+                    // q_scale e^{G_i - G_j} for j <= i as a running product of the per-token decays from j = i
+                    // down (e^{G_i - G_{j-1}} = e^{G_i - G_j} e^{g_j}): no exponentials, values only shrink.
+                    // Columns right of the warp's last row are all masked (a warp-uniform test).
+                    const int jmax = pw * 32 + 31;
+                    float e = p.q_scale;
 #pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
-                const int col = slice * DS + nt * 8 + 2 * t4;
-                if (t0 + r0 < p.T)
-                    *reinterpret_cast<uint32_t *>(p.o + (((size_t)b * p.T + t0 + r0) * p.H + h) * p.dv + col) =
-                        pack_bf16x2(acc[nt][0] + f0 * qs[nt][0], acc[nt][1] + f0 * qs[nt][1]);
-                if (t0 + r0 + 8 < p.T)
-                    *reinterpret_cast<uint32_t *>(p.o + (((size_t)b * p.T + t0 + r0 + 8) * p.H + h) * p.dv + col) =
-                        pack_bf16x2(acc[nt][2] + f1 * qs[nt][2], acc[nt][3] + f1 * qs[nt][3]);
-            }
-        } else {
-            const float dC = expf(Gv[C - 1]);
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) S[mt][nt][q] *= dC;
-#pragma unroll
-            for (int ks = 0; ks < C / 16; ++ks) {
-#pragma unroll
-                for (int mt = 0; mt < 2; ++mt) {
-                    // A = Kt^T rows (key dims) 32w + 16mt .. +16, k = tokens 16ks .. +16 (transposed load)
-                    uint32_t a0, a1, a2, a3;
-                    ldsm_x4_t(sb + OFF_KT + sw(C, ks * 16 + (mi >> 1) * 8 + r8, warp * 32 + mt * 16 + (mi & 1) * 8), a0,
-                              a1, a2, a3);
-#pragma unroll
-                    for (int np = 0; np < 4; ++np) {
-                        uint32_t b0, b1, b2, b3;
-                        ldsm_x4_t(sb + OFF_U + sw(C, ks * 16 + (mi & 1) * 8 + r8, np * 16 + (mi >> 1) * 8), b0, b1, b2,
-                                  b3);
-                        mma_bf16_16816(S[mt][2 * np], a0, a1, a2, a3, b0, b1);
-                        mma_bf16_16816(S[mt][2 * np + 1], a0, a1, a2, a3, b2, b3);
+                    for (int j = 63; j >= 0; --j) {
+                        if (j > jmax) {
+                            a[j] = 0.f;
+                            continue;
+                        }
+                        const bool in = j <= i;
+                        a[j] = in ? e * a[j] : 0.f;
+                        e = in ? e * decv[j] : e;
                     }
                 }
-            }
+                mbar_arrive(bar(B_EMPTY + s));  // last read of the stage by this thread
+                // QKm, -W and Q~ of chunk c - 1 are consumed once its O / Ds products completed
+                if (ok && c >= 1) ok = mbar_wait(bar(B_M23), (c - 1) & 1, p.dev_err);
+                if (ok) store_row64(sm + OFF_QKM, i, a, 1.f);
+                // -W row i from Dp
+                if (ok) ok = mbar_wait(bar(B_PDONE + s), (c >> 1) & 1, p.dev_err);
+                if (ok) {
+                    tc_fence_after();
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                for (int nt = 0; nt < 8; ++nt) {
-                    const int row = warp * 32 + mt * 16 + g8, col = nt * 8 + 2 * t4;
-                    *reinterpret_cast<uint32_t *>(sm + OFF_SB + sw(DK, row, col)) = pack_bf16x2(S[mt][nt][0], S[mt][nt][1]);
-                    *reinterpret_cast<uint32_t *>(sm + OFF_SB + sw(DK, row + 8, col)) =
-                        pack_bf16x2(S[mt][nt][2], S[mt][nt][3]);
+                    for (int kb = 0; kb < 2; ++kb) {
+                        tmem_ld64(tmem + lane_off + s * 192 + kb * 64, a);
+                        tmem_wait_ld();
+                        store_row64(sm + OFF_WQ + kb * 16384, i, a, 1.f);
+                    }
                 }
+            } else {
+                // thread q handles 16-byte unit q & 7 of rows (q >> 3) + 8 m (m < 8) of both 64-column boxes:
+                // the swizzled offset is a per-thread constant plus 1024 m
+                const int q = pt - 64, j0 = q >> 3;
+                const uint32_t off0 = swz(j0, q & 7);
+                // each product is formed in registers (all loads first) before its buffer frees
+                uint4 t[16];
+#pragma unroll
+                for (int n = 0; n < 16; ++n)  // Q~ = q_scale e^G Q
+                    t[n] = *reinterpret_cast<const uint4 *>(stg + (n >> 3) * 16384 + off0 + (n & 7) * 1024);
+#pragma unroll
+                for (int n = 0; n < 16; ++n) t[n] = scale8(t[n], fq2[j0 + 8 * (n & 7)]);
+                if (ok && c >= 1) ok = mbar_wait(bar(B_M1), (c - 1) & 1, p.dev_err);  // Q~ rows free
+                if (ok) {
+#pragma unroll
+                    for (int n = 0; n < 16; ++n)  // into rows 64-127 of -W | Q~
+                        *reinterpret_cast<uint4 *>(sm + OFF_WQ + 8192 + (n >> 3) * 16384 + off0 + (n & 7) * 1024) = t[n];
+                }
+#pragma unroll
+                for (int n = 0; n < 16; ++n)  // Kt = e^{G_C - G} K
+                    t[n] = *reinterpret_cast<const uint4 *>(stg + (n >> 3) * 16384 + 8192 + off0 + (n & 7) * 1024);
+#pragma unroll
+                for (int n = 0; n < 16; ++n) t[n] = scale8(t[n], fk2[j0 + 8 * (n & 7)]);
+                mbar_arrive(bar(B_EMPTY + s));
+                if (ok && c >= 1) ok = mbar_wait(bar(B_M23), (c - 1) & 1, p.dev_err);  // Kt free
+                if (ok) {
+#pragma unroll
+                    for (int n = 0; n < 16; ++n)
+                        *reinterpret_cast<uint4 *>(sm + OFF_KT + (n >> 3) * 8192 + off0 + (n & 7) * 1024) = t[n];
+                }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(bar(B_PREP + s));
+            if (!named_bar_and(1, 128, ok)) break;  // uniform: the scale vectors are rewritten next chunk
         }
-        __syncthreads();
+    } else if (warp == 8) {
+        // ------------------------------------------------------------------ state-chain MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t id_kmn = umma_idesc_bf16(128, 64, false, true);
+            constexpr uint32_t id_mnmn = umma_idesc_bf16(128, 64, true, true);
+            int last_bar = -1;
+            uint32_t last_par = 0;
+            for (int c = 0; c < n_chunks; ++c) {
+                const int slot = c & 1;
+                const uint32_t dcol = tmem + slot * 192 + 128;
+                if (!mbar_wait(bar(B_SREADY), c & 1, p.dev_err)) break;
+                if (!mbar_wait(bar(B_PREP + slot), (c >> 1) & 1, p.dev_err)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_bf16_ss(dcol, umma_desc_sw128(sb + OFF_WQ + kb * 16384 + kk * 32, 16, 1024),
+                                     umma_desc_sw128(sb + OFF_SB + (kb * 4 + kk) * 2048, 8192, 1024), id_kmn, 1);
+                umma_commit(bar(B_M1));
+                last_bar = B_M1;
+                last_par = c & 1;
+                if (!mbar_wait(bar(B_UREADY), c & 1, p.dev_err)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16_ss(dcol, umma_desc_sw128(sb + OFF_QKM - 8192 + kk * 32, 16, 1024),
+                                 umma_desc_sw128(sb + OFF_U + kk * 2048, 8192, 1024), id_kmn, 1);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16_ss(tmem + TM_DS, umma_desc_sw128(sb + OFF_KT + kk * 2048, 8192, 1024),
+                                 umma_desc_sw128(sb + OFF_U + kk * 2048, 8192, 1024), id_mnmn, kk > 0);
+                umma_commit(bar(B_M23));
+                last_bar = B_M23;
+            }
+            if (last_bar >= 0) mbar_wait(bar(last_bar), last_par, p.dev_err);  // own MMAs drained
+        }
+    } else if (warp == 9) {
+        // ------------------------------------------------------------------ prep MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t id_q = umma_idesc_bf16(128, 64, false, false);
+            constexpr uint32_t id_w = umma_idesc_bf16(128, 128, false, true);
+            constexpr uint32_t id_u = umma_idesc_bf16(128, 64, false, true);
+            int last_bar = -1;
+            uint32_t last_par = 0;
+            for (int c = 0; c < n_chunks; ++c) {
+                const int s = c & 1;
+                const uint32_t stg = sb + s * SLOT;
+                if (!mbar_wait(bar(B_FULL + s), (c >> 1) & 1, p.dev_err)) break;
+                if (c >= 1 && !mbar_wait(bar(B_DQFREE), (c - 1) & 1, p.dev_err)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_bf16_ss(tmem + TM_DQ, umma_desc_sw128(stg + kb * 16384 + kk * 32, 16, 1024),
+                                     umma_desc_sw128(stg + kb * 16384 + 8192 + kk * 32, 16, 1024), id_q, kb | kk);
+                umma_commit(bar(B_QDONE));
+                last_bar = B_QDONE;
+                last_par = c & 1;
+                if (c >= 2 && !mbar_wait(bar(B_DPFREE + s), ((c - 2) >> 1) & 1, p.dev_err)) break;
+                tc_fence_after();
+                // -W = T1 K (B = K key-major: two 64-column groups 16 KB apart) and U' = T2 V
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16_ss(tmem + s * 192, umma_desc_sw128(stg + SL_T1 + kk * 32, 16, 1024),
+                                 umma_desc_sw128(stg + 8192 + kk * 2048, 16384, 1024), id_w, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16_ss(tmem + s * 192 + 128, umma_desc_sw128(stg + SL_T2 + kk * 32, 16, 1024),
+                                 umma_desc_sw128(stg + SL_V + kk * 2048, 8192, 1024), id_u, kk > 0);
+                umma_commit(bar(B_PDONE + s));
+                umma_commit(bar(B_EMPTY + s));
+                last_bar = B_PDONE + s;
+                last_par = (c >> 1) & 1;
+            }
+            if (last_bar >= 0) mbar_wait(bar(last_bar), last_par, p.dev_err);  // own MMAs drained
+        }
+    } else {
+        // ------------------------------------------------------------------ TMA producer (+ G copy)
+        if (lane == 0) {
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            prefetch_tmap(&tmT);
+        }
+        int issued = 0;
+        for (int c = 0; c < n_chunks; ++c) {
+            const int s = c & 1;
+            const bool free_ok = c < 2 || mbar_wait(bar(B_EMPTY + s), ((c - 2) >> 1) & 1, p.dev_err);
+            if (!__all_sync(0xffffffffu, free_ok)) break;
+            const uint32_t stg = sb + s * SLOT, full = bar(B_FULL + s);
+            const size_t chunk_ix = bh * n_chunks + c;
+            if (lane == 0) {
+                const int row = b * p.T + c * C;
+                mbar_arrive_expect_tx(full, STAGE_TX);
+#pragma unroll
+                for (int d = 0; d < 2; ++d) {
+                    tma_load_3d(stg + d * 16384, &tmQ, d * 64, h, row, full);
+                    tma_load_3d(stg + d * 16384 + 8192, &tmK, d * 64, h, row, full);
+                }
+                tma_load_3d(stg + SL_V, &tmV, slice * DS, h, row, full);
+                tma_load_3d(stg + SL_T1, &tmT, 0, 0, (int)chunk_ix * 2 * C, full);
+                tma_load_3d(stg + SL_T2, &tmT, 0, 0, (int)chunk_ix * 2 * C + C, full);
+            }
+            reinterpret_cast<float2 *>(sm + s * SLOT + SL_G)[lane] =
+                __ldg(reinterpret_cast<const float2 *>(p.G + chunk_ix * C) + lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full);
+            issued = c + 1;
+        }
+        // every issued load has landed before the CTA may exit (bounded)
+        if (lane == 0)
+            for (int c = max(0, issued - 2); c < issued; ++c) mbar_wait(bar(B_FULL + (c & 1)), (c >> 1) & 1, p.dev_err);
     }
 
-    // ---- final state back to the layer's S
-    if (ok && warp < 4) {
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
-                const int row = warp * 32 + mt * 16 + g8, col = nt * 8 + 2 * t4;
-                Sg[(size_t)row * p.dv + col] = S[mt][nt][0];
-                Sg[(size_t)row * p.dv + col + 1] = S[mt][nt][1];
-                Sg[(size_t)(row + 8) * p.dv + col] = S[mt][nt][2];
-                Sg[(size_t)(row + 8) * p.dv + col + 1] = S[mt][nt][3];
-            }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
     }
 }
 
@@ -518,8 +622,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 bool deltanet_chunked_supported(int dk, int dv) { return dk == DK && dv % DS == 0 && dv <= 256; }
 
+size_t deltanet_chunked_tmat_bytes(int B, int T, int H) { return (size_t)B * H * ((T + C - 1) / C) * 2 * C * C * 2; }
+
 size_t deltanet_chunked_workspace(int B, int T, int H) {
-    return (size_t)B * H * ((T + C - 1) / C) * C * C * 2;
+    return deltanet_chunked_tmat_bytes(B, T, H) + (size_t)B * H * ((T + C - 1) / C) * C * 4;
 }
 
 cudaError_t launch_deltanet_chunked(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
@@ -530,12 +636,13 @@ cudaError_t launch_deltanet_chunked(cudaStream_t st, const CUtensorMap &tq, cons
     const int n_chunks = (T + C - 1) / C;
     cudaError_t e = cudaFuncSetAttribute(chunk_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSolveSmem);
     if (e != cudaSuccess) return e;
+    float *Gws = reinterpret_cast<float *>(static_cast<char *>(t_ws) + deltanet_chunked_tmat_bytes(B, T, H));
     chunk_solve_kernel<<<dim3(n_chunks, H, B), kSolveThreads, kSolveSmem, st>>>(
-        tk, beta, g, static_cast<__nv_bfloat16 *>(t_ws), T, H, dev_err);
+        tk, beta, g, static_cast<__nv_bfloat16 *>(t_ws), Gws, T, H, dev_err);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     ++*n_launches;
-    ChunkArgs p{beta, g, o, S, B, T, H, dv, n_chunks, q_scale, dev_err};
+    ChunkArgs p{Gws, o, S, B, T, H, dv, n_chunks, q_scale, dev_err};
     e = cudaFuncSetAttribute(deltanet_chunked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     deltanet_chunked_kernel<<<dim3(dv / DS, H, B), kThreads, kSmem, st>>>(tq, tk, tv, tt, p);

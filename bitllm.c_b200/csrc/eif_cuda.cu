@@ -918,13 +918,14 @@ static eif_status_t chunked_run(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int l
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
          reinterpret_cast<uintptr_t>(o)) & 15)
         return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "chunked prefill: q, k, v, o must be 16-byte aligned");
-    // scratch: the per-chunk T = (I + A)^-1 matrices, bf16 [batch][H][chunk][64][64]
+    // scratch: per chunk T diag(-b e^G) and T diag(b) with T = (I + A)^-1 (bf16 [batch][H][chunk][128][64]),
+    // then the cumulative log decays (fp32 [batch][H][chunk][64])
     const size_t ws = deltanet_chunked_workspace(st->batch, n_tok, st->H);
     eif_status_t rs = ensure_buffer(ctx, &ctx->ws, &ctx->ws_bytes, ws);
     if (rs != EIF_STATUS_OK) return rs;
     alignas(64) CUtensorMap tq, tk, tv, tt;
     const int rows = st->batch * n_tok;
-    const int t_rows = (int)(ws / 128);  // 64 bf16 per row
+    const int t_rows = (int)(deltanet_chunked_tmat_bytes(st->batch, n_tok, st->H) / 128);  // 64 bf16 per row
     if (!make_tok_tensor_map(&tq, q, rows, st->H, st->dk) || !make_tok_tensor_map(&tk, k, rows, st->H, st->dk) ||
         !make_tok_tensor_map(&tv, v, rows, st->H, st->dv) || !make_tok_tensor_map(&tt, ctx->ws, t_rows, 1, 64))
         return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "chunked prefill: cannot describe q / k / v for TMA");

@@ -113,7 +113,9 @@ cudaError_t launch_fullatt_prep(cudaStream_t st, const AttnPrepArgs &a);
 
 // Chunked (WY / UT) DeltaNet prefill (deltanet_chunked.cu).
 bool deltanet_chunked_supported(int dk, int dv);
-// Scratch bytes of the per-chunk T matrices (bf16 64 x 64 per sequence, head and chunk).
+// Scratch of the chunked prefill: per (sequence, head, chunk) the bf16 [128][64] pair T diag(-b e^G) ; T diag(b)
+// (deltanet_chunked_tmat_bytes, at the start), then the fp32 [64] cumulative log decays G.
+size_t deltanet_chunked_tmat_bytes(int B, int T, int H);
 size_t deltanet_chunked_workspace(int B, int T, int H);
 cudaError_t launch_deltanet_chunked(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
                                     const CUtensorMap &tv, const CUtensorMap &tt, void *t_ws, const float *beta,

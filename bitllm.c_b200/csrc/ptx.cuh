@@ -13,6 +13,11 @@
 
 EIF_DEV uint32_t smem_u32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
+// The dynamic shared-memory array rounded up to 1024 bytes by pointer arithmetic: the compiler still sees a
+// shared-memory pointer, so accesses through it become shared loads / stores (an integer round trip of
+// the address would turn them into generic ones).
+EIF_DEV uint8_t *smem_align1024(uint8_t *p) { return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u); }
+
 EIF_DEV void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
@@ -103,6 +108,24 @@ EIF_DEV float fast_exp2(float x) {
     return y;
 }
 
+// 2^x0, 2^x1 with one SFU op on a packed half pair (ex2.approx.f16x2): about 11 significant bits, results
+// below the half range flush towards 0, x above it gives +inf.  For factors that are rounded to bf16 after.
+EIF_DEV void fast_exp2_h2(float x0, float x1, float &y0, float &y1) {
+    uint32_t h;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));  // x0 in the low half
+    asm("ex2.approx.f16x2 %0, %0;" : "+r"(h));
+    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+        : "=f"(y0), "=f"(y1)
+        : "r"(h));
+}
+
+// Packed bf16 pair product (mul.rn.bf16x2).
+EIF_DEV uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 // Packed fp32 pairs (sm_100 f32x2 ALU ops): one instruction for two lanes of data.
 EIF_DEV unsigned long long f2_pack(float a, float b) {
     unsigned long long r;
@@ -139,6 +162,20 @@ EIF_DEV void split_bf16(float x, float &hi, float &lo) {
 
 EIF_DEV void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Named barrier over `threads` threads that also returns the AND of `pred` over them (a uniform verdict).
+EIF_DEV bool named_bar_and(int id, int threads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
 }
 
 // ------------------------------------------------------------------------------------------------
