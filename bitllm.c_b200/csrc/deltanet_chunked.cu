@@ -13,9 +13,9 @@
 //
 // Two kernels:
 //   chunk_solve_kernel   one CTA per (sequence, head, chunk), all in parallel: K K^T on the tensor cores,
-//                        A, then T = (I + A)^-1 in fp32 by blocked forward substitution (16 x 16 diagonal
-//                        blocks per warp, three block levels); writes T diag(-b e^G) and T diag(b) as bf16
-//                        [64 x 64] each, and G, per chunk.
+//                        A, then T = (I + A)^-1 in fp32 by forward substitution (one column of T per
+//                        thread, in registers); writes T diag(-b e^G) and T diag(b) as bf16 [64 x 64]
+//                        each, and G, per chunk.
 //   deltanet_chunked_kernel  one CTA per (sequence, head, 64-column slice of d_v): the columns of S
 //                        evolve independently (column j of u depends on column j of S only), so slices
 //                        need no communication.  Every chunk product runs on tcgen05 (bf16 operands in
@@ -69,12 +69,12 @@ __device__ __forceinline__ void load_chunk_gates(const float *beta, const float 
 // Kernel A: T = (I + A)^-1 of every chunk
 // ==================================================================================================
 constexpr int kSolveThreads = 128;
-constexpr int SOL_K = 0;                      // bf16 64 x 128 K tile (TMA)
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int SOL_K = 0;                      // bf16 64 x 128 K tile (TMA); later fp32 [64][64] T
 constexpr int SOL_A = C * DK * 2;             // fp32 [64][FP] A
-constexpr int SOL_T = SOL_A + C * FP * 4;     // fp32 [64][FP] T
-constexpr int SOL_VEC = SOL_T + C * FP * 4;   // G[64], beta[64], -beta e^G [64]
+constexpr int SOL_VEC = SOL_A + C * FP * 4;   // G[64], beta[64], -beta e^G [64]
 constexpr int SOL_BAR = SOL_VEC + 3 * C * 4;
-constexpr int kSolveSmem = SOL_BAR + 16 + 1024;
+constexpr int kSolveSmem = SOL_BAR + 16 + 1024;  // ~35 KB: six CTAs per SM
 
 // Outputs per (sequence, head, chunk): Tout [128][64] bf16 = T diag(-b e^G) ; T diag(b) (the A operands
 // of W and U' in the state kernel, with the minus sign of U = U' - W S folded in) and Gout [64] fp32 = G.
@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *sm = smem_align1024(smem_raw);
     const uint32_t sb = smem_u32(sm);
-    float *Af = reinterpret_cast<float *>(sm + SOL_A), *Tf = reinterpret_cast<float *>(sm + SOL_T);
+    float *Af = reinterpret_cast<float *>(sm + SOL_A), *Tf = reinterpret_cast<float *>(sm + SOL_K);
     float *Gv = reinterpret_cast<float *>(sm + SOL_VEC), *Bv = Gv + C, *Xv = Gv + 2 * C;
     const uint32_t bar = smem_u32(sm + SOL_BAR);
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z, n_chunks = gridDim.x;
@@ -107,7 +107,8 @@ __global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid
     if (!__syncthreads_and(ok)) return;
     if (tid < C) Xv[tid] = -Bv[tid] * expf(Gv[tid]);  // read after the solve's barriers
 
-    // K K^T: warp w owns rows 16w..16w+15; A_ij = b_i e^{G_i - G_j} k_i.k_j for j < i
+    // K K^T: warp w owns rows 16w..16w+15 and needs the columns j < 16 (w + 1) only (16-column groups
+    // np <= w); A_ij = b_i e^{G_i - G_j} k_i.k_j for j < i, 0 elsewhere
     {
         float acc[8][4];
 #pragma unroll
@@ -118,76 +119,80 @@ __global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid
             ldsm_x4(sb + SOL_K + sw(C, warp * 16 + (mi & 1) * 8 + r8, ks * 16 + (mi >> 1) * 8), a0, a1, a2, a3);
 #pragma unroll
             for (int np = 0; np < 4; ++np) {
+                if (np > warp) break;  // warp-uniform
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(sb + SOL_K + sw(C, np * 16 + (mi >> 1) * 8 + r8, ks * 16 + (mi & 1) * 8), b0, b1, b2, b3);
                 mma_bf16_16816(acc[2 * np], a0, a1, a2, a3, b0, b1);
                 mma_bf16_16816(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
             }
         }
+        const int i0 = warp * 16 + g8;
+        const float gi0 = Gv[i0] * kLog2e, gi1 = Gv[i0 + 8] * kLog2e, bi0 = Bv[i0], bi1 = Bv[i0 + 8];
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int i = warp * 16 + g8 + (q >> 1) * 8, j = nt * 8 + 2 * t4 + (q & 1);
-                Af[i * FP + j] = j < i ? Bv[i] * expf(Gv[i] - Gv[j]) * acc[nt][q] : 0.f;
-            }
+        for (int nt = 0; nt < 8; ++nt) {
+            const int j = nt * 8 + 2 * t4;
+            const float2 gj = *reinterpret_cast<const float2 *>(Gv + j);
+            const float gj0 = gj.x * kLog2e, gj1 = gj.y * kLog2e;
+            // e^{G_i - G_j} <= 1 on the SFU (ex2.approx, relative error ~2^-22)
+            *reinterpret_cast<float2 *>(Af + i0 * FP + j) =
+                make_float2(j < i0 ? bi0 * fast_exp2(gi0 - gj0) * acc[nt][0] : 0.f,
+                            j + 1 < i0 ? bi0 * fast_exp2(gi0 - gj1) * acc[nt][1] : 0.f);
+            *reinterpret_cast<float2 *>(Af + (i0 + 8) * FP + j) =
+                make_float2(j < i0 + 8 ? bi1 * fast_exp2(gi1 - gj0) * acc[nt][2] : 0.f,
+                            j + 1 < i0 + 8 ? bi1 * fast_exp2(gi1 - gj1) * acc[nt][3] : 0.f);
+        }
     }
-    __syncthreads();
+    __syncthreads();  // A complete; the K tile is dead from here on (its space holds T)
 
-    // diagonal 16 x 16 blocks (lanes 0-15 of each warp: one column each); lanes 16-31 zero the upper blocks
-    if (lane < 16) {
-        const int o = warp * 16, cidx = lane;
-        float col[16];
+    // T = (I + A)^-1 by forward substitution in fp32: t_r = [r == c] - sum_{m < r} A_rm t_m per column c.
+    // Two threads per column (lanes 2c, 2c + 1 of a warp): thread hf keeps the column entries m with
+    // (m >> 2) & 1 == hf in registers (local index 4 (m >> 3) + (m & 3)) and sums its half of each row
+    // from float4 broadcasts of A; a lane shuffle joins the halves.  Entries not yet formed are 0 and A is
+    // 0 on and above the diagonal, so no masking is needed; rows above the diagonal come out exactly 0.
+    {
+        const int cidx = tid >> 1, hf = tid & 1;
+        float tl[C / 2];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            float acc = r == cidx ? 1.f : 0.f;
+        for (int k = 0; k < C / 2; ++k) tl[k] = 0.f;
 #pragma unroll
-            for (int m = 0; m < 16; ++m)
-                if (m < r) acc -= Af[(o + r) * FP + o + m] * col[m];
-            col[r] = r < cidx ? 0.f : acc;
+        for (int r = 0; r < C; ++r) {
+            const float *arow = Af + r * FP + 4 * hf;
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+            for (int g = 0; 8 * g < r; ++g) {
+                const float4 a4 = *reinterpret_cast<const float4 *>(arow + 8 * g);
+                s0 = fmaf(a4.x, tl[4 * g], s0);
+                s1 = fmaf(a4.y, tl[4 * g + 1], s1);
+                s2 = fmaf(a4.z, tl[4 * g + 2], s2);
+                s3 = fmaf(a4.w, tl[4 * g + 3], s3);
+            }
+            float s = (s0 + s1) + (s2 + s3);
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            const float tr = (r == cidx ? 1.f : 0.f) - s;
+            const int k = 4 * (r >> 3) + (r & 3);
+            tl[k] = ((r >> 2) & 1) == hf ? tr : tl[k];
         }
 #pragma unroll
-        for (int r = 0; r < 16; ++r) Tf[(o + r) * FP + o + cidx] = col[r];
-    } else {
-        for (int e = warp * 16 + lane - 16; e < C * C; e += 64) {
-            const int i = e >> 6, j = e & 63;
-            if ((j >> 4) > (i >> 4)) Tf[i * FP + j] = 0.f;
-        }
+        for (int k = 0; k < C / 2; ++k) Tf[(8 * (k >> 2) + 4 * hf + (k & 3)) * C + cidx] = tl[k];
     }
     __syncthreads();
-    // off-diagonal blocks by level: T_IJ = -T_II sum_{K=J}^{I-1} A_IK T_KJ; R_IJ kept in block (J, I)
-    for (int lvl = 1; lvl <= 3; ++lvl) {
-        const int nblk = 4 - lvl;
-        for (int e = tid; e < nblk * 256; e += kSolveThreads) {
-            const int J = e >> 8, I = J + lvl, rr = (e >> 4) & 15, cc = e & 15;
-            float acc = 0.f;
-            for (int K = J; K < I; ++K)
-#pragma unroll
-                for (int m = 0; m < 16; ++m) acc += Af[(I * 16 + rr) * FP + K * 16 + m] * Tf[(K * 16 + m) * FP + J * 16 + cc];
-            Tf[(J * 16 + rr) * FP + I * 16 + cc] = acc;
-        }
-        __syncthreads();
-        for (int e = tid; e < nblk * 256; e += kSolveThreads) {
-            const int J = e >> 8, I = J + lvl, rr = (e >> 4) & 15, cc = e & 15;
-            float acc = 0.f;
-#pragma unroll
-            for (int m = 0; m < 16; ++m) acc -= Tf[(I * 16 + rr) * FP + I * 16 + m] * Tf[(J * 16 + m) * FP + I * 16 + cc];
-            Tf[(I * 16 + rr) * FP + J * 16 + cc] = acc;
-        }
-        __syncthreads();
-    }
     // T diag(-b e^G) ; T diag(b) (T lower triangular) -> bf16 rows of 64 for the state kernel's TMA; G
     const size_t chunk_ix = ((size_t)b * H + h) * n_chunks + c;
     __nv_bfloat16 *dst = Tout + chunk_ix * 2 * C * C;
-    for (int e = tid; e < C * C / 8; e += kSolveThreads) {
+    for (int e = tid; e < C * C / 8; e += kSolveThreads) {  // T is exactly 0 above the diagonal
         const int i = e >> 3, j0 = (e & 7) * 8;
+        const float4 ta = *reinterpret_cast<const float4 *>(Tf + i * C + j0);
+        const float4 tb = *reinterpret_cast<const float4 *>(Tf + i * C + j0 + 4);
+        const float4 xa = *reinterpret_cast<const float4 *>(Xv + j0), xb = *reinterpret_cast<const float4 *>(Xv + j0 + 4);
+        const float4 ba = *reinterpret_cast<const float4 *>(Bv + j0), bb = *reinterpret_cast<const float4 *>(Bv + j0 + 4);
+        const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
+        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        const float bv[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
         uint32_t w1[4], w2[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            const int j = j0 + 2 * q;
-            const float t0 = j <= i ? Tf[i * FP + j] : 0.f, t1 = j + 1 <= i ? Tf[i * FP + j + 1] : 0.f;
-            w1[q] = pack_bf16x2(t0 * Xv[j], t1 * Xv[j + 1]);
-            w2[q] = pack_bf16x2(t0 * Bv[j], t1 * Bv[j + 1]);
+            w1[q] = pack_bf16x2(tv[2 * q] * xv[2 * q], tv[2 * q + 1] * xv[2 * q + 1]);
+            w2[q] = pack_bf16x2(tv[2 * q] * bv[2 * q], tv[2 * q + 1] * bv[2 * q + 1]);
         }
         *reinterpret_cast<uint4 *>(dst + i * C + j0) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
         *reinterpret_cast<uint4 *>(dst + C * C + i * C + j0) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
@@ -433,14 +438,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int jmax = pw * 32 + 31;
                     float e = p.q_scale;
 #pragma unroll
-                    for (int j = 63; j >= 0; --j) {
-                        if (j > jmax) {
-                            a[j] = 0.f;
+                    for (int u = 7; u >= 0; --u) {
+                        if (8 * u > jmax) {
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) a[8 * u + q] = 0.f;
                             continue;
                         }
-                        const bool in = j <= i;
-                        a[j] = in ? e * a[j] : 0.f;
-                        e = in ? e * decv[j] : e;
+                        const float4 d0 = reinterpret_cast<const float4 *>(decv)[2 * u];
+                        const float4 d1 = reinterpret_cast<const float4 *>(decv)[2 * u + 1];
+                        const float d[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+#pragma unroll
+                        for (int q = 7; q >= 0; --q) {
+                            const int j = 8 * u + q;
+                            const bool in = j <= i;
+                            a[j] = in ? e * a[j] : 0.f;
+                            e = in ? e * d[q] : e;
+                        }
                     }
                 }
                 mbar_arrive(bar(B_EMPTY + s));  // last read of the stage by this thread
