@@ -272,7 +272,7 @@ def run_ours(args, torch, dist, rank, world, local_rank):
     pkg = __graft_entry__.load_package()
     torch.cuda.set_device(local_rank)
     GB = args.batch
-    B = GB // world
+    B = pkg.shard.shard(GB, 1, world, rank).nb  # by sequence (layers differ in head count)
     ctx = pkg.Context(local_rank)
     # one explicit stream for the library's launches, the fills and the timing events
     stream = torch.cuda.Stream()
@@ -507,7 +507,10 @@ def run_prefill(args, torch, dist, rank, world, local_rank):
     import __graft_entry__
     pkg = __graft_entry__.load_package()
     torch.cuda.set_device(local_rank)
-    B = max(1, PF_B // world)
+    # (sequence, kv-head group) units: past 8 ranks a sequence's two kv groups go to different ranks
+    sh = pkg.shard.shard(PF_B, PF_HKV, world, rank)
+    B, hkv = sh.nb, sh.nh
+    hq = hkv * (PF_HQ // PF_HKV)
     ctx = pkg.Context(local_rank)
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -515,16 +518,16 @@ def run_prefill(args, torch, dist, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     gen = torch.Generator(device=dev)
     gen.manual_seed(11 + rank)
-    kv = pkg.KVCache(ctx, 1, B, PF_S, PF_HKV, PF_D, pkg.BF16)
+    kv = pkg.KVCache(ctx, 1, B, PF_S, hkv, PF_D, pkg.BF16)
     for p in kv.layer_ptrs(0):
-        torch.as_tensor(CudaArray(p, (B * PF_S * PF_HKV * PF_D,), "<i2"), device=dev).view(torch.bfloat16).normal_(
+        torch.as_tensor(CudaArray(p, (B * PF_S * hkv * PF_D,), "<i2"), device=dev).view(torch.bfloat16).normal_(
             generator=gen)
-    q = torch.randn(B, PF_S, PF_HQ * PF_D, device=dev, generator=gen).to(torch.bfloat16)
+    q = torch.randn(B, PF_S, hq * PF_D, device=dev, generator=gen).to(torch.bfloat16)
     out = torch.empty_like(q)
     scale = 1.0 / math.sqrt(PF_D)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2: evicts q / K / V between launches
     for _ in range(args.warmup):
-        kv.attend_prefill_dev(0, q.data_ptr(), PF_S, 0, PF_HQ, scale, out.data_ptr())
+        kv.attend_prefill_dev(0, q.data_ptr(), PF_S, 0, hq, scale, out.data_ptr())
     torch.cuda.synchronize()
     ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(args.steps)]
     clocks = ClockSampler(local_rank)
@@ -536,7 +539,7 @@ def run_prefill(args, torch, dist, rank, world, local_rank):
     for s in range(args.steps):
         flush.zero_()
         ev[s][0].record()
-        kv.attend_prefill_dev(0, q.data_ptr(), PF_S, 0, PF_HQ, scale, out.data_ptr())
+        kv.attend_prefill_dev(0, q.data_ptr(), PF_S, 0, hq, scale, out.data_ptr())
         ev[s][1].record()
     torch.cuda.synchronize()
     launches = ctx.launch_count - l0
@@ -548,27 +551,28 @@ def run_prefill(args, torch, dist, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
     # e2e through the host-pointer ABI: fp32 q from pinned host memory, fp32 output read back
-    qh = torch.randn(B, PF_S, PF_HQ * PF_D, generator=torch.Generator().manual_seed(3)).pin_memory().numpy()
+    qh = torch.randn(B, PF_S, hq * PF_D, generator=torch.Generator().manual_seed(3)).pin_memory().numpy()
     ctx.set_stream(None)
-    kv.attend_prefill(0, qh, PF_S, 0, PF_HQ, scale)
+    kv.attend_prefill(0, qh, PF_S, 0, hq, scale)
     t0 = time.perf_counter()
     for _ in range(max(1, args.steps // 4)):
-        kv.attend_prefill(0, qh, PF_S, 0, PF_HQ, scale)
-    e2e_ms = (time.perf_counter() - t0) * 1e3 / max(1, args.steps // 4)
+        kv.attend_prefill(0, qh, PF_S, 0, hq, scale)
+    e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / max(1, args.steps // 4), "cuda")
     if rank != 0:
         return None
     _, tflops_peak, src = peaks()
-    flops = prefill_flops(B, PF_S)
+    flops = prefill_flops(B, PF_S) * hq / PF_HQ  # this rank's launch
     ach = flops / (ms * 1e-3) / 1e12
-    GB = B * world
+    GB = PF_B
     line = {"metric": "causal prefill attention tokens/s (BASELINE configs[1])", "value": GB * PF_S / (ms * 1e-3),
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16 in, fp32 accumulate, bf16 out", "data": "synthetic (seeded)",
             "config": {"workload": "gqa_causal_prefill (BASELINE configs[1])", "global_batch": GB, "seq_len": PF_S,
-                       "heads": "12 q / 2 kv", "head_dim": PF_D, "l2": "256 MiB flush between launches"},
-            "e2e": {"value": B * PF_S / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": qh.nbytes, "d2h_bytes_per_step": qh.nbytes,
+                       "heads": "12 q / 2 kv", "head_dim": PF_D, "l2": "256 MiB flush between launches",
+                       "parallelism": f"(sequence, kv head) units over {world} rank(s), no collective"},
+            "e2e": {"value": GB * PF_S / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": qh.nbytes * world, "d2h_bytes_per_step": qh.nbytes * world,
                     "path": "host-pointer C ABI eif_cuda_attend_prefill (fp32 in/out)"},
             "roofline": {"kernel": "attn_prefill_tc_kernel", "bound": "tensor", "achieved": ach,
                          "peak": tflops_peak, "unit": "TFLOP/s", "frac": ach / tflops_peak, "peak_source": src,
@@ -589,7 +593,8 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
     import __graft_entry__
     pkg = __graft_entry__.load_package()
     torch.cuda.set_device(local_rank)
-    B = max(1, CK_B // world)
+    sh = pkg.shard.shard(CK_B, CK_H, world, rank)  # (sequence, head) units; past 4 ranks heads split
+    B, H = sh.nb, sh.nh
     ctx = pkg.Context(local_rank)
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -597,16 +602,16 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     gen = torch.Generator(device=dev)
     gen.manual_seed(21 + rank)
-    qk = torch.randn(2, B, CK_T, CK_H, CK_D, device=dev, generator=gen)
+    qk = torch.randn(2, B, CK_T, H, CK_D, device=dev, generator=gen)
     qk = (qk / torch.sqrt((qk * qk).sum(-1, keepdim=True) + 1e-12)).to(torch.bfloat16)
     q, k = qk[0].contiguous(), qk[1].contiguous()
-    v = torch.randn(B, CK_T, CK_H, CK_D, device=dev, generator=gen).to(torch.bfloat16)
-    beta = torch.sigmoid(torch.randn(B, CK_T, CK_H, device=dev, generator=gen))
-    g = -torch.nn.functional.softplus(torch.randn(B, CK_T, CK_H, device=dev, generator=gen))
+    v = torch.randn(B, CK_T, H, CK_D, device=dev, generator=gen).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(B, CK_T, H, device=dev, generator=gen))
+    g = -torch.nn.functional.softplus(torch.randn(B, CK_T, H, device=dev, generator=gen))
     o = torch.empty_like(v)
-    st = pkg.DeltaState(ctx, 1, B, CK_H, CK_D, CK_D)
+    st = pkg.DeltaState(ctx, 1, B, H, CK_D, CK_D)
     s_ptr, _ = st.layer_ptrs(0)
-    S = torch.as_tensor(CudaArray(s_ptr, (B * CK_H * CK_D * CK_D,), "<f4"), device=dev)
+    S = torch.as_tensor(CudaArray(s_ptr, (B * H * CK_D * CK_D,), "<f4"), device=dev)
     qs = 1.0 / math.sqrt(CK_D)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
@@ -643,8 +648,9 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
     if rank != 0:
         return None
     hbm, _, src = peaks()
-    GB = B * world
-    bytes_alg = GB * CK_T * CK_H * (3 * CK_D * 2 + 2 * 4 + CK_D * 2) + 2 * GB * CK_H * CK_D * CK_D * 4
+    GB = CK_B
+    # this rank's launch: q, k, v, o (bf16) + beta, g per token-head, S read and written once
+    bytes_alg = B * CK_T * H * (3 * CK_D * 2 + 2 * 4 + CK_D * 2) + 2 * B * H * CK_D * CK_D * 4
     ach = bytes_alg / (ms * 1e-3) / 1e9
     flops_rec = 4.0 * CK_D * CK_D * GB * CK_T * CK_H
     return {"metric": "chunked DeltaNet prefill tokens/s (BASELINE configs[3])", "value": GB * CK_T / (ms * 1e-3),
@@ -653,7 +659,8 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
             "dtype": "bf16 q/k/v/o, fp32 state and accumulate", "data": "synthetic (seeded)",
             "config": {"workload": "deltanet_chunked_prefill (BASELINE configs[3])", "global_batch": GB,
                        "seq_len": CK_T, "heads": CK_H, "head_dim": CK_D, "chunk": 64,
-                       "l2": "256 MiB flush between launches"},
+                       "l2": "256 MiB flush between launches",
+                       "parallelism": f"(sequence, head) units over {world} rank(s), no collective"},
             "roofline": {"kernel": "deltanet_chunked_kernel", "bound": "hbm", "achieved": ach, "peak": hbm,
                          "unit": "GB/s", "frac": ach / hbm, "peak_source": src, "algorithmic_bytes_per_launch":
                              bytes_alg, "recurrent_equivalent_tflops": flops_rec / (ms * 1e-3) / 1e12,

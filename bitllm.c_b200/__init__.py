@@ -10,3 +10,4 @@ The directory name contains a dot, so load it by path (``__graft_entry__.load_pa
 from .eif_cuda import (BF16, F32, SUBLN_NONE, SUBLN_RMS, SUBLN_WEIGHT, STATUS, Context, DeltaState,  # noqa: F401
                        EifCudaError, KVCache, device_count, header_functions, lib, LIB_PATH)
 from .build import build  # noqa: F401
+from . import shard  # noqa: F401
