@@ -23,7 +23,8 @@
 //               first 64 columns of its own S buffer with tcgen05.st; at the end O / l -> bf16 -> global.
 // The two tiles ping-pong: while one warpgroup runs its softmax the tensor cores run the other
 // tile's PV and S.  P never touches shared memory, so each PV product reads only V from smem.
-// TMEM: S_A (and P_A) [0,128), S_B (P_B) [128,256), O_A [256,384), O_B [384,512).
+// Instantiated for head_dim 64 and 128 (one or two 64-column boxes per tile).
+// TMEM: S_A (and P_A) [0,128), S_B (P_B) [128,256), O_A [256, 256 + HD), O_B [256 + HD, 256 + 2 HD).
 // Work order: the longest causal rows first, so the tail is short tiles.
 #include <math.h>
 
@@ -33,13 +34,20 @@
 
 namespace {
 
-constexpr int BM = 128, BN = 128, HD = 128;
+constexpr int BM = 128, BN = 128;
+constexpr int BOX = BM * 128;  // 16 KB: one 64-column swizzled box of a 128-row Q, K or V tile
 constexpr int kPThreads = 320;
-constexpr int TILE = BM * HD * 2;  // 32 KB: one Q, K or V tile (two 64-column swizzled boxes)
-constexpr int OFF_Q = 0, OFF_K = 2 * TILE, OFF_V = 4 * TILE, OFF_BAR = 6 * TILE;  // Q_A, Q_B | K[2] | V[2]
-constexpr int kPSmem = OFF_BAR + 256 + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
+
+// Shared-memory plan of the HD (64 or 128) instantiation: Q_A, Q_B | K[2] | V[2], HD / 64 boxes per tile.
+template <int HD>
+struct PrefillLayout {
+    static constexpr int NBOX = HD / 64;
+    static constexpr int TILE = NBOX * BOX;
+    static constexpr int OFF_Q = 0, OFF_K = 2 * TILE, OFF_V = 4 * TILE, OFF_BAR = 6 * TILE;
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;
+};
 
 struct PrefillParams {
     int B, n_tok, start_pos, Hq, Hkv, G, max_seq, n_pairs;
@@ -94,9 +102,13 @@ enum {
     BAR_COUNT = 15
 };
 
+template <int HD>
 __global__ void __launch_bounds__(kPThreads, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
+    using L = PrefillLayout<HD>;
+    constexpr int TILE = L::TILE, NBOX = L::NBOX, OFF_Q = L::OFF_Q, OFF_K = L::OFF_K, OFF_V = L::OFF_V,
+                  OFF_BAR = L::OFF_BAR;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_align1024(smem_raw);
     const uint32_t sbase = smem_u32(smem);
@@ -151,9 +163,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
             const int nq = rows[1] > 0 ? 2 : 1;
             mbar_arrive_expect_tx(bar(BAR_Q), nq * TILE);
             for (int t = 0; t < nq; ++t)
-                for (int d = 0; d < 2; ++d)
-                    tma_load_3d(sbase + OFF_Q + t * TILE + d * (TILE / 2), &tmQ, d * 64, h, b * p.n_tok + q0[t],
-                                bar(BAR_Q));
+                for (int d = 0; d < NBOX; ++d)
+                    tma_load_3d(sbase + OFF_Q + t * TILE + d * BOX, &tmQ, d * 64, h, b * p.n_tok + q0[t], bar(BAR_Q));
             for (int j = 0; j < nkv_all; ++j) {
                 const int s = j & 1;
                 const uint32_t par = ((j >> 1) & 1) ^ 1;
@@ -161,15 +172,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 if (!mbar_wait(bar(BAR_KEMPTY + s), par, p.dev_err)) break;
                 mbar_arrive_expect_tx(bar(BAR_KFULL + s), TILE);
                 const uint32_t kdst = sbase + OFF_K + s * TILE, vdst = sbase + OFF_V + s * TILE;
-                for (int d = 0; d < 2; ++d)
+                for (int d = 0; d < NBOX; ++d)
                     for (int hf = 0; hf < 2; ++hf)
-                        tma_load_3d(kdst + d * (TILE / 2) + hf * (TILE / 4), &tmK, d * 64, kvh, row + hf * 64,
+                        tma_load_3d(kdst + d * BOX + hf * (BOX / 2), &tmK, d * 64, kvh, row + hf * 64,
                                     bar(BAR_KFULL + s));
                 if (!mbar_wait(bar(BAR_VEMPTY + s), par, p.dev_err)) break;
                 mbar_arrive_expect_tx(bar(BAR_VFULL + s), TILE);
-                for (int d = 0; d < 2; ++d)
+                for (int d = 0; d < NBOX; ++d)
                     for (int hf = 0; hf < 2; ++hf)
-                        tma_load_3d(vdst + d * (TILE / 2) + hf * (TILE / 4), &tmV, d * 64, kvh, row + hf * 64,
+                        tma_load_3d(vdst + d * BOX + hf * (BOX / 2), &tmV, d * 64, kvh, row + hf * 64,
                                     bar(BAR_VFULL + s));
             }
         }
@@ -187,9 +198,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 if (first_bad < BN) {
                     // their p is 0, but 0 * (a non-finite stale row) would be NaN: zero those V rows
                     for (int r = max(first_bad, 0); r < BN; ++r)
-                        for (int d = 0; d < 2; ++d)
+                        for (int d = 0; d < NBOX; ++d)
                             if (lane < 8)
-                                reinterpret_cast<uint4 *>(smem + OFF_V + sv * TILE + d * (TILE / 2) + r * 128)[lane] =
+                                reinterpret_cast<uint4 *>(smem + OFF_V + sv * TILE + d * BOX + r * 128)[lane] =
                                     make_uint4(0, 0, 0, 0);
                     fence_proxy_async_smem();
                     __syncwarp();
@@ -205,9 +216,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         const uint32_t vb = sbase + OFF_V + sv * TILE;
 #pragma unroll
                         for (int kk = 0; kk < BN / 16; ++kk)
-                            umma_bf16_ts(tmem + (2 + t) * BN, tmem + t * BN + kk * 8,
-                                         umma_desc_sw128(vb + kk * 2048, TILE / 2, 1024), idesc_pv,
-                                         (jj > 0 || kk > 0));
+                            umma_bf16_ts(tmem + 2 * BN + t * HD, tmem + t * BN + kk * 8,
+                                         umma_desc_sw128(vb + kk * 2048, BOX, 1024), idesc_pv, (jj > 0 || kk > 0));
                         umma_commit(bar(BAR_PEMPTY + t));
                     }
                     __syncwarp();
@@ -218,7 +228,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         const uint32_t qb = sbase + OFF_Q + t * TILE, kb = sbase + OFF_K + s * TILE;
 #pragma unroll
                         for (int kk = 0; kk < HD / 16; ++kk) {
-                            const uint32_t off = (kk >> 2) * (TILE / 2) + (kk & 3) * 32;
+                            const uint32_t off = (kk >> 2) * BOX + (kk & 3) * 32;
                             umma_bf16_ss(tmem + t * BN, umma_desc_sw128(qb + off, 16, 1024),
                                          umma_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0);
                         }
@@ -239,7 +249,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const int t = warp >> 2;
         const int r = threadIdx.x & 127;  // query row of the tile == TMEM lane
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t s_col = tmem + lane_base + t * BN, o_col = tmem + lane_base + (2 + t) * BN;
+        const uint32_t s_col = tmem + lane_base + t * BN, o_col = tmem + lane_base + 2 * BN + t * HD;
         const int qpos = p.start_pos + q0[t] + r;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
@@ -349,11 +359,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
 }  // namespace
 
-bool prefill_tc_supported(int D) { return D == HD; }
+bool prefill_tc_supported(int D) { return D == 64 || D == 128; }
 
 cudaError_t launch_attend_prefill_tc(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
                                      const CUtensorMap &tv, int B, int n_tok, int start_pos, int Hq, int Hkv,
-                                     int max_seq, float scale, __nv_bfloat16 *out, unsigned *dev_err) {
+                                     int max_seq, int D, float scale, __nv_bfloat16 *out, unsigned *dev_err) {
     PrefillParams p;
     p.B = B;
     p.n_tok = n_tok;
@@ -366,9 +376,14 @@ cudaError_t launch_attend_prefill_tc(cudaStream_t st, const CUtensorMap &tq, con
     p.scale_log2 = scale * 1.4426950408889634f;
     p.out = out;
     p.dev_err = dev_err;
-    cudaError_t e = cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
-    if (e != cudaSuccess) return e;
     const unsigned grid = (unsigned)(p.n_pairs * B * Hq);
-    attn_prefill_tc_kernel<<<grid, kPThreads, kPSmem, st>>>(tq, tk, tv, p);
-    return cudaGetLastError();
+    auto run = [&](auto kernel, int smem) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        kernel<<<grid, kPThreads, smem, st>>>(tq, tk, tv, p);
+        return cudaGetLastError();
+    };
+    if (D == 64) return run(attn_prefill_tc_kernel<64>, PrefillLayout<64>::SMEM);
+    if (D == 128) return run(attn_prefill_tc_kernel<128>, PrefillLayout<128>::SMEM);
+    return cudaErrorInvalidValue;
 }

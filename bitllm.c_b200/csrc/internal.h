@@ -122,11 +122,11 @@ cudaError_t launch_deltanet_chunked(cudaStream_t st, const CUtensorMap &tq, cons
                                     const float *g, __nv_bfloat16 *o, float *S, int B, int T, int H, int dv,
                                     float q_scale, unsigned *dev_err, int *n_launches);
 
-// Causal prefill attention on tcgen05 (attn_prefill_tc.cu).
+// Causal prefill attention on tcgen05 (attn_prefill_tc.cu), head_dim D.
 bool prefill_tc_supported(int D);
 cudaError_t launch_attend_prefill_tc(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
                                      const CUtensorMap &tv, int B, int n_tok, int start_pos, int Hq, int Hkv,
-                                     int max_seq, float scale, __nv_bfloat16 *out, unsigned *dev_err);
+                                     int max_seq, int D, float scale, __nv_bfloat16 *out, unsigned *dev_err);
 
 // Fills the TMA descriptors (made on first use per layer) and the kernel choice of `a` (eif_cuda.cu).
 void decode_prepare(eif_cuda_kv_t *kv, int layer, DecodeArgs &a);

@@ -27,13 +27,15 @@ def setup(pkg, ctx, orc, rng, B, rows, max_seq, nkv, hd=128):
     return kv, kc, vc
 
 
-@pytest.mark.parametrize("B,n_tok,start_pos,nh,nkv", [(2, 300, 0, 12, 2), (1, 128, 0, 4, 4), (3, 130, 200, 8, 2),
-                                                      (2, 1, 77, 12, 2), (1, 257, 3, 6, 1)])
-def test_prefill_vs_oracle(pkg, ctx, orc, B, n_tok, start_pos, nh, nkv):
-    rng = np.random.default_rng(n_tok * 7 + start_pos)
-    hd = 128
+@pytest.mark.parametrize("B,n_tok,start_pos,nh,nkv,hd", [
+    (2, 300, 0, 12, 2, 128), (1, 128, 0, 4, 4, 128), (3, 130, 200, 8, 2, 128), (2, 1, 77, 12, 2, 128),
+    (1, 257, 3, 6, 1, 128),
+    # head_dim 64: the Qwen2.5-0.5B attention shape (14 q / 2 kv heads) and a ragged continuation
+    (2, 300, 0, 14, 2, 64), (1, 200, 130, 7, 1, 64), (2, 1, 511, 14, 2, 64)])
+def test_prefill_vs_oracle(pkg, ctx, orc, B, n_tok, start_pos, nh, nkv, hd):
+    rng = np.random.default_rng(n_tok * 7 + start_pos + hd)
     rows = start_pos + n_tok
-    kv, kc, vc = setup(pkg, ctx, orc, rng, B, rows, rows + 5, nkv)
+    kv, kc, vc = setup(pkg, ctx, orc, rng, B, rows, rows + 5, nkv, hd)
     q = bf16(orc, rng.standard_normal((B, n_tok, nh * hd)).astype(np.float32))
     scale = 1.0 / np.sqrt(hd)
     out = kv.attend_prefill(0, q, n_tok, start_pos, nh, scale)
