@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
 }  // namespace
 
-bool prefill_tc_supported(int D) { return D == 64 || D == 128; }
+bool prefill_tc_supported(int D) { return D == 64 || D == 128 || D == 256; }
 
 cudaError_t launch_attend_prefill_tc(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
                                      const CUtensorMap &tv, int B, int n_tok, int start_pos, int Hq, int Hkv,
@@ -385,5 +385,7 @@ cudaError_t launch_attend_prefill_tc(cudaStream_t st, const CUtensorMap &tq, con
     };
     if (D == 64) return run(attn_prefill_tc_kernel<64>, PrefillLayout<64>::SMEM);
     if (D == 128) return run(attn_prefill_tc_kernel<128>, PrefillLayout<128>::SMEM);
+    if (D == 256)
+        return launch_attend_prefill_hd256(st, tq, tk, tv, B, n_tok, start_pos, Hq, Hkv, max_seq, scale, out, dev_err);
     return cudaErrorInvalidValue;
 }

@@ -571,7 +571,7 @@ static eif_status_t prefill_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int la
         return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rows [%d, %d) outside the cache [0, %d)", start_pos,
                     start_pos + n_tok, kv->max_seq);
     if (kv->dtype != EIF_CUDA_BF16 || !prefill_tc_supported(kv->hd))
-        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "prefill attention needs a bf16 cache with head_dim 64 or 128");
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "prefill attention needs a bf16 cache with head_dim 64, 128 or 256");
     if ((size_t)kv->batch * n_tok > 0x7fffffffull) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "too many rows");
     return EIF_STATUS_OK;
 }

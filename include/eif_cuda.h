@@ -152,7 +152,7 @@ eif_status_t eif_cuda_attend_decode_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, 
  * token i attending to cache rows 0 .. start_pos+i.  Replaces the batched prefill attention of
  * tinyllm_forward_batch_embeddings (src/eif_tinyllm.c:1158-1268) and the per-token fullatt_attend of
  * Qwen3.5's prefill_chunk (src/eif_qwen35.c:1122-1133, without gate / SubLN).  The chunk's k / v rows must
- * already be in the cache (kv_upload, kv_append).  Needs a bf16 cache with head_dim 128.
+ * already be in the cache (kv_upload, kv_append).  Needs a bf16 cache with head_dim 64, 128 or 256.
  *   q   [batch][n_tok][n_heads*head_dim], out the same shape
  * _dev: bf16 device arrays (16-byte aligned), asynchronous.  Host variant: fp32 host arrays (rounded to
  * bf16 on the device, the output widened back).

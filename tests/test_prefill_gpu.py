@@ -31,7 +31,9 @@ def setup(pkg, ctx, orc, rng, B, rows, max_seq, nkv, hd=128):
     (2, 300, 0, 12, 2, 128), (1, 128, 0, 4, 4, 128), (3, 130, 200, 8, 2, 128), (2, 1, 77, 12, 2, 128),
     (1, 257, 3, 6, 1, 128),
     # head_dim 64: the Qwen2.5-0.5B attention shape (14 q / 2 kv heads) and a ragged continuation
-    (2, 300, 0, 14, 2, 64), (1, 200, 130, 7, 1, 64), (2, 1, 511, 14, 2, 64)])
+    (2, 300, 0, 14, 2, 64), (1, 200, 130, 7, 1, 64), (2, 1, 511, 14, 2, 64),
+    # head_dim 256: the Qwen3.5 full-attention shape (8 q / 2 kv heads), its own kernel
+    (1, 300, 0, 8, 2, 256), (2, 130, 70, 8, 2, 256), (1, 1, 40, 8, 2, 256), (1, 64, 0, 4, 1, 256)])
 def test_prefill_vs_oracle(pkg, ctx, orc, B, n_tok, start_pos, nh, nkv, hd):
     rng = np.random.default_rng(n_tok * 7 + start_pos + hd)
     rows = start_pos + n_tok
