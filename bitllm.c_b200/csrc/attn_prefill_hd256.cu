@@ -53,7 +53,8 @@ enum {
 struct Params {
     int B, n_tok, start_pos, Hq, G, max_seq, n_tiles;
     float scale_log2;
-    __nv_bfloat16 *out;
+    __nv_bfloat16 *out;  // bf16 output, unless out_f32 is set
+    float *out_f32;
     unsigned *dev_err;
 };
 
@@ -273,23 +274,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok && mbar_wait(bar(BAR_PEMPTY), (nkv - 1) & 1, p.dev_err)) {
             tc_fence_after();
             const float inv = 1.0f / l;
-            __nv_bfloat16 *orow = p.out + (((size_t)b * p.n_tok + q0 + r) * p.Hq + h) * HD;
+            const size_t orow = (((size_t)b * p.n_tok + q0 + r) * p.Hq + h) * HD;
 #pragma unroll 1
             for (int c = 0; c < HD / 32; ++c) {
                 float o[32];
                 tmem_ld32(o_col + c * 32, o);
                 tmem_wait_ld();
-                if (r < rows) {
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        uint4 w;
-                        w.x = pack_bf16x2(o[q4 * 8 + 0] * inv, o[q4 * 8 + 1] * inv);
-                        w.y = pack_bf16x2(o[q4 * 8 + 2] * inv, o[q4 * 8 + 3] * inv);
-                        w.z = pack_bf16x2(o[q4 * 8 + 4] * inv, o[q4 * 8 + 5] * inv);
-                        w.w = pack_bf16x2(o[q4 * 8 + 6] * inv, o[q4 * 8 + 7] * inv);
-                        *reinterpret_cast<uint4 *>(orow + c * 32 + q4 * 8) = w;
-                    }
-                }
+                if (r < rows)
+                    store_scaled32(p.out + orow + c * 32, p.out_f32 ? p.out_f32 + orow + c * 32 : nullptr, o, inv);
             }
         }
     }
@@ -306,7 +298,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 cudaError_t launch_attend_prefill_hd256(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
                                         const CUtensorMap &tv, int B, int n_tok, int start_pos, int Hq, int Hkv,
-                                        int max_seq, float scale, __nv_bfloat16 *out, unsigned *dev_err) {
+                                        int max_seq, float scale, __nv_bfloat16 *out, float *out_f32,
+                                        unsigned *dev_err) {
     Params p;
     p.B = B;
     p.n_tok = n_tok;
@@ -317,6 +310,7 @@ cudaError_t launch_attend_prefill_hd256(cudaStream_t st, const CUtensorMap &tq, 
     p.n_tiles = (n_tok + BM - 1) / BM;
     p.scale_log2 = scale * 1.4426950408889634f;
     p.out = out;
+    p.out_f32 = out_f32;
     p.dev_err = dev_err;
     cudaError_t e = cudaFuncSetAttribute(attn_prefill_hd256_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;

@@ -52,7 +52,8 @@ struct PrefillLayout {
 struct PrefillParams {
     int B, n_tok, start_pos, Hq, Hkv, G, max_seq, n_pairs;
     float scale_log2;
-    __nv_bfloat16 *out;
+    __nv_bfloat16 *out;  // bf16 output, unless out_f32 is set
+    float *out_f32;
     unsigned *dev_err;
 };
 
@@ -328,23 +329,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (ok && nkv[t] > 0 && mbar_wait(bar(BAR_PEMPTY + t), (nkv[t] - 1) & 1, p.dev_err)) {
             tc_fence_after();
             const float inv = 1.0f / l;
-            __nv_bfloat16 *orow = p.out + (((size_t)b * p.n_tok + q0[t] + r) * p.Hq + h) * HD;
+            const size_t orow = (((size_t)b * p.n_tok + q0[t] + r) * p.Hq + h) * HD;
 #pragma unroll
             for (int c = 0; c < HD / 32; ++c) {
                 float o[32];
                 tmem_ld32(o_col + c * 32, o);
                 tmem_wait_ld();
-                if (r < rows[t]) {
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        uint4 w;
-                        w.x = pack_bf16x2(o[q4 * 8 + 0] * inv, o[q4 * 8 + 1] * inv);
-                        w.y = pack_bf16x2(o[q4 * 8 + 2] * inv, o[q4 * 8 + 3] * inv);
-                        w.z = pack_bf16x2(o[q4 * 8 + 4] * inv, o[q4 * 8 + 5] * inv);
-                        w.w = pack_bf16x2(o[q4 * 8 + 6] * inv, o[q4 * 8 + 7] * inv);
-                        *reinterpret_cast<uint4 *>(orow + c * 32 + q4 * 8) = w;
-                    }
-                }
+                if (r < rows[t])
+                    store_scaled32(p.out + orow + c * 32, p.out_f32 ? p.out_f32 + orow + c * 32 : nullptr, o, inv);
             }
         }
     }
@@ -363,7 +355,8 @@ bool prefill_tc_supported(int D) { return D == 64 || D == 128 || D == 256; }
 
 cudaError_t launch_attend_prefill_tc(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
                                      const CUtensorMap &tv, int B, int n_tok, int start_pos, int Hq, int Hkv,
-                                     int max_seq, int D, float scale, __nv_bfloat16 *out, unsigned *dev_err) {
+                                     int max_seq, int D, float scale, __nv_bfloat16 *out, float *out_f32,
+                                     unsigned *dev_err) {
     PrefillParams p;
     p.B = B;
     p.n_tok = n_tok;
@@ -375,6 +368,7 @@ cudaError_t launch_attend_prefill_tc(cudaStream_t st, const CUtensorMap &tq, con
     p.n_pairs = (n_tok + 2 * BM - 1) / (2 * BM);
     p.scale_log2 = scale * 1.4426950408889634f;
     p.out = out;
+    p.out_f32 = out_f32;
     p.dev_err = dev_err;
     const unsigned grid = (unsigned)(p.n_pairs * B * Hq);
     auto run = [&](auto kernel, int smem) {
@@ -386,6 +380,7 @@ cudaError_t launch_attend_prefill_tc(cudaStream_t st, const CUtensorMap &tq, con
     if (D == 64) return run(attn_prefill_tc_kernel<64>, PrefillLayout<64>::SMEM);
     if (D == 128) return run(attn_prefill_tc_kernel<128>, PrefillLayout<128>::SMEM);
     if (D == 256)
-        return launch_attend_prefill_hd256(st, tq, tk, tv, B, n_tok, start_pos, Hq, Hkv, max_seq, scale, out, dev_err);
+        return launch_attend_prefill_hd256(st, tq, tk, tv, B, n_tok, start_pos, Hq, Hkv, max_seq, scale, out, out_f32,
+                                           dev_err);
     return cudaErrorInvalidValue;
 }

@@ -589,9 +589,11 @@ static bool make_q_tensor_map(CUtensorMap *map, const void *q, int rows, int Hq,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// out_f32 set: the attention goes there as fp32 (out_dev unused), else as bf16 to out_dev.
 static eif_status_t prefill_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const void *q_dev, int n_tok,
-                                int start_pos, int n_heads, float scale, void *out_dev) {
-    if ((reinterpret_cast<uintptr_t>(q_dev) | reinterpret_cast<uintptr_t>(out_dev)) & 15)
+                                int start_pos, int n_heads, float scale, void *out_dev, float *out_f32 = nullptr) {
+    if ((reinterpret_cast<uintptr_t>(q_dev) | reinterpret_cast<uintptr_t>(out_dev) |
+         reinterpret_cast<uintptr_t>(out_f32)) & 15)
         return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "prefill: q and out must be 16-byte aligned");
     DecodeArgs probe{};
     decode_prepare(kv, layer, probe);  // makes the layer's K / V tensor maps
@@ -600,7 +602,7 @@ static eif_status_t prefill_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int laye
     if (!make_q_tensor_map(&tq, q_dev, kv->batch * n_tok, n_heads, kv->hd))
         return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "prefill: cannot describe q for TMA");
     CK(launch_attend_prefill_tc(ctx->stream, tq, *probe.tmk, *probe.tmv, kv->batch, n_tok, start_pos, n_heads,
-                                kv->n_kv, kv->max_seq, kv->hd, scale, static_cast<__nv_bfloat16 *>(out_dev),
+                                kv->n_kv, kv->max_seq, kv->hd, scale, static_cast<__nv_bfloat16 *>(out_dev), out_f32,
                                 ctx->dev_err));
     ctx->launches += 1;
     return EIF_STATUS_OK;
@@ -636,6 +638,76 @@ EIF_API eif_status_t eif_cuda_attend_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t 
     CK(launch_bf16_to_f32(ctx->stream, reinterpret_cast<__nv_bfloat16 *>(s + o_o), reinterpret_cast<float *>(s + o_f), n));
     ctx->launches += 1;
     CK(cudaMemcpyAsync(out, s + o_f, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// Gated prefill: the raw attention goes to the context scratch in fp32, then the row epilogue writes
+// SubLN(o * sigmoid(gate)) as fp32.
+static eif_status_t prefill_gated_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const void *q_dev, int n_tok,
+                                      int start_pos, int n_heads, float scale, const float *gate_dev,
+                                      eif_cuda_subln_t subln, const float *sub_norm_dev, float *out_dev) {
+    const int dim = n_heads * kv->hd;
+    const size_t n = (size_t)kv->batch * n_tok * dim;
+    eif_status_t st = ensure_buffer(ctx, &ctx->ws, &ctx->ws_bytes, n * 4);
+    if (st != EIF_STATUS_OK) return st;
+    float *raw = static_cast<float *>(ctx->ws);
+    st = prefill_run(ctx, kv, layer, q_dev, n_tok, start_pos, n_heads, scale, nullptr, raw);
+    if (st != EIF_STATUS_OK) return st;
+    CK(launch_gate_subln(ctx->stream, raw, gate_dev, kv->batch * n_tok, dim, (int)subln, sub_norm_dev, out_dev));
+    ctx->launches += 1;
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t subln_check(eif_cuda_ctx_t *ctx, eif_cuda_subln_t subln, const void *sub_norm) {
+    if (subln != EIF_CUDA_SUBLN_NONE && subln != EIF_CUDA_SUBLN_RMS && subln != EIF_CUDA_SUBLN_WEIGHT)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "unknown SubLN mode %d", (int)subln);
+    if (subln == EIF_CUDA_SUBLN_WEIGHT && !sub_norm)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "SubLN with weights needs sub_norm");
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_attend_prefill_gated_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
+                                                       const void *q_dev, int n_tok, int start_pos, int n_heads,
+                                                       float scale, const float *gate_dev, eif_cuda_subln_t subln,
+                                                       const float *sub_norm_dev, float *out_dev) {
+    eif_status_t st = prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st != EIF_STATUS_OK) return st;
+    st = subln_check(ctx, subln, sub_norm_dev);
+    if (st != EIF_STATUS_OK) return st;
+    if (!q_dev || !out_dev) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "attend_prefill_gated_dev: NULL pointer");
+    DeviceGuard g(ctx);
+    return prefill_gated_run(ctx, kv, layer, q_dev, n_tok, start_pos, n_heads, scale, gate_dev, subln, sub_norm_dev,
+                             out_dev);
+}
+
+EIF_API eif_status_t eif_cuda_attend_prefill_gated(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
+                                                   int n_tok, int start_pos, int n_heads, float scale,
+                                                   const float *gate, eif_cuda_subln_t subln, const float *sub_norm,
+                                                   float *out) {
+    eif_status_t st = prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st != EIF_STATUS_OK) return st;
+    st = subln_check(ctx, subln, sub_norm);
+    if (st != EIF_STATUS_OK) return st;
+    if (!q || !out) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "attend_prefill_gated: NULL pointer");
+    DeviceGuard g(ctx);
+    const size_t row = (size_t)n_heads * kv->hd, n = (size_t)kv->batch * n_tok * row;
+    Carver cv;
+    const size_t o_f = cv.take(n * 4), o_q = cv.take(n * 2), o_g = gate ? cv.take(n * 4) : 0,
+                 o_n = subln == EIF_CUDA_SUBLN_WEIGHT ? cv.take(row * 4) : 0;
+    st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (st != EIF_STATUS_OK) return st;
+    char *s = static_cast<char *>(ctx->stage);
+    float *f = reinterpret_cast<float *>(s + o_f);
+    CK(cudaMemcpyAsync(f, q, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(launch_f32_to_bf16(ctx->stream, f, reinterpret_cast<__nv_bfloat16 *>(s + o_q), n));
+    ctx->launches += 1;
+    if (gate) CK(cudaMemcpyAsync(s + o_g, gate, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (subln == EIF_CUDA_SUBLN_WEIGHT) CK(cudaMemcpyAsync(s + o_n, sub_norm, row * 4, cudaMemcpyHostToDevice, ctx->stream));
+    st = prefill_gated_run(ctx, kv, layer, s + o_q, n_tok, start_pos, n_heads, scale,
+                           gate ? reinterpret_cast<float *>(s + o_g) : nullptr, subln,
+                           subln == EIF_CUDA_SUBLN_WEIGHT ? reinterpret_cast<float *>(s + o_n) : nullptr, f);
+    if (st != EIF_STATUS_OK) return st;
+    CK(cudaMemcpyAsync(out, f, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return wait_stream(ctx);
 }
 

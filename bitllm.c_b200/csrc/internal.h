@@ -126,11 +126,16 @@ cudaError_t launch_deltanet_chunked(cudaStream_t st, const CUtensorMap &tq, cons
 bool prefill_tc_supported(int D);
 cudaError_t launch_attend_prefill_tc(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
                                      const CUtensorMap &tv, int B, int n_tok, int start_pos, int Hq, int Hkv,
-                                     int max_seq, int D, float scale, __nv_bfloat16 *out, unsigned *dev_err);
+                                     int max_seq, int D, float scale, __nv_bfloat16 *out, float *out_f32,
+                                     unsigned *dev_err);  // out_f32 set: fp32 output there instead of bf16
+// Row epilogue after prefill (gate_subln.cu): out = SubLN(o * sigmoid(gate)) per row of `dim` values.
+cudaError_t launch_gate_subln(cudaStream_t st, const float *o, const float *gate, int rows, int dim, int subln,
+                              const float *sub_norm, float *out);
 // head_dim 256 (attn_prefill_hd256.cu): one query tile per CTA, double-buffered S.
 cudaError_t launch_attend_prefill_hd256(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
                                         const CUtensorMap &tv, int B, int n_tok, int start_pos, int Hq, int Hkv,
-                                        int max_seq, float scale, __nv_bfloat16 *out, unsigned *dev_err);
+                                        int max_seq, float scale, __nv_bfloat16 *out, float *out_f32,
+                                        unsigned *dev_err);
 
 // Fills the TMA descriptors (made on first use per layer) and the kernel choice of `a` (eif_cuda.cu).
 void decode_prepare(eif_cuda_kv_t *kv, int layer, DecodeArgs &a);

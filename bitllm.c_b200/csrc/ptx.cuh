@@ -154,6 +154,24 @@ EIF_DEV uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t *>(&v);
 }
 
+// 32 consecutive values of an output row times `inv`: fp32 to `of` when it is not null, else bf16 to `ob`
+// (both 16-byte aligned).
+EIF_DEV void store_scaled32(__nv_bfloat16 *ob, float *of, const float (&o)[32], float inv) {
+    if (of) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4 *>(of + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+    } else {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+            *reinterpret_cast<uint4 *>(ob + q4 * 8) =
+                make_uint4(pack_bf16x2(o[q4 * 8 + 0] * inv, o[q4 * 8 + 1] * inv),
+                           pack_bf16x2(o[q4 * 8 + 2] * inv, o[q4 * 8 + 3] * inv),
+                           pack_bf16x2(o[q4 * 8 + 4] * inv, o[q4 * 8 + 5] * inv),
+                           pack_bf16x2(o[q4 * 8 + 6] * inv, o[q4 * 8 + 7] * inv));
+    }
+}
+
 // x = hi + lo with hi = bf16(x), lo = bf16(x - hi): the pair carries ~16 significant bits of x.
 EIF_DEV void split_bf16(float x, float &hi, float &lo) {
     hi = __bfloat162float(__float2bfloat16_rn(x));

@@ -77,6 +77,8 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_attend_decode_noalloc_dev": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _P, _I, _P, _P]),
         "eif_cuda_attend_prefill": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P]),
         "eif_cuda_attend_prefill_dev": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P]),
+        "eif_cuda_attend_prefill_gated": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P, _I, _P, _P]),
+        "eif_cuda_attend_prefill_gated_dev": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P, _I, _P, _P]),
         "eif_cuda_delta_alloc": (_I, [_P, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
         "eif_cuda_delta_free": (None, [_P]),
         "eif_cuda_delta_reset": (_I, [_P, _P]),
@@ -285,6 +287,26 @@ class KVCache:
         """bf16 device arrays [batch][n_tok][n_heads*head_dim]; asynchronous on the context's stream."""
         self.ctx.check(lib().eif_cuda_attend_prefill_dev(self.ctx.handle, self._h, layer, q_dev, n_tok, start_pos,
                                                          n_heads, float(scale), out_dev), "attend_prefill_dev")
+
+    def attend_prefill_gated(self, layer: int, q, n_tok: int, start_pos: int, n_heads: int, scale: float,
+                             gate=None, subln: int = SUBLN_NONE, sub_norm=None):
+        """Qwen3.5 prefill attention with the output gate and SubLN: fp32 host arrays in and out."""
+        qq = _f32(q)
+        gg = _f32(gate) if gate is not None else None
+        nn = _f32(sub_norm) if sub_norm is not None else None
+        out = np.zeros((self.batch, n_tok, n_heads * self.head_dim), np.float32)
+        self.ctx.check(lib().eif_cuda_attend_prefill_gated(self.ctx.handle, self._h, layer, _ptr(qq), n_tok, start_pos,
+                                                           n_heads, float(scale), _ptr(gg), int(subln), _ptr(nn),
+                                                           _ptr(out)), "attend_prefill_gated")
+        return out
+
+    def attend_prefill_gated_dev(self, layer: int, q_dev: int, n_tok: int, start_pos: int, n_heads: int,
+                                 scale: float, out_dev: int, gate_dev: int | None = None, subln: int = SUBLN_NONE,
+                                 sub_norm_dev: int | None = None):
+        """q bf16, gate / sub_norm / out fp32 device arrays; asynchronous on the context's stream."""
+        self.ctx.check(lib().eif_cuda_attend_prefill_gated_dev(self.ctx.handle, self._h, layer, q_dev, n_tok, start_pos,
+                                                               n_heads, float(scale), gate_dev, int(subln),
+                                                               sub_norm_dev, out_dev), "attend_prefill_gated_dev")
 
     def attend_decode_dev(self, layer: int, q_dev: int, pos_dev: int, max_pos: int, n_heads: int, scale: float,
                           out_dev: int, gate_dev: int | None = None, subln: int = SUBLN_NONE,

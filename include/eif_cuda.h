@@ -162,6 +162,21 @@ eif_status_t eif_cuda_attend_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int
 eif_status_t eif_cuda_attend_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const void *q_dev,
                                          int n_tok, int start_pos, int n_heads, float scale, void *out_dev);
 
+/* Qwen3.5 gated prefill attention: what prefill_chunk gets from fullatt_attend per token
+ * (src/eif_qwen35.c:1122-1133 -> :741-789), i.e. the causal prefill above followed, row by row, by the
+ * output gate and SubLN of eif_cuda_attend_decode (out = SubLN(o * sigmoid(gate))).
+ *   gate  NULL, or [batch][n_tok][n_heads*head_dim] fp32; sub_norm [n_heads*head_dim] for EIF_CUDA_SUBLN_WEIGHT
+ *   out   [batch][n_tok][n_heads*head_dim] fp32
+ * _dev: q bf16 (16-byte aligned), gate / sub_norm / out fp32 device arrays, asynchronous.  Host variant: fp32
+ * host arrays. */
+eif_status_t eif_cuda_attend_prefill_gated(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
+                                           int n_tok, int start_pos, int n_heads, float scale, const float *gate,
+                                           eif_cuda_subln_t subln, const float *sub_norm, float *out);
+eif_status_t eif_cuda_attend_prefill_gated_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
+                                               const void *q_dev, int n_tok, int start_pos, int n_heads, float scale,
+                                               const float *gate_dev, eif_cuda_subln_t subln,
+                                               const float *sub_norm_dev, float *out_dev);
+
 /* Same computation and arguments as eif_cuda_attend_decode_dev, for callers that may not allocate device
  * memory after start-up (an engine whose device memory is all reserved up front, or one running under a
  * fixed memory budget).  No counterpart in the reference.  It calls no cudaMalloc / cudaFree: the split-K

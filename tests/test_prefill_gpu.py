@@ -84,6 +84,26 @@ def test_prefill_is_causal(pkg, ctx, orc):
     assert np.all(np.isfinite(b2))
 
 
+@pytest.mark.parametrize("subln,hd,nh,nkv", [(2, 256, 8, 2), (1, 256, 8, 2), (0, 256, 8, 2), (2, 128, 12, 2)])
+def test_prefill_gated_vs_oracle(pkg, ctx, orc, subln, hd, nh, nkv):
+    """Qwen3.5 prefill attention as prefill_chunk gets it (fullatt_attend per token with the output gate and
+    SubLN, src/eif_qwen35.c:1122-1133, :773-789), against the oracle's gated attention + SubLN per token."""
+    rng = np.random.default_rng(100 + subln + hd)
+    B, n_tok, start_pos = 2, 150, 40
+    rows = start_pos + n_tok
+    kv, kc, vc = setup(pkg, ctx, orc, rng, B, rows, rows + 3, nkv, hd)
+    q = bf16(orc, rng.standard_normal((B, n_tok, nh * hd)).astype(np.float32))
+    gate = rng.standard_normal((B, n_tok, nh * hd)).astype(np.float32)
+    sub_norm = (1.0 + 0.1 * rng.standard_normal(nh * hd)).astype(np.float32)
+    scale = 1.0 / np.sqrt(hd)
+    out = kv.attend_prefill_gated(0, q, n_tok, start_pos, nh, scale, gate, subln, sub_norm if subln == 2 else None)
+    for b in range(B):
+        ref = np.stack([orc.subln(orc.attend_decode(q[b, i], kc[b], vc[b], start_pos + i, nh, nkv, hd, scale, gate[b, i]),
+                                  sub_norm if subln == 2 else None, subln) for i in range(n_tok)])
+        assert rel_l2(out[b], ref) <= REL
+        assert np.max(np.abs(out[b] - ref)) <= ABS
+
+
 def test_prefill_bad_arguments(pkg, ctx):
     kv32 = pkg.KVCache(ctx, 1, 1, 64, 2, 128, pkg.F32)
     with pytest.raises(pkg.EifCudaError) as e:
