@@ -253,7 +253,8 @@ enum {
 
 struct ChunkArgs {
     const float *G;         // [B][H][n_chunks][64] cumulative log decays (chunk_solve_kernel)
-    __nv_bfloat16 *o;       // [B][T][H][dv]
+    __nv_bfloat16 *o;       // [B][T][H][dv] bf16, unless o_f32 is set
+    float *o_f32;           // [B][T][H][dv] fp32 output, or null
     float *S;               // layer state [B][H][DK][dv]
     int B, T, H, dv, n_chunks;
     float q_scale;
@@ -383,12 +384,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(bar(B_DPFREE + slot));
                 const int t = c * C + r - 64;
                 if (t < p.T) {
-                    uint4 *dst = reinterpret_cast<uint4 *>(p.o + (((size_t)b * p.T + t) * p.H + h) * p.dv + slice * DS);
-#pragma unroll
-                    for (int u = 0; u < 8; ++u)
-                        dst[u] = make_uint4(pack_bf16x2(o[8 * u], o[8 * u + 1]), pack_bf16x2(o[8 * u + 2], o[8 * u + 3]),
-                                            pack_bf16x2(o[8 * u + 4], o[8 * u + 5]),
-                                            pack_bf16x2(o[8 * u + 6], o[8 * u + 7]));
+                    const size_t orow = (((size_t)b * p.T + t) * p.H + h) * p.dv + slice * DS;
+                    store_scaled32(p.o + orow, p.o_f32 ? p.o_f32 + orow : nullptr, *reinterpret_cast<float(*)[32]>(o),
+                                   1.f);
+                    store_scaled32(p.o + orow + 32, p.o_f32 ? p.o_f32 + orow + 32 : nullptr,
+                                   *reinterpret_cast<float(*)[32]>(o + 32), 1.f);
                 }
             } else {
                 tc_fence_before();
@@ -643,8 +643,8 @@ size_t deltanet_chunked_workspace(int B, int T, int H) {
 
 cudaError_t launch_deltanet_chunked(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
                                     const CUtensorMap &tv, const CUtensorMap &tt, void *t_ws, const float *beta,
-                                    const float *g, __nv_bfloat16 *o, float *S, int B, int T, int H, int dv,
-                                    float q_scale, unsigned *dev_err, int *n_launches) {
+                                    const float *g, __nv_bfloat16 *o, float *o_f32, float *S, int B, int T, int H,
+                                    int dv, float q_scale, unsigned *dev_err, int *n_launches) {
     *n_launches = 0;
     const int n_chunks = (T + C - 1) / C;
     cudaError_t e = cudaFuncSetAttribute(chunk_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSolveSmem);
@@ -655,7 +655,7 @@ cudaError_t launch_deltanet_chunked(cudaStream_t st, const CUtensorMap &tq, cons
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     ++*n_launches;
-    ChunkArgs p{Gws, o, S, B, T, H, dv, n_chunks, q_scale, dev_err};
+    ChunkArgs p{Gws, o, o_f32, S, B, T, H, dv, n_chunks, q_scale, dev_err};
     e = cudaFuncSetAttribute(deltanet_chunked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     deltanet_chunked_kernel<<<dim3(dv / DS, H, B), kThreads, kSmem, st>>>(tq, tk, tv, tt, p);

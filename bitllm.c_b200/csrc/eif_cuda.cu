@@ -986,29 +986,112 @@ static eif_status_t chunked_check(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int
     return EIF_STATUS_OK;
 }
 
-static eif_status_t chunked_run(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const void *q, const void *k,
-                                const void *v, const float *beta, const float *g, int n_tok, float q_scale, void *o) {
+// The chunked rule with its per-chunk scratch at t_ws (deltanet_chunked_workspace bytes): o as bf16, or as
+// fp32 to o_f32 when that is set.
+static eif_status_t chunked_launch(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const void *q, const void *k,
+                                   const void *v, const float *beta, const float *g, int n_tok, float q_scale, void *o,
+                                   float *o_f32, void *t_ws) {
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
-         reinterpret_cast<uintptr_t>(o)) & 15)
+         reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(o_f32)) & 15)
         return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "chunked prefill: q, k, v, o must be 16-byte aligned");
-    // scratch: per chunk T diag(-b e^G) and T diag(b) with T = (I + A)^-1 (bf16 [batch][H][chunk][128][64]),
-    // then the cumulative log decays (fp32 [batch][H][chunk][64])
-    const size_t ws = deltanet_chunked_workspace(st->batch, n_tok, st->H);
-    eif_status_t rs = ensure_buffer(ctx, &ctx->ws, &ctx->ws_bytes, ws);
-    if (rs != EIF_STATUS_OK) return rs;
     alignas(64) CUtensorMap tq, tk, tv, tt;
     const int rows = st->batch * n_tok;
     const int t_rows = (int)(deltanet_chunked_tmat_bytes(st->batch, n_tok, st->H) / 128);  // 64 bf16 per row
     if (!make_tok_tensor_map(&tq, q, rows, st->H, st->dk) || !make_tok_tensor_map(&tk, k, rows, st->H, st->dk) ||
-        !make_tok_tensor_map(&tv, v, rows, st->H, st->dv) || !make_tok_tensor_map(&tt, ctx->ws, t_rows, 1, 64))
+        !make_tok_tensor_map(&tv, v, rows, st->H, st->dv) || !make_tok_tensor_map(&tt, t_ws, t_rows, 1, 64))
         return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "chunked prefill: cannot describe q / k / v for TMA");
     int nl = 0;
-    const cudaError_t e = launch_deltanet_chunked(ctx->stream, tq, tk, tv, tt, ctx->ws, beta, g,
-                                                  static_cast<__nv_bfloat16 *>(o), st->S[layer], st->batch, n_tok,
-                                                  st->H, st->dv, q_scale, ctx->dev_err, &nl);
+    const cudaError_t e = launch_deltanet_chunked(ctx->stream, tq, tk, tv, tt, t_ws, beta, g,
+                                                  static_cast<__nv_bfloat16 *>(o), o_f32, st->S[layer], st->batch,
+                                                  n_tok, st->H, st->dv, q_scale, ctx->dev_err, &nl);
     ctx->launches += nl;
     if (e != cudaSuccess) return cuda_fail(ctx, e, "deltanet_chunked launch");
     return EIF_STATUS_OK;
+}
+
+static eif_status_t chunked_run(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const void *q, const void *k,
+                                const void *v, const float *beta, const float *g, int n_tok, float q_scale, void *o) {
+    // scratch: per chunk T diag(-b e^G) and T diag(b) with T = (I + A)^-1 (bf16 [batch][H][chunk][128][64]),
+    // then the cumulative log decays (fp32 [batch][H][chunk][64])
+    eif_status_t rs = ensure_buffer(ctx, &ctx->ws, &ctx->ws_bytes, deltanet_chunked_workspace(st->batch, n_tok, st->H));
+    if (rs != EIF_STATUS_OK) return rs;
+    return chunked_launch(ctx, st, layer, q, k, v, beta, g, n_tok, q_scale, o, nullptr, ctx->ws);
+}
+
+// The whole deltanet_core over a prefill chunk: pre ops -> chunked rule (fp32 output) -> gated RMSNorm.
+static eif_status_t prefill_core_run(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *qkv,
+                                     const float *z, const float *b_raw, const float *a_raw, int n_tok, float *out) {
+    const size_t tok = (size_t)st->batch * n_tok * st->H;
+    Carver cv;
+    const size_t o_q = cv.take(tok * st->dk * 2), o_k = cv.take(tok * st->dk * 2), o_v = cv.take(tok * st->dv * 2),
+                 o_b = cv.take(tok * 4), o_g = cv.take(tok * 4), o_o = cv.take(tok * st->dv * 4),
+                 o_t = cv.take(deltanet_chunked_workspace(st->batch, n_tok, st->H));
+    eif_status_t rs = ensure_buffer(ctx, &ctx->ws, &ctx->ws_bytes, cv.off);
+    if (rs != EIF_STATUS_OK) return rs;
+    char *s = static_cast<char *>(ctx->ws);
+    const size_t ncw = (size_t)st->conv_dim * st->conv_k;
+    const float *w = st->weights[layer];
+    DeltaPrefillArgs a{qkv, z, b_raw, a_raw, st->conv[layer], w, w + ncw, w + ncw + st->H, w + ncw + 2 * st->H,
+                       reinterpret_cast<__nv_bfloat16 *>(s + o_q), reinterpret_cast<__nv_bfloat16 *>(s + o_k),
+                       reinterpret_cast<__nv_bfloat16 *>(s + o_v), reinterpret_cast<float *>(s + o_b),
+                       reinterpret_cast<float *>(s + o_g), reinterpret_cast<float *>(s + o_o), out, st->batch, n_tok,
+                       st->H, st->dk, st->dv, st->conv_k};
+    CK(launch_deltanet_prefill_pre(ctx->stream, a));
+    ctx->launches += 2;
+    rs = chunked_launch(ctx, st, layer, a.q, a.k, a.v, a.beta, a.g, n_tok, 1.0f, nullptr,
+                        reinterpret_cast<float *>(s + o_o), s + o_t);
+    if (rs != EIF_STATUS_OK) return rs;
+    CK(launch_deltanet_prefill_post(ctx->stream, a));
+    ctx->launches += 1;
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t prefill_core_check(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, int n_tok) {
+    eif_status_t rs = core_check(ctx, st, layer);
+    if (rs != EIF_STATUS_OK) return rs;
+    rs = chunked_check(ctx, st, layer, n_tok);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (st->conv_k < 1) return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "deltanet prefill core: the state has no conv window");
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_deltanet_prefill_core_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer,
+                                                        const float *qkv_dev, const float *z_dev, const float *b_dev,
+                                                        const float *a_dev, int n_tok, float *out_dev) {
+    eif_status_t rs = prefill_core_check(ctx, st, layer, n_tok);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!qkv_dev || !z_dev || !b_dev || !a_dev || !out_dev)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "deltanet_prefill_core_dev: NULL pointer");
+    DeviceGuard gd(ctx);
+    return prefill_core_run(ctx, st, layer, qkv_dev, z_dev, b_dev, a_dev, n_tok, out_dev);
+}
+
+EIF_API eif_status_t eif_cuda_deltanet_prefill_core(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer,
+                                                    const float *qkv, const float *z, const float *b_raw,
+                                                    const float *a_raw, int n_tok, float *out) {
+    eif_status_t rs = prefill_core_check(ctx, st, layer, n_tok);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!qkv || !z || !b_raw || !a_raw || !out)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "deltanet_prefill_core: NULL pointer");
+    DeviceGuard gd(ctx);
+    const size_t tok = (size_t)st->batch * n_tok, nq = tok * st->conv_dim, nz = tok * st->H * st->dv,
+                 nh = tok * st->H;
+    Carver cv;
+    const size_t o_q = cv.take(nq * 4), o_z = cv.take(nz * 4), o_b = cv.take(nh * 4), o_a = cv.take(nh * 4),
+                 o_o = cv.take(nz * 4);
+    rs = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (rs != EIF_STATUS_OK) return rs;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_q, qkv, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_z, z, nz * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_b, b_raw, nh * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_a, a_raw, nh * 4, cudaMemcpyHostToDevice, ctx->stream));
+    rs = prefill_core_run(ctx, st, layer, reinterpret_cast<float *>(s + o_q), reinterpret_cast<float *>(s + o_z),
+                          reinterpret_cast<float *>(s + o_b), reinterpret_cast<float *>(s + o_a), n_tok,
+                          reinterpret_cast<float *>(s + o_o));
+    if (rs != EIF_STATUS_OK) return rs;
+    CK(cudaMemcpyAsync(out, s + o_o, nz * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
 }
 
 EIF_API eif_status_t eif_cuda_deltanet_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer,

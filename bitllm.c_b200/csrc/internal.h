@@ -119,8 +119,22 @@ size_t deltanet_chunked_tmat_bytes(int B, int T, int H);
 size_t deltanet_chunked_workspace(int B, int T, int H);
 cudaError_t launch_deltanet_chunked(cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk,
                                     const CUtensorMap &tv, const CUtensorMap &tt, void *t_ws, const float *beta,
-                                    const float *g, __nv_bfloat16 *o, float *S, int B, int T, int H, int dv,
-                                    float q_scale, unsigned *dev_err, int *n_launches);
+                                    const float *g, __nv_bfloat16 *o, float *o_f32, float *S, int B, int T, int H,
+                                    int dv, float q_scale, unsigned *dev_err, int *n_launches);  // o_f32: fp32 out
+
+// Chunk-level DeltaNet pre / post ops of the prefill core (deltanet_prefill_ops.cu).
+struct DeltaPrefillArgs {
+    const float *qkv, *z, *b_raw, *a_raw;  // [B][n_tok][conv_dim], [B][n_tok][H*dv], [B][n_tok][H] x 2
+    float *conv;                           // [B][conv_dim][conv_k] window, updated to the chunk's last inputs
+    const float *conv_w, *dt_bias, *a_exp, *norm_w;
+    __nv_bfloat16 *q, *k, *v;              // [B][n_tok][H][dk | dk | dv] (q L2-normalised and scaled)
+    float *beta, *g;                       // [B][n_tok][H]
+    const float *o;                        // [B][n_tok][H][dv] fp32, the rule's output
+    float *out;                            // [B][n_tok][H*dv]
+    int B, n_tok, H, dk, dv, conv_k;
+};
+cudaError_t launch_deltanet_prefill_pre(cudaStream_t st, const DeltaPrefillArgs &a);
+cudaError_t launch_deltanet_prefill_post(cudaStream_t st, const DeltaPrefillArgs &a);
 
 // Causal prefill attention on tcgen05 (attn_prefill_tc.cu), head_dim D.
 bool prefill_tc_supported(int D);

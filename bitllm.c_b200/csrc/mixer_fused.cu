@@ -209,6 +209,8 @@ cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *
     const dim3 grid(a.H, a.B);
     if (a.dk == 128 && a.dv == 128)
         deltanet_core_kernel<128, 128, 256><<<grid, 256, 0, st>>>(a);
+    else if (a.dk == 128 && a.dv == 64)
+        deltanet_core_kernel<128, 64, 256><<<grid, 256, 0, st>>>(a);
     else if (a.dk == 64 && a.dv == 64)
         deltanet_core_kernel<64, 64, 128><<<grid, 128, 0, st>>>(a);
     else {

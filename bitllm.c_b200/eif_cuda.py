@@ -90,6 +90,8 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_delta_set_weights": (_I, [_P, _P, _I, _P, _P, _P, _P]),
         "eif_cuda_deltanet_core": (_I, [_P, _P, _I, _P, _P, _P, _P, _P]),
         "eif_cuda_deltanet_core_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _P]),
+        "eif_cuda_deltanet_prefill_core": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P]),
+        "eif_cuda_deltanet_prefill_core_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P]),
         "eif_cuda_deltanet_prefill": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _I, _F, _P]),
         "eif_cuda_deltanet_prefill_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _I, _F, _P]),
         "eif_cuda_kv_set_norms": (_I, [_P, _P, _I, _P, _P]),
@@ -386,6 +388,20 @@ class DeltaState:
     def core_dev(self, layer: int, qkv_dev, z_dev, b_dev, a_dev, out_dev):
         self.ctx.check(lib().eif_cuda_deltanet_core_dev(self.ctx.handle, self._h, layer, qkv_dev, z_dev, b_dev, a_dev,
                                                         out_dev), "deltanet_core_dev")
+
+    def prefill_core(self, layer: int, qkv, z, b_raw, a_raw):
+        """deltanet_core over a chunk of n_tok tokens per sequence (qkv [batch][n_tok][conv_dim], z
+        [batch][n_tok][H*d_v], b, a [batch][n_tok][H]); returns out [batch][n_tok][H*d_v]."""
+        a = [_f32(x) for x in (qkv, z, b_raw, a_raw)]
+        n_tok = a[0].shape[1]
+        out = np.zeros((self.batch, n_tok, self.H * self.dv), np.float32)
+        self.ctx.check(lib().eif_cuda_deltanet_prefill_core(self.ctx.handle, self._h, layer, *[_ptr(x) for x in a],
+                                                            n_tok, _ptr(out)), "deltanet_prefill_core")
+        return out
+
+    def prefill_core_dev(self, layer: int, qkv_dev, z_dev, b_dev, a_dev, n_tok: int, out_dev):
+        self.ctx.check(lib().eif_cuda_deltanet_prefill_core_dev(self.ctx.handle, self._h, layer, qkv_dev, z_dev, b_dev,
+                                                                a_dev, n_tok, out_dev), "deltanet_prefill_core_dev")
 
     def prefill(self, layer: int, q, k, v, beta, g, q_scale: float):
         """Chunked prefill of n_tok tokens per sequence (fp32 host arrays; q, k [batch][n_tok][H][d_k],

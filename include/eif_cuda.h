@@ -238,6 +238,20 @@ eif_status_t eif_cuda_deltanet_core(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, i
 eif_status_t eif_cuda_deltanet_core_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *qkv_dev,
                                         const float *z_dev, const float *b_dev, const float *a_dev, float *out_dev);
 
+/* The whole DeltaNet mixer over a prefill chunk of n_tok tokens per sequence: what prefill_chunk gets from
+ * calling deltanet_core once per token (src/eif_qwen35.c:1104-1106 -> :546-656), with the delta rule in
+ * the chunked WY / UT form.  Conv window, S and the output are those of n_tok consecutive
+ * eif_cuda_deltanet_core calls; q / k / v reach the rule as bf16 (the prefill tolerance, not the fp32 one).
+ *   qkv [batch][n_tok][conv_dim], z / out [batch][n_tok][n_heads*d_v], b, a [batch][n_tok][n_heads]
+ * Needs the layer's weights (eif_cuda_delta_set_weights), d_k = 128, d_v a multiple of 64 up to 256.
+ * _dev: fp32 device arrays, asynchronous.  Host variant: fp32 host arrays. */
+eif_status_t eif_cuda_deltanet_prefill_core(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer, const float *qkv,
+                                            const float *z, const float *b_raw, const float *a_raw, int n_tok,
+                                            float *out);
+eif_status_t eif_cuda_deltanet_prefill_core_dev(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int layer,
+                                                const float *qkv_dev, const float *z_dev, const float *b_dev,
+                                                const float *a_dev, int n_tok, float *out_dev);
+
 /*
  * DeltaNet prefill of n_tok tokens per sequence in the chunked WY / UT form (64-token chunks, the chunk
  * products on tensor cores, fp32 state carried across chunks), starting from and updating the layer's S.

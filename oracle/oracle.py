@@ -183,3 +183,37 @@ def round_bf16(x):
     y = c32(x).copy()
     port().orc_round_bf16(_fp(y), y.size)
     return y
+
+
+def deltanet_core_bf16_rule(qkv_raw, z, b_raw, a_raw, conv_state, S, conv_w, dt_bias, A_log, norm_w):
+    """deltanet_core over consecutive tokens with the rule's q / k / v rounded to bf16: the recurrent
+    reference "on the same bf16-rounded inputs" for a path whose rule runs on bf16 operands.
+
+    The steps around the rule follow src/eif_qwen35.c in float64: causal conv1d over the conv_k window +
+    SiLU (:560-572), L2 norms with eps 1e-12 and q scaled by 1/sqrt(d_k) (:579-585), beta = sigmoid(b),
+    g = -exp(A_log) softplus(a + dt_bias) (:587-592); q / k / v are then rounded to bf16 and the port's rule
+    (:594-639) runs token by token in fp32; the gated RMSNorm (:642-653) closes in float64.
+    qkv_raw [T][conv_dim], z [T][H*dv], b_raw / a_raw [T][H]; conv_state [conv_dim][conv_k] and S [H][dk][dv]
+    are updated IN PLACE; returns out [T][H*dv]."""
+    H, dk, dv = S.shape
+    T, conv_dim = qkv_raw.shape
+    ck = conv_state.shape[-1]
+    silu = lambda x: x / (1.0 + np.exp(-x))  # noqa: E731
+    win = np.concatenate([conv_state.T.astype(np.float64), np.asarray(qkv_raw, np.float64)], 0)
+    y = np.stack([silu((win[t + 1:t + 1 + ck] * np.asarray(conv_w, np.float64).T).sum(0)) for t in range(T)])
+    conv_state[:] = win[T:T + ck].T if T >= ck else win[T:].T
+    q = y[:, :H * dk].reshape(T, H, dk)
+    k = y[:, H * dk:2 * H * dk].reshape(T, H, dk)
+    v = y[:, 2 * H * dk:].reshape(T, H, dv)
+    q = q / np.sqrt((q * q).sum(-1, keepdims=True) + 1e-12) / np.sqrt(dk)
+    k = k / np.sqrt((k * k).sum(-1, keepdims=True) + 1e-12)
+    beta = 1.0 / (1.0 + np.exp(-np.asarray(b_raw, np.float64)))
+    g = -np.exp(np.asarray(A_log, np.float64)) * np.log1p(np.exp(np.asarray(a_raw, np.float64) + dt_bias))
+    out = np.zeros((T, H * dv), np.float32)
+    zz = np.asarray(z, np.float64).reshape(T, H, dv)
+    for t in range(T):
+        o = deltanet_rule(S, round_bf16(q[t]).ravel(), round_bf16(k[t]).ravel(), round_bf16(v[t]).ravel(),
+                          beta[t].astype(np.float32), g[t].astype(np.float32), 1.0).reshape(H, dv).astype(np.float64)
+        o = o / np.sqrt((o * o).mean(-1, keepdims=True) + 1e-6) * np.asarray(norm_w, np.float64) * silu(zz[t])
+        out[t] = o.ravel()
+    return out

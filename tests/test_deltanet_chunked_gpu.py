@@ -68,6 +68,51 @@ def test_config4_full_size(pkg, ctx, orc):
     assert rel_l2(Sg, S) <= REL and np.max(np.abs(Sg - S)) <= ABS
 
 
+@pytest.mark.parametrize("B,n_tok,H,dv", [(2, 150, 4, 128), (1, 3, 2, 128), (1, 70, 2, 64), (3, 64, 16, 128)])
+def test_prefill_core_vs_per_token(pkg, ctx, orc, B, n_tok, H, dv):
+    """eif_cuda_deltanet_prefill_core over a chunk against the C restatement of deltanet_core run token by
+    token, as prefill_chunk does (src/eif_qwen35.c:1104-1106): outputs, final S, final conv window; then
+    the per-token fused mixer continues on the same state.
+
+    Tolerances: against the fp32 per-token restatement, rel-L2 <= 1e-2 on outputs and state (the conv window
+    exactly); element by element, against the recurrent reference on the same bf16-rounded rule inputs
+    (oracle.deltanet_core_bf16_rule), |err| <= 2e-2 + 1e-2 |ref|.  The outputs leave through the gated
+    RMSNorm (unit RMS per head, times silu(z)), so they reach |out| ~ 13 here and a head whose raw output
+    nearly cancels is magnified: the fp32 recurrence on bf16-rounded inputs is itself up to 0.07 away from
+    the fp32 one at such elements, so the per-element bound is taken against it, with a relative term."""
+    rng = np.random.default_rng(n_tok + 10 * H + dv)
+    dk, ck = 128, 4
+    conv_dim = 2 * H * dk + H * dv
+    w = dict(conv_w=(rng.standard_normal((conv_dim, ck)) * 0.5).astype(np.float32),
+             dt_bias=rng.standard_normal(H).astype(np.float32), A_log=(0.5 * rng.standard_normal(H)).astype(np.float32),
+             norm_w=(1 + 0.1 * rng.standard_normal(dv)).astype(np.float32))
+    st = pkg.DeltaState(ctx, 1, B, H, dk, dv, ck)
+    st.set_weights(0, **w)
+    S0 = (0.02 * rng.standard_normal((B, H, dk, dv))).astype(np.float32)
+    conv0 = rng.standard_normal((B, conv_dim, ck)).astype(np.float32)
+    for b in range(B):
+        st.upload(0, b, S=S0[b], conv_state=conv0[b])
+    T = n_tok + 2
+    qkv = rng.standard_normal((B, T, conv_dim)).astype(np.float32)
+    z = rng.standard_normal((B, T, H * dv)).astype(np.float32)
+    bb = rng.standard_normal((B, T, H)).astype(np.float32)
+    aa = rng.standard_normal((B, T, H)).astype(np.float32)
+    out = st.prefill_core(0, qkv[:, :n_tok], z[:, :n_tok], bb[:, :n_tok], aa[:, :n_tok])
+    nxt = [st.core(0, qkv[:, t], z[:, t], bb[:, t], aa[:, t]) for t in range(n_tok, T)]
+    for b in range(B):
+        S, conv = S0[b].copy(), conv0[b].copy()
+        ref = np.stack([orc.deltanet_core(qkv[b, t], z[b, t], bb[b, t], aa[b, t], conv, S, **w) for t in range(T)])
+        assert rel_l2(out[b], ref[:n_tok]) <= REL, b
+        ref16 = orc.deltanet_core_bf16_rule(qkv[b, :n_tok], z[b, :n_tok], bb[b, :n_tok], aa[b, :n_tok],
+                                            conv0[b].copy(), S0[b].copy(), **w)
+        assert np.all(np.abs(out[b] - ref16) <= ABS + 1e-2 * np.abs(ref16)), b
+        got = np.stack([o[b] for o in nxt])
+        assert rel_l2(got, ref[n_tok:]) <= REL, b
+        Sg, cg = st.download(0, b)
+        assert rel_l2(Sg, S) <= REL and np.max(np.abs(Sg - S)) <= ABS, b
+        assert np.array_equal(cg, conv), b  # the window holds the raw inputs: exact
+
+
 def test_chunked_then_recurrent_steps_continue(pkg, ctx, orc):
     """Prefill by chunks, then decode token by token with the recurrent step kernel on the same state:
     the state handed over is the recurrent one."""
