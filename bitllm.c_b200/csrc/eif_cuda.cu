@@ -1198,16 +1198,68 @@ static eif_status_t prep_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer
     return EIF_STATUS_OK;
 }
 
+// pos set: one token per sequence at pos[b]; else n_tok tokens per sequence at start_pos + i.
 static eif_status_t prep_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg, const float *k,
-                             const float *v, const int *pos, int n_heads, float *q_out, float *gate_out) {
+                             const float *v, const int *pos, int n_heads, float *q_out, float *gate_out,
+                             int n_tok = 1, int start_pos = 0, __nv_bfloat16 *q_out_bf16 = nullptr) {
     eif_status_t rs = ensure_rope_table(ctx, kv);
     if (rs != EIF_STATUS_OK) return rs;
     AttnPrepArgs a{qg, k, v, kv->q_norm[layer], kv->k_norm[layer], kv->rope_cos, kv->rope_sin, pos, kv->k[layer],
                    kv->v[layer], kv->dtype, q_out, gate_out, kv->batch, n_heads, kv->n_kv, kv->hd,
-                   (int)(kv->hd * 0.25f), kv->max_seq, ctx->dev_err};
+                   (int)(kv->hd * 0.25f), kv->max_seq, ctx->dev_err, q_out_bf16, n_tok, start_pos};
     CK(launch_fullatt_prep(ctx->stream, a));
     ctx->launches += 1;
     return EIF_STATUS_OK;
+}
+
+static eif_status_t prep_prefill_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int n_tok, int start_pos,
+                                       int n_heads) {
+    eif_status_t rs = prep_check(ctx, kv, layer, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (n_tok < 1 || start_pos < 0 || start_pos + n_tok > kv->max_seq)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rows [%d, %d) outside the cache [0, %d)", start_pos,
+                    start_pos + n_tok, kv->max_seq);
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_fullatt_prep_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
+                                                       const float *qg_dev, const float *k_dev, const float *v_dev,
+                                                       int n_tok, int start_pos, int n_heads, void *q_out_dev,
+                                                       float *gate_out_dev) {
+    eif_status_t rs = prep_prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!qg_dev || !k_dev || !v_dev || !q_out_dev || !gate_out_dev)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "fullatt_prep_prefill_dev: NULL pointer");
+    DeviceGuard g(ctx);
+    return prep_run(ctx, kv, layer, qg_dev, k_dev, v_dev, nullptr, n_heads, nullptr, gate_out_dev, n_tok, start_pos,
+                    static_cast<__nv_bfloat16 *>(q_out_dev));
+}
+
+EIF_API eif_status_t eif_cuda_fullatt_prep_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg,
+                                                   const float *k, const float *v, int n_tok, int start_pos,
+                                                   int n_heads, float *q_out, float *gate_out) {
+    eif_status_t rs = prep_prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!qg || !k || !v || !q_out || !gate_out)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "fullatt_prep_prefill: NULL pointer");
+    DeviceGuard g(ctx);
+    const size_t rows = (size_t)kv->batch * n_tok, nq = rows * n_heads * kv->hd, nk = rows * kv->n_kv * kv->hd;
+    Carver cv;
+    const size_t o_qg = cv.take(2 * nq * 4), o_k = cv.take(nk * 4), o_v = cv.take(nk * 4), o_q = cv.take(nq * 4),
+                 o_g = cv.take(nq * 4);
+    rs = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (rs != EIF_STATUS_OK) return rs;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_qg, qg, 2 * nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_k, k, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_v, v, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    rs = prep_run(ctx, kv, layer, reinterpret_cast<float *>(s + o_qg), reinterpret_cast<float *>(s + o_k),
+                  reinterpret_cast<float *>(s + o_v), nullptr, n_heads, reinterpret_cast<float *>(s + o_q),
+                  reinterpret_cast<float *>(s + o_g), n_tok, start_pos);
+    if (rs != EIF_STATUS_OK) return rs;
+    CK(cudaMemcpyAsync(q_out, s + o_q, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaMemcpyAsync(gate_out, s + o_g, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
 }
 
 EIF_API eif_status_t eif_cuda_fullatt_prep_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg_dev,

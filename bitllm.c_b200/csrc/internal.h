@@ -99,15 +99,17 @@ struct DeltaCoreArgs {
 cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *supported);
 
 struct AttnPrepArgs {
-    const float *qg, *k, *v;  // [B][nh][2*hd], [B][nkv*hd], [B][nkv*hd]
+    const float *qg, *k, *v;  // rows r = (b, token): [B*n_tok][nh][2*hd], [B*n_tok][nkv*hd], [B*n_tok][nkv*hd]
     const float *q_norm, *k_norm;  // [hd]
     const float *rope_cos, *rope_sin;  // [max_seq][n_rot/2]
-    const int *pos;  // [B]
+    const int *pos;  // [B] (one token per sequence), or null: row (b, i) sits at start_pos + i
     void *Kc, *Vc;   // layer cache
     eif_cuda_dtype_t dtype;
-    float *q_out, *gate_out;  // [B][nh*hd]
+    float *q_out, *gate_out;  // [B*n_tok][nh*hd] (q_out unused when q_out_bf16 is set)
     int B, nh, nkv, hd, n_rot, max_seq;
     unsigned *dev_err;
+    __nv_bfloat16 *q_out_bf16;  // q as bf16 (the prefill attention's input), or null
+    int n_tok, start_pos;
 };
 cudaError_t launch_fullatt_prep(cudaStream_t st, const AttnPrepArgs &a);
 

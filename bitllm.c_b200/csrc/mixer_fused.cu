@@ -150,11 +150,13 @@ __global__ void __launch_bounds__(THREADS) deltanet_core_kernel(const DeltaCoreA
 }
 
 // One CTA per sequence.
+// One CTA per token row r = (sequence b, token i of n_tok): at position pos[b] (decode, n_tok = 1) or
+// start_pos + i (a prefill chunk, pos null).  Input and output rows are indexed by r, cache rows by (b, p).
 __global__ void __launch_bounds__(256) fullatt_prep_kernel(const AttnPrepArgs a) {
-    const int b = blockIdx.x;
+    const int r = blockIdx.x, b = r / a.n_tok;
     const int hd = a.hd, nh = a.nh, nkv = a.nkv, n_rot = a.n_rot, half = n_rot / 2;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const int p = a.pos[b];
+    const int p = a.pos ? a.pos[b] : a.start_pos + r % a.n_tok;
     const bool pos_ok = p >= 0 && p < a.max_seq;
     if (!pos_ok && tid == 0) atomicOr(a.dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
     const float *cs = a.rope_cos + (size_t)(pos_ok ? p : 0) * half;
@@ -163,13 +165,13 @@ __global__ void __launch_bounds__(256) fullatt_prep_kernel(const AttnPrepArgs a)
     for (int hh = warp; hh < nh + nkv; hh += nw) {
         const bool isq = hh < nh;
         const int hi = isq ? hh : hh - nh;
-        const float *src = isq ? a.qg + ((size_t)b * nh + hi) * 2 * hd : a.k + ((size_t)b * nkv + hi) * hd;
+        const float *src = isq ? a.qg + ((size_t)r * nh + hi) * 2 * hd : a.k + ((size_t)r * nkv + hi) * hd;
         const float *wn = isq ? a.q_norm : a.k_norm;
         float ss = 0.f;
         for (int i = lane; i < hd; i += 32) ss += src[i] * src[i];
         ss = warp_sum(ss);
         const float inv = 1.0f / sqrtf(ss / hd + 1e-6f);
-        float *dst = isq ? a.q_out + ((size_t)b * nh + hi) * hd : nullptr;
+        const size_t qrow = ((size_t)r * nh + hi) * hd;
         for (int i = lane; i < hd; i += 32) {
             float y = src[i] * inv * wn[i];
             if (i < n_rot) {
@@ -179,7 +181,10 @@ __global__ void __launch_bounds__(256) fullatt_prep_kernel(const AttnPrepArgs a)
                 y = i < half ? x0 * cs[j] - x1 * sn[j] : x0 * sn[j] + x1 * cs[j];
             }
             if (isq) {
-                dst[i] = y;
+                if (a.q_out_bf16)
+                    a.q_out_bf16[qrow + i] = __float2bfloat16_rn(y);
+                else
+                    a.q_out[qrow + i] = y;
             } else if (pos_ok) {
                 const size_t row = (((size_t)b * a.max_seq + p) * nkv + hi) * hd + i;
                 if (a.dtype == EIF_CUDA_F32)
@@ -189,12 +194,12 @@ __global__ void __launch_bounds__(256) fullatt_prep_kernel(const AttnPrepArgs a)
             }
         }
         if (isq)
-            for (int i = lane; i < hd; i += 32) a.gate_out[((size_t)b * nh + hi) * hd + i] = src[hd + i];
+            for (int i = lane; i < hd; i += 32) a.gate_out[qrow + i] = src[hd + i];
     }
     if (pos_ok)
         for (int i = tid; i < nkv * hd; i += blockDim.x) {
             const size_t row = ((size_t)b * a.max_seq + p) * nkv * hd + i;
-            const float v = a.v[(size_t)b * nkv * hd + i];
+            const float v = a.v[(size_t)r * nkv * hd + i];
             if (a.dtype == EIF_CUDA_F32)
                 static_cast<float *>(a.Vc)[row] = v;
             else
@@ -221,6 +226,6 @@ cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *
 }
 
 cudaError_t launch_fullatt_prep(cudaStream_t st, const AttnPrepArgs &a) {
-    fullatt_prep_kernel<<<a.B, 256, 0, st>>>(a);
+    fullatt_prep_kernel<<<a.B * a.n_tok, 256, 0, st>>>(a);
     return cudaGetLastError();
 }

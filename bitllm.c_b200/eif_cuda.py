@@ -97,6 +97,8 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_kv_set_norms": (_I, [_P, _P, _I, _P, _P]),
         "eif_cuda_fullatt_prep": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P, _P]),
         "eif_cuda_fullatt_prep_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P, _P]),
+        "eif_cuda_fullatt_prep_prefill": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _P, _P]),
+        "eif_cuda_fullatt_prep_prefill_dev": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _P, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -275,6 +277,24 @@ class KVCache:
     def fullatt_prep_dev(self, layer: int, qg_dev, k_dev, v_dev, pos_dev, n_heads: int, q_out_dev, gate_out_dev):
         self.ctx.check(lib().eif_cuda_fullatt_prep_dev(self.ctx.handle, self._h, layer, qg_dev, k_dev, v_dev, pos_dev,
                                                        n_heads, q_out_dev, gate_out_dev), "fullatt_prep_dev")
+
+    def fullatt_prep_prefill(self, layer: int, qg, k, v, n_tok: int, start_pos: int, n_heads: int):
+        """fullatt_prep for n_tok tokens per sequence at start_pos + i: returns (q, gate)
+        [batch][n_tok][n_heads*head_dim] and writes the chunk's cache rows."""
+        qq, kk, vv = _f32(qg), _f32(k), _f32(v)
+        q = np.zeros((self.batch, n_tok, n_heads * self.head_dim), np.float32)
+        g = np.zeros_like(q)
+        self.ctx.check(lib().eif_cuda_fullatt_prep_prefill(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk),
+                                                           _ptr(vv), n_tok, start_pos, n_heads, _ptr(q), _ptr(g)),
+                       "fullatt_prep_prefill")
+        return q, g
+
+    def fullatt_prep_prefill_dev(self, layer: int, qg_dev, k_dev, v_dev, n_tok: int, start_pos: int, n_heads: int,
+                                 q_out_dev, gate_out_dev):
+        """q_out as bf16 device array; the rest fp32 device arrays; asynchronous."""
+        self.ctx.check(lib().eif_cuda_fullatt_prep_prefill_dev(self.ctx.handle, self._h, layer, qg_dev, k_dev, v_dev,
+                                                               n_tok, start_pos, n_heads, q_out_dev, gate_out_dev),
+                       "fullatt_prep_prefill_dev")
 
     def attend_prefill(self, layer: int, q, n_tok: int, start_pos: int, n_heads: int, scale: float):
         """Causal prefill: q [batch][n_tok][n_heads*head_dim] fp32 -> out of the same shape (fp32)."""

@@ -284,6 +284,19 @@ eif_status_t eif_cuda_fullatt_prep_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, i
                                        const float *k_dev, const float *v_dev, const int *pos_dev, int n_heads,
                                        float *q_out_dev, float *gate_out_dev);
 
+/* fullatt_prep for a prefill chunk: token i of every sequence at position start_pos + i (the per-token
+ * fullatt_prep calls of prefill_chunk, src/eif_qwen35.c:1122-1133), one launch.
+ *   qg [batch][n_tok][n_heads*2*head_dim], k, v [batch][n_tok][n_kv_heads*head_dim];
+ *   q_out, gate_out [batch][n_tok][n_heads*head_dim]
+ * _dev: q_out as bf16 (the input of eif_cuda_attend_prefill_gated_dev), the rest fp32 device arrays,
+ * asynchronous.  Host variant: fp32 host arrays. */
+eif_status_t eif_cuda_fullatt_prep_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg,
+                                           const float *k, const float *v, int n_tok, int start_pos, int n_heads,
+                                           float *q_out, float *gate_out);
+eif_status_t eif_cuda_fullatt_prep_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
+                                               const float *qg_dev, const float *k_dev, const float *v_dev, int n_tok,
+                                               int start_pos, int n_heads, void *q_out_dev, float *gate_out_dev);
+
 #ifdef __cplusplus
 }
 #endif

@@ -108,3 +108,45 @@ def test_qwen35_attention_layer_chain(pkg, ctx, orc, dtype):
             ref = orc.subln(orc.attend_decode(rq, kc[b], vc[b], pos[b], nh, nkv, hd, 1.0 / 16, gate=rg), sub, 2)
             assert rel_l2(out[b], ref) <= TOL, (step, b)
         pos = pos + 1
+
+
+def test_qwen35_attention_prefill_chain(pkg, ctx, orc):
+    """A Qwen3.5 full-attention layer over a prefill chunk as prefill_chunk runs it (src/eif_qwen35.c:1122-1133):
+    fullatt_prep for every token of the chunk (one launch), then the gated causal prefill attention, on a bf16
+    cache that already holds earlier rows; against fullatt_prep + attention + gate + SubLN token by token.
+    fp32 prep outputs: rel-L2 <= 1e-5; the bf16 prefill attention: rel-L2 <= 1e-2, max-abs <= 2e-2."""
+    rng = np.random.default_rng(91)
+    B, nh, nkv, hd, start, n = 2, 8, 2, 256, 20, 100
+    T = start + n + 4
+    kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, pkg.BF16)
+    qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    sub = (1 + 0.1 * rng.standard_normal(nh * hd)).astype(np.float32)
+    kv.set_norms(0, qn, kn)
+    kc = np.zeros((B, T, nkv * hd), np.float32)
+    vc = np.zeros_like(kc)
+    kc[:, :start] = orc.round_bf16(rng.standard_normal((B, start, nkv * hd))).reshape(B, start, -1)
+    vc[:, :start] = orc.round_bf16(rng.standard_normal((B, start, nkv * hd))).reshape(B, start, -1)
+    for b in range(B):
+        kv.upload(0, b, 0, kc[b, :start], vc[b, :start])
+    qg = rng.standard_normal((B, n, nh * 2 * hd)).astype(np.float32)
+    k = rng.standard_normal((B, n, nkv * hd)).astype(np.float32)
+    v = rng.standard_normal((B, n, nkv * hd)).astype(np.float32)
+    q, g = kv.fullatt_prep_prefill(0, qg, k, v, n, start, nh)
+    out = kv.attend_prefill_gated(0, q, n, start, nh, 1.0 / 16, g, pkg.SUBLN_WEIGHT, sub)
+    for b in range(B):
+        rq = np.zeros((n, nh * hd), np.float32)
+        for i in range(n):
+            rq[i], rg, _ = orc.fullatt_prep(qg[b, i], k[b, i], v[b, i], qn, kn, kc[b], vc[b], start + i, nh, nkv, hd)
+            assert np.array_equal(g[b, i], rg)
+            kc[b, start + i] = orc.round_bf16(kc[b, start + i])
+            vc[b, start + i] = orc.round_bf16(vc[b, start + i])
+        assert rel_l2(q[b], rq) <= TOL
+        kd, vd = kv.download(0, b, 0, start + n)
+        assert np.array_equal(vd, vc[b, :start + n])
+        # k is normed and rotated in fp32 on both sides (rel ~1e-7 apart), then rounded to bf16: one ulp at most
+        assert np.all(np.abs(kd - kc[b, :start + n]) <= 2.0 ** -7 * np.abs(kc[b, :start + n]) + 1e-30)
+        q16 = orc.round_bf16(rq).reshape(n, -1)
+        ref = np.stack([orc.subln(orc.attend_decode(q16[i], kc[b], vc[b], start + i, nh, nkv, hd, 1.0 / 16, gate=g[b, i]),
+                                  sub, 2) for i in range(n)])
+        assert rel_l2(out[b], ref) <= 1e-2 and np.max(np.abs(out[b] - ref)) <= 2e-2
