@@ -223,6 +223,11 @@ class HybridHost:
                       v=pinned(rng.standard_normal((B, AT_HKV * AT_D))))
         self.sub_norm = [pinned(w["sub_norm"]) for w in weights.at]
         self.pos = pinned(np.full(B, CTX - 1), np.int32)
+        # the results land in pinned host arrays too (an engine keeps its activations in such buffers)
+        self.dn_out = pinned(np.zeros((B, DN_H * DN_D)))
+        self.q = pinned(np.zeros((B, AT_HQ * AT_D)))
+        self.gate = pinned(np.zeros((B, AT_HQ * AT_D)))
+        self.out = pinned(np.zeros((B, AT_HQ * AT_D)))
         h = self.h
         self.h2d = 0
         self.d2h = 0
@@ -242,12 +247,13 @@ class HybridHost:
         h = self.h
         for typ in LAYER_TYPES:
             if typ == "D":
-                hy.dn.core(d, h["qkv"], h["z"], h["b"], h["a"])
+                hy.dn.core(d, h["qkv"], h["z"], h["b"], h["a"], out=self.dn_out)
                 d += 1
             else:
-                q, g = hy.kv.fullatt_prep(a, h["qg"], h["k"], h["v"], self.pos, AT_HQ)
+                q, g = hy.kv.fullatt_prep(a, h["qg"], h["k"], h["v"], self.pos, AT_HQ, q_out=self.q,
+                                          gate_out=self.gate)
                 hy.kv.attend_decode(a, q, self.pos, AT_HQ, hy.scale, gate=g, subln=hy.pkg.SUBLN_WEIGHT,
-                                    sub_norm=self.sub_norm[a])
+                                    sub_norm=self.sub_norm[a], out=self.out)
                 a += 1
 
 

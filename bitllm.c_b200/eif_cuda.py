@@ -123,6 +123,15 @@ def _i32(a):
     return np.ascontiguousarray(a, dtype=np.int32)
 
 
+def _out(a, shape):
+    """A caller-provided fp32 output array of exactly `shape` (C-contiguous), or a fresh zeroed one."""
+    if a is None:
+        return np.zeros(shape, np.float32)
+    if a.dtype != np.float32 or not a.flags["C_CONTIGUOUS"] or a.shape != tuple(shape):
+        raise ValueError(f"output array must be C-contiguous float32 of shape {tuple(shape)}")
+    return a
+
+
 def device_count() -> int:
     return lib().eif_cuda_device_count()
 
@@ -248,12 +257,13 @@ class KVCache:
                        "kv_append_dev")
 
     def attend_decode(self, layer: int, q, pos, n_heads: int, scale: float, gate=None, subln: int = SUBLN_NONE,
-                      sub_norm=None):
-        """q [batch][n_heads*head_dim] fp32 -> out [batch][n_heads*head_dim] fp32."""
+                      sub_norm=None, out=None):
+        """q [batch][n_heads*head_dim] fp32 -> out [batch][n_heads*head_dim] fp32 (written into `out` when
+        given, e.g. a pinned host array)."""
         qq, pp = _f32(q), _i32(pos)
         gg = _f32(gate) if gate is not None else None
         nn = _f32(sub_norm) if sub_norm is not None else None
-        out = np.zeros((self.batch, n_heads * self.head_dim), np.float32)
+        out = _out(out, (self.batch, n_heads * self.head_dim))
         self.ctx.check(lib().eif_cuda_attend_decode(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(pp), n_heads,
                                                     float(scale), _ptr(gg), int(subln), _ptr(nn), _ptr(out)),
                        "attend_decode")
@@ -264,12 +274,12 @@ class KVCache:
         qn, kn = _f32(q_norm), _f32(k_norm)
         self.ctx.check(lib().eif_cuda_kv_set_norms(self.ctx.handle, self._h, layer, _ptr(qn), _ptr(kn)), "kv_set_norms")
 
-    def fullatt_prep(self, layer: int, qg, k, v, pos, n_heads: int):
-        """fullatt_prep for one token per sequence: returns (q, gate) [batch][n_heads*head_dim]; writes k, v
-        (normed and rotated k) into cache row pos[b]."""
+    def fullatt_prep(self, layer: int, qg, k, v, pos, n_heads: int, q_out=None, gate_out=None):
+        """fullatt_prep for one token per sequence: returns (q, gate) [batch][n_heads*head_dim] (in q_out /
+        gate_out when given); writes k, v (normed and rotated k) into cache row pos[b]."""
         qq, kk, vv, pp = _f32(qg), _f32(k), _f32(v), _i32(pos)
-        q = np.zeros((self.batch, n_heads * self.head_dim), np.float32)
-        g = np.zeros_like(q)
+        q = _out(q_out, (self.batch, n_heads * self.head_dim))
+        g = _out(gate_out, (self.batch, n_heads * self.head_dim))
         self.ctx.check(lib().eif_cuda_fullatt_prep(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv),
                                                    _ptr(pp), n_heads, _ptr(q), _ptr(g)), "fullatt_prep")
         return q, g
@@ -397,10 +407,11 @@ class DeltaState:
         self.ctx.check(lib().eif_cuda_delta_set_weights(self.ctx.handle, self._h, layer, *[_ptr(x) for x in a]),
                        "delta_set_weights")
 
-    def core(self, layer: int, qkv, z, b_raw, a_raw):
-        """deltanet_core for one token of every sequence: returns out [batch][H*d_v]."""
+    def core(self, layer: int, qkv, z, b_raw, a_raw, out=None):
+        """deltanet_core for one token of every sequence: returns out [batch][H*d_v] (written into `out`
+        when given, e.g. a pinned host array)."""
         a = [_f32(x) for x in (qkv, z, b_raw, a_raw)]
-        out = np.zeros((self.batch, self.H * self.dv), np.float32)
+        out = _out(out, (self.batch, self.H * self.dv))
         self.ctx.check(lib().eif_cuda_deltanet_core(self.ctx.handle, self._h, layer, *[_ptr(x) for x in a], _ptr(out)),
                        "deltanet_core")
         return out
