@@ -69,7 +69,17 @@ class ClockSampler:
         self.proc = None
         self.lines = []
 
+    def _once(self):
+        """One synchronous reading (brackets timed regions shorter than the 200 ms period)."""
+        try:
+            r = subprocess.run(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
+                                "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=10)
+            self.lines.extend(ln.strip() for ln in r.stdout.splitlines() if ln.strip())
+        except (FileNotFoundError, OSError, subprocess.TimeoutExpired):
+            pass
+
     def start(self):
+        self._once()
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -89,6 +99,7 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        self._once()
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
@@ -496,16 +507,55 @@ def cpu_prefill_reference(seconds=20.0):
     positions = list(range(PF_S - 1, -1, -PF_S // 256))
     pool = ThreadPoolExecutor(max_workers=ncpu)
     done, t0 = [], time.perf_counter()
-    for i in range(0, len(positions), ncpu):
-        done += list(pool.map(one, positions[i:i + ncpu]))
-        if time.perf_counter() - t0 > seconds:
-            break
+    while time.perf_counter() - t0 < seconds:  # cycle over the spread of positions for the time budget
+        for i in range(0, len(positions), ncpu):
+            done += list(pool.map(one, positions[i:i + ncpu]))
     el = time.perf_counter() - t0
     pool.shutdown()
     flops_done = sum(4.0 * PF_HQ * PF_D * (t + 1) for t in done)
     tps = PF_B * PF_S / (el * prefill_flops(PF_B, PF_S) / flops_done)
-    return tps, ncpu, kind, (f"{len(done)} of the {PF_S} query tokens of one sequence (positions spread over the "
-                             f"causal range), one token per host thread, {el:.1f} s; scaled by FLOPs to {PF_B} x {PF_S}")
+    return tps, ncpu, kind, (f"{len(done)} query tokens of one sequence (256 positions spread over the causal "
+                             f"range, repeated), one token per host thread, {el:.1f} s; scaled by FLOPs to "
+                             f"{PF_B} x {PF_S}")
+
+
+def cpu_chunked_reference(seconds=10.0):
+    """What the engine's prefill_chunk runs for a DeltaNet layer: the reference's deltanet_core once per
+    token (src/eif_qwen35.c:1104-1106; conv window, norms, gates, the rule, gated RMSNorm), 16 heads of
+    d 128 from a zero state, one sequence per host thread for the time budget.  Returns tokens/s of all
+    threads together (the rule, config 4's work, is the bulk of each call)."""
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as orc
+    ncpu = len(os.sched_getaffinity(0))
+    kind = "reference" if orc.ref_available() else "port"
+    lib = orc.ref() if kind == "reference" else None
+    if kind == "reference":
+        orc.ref().ref_set_threads(1)
+    W = Weights().dn[0]
+    rng = np.random.default_rng(6)
+    xs = [dict(qkv=rng.standard_normal(DN_CONV).astype(np.float32), z=rng.standard_normal(DN_H * DN_D).astype(
+        np.float32), b=rng.standard_normal(DN_H).astype(np.float32), a=rng.standard_normal(DN_H).astype(np.float32))
+          for _ in range(16)]
+
+    def run(_):
+        S = np.zeros((DN_H, DN_D, DN_D), np.float32)
+        conv = np.zeros((DN_CONV, CONV_K), np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            x = xs[n % len(xs)]
+            orc.deltanet_core(x["qkv"], x["z"], x["b"], x["a"], conv, S, lib=lib, **W)
+            n += 1
+        return n, time.perf_counter() - t0
+
+    pool = ThreadPoolExecutor(max_workers=ncpu)
+    res = list(pool.map(run, range(ncpu)))
+    pool.shutdown()
+    tokens = sum(n for n, _ in res)
+    el = max(t for _, t in res)
+    return tokens / el, ncpu, kind, (f"{tokens} tokens of deltanet_core (16 heads, d 128), one sequence per host "
+                                     f"thread, {el:.1f} s")
 
 
 def run_prefill(args, torch, dist, rank, world, local_rank):
@@ -651,6 +701,26 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
+    # e2e through the host-pointer entry: fp32 q / k / v / beta / g from pinned host memory, fp32 o read back
+    e2e = None
+    if not args.no_e2e:
+        def pinned(t_):
+            return t_.float().cpu().pin_memory()
+        hq, hk, hv, hb, hg = (pinned(x) for x in (q, k, v, beta, g))
+        ho = torch.empty(B, CK_T, H, CK_D).pin_memory()
+        ctx.set_stream(None)
+        reps = max(1, args.steps // 4)
+        st.reset()
+        st.prefill(0, hq.numpy(), hk.numpy(), hv.numpy(), hb.numpy(), hg.numpy(), qs, out=ho.numpy())  # warm
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            st.reset()
+            st.prefill(0, hq.numpy(), hk.numpy(), hv.numpy(), hb.numpy(), hg.numpy(), qs, out=ho.numpy())
+        e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / reps, "cuda")
+        nb = sum(x.numel() * 4 for x in (hq, hk, hv, hb, hg))
+        e2e = {"value": CK_B * CK_T / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": nb * world, "d2h_bytes_per_step": ho.numel() * 4 * world,
+               "path": "host-pointer C ABI eif_cuda_deltanet_prefill (fp32 in/out; state reset included)"}
     if rank != 0:
         return None
     hbm, _, src = peaks()
@@ -659,7 +729,7 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
     bytes_alg = B * CK_T * H * (3 * CK_D * 2 + 2 * 4 + CK_D * 2) + 2 * B * H * CK_D * CK_D * 4
     ach = bytes_alg / (ms * 1e-3) / 1e9
     flops_rec = 4.0 * CK_D * CK_D * GB * CK_T * CK_H
-    return {"metric": "chunked DeltaNet prefill tokens/s (BASELINE configs[3])", "value": GB * CK_T / (ms * 1e-3),
+    line = {"metric": "chunked DeltaNet prefill tokens/s (BASELINE configs[3])", "value": GB * CK_T / (ms * 1e-3),
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16 q/k/v/o, fp32 state and accumulate", "data": "synthetic (seeded)",
@@ -672,6 +742,12 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
                              bytes_alg, "recurrent_equivalent_tflops": flops_rec / (ms * 1e-3) / 1e12,
                          "traffic": None},
             "gpu_launches": launches, "clocks": clk}
+    if e2e is not None:
+        line["e2e"] = e2e
+    if world == 1 and not args.no_cpu_baseline:
+        tps, cores, kind, sample = cpu_chunked_reference()
+        line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
+    return line
 
 
 def main():

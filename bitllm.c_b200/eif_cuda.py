@@ -434,12 +434,13 @@ class DeltaState:
         self.ctx.check(lib().eif_cuda_deltanet_prefill_core_dev(self.ctx.handle, self._h, layer, qkv_dev, z_dev, b_dev,
                                                                 a_dev, n_tok, out_dev), "deltanet_prefill_core_dev")
 
-    def prefill(self, layer: int, q, k, v, beta, g, q_scale: float):
+    def prefill(self, layer: int, q, k, v, beta, g, q_scale: float, out=None):
         """Chunked prefill of n_tok tokens per sequence (fp32 host arrays; q, k [batch][n_tok][H][d_k],
-        v [batch][n_tok][H][d_v], beta, g [batch][n_tok][H]); returns o [batch][n_tok][H][d_v]."""
+        v [batch][n_tok][H][d_v], beta, g [batch][n_tok][H]); returns o [batch][n_tok][H][d_v] (in `out`
+        when given)."""
         qq, kk, vv, bb, gg = (_f32(x) for x in (q, k, v, beta, g))
         n_tok = qq.shape[1]
-        o = np.zeros((self.batch, n_tok, self.H, self.dv), np.float32)
+        o = _out(out, (self.batch, n_tok, self.H, self.dv))
         self.ctx.check(lib().eif_cuda_deltanet_prefill(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv),
                                                        _ptr(bb), _ptr(gg), n_tok, float(q_scale), _ptr(o)),
                        "deltanet_prefill")
