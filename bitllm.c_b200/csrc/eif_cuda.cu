@@ -914,7 +914,7 @@ static eif_status_t core_run(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int laye
     const size_t ncw = (size_t)st->conv_dim * st->conv_k;
     const float *w = st->weights[layer];
     DeltaCoreArgs a{st->S[layer], st->conv[layer], qkv, z, b_raw, a_raw, w, w + ncw, w + ncw + st->H,
-                    w + ncw + 2 * st->H, out, st->batch, st->H, st->dk, st->dv, st->conv_k};
+                    w + ncw + 2 * st->H, out, st->batch, st->H, st->dk, st->dv, st->conv_k, ctx->dev_err};
     bool ok = true;
     cudaError_t e = launch_deltanet_core(ctx->stream, a, &ok);
     if (!ok) return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "deltanet_core: d_k %d / d_v %d not supported", st->dk, st->dv);

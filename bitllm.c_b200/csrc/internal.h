@@ -95,6 +95,7 @@ struct DeltaCoreArgs {
     const float *conv_w, *dt_bias, *a_exp, *norm_w;  // layer weights: [conv_dim][conv_k], [H], [H], [dv]
     float *out;  // [B][H*dv]
     int B, H, dk, dv, conv_k;
+    unsigned *dev_err;
 };
 cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *supported);
 

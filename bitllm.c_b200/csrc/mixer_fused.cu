@@ -17,6 +17,7 @@
 
 #include "internal.h"
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace {
 
@@ -40,12 +41,22 @@ __global__ void __launch_bounds__(THREADS) deltanet_core_kernel(const DeltaCoreA
     __shared__ float red[NW];
     __shared__ float4 cred[NW][LPR];
     __shared__ float gates[2];
+    __shared__ __align__(8) uint64_t s_bar;
+    extern __shared__ __align__(128) float Ssm[];  // the head's S [DK][DV]
 
+    // the head's state (contiguous DK*DV floats) streams into shared memory while the conv / norm / gate
+    // work below runs: one thread issues bulk copies completing on s_bar (waited on after later barriers)
     float *Sh = a.S + bh * DK * DV;
     const int col0 = lc * 4;
-    float4 s[NP];
-#pragma unroll
-    for (int p = 0; p < NP; ++p) s[p] = __ldcs(reinterpret_cast<const float4 *>(Sh + (size_t)(rg + p * RP) * DV + col0));
+    const uint32_t sbar = smem_u32(&s_bar);
+    if (tid == 0) {
+        constexpr uint32_t bytes = DK * DV * 4, piece = bytes < 16384 ? bytes : 16384;
+        mbar_init(sbar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(sbar, bytes);
+        for (uint32_t off = 0; off < bytes; off += piece)
+            bulk_load(smem_u32(Ssm) + off, reinterpret_cast<const char *>(Sh) + off, piece, sbar);
+    }
 
     // causal conv1d + SiLU on this head's channels: q [h*DK, +DK), k [key_dim + h*DK, +DK), v [2*key_dim + h*DV, +DV)
     const int ck = a.conv_k;
@@ -112,12 +123,16 @@ __global__ void __launch_bounds__(THREADS) deltanet_core_kernel(const DeltaCoreA
     };
 
     const float decay = expf(gates[1]), bet = gates[0];
+    // a wait that gives up leaves S untouched (the error word tells the host)
+    const bool s_ok = mbar_wait(sbar, 0, a.dev_err);
+    const float4 *Srow = reinterpret_cast<const float4 *>(Ssm) + col0 / 4;
     float4 e = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
         const float ki = sk[rg + p * RP];
-        s[p].x *= decay; s[p].y *= decay; s[p].z *= decay; s[p].w *= decay;
-        e.x += s[p].x * ki; e.y += s[p].y * ki; e.z += s[p].z * ki; e.w += s[p].w * ki;
+        float4 s = Srow[(rg + p * RP) * (DV / 4)];
+        s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;
+        e.x += s.x * ki; e.y += s.y * ki; e.z += s.z * ki; e.w += s.w * ki;
     }
     e = colsum(e);
     const float4 vv = make_float4(sv[col0], sv[col0 + 1], sv[col0 + 2], sv[col0 + 3]);
@@ -127,10 +142,12 @@ __global__ void __launch_bounds__(THREADS) deltanet_core_kernel(const DeltaCoreA
     for (int p = 0; p < NP; ++p) {
         const int i = rg + p * RP;
         const float ki = bet * sk[i];
-        s[p].x += ki * dlt.x; s[p].y += ki * dlt.y; s[p].z += ki * dlt.z; s[p].w += ki * dlt.w;
-        __stcs(reinterpret_cast<float4 *>(Sh + (size_t)i * DV + col0), s[p]);
+        float4 s = Srow[i * (DV / 4)];
+        s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;  // as in the first pass
+        s.x += ki * dlt.x; s.y += ki * dlt.y; s.z += ki * dlt.z; s.w += ki * dlt.w;
+        if (s_ok) __stcs(reinterpret_cast<float4 *>(Sh + (size_t)i * DV + col0), s);
         const float qi = sq[i];
-        o.x += s[p].x * qi; o.y += s[p].y * qi; o.z += s[p].z * qi; o.w += s[p].w * qi;
+        o.x += s.x * qi; o.y += s.y * qi; o.z += s.z * qi; o.w += s.w * qi;
     }
     o = colsum(o);
     // gated RMSNorm over the head's d_v outputs (threads of row group 0 hold the whole row)
@@ -212,17 +229,17 @@ __global__ void __launch_bounds__(256) fullatt_prep_kernel(const AttnPrepArgs a)
 cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *supported) {
     *supported = true;
     const dim3 grid(a.H, a.B);
-    if (a.dk == 128 && a.dv == 128)
-        deltanet_core_kernel<128, 128, 256><<<grid, 256, 0, st>>>(a);
-    else if (a.dk == 128 && a.dv == 64)
-        deltanet_core_kernel<128, 64, 256><<<grid, 256, 0, st>>>(a);
-    else if (a.dk == 64 && a.dv == 64)
-        deltanet_core_kernel<64, 64, 128><<<grid, 128, 0, st>>>(a);
-    else {
-        *supported = false;
-        return cudaSuccess;
-    }
-    return cudaGetLastError();
+    auto run = [&](auto kernel, int threads, int smem) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        kernel<<<grid, threads, smem, st>>>(a);
+        return cudaGetLastError();
+    };
+    if (a.dk == 128 && a.dv == 128) return run(deltanet_core_kernel<128, 128, 256>, 256, 128 * 128 * 4);
+    if (a.dk == 128 && a.dv == 64) return run(deltanet_core_kernel<128, 64, 256>, 256, 128 * 64 * 4);
+    if (a.dk == 64 && a.dv == 64) return run(deltanet_core_kernel<64, 64, 128>, 128, 64 * 64 * 4);
+    *supported = false;
+    return cudaSuccess;
 }
 
 cudaError_t launch_fullatt_prep(cudaStream_t st, const AttnPrepArgs &a) {

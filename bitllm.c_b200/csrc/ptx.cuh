@@ -75,6 +75,15 @@ EIF_DEV void tma_load_3d(uint32_t dst, const CUtensorMap *map, int c0, int c1, i
         : "memory");
 }
 
+// Contiguous bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16), completion
+// counted on `bar` (no multicast).
+EIF_DEV void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
 EIF_DEV void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
