@@ -288,7 +288,7 @@ def run_ours(args, torch, dist, rank, world, local_rank):
     import __graft_entry__
     pkg = __graft_entry__.load_package()
     torch.cuda.set_device(local_rank)
-    GB = args.batch
+    GB = args.batch or BATCH
     B = pkg.shard.shard(GB, 1, world, rank).nb  # by sequence (layers differ in head count)
     ctx = pkg.Context(local_rank)
     # one explicit stream for the library's launches, the fills and the timing events
@@ -564,7 +564,8 @@ def run_prefill(args, torch, dist, rank, world, local_rank):
     pkg = __graft_entry__.load_package()
     torch.cuda.set_device(local_rank)
     # (sequence, kv-head group) units: past 8 ranks a sequence's two kv groups go to different ranks
-    sh = pkg.shard.shard(PF_B, PF_HKV, world, rank)
+    GBP = args.batch or PF_B  # global batch (a smaller one only for profiling captures)
+    sh = pkg.shard.shard(GBP, PF_HKV, world, rank)
     B, hkv = sh.nb, sh.nh
     hq = hkv * (PF_HQ // PF_HKV)
     ctx = pkg.Context(local_rank)
@@ -619,7 +620,7 @@ def run_prefill(args, torch, dist, rank, world, local_rank):
     _, tflops_peak, src = peaks()
     flops = prefill_flops(B, PF_S) * hq / PF_HQ  # this rank's launch
     ach = flops / (ms * 1e-3) / 1e12
-    GB = PF_B
+    GB = GBP
     line = {"metric": "causal prefill attention tokens/s (BASELINE configs[1])", "value": GB * PF_S / (ms * 1e-3),
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -649,7 +650,8 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
     import __graft_entry__
     pkg = __graft_entry__.load_package()
     torch.cuda.set_device(local_rank)
-    sh = pkg.shard.shard(CK_B, CK_H, world, rank)  # (sequence, head) units; past 4 ranks heads split
+    GBC = args.batch or CK_B  # global batch (a smaller one only for profiling captures)
+    sh = pkg.shard.shard(GBC, CK_H, world, rank)  # (sequence, head) units; past 4 ranks heads split
     B, H = sh.nb, sh.nh
     ctx = pkg.Context(local_rank)
     stream = torch.cuda.Stream()
@@ -718,13 +720,13 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
             st.prefill(0, hq.numpy(), hk.numpy(), hv.numpy(), hb.numpy(), hg.numpy(), qs, out=ho.numpy())
         e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / reps, "cuda")
         nb = sum(x.numel() * 4 for x in (hq, hk, hv, hb, hg))
-        e2e = {"value": CK_B * CK_T / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+        e2e = {"value": GBC * CK_T / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": nb * world, "d2h_bytes_per_step": ho.numel() * 4 * world,
                "path": "host-pointer C ABI eif_cuda_deltanet_prefill (fp32 in/out; state reset included)"}
     if rank != 0:
         return None
     hbm, _, src = peaks()
-    GB = CK_B
+    GB = GBC
     # this rank's launch: q, k, v, o (bf16) + beta, g per token-head, S read and written once
     bytes_alg = B * CK_T * H * (3 * CK_D * 2 + 2 * 4 + CK_D * 2) + 2 * B * H * CK_D * CK_D * 4
     ach = bytes_alg / (ms * 1e-3) / 1e9
@@ -760,7 +762,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-pointer end-to-end leg (profiling runs)")
-    ap.add_argument("--batch", type=int, default=BATCH, help="global batch (default: the config's 256)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="global batch (default: the workload's config: 256 hybrid, 8 prefill, 4 chunked)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
