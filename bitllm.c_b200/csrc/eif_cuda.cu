@@ -326,6 +326,10 @@ EIF_API void eif_cuda_kv_free(eif_cuda_kv_t *kv) {
         DeviceGuard g(kv->ctx);
         cudaFree(kv->rope_cos);
     }
+    if (kv->tl_cos) {
+        DeviceGuard g(kv->ctx);
+        cudaFree(kv->tl_cos);
+    }
     free(kv->q_norm);
     free(kv->k_norm);
     delete kv;
@@ -1137,6 +1141,149 @@ EIF_API eif_status_t eif_cuda_deltanet_prefill(eif_cuda_ctx_t *ctx, eif_cuda_del
     CK(launch_bf16_to_f32(ctx->stream, reinterpret_cast<__nv_bfloat16 *>(s + o_o), f, nv));
     ctx->launches += 1;
     CK(cudaMemcpyAsync(o, f, nv * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// =================================================================================================
+// tinyllm RoPE + cache write
+// =================================================================================================
+
+EIF_API eif_status_t eif_cuda_kv_set_rope(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, float theta, int interleaved) {
+    if (!ctx || !kv || kv->ctx != ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    if (!(theta > 0.f)) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rope theta %g", (double)theta);
+    if (kv->hd % 2 || kv->hd > 256)
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "rope: head_dim %d (even, <= 256)", kv->hd);
+    DeviceGuard g(ctx);
+    const int half = kv->hd / 2;
+    const size_t n = (size_t)kv->max_seq * half;
+    float *hc = (float *)malloc(2 * n * sizeof(float));
+    if (!hc) return fail(ctx, EIF_STATUS_OUT_OF_MEMORY, "rope table");
+    // the reference's per-position table (src/eif_tinyllm.c:399-404), for every position of the cache
+    for (int j = 0; j < half; ++j) {
+        const float freq = 1.0f / powf(theta, (float)(2 * j) / (float)kv->hd);
+        for (int pos = 0; pos < kv->max_seq; ++pos) {
+            const float val = (float)pos * freq;
+            hc[(size_t)pos * half + j] = cosf(val);
+            hc[n + (size_t)pos * half + j] = sinf(val);
+        }
+    }
+    cudaError_t e = cudaSuccess;
+    if (!kv->tl_cos) {
+        float *d = nullptr;
+        e = cudaMalloc(&d, 2 * n * sizeof(float));
+        if (e == cudaSuccess) {
+            kv->tl_cos = d;
+            kv->tl_sin = d + n;
+        }
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(kv->tl_cos, hc, 2 * n * sizeof(float), cudaMemcpyHostToDevice);
+    free(hc);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "rope table");
+    kv->tl_interleaved = interleaved != 0;
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t rope_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int n_heads) {
+    if (!ctx || !kv || kv->ctx != ctx) return EIF_STATUS_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= kv->n_layers) return fail(ctx, EIF_STATUS_INVALID_LAYER, "layer %d out of range", layer);
+    if (n_heads <= 0 || n_heads % kv->n_kv)
+        return fail(ctx, EIF_STATUS_SHAPE_MISMATCH, "n_heads %d is not a multiple of n_kv_heads %d", n_heads, kv->n_kv);
+    if (!kv->tl_cos) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "no RoPE table (eif_cuda_kv_set_rope)");
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t rope_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q, const float *k,
+                             const float *v, const int *pos, int n_tok, int start_pos, int n_heads, float *q_out,
+                             __nv_bfloat16 *q_out_bf16) {
+    RopeArgs a{q, k, v, kv->tl_cos, kv->tl_sin, pos, kv->k[layer], kv->v[layer], kv->dtype, q_out, q_out_bf16,
+               kv->batch, n_tok, start_pos, n_heads, kv->n_kv, kv->hd, kv->max_seq, kv->tl_interleaved, ctx->dev_err};
+    CK(launch_rope_append(ctx->stream, a));
+    ctx->launches += 1;
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_rope_append_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_dev,
+                                              const float *k_dev, const float *v_dev, const int *pos_dev, int n_heads,
+                                              float *q_out_dev) {
+    eif_status_t rs = rope_check(ctx, kv, layer, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!q_dev || !k_dev || !v_dev || !pos_dev || !q_out_dev)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rope_append_dev: NULL pointer");
+    DeviceGuard g(ctx);
+    return rope_run(ctx, kv, layer, q_dev, k_dev, v_dev, pos_dev, 1, 0, n_heads, q_out_dev, nullptr);
+}
+
+EIF_API eif_status_t eif_cuda_rope_append(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
+                                          const float *k, const float *v, const int *pos, int n_heads, float *q_out) {
+    eif_status_t rs = rope_check(ctx, kv, layer, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!q || !k || !v || !pos || !q_out) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rope_append: NULL pointer");
+    for (int b = 0; b < kv->batch; ++b)
+        if (pos[b] < 0 || pos[b] >= kv->max_seq)
+            return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "pos[%d] = %d outside [0, %d)", b, pos[b], kv->max_seq);
+    DeviceGuard g(ctx);
+    const size_t B = kv->batch, nq = B * n_heads * kv->hd, nk = B * kv->n_kv * kv->hd;
+    Carver cv;
+    const size_t o_q = cv.take(nq * 4), o_k = cv.take(nk * 4), o_v = cv.take(nk * 4), o_p = cv.take(B * 4),
+                 o_o = cv.take(nq * 4);
+    rs = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (rs != EIF_STATUS_OK) return rs;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_q, q, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_k, k, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_v, v, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_p, pos, B * 4, cudaMemcpyHostToDevice, ctx->stream));
+    rs = rope_run(ctx, kv, layer, reinterpret_cast<float *>(s + o_q), reinterpret_cast<float *>(s + o_k),
+                  reinterpret_cast<float *>(s + o_v), reinterpret_cast<int *>(s + o_p), 1, 0, n_heads,
+                  reinterpret_cast<float *>(s + o_o), nullptr);
+    if (rs != EIF_STATUS_OK) return rs;
+    CK(cudaMemcpyAsync(q_out, s + o_o, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+static eif_status_t rope_prefill_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int n_tok, int start_pos,
+                                       int n_heads) {
+    eif_status_t rs = rope_check(ctx, kv, layer, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (n_tok < 1 || start_pos < 0 || start_pos + n_tok > kv->max_seq)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rows [%d, %d) outside the cache [0, %d)", start_pos,
+                    start_pos + n_tok, kv->max_seq);
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_rope_append_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
+                                                      const float *q_dev, const float *k_dev, const float *v_dev,
+                                                      int n_tok, int start_pos, int n_heads, void *q_out_dev) {
+    eif_status_t rs = rope_prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!q_dev || !k_dev || !v_dev || !q_out_dev)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rope_append_prefill_dev: NULL pointer");
+    DeviceGuard g(ctx);
+    return rope_run(ctx, kv, layer, q_dev, k_dev, v_dev, nullptr, n_tok, start_pos, n_heads, nullptr,
+                    static_cast<__nv_bfloat16 *>(q_out_dev));
+}
+
+EIF_API eif_status_t eif_cuda_rope_append_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
+                                                  const float *k, const float *v, int n_tok, int start_pos,
+                                                  int n_heads, float *q_out) {
+    eif_status_t rs = rope_prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!q || !k || !v || !q_out) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rope_append_prefill: NULL pointer");
+    DeviceGuard g(ctx);
+    const size_t rows = (size_t)kv->batch * n_tok, nq = rows * n_heads * kv->hd, nk = rows * kv->n_kv * kv->hd;
+    Carver cv;
+    const size_t o_q = cv.take(nq * 4), o_k = cv.take(nk * 4), o_v = cv.take(nk * 4), o_o = cv.take(nq * 4);
+    rs = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (rs != EIF_STATUS_OK) return rs;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_q, q, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_k, k, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_v, v, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    rs = rope_run(ctx, kv, layer, reinterpret_cast<float *>(s + o_q), reinterpret_cast<float *>(s + o_k),
+                  reinterpret_cast<float *>(s + o_v), nullptr, n_tok, start_pos, n_heads,
+                  reinterpret_cast<float *>(s + o_o), nullptr);
+    if (rs != EIF_STATUS_OK) return rs;
+    CK(cudaMemcpyAsync(q_out, s + o_o, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return wait_stream(ctx);
 }
 

@@ -51,6 +51,9 @@ struct eif_cuda_kv {
     // Qwen3.5 attention prep: per-layer q_norm / k_norm [hd] and the partial-RoPE cos / sin table
     float **q_norm = nullptr, **k_norm = nullptr;
     float *rope_cos = nullptr, *rope_sin = nullptr;  // [max_seq][hd/8], theta 1e7 (made on first use)
+    // tinyllm RoPE: full-width tables [max_seq][hd/2] for the model's theta (eif_cuda_kv_set_rope)
+    float *tl_cos = nullptr, *tl_sin = nullptr;
+    int tl_interleaved = 0;
 };
 
 struct eif_cuda_delta {
@@ -113,6 +116,20 @@ struct AttnPrepArgs {
     int n_tok, start_pos;
 };
 cudaError_t launch_fullatt_prep(cudaStream_t st, const AttnPrepArgs &a);
+
+// tinyllm RoPE + cache write (rope.cu): rows r = (b, token) as in AttnPrepArgs.
+struct RopeArgs {
+    const float *q, *k, *v;            // [B*n_tok][nh*hd], [B*n_tok][nkv*hd], [B*n_tok][nkv*hd]
+    const float *cos_t, *sin_t;        // [max_seq][hd/2]
+    const int *pos;                    // [B] or null (row (b, i) at start_pos + i)
+    void *Kc, *Vc;
+    eif_cuda_dtype_t dtype;
+    float *q_out;                      // [B*n_tok][nh*hd] fp32, unless q_out_bf16 is set
+    __nv_bfloat16 *q_out_bf16;
+    int B, n_tok, start_pos, nh, nkv, hd, max_seq, interleaved;
+    unsigned *dev_err;
+};
+cudaError_t launch_rope_append(cudaStream_t st, const RopeArgs &a);
 
 // Chunked (WY / UT) DeltaNet prefill (deltanet_chunked.cu).
 bool deltanet_chunked_supported(int dk, int dv);

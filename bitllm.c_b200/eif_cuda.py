@@ -72,6 +72,11 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_kv_layer_ptrs": (_I, [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
         "eif_cuda_kv_append": (_I, [_P, _P, _I, _P, _P, _P]),
         "eif_cuda_kv_append_dev": (_I, [_P, _P, _I, _P, _P, _P]),
+        "eif_cuda_kv_set_rope": (_I, [_P, _P, _F, _I]),
+        "eif_cuda_rope_append": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P]),
+        "eif_cuda_rope_append_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P]),
+        "eif_cuda_rope_append_prefill": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _P]),
+        "eif_cuda_rope_append_prefill_dev": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _P]),
         "eif_cuda_attend_decode": (_I, [_P, _P, _I, _P, _P, _I, _F, _P, _I, _P, _P]),
         "eif_cuda_attend_decode_dev": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _P, _I, _P, _P]),
         "eif_cuda_attend_decode_noalloc_dev": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _P, _I, _P, _P]),
@@ -255,6 +260,39 @@ class KVCache:
     def append_dev(self, layer: int, pos_dev: int, k_dev: int, v_dev: int):
         self.ctx.check(lib().eif_cuda_kv_append_dev(self.ctx.handle, self._h, layer, pos_dev, k_dev, v_dev),
                        "kv_append_dev")
+
+    def set_rope(self, theta: float, interleaved: bool = False):
+        """tinyllm RoPE tables of the model's theta; interleaved = adjacent pairs (llama-style)."""
+        self.ctx.check(lib().eif_cuda_kv_set_rope(self.ctx.handle, self._h, float(theta), int(bool(interleaved))),
+                       "kv_set_rope")
+
+    def rope_append(self, layer: int, q, k, v, pos, n_heads: int, q_out=None):
+        """RoPE of q and k at pos[b] and the cache write of k, v: returns the rotated q [batch][n_heads*hd]."""
+        qq, kk, vv, pp = _f32(q), _f32(k), _f32(v), _i32(pos)
+        out = _out(q_out, (self.batch, n_heads * self.head_dim))
+        self.ctx.check(lib().eif_cuda_rope_append(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv),
+                                                  _ptr(pp), n_heads, _ptr(out)), "rope_append")
+        return out
+
+    def rope_append_dev(self, layer: int, q_dev, k_dev, v_dev, pos_dev, n_heads: int, q_out_dev):
+        self.ctx.check(lib().eif_cuda_rope_append_dev(self.ctx.handle, self._h, layer, q_dev, k_dev, v_dev, pos_dev,
+                                                      n_heads, q_out_dev), "rope_append_dev")
+
+    def rope_append_prefill(self, layer: int, q, k, v, n_tok: int, start_pos: int, n_heads: int):
+        """RoPE + cache write for n_tok tokens per sequence at start_pos + i: returns the rotated q."""
+        qq, kk, vv = _f32(q), _f32(k), _f32(v)
+        out = np.zeros((self.batch, n_tok, n_heads * self.head_dim), np.float32)
+        self.ctx.check(lib().eif_cuda_rope_append_prefill(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk),
+                                                          _ptr(vv), n_tok, start_pos, n_heads, _ptr(out)),
+                       "rope_append_prefill")
+        return out
+
+    def rope_append_prefill_dev(self, layer: int, q_dev, k_dev, v_dev, n_tok: int, start_pos: int, n_heads: int,
+                                q_out_dev):
+        """q_out as bf16 device array (the prefill attention's input); q / k / v fp32 device arrays."""
+        self.ctx.check(lib().eif_cuda_rope_append_prefill_dev(self.ctx.handle, self._h, layer, q_dev, k_dev, v_dev,
+                                                              n_tok, start_pos, n_heads, q_out_dev),
+                       "rope_append_prefill_dev")
 
     def attend_decode(self, layer: int, q, pos, n_heads: int, scale: float, gate=None, subln: int = SUBLN_NONE,
                       sub_norm=None, out=None):

@@ -124,6 +124,34 @@ eif_status_t eif_cuda_kv_append(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int laye
 eif_status_t eif_cuda_kv_append_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const int *pos_dev,
                                     const float *k_dev, const float *v_dev);
 
+/* tinyllm RoPE (src/eif_tinyllm.c:395-405, 481-507): the per-position cos / sin tables of the model's theta
+ * (freq_j = 1 / theta^(2j/head_dim), the reference's float formula, computed on the host for every position
+ * of the cache) and the pair convention: interleaved = 0 rotates (j, j + head_dim/2) (NeoX, Qwen2),
+ * interleaved != 0 rotates (2j, 2j+1) (llama-style GGUF).  Call once per cache before the rope_append calls. */
+eif_status_t eif_cuda_kv_set_rope(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, float theta, int interleaved);
+
+/* RoPE of the new token's q and k at pos[b], and the cache write of k (rotated) and v at row pos[b]:
+ * tinyllm_forward_embedding_ex's rotation (:481-507) plus its cache write (:415-418), one launch.
+ *   q, q_out [batch][n_heads*head_dim]; k, v [batch][n_kv_heads*head_dim]
+ * _dev: fp32 device arrays, asynchronous.  Host variant: fp32 host arrays. */
+eif_status_t eif_cuda_rope_append(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q, const float *k,
+                                  const float *v, const int *pos, int n_heads, float *q_out);
+eif_status_t eif_cuda_rope_append_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_dev,
+                                      const float *k_dev, const float *v_dev, const int *pos_dev, int n_heads,
+                                      float *q_out_dev);
+
+/* The same for a prefill chunk: token i of every sequence at position start_pos + i (the per-token tables of
+ * the batched prefill, src/eif_tinyllm.c:994-1006).
+ *   q, q_out [batch][n_tok][n_heads*head_dim]; k, v [batch][n_tok][n_kv_heads*head_dim]
+ * _dev: q_out as bf16 (the input of eif_cuda_attend_prefill_dev), the rest fp32 device arrays, asynchronous.
+ * Host variant: fp32 host arrays. */
+eif_status_t eif_cuda_rope_append_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
+                                          const float *k, const float *v, int n_tok, int start_pos, int n_heads,
+                                          float *q_out);
+eif_status_t eif_cuda_rope_append_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_dev,
+                                              const float *k_dev, const float *v_dev, int n_tok, int start_pos,
+                                              int n_heads, void *q_out_dev);
+
 /* ---------------------------------------------------------------------------------------------
  * Decode attention: one new query token per sequence over cache rows [0, pos[b]].
  * Replaces the head loop of fullatt_attend (src/eif_qwen35.c:741-790) and the inline tinyllm decode
