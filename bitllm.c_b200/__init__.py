@@ -7,7 +7,7 @@ The directory name contains a dot, so load it by path (``__graft_entry__.load_pa
     spec = importlib.util.spec_from_file_location(
         "bitllm_c_b200", "bitllm.c_b200/__init__.py", submodule_search_locations=["bitllm.c_b200"])
 """
-from .eif_cuda import (BF16, F32, SUBLN_NONE, SUBLN_RMS, SUBLN_WEIGHT, STATUS, Context, DeltaState,  # noqa: F401
+from .eif_cuda import (BF16, F32, INT8, SUBLN_NONE, SUBLN_RMS, SUBLN_WEIGHT, STATUS, Context, DeltaState,  # noqa: F401
                        EifCudaError, KVCache, device_count, header_functions, lib, LIB_PATH)
 from .build import build  # noqa: F401
 from . import shard  # noqa: F401

@@ -11,8 +11,10 @@
 // (running max m, sum l, o[G][D]) in scratch; attn_decode_combine merges the chunks of a sequence
 // with a log-sum-exp rescale, applies the gate and the SubLN of the whole row and writes out.
 //
-// This file holds the SIMT kernel (fp32 or bf16 cache, fp32 arithmetic): lanes own keys for the
-// scores and own head-dim slices for P.V.  It is the exact-parity path for fp32 caches.
+// This file holds the SIMT kernel (fp32, bf16 or INT8 cache, fp32 arithmetic): lanes own keys for the
+// scores and own head-dim slices for P.V.  It is the exact-parity path for fp32 caches, and the INT8 path
+// (tinyllm kv_type 1, src/eif_tinyllm.c:563-571, 618-625): score = (q . codes) * k_scale * scale, and the
+// key's probability times its v_scale weights the V codes; codes widen to fp32 exactly (i8x4_to_f32).
 #include <math.h>
 
 #include "internal.h"
@@ -27,10 +29,12 @@ template <typename KT, int D, int G>
 __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
     const KT *__restrict__ Kc, const KT *__restrict__ Vc, const float *__restrict__ q, const int *__restrict__ pos,
     int max_seq, int Hkv, int chunk, int nchunk, float scale, float *__restrict__ part_o,
-    float2 *__restrict__ part_ml, unsigned *__restrict__ dev_err) {
+    float2 *__restrict__ part_ml, unsigned *__restrict__ dev_err, const float *__restrict__ k_scale,
+    const float *__restrict__ v_scale) {
     constexpr int DL = D / 32;  // head-dim elements per lane in P.V
     static_assert(D % 32 == 0 && (DL == 2 || DL == 4 || DL == 8), "head_dim 64/128/256");
-    constexpr int KV_VEC = (sizeof(KT) == 4) ? 4 : 8;  // elements per K load
+    constexpr bool kI8 = sizeof(KT) == 1;  // INT8 cache: codes, one K and one V scale per (row, kv head)
+    constexpr int KV_VEC = 16 / (int)sizeof(KT);  // elements per 16-byte K load
 
     const int c = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -72,6 +76,14 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
         float s[G];
 #pragma unroll
         for (int h = 0; h < G; ++h) s[h] = 0.f;
+        float ksc = 1.f, vsc = 1.f;
+        if constexpr (kI8) {
+            if (valid) {
+                const size_t si = ((size_t)b * max_seq + t) * Hkv + kvh;
+                ksc = k_scale[si];
+                vsc = v_scale[si];
+            }
+        }
         if (valid) {
             const KT *kr = Kb + (size_t)t * row_stride;
 #pragma unroll 4
@@ -87,7 +99,8 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
         }
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-            const float sc = valid ? s[h] * scale : -INFINITY;
+            // INT8: (q . codes * k_scale) * scale, the reference's order (src/eif_tinyllm.c:571)
+            const float sc = valid ? (kI8 ? (s[h] * ksc) * scale : s[h] * scale) : -INFINITY;
             const float m_new = fmaxf(m[h], warp_max(sc));
             const float corr = expf(m[h] - m_new);  // 0 on the first block (m = -inf)
             const float pr = valid ? expf(sc - m_new) : 0.f;
@@ -95,7 +108,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
 #pragma unroll
             for (int i = 0; i < DL; ++i) acc[h][i] *= corr;
             m[h] = m_new;
-            s[h] = pr;
+            s[h] = kI8 ? pr * vsc : pr;  // INT8: p * v_scale weights the codes (src/eif_tinyllm.c:622-625)
         }
         const int nvalid = min(32, t_end - t0);
         for (int j = 0; j < nvalid; ++j) {
@@ -267,7 +280,7 @@ cudaError_t launch_simt(cudaStream_t st, const DecodeArgs &a, const Split &sp, f
     dim3 grid(sp.nchunk, a.Hkv, a.B);
     attn_decode_simt_kernel<KT, D, G><<<grid, kDecodeThreads, 0, st>>>(
         static_cast<const KT *>(a.K), static_cast<const KT *>(a.V), a.q, a.pos, a.max_seq, a.Hkv, sp.chunk,
-        sp.nchunk, a.scale, part_o, part_ml, a.dev_err);
+        sp.nchunk, a.scale, part_o, part_ml, a.dev_err, a.k_scale, a.v_scale);
     return cudaGetLastError();
 }
 
@@ -321,6 +334,8 @@ cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws,
         e = launch_attend_decode_tc(st, *a.tmk, *a.tmv, a, sp.nchunk, sp.chunk, part_o, part_ml, sm_count);
     else if (a.dtype == EIF_CUDA_F32)
         e = dispatch_d<float>(st, a, sp, part_o, part_ml, supported);
+    else if (a.dtype == EIF_CUDA_INT8)
+        e = dispatch_d<int8_t>(st, a, sp, part_o, part_ml, supported);
     else
         e = dispatch_d<__nv_bfloat16>(st, a, sp, part_o, part_ml, supported);
     if (!*supported || e != cudaSuccess) return e;

@@ -74,3 +74,75 @@ struct KvLoad<__nv_bfloat16, N> {
         }
     }
 };
+
+// ---- INT8 KV cache (tinyllm kv_type 1) ----
+
+// Four packed int8 values -> fp32, exactly: the byte x + 128 is placed in the low mantissa bits of 2^23
+// (0x4B0000uu == 2^23 + uu), and 2^23 + 128 is subtracted.  One byte permute and one add per value.
+EIF_DEV void i8x4_to_f32(uint32_t w, float *o) {
+    const uint32_t u = w ^ 0x80808080u;
+    o[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)) - 8388736.0f;
+    o[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)) - 8388736.0f;
+    o[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)) - 8388736.0f;
+    o[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)) - 8388736.0f;
+}
+
+template <int N>
+struct KvLoad<int8_t, N> {
+    static EIF_DEV void load(const int8_t *p, float *out) {
+        if constexpr (N == 2) {
+            const uint32_t a = *reinterpret_cast<const uint16_t *>(p);
+            float t[4];
+            i8x4_to_f32(a, t);
+            out[0] = t[0]; out[1] = t[1];
+        } else if constexpr (N == 4) {
+            i8x4_to_f32(*reinterpret_cast<const uint32_t *>(p), out);
+        } else if constexpr (N == 8) {
+            const uint2 a = *reinterpret_cast<const uint2 *>(p);
+            i8x4_to_f32(a.x, out);
+            i8x4_to_f32(a.y, out + 4);
+        } else {
+            static_assert(N == 16, "2, 4, 8 or 16 int8 values");
+            const uint4 a = *reinterpret_cast<const uint4 *>(p);
+            i8x4_to_f32(a.x, out);
+            i8x4_to_f32(a.y, out + 4);
+            i8x4_to_f32(a.z, out + 8);
+            i8x4_to_f32(a.w, out + 12);
+        }
+    }
+};
+
+// Quantise one head of `hd` = 32 * VPL values held by a warp (lane l owns x[l*VPL .. l*VPL+VPL)) the way
+// tinyllm's cache write does (src/eif_tinyllm.c:509-553): amax over the head; scale = amax / 127 and
+// inv = 127 / amax (1 / 127 both when amax < 1e-12); code = trunc(x * inv +- 0.5) clamped to [-128, 127].
+// The reference is built with -ffast-math (CMakeLists.txt:19), under which its compiler turns amax / 127.0f
+// into amax * (1 / 127.0f) and fuses x * inv + 0.5 into one fma; both forms are reproduced here, so codes
+// and scales are bit-identical to the compiled reference.  Writes the lane's VPL codes to dst + l*VPL and,
+// from lane 0, the scale.
+template <int VPL>
+EIF_DEV void quantize_head_warp(const float (&x)[VPL], int8_t *dst, float *scale_out, int lane) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    amax = warp_max(amax);
+    const bool tiny = amax < 1e-12f;
+    const float scale = tiny ? 1.0f : amax * (1.0f / 127.0f);
+    const float inv = __fdiv_rn(127.0f, tiny ? 1.0f : amax);
+    uint32_t packed[(VPL + 3) / 4] = {};
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        int c = __float2int_rz(__fmaf_rn(x[i], inv, x[i] >= 0.f ? 0.5f : -0.5f));
+        c = max(-128, min(127, c));
+        packed[i / 4] |= (uint32_t)(c & 0xff) << (8 * (i % 4));
+    }
+    int8_t *d = dst + lane * VPL;
+    if constexpr (VPL == 2) {
+        *reinterpret_cast<uint16_t *>(d) = (uint16_t)packed[0];
+    } else if constexpr (VPL == 4) {
+        *reinterpret_cast<uint32_t *>(d) = packed[0];
+    } else {
+        static_assert(VPL == 8, "head_dim 64, 128 or 256");
+        *reinterpret_cast<uint2 *>(d) = make_uint2(packed[0], packed[1]);
+    }
+    if (lane == 0) *scale_out = scale;
+}

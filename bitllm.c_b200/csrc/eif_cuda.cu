@@ -257,7 +257,10 @@ EIF_API uint64_t eif_cuda_launch_count(const eif_cuda_ctx_t *ctx) { return ctx ?
 // KV cache
 // =================================================================================================
 
-static size_t dtype_size(eif_cuda_dtype_t t) { return t == EIF_CUDA_BF16 ? 2 : 4; }
+static size_t dtype_size(eif_cuda_dtype_t t) { return t == EIF_CUDA_INT8 ? 1 : t == EIF_CUDA_BF16 ? 2 : 4; }
+
+// Bytes of one layer's K (or V) scale array of an INT8 cache: [batch][max_seq][n_kv] fp32.
+static size_t scale_bytes(const eif_cuda_kv_t *kv) { return (size_t)kv->batch * kv->max_seq * kv->n_kv * 4; }
 
 EIF_API eif_status_t eif_cuda_kv_alloc(eif_cuda_ctx_t *ctx, int n_layers, int batch, int max_seq_len,
                                        int n_kv_heads, int head_dim, eif_cuda_dtype_t dtype, eif_cuda_kv_t **out) {
@@ -265,8 +268,10 @@ EIF_API eif_status_t eif_cuda_kv_alloc(eif_cuda_ctx_t *ctx, int n_layers, int ba
     *out = nullptr;
     if (n_layers <= 0 || batch <= 0 || max_seq_len <= 0 || n_kv_heads <= 0 || head_dim <= 0 || head_dim % 8)
         return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "kv_alloc: bad shape");
-    if (dtype != EIF_CUDA_F32 && dtype != EIF_CUDA_BF16)
-        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "kv_alloc: dtype must be F32 or BF16");
+    if (dtype != EIF_CUDA_F32 && dtype != EIF_CUDA_BF16 && dtype != EIF_CUDA_INT8)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "kv_alloc: dtype must be F32, BF16 or INT8");
+    if (dtype == EIF_CUDA_INT8 && head_dim != 64 && head_dim != 128 && head_dim != 256)
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "kv_alloc: an INT8 cache needs head_dim 64, 128 or 256");
     DeviceGuard g(ctx);
     eif_cuda_kv_t *kv = new eif_cuda_kv_t();
     kv->ctx = ctx;
@@ -284,12 +289,22 @@ EIF_API eif_status_t eif_cuda_kv_alloc(eif_cuda_ctx_t *ctx, int n_layers, int ba
     kv->tm_ready = (bool *)calloc(n_layers, sizeof(bool));
     kv->q_norm = (float **)calloc(n_layers, sizeof(float *));
     kv->k_norm = (float **)calloc(n_layers, sizeof(float *));
+    if (dtype == EIF_CUDA_INT8) {
+        kv->ks = (float **)calloc(n_layers, sizeof(float *));
+        kv->vs = (float **)calloc(n_layers, sizeof(float *));
+    }
     const size_t bytes = kv->layer_elems * dtype_size(dtype);
     for (int l = 0; l < n_layers; ++l) {
         cudaError_t e = cudaMalloc(&kv->k[l], bytes);
         if (e == cudaSuccess) e = cudaMalloc(&kv->v[l], bytes);
         if (e == cudaSuccess) e = cudaMemsetAsync(kv->k[l], 0, bytes, ctx->stream);
         if (e == cudaSuccess) e = cudaMemsetAsync(kv->v[l], 0, bytes, ctx->stream);
+        if (e == cudaSuccess && kv->ks) {
+            e = cudaMalloc(&kv->ks[l], scale_bytes(kv));
+            if (e == cudaSuccess) e = cudaMalloc(&kv->vs[l], scale_bytes(kv));
+            if (e == cudaSuccess) e = cudaMemsetAsync(kv->ks[l], 0, scale_bytes(kv), ctx->stream);
+            if (e == cudaSuccess) e = cudaMemsetAsync(kv->vs[l], 0, scale_bytes(kv), ctx->stream);
+        }
         if (e != cudaSuccess) {
             cudaGetLastError();
             eif_cuda_kv_free(kv);
@@ -315,10 +330,14 @@ EIF_API void eif_cuda_kv_free(eif_cuda_kv_t *kv) {
             if (kv->k && kv->k[l]) cudaFree(kv->k[l]);
             if (kv->v && kv->v[l]) cudaFree(kv->v[l]);
             if (kv->q_norm && kv->q_norm[l]) cudaFree(kv->q_norm[l]);
+            if (kv->ks && kv->ks[l]) cudaFree(kv->ks[l]);
+            if (kv->vs && kv->vs[l]) cudaFree(kv->vs[l]);
         }
     }
     free(kv->k);
     free(kv->v);
+    free(kv->ks);
+    free(kv->vs);
     free(kv->tmk);
     free(kv->tmv);
     free(kv->tm_ready);
@@ -342,6 +361,10 @@ EIF_API eif_status_t eif_cuda_kv_reset(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv) {
     for (int l = 0; l < kv->n_layers; ++l) {
         CK(cudaMemsetAsync(kv->k[l], 0, bytes, ctx->stream));
         CK(cudaMemsetAsync(kv->v[l], 0, bytes, ctx->stream));
+        if (kv->ks) {  // tinyllm_reset zeroes the scales too (src/eif_tinyllm.c:180-187)
+            CK(cudaMemsetAsync(kv->ks[l], 0, scale_bytes(kv), ctx->stream));
+            CK(cudaMemsetAsync(kv->vs[l], 0, scale_bytes(kv), ctx->stream));
+        }
     }
     return wait_stream(ctx);
 }
@@ -379,9 +402,16 @@ EIF_API eif_status_t eif_cuda_kv_upload(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, 
         float *sv = reinterpret_cast<float *>(static_cast<char *>(ctx->stage) + a256(n * 4));
         CK(cudaMemcpyAsync(sk, k_rows, n * 4, cudaMemcpyHostToDevice, ctx->stream));
         CK(cudaMemcpyAsync(sv, v_rows, n * 4, cudaMemcpyHostToDevice, ctx->stream));
-        CK(launch_f32_to_bf16(ctx->stream, sk, static_cast<__nv_bfloat16 *>(kv->k[layer]) + off, n));
-        CK(launch_f32_to_bf16(ctx->stream, sv, static_cast<__nv_bfloat16 *>(kv->v[layer]) + off, n));
-        ctx->launches += 2;
+        if (kv->dtype == EIF_CUDA_INT8) {
+            CK(launch_kv_quantize(ctx->stream, static_cast<int8_t *>(kv->k[layer]), static_cast<int8_t *>(kv->v[layer]),
+                                  kv->ks[layer], kv->vs[layer], nullptr, (size_t)seq * kv->max_seq + row0, sk, sv,
+                                  n_rows, kv->max_seq, kv->n_kv, kv->hd, ctx->dev_err));
+            ctx->launches += 1;
+        } else {
+            CK(launch_f32_to_bf16(ctx->stream, sk, static_cast<__nv_bfloat16 *>(kv->k[layer]) + off, n));
+            CK(launch_f32_to_bf16(ctx->stream, sv, static_cast<__nv_bfloat16 *>(kv->v[layer]) + off, n));
+            ctx->launches += 2;
+        }
     }
     return wait_stream(ctx);
 }
@@ -406,8 +436,16 @@ EIF_API eif_status_t eif_cuda_kv_download(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv
         if (st != EIF_STATUS_OK) return st;
         float *sk = static_cast<float *>(ctx->stage);
         float *sv = reinterpret_cast<float *>(static_cast<char *>(ctx->stage) + a256(n * 4));
-        CK(launch_bf16_to_f32(ctx->stream, static_cast<__nv_bfloat16 *>(kv->k[layer]) + off, sk, n));
-        CK(launch_bf16_to_f32(ctx->stream, static_cast<__nv_bfloat16 *>(kv->v[layer]) + off, sv, n));
+        if (kv->dtype == EIF_CUDA_INT8) {
+            const size_t r0 = (size_t)seq * kv->max_seq + row0;
+            CK(launch_kv_dequantize(ctx->stream, static_cast<int8_t *>(kv->k[layer]), kv->ks[layer], r0, sk, n_rows,
+                                    kv->n_kv, kv->hd));
+            CK(launch_kv_dequantize(ctx->stream, static_cast<int8_t *>(kv->v[layer]), kv->vs[layer], r0, sv, n_rows,
+                                    kv->n_kv, kv->hd));
+        } else {
+            CK(launch_bf16_to_f32(ctx->stream, static_cast<__nv_bfloat16 *>(kv->k[layer]) + off, sk, n));
+            CK(launch_bf16_to_f32(ctx->stream, static_cast<__nv_bfloat16 *>(kv->v[layer]) + off, sv, n));
+        }
         ctx->launches += 2;
         CK(cudaMemcpyAsync(k_rows, sk, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
         CK(cudaMemcpyAsync(v_rows, sv, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
@@ -422,10 +460,43 @@ EIF_API eif_status_t eif_cuda_kv_layer_ptrs(const eif_cuda_kv_t *kv, int layer, 
     return EIF_STATUS_OK;
 }
 
+EIF_API eif_status_t eif_cuda_kv_download_int8(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int seq, int row0,
+                                               int n_rows, int8_t *k_codes, int8_t *v_codes, float *k_scale,
+                                               float *v_scale) {
+    eif_status_t st = kv_rows_check(ctx, kv, layer, seq, row0, n_rows);
+    if (st != EIF_STATUS_OK) return st;
+    if (kv->dtype != EIF_CUDA_INT8) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "kv_download_int8: not an INT8 cache");
+    if (!k_codes || !v_codes || !k_scale || !v_scale)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "kv_download_int8: NULL output");
+    if (n_rows == 0) return EIF_STATUS_OK;
+    DeviceGuard g(ctx);
+    const size_t r0 = (size_t)seq * kv->max_seq + row0;
+    const size_t n = (size_t)n_rows * kv->n_kv * kv->hd, ns = (size_t)n_rows * kv->n_kv;
+    const size_t off = r0 * kv->n_kv * kv->hd, soff = r0 * kv->n_kv;
+    CK(cudaMemcpyAsync(k_codes, static_cast<int8_t *>(kv->k[layer]) + off, n, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaMemcpyAsync(v_codes, static_cast<int8_t *>(kv->v[layer]) + off, n, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaMemcpyAsync(k_scale, kv->ks[layer] + soff, ns * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaMemcpyAsync(v_scale, kv->vs[layer] + soff, ns * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+EIF_API eif_status_t eif_cuda_kv_layer_scales(const eif_cuda_kv_t *kv, int layer, float **k_scale_dev,
+                                              float **v_scale_dev) {
+    if (!kv || layer < 0 || layer >= kv->n_layers || kv->dtype != EIF_CUDA_INT8) return EIF_STATUS_INVALID_ARGUMENT;
+    if (k_scale_dev) *k_scale_dev = kv->ks[layer];
+    if (v_scale_dev) *v_scale_dev = kv->vs[layer];
+    return EIF_STATUS_OK;
+}
+
 static eif_status_t kv_append_impl(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const int *pos_dev,
                                    const float *k_dev, const float *v_dev) {
-    CK(launch_kv_append(ctx->stream, kv->k[layer], kv->v[layer], kv->dtype, pos_dev, k_dev, v_dev, kv->batch,
-                        kv->max_seq, kv->n_kv * kv->hd, ctx->dev_err));
+    if (kv->dtype == EIF_CUDA_INT8)
+        CK(launch_kv_quantize(ctx->stream, static_cast<int8_t *>(kv->k[layer]), static_cast<int8_t *>(kv->v[layer]),
+                              kv->ks[layer], kv->vs[layer], pos_dev, 0, k_dev, v_dev, kv->batch, kv->max_seq,
+                              kv->n_kv, kv->hd, ctx->dev_err));
+    else
+        CK(launch_kv_append(ctx->stream, kv->k[layer], kv->v[layer], kv->dtype, pos_dev, k_dev, v_dev, kv->batch,
+                            kv->max_seq, kv->n_kv * kv->hd, ctx->dev_err));
     ctx->launches += 1;
     return EIF_STATUS_OK;
 }
@@ -486,6 +557,10 @@ void decode_prepare(eif_cuda_kv_t *kv, int layer, DecodeArgs &a) {
             a.tmk = &kv->tmk[layer];
             a.tmv = &kv->tmv[layer];
         }
+    }
+    if (kv->dtype == EIF_CUDA_INT8) {
+        a.k_scale = kv->ks[layer];
+        a.v_scale = kv->vs[layer];
     }
     a.force_simt = env_flag("BITLLM_DECODE_SIMT");
 }
@@ -575,7 +650,9 @@ static eif_status_t prefill_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int la
         return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rows [%d, %d) outside the cache [0, %d)", start_pos,
                     start_pos + n_tok, kv->max_seq);
     if (kv->dtype != EIF_CUDA_BF16 || !prefill_tc_supported(kv->hd))
-        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "prefill attention needs a bf16 cache with head_dim 64, 128 or 256");
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED,
+                    "prefill attention needs a bf16 cache with head_dim 64, 128 or 256 (an INT8 cache is read by "
+                    "the decode attention)");
     if ((size_t)kv->batch * n_tok > 0x7fffffffull) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "too many rows");
     return EIF_STATUS_OK;
 }
@@ -1158,9 +1235,12 @@ EIF_API eif_status_t eif_cuda_kv_set_rope(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv
     const size_t n = (size_t)kv->max_seq * half;
     float *hc = (float *)malloc(2 * n * sizeof(float));
     if (!hc) return fail(ctx, EIF_STATUS_OUT_OF_MEMORY, "rope table");
-    // the reference's per-position table (src/eif_tinyllm.c:399-404), for every position of the cache
+    // the reference's per-position table (src/eif_tinyllm.c:399-404), for every position of the cache.  Its
+    // source reads freq = 1.0f / powf(theta, e); its build (-ffast-math, CMakeLists.txt:19) folds that into
+    // powf(theta, -e), which rounds differently in the last bit for some j, so the folded form is computed
+    // here and the tables equal the compiled reference's bit for bit.
     for (int j = 0; j < half; ++j) {
-        const float freq = 1.0f / powf(theta, (float)(2 * j) / (float)kv->hd);
+        const float freq = powf(theta, -((float)(2 * j) / (float)kv->hd));
         for (int pos = 0; pos < kv->max_seq; ++pos) {
             const float val = (float)pos * freq;
             hc[(size_t)pos * half + j] = cosf(val);
@@ -1189,6 +1269,9 @@ static eif_status_t rope_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer
     if (n_heads <= 0 || n_heads % kv->n_kv)
         return fail(ctx, EIF_STATUS_SHAPE_MISMATCH, "n_heads %d is not a multiple of n_kv_heads %d", n_heads, kv->n_kv);
     if (!kv->tl_cos) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "no RoPE table (eif_cuda_kv_set_rope)");
+    if (kv->dtype == EIF_CUDA_INT8 && (size_t)kv->n_kv * kv->hd * 4 > 48 * 1024)
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "INT8 rope_append: n_kv_heads * head_dim %d above 12288",
+                    kv->n_kv * kv->hd);
     return EIF_STATUS_OK;
 }
 
@@ -1197,6 +1280,10 @@ static eif_status_t rope_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, 
                              __nv_bfloat16 *q_out_bf16) {
     RopeArgs a{q, k, v, kv->tl_cos, kv->tl_sin, pos, kv->k[layer], kv->v[layer], kv->dtype, q_out, q_out_bf16,
                kv->batch, n_tok, start_pos, n_heads, kv->n_kv, kv->hd, kv->max_seq, kv->tl_interleaved, ctx->dev_err};
+    if (kv->dtype == EIF_CUDA_INT8) {
+        a.k_scale = kv->ks[layer];
+        a.v_scale = kv->vs[layer];
+    }
     CK(launch_rope_append(ctx->stream, a));
     ctx->launches += 1;
     return EIF_STATUS_OK;
@@ -1342,6 +1429,8 @@ static eif_status_t prep_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer
         return fail(ctx, EIF_STATUS_SHAPE_MISMATCH, "n_heads %d is not a multiple of n_kv_heads %d", n_heads, kv->n_kv);
     if (!kv->q_norm[layer]) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "layer %d has no q/k norms (kv_set_norms)", layer);
     if (kv->hd > 1024) return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "head_dim %d", kv->hd);
+    if (kv->dtype == EIF_CUDA_INT8)  // Qwen3.5 keeps an fp32 cache (include/eif_qwen35.h:204-208)
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "Qwen3.5 attention prep writes fp32 or bf16 caches, not INT8");
     return EIF_STATUS_OK;
 }
 

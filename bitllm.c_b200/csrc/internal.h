@@ -44,6 +44,8 @@ struct eif_cuda_kv {
     size_t layer_elems = 0;  // batch * max_seq * n_kv * hd
     void **k = nullptr;      // [n_layers] device pointers
     void **v = nullptr;
+    // INT8 caches: per-layer scales [batch][max_seq][n_kv] of K and V (nullptr for the other dtypes)
+    float **ks = nullptr, **vs = nullptr;
     // TMA descriptors of the bf16 layers (64-key x 64-dim boxes, 128-byte swizzle), made on first use
     CUtensorMap *tmk = nullptr;
     CUtensorMap *tmv = nullptr;
@@ -89,6 +91,8 @@ struct DecodeArgs {
     const CUtensorMap *tmv = nullptr;
     bool force_simt = false;
     size_t max_ws_bytes = 0;  // 0: the split may use any amount of scratch; else it must fit in this many bytes
+    const float *k_scale = nullptr;  // INT8 caches: [B][max_seq][Hkv] scales of K and V
+    const float *v_scale = nullptr;
 };
 
 // Fused per-token mixer bodies (mixer_fused.cu).
@@ -128,6 +132,7 @@ struct RopeArgs {
     __nv_bfloat16 *q_out_bf16;
     int B, n_tok, start_pos, nh, nkv, hd, max_seq, interleaved;
     unsigned *dev_err;
+    float *k_scale = nullptr, *v_scale = nullptr;  // INT8 caches: [B][max_seq][nkv]
 };
 cudaError_t launch_rope_append(cudaStream_t st, const RopeArgs &a);
 
@@ -186,5 +191,13 @@ cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws,
 
 cudaError_t launch_kv_append(cudaStream_t st, void *K, void *V, eif_cuda_dtype_t dtype, const int *pos,
                              const float *k, const float *v, int B, int max_seq, int kv_dim, unsigned *dev_err);
+// INT8 caches (kv.cu).  Quantise fp32 rows (k, v: [n_rows][nkv*hd]) into cache rows: row r lands at
+// b * max_seq + pos[b] with b = r when pos is set (one new token per sequence), else at dst_row0 + r.
+cudaError_t launch_kv_quantize(cudaStream_t st, int8_t *K, int8_t *V, float *ks, float *vs, const int *pos,
+                               size_t dst_row0, const float *k, const float *v, int n_rows, int max_seq, int nkv,
+                               int hd, unsigned *dev_err);
+// code * scale of n_rows consecutive cache rows starting at src_row0, into fp32 [n_rows][nkv*hd].
+cudaError_t launch_kv_dequantize(cudaStream_t st, const int8_t *K, const float *ks, size_t src_row0, float *out,
+                                 int n_rows, int nkv, int hd);
 cudaError_t launch_f32_to_bf16(cudaStream_t st, const float *src, __nv_bfloat16 *dst, size_t n);
 cudaError_t launch_bf16_to_f32(cudaStream_t st, const __nv_bfloat16 *src, float *dst, size_t n);

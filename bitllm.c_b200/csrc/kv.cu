@@ -2,7 +2,8 @@
 //
 // kv_append writes the new token's rotated k / v at row pos[b] of every sequence: the memcpy into
 // the cache at src/eif_qwen35.c:734-736 and the direct cache writes of src/eif_tinyllm.c:417-418,
-// for a whole batch in one launch.  A bf16 cache rounds to nearest even.
+// for a whole batch in one launch.  A bf16 cache rounds to nearest even.  An INT8 cache (tinyllm kv_type 1)
+// is written by kv_quantize_kernel: codes and a scale per (row, kv head) as at src/eif_tinyllm.c:509-553.
 #include "internal.h"
 #include "common.cuh"
 
@@ -42,6 +43,49 @@ __global__ void bf16_to_f32_kernel(const __nv_bfloat16 *__restrict__ s, float *_
         d[i] = __bfloat162float(s[i]);
 }
 
+// INT8 cache write: one warp per (row, kv head, K or V), lane l holding values [l*VPL, l*VPL + VPL) of the
+// head; quantize_head_warp makes the codes and the scale.
+template <int VPL>
+__global__ void __launch_bounds__(256) kv_quantize_kernel(int8_t *__restrict__ K, int8_t *__restrict__ V,
+                                                          float *__restrict__ ks, float *__restrict__ vs,
+                                                          const int *__restrict__ pos, size_t dst_row0,
+                                                          const float *__restrict__ k, const float *__restrict__ v,
+                                                          int n_rows, int max_seq, int nkv,
+                                                          unsigned *__restrict__ dev_err) {
+    constexpr int HD = 32 * VPL;
+    const int lane = threadIdx.x & 31;
+    const long item = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= 2L * n_rows * nkv) return;
+    const bool is_v = item & 1;
+    const long rh = item >> 1;
+    const int r = (int)(rh / nkv), h = (int)(rh % nkv);
+    size_t drow;
+    if (pos) {
+        const int p = pos[r];
+        if (p < 0 || p >= max_seq) {
+            if (lane == 0 && h == 0 && !is_v) atomicOr(dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
+            return;
+        }
+        drow = (size_t)r * max_seq + p;
+    } else {
+        drow = dst_row0 + r;
+    }
+    float x[VPL];
+    const float *src = (is_v ? v : k) + ((size_t)r * nkv + h) * HD + lane * VPL;  // caller's rows: no alignment
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) x[i] = src[i];
+    quantize_head_warp<VPL>(x, (is_v ? V : K) + (drow * nkv + h) * HD, (is_v ? vs : ks) + drow * nkv + h, lane);
+}
+
+__global__ void kv_dequantize_kernel(const int8_t *__restrict__ K, const float *__restrict__ ks, size_t src_row0,
+                                     float *__restrict__ out, size_t n, int nkv, int hd) {
+    const size_t base = src_row0 * nkv * hd;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t head = i / hd;  // (row, kv head) of element i, counted from src_row0
+        out[i] = (float)K[base + i] * ks[src_row0 * nkv + head];
+    }
+}
+
 unsigned grid_for(size_t n) {
     size_t g = (n + 255) / 256;
     if (g > 148u * 16u) g = 148u * 16u;
@@ -70,5 +114,37 @@ cudaError_t launch_f32_to_bf16(cudaStream_t st, const float *src, __nv_bfloat16 
 
 cudaError_t launch_bf16_to_f32(cudaStream_t st, const __nv_bfloat16 *src, float *dst, size_t n) {
     bf16_to_f32_kernel<<<grid_for(n), 256, 0, st>>>(src, dst, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_quantize(cudaStream_t st, int8_t *K, int8_t *V, float *ks, float *vs, const int *pos,
+                               size_t dst_row0, const float *k, const float *v, int n_rows, int max_seq, int nkv,
+                               int hd, unsigned *dev_err) {
+    const long warps = 2L * n_rows * nkv;
+    const unsigned grid = (unsigned)((warps + 7) / 8);
+    if (grid == 0) return cudaSuccess;
+    switch (hd) {
+        case 64:
+            kv_quantize_kernel<2><<<grid, 256, 0, st>>>(K, V, ks, vs, pos, dst_row0, k, v, n_rows, max_seq, nkv,
+                                                         dev_err);
+            break;
+        case 128:
+            kv_quantize_kernel<4><<<grid, 256, 0, st>>>(K, V, ks, vs, pos, dst_row0, k, v, n_rows, max_seq, nkv,
+                                                         dev_err);
+            break;
+        case 256:
+            kv_quantize_kernel<8><<<grid, 256, 0, st>>>(K, V, ks, vs, pos, dst_row0, k, v, n_rows, max_seq, nkv,
+                                                         dev_err);
+            break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_dequantize(cudaStream_t st, const int8_t *K, const float *ks, size_t src_row0, float *out,
+                                 int n_rows, int nkv, int hd) {
+    const size_t n = (size_t)n_rows * nkv * hd;
+    if (n == 0) return cudaSuccess;
+    kv_dequantize_kernel<<<grid_for(n), 256, 0, st>>>(K, ks, src_row0, out, n, nkv, hd);
     return cudaGetLastError();
 }

@@ -9,12 +9,23 @@
 //
 // rope_append_kernel: one CTA per token row r = (sequence b, token i): position pos[b] (one token per
 // sequence) or start_pos + i (a chunk); every thread takes (head, pair) items of q and k, then the v row.
+// An INT8 cache stages the rotated k row in shared memory and quantises k and v per head, one warp each.
 #include "internal.h"
 #include "common.cuh"
 
 namespace {
 
+// INT8 cache: one warp quantises one head of hd = 32 * VPL values read from src (shared or global memory).
+template <int VPL>
+__device__ void quantize_from(const float *src, int8_t *dst, float *scale_out, int lane) {
+    float x[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) x[i] = src[lane * VPL + i];
+    quantize_head_warp<VPL>(x, dst, scale_out, lane);
+}
+
 __global__ void __launch_bounds__(256) rope_append_kernel(const RopeArgs a) {
+    extern __shared__ float krot[];  // INT8 caches: the rotated k row [nkv][hd], quantised once complete
     const int r = blockIdx.x, b = r / a.n_tok;
     const int hd = a.hd, half = hd / 2, nh = a.nh, nkv = a.nkv;
     const int p = a.pos ? a.pos[b] : a.start_pos + r % a.n_tok;
@@ -30,7 +41,9 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeArgs a) {
         const float *src = isq ? a.q + ((size_t)r * nh + hi) * hd : a.k + ((size_t)r * nkv + hi) * hd;
         const int ia = a.interleaved ? 2 * j : j, ib = a.interleaved ? 2 * j + 1 : j + half;
         const float x0 = src[ia], x1 = src[ib], c = cs[j], s = sn[j];
-        const float y0 = x0 * c - x1 * s, y1 = x1 * c + x0 * s;
+        // x0 c - x1 s and x1 c + x0 s with the first product fused, as the reference's -mfma build contracts
+        // them: bit-identical rotated rows (and so INT8 scales, which inherit amax's last bit)
+        const float y0 = __fmaf_rn(x0, c, -__fmul_rn(x1, s)), y1 = __fmaf_rn(x1, c, __fmul_rn(x0, s));
         if (isq) {
             const size_t o = ((size_t)r * nh + hi) * hd;
             if (a.q_out_bf16) {
@@ -42,7 +55,10 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeArgs a) {
             }
         } else if (pos_ok) {
             const size_t o = crow + (size_t)hi * hd;
-            if (a.dtype == EIF_CUDA_F32) {
+            if (a.dtype == EIF_CUDA_INT8) {
+                krot[hi * hd + ia] = y0;
+                krot[hi * hd + ib] = y1;
+            } else if (a.dtype == EIF_CUDA_F32) {
                 static_cast<float *>(a.Kc)[o + ia] = y0;
                 static_cast<float *>(a.Kc)[o + ib] = y1;
             } else {
@@ -50,6 +66,26 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeArgs a) {
                 static_cast<__nv_bfloat16 *>(a.Kc)[o + ib] = __float2bfloat16_rn(y1);
             }
         }
+    }
+    if (a.dtype == EIF_CUDA_INT8) {
+        // the quantised write of the rotated k and of v (src/eif_tinyllm.c:509-553): one warp per head
+        __syncthreads();
+        if (!pos_ok) return;
+        const int lane = threadIdx.x & 31;
+        for (int it = threadIdx.x >> 5; it < 2 * nkv; it += blockDim.x >> 5) {
+            const bool is_v = it >= nkv;
+            const int h = is_v ? it - nkv : it;
+            const float *src = is_v ? a.v + ((size_t)r * nkv + h) * hd : krot + h * hd;
+            int8_t *dst = static_cast<int8_t *>(is_v ? a.Vc : a.Kc) + crow + (size_t)h * hd;
+            float *sc = (is_v ? a.v_scale : a.k_scale) + ((size_t)b * a.max_seq + p) * nkv + h;
+            if (hd == 64)
+                quantize_from<2>(src, dst, sc, lane);
+            else if (hd == 128)
+                quantize_from<4>(src, dst, sc, lane);
+            else
+                quantize_from<8>(src, dst, sc, lane);
+        }
+        return;
     }
     if (pos_ok)
         for (int i = threadIdx.x; i < nkv * hd; i += blockDim.x) {
@@ -64,6 +100,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeArgs a) {
 }  // namespace
 
 cudaError_t launch_rope_append(cudaStream_t st, const RopeArgs &a) {
-    rope_append_kernel<<<a.B * a.n_tok, 256, 0, st>>>(a);
+    const size_t smem = a.dtype == EIF_CUDA_INT8 ? (size_t)a.nkv * a.hd * sizeof(float) : 0;
+    rope_append_kernel<<<a.B * a.n_tok, 256, smem, st>>>(a);
     return cudaGetLastError();
 }

@@ -23,7 +23,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "eif_cuda.h")
 # eif_status_t (include/eif_status.h:8-19 of bitllm.c)
 STATUS = {0: "OK", -1: "ERROR", -2: "INVALID_ARGUMENT", -3: "OUT_OF_MEMORY", -4: "NOT_IMPLEMENTED",
           -5: "NOT_SUPPORTED", -6: "TIMEOUT", -7: "INTERNAL_ERROR", -8: "INVALID_LAYER", -9: "SHAPE_MISMATCH"}
-F32, BF16 = 0, 1
+F32, BF16, INT8 = 0, 1, 2
 SUBLN_NONE, SUBLN_RMS, SUBLN_WEIGHT = 0, 1, 2
 
 _P = ctypes.c_void_p
@@ -70,6 +70,8 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_kv_upload": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
         "eif_cuda_kv_download": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
         "eif_cuda_kv_layer_ptrs": (_I, [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
+        "eif_cuda_kv_download_int8": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
+        "eif_cuda_kv_layer_scales": (_I, [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
         "eif_cuda_kv_append": (_I, [_P, _P, _I, _P, _P, _P]),
         "eif_cuda_kv_append_dev": (_I, [_P, _P, _I, _P, _P, _P]),
         "eif_cuda_kv_set_rope": (_I, [_P, _P, _F, _I]),
@@ -250,6 +252,23 @@ class KVCache:
         k, v = _P(), _P()
         self.ctx.check(lib().eif_cuda_kv_layer_ptrs(self._h, layer, ctypes.byref(k), ctypes.byref(v)),
                        "kv_layer_ptrs")
+        return k.value, v.value
+
+    def download_int8(self, layer: int, seq: int, row0: int, n_rows: int):
+        """INT8 caches: (k_codes, v_codes) int8 [n_rows][kv_dim] and (k_scale, v_scale) fp32 [n_rows][n_kv]."""
+        kc = np.zeros((n_rows, self.kv_dim), np.int8)
+        vc = np.zeros((n_rows, self.kv_dim), np.int8)
+        ks = np.zeros((n_rows, self.n_kv_heads), np.float32)
+        vs = np.zeros((n_rows, self.n_kv_heads), np.float32)
+        self.ctx.check(lib().eif_cuda_kv_download_int8(self.ctx.handle, self._h, layer, seq, row0, n_rows, _ptr(kc),
+                                                       _ptr(vc), _ptr(ks), _ptr(vs)), "kv_download_int8")
+        return kc, vc, ks, vs
+
+    def layer_scales(self, layer: int):
+        """INT8 caches: device pointers of the layer's K / V scales [batch][max_seq_len][n_kv_heads] fp32."""
+        k, v = _P(), _P()
+        self.ctx.check(lib().eif_cuda_kv_layer_scales(self._h, layer, ctypes.byref(k), ctypes.byref(v)),
+                       "kv_layer_scales")
         return k.value, v.value
 
     def append(self, layer: int, pos, k, v):

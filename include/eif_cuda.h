@@ -58,7 +58,9 @@ typedef struct eif_cuda_ctx eif_cuda_ctx_t;      /* one device, one stream; not 
 typedef struct eif_cuda_kv eif_cuda_kv_t;        /* device KV cache of n_layers x batch sequences */
 typedef struct eif_cuda_delta eif_cuda_delta_t;  /* device DeltaNet states of n_layers x batch sequences */
 
-typedef enum { EIF_CUDA_F32 = 0, EIF_CUDA_BF16 = 1 } eif_cuda_dtype_t;
+/* KV cache element type.  EIF_CUDA_INT8 is tinyllm's quantised cache (kv_type 1, src/eif_tinyllm.c:136-143):
+ * int8 rows plus one fp32 scale per (row, kv head) for K and one for V; head_dim 64, 128 or 256. */
+typedef enum { EIF_CUDA_F32 = 0, EIF_CUDA_BF16 = 1, EIF_CUDA_INT8 = 2 } eif_cuda_dtype_t;
 
 /* SubLN applied after the attention output gate (src/eif_qwen35.c:779-789). */
 typedef enum {
@@ -108,7 +110,9 @@ void eif_cuda_kv_free(eif_cuda_kv_t *kv);
 eif_status_t eif_cuda_kv_reset(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv);
 
 /* Copy rows [row0, row0+n_rows) of (layer, seq) from / to host fp32 arrays [n_rows][n_kv_heads*head_dim].
- * A bf16 cache converts on the device (round to nearest even) and widens on download. */
+ * A bf16 cache converts on the device (round to nearest even) and widens on download.  An INT8 cache
+ * quantises each (row, kv head) on upload exactly as tinyllm's cache write does (src/eif_tinyllm.c:509-553)
+ * and returns code * scale on download. */
 eif_status_t eif_cuda_kv_upload(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int seq, int row0, int n_rows,
                                 const float *k_rows, const float *v_rows);
 eif_status_t eif_cuda_kv_download(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int seq, int row0,
@@ -116,6 +120,17 @@ eif_status_t eif_cuda_kv_download(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int la
 
 /* Device base pointers of one layer: [batch][max_seq_len][n_kv_heads][head_dim] of the cache dtype. */
 eif_status_t eif_cuda_kv_layer_ptrs(const eif_cuda_kv_t *kv, int layer, void **k_dev, void **v_dev);
+
+/* INT8 caches: the raw codes [n_rows][n_kv_heads*head_dim] and scales [n_rows][n_kv_heads] of rows
+ * [row0, row0+n_rows) of (layer, seq) -- tinyllm_state_t's key_cache_i8 / value_cache_i8 rows and its
+ * key_scale / value_scale entries (include/eif_tinyllm.h:153-157, indexed as src/eif_tinyllm.c:511-520).
+ * EIF_STATUS_INVALID_ARGUMENT for another dtype. */
+eif_status_t eif_cuda_kv_download_int8(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int seq, int row0,
+                                       int n_rows, int8_t *k_codes, int8_t *v_codes, float *k_scale,
+                                       float *v_scale);
+/* Device pointers of one INT8 layer's scales: [batch][max_seq_len][n_kv_heads] fp32. */
+eif_status_t eif_cuda_kv_layer_scales(const eif_cuda_kv_t *kv, int layer, float **k_scale_dev,
+                                      float **v_scale_dev);
 
 /* Append the new token's rotated k / v ([batch][n_kv_heads*head_dim] fp32) at row pos[b] of every
  * sequence -- the memcpy into the cache at src/eif_qwen35.c:734-736 and src/eif_tinyllm.c:417-418. */

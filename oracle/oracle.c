@@ -182,6 +182,77 @@ ORC_EXPORT void orc_attend_decode(const float *q, const float *k_cache, const fl
 }
 
 /*
+ * tinyllm INT8 KV cache write of one row (src/eif_tinyllm.c:509-553): per kv head, amax over the head's
+ * hd values; scale = amax / 127 and inv = 127 / amax (both with amax := 1 when amax < 1e-12);
+ * code = (long)(x * inv + (x >= 0 ? 0.5 : -0.5)) clamped to [-128, 127].
+ *   x       [nkv*hd]   the rotated k (or v) row
+ *   codes   [nkv*hd]   scales [nkv]
+ * The reference is compiled with -O3 -mfma -ffast-math (CMakeLists.txt:19).  Under those flags its
+ * compiler evaluates amax / 127.0f as amax * (1.0f / 127.0f) and contracts x * inv + 0.5 into one fma;
+ * both are written out here so that this restatement gives the compiled reference's bits whatever flags
+ * it is itself built with (pinned by tests/golden/tinyllm_int8_kv.npz).
+ */
+ORC_EXPORT void orc_kv_quantize(const float *x, int nkv, int hd, int8_t *codes, float *scales)
+{
+    for (int h = 0; h < nkv; h++) {
+        const float *xh = x + (size_t)h * hd;
+        float amax = 0.0f;
+        for (int j = 0; j < hd; j++) {
+            const float a = fabsf(xh[j]);
+            if (a > amax) amax = a;
+        }
+        const int tiny = amax < 1e-12f;
+        scales[h] = tiny ? 1.0f : amax * (1.0f / 127.0f);
+        const float inv = 127.0f / (tiny ? 1.0f : amax);
+        for (int j = 0; j < hd; j++) {
+            long qv = (long)fmaf(xh[j], inv, xh[j] >= 0.0f ? 0.5f : -0.5f);
+            if (qv > 127) qv = 127;
+            else if (qv < -128) qv = -128;
+            codes[(size_t)h * hd + j] = (int8_t)qv;
+        }
+    }
+}
+
+/*
+ * tinyllm decode attention over an INT8 cache (src/eif_tinyllm.c:557-571, 615-625), rows [0, pos]:
+ *   score_t = (sum_i q_i * code_k[t][i]) * k_scale[t] * scale
+ *   softmax (src/eif_tinyllm.c:334-352: max-subtract, expf, times 1/sum)
+ *   out_i   = sum_t (att_t * v_scale[t]) * code_v[t][i]
+ *   k_codes / v_codes [>= pos+1][nkv*hd], k_scale / v_scale [>= pos+1][nkv]
+ */
+ORC_EXPORT void orc_attend_decode_i8(const float *q, const int8_t *k_codes, const float *k_scale,
+                                     const int8_t *v_codes, const float *v_scale, int pos, int nh, int nkv, int hd,
+                                     float scale, float *out)
+{
+    const int kv_dim = nkv * hd, group = nh / nkv, n = pos + 1;
+    float *att = (float *)malloc(sizeof(float) * (size_t)n);
+    for (int h = 0; h < nh; h++) {
+        const float *qh = q + (size_t)h * hd;
+        const int kvh = h / group;
+        for (int t = 0; t < n; t++) {
+            const int8_t *kt = k_codes + (size_t)t * kv_dim + (size_t)kvh * hd;
+            float s = 0.0f;
+            for (int i = 0; i < hd; i++) s += qh[i] * (float)kt[i];
+            att[t] = (s * k_scale[(size_t)t * nkv + kvh]) * scale;
+        }
+        float mx = att[0];
+        for (int t = 1; t < n; t++) if (att[t] > mx) mx = att[t];
+        float sum = 0.0f;
+        for (int t = 0; t < n; t++) { att[t] = expf(att[t] - mx); sum += att[t]; }
+        const float inv_sum = 1.0f / sum;
+        for (int t = 0; t < n; t++) att[t] *= inv_sum;
+        float *oh = out + (size_t)h * hd;
+        for (int i = 0; i < hd; i++) oh[i] = 0.0f;
+        for (int t = 0; t < n; t++) {
+            const int8_t *vt = v_codes + (size_t)t * kv_dim + (size_t)kvh * hd;
+            const float a = att[t] * v_scale[(size_t)t * nkv + kvh];
+            for (int i = 0; i < hd; i++) oh[i] += a * (float)vt[i];
+        }
+    }
+    free(att);
+}
+
+/*
  * SubLN before o_proj (src/eif_qwen35.c:779-789): mode 2 = rsqrt(mean+1e-6) * sub_norm,
  * mode 1 = rsqrt only (!plain_linear, no sub_norm), mode 0 = copy.  In place over [n].
  */
@@ -246,6 +317,9 @@ ORC_EXPORT void orc_attend_prefill(const float *q, const float *k_cache, const f
 ORC_EXPORT void orc_rope_table(int pos, int hd, float theta, float *cos_out, float *sin_out)
 {
     for (int j = 0; j < hd / 2; j++) {
+        /* the reference's expression as written; this file is compiled with the reference's own flags
+         * (oracle/Makefile), so the compiler rewrites it the same way (under -ffast-math the result equals
+         * powf(theta, -e) from libm, which is what the device tables use; pinned by tests/golden/tinyllm_*) */
         const float freq = 1.0f / powf(theta, (float)(2 * j) / (float)hd);
         const float val = (float)pos * freq;
         cos_out[j] = cosf(val);
@@ -267,8 +341,10 @@ ORC_EXPORT void orc_rope_apply(float *x, int n_heads, int hd, const float *c, co
             const int ia = interleaved ? 2 * j : j;
             const int ib = interleaved ? 2 * j + 1 : j + half;
             const float x0 = xh[ia], x1 = xh[ib];
-            xh[ia] = x0 * c[j] - x1 * s[j];
-            xh[ib] = x1 * c[j] + x0 * s[j];
+            /* x0 c - x1 s, x1 c + x0 s with the first product fused, as the reference's -mfma build contracts
+             * them (bit-identical to its rotated rows, tests/golden/tinyllm_*.npz) */
+            xh[ia] = fmaf(x0, c[j], -(x1 * s[j]));
+            xh[ib] = fmaf(x1, c[j], x0 * s[j]);
         }
     }
 }

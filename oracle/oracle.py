@@ -21,6 +21,7 @@ PORT_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libbitllm_ref.so")
 
 _F = ctypes.POINTER(ctypes.c_float)
+_I8 = ctypes.POINTER(ctypes.c_int8)
 _port = None
 _ref = None
 
@@ -58,6 +59,8 @@ def port():
         _port.orc_rope_partial.argtypes = [_F, i, i, i]
         _port.orc_fullatt_prep.argtypes = [_F, _F, _F, _F, _F, _F, _F, _F, _F, i, i, i, i]
         _port.orc_round_bf16.argtypes = [_F, ctypes.c_size_t]
+        _port.orc_kv_quantize.argtypes = [_F, i, i, _I8, _F]
+        _port.orc_attend_decode_i8.argtypes = [_F, _I8, _F, _I8, _F, i, i, i, i, f, _F]
     return _port
 
 
@@ -77,6 +80,9 @@ def ref():
         _ref.ref_fullatt_prep.argtypes = [_F, _F, _F, _F, _F, _F, _F, _F, _F, i, i, i, i]
         _ref.ref_fullatt_attend.argtypes = [_F, _F, _F, _F, _F, _F, i, i, i, i, i]
         _ref.ref_omp_threads.restype = i
+        _ref.ref_tinyllm_decode_steps.argtypes = [i, i, i, i, ctypes.c_float, i, i, i, _F, _F, _F, _F, _F, _F,
+                                                  _I8, _I8, _F, _F, _F]
+        _ref.ref_tinyllm_decode_steps.restype = i
         _ref.ref_set_threads.argtypes = [i]
     return _ref
 
@@ -176,6 +182,49 @@ def ref_fullatt_attend(q, gate, k_cache, v_cache, sub_norm, plain_linear, pos, n
     ref().ref_fullatt_attend(_fp(c32(q)), _fp(c32(gate)), _fp(o), _fp(k_cache), _fp(v_cache),
                              _fp(c32(sub_norm)) if sub_norm is not None else None, int(plain_linear), int(pos),
                              nh, nkv, hd)
+    return o
+
+
+def _i8p(a):
+    assert a.dtype == np.int8 and a.flags["C_CONTIGUOUS"], "oracle code buffers are contiguous int8"
+    return a.ctypes.data_as(_I8)
+
+
+def kv_quantize(x, nkv, hd):
+    """tinyllm INT8 cache write of rows x [..., nkv*hd]: returns (codes int8 [..., nkv*hd], scales [..., nkv])."""
+    x = c32(x)
+    rows = x.reshape(-1, nkv * hd)
+    codes = np.zeros(rows.shape, np.int8)
+    scales = np.zeros((rows.shape[0], nkv), np.float32)
+    for r in range(rows.shape[0]):
+        port().orc_kv_quantize(_fp(c32(rows[r])), nkv, hd, _i8p(codes[r]), _fp(scales[r]))
+    return codes.reshape(x.shape), scales.reshape(x.shape[:-1] + (nkv,))
+
+
+def attend_decode_i8(q, k_codes, k_scale, v_codes, v_scale, pos, nh, nkv, hd, scale):
+    """tinyllm decode attention of one token over INT8 cache rows [0, pos]."""
+    out = np.zeros(nh * hd, np.float32)
+    port().orc_attend_decode_i8(_fp(c32(q)), _i8p(np.ascontiguousarray(k_codes, np.int8)), _fp(c32(k_scale)),
+                                _i8p(np.ascontiguousarray(v_codes, np.int8)), _fp(c32(v_scale)), int(pos), nh, nkv,
+                                hd, float(scale), _fp(out))
+    return out
+
+
+def ref_tinyllm_decode_steps(q, k, v, nh, nkv, hd, seq_len, theta, interleaved, kv_type):
+    """The reference's own tinyllm forward over len(q) decode steps (oracle/ref_shim.c); needs oracle/_ref.
+
+    Returns a dict of per-step arrays: q_rot, k_row, v_row, (INT8) k_codes, v_codes, k_scale, v_scale, attn."""
+    n = q.shape[0]
+    o = dict(q_rot=np.zeros((n, nh * hd), np.float32), k_row=np.zeros((n, nkv * hd), np.float32),
+             v_row=np.zeros((n, nkv * hd), np.float32), k_codes=np.zeros((n, nkv * hd), np.int8),
+             v_codes=np.zeros((n, nkv * hd), np.int8), k_scale=np.zeros((n, nkv), np.float32),
+             v_scale=np.zeros((n, nkv), np.float32), attn=np.zeros((n, nh * hd), np.float32))
+    rc = ref().ref_tinyllm_decode_steps(nh, nkv, hd, seq_len, float(theta), int(interleaved), int(kv_type), n,
+                                        _fp(c32(q)), _fp(c32(k)), _fp(c32(v)), _fp(o["q_rot"]), _fp(o["k_row"]),
+                                        _fp(o["v_row"]), _i8p(o["k_codes"]), _i8p(o["v_codes"]), _fp(o["k_scale"]),
+                                        _fp(o["v_scale"]), _fp(o["attn"]))
+    if rc != 0:
+        raise RuntimeError("the reference rejected the tinyllm configuration")
     return o
 
 

@@ -18,6 +18,12 @@ reference without the reference being present.
                         applied by the tinyllm restatement before the cache is filled
   prefill_small.npz     fullatt_attend per token with the causal bound pos = start_pos + i, which is
                         what tinyllm_forward_batch_embeddings (src/eif_tinyllm.c:1158-1268) computes
+  tinyllm_*.npz         tinyllm_forward_embedding_ex (src/eif_tinyllm.c:371-857) over consecutive decode
+                        steps of a one-layer model whose attention is observable (oracle/ref_shim.c,
+                        ref_tinyllm_decode_steps): RoPE (:481-507), the cache write -- fp32, or INT8 codes
+                        and scales (:509-553) -- and the attention output (:555-656)
+
+    python tests/golden/gen_golden.py [fixture-name ...]   # default: every fixture
 """
 from __future__ import annotations
 
@@ -117,14 +123,63 @@ def gen_prefill_small(seed, nh, nkv, hd, n_tok, start_pos):
              meta=np.array([nh, nkv, hd, n_tok, start_pos], np.int32))
 
 
+def gen_tinyllm(name, seed, nh, nkv, hd, n_steps, theta, interleaved, kv_type, check_steps):
+    """Decode steps 0..n_steps-1 through the reference's tinyllm forward.  k rows span two decades of
+    scale; for the INT8 cache, k row 5 is zero (amax 0 -> scale 1), v row 9's first head is below the
+    1e-12 floor, and v rows 20-23 sit next to rounding boundaries of code = trunc(x * inv +- 0.5)."""
+    rng = np.random.default_rng(seed)
+    kv_dim = nkv * hd
+    q = rng.standard_normal((n_steps, nh * hd)).astype(np.float32)
+    k = (rng.standard_normal((n_steps, kv_dim)) * rng.uniform(0.1, 10.0, (n_steps, 1))).astype(np.float32)
+    v = (rng.standard_normal((n_steps, kv_dim)) * rng.uniform(0.3, 3.0, (n_steps, 1))).astype(np.float32)
+    if kv_type == 1:
+        k[5] = 0.0
+        v[9, :hd] = 1e-13
+        inv = np.float32(127) / np.float32(100)
+        for t in range(20, 24):
+            m = rng.integers(-127, 127, kv_dim)
+            base = ((m + 0.5) / np.float64(inv)).astype(np.float32)
+            step = rng.integers(-1, 2, kv_dim)
+            row = np.where(step == 0, base, np.nextafter(base, np.where(step > 0, np.inf, -np.inf).astype(np.float32)))
+            row = np.clip(row, -100.0, 100.0).astype(np.float32)
+            row[::hd] = 100.0  # amax of every head: inv = 127 / 100, inexact
+            v[t] = row
+    o = orc.ref_tinyllm_decode_steps(q, k, v, nh, nkv, hd, n_steps, theta, interleaved, kv_type)
+    steps = np.array(check_steps, np.int32)
+    extra = dict(k_codes=o["k_codes"], v_codes=o["v_codes"], k_scale=o["k_scale"], v_scale=o["v_scale"]) \
+        if kv_type == 1 else {}
+    np.savez(os.path.join(HERE, name), q=q, k=k, v=v, steps=steps, q_rot=o["q_rot"][steps], attn=o["attn"][steps],
+             k_row=o["k_row"], v_row=o["v_row"], theta=np.float32(theta),
+             meta=np.array([nh, nkv, hd, n_steps, interleaved, kv_type], np.int32), **extra)
+
+
+FIXTURES = {
+    "deltanet_core_h2d128.npz": lambda: gen_deltanet_core("deltanet_core_h2d128.npz", 1001, H=2, dk=128, dv=128,
+                                                          conv_k=4, n_steps=6),
+    "deltanet_core_h3d64.npz": lambda: gen_deltanet_core("deltanet_core_h3d64.npz", 1002, H=3, dk=64, dv=64,
+                                                         conv_k=4, n_steps=5),
+    "fullatt_prep.npz": lambda: gen_fullatt_prep(1003, nh=8, nkv=2, hd=256, max_seq=16, pos=11),
+    "fullatt_attend.npz": lambda: gen_fullatt_attend(1004, nh=8, nkv=2, hd=256, n_rows=40, pos=37),
+    "decode_cfg1.npz": lambda: gen_decode_cfg1(1005),
+    "prefill_small.npz": lambda: gen_prefill_small(1006, nh=6, nkv=2, hd=64, n_tok=24, start_pos=8),
+    # BASELINE config 1's heads (14 / 2, hd 64, NeoX theta 1e6), fp32 cache, past the reference's
+    # OpenMP threshold pos >= 64 (src/eif_tinyllm.c:557)
+    "tinyllm_f32_cfg1.npz": lambda: gen_tinyllm("tinyllm_f32_cfg1.npz", 1007, 14, 2, 64, 72, 1e6, 0, 0,
+                                                [0, 1, 2, 31, 63, 64, 65, 71]),
+    "tinyllm_int8_hd64.npz": lambda: gen_tinyllm("tinyllm_int8_hd64.npz", 1008, 4, 2, 64, 72, 1e6, 0, 1,
+                                                 [0, 1, 5, 9, 23, 63, 64, 71]),
+    "tinyllm_int8_hd128.npz": lambda: gen_tinyllm("tinyllm_int8_hd128.npz", 1009, 4, 1, 128, 40, 1e4, 1, 1,
+                                                  [0, 1, 5, 9, 22, 39]),
+    "tinyllm_int8_hd256.npz": lambda: gen_tinyllm("tinyllm_int8_hd256.npz", 1010, 2, 1, 256, 24, 5e5, 0, 1,
+                                                  [0, 3, 9, 21, 23]),
+}
+
+
 def main():
     orc.build(ref=True)
-    gen_deltanet_core("deltanet_core_h2d128.npz", 1001, H=2, dk=128, dv=128, conv_k=4, n_steps=6)
-    gen_deltanet_core("deltanet_core_h3d64.npz", 1002, H=3, dk=64, dv=64, conv_k=4, n_steps=5)
-    gen_fullatt_prep(1003, nh=8, nkv=2, hd=256, max_seq=16, pos=11)
-    gen_fullatt_attend(1004, nh=8, nkv=2, hd=256, n_rows=40, pos=37)
-    gen_decode_cfg1(1005)
-    gen_prefill_small(1006, nh=6, nkv=2, hd=64, n_tok=24, start_pos=8)
+    names = sys.argv[1:] or list(FIXTURES)
+    for n in names:
+        FIXTURES[n]()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f"{f:32s} {os.path.getsize(os.path.join(HERE, f)):>9d} B")

@@ -1,0 +1,120 @@
+"""tinyllm's INT8 KV cache on the device (EIF_CUDA_INT8): the quantised cache write (src/eif_tinyllm.c:509-553)
+through kv_upload / kv_append / rope_append, and the decode attention over codes and scales (:555-571, 615-625),
+through the C ABI.  Codes and scales: bit-exact against the reference's own forward (tests/golden/tinyllm_int8_*)
+and the C restatement; attention: rel-L2 <= 1e-5 (the fp32 decode tolerance)."""
+import numpy as np
+import pytest
+
+from conftest import golden, rel_l2
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def bits_equal(a, b):
+    return np.array_equal(np.asarray(a, np.float32).view(np.uint32), np.asarray(b, np.float32).view(np.uint32))
+
+
+@pytest.mark.parametrize("name", ["tinyllm_int8_hd64.npz", "tinyllm_int8_hd128.npz", "tinyllm_int8_hd256.npz"])
+def test_decode_chain_vs_reference(pkg, ctx, name):
+    """Every decode step of the reference's tinyllm forward: rope_append into the INT8 cache, attend_decode;
+    codes and scales of every row bit-exact, the attention of the recorded steps within 1e-5."""
+    d = golden(name)
+    nh, nkv, hd, n, inter, _ = (int(x) for x in d["meta"])
+    kv = pkg.KVCache(ctx, 1, 1, n, nkv, hd, pkg.INT8)
+    kv.set_rope(float(d["theta"]), bool(inter))
+    steps = list(d["steps"])
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(hd)))
+    for t in range(n):
+        pos = np.array([t], np.int32)
+        qr = kv.rope_append(0, d["q"][t][None], d["k"][t][None], d["v"][t][None], pos, nh)
+        if t in steps:
+            i = steps.index(t)
+            assert np.array_equal(qr[0], d["q_rot"][i]), t  # the reference's tables and rounding
+            out = kv.attend_decode(0, qr, pos, nh, scale)
+            assert rel_l2(out[0], d["attn"][i]) <= TOL, t
+    kc, vc, ks, vs = kv.download_int8(0, 0, 0, n)
+    assert np.array_equal(kc, d["k_codes"]) and np.array_equal(vc, d["v_codes"])
+    assert bits_equal(ks, d["k_scale"]) and bits_equal(vs, d["v_scale"])
+
+
+def test_upload_and_download(pkg, ctx, orc):
+    """kv_upload quantises each (row, kv head); kv_download returns code * scale; reset zeroes codes and scales."""
+    rng = np.random.default_rng(3)
+    nkv, hd, T = 3, 128, 40
+    kv = pkg.KVCache(ctx, 2, 2, T, nkv, hd, pkg.INT8)
+    k = (rng.standard_normal((T, nkv * hd)) * rng.uniform(0.01, 50, (T, 1))).astype(np.float32)
+    v = rng.standard_normal((T, nkv * hd)).astype(np.float32)
+    k[3] = 0.0
+    v[4, hd:2 * hd] = 1e-13
+    kv.upload(1, 1, 0, k, v)
+    kc, vc, ks, vs = kv.download_int8(1, 1, 0, T)
+    rk, rks = orc.kv_quantize(k, nkv, hd)
+    rv, rvs = orc.kv_quantize(v, nkv, hd)
+    assert np.array_equal(kc, rk) and np.array_equal(vc, rv) and bits_equal(ks, rks) and bits_equal(vs, rvs)
+    kd, vd = kv.download(1, 1, 0, T)
+    want = (rk.reshape(T, nkv, hd).astype(np.float32) * rks[:, :, None]).reshape(T, -1)
+    assert np.array_equal(kd, want)
+    # other (layer, sequence) slots untouched
+    kc0, _, ks0, _ = kv.download_int8(0, 1, 0, T)
+    assert not kc0.any() and not ks0.any()
+    kv.reset()
+    kc, vc, ks, vs = kv.download_int8(1, 1, 0, T)
+    assert not kc.any() and not vc.any() and not ks.any() and not vs.any()
+
+
+def test_append_batch(pkg, ctx, orc):
+    """kv_append of one token per sequence at different positions."""
+    rng = np.random.default_rng(4)
+    B, nkv, hd, T = 5, 2, 256, 33
+    kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, pkg.INT8)
+    pos = np.array([0, 7, 32, 1, 16], np.int32)
+    k = rng.standard_normal((B, nkv * hd)).astype(np.float32) * 3
+    v = rng.standard_normal((B, nkv * hd)).astype(np.float32)
+    kv.append(0, pos, k, v)
+    rk, rks = orc.kv_quantize(k, nkv, hd)
+    rv, rvs = orc.kv_quantize(v, nkv, hd)
+    for b in range(B):
+        kc, vc, ks, vs = kv.download_int8(0, b, int(pos[b]), 1)
+        assert np.array_equal(kc[0], rk[b]) and np.array_equal(vc[0], rv[b])
+        assert bits_equal(ks[0], rks[b]) and bits_equal(vs[0], rvs[b])
+
+
+@pytest.mark.parametrize("nh,nkv,hd,T", [(14, 2, 64, 700), (8, 2, 128, 1500), (8, 1, 256, 300), (6, 6, 64, 129),
+                                         (16, 2, 128, 64)])
+def test_decode_vs_oracle(pkg, ctx, orc, nh, nkv, hd, T):
+    """attend_decode over an uploaded INT8 cache, a batch of sequences at different positions (split-K chunks,
+    groups 1..8), against the restatement's INT8 attention on the same codes."""
+    rng = np.random.default_rng(nh * 1000 + hd + T)
+    B = 3
+    kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, pkg.INT8)
+    pos = np.array([T - 1, T // 2, 0], np.int32)
+    codes = []
+    for b in range(B):
+        k = (rng.standard_normal((T, nkv * hd)) * rng.uniform(0.2, 4, (T, 1))).astype(np.float32)
+        v = rng.standard_normal((T, nkv * hd)).astype(np.float32)
+        kv.upload(0, b, 0, k, v)
+        codes.append(kv.download_int8(0, b, 0, T))
+    q = rng.standard_normal((B, nh * hd)).astype(np.float32)
+    scale = 1.0 / np.sqrt(hd)
+    out = kv.attend_decode(0, q, pos, nh, scale)
+    for b in range(B):
+        kc, vc, ks, vs = codes[b]
+        ref = orc.attend_decode_i8(q[b], kc, ks, vc, vs, int(pos[b]), nh, nkv, hd, scale)
+        assert rel_l2(out[b], ref) <= TOL, b
+
+
+def test_int8_rejections(pkg, ctx):
+    """INT8 caches: head_dim 64/128/256 only; no prefill attention or Qwen3.5 prep over them; the raw download
+    needs an INT8 cache."""
+    with pytest.raises(pkg.EifCudaError) as e:
+        pkg.KVCache(ctx, 1, 1, 8, 2, 96, pkg.INT8)
+    assert e.value.name == "NOT_SUPPORTED"
+    kv = pkg.KVCache(ctx, 1, 1, 64, 2, 64, pkg.INT8)
+    with pytest.raises(pkg.EifCudaError) as e:
+        kv.attend_prefill(0, np.zeros((1, 8, 4 * 64), np.float32), 8, 0, 4, 0.125)
+    assert e.value.name == "NOT_SUPPORTED"
+    f32 = pkg.KVCache(ctx, 1, 1, 8, 2, 64, pkg.F32)
+    with pytest.raises(pkg.EifCudaError) as e:
+        f32.download_int8(0, 0, 0, 1)
+    assert e.value.name == "INVALID_ARGUMENT"

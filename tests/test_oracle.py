@@ -105,3 +105,77 @@ def test_port_vs_reference_attend_random(orc):
         o = orc.attend_decode(q, kc, vc, T - 1, nh, nkv, hd, scale, gate=gate)
         r = orc.ref_fullatt_attend(q, gate, kc, vc, None, 1, T - 1, nh, nkv, hd)
         assert rel_l2(o, r) < 1e-6
+
+
+TINYLLM = ["tinyllm_f32_cfg1.npz", "tinyllm_int8_hd64.npz", "tinyllm_int8_hd128.npz", "tinyllm_int8_hd256.npz"]
+
+
+@pytest.mark.parametrize("name", TINYLLM)
+def test_tinyllm_golden(orc, name):
+    """tinyllm's own forward (src/eif_tinyllm.c:371-857) over decode steps: RoPE, the fp32 or INT8 cache write
+    and the attention output, against the restatement.  INT8 codes and scales are bit-exact."""
+    d = golden(name)
+    nh, nkv, hd, n, inter, kv_type = (int(x) for x in d["meta"])
+    theta = float(d["theta"])
+    scale = np.float32(1.0) / np.sqrt(np.float32(hd))
+    k_rot = np.stack([orc.rope_apply(d["k"][t], nkv, hd, t, theta, inter) for t in range(n)])
+    for i, t in enumerate(d["steps"]):  # RoPE tables and rotation bit-identical to the compiled reference
+        assert np.array_equal(orc.rope_apply(d["q"][t], nh, hd, t, theta, inter), d["q_rot"][i]), t
+    if kv_type == 0:
+        assert np.array_equal(k_rot, d["k_row"]) and np.array_equal(d["v_row"], d["v"])
+        for i, t in enumerate(d["steps"]):
+            o = orc.attend_decode(d["q_rot"][i], d["k_row"][:t + 1], d["v_row"][:t + 1], t, nh, nkv, hd, scale)
+            assert rel_l2(o, d["attn"][i]) <= 1e-6, t
+        return
+    # the fp32 row of step 0 is overwritten by the reference's INT8 rows (they alias one buffer,
+    # src/eif_tinyllm.c:136-138); rows >= 1 are intact when read right after their step
+    assert np.array_equal(k_rot[1:], d["k_row"][1:]) and np.array_equal(d["v_row"][1:], d["v"][1:])
+    kc, ks = orc.kv_quantize(np.concatenate([k_rot[:1], d["k_row"][1:]]), nkv, hd)
+    vc, vs = orc.kv_quantize(d["v"], nkv, hd)
+    assert np.array_equal(kc, d["k_codes"]) and np.array_equal(vc, d["v_codes"])
+    assert np.array_equal(ks.view(np.uint32), d["k_scale"].view(np.uint32))
+    assert np.array_equal(vs.view(np.uint32), d["v_scale"].view(np.uint32))
+    for i, t in enumerate(d["steps"]):
+        o = orc.attend_decode_i8(d["q_rot"][i], d["k_codes"][:t + 1], d["k_scale"][:t + 1], d["v_codes"][:t + 1],
+                                 d["v_scale"][:t + 1], t, nh, nkv, hd, scale)
+        assert rel_l2(o, d["attn"][i]) <= 1e-6, t
+
+
+def test_int8_quantize_edges(orc):
+    """The quantiser's edge rows: all zero (amax 0 -> scale 1, codes 0), below the 1e-12 floor, a head whose
+    amax sits at the clamp (+-127 reached, -128 never produced by the symmetric scale), and sign handling."""
+    hd = 64
+    x = np.zeros((4, 2 * hd), np.float32)
+    x[1, :hd] = 5e-13
+    x[1, hd:] = -5e-13
+    x[2, :hd] = np.linspace(-3.0, 3.0, hd, dtype=np.float32)
+    x[3, :hd] = -1.0
+    x[3, hd:] = 0.25
+    c, s = orc.kv_quantize(x, 2, hd)
+    assert np.all(c[0] == 0) and np.all(s[0] == 1.0)
+    assert np.all(c[1] == 0) and np.all(s[1] == 1.0)
+    assert c[2, 0] == -127 and c[2, hd - 1] == 127 and np.isclose(s[2, 0], 3.0 / 127)
+    assert np.all(c[3, :hd] == -127) and np.all(c[3, hd:] == 127)
+    assert s[2, 1] == 1.0 and np.all(c[2, hd:] == 0)
+
+
+def test_rope_table_folded_form(orc):
+    """The device tables (eif_cuda_kv_set_rope) compute freq = powf(theta, -2j/hd) with libm, the form the
+    reference's -ffast-math build gives its 1.0f / powf(theta, 2j/hd); check that form against the
+    restatement compiled with the reference's flags, over the thetas and head sizes of the tinyllm models."""
+    import ctypes
+    libm = ctypes.CDLL("libm.so.6")
+    for fn in ("powf", "cosf", "sinf"):
+        getattr(libm, fn).restype = ctypes.c_float
+    libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+    libm.cosf.argtypes = [ctypes.c_float]
+    libm.sinf.argtypes = [ctypes.c_float]
+    f32 = np.float32
+    for theta in (1e4, 1e5, 5e5, 1e6, 5e6):
+        for hd in (64, 128, 256):
+            freq = [f32(libm.powf(f32(theta), -(f32(2 * j) / f32(hd)))) for j in range(hd // 2)]
+            for pos in range(0, 4096, 251):
+                c, s = orc.rope_table(pos, hd, theta)
+                vals = [f32(pos) * f for f in freq]
+                assert np.array_equal(c, np.array([libm.cosf(v) for v in vals], f32)), (theta, hd, pos)
+                assert np.array_equal(s, np.array([libm.sinf(v) for v in vals], f32)), (theta, hd, pos)

@@ -97,3 +97,23 @@ def test_rope_needs_table(pkg, ctx):
         kv.rope_append(0, np.zeros((1, 128), np.float32), np.zeros((1, 128), np.float32),
                        np.zeros((1, 128), np.float32), np.array([0]), 2)
     assert e.value.name == "INVALID_ARGUMENT"
+
+
+def test_tinyllm_decode_vs_reference(pkg, ctx):
+    """The reference's own tinyllm forward (tests/golden/tinyllm_f32_cfg1.npz: BASELINE config 1's heads, fp32
+    cache, 72 steps past its OpenMP threshold): rope_append + attend_decode per step, rel-L2 <= 1e-5."""
+    from conftest import golden
+    d = golden("tinyllm_f32_cfg1.npz")
+    nh, nkv, hd, n, inter, _ = (int(x) for x in d["meta"])
+    kv = pkg.KVCache(ctx, 1, 1, n, nkv, hd, pkg.F32)
+    kv.set_rope(float(d["theta"]), bool(inter))
+    steps = list(d["steps"])
+    for t in range(n):
+        pos = np.array([t], np.int32)
+        qr = kv.rope_append(0, d["q"][t][None], d["k"][t][None], d["v"][t][None], pos, nh)
+        if t in steps:
+            i = steps.index(t)
+            assert np.array_equal(qr[0], d["q_rot"][i])  # the reference's tables and rounding, bit for bit
+            assert rel_l2(kv.attend_decode(0, qr, pos, nh, 0.125)[0], d["attn"][i]) <= TOL, t
+    kd, vd = kv.download(0, 0, 0, n)
+    assert np.array_equal(kd, d["k_row"]) and np.array_equal(vd, d["v_row"])
