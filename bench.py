@@ -752,10 +752,199 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
     return line
 
 
+DC_HQ, DC_HKV, DC_D, DC_THETA = 14, 2, 64, 1e6  # BASELINE configs[0]'s heads (Qwen2.5-0.5B), NeoX RoPE
+DC_B, DC_CTX = 256, 4096  # the batched variant; configs[0] itself is --batch 1 --ctx 512 --kv f32
+KV_ELT = {"f32": 4, "bf16": 2, "int8": 1}
+
+
+def decode_bytes(B, L, hkv, kv):
+    """Algorithmic bytes of one decode-attention launch: K and V rows [0, L) of every (sequence, kv head),
+    plus the per-(row, kv head) K and V scales of an INT8 cache (q and out are < 0.1 %)."""
+    b = 2.0 * B * hkv * L * DC_D * KV_ELT[kv]
+    if kv == "int8":
+        b += 2.0 * B * hkv * L * 4
+    return b
+
+
+def cpu_decode_reference(kv_name, L, seconds=10.0):
+    """The reference's decode attention of one token at pos L-1, one sequence per host thread for the time
+    budget: fp32 / bf16 caches -> the reference's fullatt_attend on fp32 rows (gate +100 -> sigmoid 1, plain:
+    the tinyllm GQA core, src/eif_tinyllm.c:557-656 computes the same); INT8 -> the restatement of the
+    tinyllm INT8 loop (src/eif_tinyllm.c:563-571, 618-625; the reference has it inline only).  RoPE and the
+    cache write are not timed (O(D) next to O(L D))."""
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as orc
+    ncpu = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(8)
+    kv_dim = DC_HKV * DC_D
+    q = rng.standard_normal(DC_HQ * DC_D).astype(np.float32)
+    gate = np.full(DC_HQ * DC_D, 100.0, np.float32)
+    if kv_name == "int8":
+        kind = "port"
+        kc = rng.integers(-127, 128, (L, kv_dim)).astype(np.int8)
+        vc = rng.integers(-127, 128, (L, kv_dim)).astype(np.int8)
+        ks = rng.uniform(0.005, 0.03, (L, DC_HKV)).astype(np.float32)
+        vs = rng.uniform(0.005, 0.03, (L, DC_HKV)).astype(np.float32)
+    else:
+        kind = "reference" if orc.ref_available() else "port"
+        kc = rng.standard_normal((L, kv_dim)).astype(np.float32)
+        vc = rng.standard_normal((L, kv_dim)).astype(np.float32)
+    if kind == "reference":
+        orc.ref().ref_set_threads(1)
+
+    def run(_):
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            if kv_name == "int8":
+                orc.attend_decode_i8(q, kc, ks, vc, vs, L - 1, DC_HQ, DC_HKV, DC_D, 0.125)
+            elif kind == "reference":
+                orc.ref_fullatt_attend(q, gate, kc, vc, None, 1, L - 1, DC_HQ, DC_HKV, DC_D)
+            else:
+                orc.attend_decode(q, kc, vc, L - 1, DC_HQ, DC_HKV, DC_D, 0.125)
+            n += 1
+        return n, time.perf_counter() - t0
+
+    pool = ThreadPoolExecutor(max_workers=ncpu)
+    res = list(pool.map(run, range(ncpu)))
+    pool.shutdown()
+    tokens = sum(n for n, _ in res)
+    el = max(t for _, t in res)
+    return tokens / el, ncpu, kind, (f"{tokens} decode tokens at ctx {L} ({kv_name} cache as the reference holds "
+                                     f"it: {'int8 codes + scales' if kv_name == 'int8' else 'fp32'}), one sequence "
+                                     f"per host thread, {el:.1f} s")
+
+
+def run_decode(args, torch, dist, rank, world, local_rank):
+    """tinyllm GQA decode at BASELINE configs[0]'s head shape (14 q / 2 kv heads, head_dim 64, NeoX RoPE
+    theta 1e6), batched: one decode step of one attention layer for `--batch` sequences at context `--ctx`
+    over an fp32, bf16 or INT8 (`--kv`) cache -- rope_append (RoPE of the new q and k, quantised or plain
+    cache write) then attend_decode over rows [0, ctx)."""
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    torch.cuda.set_device(local_rank)
+    kv_name = args.kv
+    GB, L = args.batch or DC_B, args.ctx or DC_CTX
+    sh = pkg.shard.shard(GB, DC_HKV, world, rank)  # (sequence, kv group) units
+    B, hkv = sh.nb, sh.nh
+    hq = hkv * (DC_HQ // DC_HKV)
+    ctx = pkg.Context(local_rank)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(21 + rank)
+    dt = {"f32": pkg.F32, "bf16": pkg.BF16, "int8": pkg.INT8}[kv_name]
+    kv = pkg.KVCache(ctx, 1, B, L, hkv, DC_D, dt)
+    kv.set_rope(DC_THETA)
+    n_el = B * L * hkv * DC_D
+    for p in kv.layer_ptrs(0):  # cache ~ N(0,1) (fp32 / bf16) or uniform codes with scales ~ U(0.005, 0.03)
+        if kv_name == "f32":
+            torch.as_tensor(CudaArray(p, (n_el,), "<f4"), device=dev).normal_(generator=gen)
+        elif kv_name == "bf16":
+            torch.as_tensor(CudaArray(p, (n_el,), "<i2"), device=dev).view(torch.bfloat16).normal_(generator=gen)
+        else:
+            t = torch.as_tensor(CudaArray(p, (n_el,), "|i1"), device=dev)
+            t.copy_(torch.randint(-127, 128, (n_el,), device=dev, generator=gen, dtype=torch.int8))
+    if kv_name == "int8":  # head-major scales, rows padded to a multiple of 64
+        for p in kv.layer_scales(0):
+            torch.as_tensor(CudaArray(p, (B * hkv * ((L + 63) // 64 * 64),), "<f4"), device=dev).uniform_(
+                0.005, 0.03, generator=gen)
+    q = torch.randn(B, hq * DC_D, device=dev, generator=gen)
+    k = torch.randn(B, hkv * DC_D, device=dev, generator=gen)
+    v = torch.randn(B, hkv * DC_D, device=dev, generator=gen)
+    pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
+    q_rot = torch.empty_like(q)
+    out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(DC_D)
+    bytes_alg = decode_bytes(B, L, hkv, kv_name)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if bytes_alg < (1 << 30) else None
+
+    def step(ev=None):
+        kv.rope_append_dev(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), hq, q_rot.data_ptr())
+        if ev is not None:
+            ev[1].record()
+        kv.attend_decode_dev(0, q_rot.data_ptr(), pos.data_ptr(), L - 1, hq, scale, out.data_ptr())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    clocks = ClockSampler(local_rank)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    l0 = ctx.launch_count
+    for s in range(args.steps):
+        if flush is not None:
+            flush.zero_()  # caches smaller than 1 GiB: evict them from L2 between steps
+        ev[s][0].record()
+        step(ev[s])
+        ev[s][2].record()
+    torch.cuda.synchronize()
+    launches = ctx.launch_count - l0
+    clk = clocks.stop()
+    ctx.synchronize()
+    ms = float(np.mean([e[0].elapsed_time(e[2]) for e in ev]))
+    att_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in ev]))
+    ms = pkg.shard.max_over_ranks(dist, ms, "cuda")
+    # e2e through the host-pointer ABI: pinned fp32 q / k / v / pos in, rotated q and the output back
+    hg = torch.Generator().manual_seed(5)
+    qh = torch.randn(B, hq * DC_D, generator=hg).pin_memory().numpy()
+    kh = torch.randn(B, hkv * DC_D, generator=hg).pin_memory().numpy()
+    vh = torch.randn(B, hkv * DC_D, generator=hg).pin_memory().numpy()
+    ph = torch.full((B,), L - 1, dtype=torch.int32).pin_memory().numpy()
+    qr = torch.empty(B, hq * DC_D).pin_memory().numpy()
+    oh = torch.empty(B, hq * DC_D).pin_memory().numpy()
+    ctx.set_stream(None)
+    n_e2e = max(3, args.steps)
+    kv.rope_append(0, qh, kh, vh, ph, hq, q_out=qr)
+    kv.attend_decode(0, qr, ph, hq, scale, out=oh)
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        kv.rope_append(0, qh, kh, vh, ph, hq, q_out=qr)
+        kv.attend_decode(0, qr, ph, hq, scale, out=oh)
+    e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / n_e2e, "cuda")
+    if rank != 0:
+        return None
+    hbm, _, src = peaks()
+    ach = bytes_alg / (att_ms * 1e-3) / 1e9
+    h2d = (qh.nbytes + kh.nbytes + vh.nbytes + 2 * ph.nbytes + qr.nbytes) * world
+    d2h = (qr.nbytes + oh.nbytes) * world
+    cfg_name = "BASELINE configs[0] exactly" if (GB, L, kv_name) == (1, 512, "f32") else \
+        "BASELINE configs[0]'s heads, batched"
+    line = {"metric": "tinyllm GQA decode tokens/s (one attention layer: RoPE + cache write + attention)",
+            "value": GB / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 arithmetic over a " + kv_name + " cache", "data": "synthetic (seeded)",
+            "config": {"workload": f"tinyllm_decode ({cfg_name})", "global_batch": GB, "ctx": L,
+                       "heads": "14 q / 2 kv", "head_dim": DC_D, "kv_dtype": kv_name,
+                       "l2": "256 MiB flush between steps" if flush is not None else "cache > L2",
+                       "parallelism": f"(sequence, kv group) units over {world} rank(s), no collective"},
+            "e2e": {"value": GB / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "host-pointer C ABI eif_cuda_rope_append + eif_cuda_attend_decode (pinned)"},
+            "roofline": {"kernel": "attn_decode_tc_kernel + combine" if kv_name == "bf16"
+                         else "attn_decode_simt_kernel + combine", "bound": "hbm", "achieved": ach, "peak": hbm,
+                         "unit": "GB/s", "frac": ach / hbm, "peak_source": src,
+                         "algorithmic_bytes_per_launch": bytes_alg, "attention_ms": att_ms, "traffic": None},
+            "gpu_launches": launches, "clocks": clk}
+    if world == 1 and not args.no_cpu_baseline:
+        tps, cores, kind, sample = cpu_decode_reference(kv_name, L)
+        line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", default="hybrid", choices=["hybrid", "prefill", "chunked"],
-                    help="hybrid = BASELINE configs[4] (the headline); prefill = configs[1]; chunked = configs[3]")
+    ap.add_argument("--workload", default="hybrid", choices=["hybrid", "prefill", "chunked", "decode"],
+                    help="hybrid = BASELINE configs[4] (the headline); prefill = configs[1]; chunked = configs[3]; "
+                         "decode = configs[0]'s tinyllm heads, batched (--kv f32 | bf16 | int8, --ctx)")
+    ap.add_argument("--kv", default="f32", choices=["f32", "bf16", "int8"], help="decode workload: cache dtype")
+    ap.add_argument("--ctx", type=int, default=None, help="decode workload: context length (default 4096)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -787,8 +976,8 @@ def main():
         torch.cuda.set_device(local_rank)
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         dist = tdist
-    if args.workload in ("prefill", "chunked"):
-        run = run_prefill if args.workload == "prefill" else run_chunked
+    if args.workload in ("prefill", "chunked", "decode"):
+        run = {"prefill": run_prefill, "chunked": run_chunked, "decode": run_decode}[args.workload]
         line = run(args, torch, dist, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)

@@ -30,7 +30,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
     const KT *__restrict__ Kc, const KT *__restrict__ Vc, const float *__restrict__ q, const int *__restrict__ pos,
     int max_seq, int Hkv, int chunk, int nchunk, float scale, float *__restrict__ part_o,
     float2 *__restrict__ part_ml, unsigned *__restrict__ dev_err, const float *__restrict__ k_scale,
-    const float *__restrict__ v_scale) {
+    const float *__restrict__ v_scale, int sstride) {
     constexpr int DL = D / 32;  // head-dim elements per lane in P.V
     static_assert(D % 32 == 0 && (DL == 2 || DL == 4 || DL == 8), "head_dim 64/128/256");
     constexpr bool kI8 = sizeof(KT) == 1;  // INT8 cache: codes, one K and one V scale per (row, kv head)
@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
         float ksc = 1.f, vsc = 1.f;
         if constexpr (kI8) {
             if (valid) {
-                const size_t si = ((size_t)b * max_seq + t) * Hkv + kvh;
+                const size_t si = ((size_t)b * Hkv + kvh) * sstride + t;
                 ksc = k_scale[si];
                 vsc = v_scale[si];
             }
@@ -231,7 +231,8 @@ size_t partials_bytes(const DecodeArgs &a, int nchunk) {
 }
 
 bool use_tc(const DecodeArgs &a) {
-    return a.dtype == EIF_CUDA_BF16 && a.tmk && a.tmv && !a.force_simt && decode_tc_supported(a.D, a.Hq / a.Hkv);
+    return (a.dtype == EIF_CUDA_BF16 || a.dtype == EIF_CUDA_INT8) && a.tmk && a.tmv && !a.force_simt &&
+           decode_tc_supported(a.D, a.Hq / a.Hkv);
 }
 
 // Tensor-core path: persistent CTAs (one per SM) take items round-robin, so pick the chunk count that
@@ -239,7 +240,8 @@ bool use_tc(const DecodeArgs &a) {
 Split choose_split_tc(const DecodeArgs &a, int sm_count) {
     const long units = (long)a.B * a.Hkv;
     const long tpu = (a.max_len + 63) / 64;  // 64-key tiles per unit
-    const double tile_bytes = 64.0 * a.D * 2 * 2;
+    // K + V bytes of a 64-key tile (INT8: codes plus the two scales of every key)
+    const double tile_bytes = a.dtype == EIF_CUDA_INT8 ? 64.0 * (a.D * 2 + 8) : 64.0 * a.D * 2 * 2;
     const double part_bytes = 2.0 * (a.Hq / a.Hkv) * a.D * 4;
     int best = 1;
     double best_cost = 1e300;
@@ -280,7 +282,7 @@ cudaError_t launch_simt(cudaStream_t st, const DecodeArgs &a, const Split &sp, f
     dim3 grid(sp.nchunk, a.Hkv, a.B);
     attn_decode_simt_kernel<KT, D, G><<<grid, kDecodeThreads, 0, st>>>(
         static_cast<const KT *>(a.K), static_cast<const KT *>(a.V), a.q, a.pos, a.max_seq, a.Hkv, sp.chunk,
-        sp.nchunk, a.scale, part_o, part_ml, a.dev_err, a.k_scale, a.v_scale);
+        sp.nchunk, a.scale, part_o, part_ml, a.dev_err, a.k_scale, a.v_scale, a.scale_stride);
     return cudaGetLastError();
 }
 
@@ -330,7 +332,9 @@ cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws,
     float *part_o = static_cast<float *>(ws);
     float2 *part_ml = reinterpret_cast<float2 *>(static_cast<char *>(ws) + o_bytes);
     cudaError_t e;
-    if (sp.tc)
+    if (sp.tc && a.dtype == EIF_CUDA_INT8)
+        e = launch_attend_decode_i8(st, *a.tmk, *a.tmv, a, sp.nchunk, sp.chunk, part_o, part_ml, sm_count);
+    else if (sp.tc)
         e = launch_attend_decode_tc(st, *a.tmk, *a.tmv, a, sp.nchunk, sp.chunk, part_o, part_ml, sm_count);
     else if (a.dtype == EIF_CUDA_F32)
         e = dispatch_d<float>(st, a, sp, part_o, part_ml, supported);

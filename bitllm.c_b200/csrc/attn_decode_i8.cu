@@ -1,0 +1,411 @@
+// attn_decode_i8.cu -- split-K GQA decode attention over tinyllm's INT8 KV cache on B200 tensor cores.
+//
+// Same contract as the other decode kernels (attn_decode.cu, attn_decode_tc.cu): every (sequence, kv head,
+// key chunk) item leaves an unnormalised partial (m, l, o[G][D]) that attn_decode_combine merges.  The
+// arithmetic is tinyllm's INT8 branch (src/eif_tinyllm.c:563-571, 618-625): score_t = (q . code_k[t]) *
+// k_scale[t] * scale, softmax, o = sum_t (p_t * v_scale[t]) * code_v[t].
+//
+// Structure (persistent, one CTA per SM, 4 NG + 1 warps):
+//   last warp, producer: one lane streams K and V tiles of 64 keys x D int8 codes through an NS-stage ring
+//           with 3-D TMA tile loads (boxes of 64 keys x 64 bytes, 64-byte swizzle, no multicast) and copies
+//           the tile's 64 K and 64 V scales (aligned 256-byte runs of the head-major scale rows) into the
+//           same stage with bulk asynchronous copies on the same "full" mbarrier;
+//   warps 0 .. 4NG-1 consumers in NG groups of 4 that take tiles round-robin, so NG tiles are in flight
+//           per SM: NG = 4 at head_dim 64, 2 at 128, 1 at 256, as many as the registers allow; within a
+//           group each warp takes 16 keys of the tile:
+//     S = Q K^T   A = the query, MMA rows 0-7 = heads (high f16 part), rows 8-15 = the same heads (low part),
+//                 so all G <= 8 heads of the kv head ride in one m16n8k16; B = the K codes, loaded with
+//                 ldmatrix from the int8 tile viewed as 16-bit pairs and widened in registers to exact f16
+//                 (byte permute into 0x64uu = 1024 + (x + 128), one f16x2 subtract).  ldmatrix hands each
+//                 thread 4 consecutive dims; the MMA's k slots (2t, 2t+1, 2t+8, 2t+9) are mapped to dims
+//                 (4t .. 4t+3) for both operands, a permutation of the reduction that leaves the sum alone;
+//     softmax     online in base 2; the S accumulator of a thread (head g, keys 2t, 2t+1, 2t+8, 2t+9) is
+//                 already the A-fragment layout of P, so no transpose;
+//     O += P V    A = p * v_scale (f16 high / low rows as for q); B = the V codes from ldmatrix.trans of
+//                 the 16-bit view, which gives each thread two keys of two adjacent dims: the even dims
+//                 and the odd dims of a 16-dim chunk form two n-tiles.
+// Exactness: codes are exact in f16, products are exact in the fp32 accumulator; the query and the
+// probabilities are split as hi + lo (22 significant bits) after scaling by powers of two into f16's
+// normal range (q: per head to a maximum in [2^13, 2^14); p * v_scale: by 2^12); both scalings are undone
+// exactly.  Results match fp32 arithmetic on the codes to ~1e-7.
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "internal.h"
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace {
+
+constexpr int KT = 64;          // keys per tile
+constexpr int kGroup = 4;       // consumer warps per group, 16 keys of a tile each
+constexpr int kSmemLimit = 227 * 1024;
+constexpr int HS = 8;           // head slots: MMA rows g (high part) and g + 8 (low part)
+constexpr float kPScale = 4096.f, kPUnscale = 1.f / 4096.f;
+
+// NG consumer groups take alternate tiles (more tiles in flight per SM where the registers allow).
+template <int D, int NG>
+struct I8Cfg {
+    static constexpr int NW = kGroup * NG;            // consumer warps
+    static constexpr int THREADS = 32 * (NW + 1);
+    static constexpr int BOX = 64 * 64;               // 64 keys x 64 code bytes, 64-byte swizzle
+    static constexpr int TILE = (D / 64) * BOX;       // K (or V) tile bytes
+    static constexpr int STAGE = 2 * TILE;
+    static constexpr int SCALES = 2 * KT * 4;         // per stage: the K and V scales of the tile's keys
+    static constexpr int EXTRA = NW * HS * D * 4              // merge buffer o
+                                 + 2 * NW * HS * 4            // merge m, l
+                                 + 64 * 8                     // barriers
+                                 + 1024;                      // alignment slack
+    static constexpr int NS_FIT = (kSmemLimit - EXTRA) / (STAGE + SCALES);
+    static constexpr int NS = NS_FIT > 16 ? 16 : NS_FIT;
+    static constexpr int SMEM = NS * (STAGE + SCALES) + EXTRA;
+    static_assert(NS >= 2, "pipeline needs two stages");
+};
+
+struct I8Params {
+    const float *q;
+    const float *ks, *vs;  // [B][Hkv][sstride] scales
+    const int *pos;
+    int max_seq, Hkv, G, Hq, sstride;
+    int nchunk, chunk_keys, n_items;
+    float qscale;  // scale * log2(e)
+    float *part_o;
+    float2 *part_ml;
+    unsigned *dev_err;
+};
+
+struct ItemInfo {
+    int b, kvh, t_begin, t_end, ntiles;
+};
+
+__device__ __forceinline__ ItemInfo item_info(const I8Params &p, int item, bool report) {
+    ItemInfo it;
+    const int unit = item / p.nchunk, c = item - unit * p.nchunk;
+    it.b = unit / p.Hkv;
+    it.kvh = unit - it.b * p.Hkv;
+    int pp = p.pos[it.b];
+    if (pp < 0 || pp >= p.max_seq) {
+        if (report) atomicOr(p.dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
+        pp = -1;
+    }
+    it.t_begin = c * p.chunk_keys;
+    it.t_end = min(pp + 1, it.t_begin + p.chunk_keys);
+    it.ntiles = it.t_end > it.t_begin ? (it.t_end - it.t_begin + KT - 1) / KT : 0;
+    return it;
+}
+
+// Two of the four codes of `u` (= packed int8 ^ 0x80808080, i.e. x + 128 per byte) as an exact f16 pair:
+// byte_perm places each byte under 0x64 (f16 0x64uu = 1024 + u), then 1152 = 1024 + 128 is subtracted.
+__device__ __forceinline__ uint32_t codes_f16x2(uint32_t u, uint32_t sel) {
+    const uint32_t h = __byte_perm(u, 0x64646464u, sel);
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
+    return r;
+}
+constexpr uint32_t kSelB01 = 0x5140, kSelB23 = 0x5342;  // bytes (0, 1) / (2, 3)
+constexpr uint32_t kSelB02 = 0x5240, kSelB13 = 0x5341;  // bytes (0, 2) / (1, 3)
+
+// (x0, x1) = hi + lo with hi = f16(x), lo = f16(x - hi); x0 in the low halves.
+__device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Shared-memory address of the 16-byte chunk `chunk` (16 dims) of row `key` in a tile of D/64 boxes, each
+// 64 keys x 64 bytes with the TMA 64-byte swizzle (bits 4-5 of the offset XOR bits 7-8).
+__device__ __forceinline__ uint32_t tile_addr(uint32_t base, int key, int chunk) {
+    return base + (chunk >> 2) * 4096 + key * 64 + (((chunk & 3) ^ ((key >> 1) & 3)) << 4);
+}
+
+template <int D, int NG>
+__global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
+    attn_decode_i8_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                          const I8Params p) {
+    using C = I8Cfg<D, NG>;
+    constexpr int NS = C::NS, KS = D / 16, NT = D / 8, NW = C::NW;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_align1024(smem_raw);
+    float *sbuf = reinterpret_cast<float *>(smem + NS * C::STAGE);  // [NS][2][64] K, V scales per stage
+    float *ow = sbuf + NS * 2 * KT;                                 // [4][HS][D]
+    float *mw = ow + NW * HS * D;                                   // [NW][HS]
+    float *lw = mw + NW * HS;                                       // [NW][HS]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(lw + NW * HS);
+    // bars: full[NS], empty[NS], merged, drained
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NS);
+    const uint32_t merged = smem_u32(bars + 2 * NS), drained = smem_u32(bars + 2 * NS + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, kGroup);  // the 4 warps of the group that takes the tile
+        }
+        mbar_init(merged, NW);
+        mbar_init(drained, NW);
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == NW) {
+        // ------------------------------------------------------------------ producer
+        // one lane: per tile the TMA loads of the K / V codes and two bulk copies of their 64 K / V scales
+        // (256-byte runs of the head-major scale rows; keys past t_end come along and are masked)
+        if (lane != 0) return;
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+        uint32_t it = 0;
+        for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+            const ItemInfo inf = item_info(p, item, false);
+            for (int i = 0; i < inf.ntiles; ++i, ++it) {
+                const uint32_t s = it % NS, ph = (it / NS) & 1;
+                if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.dev_err)) return;
+                const uint32_t fb = full0 + 8 * s;
+                const int t0 = inf.t_begin + i * KT;
+                const int row = inf.b * p.max_seq + t0;
+                mbar_arrive_expect_tx(fb, C::STAGE + C::SCALES);
+                const uint32_t kdst = smem_u32(smem + s * C::STAGE), vdst = kdst + C::TILE;
+#pragma unroll
+                for (int j = 0; j < D / 64; ++j) {
+                    tma_load_3d(kdst + j * C::BOX, &tmK, j * 64, inf.kvh, row, fb);
+                    tma_load_3d(vdst + j * C::BOX, &tmV, j * 64, inf.kvh, row, fb);
+                }
+                const size_t srow = ((size_t)inf.b * p.Hkv + inf.kvh) * p.sstride + t0;
+                const uint32_t sdst = smem_u32(sbuf + s * 2 * KT);
+                bulk_load(sdst, p.ks + srow, KT * 4, fb);
+                bulk_load(sdst + KT * 4, p.vs + srow, KT * 4, fb);
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------------- consumers
+    const int g = lane >> 2, t = lane & 3;
+    const int mi = lane >> 3, mr = lane & 7;               // ldmatrix: matrix / row this lane addresses
+    const int grp = warp / kGroup, wk = (warp % kGroup) * 16;  // group; first tile row of this warp's keys
+    const int my_key = wk + (mi & 1) * 8 + mr;             // tile row (key) of this lane's ldmatrix rows
+    uint32_t it_base = 0, item_no = 0;
+    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++item_no) {
+        const ItemInfo inf = item_info(p, item, warp == 0 && lane == 0);
+
+        // ---- query fragments: head g of the kv group, dims (4t .. 4t+3) of every 16-dim chunk, scaled by
+        //      2^e so that the head's largest |q * qscale| lies in [2^13, 2^14), split into f16 hi / lo
+        const bool on = g < p.G;
+        const float *qh = p.q + ((size_t)inf.b * p.Hq + (size_t)inf.kvh * p.G + (on ? g : 0)) * D;
+        float qv[KS][4];
+        float amax = 0.f;
+#pragma unroll
+        for (int kc = 0; kc < KS; ++kc) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) qv[kc][e] = on ? qh[kc * 16 + 4 * t + e] * p.qscale : 0.f;
+            amax = fmax3(amax, fmaxf(fabsf(qv[kc][0]), fabsf(qv[kc][1])), fmaxf(fabsf(qv[kc][2]), fabsf(qv[kc][3])));
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        int e2 = 0;
+        if (amax > 0.f && isfinite(amax)) {
+            int ex;
+            frexpf(amax, &ex);  // amax in [2^(ex-1), 2^ex)
+            e2 = max(-126, min(126, 14 - ex));
+        }
+        const float qmul = __int_as_float((127 + e2) << 23), qdiv = __int_as_float((127 - e2) << 23);
+        uint32_t qf[KS][4];
+#pragma unroll
+        for (int kc = 0; kc < KS; ++kc) {
+            split_f16x2(qv[kc][0] * qmul, qv[kc][1] * qmul, qf[kc][0], qf[kc][1]);
+            split_f16x2(qv[kc][2] * qmul, qv[kc][3] * qmul, qf[kc][2], qf[kc][3]);
+        }
+
+        float oacc[NT][4];
+#pragma unroll
+        for (int n = 0; n < NT; ++n) oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.f;
+        float m_run = -INFINITY, l_run = 0.f;
+
+        for (int i = grp; i < inf.ntiles; i += NG) {  // this group's tiles of the item
+            const uint32_t it = it_base + i;
+            const uint32_t s = it % NS, ph = (it / NS) & 1;
+            const int key0 = inf.t_begin + i * KT + wk;         // first key of this warp
+            const int nvalid = inf.t_end - key0;                // keys of the warp below t_end (may be <= 0)
+            if (!mbar_wait(full0 + 8 * s, ph, p.dev_err)) return;
+            const float *scs = sbuf + s * 2 * KT + wk;          // this warp's keys: K scales, V scales at +64
+            const uint32_t kbase = smem_u32(smem + s * C::STAGE), vbase = kbase + C::TILE;
+
+            // ---- S = Q K^T: n-tiles of keys 0-7 and 8-15 of the warp
+            float sacc[2][4];
+#pragma unroll
+            for (int n = 0; n < 2; ++n) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
+#pragma unroll
+            for (int kp = 0; kp < KS / 2; ++kp) {
+                uint32_t r0, r1, r2, r3;  // (keys 0-7 | 8-15) x (chunk 2kp | 2kp+1)
+                ldsm_x4(tile_addr(kbase, my_key, 2 * kp + (mi >> 1)), r0, r1, r2, r3);
+                r0 ^= 0x80808080u;
+                r1 ^= 0x80808080u;
+                r2 ^= 0x80808080u;
+                r3 ^= 0x80808080u;
+                const uint32_t *qa = qf[2 * kp], *qb = qf[2 * kp + 1];
+                mma_f16_16816(sacc[0], qa[0], qa[1], qa[2], qa[3], codes_f16x2(r0, kSelB01), codes_f16x2(r0, kSelB23));
+                mma_f16_16816(sacc[1], qa[0], qa[1], qa[2], qa[3], codes_f16x2(r1, kSelB01), codes_f16x2(r1, kSelB23));
+                mma_f16_16816(sacc[0], qb[0], qb[1], qb[2], qb[3], codes_f16x2(r2, kSelB01), codes_f16x2(r2, kSelB23));
+                mma_f16_16816(sacc[1], qb[0], qb[1], qb[2], qb[3], codes_f16x2(r3, kSelB01), codes_f16x2(r3, kSelB23));
+            }
+
+            // ---- online softmax (base 2) for head g over keys 2t, 2t+1, 8+2t, 9+2t
+            const int kk[4] = {2 * t, 2 * t + 1, 8 + 2 * t, 9 + 2 * t};
+            float sv[4], vsc[4];
+            sv[0] = sacc[0][0] + sacc[0][2];
+            sv[1] = sacc[0][1] + sacc[0][3];
+            sv[2] = sacc[1][0] + sacc[1][2];
+            sv[3] = sacc[1][1] + sacc[1][3];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {  // keys past t_end: masked (their scale slots hold stale values)
+                const bool ok = kk[e] < nvalid;
+                vsc[e] = ok ? scs[KT + kk[e]] : 0.f;
+                sv[e] = ok ? (sv[e] * qdiv) * scs[kk[e]] : -INFINITY;
+                mx = fmaxf(mx, sv[e]);
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float m_new = fmaxf(m_run, mx);
+            const float m_use = m_new == -INFINITY ? 0.f : m_new;
+            const float corr = fast_exp2(m_run - m_use);
+            float pv[4], psum = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float pe = fast_exp2(sv[e] - m_use);
+                psum += pe;
+                pv[e] = pe * vsc[e] * kPScale;
+            }
+            l_run = l_run * corr + psum;
+            m_run = m_new;
+            if (__any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    oacc[n][0] *= corr;
+                    oacc[n][1] *= corr;
+                    oacc[n][2] *= corr;
+                    oacc[n][3] *= corr;
+                }
+            }
+            uint32_t pa0, pa1, pa2, pa3;  // rows g (hi) / g+8 (lo); k slots = keys (2t, 2t+1) and (8+2t, 9+2t)
+            split_f16x2(pv[0], pv[1], pa0, pa1);
+            split_f16x2(pv[2], pv[3], pa2, pa3);
+
+            // ---- O += P V: ldmatrix.trans of (keys 0-7 | 8-15) x (chunk 2cp | 2cp+1); even / odd dims of a
+            //      chunk are n-tiles 2c and 2c+1
+#pragma unroll
+            for (int cp = 0; cp < D / 32; ++cp) {
+                uint32_t r0, r1, r2, r3;
+                ldsm_x4_t(tile_addr(vbase, my_key, 2 * cp + (mi >> 1)), r0, r1, r2, r3);
+                r0 ^= 0x80808080u;
+                r1 ^= 0x80808080u;
+                r2 ^= 0x80808080u;
+                r3 ^= 0x80808080u;
+                mma_f16_16816(oacc[4 * cp + 0], pa0, pa1, pa2, pa3, codes_f16x2(r0, kSelB02), codes_f16x2(r1, kSelB02));
+                mma_f16_16816(oacc[4 * cp + 1], pa0, pa1, pa2, pa3, codes_f16x2(r0, kSelB13), codes_f16x2(r1, kSelB13));
+                mma_f16_16816(oacc[4 * cp + 2], pa0, pa1, pa2, pa3, codes_f16x2(r2, kSelB02), codes_f16x2(r3, kSelB02));
+                mma_f16_16816(oacc[4 * cp + 3], pa0, pa1, pa2, pa3, codes_f16x2(r2, kSelB13), codes_f16x2(r3, kSelB13));
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty0 + 8 * s);
+        }
+
+        it_base += inf.ntiles;
+
+        // ---- item epilogue: l over the 4 lanes of a head, hi + lo rows, merge the NW warps
+        float l = l_run;
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        // the previous item's merge must be finished reading ow before it is overwritten
+        if (item_no > 0 && !mbar_wait(drained, (item_no - 1) & 1, p.dev_err)) return;
+        if (on) {
+            float *oh = ow + (warp * HS + g) * D;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                const int d = (n >> 1) * 16 + 4 * t + (n & 1);  // n-tile n, column 2t -> dim d; 2t+1 -> d + 2
+                oh[d] = (oacc[n][0] + oacc[n][2]) * kPUnscale;
+                oh[d + 2] = (oacc[n][1] + oacc[n][3]) * kPUnscale;
+            }
+            if (t == 0) {
+                mw[warp * HS + g] = m_run;
+                lw[warp * HS + g] = l;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(merged);
+        if (!mbar_wait(merged, item_no & 1, p.dev_err)) return;
+        const size_t pbase = (size_t)item * p.G;
+        for (int idx = threadIdx.x; idx < p.G * D; idx += 32 * NW) {
+            const int h = idx / D, d = idx - h * D;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) M = fmaxf(M, mw[w * HS + h]);
+            float O = 0.f, L = 0.f;
+            if (M != -INFINITY) {
+#pragma unroll
+                for (int w = 0; w < NW; ++w) {
+                    const float f = fast_exp2(mw[w * HS + h] - M);
+                    O += ow[(w * HS + h) * D + d] * f;
+                    L += lw[w * HS + h] * f;
+                }
+            }
+            p.part_o[(pbase + h) * D + d] = O;
+            if (d == 0) p.part_ml[pbase + h] = make_float2(M == -INFINITY ? -INFINITY : M * 0.69314718055994531f, L);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(drained);
+    }
+}
+
+template <int D, int NG>
+cudaError_t launch_i8_t(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv, const I8Params &p,
+                        int sm_count) {
+    using C = I8Cfg<D, NG>;
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_decode_i8_kernel<D, NG>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    const int grid = p.n_items < sm_count ? p.n_items : sm_count;
+    attn_decode_i8_kernel<D, NG><<<grid, C::THREADS, C::SMEM, st>>>(tk, tv, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
+                                    const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,
+                                    float2 *part_ml, int sm_count) {
+    I8Params p;
+    p.q = a.q;
+    p.ks = a.k_scale;
+    p.vs = a.v_scale;
+    p.sstride = a.scale_stride;
+    p.pos = a.pos;
+    p.max_seq = a.max_seq;
+    p.Hkv = a.Hkv;
+    p.G = a.Hq / a.Hkv;
+    p.Hq = a.Hq;
+    p.nchunk = nchunk;
+    p.chunk_keys = chunk_keys;
+    p.n_items = a.B * a.Hkv * nchunk;
+    p.qscale = a.scale * 1.4426950408889634f;
+    p.part_o = part_o;
+    p.part_ml = part_ml;
+    p.dev_err = a.dev_err;
+    switch (a.D) {
+        case 64: return launch_i8_t<64, 4>(st, tk, tv, p, sm_count);   // 105 registers: four groups
+        case 128: return launch_i8_t<128, 2>(st, tk, tv, p, sm_count);
+        case 256: return launch_i8_t<256, 1>(st, tk, tv, p, sm_count);  // 249 registers: one group
+        default: return cudaErrorInvalidValue;
+    }
+}

@@ -134,18 +134,27 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-// TMA descriptor of one bf16 cache array [batch*max_seq][n_kv][hd] as a 3-D tensor (hd, n_kv, rows),
-// boxes of 64 dims x 1 head x 64 rows with the 128-byte swizzle the decode kernel's ldmatrix expects.
+// TMA descriptor of one cache array [batch*max_seq][n_kv][hd] as a 3-D tensor (hd, n_kv, rows), boxes of
+// 64 dims x 1 head x 64 rows with the swizzle the decode kernels' ldmatrix addressing expects: bf16 rows
+// of 128 bytes with the 128-byte swizzle, INT8 code rows of 64 bytes with the 64-byte swizzle.
 bool make_kv_tensor_map(CUtensorMap *map, void *base, const eif_cuda_kv_t *kv) {
     EncodeTiledFn enc = encode_tiled();
     if (!enc || kv->hd % 64) return false;
+    const bool i8 = kv->dtype == EIF_CUDA_INT8;
+    const cuuint64_t elt = i8 ? 1 : 2;
     const cuuint64_t dims[3] = {(cuuint64_t)kv->hd, (cuuint64_t)kv->n_kv, (cuuint64_t)kv->batch * kv->max_seq};
-    const cuuint64_t strides[2] = {(cuuint64_t)kv->hd * 2, (cuuint64_t)kv->n_kv * kv->hd * 2};
+    const cuuint64_t strides[2] = {(cuuint64_t)kv->hd * elt, (cuuint64_t)kv->n_kv * kv->hd * elt};
     const cuuint32_t box[3] = {64, 1, 64};
     const cuuint32_t es[3] = {1, 1, 1};
-    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    // L2 promotion no wider than one kv head's row: the rows of the other kv heads in between belong to other
+    // work items, and a wider promotion would fetch them from HBM with every tile
+    const size_t head_row = (size_t)kv->hd * elt;
+    const CUtensorMapL2promotion promo = head_row >= 256   ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+                                         : head_row >= 128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
+                                                           : CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
+    return enc(map, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides,
+               box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, i8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+               promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool env_flag(const char *name) {
@@ -259,8 +268,8 @@ EIF_API uint64_t eif_cuda_launch_count(const eif_cuda_ctx_t *ctx) { return ctx ?
 
 static size_t dtype_size(eif_cuda_dtype_t t) { return t == EIF_CUDA_INT8 ? 1 : t == EIF_CUDA_BF16 ? 2 : 4; }
 
-// Bytes of one layer's K (or V) scale array of an INT8 cache: [batch][max_seq][n_kv] fp32.
-static size_t scale_bytes(const eif_cuda_kv_t *kv) { return (size_t)kv->batch * kv->max_seq * kv->n_kv * 4; }
+// Bytes of one layer's K (or V) scale array of an INT8 cache: [batch][n_kv][scale_stride] fp32.
+static size_t scale_bytes(const eif_cuda_kv_t *kv) { return (size_t)kv->batch * kv->n_kv * kv->scale_stride * 4; }
 
 EIF_API eif_status_t eif_cuda_kv_alloc(eif_cuda_ctx_t *ctx, int n_layers, int batch, int max_seq_len,
                                        int n_kv_heads, int head_dim, eif_cuda_dtype_t dtype, eif_cuda_kv_t **out) {
@@ -292,6 +301,7 @@ EIF_API eif_status_t eif_cuda_kv_alloc(eif_cuda_ctx_t *ctx, int n_layers, int ba
     if (dtype == EIF_CUDA_INT8) {
         kv->ks = (float **)calloc(n_layers, sizeof(float *));
         kv->vs = (float **)calloc(n_layers, sizeof(float *));
+        kv->scale_stride = (max_seq_len + 63) / 64 * 64;
     }
     const size_t bytes = kv->layer_elems * dtype_size(dtype);
     for (int l = 0; l < n_layers; ++l) {
@@ -404,8 +414,8 @@ EIF_API eif_status_t eif_cuda_kv_upload(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, 
         CK(cudaMemcpyAsync(sv, v_rows, n * 4, cudaMemcpyHostToDevice, ctx->stream));
         if (kv->dtype == EIF_CUDA_INT8) {
             CK(launch_kv_quantize(ctx->stream, static_cast<int8_t *>(kv->k[layer]), static_cast<int8_t *>(kv->v[layer]),
-                                  kv->ks[layer], kv->vs[layer], nullptr, (size_t)seq * kv->max_seq + row0, sk, sv,
-                                  n_rows, kv->max_seq, kv->n_kv, kv->hd, ctx->dev_err));
+                                  kv->ks[layer], kv->vs[layer], nullptr, seq, row0, sk, sv, n_rows, kv->max_seq,
+                                  kv->n_kv, kv->hd, kv->scale_stride, ctx->dev_err));
             ctx->launches += 1;
         } else {
             CK(launch_f32_to_bf16(ctx->stream, sk, static_cast<__nv_bfloat16 *>(kv->k[layer]) + off, n));
@@ -437,11 +447,10 @@ EIF_API eif_status_t eif_cuda_kv_download(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv
         float *sk = static_cast<float *>(ctx->stage);
         float *sv = reinterpret_cast<float *>(static_cast<char *>(ctx->stage) + a256(n * 4));
         if (kv->dtype == EIF_CUDA_INT8) {
-            const size_t r0 = (size_t)seq * kv->max_seq + row0;
-            CK(launch_kv_dequantize(ctx->stream, static_cast<int8_t *>(kv->k[layer]), kv->ks[layer], r0, sk, n_rows,
-                                    kv->n_kv, kv->hd));
-            CK(launch_kv_dequantize(ctx->stream, static_cast<int8_t *>(kv->v[layer]), kv->vs[layer], r0, sv, n_rows,
-                                    kv->n_kv, kv->hd));
+            CK(launch_kv_dequantize(ctx->stream, static_cast<int8_t *>(kv->k[layer]), kv->ks[layer], seq, row0, sk,
+                                    n_rows, kv->max_seq, kv->n_kv, kv->hd, kv->scale_stride));
+            CK(launch_kv_dequantize(ctx->stream, static_cast<int8_t *>(kv->v[layer]), kv->vs[layer], seq, row0, sv,
+                                    n_rows, kv->max_seq, kv->n_kv, kv->hd, kv->scale_stride));
         } else {
             CK(launch_bf16_to_f32(ctx->stream, static_cast<__nv_bfloat16 *>(kv->k[layer]) + off, sk, n));
             CK(launch_bf16_to_f32(ctx->stream, static_cast<__nv_bfloat16 *>(kv->v[layer]) + off, sv, n));
@@ -471,12 +480,18 @@ EIF_API eif_status_t eif_cuda_kv_download_int8(eif_cuda_ctx_t *ctx, eif_cuda_kv_
     if (n_rows == 0) return EIF_STATUS_OK;
     DeviceGuard g(ctx);
     const size_t r0 = (size_t)seq * kv->max_seq + row0;
-    const size_t n = (size_t)n_rows * kv->n_kv * kv->hd, ns = (size_t)n_rows * kv->n_kv;
-    const size_t off = r0 * kv->n_kv * kv->hd, soff = r0 * kv->n_kv;
+    const size_t n = (size_t)n_rows * kv->n_kv * kv->hd;
+    const size_t off = r0 * kv->n_kv * kv->hd;
     CK(cudaMemcpyAsync(k_codes, static_cast<int8_t *>(kv->k[layer]) + off, n, cudaMemcpyDeviceToHost, ctx->stream));
     CK(cudaMemcpyAsync(v_codes, static_cast<int8_t *>(kv->v[layer]) + off, n, cudaMemcpyDeviceToHost, ctx->stream));
-    CK(cudaMemcpyAsync(k_scale, kv->ks[layer] + soff, ns * 4, cudaMemcpyDeviceToHost, ctx->stream));
-    CK(cudaMemcpyAsync(v_scale, kv->vs[layer] + soff, ns * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    // the device keeps scales head-major; the engine's order is [row][kv head]: one strided copy per head
+    for (int h = 0; h < kv->n_kv; ++h) {
+        const size_t soff = ((size_t)seq * kv->n_kv + h) * kv->scale_stride + row0;
+        CK(cudaMemcpy2DAsync(k_scale + h, (size_t)kv->n_kv * 4, kv->ks[layer] + soff, 4, 4, n_rows,
+                             cudaMemcpyDeviceToHost, ctx->stream));
+        CK(cudaMemcpy2DAsync(v_scale + h, (size_t)kv->n_kv * 4, kv->vs[layer] + soff, 4, 4, n_rows,
+                             cudaMemcpyDeviceToHost, ctx->stream));
+    }
     return wait_stream(ctx);
 }
 
@@ -492,8 +507,8 @@ static eif_status_t kv_append_impl(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int l
                                    const float *k_dev, const float *v_dev) {
     if (kv->dtype == EIF_CUDA_INT8)
         CK(launch_kv_quantize(ctx->stream, static_cast<int8_t *>(kv->k[layer]), static_cast<int8_t *>(kv->v[layer]),
-                              kv->ks[layer], kv->vs[layer], pos_dev, 0, k_dev, v_dev, kv->batch, kv->max_seq,
-                              kv->n_kv, kv->hd, ctx->dev_err));
+                              kv->ks[layer], kv->vs[layer], pos_dev, 0, 0, k_dev, v_dev, kv->batch, kv->max_seq,
+                              kv->n_kv, kv->hd, kv->scale_stride, ctx->dev_err));
     else
         CK(launch_kv_append(ctx->stream, kv->k[layer], kv->v[layer], kv->dtype, pos_dev, k_dev, v_dev, kv->batch,
                             kv->max_seq, kv->n_kv * kv->hd, ctx->dev_err));
@@ -548,7 +563,7 @@ static eif_status_t decode_check(eif_cuda_ctx_t *ctx, const eif_cuda_kv_t *kv, i
 }
 
 void decode_prepare(eif_cuda_kv_t *kv, int layer, DecodeArgs &a) {
-    if (kv->dtype == EIF_CUDA_BF16) {
+    if (kv->dtype == EIF_CUDA_BF16 || kv->dtype == EIF_CUDA_INT8) {
         if (!kv->tm_ready[layer]) {
             kv->tm_ready[layer] = make_kv_tensor_map(&kv->tmk[layer], kv->k[layer], kv) &&
                                   make_kv_tensor_map(&kv->tmv[layer], kv->v[layer], kv);
@@ -561,6 +576,7 @@ void decode_prepare(eif_cuda_kv_t *kv, int layer, DecodeArgs &a) {
     if (kv->dtype == EIF_CUDA_INT8) {
         a.k_scale = kv->ks[layer];
         a.v_scale = kv->vs[layer];
+        a.scale_stride = kv->scale_stride;
     }
     a.force_simt = env_flag("BITLLM_DECODE_SIMT");
 }
@@ -1283,6 +1299,7 @@ static eif_status_t rope_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, 
     if (kv->dtype == EIF_CUDA_INT8) {
         a.k_scale = kv->ks[layer];
         a.v_scale = kv->vs[layer];
+        a.scale_stride = kv->scale_stride;
     }
     CK(launch_rope_append(ctx->stream, a));
     ctx->launches += 1;

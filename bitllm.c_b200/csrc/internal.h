@@ -44,8 +44,10 @@ struct eif_cuda_kv {
     size_t layer_elems = 0;  // batch * max_seq * n_kv * hd
     void **k = nullptr;      // [n_layers] device pointers
     void **v = nullptr;
-    // INT8 caches: per-layer scales [batch][max_seq][n_kv] of K and V (nullptr for the other dtypes)
+    // INT8 caches: per-layer scales of K and V, head-major [batch][n_kv][scale_stride] with scale_stride =
+    // max_seq rounded up to 64, so the 64 scales of a key tile are one aligned 256-byte run (nullptr otherwise)
     float **ks = nullptr, **vs = nullptr;
+    int scale_stride = 0;
     // TMA descriptors of the bf16 layers (64-key x 64-dim boxes, 128-byte swizzle), made on first use
     CUtensorMap *tmk = nullptr;
     CUtensorMap *tmv = nullptr;
@@ -91,8 +93,9 @@ struct DecodeArgs {
     const CUtensorMap *tmv = nullptr;
     bool force_simt = false;
     size_t max_ws_bytes = 0;  // 0: the split may use any amount of scratch; else it must fit in this many bytes
-    const float *k_scale = nullptr;  // INT8 caches: [B][max_seq][Hkv] scales of K and V
+    const float *k_scale = nullptr;  // INT8 caches: [B][Hkv][scale_stride] scales of K and V
     const float *v_scale = nullptr;
+    int scale_stride = 0;
 };
 
 // Fused per-token mixer bodies (mixer_fused.cu).
@@ -132,7 +135,8 @@ struct RopeArgs {
     __nv_bfloat16 *q_out_bf16;
     int B, n_tok, start_pos, nh, nkv, hd, max_seq, interleaved;
     unsigned *dev_err;
-    float *k_scale = nullptr, *v_scale = nullptr;  // INT8 caches: [B][max_seq][nkv]
+    float *k_scale = nullptr, *v_scale = nullptr;  // INT8 caches: [B][nkv][scale_stride]
+    int scale_stride = 0;
 };
 cudaError_t launch_rope_append(cudaStream_t st, const RopeArgs &a);
 
@@ -184,6 +188,10 @@ bool decode_tc_supported(int D, int G);
 cudaError_t launch_attend_decode_tc(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
                                     const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,
                                     float2 *part_ml, int sm_count);
+// Tensor-core decode over an INT8 cache (attn_decode_i8.cu); tk / tv: 64-byte-swizzled int8 tensor maps.
+cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
+                                    const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,
+                                    float2 *part_ml, int sm_count);
 // Workspace bytes needed by launch_attend_decode for these args and the chosen split.
 size_t decode_workspace_bytes(const DecodeArgs &a, int sm_count);
 cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws, size_t ws_bytes, int sm_count,
@@ -191,13 +199,14 @@ cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws,
 
 cudaError_t launch_kv_append(cudaStream_t st, void *K, void *V, eif_cuda_dtype_t dtype, const int *pos,
                              const float *k, const float *v, int B, int max_seq, int kv_dim, unsigned *dev_err);
-// INT8 caches (kv.cu).  Quantise fp32 rows (k, v: [n_rows][nkv*hd]) into cache rows: row r lands at
-// b * max_seq + pos[b] with b = r when pos is set (one new token per sequence), else at dst_row0 + r.
+// INT8 caches (kv.cu).  Quantise fp32 rows (k, v: [n_rows][nkv*hd]) into the cache: row r lands in
+// sequence r at position pos[r] when pos is set (one new token per sequence), else in sequence `seq` at
+// position t0 + r.  Scales are [B][nkv][scale_stride].
 cudaError_t launch_kv_quantize(cudaStream_t st, int8_t *K, int8_t *V, float *ks, float *vs, const int *pos,
-                               size_t dst_row0, const float *k, const float *v, int n_rows, int max_seq, int nkv,
-                               int hd, unsigned *dev_err);
-// code * scale of n_rows consecutive cache rows starting at src_row0, into fp32 [n_rows][nkv*hd].
-cudaError_t launch_kv_dequantize(cudaStream_t st, const int8_t *K, const float *ks, size_t src_row0, float *out,
-                                 int n_rows, int nkv, int hd);
+                               int seq, int t0, const float *k, const float *v, int n_rows, int max_seq, int nkv,
+                               int hd, int scale_stride, unsigned *dev_err);
+// code * scale of rows [t0, t0 + n_rows) of sequence `seq`, into fp32 [n_rows][nkv*hd].
+cudaError_t launch_kv_dequantize(cudaStream_t st, const int8_t *K, const float *ks, int seq, int t0, float *out,
+                                 int n_rows, int max_seq, int nkv, int hd, int scale_stride);
 cudaError_t launch_f32_to_bf16(cudaStream_t st, const float *src, __nv_bfloat16 *dst, size_t n);
 cudaError_t launch_bf16_to_f32(cudaStream_t st, const __nv_bfloat16 *src, float *dst, size_t n);

@@ -48,9 +48,9 @@ __global__ void bf16_to_f32_kernel(const __nv_bfloat16 *__restrict__ s, float *_
 template <int VPL>
 __global__ void __launch_bounds__(256) kv_quantize_kernel(int8_t *__restrict__ K, int8_t *__restrict__ V,
                                                           float *__restrict__ ks, float *__restrict__ vs,
-                                                          const int *__restrict__ pos, size_t dst_row0,
+                                                          const int *__restrict__ pos, int seq, int t0,
                                                           const float *__restrict__ k, const float *__restrict__ v,
-                                                          int n_rows, int max_seq, int nkv,
+                                                          int n_rows, int max_seq, int nkv, int sstride,
                                                           unsigned *__restrict__ dev_err) {
     constexpr int HD = 32 * VPL;
     const int lane = threadIdx.x & 31;
@@ -59,30 +59,31 @@ __global__ void __launch_bounds__(256) kv_quantize_kernel(int8_t *__restrict__ K
     const bool is_v = item & 1;
     const long rh = item >> 1;
     const int r = (int)(rh / nkv), h = (int)(rh % nkv);
-    size_t drow;
+    int b = seq, t = t0 + r;
     if (pos) {
-        const int p = pos[r];
-        if (p < 0 || p >= max_seq) {
+        b = r;
+        t = pos[r];
+        if (t < 0 || t >= max_seq) {
             if (lane == 0 && h == 0 && !is_v) atomicOr(dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
             return;
         }
-        drow = (size_t)r * max_seq + p;
-    } else {
-        drow = dst_row0 + r;
     }
+    const size_t drow = (size_t)b * max_seq + t;
     float x[VPL];
     const float *src = (is_v ? v : k) + ((size_t)r * nkv + h) * HD + lane * VPL;  // caller's rows: no alignment
 #pragma unroll
     for (int i = 0; i < VPL; ++i) x[i] = src[i];
-    quantize_head_warp<VPL>(x, (is_v ? V : K) + (drow * nkv + h) * HD, (is_v ? vs : ks) + drow * nkv + h, lane);
+    quantize_head_warp<VPL>(x, (is_v ? V : K) + (drow * nkv + h) * HD,
+                            (is_v ? vs : ks) + ((size_t)b * nkv + h) * sstride + t, lane);
 }
 
-__global__ void kv_dequantize_kernel(const int8_t *__restrict__ K, const float *__restrict__ ks, size_t src_row0,
-                                     float *__restrict__ out, size_t n, int nkv, int hd) {
-    const size_t base = src_row0 * nkv * hd;
+__global__ void kv_dequantize_kernel(const int8_t *__restrict__ K, const float *__restrict__ ks, int seq, int t0,
+                                     float *__restrict__ out, size_t n, int max_seq, int nkv, int hd, int sstride) {
+    const size_t base = ((size_t)seq * max_seq + t0) * nkv * hd;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const size_t head = i / hd;  // (row, kv head) of element i, counted from src_row0
-        out[i] = (float)K[base + i] * ks[src_row0 * nkv + head];
+        const size_t rh = i / hd;  // (row, kv head) of element i, rows counted from t0
+        const int r = (int)(rh / nkv), h = (int)(rh % nkv);
+        out[i] = (float)K[base + i] * ks[((size_t)seq * nkv + h) * sstride + t0 + r];
     }
 }
 
@@ -118,33 +119,33 @@ cudaError_t launch_bf16_to_f32(cudaStream_t st, const __nv_bfloat16 *src, float 
 }
 
 cudaError_t launch_kv_quantize(cudaStream_t st, int8_t *K, int8_t *V, float *ks, float *vs, const int *pos,
-                               size_t dst_row0, const float *k, const float *v, int n_rows, int max_seq, int nkv,
-                               int hd, unsigned *dev_err) {
+                               int seq, int t0, const float *k, const float *v, int n_rows, int max_seq, int nkv,
+                               int hd, int scale_stride, unsigned *dev_err) {
     const long warps = 2L * n_rows * nkv;
     const unsigned grid = (unsigned)((warps + 7) / 8);
     if (grid == 0) return cudaSuccess;
     switch (hd) {
         case 64:
-            kv_quantize_kernel<2><<<grid, 256, 0, st>>>(K, V, ks, vs, pos, dst_row0, k, v, n_rows, max_seq, nkv,
-                                                         dev_err);
+            kv_quantize_kernel<2><<<grid, 256, 0, st>>>(K, V, ks, vs, pos, seq, t0, k, v, n_rows, max_seq, nkv,
+                                                         scale_stride, dev_err);
             break;
         case 128:
-            kv_quantize_kernel<4><<<grid, 256, 0, st>>>(K, V, ks, vs, pos, dst_row0, k, v, n_rows, max_seq, nkv,
-                                                         dev_err);
+            kv_quantize_kernel<4><<<grid, 256, 0, st>>>(K, V, ks, vs, pos, seq, t0, k, v, n_rows, max_seq, nkv,
+                                                         scale_stride, dev_err);
             break;
         case 256:
-            kv_quantize_kernel<8><<<grid, 256, 0, st>>>(K, V, ks, vs, pos, dst_row0, k, v, n_rows, max_seq, nkv,
-                                                         dev_err);
+            kv_quantize_kernel<8><<<grid, 256, 0, st>>>(K, V, ks, vs, pos, seq, t0, k, v, n_rows, max_seq, nkv,
+                                                         scale_stride, dev_err);
             break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
 
-cudaError_t launch_kv_dequantize(cudaStream_t st, const int8_t *K, const float *ks, size_t src_row0, float *out,
-                                 int n_rows, int nkv, int hd) {
+cudaError_t launch_kv_dequantize(cudaStream_t st, const int8_t *K, const float *ks, int seq, int t0, float *out,
+                                 int n_rows, int max_seq, int nkv, int hd, int scale_stride) {
     const size_t n = (size_t)n_rows * nkv * hd;
     if (n == 0) return cudaSuccess;
-    kv_dequantize_kernel<<<grid_for(n), 256, 0, st>>>(K, ks, src_row0, out, n, nkv, hd);
+    kv_dequantize_kernel<<<grid_for(n), 256, 0, st>>>(K, ks, seq, t0, out, n, max_seq, nkv, hd, scale_stride);
     return cudaGetLastError();
 }

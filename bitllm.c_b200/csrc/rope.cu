@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeArgs a) {
             const int h = is_v ? it - nkv : it;
             const float *src = is_v ? a.v + ((size_t)r * nkv + h) * hd : krot + h * hd;
             int8_t *dst = static_cast<int8_t *>(is_v ? a.Vc : a.Kc) + crow + (size_t)h * hd;
-            float *sc = (is_v ? a.v_scale : a.k_scale) + ((size_t)b * a.max_seq + p) * nkv + h;
+            float *sc = (is_v ? a.v_scale : a.k_scale) + ((size_t)b * nkv + h) * a.scale_stride + p;
             if (hd == 64)
                 quantize_from<2>(src, dst, sc, lane);
             else if (hd == 128)

@@ -265,7 +265,8 @@ class KVCache:
         return kc, vc, ks, vs
 
     def layer_scales(self, layer: int):
-        """INT8 caches: device pointers of the layer's K / V scales [batch][max_seq_len][n_kv_heads] fp32."""
+        """INT8 caches: device pointers of the layer's K / V scales, head-major [batch][n_kv_heads][stride] fp32,
+        stride = max_seq_len rounded up to 64."""
         k, v = _P(), _P()
         self.ctx.check(lib().eif_cuda_kv_layer_scales(self._h, layer, ctypes.byref(k), ctypes.byref(v)),
                        "kv_layer_scales")

@@ -128,7 +128,8 @@ eif_status_t eif_cuda_kv_layer_ptrs(const eif_cuda_kv_t *kv, int layer, void **k
 eif_status_t eif_cuda_kv_download_int8(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int seq, int row0,
                                        int n_rows, int8_t *k_codes, int8_t *v_codes, float *k_scale,
                                        float *v_scale);
-/* Device pointers of one INT8 layer's scales: [batch][max_seq_len][n_kv_heads] fp32. */
+/* Device pointers of one INT8 layer's scales, head-major: [batch][n_kv_heads][stride] fp32 with stride =
+ * max_seq_len rounded up to 64 (entry (b, h, t) scales row t of kv head h of sequence b). */
 eif_status_t eif_cuda_kv_layer_scales(const eif_cuda_kv_t *kv, int layer, float **k_scale_dev,
                                       float **v_scale_dev);
 

@@ -80,11 +80,15 @@ def test_append_batch(pkg, ctx, orc):
         assert bits_equal(ks[0], rks[b]) and bits_equal(vs[0], rvs[b])
 
 
+@pytest.mark.parametrize("simt", [False, True], ids=["tensor-core", "simt"])
 @pytest.mark.parametrize("nh,nkv,hd,T", [(14, 2, 64, 700), (8, 2, 128, 1500), (8, 1, 256, 300), (6, 6, 64, 129),
-                                         (16, 2, 128, 64)])
-def test_decode_vs_oracle(pkg, ctx, orc, nh, nkv, hd, T):
+                                         (16, 2, 128, 64), (3, 1, 64, 4000)])
+def test_decode_vs_oracle(pkg, ctx, orc, monkeypatch, simt, nh, nkv, hd, T):
     """attend_decode over an uploaded INT8 cache, a batch of sequences at different positions (split-K chunks,
-    groups 1..8), against the restatement's INT8 attention on the same codes."""
+    groups 1..8, ragged last tiles), against the restatement's INT8 attention on the same codes; both the
+    tensor-core kernel and the SIMT kernel (BITLLM_DECODE_SIMT=1)."""
+    if simt:
+        monkeypatch.setenv("BITLLM_DECODE_SIMT", "1")
     rng = np.random.default_rng(nh * 1000 + hd + T)
     B = 3
     kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, pkg.INT8)
