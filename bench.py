@@ -927,8 +927,9 @@ def run_decode(args, torch, dist, rank, world, local_rank):
             "e2e": {"value": GB / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "host-pointer C ABI eif_cuda_rope_append + eif_cuda_attend_decode (pinned)"},
-            "roofline": {"kernel": "attn_decode_tc_kernel + combine" if kv_name == "bf16"
-                         else "attn_decode_simt_kernel + combine", "bound": "hbm", "achieved": ach, "peak": hbm,
+            "roofline": {"kernel": {"bf16": "attn_decode_tc_kernel", "int8": "attn_decode_i8_kernel"}.get(
+                             kv_name, "attn_decode_simt_kernel") + " + combine", "bound": "hbm", "achieved": ach,
+                         "peak": hbm,
                          "unit": "GB/s", "frac": ach / hbm, "peak_source": src,
                          "algorithmic_bytes_per_launch": bytes_alg, "attention_ms": att_ms, "traffic": None},
             "gpu_launches": launches, "clocks": clk}
