@@ -11,10 +11,13 @@
 // (running max m, sum l, o[G][D]) in scratch; attn_decode_combine merges the chunks of a sequence
 // with a log-sum-exp rescale, applies the gate and the SubLN of the whole row and writes out.
 //
-// This file holds the SIMT kernel (fp32, bf16 or INT8 cache, fp32 arithmetic): lanes own keys for the
-// scores and own head-dim slices for P.V.  It is the exact-parity path for fp32 caches, and the INT8 path
-// (tinyllm kv_type 1, src/eif_tinyllm.c:563-571, 618-625): score = (q . codes) * k_scale * scale, and the
-// key's probability times its v_scale weights the V codes; codes widen to fp32 exactly (i8x4_to_f32).
+// This file holds the split choice, the combine and the SIMT kernel (fp32, bf16 or INT8 cache, fp32
+// arithmetic, K / V read straight from global memory): lanes own keys for the scores and own head-dim
+// slices for P.V.  The TMA-fed kernels take the common shapes (attn_decode_tc.cu: bf16, attn_decode_i8.cu:
+// INT8, attn_decode_f32.cu: fp32 at head_dim 64 / 128); the SIMT kernel serves the rest (fp32 at head_dim
+// 256, BITLLM_DECODE_SIMT=1).  Its INT8 branch is tinyllm kv_type 1 (src/eif_tinyllm.c:563-571, 618-625):
+// score = (q . codes) * k_scale * scale, and the key's probability times its v_scale weights the V codes;
+// codes widen to fp32 exactly (i8x4_to_f32).
 #include <math.h>
 
 #include "internal.h"
@@ -111,14 +114,30 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
             s[h] = kI8 ? pr * vsc : pr;  // INT8: p * v_scale weights the codes (src/eif_tinyllm.c:622-625)
         }
         const int nvalid = min(32, t_end - t0);
-        for (int j = 0; j < nvalid; ++j) {
-            float vv[DL];
-            KvLoad<KT, DL>::load(Vb + (size_t)(t0 + j) * row_stride + lane * DL, vv);
+        const KT *vrow = Vb + (size_t)t0 * row_stride + lane * DL;
+        if (nvalid == 32) {
+            // a full block: a constant trip count, unrolled so that eight rows' loads are in flight together
+#pragma unroll 8
+            for (int j = 0; j < 32; ++j) {
+                float vv[DL];
+                KvLoad<KT, DL>::load(vrow + (size_t)j * row_stride, vv);
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
-                const float pj = __shfl_sync(0xffffffffu, s[h], j);
+                for (int h = 0; h < G; ++h) {
+                    const float pj = __shfl_sync(0xffffffffu, s[h], j);
 #pragma unroll
-                for (int i = 0; i < DL; ++i) acc[h][i] += pj * vv[i];
+                    for (int i = 0; i < DL; ++i) acc[h][i] += pj * vv[i];
+                }
+            }
+        } else {
+            for (int j = 0; j < nvalid; ++j) {
+                float vv[DL];
+                KvLoad<KT, DL>::load(vrow + (size_t)j * row_stride, vv);
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float pj = __shfl_sync(0xffffffffu, s[h], j);
+#pragma unroll
+                    for (int i = 0; i < DL; ++i) acc[h][i] += pj * vv[i];
+                }
             }
         }
     }
@@ -230,9 +249,11 @@ size_t partials_bytes(const DecodeArgs &a, int nchunk) {
     return align256(units * nchunk * G * a.D * sizeof(float)) + align256(units * nchunk * G * sizeof(float2));
 }
 
+// The TMA-fed persistent kernels: bf16 / INT8 caches on the tensor cores, fp32 caches in fp32 FMAs.
 bool use_tc(const DecodeArgs &a) {
-    return (a.dtype == EIF_CUDA_BF16 || a.dtype == EIF_CUDA_INT8) && a.tmk && a.tmv && !a.force_simt &&
-           decode_tc_supported(a.D, a.Hq / a.Hkv);
+    if (!a.tmk || !a.tmv || a.force_simt) return false;
+    if (a.dtype == EIF_CUDA_F32) return decode_f32_supported(a.D, a.Hq / a.Hkv);
+    return decode_tc_supported(a.D, a.Hq / a.Hkv);
 }
 
 // Tensor-core path: persistent CTAs (one per SM) take items round-robin, so pick the chunk count that
@@ -241,7 +262,8 @@ Split choose_split_tc(const DecodeArgs &a, int sm_count) {
     const long units = (long)a.B * a.Hkv;
     const long tpu = (a.max_len + 63) / 64;  // 64-key tiles per unit
     // K + V bytes of a 64-key tile (INT8: codes plus the two scales of every key)
-    const double tile_bytes = a.dtype == EIF_CUDA_INT8 ? 64.0 * (a.D * 2 + 8) : 64.0 * a.D * 2 * 2;
+    const double tile_bytes = a.dtype == EIF_CUDA_INT8 ? 64.0 * (a.D * 2 + 8)
+                              : 64.0 * a.D * 2 * (a.dtype == EIF_CUDA_F32 ? 4 : 2);
     const double part_bytes = 2.0 * (a.Hq / a.Hkv) * a.D * 4;
     int best = 1;
     double best_cost = 1e300;
@@ -332,7 +354,9 @@ cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws,
     float *part_o = static_cast<float *>(ws);
     float2 *part_ml = reinterpret_cast<float2 *>(static_cast<char *>(ws) + o_bytes);
     cudaError_t e;
-    if (sp.tc && a.dtype == EIF_CUDA_INT8)
+    if (sp.tc && a.dtype == EIF_CUDA_F32)
+        e = launch_attend_decode_f32(st, *a.tmk, *a.tmv, a, sp.nchunk, sp.chunk, part_o, part_ml, sm_count);
+    else if (sp.tc && a.dtype == EIF_CUDA_INT8)
         e = launch_attend_decode_i8(st, *a.tmk, *a.tmv, a, sp.nchunk, sp.chunk, part_o, part_ml, sm_count);
     else if (sp.tc)
         e = launch_attend_decode_tc(st, *a.tmk, *a.tmv, a, sp.nchunk, sp.chunk, part_o, part_ml, sm_count);

@@ -57,9 +57,12 @@ struct I8Cfg {
                                  + 64 * 8                     // barriers
                                  + 1024;                      // alignment slack
     static constexpr int NS_FIT = (kSmemLimit - EXTRA) / (STAGE + SCALES);
-    static constexpr int NS = NS_FIT > 16 ? 16 : NS_FIT;
+    // a multiple of NG: consecutive uses of a stage within an item go to the same group, which has consumed
+    // the previous use itself before it polls the next (a parity wait cannot tell use k from use k-2, and
+    // TMA copies complete out of order)
+    static constexpr int NS = (NS_FIT > 16 ? 16 : NS_FIT) / NG * NG;
     static constexpr int SMEM = NS * (STAGE + SCALES) + EXTRA;
-    static_assert(NS >= 2, "pipeline needs two stages");
+    static_assert(NS >= 2 && NS % NG == 0, "ring depth a multiple of the consumer groups");
 };
 
 struct I8Params {

@@ -134,17 +134,18 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-// TMA descriptor of one cache array [batch*max_seq][n_kv][hd] as a 3-D tensor (hd, n_kv, rows), boxes of
-// 64 dims x 1 head x 64 rows with the swizzle the decode kernels' ldmatrix addressing expects: bf16 rows
-// of 128 bytes with the 128-byte swizzle, INT8 code rows of 64 bytes with the 64-byte swizzle.
+// TMA descriptor of one cache array [batch*max_seq][n_kv][hd] as a 3-D tensor (hd, n_kv, rows) with the boxes
+// and swizzle each decode kernel's shared-memory addressing expects: bf16 64 dims x 64 keys (128-byte rows,
+// 128-byte swizzle), INT8 64 dims x 64 keys (64-byte rows, 64-byte swizzle), fp32 32 dims x 32 keys
+// (128-byte rows, 128-byte swizzle).
 bool make_kv_tensor_map(CUtensorMap *map, void *base, const eif_cuda_kv_t *kv) {
     EncodeTiledFn enc = encode_tiled();
     if (!enc || kv->hd % 64) return false;
-    const bool i8 = kv->dtype == EIF_CUDA_INT8;
-    const cuuint64_t elt = i8 ? 1 : 2;
+    const bool i8 = kv->dtype == EIF_CUDA_INT8, f32 = kv->dtype == EIF_CUDA_F32;
+    const cuuint64_t elt = i8 ? 1 : f32 ? 4 : 2;
     const cuuint64_t dims[3] = {(cuuint64_t)kv->hd, (cuuint64_t)kv->n_kv, (cuuint64_t)kv->batch * kv->max_seq};
     const cuuint64_t strides[2] = {(cuuint64_t)kv->hd * elt, (cuuint64_t)kv->n_kv * kv->hd * elt};
-    const cuuint32_t box[3] = {64, 1, 64};
+    const cuuint32_t box[3] = {f32 ? 32u : 64u, 1, f32 ? 32u : 64u};
     const cuuint32_t es[3] = {1, 1, 1};
     // L2 promotion no wider than one kv head's row: the rows of the other kv heads in between belong to other
     // work items, and a wider promotion would fetch them from HBM with every tile
@@ -152,7 +153,7 @@ bool make_kv_tensor_map(CUtensorMap *map, void *base, const eif_cuda_kv_t *kv) {
     const CUtensorMapL2promotion promo = head_row >= 256   ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
                                          : head_row >= 128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
                                                            : CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
-    return enc(map, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides,
+    return enc(map, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides,
                box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, i8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -563,15 +564,13 @@ static eif_status_t decode_check(eif_cuda_ctx_t *ctx, const eif_cuda_kv_t *kv, i
 }
 
 void decode_prepare(eif_cuda_kv_t *kv, int layer, DecodeArgs &a) {
-    if (kv->dtype == EIF_CUDA_BF16 || kv->dtype == EIF_CUDA_INT8) {
-        if (!kv->tm_ready[layer]) {
-            kv->tm_ready[layer] = make_kv_tensor_map(&kv->tmk[layer], kv->k[layer], kv) &&
-                                  make_kv_tensor_map(&kv->tmv[layer], kv->v[layer], kv);
-        }
-        if (kv->tm_ready[layer]) {
-            a.tmk = &kv->tmk[layer];
-            a.tmv = &kv->tmv[layer];
-        }
+    if (!kv->tm_ready[layer]) {
+        kv->tm_ready[layer] = make_kv_tensor_map(&kv->tmk[layer], kv->k[layer], kv) &&
+                              make_kv_tensor_map(&kv->tmv[layer], kv->v[layer], kv);
+    }
+    if (kv->tm_ready[layer]) {
+        a.tmk = &kv->tmk[layer];
+        a.tmv = &kv->tmv[layer];
     }
     if (kv->dtype == EIF_CUDA_INT8) {
         a.k_scale = kv->ks[layer];

@@ -48,7 +48,7 @@ struct eif_cuda_kv {
     // max_seq rounded up to 64, so the 64 scales of a key tile are one aligned 256-byte run (nullptr otherwise)
     float **ks = nullptr, **vs = nullptr;
     int scale_stride = 0;
-    // TMA descriptors of the bf16 layers (64-key x 64-dim boxes, 128-byte swizzle), made on first use
+    // TMA descriptors of the layers (the decode kernels' boxes for the cache dtype), made on first use
     CUtensorMap *tmk = nullptr;
     CUtensorMap *tmv = nullptr;
     bool *tm_ready = nullptr;
@@ -89,7 +89,7 @@ struct DecodeArgs {
     const float *sub_norm;
     float *out;
     unsigned *dev_err;
-    const CUtensorMap *tmk = nullptr;  // bf16 caches: TMA descriptors of K / V (nullptr -> SIMT kernel)
+    const CUtensorMap *tmk = nullptr;  // TMA descriptors of K / V (nullptr -> SIMT kernel)
     const CUtensorMap *tmv = nullptr;
     bool force_simt = false;
     size_t max_ws_bytes = 0;  // 0: the split may use any amount of scratch; else it must fit in this many bytes
@@ -188,6 +188,11 @@ bool decode_tc_supported(int D, int G);
 cudaError_t launch_attend_decode_tc(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
                                     const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,
                                     float2 *part_ml, int sm_count);
+// TMA-fed decode over an fp32 cache (attn_decode_f32.cu); tk / tv: 32-key x 32-float boxes, 128-byte swizzle.
+bool decode_f32_supported(int D, int G);
+cudaError_t launch_attend_decode_f32(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
+                                     const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,
+                                     float2 *part_ml, int sm_count);
 // Tensor-core decode over an INT8 cache (attn_decode_i8.cu); tk / tv: 64-byte-swizzled int8 tensor maps.
 cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
                                     const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,

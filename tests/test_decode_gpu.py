@@ -191,3 +191,39 @@ def test_device_pos_out_of_range_reported(pkg, ctx):
     assert e.value.name == "INVALID_ARGUMENT"
     ctx.synchronize()  # error word cleared
     assert torch.all(out[1] == 0)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "int8"])
+@pytest.mark.parametrize("hd,nh,nkv", [(64, 14, 2), (128, 8, 2), (64, 2, 2)])
+def test_many_items_per_cta(pkg, ctx, orc, dtype, hd, nh, nkv):
+    """Batches whose (sequence, kv head, chunk) items outnumber the SMs, so every persistent CTA runs several
+    items and its TMA ring is reused across them and across consumer warps (the regime of the benchmarks).
+    Sampled sequences against the restatement; INT8 through the codes it stored."""
+    rng = np.random.default_rng(hd + nh + 7)
+    B, T = 200, 700
+    dt = {"f32": pkg.F32, "bf16": pkg.BF16, "int8": pkg.INT8}[dtype]
+    kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, dt)
+    pos = rng.integers(T // 2, T, B).astype(np.int32)
+    pos[:3] = [T - 1, 0, 63]
+    sample = [0, 1, 2, 77, 150, B - 1]
+    rows = {}
+    for b in range(B):
+        k = rng.standard_normal((T, nkv * hd)).astype(np.float32)
+        v = rng.standard_normal((T, nkv * hd)).astype(np.float32)
+        kv.upload(0, b, 0, k, v)
+        if b in sample:
+            rows[b] = (k, v)
+    q = rng.standard_normal((B, nh * hd)).astype(np.float32)
+    scale = 1.0 / np.sqrt(hd)
+    for _ in range(2):  # a second call reuses the context's scratch and the layer's tensor maps
+        out = kv.attend_decode(0, q, pos, nh, scale)
+    for b in sample:
+        if dtype == "int8":
+            kc, vc, ks, vs = kv.download_int8(0, b, 0, T)
+            ref = orc.attend_decode_i8(q[b], kc, ks, vc, vs, int(pos[b]), nh, nkv, hd, scale)
+        else:
+            k, v = rows[b]
+            if dtype == "bf16":
+                k, v = orc.round_bf16(k).reshape(k.shape), orc.round_bf16(v).reshape(v.shape)
+            ref = orc.attend_decode(q[b], k, v, int(pos[b]), nh, nkv, hd, scale)
+        assert rel_l2(out[b], ref) <= TOL, (b, int(pos[b]))
