@@ -17,8 +17,8 @@
 //     P V      lane = head dims (D / 32 each): the probabilities broadcast from a per-warp buffer, the V rows
 //              from the swizzled tile; keys past pos are skipped, so stale rows are never read.
 // The SIMT kernel of attn_decode.cu reads K and V straight from global memory with one dependent load per
-// key in P V; this one keeps NS 32-key tiles in flight per SM (8 at head_dim 64 with 8 consumer warps, 4 at
-// 128 with 4).
+// key in P V; this one keeps NS 32-key tiles in flight per SM (12 at head_dim 64, 4 at 128), with 4
+// consumer warps (more warps would take the shared memory the deeper ring needs).
 #include <math.h>
 
 #include "internal.h"
@@ -37,7 +37,7 @@ constexpr int HS = 8;           // head slots (G <= 8)
 // complete out of order).  Items are separated by the merge barrier.
 template <int D>
 struct F32Cfg {
-    static constexpr int NW = D == 64 ? 8 : 4;       // consumer warps
+    static constexpr int NW = 4;                     // consumer warps
     static constexpr int THREADS = 32 * (NW + 1);
     static constexpr int BOX = KT * 128;              // 32 keys x 32 floats, 128-byte swizzle
     static constexpr int TILE = (D / 32) * BOX;       // K (or V) tile bytes
