@@ -752,6 +752,118 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
     return line
 
 
+RC_B, RC_H, RC_D, RC_STEPS, RC_NIN = 64, 16, 128, 1024, 16  # BASELINE configs[2]; RC_NIN input sets, cycled
+RC_LAYERS = 2  # states alternated step by step: 2 x 64 MiB > L2, so every step streams its state from HBM
+
+
+def run_recurrent(args, torch, dist, rank, world, local_rank):
+    """the Gated DeltaNet delta rule over 64 sequences x 16 heads, d_k = d_v = 128, fp32
+    state ~ N(0, 0.02), 1024 sequential decode steps (one bench step = the 1024 steps): q, k ~ N(0,1)
+    L2-normalised per head, v ~ N(0,1), beta = sigmoid(N(0,1)), log-decay g = -softplus(N(0,1)) (alpha = e^g),
+    q_scale = 1/sqrt(d_k).  RC_NIN seeded input sets are cycled over the steps.  The state of one layer
+    (64 MiB) would stay in the 126 MB L2 from one step to the next; the engine interleaves layers, so its
+    state goes back to HBM every step (BASELINE's configs[2] note): the steps alternate between RC_LAYERS
+    layers' states, and each bench step is 1024 rule steps (512 per layer)."""
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    torch.cuda.set_device(local_rank)
+    GB = args.batch or RC_B
+    sh = pkg.shard.shard(GB, RC_H, world, rank)  # (sequence, head) units
+    B, H = sh.nb, sh.nh
+    ctx = pkg.Context(local_rank)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(31 + rank)
+    st = pkg.DeltaState(ctx, RC_LAYERS, B, H, RC_D, RC_D, 0)
+    for layer in range(RC_LAYERS):
+        s_ptr, _ = st.layer_ptrs(layer)
+        torch.as_tensor(CudaArray(s_ptr, (B * H * RC_D * RC_D,), "<f4"), device=dev).normal_(0, 0.02, generator=gen)
+
+    def l2n(x):
+        return x / x.norm(dim=-1, keepdim=True)
+    ins = []
+    for _ in range(RC_NIN):
+        q = l2n(torch.randn(B, H, RC_D, device=dev, generator=gen)).reshape(B, H * RC_D).contiguous()
+        k = l2n(torch.randn(B, H, RC_D, device=dev, generator=gen)).reshape(B, H * RC_D).contiguous()
+        v = torch.randn(B, H * RC_D, device=dev, generator=gen)
+        beta = torch.sigmoid(torch.randn(B, H, device=dev, generator=gen))
+        g = -torch.nn.functional.softplus(torch.randn(B, H, device=dev, generator=gen))
+        ins.append((q, k, v, beta, g))
+    o = torch.empty(B, H * RC_D, device=dev)
+    q_scale = 1.0 / math.sqrt(RC_D)
+
+    def rule(i):
+        q, k, v, beta, g = ins[i % RC_NIN]
+        st.step_dev(i % RC_LAYERS, q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(), g.data_ptr(), q_scale,
+                    o.data_ptr())
+
+    for _ in range(args.warmup):
+        for i in range(RC_STEPS):
+            rule(i)
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(args.steps)]
+    clocks = ClockSampler(local_rank)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    l0 = ctx.launch_count
+    for s_ in range(args.steps):
+        ev[s_][0].record()
+        for i in range(RC_STEPS):
+            rule(i)
+        ev[s_][1].record()
+    torch.cuda.synchronize()
+    launches = ctx.launch_count - l0
+    clk = clocks.stop()
+    ctx.synchronize()
+    ms = float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
+    ms = pkg.shard.max_over_ranks(dist, ms, "cuda")
+    launch_ms = ms / RC_STEPS  # the timed region is the 1024 rule launches back to back, nothing else
+    # e2e through the host-pointer ABI: every step copies q / k / v / beta / g from pinned host memory and
+    # reads o back (the state stays on the device, as the engine's does)
+    hin = [tuple(x.cpu().pin_memory().numpy() for x in ins[i]) for i in range(RC_NIN)]
+    oh = torch.empty(B, H * RC_D).pin_memory().numpy()
+    ctx.set_stream(None)
+    st.step(0, *hin[0], q_scale, out=oh)
+    t0 = time.perf_counter()
+    for i in range(RC_STEPS):
+        st.step(i % RC_LAYERS, *hin[i % RC_NIN], q_scale, out=oh)
+    e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3, "cuda")
+    if rank != 0:
+        return None
+    hbm, _, src = peaks()
+    sbytes = 2.0 * B * H * RC_D * RC_D * 4
+    io_bytes = 4.0 * B * H * RC_D * 4 + 2.0 * B * H * 4
+    ach = (sbytes + io_bytes) / (launch_ms * 1e-3) / 1e9
+    h2d = sum(x.nbytes for x in hin[0]) * world
+    d2h = oh.nbytes * world
+    line = {"metric": "Gated DeltaNet recurrent decode tokens/s (BASELINE configs[2], 1024 sequential steps)",
+            "value": GB * RC_STEPS / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "config": {"workload": "deltanet_recurrent_decode (BASELINE configs[2])", "global_batch": GB,
+                       "heads": RC_H, "d_k": RC_D, "d_v": RC_D, "steps_per_bench_step": RC_STEPS,
+                       "l2": f"state streamed from HBM every step ({RC_LAYERS} layers' states alternated, as "
+                             "the engine interleaves layers); inputs cycled",
+                       "parallelism": f"(sequence, head) units over {world} rank(s), no collective"},
+            "e2e": {"value": GB * RC_STEPS / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": h2d * RC_STEPS, "d2h_bytes_per_step": d2h * RC_STEPS,
+                    "path": "host-pointer C ABI eif_cuda_deltanet_step (pinned), 1024 calls"},
+            "roofline": {"kernel": "delta_rule_kernel", "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                         "frac": ach / hbm, "peak_source": src, "algorithmic_bytes_per_launch": sbytes + io_bytes,
+                         "launch_ms": launch_ms, "traffic": None},
+            "gpu_launches": launches, "clocks": clk}
+    if world == 1 and not args.no_cpu_baseline:
+        tps, cores, kind, sample = cpu_chunked_reference()
+        line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": kind,
+                                "sample": sample + " (the engine runs config 3's rule inside deltanet_core)"}
+    return line
+
+
 DC_HQ, DC_HKV, DC_D, DC_THETA = 14, 2, 64, 1e6  # BASELINE configs[0]'s heads (Qwen2.5-0.5B), NeoX RoPE
 DC_B, DC_CTX = 256, 4096  # the batched variant; configs[0] itself is --batch 1 --ctx 512 --kv f32
 KV_ELT = {"f32": 4, "bf16": 2, "int8": 1}
@@ -941,9 +1053,10 @@ def run_decode(args, torch, dist, rank, world, local_rank):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", default="hybrid", choices=["hybrid", "prefill", "chunked", "decode"],
+    ap.add_argument("--workload", default="hybrid", choices=["hybrid", "prefill", "chunked", "decode", "recurrent"],
                     help="hybrid = BASELINE configs[4] (the headline); prefill = configs[1]; chunked = configs[3]; "
-                         "decode = configs[0]'s tinyllm heads, batched (--kv f32 | bf16 | int8, --ctx)")
+                         "recurrent = configs[2]; decode = configs[0]'s tinyllm heads, batched (--kv f32 | bf16 | "
+                         "int8, --ctx)")
     ap.add_argument("--kv", default="f32", choices=["f32", "bf16", "int8"], help="decode workload: cache dtype")
     ap.add_argument("--ctx", type=int, default=None, help="decode workload: context length (default 4096)")
     ap.add_argument("--gpus", type=int, default=1)
@@ -977,8 +1090,9 @@ def main():
         torch.cuda.set_device(local_rank)
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         dist = tdist
-    if args.workload in ("prefill", "chunked", "decode"):
-        run = {"prefill": run_prefill, "chunked": run_chunked, "decode": run_decode}[args.workload]
+    if args.workload in ("prefill", "chunked", "decode", "recurrent"):
+        run = {"prefill": run_prefill, "chunked": run_chunked, "decode": run_decode,
+               "recurrent": run_recurrent}[args.workload]
         line = run(args, torch, dist, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)

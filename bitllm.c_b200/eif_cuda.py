@@ -451,10 +451,11 @@ class DeltaState:
                        "delta_layer_ptrs")
         return s.value, c.value
 
-    def step(self, layer: int, q, k, v, beta, g, q_scale: float):
-        """One token of the delta rule for every sequence: returns o [batch][H*d_v]."""
+    def step(self, layer: int, q, k, v, beta, g, q_scale: float, out=None):
+        """One token of the delta rule for every sequence: returns o [batch][H*d_v] (written into `out` when
+        given, e.g. a pinned host array)."""
         qq, kk, vv, bb, gg = _f32(q), _f32(k), _f32(v), _f32(beta), _f32(g)
-        o = np.zeros((self.batch, self.H * self.dv), np.float32)
+        o = _out(out, (self.batch, self.H * self.dv))
         self.ctx.check(lib().eif_cuda_deltanet_step(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv),
                                                     _ptr(bb), _ptr(gg), float(q_scale), _ptr(o)), "deltanet_step")
         return o
