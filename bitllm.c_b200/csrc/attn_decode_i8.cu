@@ -7,7 +7,8 @@
 //
 // Structure (persistent, one CTA per SM, 4 NG + 1 warps):
 //   last warp, producer: one lane streams K and V tiles of 64 keys x D int8 codes through an NS-stage ring
-//           with 3-D TMA tile loads (boxes of 64 keys x 64 bytes, 64-byte swizzle, no multicast) and copies
+//           with 3-D TMA tile loads (boxes of 64 keys x 128 bytes with the 128-byte swizzle at head_dim >= 128,
+//           64 keys x 64 bytes with the 64-byte swizzle at head_dim 64; no multicast) and copies
 //           the tile's 64 K and 64 V scales (aligned 256-byte runs of the head-major scale rows) into the
 //           same stage with bulk asynchronous copies on the same "full" mbarrier;
 //   warps 0 .. 4NG-1 consumers in NG groups of 4 that take tiles round-robin, so NG tiles are in flight
@@ -48,8 +49,9 @@ template <int D, int NG>
 struct I8Cfg {
     static constexpr int NW = kGroup * NG;            // consumer warps
     static constexpr int THREADS = 32 * (NW + 1);
-    static constexpr int BOX = 64 * 64;               // 64 keys x 64 code bytes, 64-byte swizzle
-    static constexpr int TILE = (D / 64) * BOX;       // K (or V) tile bytes
+    static constexpr int BW = D >= 128 ? 128 : 64;    // box width in code bytes (= dims); the swizzle span
+    static constexpr int BOX = 64 * BW;               // 64 keys x BW code bytes
+    static constexpr int TILE = (D / BW) * BOX;       // K (or V) tile bytes
     static constexpr int STAGE = 2 * TILE;
     static constexpr int SCALES = 2 * KT * 4;         // per stage: the K and V scales of the tile's keys
     static constexpr int EXTRA = NW * HS * D * 4              // merge buffer o
@@ -126,10 +128,15 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Shared-memory address of the 16-byte chunk `chunk` (16 dims) of row `key` in a tile of D/64 boxes, each
-// 64 keys x 64 bytes with the TMA 64-byte swizzle (bits 4-5 of the offset XOR bits 7-8).
+// Shared-memory address of the 16-byte chunk `chunk` (16 dims) of row `key` in a tile of boxes of 64 keys x
+// BW bytes: the TMA 128-byte swizzle XORs the chunk index with the row index mod 8 (BW 128), the 64-byte
+// swizzle bits 4-5 of the offset with bits 7-8 (BW 64).
+template <int BW>
 __device__ __forceinline__ uint32_t tile_addr(uint32_t base, int key, int chunk) {
-    return base + (chunk >> 2) * 4096 + key * 64 + (((chunk & 3) ^ ((key >> 1) & 3)) << 4);
+    if constexpr (BW == 128)
+        return base + (chunk >> 3) * 8192 + key * 128 + (((chunk & 7) ^ (key & 7)) << 4);
+    else
+        return base + (chunk >> 2) * 4096 + key * 64 + (((chunk & 3) ^ ((key >> 1) & 3)) << 4);
 }
 
 template <int D, int NG>
@@ -180,9 +187,9 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
                 mbar_arrive_expect_tx(fb, C::STAGE + C::SCALES);
                 const uint32_t kdst = smem_u32(smem + s * C::STAGE), vdst = kdst + C::TILE;
 #pragma unroll
-                for (int j = 0; j < D / 64; ++j) {
-                    tma_load_3d(kdst + j * C::BOX, &tmK, j * 64, inf.kvh, row, fb);
-                    tma_load_3d(vdst + j * C::BOX, &tmV, j * 64, inf.kvh, row, fb);
+                for (int j = 0; j < D / C::BW; ++j) {
+                    tma_load_3d(kdst + j * C::BOX, &tmK, j * C::BW, inf.kvh, row, fb);
+                    tma_load_3d(vdst + j * C::BOX, &tmV, j * C::BW, inf.kvh, row, fb);
                 }
                 const size_t srow = ((size_t)inf.b * p.Hkv + inf.kvh) * p.sstride + t0;
                 const uint32_t sdst = smem_u32(sbuf + s * 2 * KT);
@@ -251,7 +258,7 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
 #pragma unroll
             for (int kp = 0; kp < KS / 2; ++kp) {
                 uint32_t r0, r1, r2, r3;  // (keys 0-7 | 8-15) x (chunk 2kp | 2kp+1)
-                ldsm_x4(tile_addr(kbase, my_key, 2 * kp + (mi >> 1)), r0, r1, r2, r3);
+                ldsm_x4(tile_addr<C::BW>(kbase, my_key, 2 * kp + (mi >> 1)), r0, r1, r2, r3);
                 r0 ^= 0x80808080u;
                 r1 ^= 0x80808080u;
                 r2 ^= 0x80808080u;
@@ -310,7 +317,7 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
 #pragma unroll
             for (int cp = 0; cp < D / 32; ++cp) {
                 uint32_t r0, r1, r2, r3;
-                ldsm_x4_t(tile_addr(vbase, my_key, 2 * cp + (mi >> 1)), r0, r1, r2, r3);
+                ldsm_x4_t(tile_addr<C::BW>(vbase, my_key, 2 * cp + (mi >> 1)), r0, r1, r2, r3);
                 r0 ^= 0x80808080u;
                 r1 ^= 0x80808080u;
                 r2 ^= 0x80808080u;

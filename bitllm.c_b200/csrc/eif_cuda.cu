@@ -136,8 +136,8 @@ EncodeTiledFn encode_tiled() {
 
 // TMA descriptor of one cache array [batch*max_seq][n_kv][hd] as a 3-D tensor (hd, n_kv, rows) with the boxes
 // and swizzle each decode kernel's shared-memory addressing expects: bf16 64 dims x 64 keys (128-byte rows,
-// 128-byte swizzle), INT8 64 dims x 64 keys (64-byte rows, 64-byte swizzle), fp32 32 dims x 32 keys
-// (128-byte rows, 128-byte swizzle).
+// 128-byte swizzle), INT8 128 dims x 64 keys (128-byte rows, 128-byte swizzle; 64 dims and the 64-byte
+// swizzle at head_dim 64), fp32 32 dims x 32 keys (128-byte rows, 128-byte swizzle).
 bool make_kv_tensor_map(CUtensorMap *map, void *base, const eif_cuda_kv_t *kv) {
     EncodeTiledFn enc = encode_tiled();
     if (!enc || kv->hd % 64) return false;
@@ -145,7 +145,9 @@ bool make_kv_tensor_map(CUtensorMap *map, void *base, const eif_cuda_kv_t *kv) {
     const cuuint64_t elt = i8 ? 1 : f32 ? 4 : 2;
     const cuuint64_t dims[3] = {(cuuint64_t)kv->hd, (cuuint64_t)kv->n_kv, (cuuint64_t)kv->batch * kv->max_seq};
     const cuuint64_t strides[2] = {(cuuint64_t)kv->hd * elt, (cuuint64_t)kv->n_kv * kv->hd * elt};
-    const cuuint32_t box[3] = {f32 ? 32u : 64u, 1, f32 ? 32u : 64u};
+    // INT8: 128-byte rows (128 dims) from head_dim 128 up; 64-byte rows at head_dim 64
+    const cuuint32_t box0 = f32 ? 32u : (i8 && kv->hd >= 128) ? 128u : 64u;
+    const cuuint32_t box[3] = {box0, 1, f32 ? 32u : 64u};
     const cuuint32_t es[3] = {1, 1, 1};
     // L2 promotion no wider than one kv head's row: the rows of the other kv heads in between belong to other
     // work items, and a wider promotion would fetch them from HBM with every tile
@@ -154,7 +156,8 @@ bool make_kv_tensor_map(CUtensorMap *map, void *base, const eif_cuda_kv_t *kv) {
                                          : head_row >= 128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
                                                            : CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
     return enc(map, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides,
-               box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, i8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+               box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               (i8 && kv->hd < 128) ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
