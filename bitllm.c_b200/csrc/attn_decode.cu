@@ -185,34 +185,55 @@ __global__ void __launch_bounds__(256) attn_decode_combine_kernel(
     float *rowbuf = smem + Hq * nchunk;  // [Hq*D]
     __shared__ float red[32];
 
-    for (int hc = threadIdx.x; hc < Hq; hc += blockDim.x) {
+    // chunk weights: one warp per head, lanes over the chunks
+    const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int hc = threadIdx.x >> 5; hc < Hq; hc += nw) {
         const int kvh = hc / G, g = hc % G;
-        const size_t base = ((size_t)b * Hkv + kvh) * nchunk;
+        const float2 *ml = part_ml + ((size_t)b * Hkv + kvh) * nchunk * G + g;  // chunk c at ml[c * G]
         float M = -INFINITY;
-        for (int c = 0; c < nchunk; ++c) M = fmaxf(M, part_ml[(base + c) * G + g].x);
+        for (int c = lane; c < nchunk; c += 32) M = fmaxf(M, ml[(size_t)c * G].x);
+        M = warp_max(M);
         float Ls = 0.f;
         if (M != -INFINITY)
-            for (int c = 0; c < nchunk; ++c) {
-                const float2 ml = part_ml[(base + c) * G + g];
-                Ls += ml.y * expf(ml.x - M);
+            for (int c = lane; c < nchunk; c += 32) {
+                const float2 v = ml[(size_t)c * G];
+                Ls += v.y * expf(v.x - M);
             }
-        for (int c = 0; c < nchunk; ++c) {
-            const float2 ml = part_ml[(base + c) * G + g];
-            w[hc * nchunk + c] = (M == -INFINITY || Ls == 0.f) ? 0.f : expf(ml.x - M) / Ls;
-        }
+        Ls = warp_sum(Ls);
+        for (int c = lane; c < nchunk; c += 32)
+            w[hc * nchunk + c] = (M == -INFINITY || Ls == 0.f) ? 0.f : expf(ml[(size_t)c * G].x - M) / Ls;
     }
     __syncthreads();
 
+    // weighted sum over the chunks, kCombineRun row elements per thread at once (their loads of a chunk are
+    // independent, so they are in flight together)
+    constexpr int kCombineRun = 8;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < row; i += blockDim.x) {
-        const int h = i / D, d = i % D;
-        const int kvh = h / G, g = h % G;
-        const size_t base = ((size_t)b * Hkv + kvh) * nchunk;
-        float o = 0.f;
-        for (int c = 0; c < nchunk; ++c) o += part_o[((base + c) * G + g) * D + d] * w[h * nchunk + c];
-        if (gate) o *= 1.0f / (1.0f + expf(-gate[(size_t)b * row + i]));
-        rowbuf[i] = o;
-        ss += o * o;
+    for (int i0 = threadIdx.x; i0 < row; i0 += kCombineRun * blockDim.x) {
+        const float *po[kCombineRun];
+        const float *wh[kCombineRun];
+        float o[kCombineRun];
+#pragma unroll
+        for (int k = 0; k < kCombineRun; ++k) {
+            const int i = min(i0 + k * (int)blockDim.x, row - 1);  // clamped lanes compute a copy, not stored
+            const int h = i / D, d = i % D;
+            const int kvh = h / G, g = h % G;
+            po[k] = part_o + (((size_t)b * Hkv + kvh) * nchunk * G + g) * D + d;
+            wh[k] = w + h * nchunk;
+            o[k] = 0.f;
+        }
+        for (int c = 0; c < nchunk; ++c)
+#pragma unroll
+            for (int k = 0; k < kCombineRun; ++k) o[k] += po[k][(size_t)c * G * D] * wh[k][c];
+#pragma unroll
+        for (int k = 0; k < kCombineRun; ++k) {
+            const int i = i0 + k * (int)blockDim.x;
+            if (i >= row) break;
+            float v = o[k];
+            if (gate) v *= 1.0f / (1.0f + expf(-gate[(size_t)b * row + i]));
+            rowbuf[i] = v;
+            ss += v * v;
+        }
     }
     if (subln != EIF_CUDA_SUBLN_NONE) {
         ss = warp_sum(ss);
@@ -264,7 +285,15 @@ Split choose_split_tc(const DecodeArgs &a, int sm_count) {
     // K + V bytes of a 64-key tile (INT8: codes plus the two scales of every key)
     const double tile_bytes = a.dtype == EIF_CUDA_INT8 ? 64.0 * (a.D * 2 + 8)
                               : 64.0 * a.D * 2 * (a.dtype == EIF_CUDA_F32 ? 4 : 2);
-    const double part_bytes = 2.0 * (a.Hq / a.Hkv) * a.D * 4;
+    // Cost of a split, in bytes streamed by the busiest CTA (items go round-robin over the persistent
+    // CTAs): its tiles plus a fixed cost per item.  The bf16 kernel at head_dim 256 (three 64 KB stages
+    // per CTA) was measured elastic: a CTA with more items than the others streams up to half again its
+    // fair share of HBM while they idle, so the whole job's bytes per SM bound it first, and an
+    // item (q load, merge of the four warps, its share of the combine) costs about 64 KB of streaming;
+    // the others were measured best at the most even split, with the partial's bytes as the item cost.
+    const bool elastic = a.dtype == EIF_CUDA_BF16 && a.D >= 256;
+    const double item_bytes = elastic ? 65536.0 : 2.0 * (a.Hq / a.Hkv) * a.D * 4;
+    const double fair = (double)units * tpu * tile_bytes / sm_count;
     int best = 1;
     double best_cost = 1e300;
     for (int nc = 1; nc <= 64 && nc <= tpu; ++nc) {
@@ -273,7 +302,8 @@ Split choose_split_tc(const DecodeArgs &a, int sm_count) {
         const long items = units * ncu;
         if (a.max_ws_bytes && ncu > 1 && partials_bytes(a, (int)ncu) > a.max_ws_bytes) break;
         const long per_cta = (items + sm_count - 1) / sm_count;
-        const double cost = per_cta * ct * tile_bytes + per_cta * part_bytes;
+        const double busiest = per_cta * ct * tile_bytes;
+        const double cost = (elastic ? fmax(fair, busiest / 1.5) : busiest) + per_cta * item_bytes;
         if (cost < best_cost * 0.999) {
             best_cost = cost;
             best = (int)ncu;

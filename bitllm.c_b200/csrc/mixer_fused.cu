@@ -6,13 +6,20 @@
 //   delta rule (:594-639) and the gated RMSNorm o * rsqrt(mean(o^2) + 1e-6) * norm_w * silu(z)
 //   (:642-653).  One CTA per (sequence, head): it owns that head's q, k and v conv channels (so every
 //   conv-window row is updated by exactly one CTA) and all d_v columns of S (so the RMSNorm of the
-//   head's output row closes inside the CTA).  S makes one trip HBM -> registers -> HBM.
+//   head's output row closes inside the CTA).  S crosses HBM once each way.
+//   S is read from global memory twice and never staged: the retrieve pass from HBM, the update pass
+//   from L2, where the first pass just left it (at four CTAs of 256 threads per SM at most 38 MB of
+//   state is in flight, well inside L2).  Without a shared-memory copy of S, four CTAs fit per SM and
+//   up to 4 x SMs heads run in one wave (a copy of the head's S in shared memory allows three, and at
+//   small batches its second wave of a few CTAs set the time).
 //
 // fullatt_prep_kernel: fullatt_prep (src/eif_qwen35.c:699-737) for one token of every sequence:
 //   split the interleaved [q | gate] heads, RMSNorm q and k per head with q_norm / k_norm (eps 1e-6),
 //   rotate the first head_dim/4 dims of q and k (half-split pairs, theta 1e7: rope_partial,
 //   :502-535) with a cos / sin table computed on the host by the reference's formula, and write k, v
-//   into cache row pos[b].
+//   into cache row pos[b].  fullatt_prep_warp_kernel does the same with one warp per (row, head) and
+//   vector loads (head_dim 64 / 128 / 256, aligned rows); fullatt_prep_kernel, one CTA per row with
+//   scalar accesses, takes every other shape.
 #include <math.h>
 
 #include "internal.h"
@@ -24,7 +31,7 @@ namespace {
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
 template <int DK, int DV, int THREADS>
-__global__ void __launch_bounds__(THREADS) deltanet_core_kernel(const DeltaCoreArgs a) {
+__global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCoreArgs a) {
     constexpr int LPR = DV / 4;        // threads per S row (float4 each)
     constexpr int RP = THREADS / LPR;  // rows per pass
     constexpr int NP = DK / RP;        // passes
@@ -41,22 +48,9 @@ __global__ void __launch_bounds__(THREADS) deltanet_core_kernel(const DeltaCoreA
     __shared__ float red[NW];
     __shared__ float4 cred[NW][LPR];
     __shared__ float gates[2];
-    __shared__ __align__(8) uint64_t s_bar;
-    extern __shared__ __align__(128) float Ssm[];  // the head's S [DK][DV]
 
-    // the head's state (contiguous DK*DV floats) streams into shared memory while the conv / norm / gate
-    // work below runs: one thread issues bulk copies completing on s_bar (waited on after later barriers)
     float *Sh = a.S + bh * DK * DV;
     const int col0 = lc * 4;
-    const uint32_t sbar = smem_u32(&s_bar);
-    if (tid == 0) {
-        constexpr uint32_t bytes = DK * DV * 4, piece = bytes < 16384 ? bytes : 16384;
-        mbar_init(sbar, 1);
-        fence_barrier_init();
-        mbar_arrive_expect_tx(sbar, bytes);
-        for (uint32_t off = 0; off < bytes; off += piece)
-            bulk_load(smem_u32(Ssm) + off, reinterpret_cast<const char *>(Sh) + off, piece, sbar);
-    }
 
     // causal conv1d + SiLU on this head's channels: q [h*DK, +DK), k [key_dim + h*DK, +DK), v [2*key_dim + h*DV, +DV)
     const int ck = a.conv_k;
@@ -124,30 +118,45 @@ __global__ void __launch_bounds__(THREADS) deltanet_core_kernel(const DeltaCoreA
 
     const float decay = expf(gates[1]), bet = gates[0];
     // a wait that gives up leaves S untouched (the error word tells the host)
-    const bool s_ok = mbar_wait(sbar, 0, a.dev_err);
-    const float4 *Srow = reinterpret_cast<const float4 *>(Ssm) + col0 / 4;
+    const float4 *Srow = reinterpret_cast<const float4 *>(Sh) + col0 / 4;
+    // rows go in batches of SB loads before their arithmetic, so that the loads of a batch are in flight
+    // together (the update pass stores to the rows it reads, and the compiler would not move a later
+    // load above such a store)
+    constexpr int SB = NP < 8 ? NP : 8;
     float4 e = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int p = 0; p < NP; ++p) {
-        const float ki = sk[rg + p * RP];
-        float4 s = Srow[(rg + p * RP) * (DV / 4)];
-        s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;
-        e.x += s.x * ki; e.y += s.y * ki; e.z += s.z * ki; e.w += s.w * ki;
+    for (int p0 = 0; p0 < NP; p0 += SB) {
+        float4 sr[SB];
+#pragma unroll
+        for (int u = 0; u < SB; ++u) sr[u] = Srow[(rg + (p0 + u) * RP) * (DV / 4)];
+#pragma unroll
+        for (int u = 0; u < SB; ++u) {
+            const float ki = sk[rg + (p0 + u) * RP];
+            float4 s = sr[u];
+            s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;
+            e.x += s.x * ki; e.y += s.y * ki; e.z += s.z * ki; e.w += s.w * ki;
+        }
     }
     e = colsum(e);
     const float4 vv = make_float4(sv[col0], sv[col0 + 1], sv[col0 + 2], sv[col0 + 3]);
     const float4 dlt = make_float4(vv.x - e.x, vv.y - e.y, vv.z - e.z, vv.w - e.w);
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int p = 0; p < NP; ++p) {
-        const int i = rg + p * RP;
-        const float ki = bet * sk[i];
-        float4 s = Srow[i * (DV / 4)];
-        s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;  // as in the first pass
-        s.x += ki * dlt.x; s.y += ki * dlt.y; s.z += ki * dlt.z; s.w += ki * dlt.w;
-        if (s_ok) __stcs(reinterpret_cast<float4 *>(Sh + (size_t)i * DV + col0), s);
-        const float qi = sq[i];
-        o.x += s.x * qi; o.y += s.y * qi; o.z += s.z * qi; o.w += s.w * qi;
+    for (int p0 = 0; p0 < NP; p0 += SB) {
+        float4 sr[SB];
+#pragma unroll
+        for (int u = 0; u < SB; ++u) sr[u] = Srow[(rg + (p0 + u) * RP) * (DV / 4)];
+#pragma unroll
+        for (int u = 0; u < SB; ++u) {
+            const int i = rg + (p0 + u) * RP;
+            const float ki = bet * sk[i];
+            float4 s = sr[u];
+            s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;  // as in the first pass
+            s.x += ki * dlt.x; s.y += ki * dlt.y; s.z += ki * dlt.z; s.w += ki * dlt.w;
+            __stcs(reinterpret_cast<float4 *>(Sh + (size_t)i * DV + col0), s);
+            const float qi = sq[i];
+            o.x += s.x * qi; o.y += s.y * qi; o.z += s.z * qi; o.w += s.w * qi;
+        }
     }
     o = colsum(o);
     // gated RMSNorm over the head's d_v outputs (threads of row group 0 hold the whole row)
@@ -224,25 +233,154 @@ __global__ void __launch_bounds__(256) fullatt_prep_kernel(const AttnPrepArgs a)
         }
 }
 
+// The same prep with one warp per (token row, head) -- q heads, k heads, then one warp for the row's v --
+// and every lane holding VPL = hd / 32 consecutive elements: each row of q, gate, k, v and the norm
+// weights is read with one vector load per lane, all before any store, and the rotation partner
+// (element i +- n_rot / 2) comes from lane +- n_rot / (2 VPL) by a shuffle.  Same arithmetic per element
+// as fullatt_prep_kernel; the sum of squares is taken in another order (within float rounding).
+template <int VPL>
+__device__ __forceinline__ void load_vec(float (&x)[VPL], const float *src) {
+    if constexpr (VPL == 2) {
+        const float2 t = *reinterpret_cast<const float2 *>(src);
+        x[0] = t.x; x[1] = t.y;
+    } else {
+#pragma unroll
+        for (int k = 0; k < VPL; k += 4) {
+            const float4 t = *reinterpret_cast<const float4 *>(src + k);
+            x[k] = t.x; x[k + 1] = t.y; x[k + 2] = t.z; x[k + 3] = t.w;
+        }
+    }
+}
+template <int VPL>
+__device__ __forceinline__ void store_vec(float *dst, const float (&x)[VPL]) {
+    if constexpr (VPL == 2) {
+        *reinterpret_cast<float2 *>(dst) = make_float2(x[0], x[1]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < VPL; k += 4)
+            *reinterpret_cast<float4 *>(dst + k) = make_float4(x[k], x[k + 1], x[k + 2], x[k + 3]);
+    }
+}
+template <int VPL>
+__device__ __forceinline__ void store_vec_bf16(__nv_bfloat16 *dst, const float (&x)[VPL]) {
+    uint32_t w[VPL / 2];
+#pragma unroll
+    for (int k = 0; k < VPL / 2; ++k) w[k] = pack_bf16x2(x[2 * k], x[2 * k + 1]);
+    if constexpr (VPL == 2) *reinterpret_cast<uint32_t *>(dst) = w[0];
+    else if constexpr (VPL == 4) *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
+    else
+#pragma unroll
+        for (int k = 0; k < VPL / 2; k += 4) *reinterpret_cast<uint4 *>(dst + 2 * k) = make_uint4(w[k], w[k + 1], w[k + 2], w[k + 3]);
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(256) fullatt_prep_warp_kernel(const AttnPrepArgs a) {
+    const int hd = a.hd, nh = a.nh, nkv = a.nkv, half = a.n_rot / 2;
+    const int per_row = nh + nkv + 1;
+    const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (gw >= a.B * a.n_tok * per_row) return;  // warp-uniform; the kernel has no block barrier
+    const int r = gw / per_row, hh = gw % per_row, b = r / a.n_tok;
+    const int p = a.pos ? a.pos[b] : a.start_pos + r % a.n_tok;
+    const bool pos_ok = p >= 0 && p < a.max_seq;
+    if (hh == nh + nkv) {  // v row -> cache
+        if (!pos_ok) return;
+        const float *src = a.v + (size_t)r * nkv * hd;
+        const size_t row = ((size_t)b * a.max_seq + p) * nkv * hd;
+        for (int i = lane * VPL; i < nkv * hd; i += 32 * VPL) {
+            float x[VPL];
+            load_vec<VPL>(x, src + i);
+            if (a.dtype == EIF_CUDA_F32)
+                store_vec<VPL>(static_cast<float *>(a.Vc) + row + i, x);
+            else
+                store_vec_bf16<VPL>(static_cast<__nv_bfloat16 *>(a.Vc) + row + i, x);
+        }
+        return;
+    }
+    if (!pos_ok && hh == 0 && lane == 0) atomicOr(a.dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
+    const bool isq = hh < nh;
+    const int hi = isq ? hh : hh - nh, i0 = lane * VPL;
+    const float *src = isq ? a.qg + ((size_t)r * nh + hi) * 2 * hd : a.k + ((size_t)r * nkv + hi) * hd;
+    float x[VPL], w[VPL], g[VPL];
+    load_vec<VPL>(x, src + i0);
+    load_vec<VPL>(w, (isq ? a.q_norm : a.k_norm) + i0);
+    if (isq) load_vec<VPL>(g, src + hd + i0);
+    const bool rot = i0 < 2 * half;  // whole lanes: half is a multiple of VPL
+    float cs[VPL], sn[VPL];
+    if (rot) {
+        const int j0 = i0 < half ? i0 : i0 - half;
+        const float *c = a.rope_cos + (size_t)(pos_ok ? p : 0) * half + j0;
+        const float *t = a.rope_sin + (size_t)(pos_ok ? p : 0) * half + j0;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            cs[k] = c[k];
+            sn[k] = t[k];
+        }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) ss += x[k] * x[k];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / hd + 1e-6f);
+    float y[VPL];
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) y[k] = x[k] * inv * w[k];
+    const int dl = half / VPL;
+    const int partner = !rot ? lane : (i0 < half ? lane + dl : lane - dl);
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+        const float o = __shfl_sync(0xffffffffu, y[k], partner);
+        if (rot) {
+            const float x0 = i0 < half ? y[k] : o, x1 = i0 < half ? o : y[k];
+            y[k] = i0 < half ? x0 * cs[k] - x1 * sn[k] : x0 * sn[k] + x1 * cs[k];
+        }
+    }
+    if (isq) {
+        const size_t qrow = ((size_t)r * nh + hi) * hd + i0;
+        if (a.q_out_bf16)
+            store_vec_bf16<VPL>(a.q_out_bf16 + qrow, y);
+        else
+            store_vec<VPL>(a.q_out + qrow, y);
+        store_vec<VPL>(a.gate_out + qrow, g);
+    } else if (pos_ok) {
+        const size_t row = (((size_t)b * a.max_seq + p) * nkv + hi) * hd + i0;
+        if (a.dtype == EIF_CUDA_F32)
+            store_vec<VPL>(static_cast<float *>(a.Kc) + row, y);
+        else
+            store_vec_bf16<VPL>(static_cast<__nv_bfloat16 *>(a.Kc) + row, y);
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *supported) {
     *supported = true;
     const dim3 grid(a.H, a.B);
-    auto run = [&](auto kernel, int threads, int smem) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        kernel<<<grid, threads, smem, st>>>(a);
+    auto run = [&](auto kernel, int threads) {
+        kernel<<<grid, threads, 0, st>>>(a);
         return cudaGetLastError();
     };
-    if (a.dk == 128 && a.dv == 128) return run(deltanet_core_kernel<128, 128, 256>, 256, 128 * 128 * 4);
-    if (a.dk == 128 && a.dv == 64) return run(deltanet_core_kernel<128, 64, 256>, 256, 128 * 64 * 4);
-    if (a.dk == 64 && a.dv == 64) return run(deltanet_core_kernel<64, 64, 128>, 128, 64 * 64 * 4);
+    if (a.dk == 128 && a.dv == 128) return run(deltanet_core_kernel<128, 128, 256>, 256);
+    if (a.dk == 128 && a.dv == 64) return run(deltanet_core_kernel<128, 64, 256>, 256);
+    if (a.dk == 64 && a.dv == 64) return run(deltanet_core_kernel<64, 64, 128>, 128);
     *supported = false;
     return cudaSuccess;
 }
 
 cudaError_t launch_fullatt_prep(cudaStream_t st, const AttnPrepArgs &a) {
-    fullatt_prep_kernel<<<a.B * a.n_tok, 256, 0, st>>>(a);
+    // the warp-per-head form needs hd in {64, 128, 256}, whole lanes of rotated pairs and vector-aligned rows
+    const int vpl = a.hd / 32, half = a.n_rot / 2;
+    auto al = [&](const void *q) { return ((uintptr_t)q % (vpl == 2 ? 8 : 16)) == 0; };
+    const bool warp_form = (a.hd == 64 || a.hd == 128 || a.hd == 256) && half % vpl == 0 && a.n_rot <= a.hd &&
+                           al(a.qg) && al(a.k) && al(a.v) && al(a.q_norm) && al(a.k_norm) && al(a.Kc) && al(a.Vc) &&
+                           al(a.gate_out) && (a.q_out_bf16 ? al(a.q_out_bf16) : al(a.q_out));
+    if (!warp_form) {
+        fullatt_prep_kernel<<<a.B * a.n_tok, 256, 0, st>>>(a);
+        return cudaGetLastError();
+    }
+    const long warps = (long)a.B * a.n_tok * (a.nh + a.nkv + 1);
+    const unsigned blocks = (unsigned)((warps + 7) / 8);
+    if (vpl == 2) fullatt_prep_warp_kernel<2><<<blocks, 256, 0, st>>>(a);
+    else if (vpl == 4) fullatt_prep_warp_kernel<4><<<blocks, 256, 0, st>>>(a);
+    else fullatt_prep_warp_kernel<8><<<blocks, 256, 0, st>>>(a);
     return cudaGetLastError();
 }

@@ -77,6 +77,83 @@ def test_fullatt_prep_golden(pkg, ctx):
     assert np.array_equal(vd[0], d["v_row"])
 
 
+def test_deltanet_core_batch_independent(pkg, ctx, orc):
+    """40 sequences x 16 heads (more heads than one wave of CTAs) and the first 5 of them alone give the
+    same bits (outputs and states), and the large batch matches the port."""
+    rng = np.random.default_rng(79)
+    H, d, ck = 16, 128, 4
+    conv_dim = 3 * H * d
+    w = dict(conv_w=(rng.standard_normal((conv_dim, ck)) * 0.5).astype(np.float32),
+             dt_bias=rng.standard_normal(H).astype(np.float32), A_log=(0.5 * rng.standard_normal(H)).astype(np.float32),
+             norm_w=(1 + 0.1 * rng.standard_normal(d)).astype(np.float32))
+    outs, states = {}, {}
+    S = (0.02 * rng.standard_normal((40, H, d, d))).astype(np.float32)
+    conv = rng.standard_normal((40, conv_dim, ck)).astype(np.float32)
+    xs = [(rng.standard_normal((40, conv_dim)).astype(np.float32), rng.standard_normal((40, H * d)).astype(np.float32),
+           rng.standard_normal((40, H)).astype(np.float32), rng.standard_normal((40, H)).astype(np.float32))
+          for _ in range(2)]
+    for B in (40, 5):
+        st = pkg.DeltaState(ctx, 1, B, H, d, d, ck)
+        st.set_weights(0, **w)
+        for b in range(B):
+            st.upload(0, b, S=S[b], conv_state=conv[b])
+        outs[B] = [st.core(0, *(x[:B] for x in xt)) for xt in xs]
+        states[B] = [st.download(0, b)[0] for b in range(5)]
+    for t in range(2):
+        assert np.array_equal(outs[40][t][:5], outs[5][t])
+    for b in range(5):
+        assert np.array_equal(states[40][b], states[5][b])
+    Sr, cr = S.copy(), conv.copy()
+    for t, (qkv, z, bb, aa) in enumerate(xs):
+        for b in (0, 17, 39):
+            ref = orc.deltanet_core(qkv[b], z[b], bb[b], aa[b], cr[b], Sr[b], **w)
+            assert rel_l2(outs[40][t][b], ref) <= TOL, (t, b)
+
+
+@pytest.mark.parametrize("hd", [64, 128, 256])
+def test_fullatt_prep_head_dims(pkg, ctx, orc, hd):
+    """fullatt_prep for 2 sequences at head_dim 64 / 128 / 256 (2, 4, 8 elements per lane in the
+    warp-per-head kernel), fp32 cache, against the restatement; then the same rows through the
+    device-pointer entry with every array one float off 16-byte alignment (the per-row kernel)."""
+    import torch
+    rng = np.random.default_rng(92 + hd)
+    B, nh, nkv, T = 2, 4, 2, 16
+    kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, pkg.F32)
+    qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kv.set_norms(0, qn, kn)
+    qg = rng.standard_normal((B, nh * 2 * hd)).astype(np.float32)
+    k = rng.standard_normal((B, nkv * hd)).astype(np.float32)
+    v = rng.standard_normal((B, nkv * hd)).astype(np.float32)
+    pos = np.array([3, 9], np.int32)
+    q, g = kv.fullatt_prep(0, qg, k, v, pos, nh)
+    kc = np.zeros((T, nkv * hd), np.float32)
+    for b in range(B):
+        rq, rg, rk = orc.fullatt_prep(qg[b], k[b], v[b], qn, kn, kc.copy(), kc.copy(), pos[b], nh, nkv, hd)
+        assert rel_l2(q[b], rq) <= TOL and np.array_equal(g[b], rg)
+        kd, vd = kv.download(0, b, pos[b], 1)
+        assert rel_l2(kd[0], rk) <= TOL and np.array_equal(vd[0], v[b])
+
+    def off(a):  # a device copy starting one float past a 16-byte boundary
+        t = torch.zeros(a.size + 1, dtype=torch.float32, device="cuda")
+        t[1:] = torch.from_numpy(np.ascontiguousarray(a).ravel()).cuda()
+        return t
+    tq, tk, tv = off(qg), off(k), off(v)
+    tqo, tgo = off(np.zeros_like(q)), off(np.zeros_like(g))
+    tpos = torch.from_numpy(pos + 1).cuda()
+    torch.cuda.synchronize()
+    kv.fullatt_prep_dev(0, tq.data_ptr() + 4, tk.data_ptr() + 4, tv.data_ptr() + 4, tpos.data_ptr(), nh,
+                        tqo.data_ptr() + 4, tgo.data_ptr() + 4)
+    ctx.synchronize()
+    q2 = tqo[1:].cpu().numpy().reshape(q.shape)
+    assert np.array_equal(tgo[1:].cpu().numpy().reshape(g.shape), g)
+    for b in range(B):  # rows at pos + 1
+        rq, _, rk = orc.fullatt_prep(qg[b], k[b], v[b], qn, kn, kc.copy(), kc.copy(), pos[b] + 1, nh, nkv, hd)
+        assert rel_l2(q2[b], rq) <= TOL
+        kd, vd = kv.download(0, b, pos[b] + 1, 1)
+        assert rel_l2(kd[0], rk) <= TOL and np.array_equal(vd[0], v[b])
+
+
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 def test_qwen35_attention_layer_chain(pkg, ctx, orc, dtype):
     """Several decode steps of a Qwen3.5 full-attention layer for a batch with ragged positions:
