@@ -931,8 +931,9 @@ def cpu_decode_reference(kv_name, L, seconds=10.0):
 def run_decode(args, torch, dist, rank, world, local_rank):
     """tinyllm GQA decode at BASELINE configs[0]'s head shape (14 q / 2 kv heads, head_dim 64, NeoX RoPE
     theta 1e6), batched: one decode step of one attention layer for `--batch` sequences at context `--ctx`
-    over an fp32, bf16 or INT8 (`--kv`) cache -- rope_append (RoPE of the new q and k, quantised or plain
-    cache write) then attend_decode over rows [0, ctx)."""
+    over an fp32, bf16 or INT8 (`--kv`) cache -- eif_cuda_decode_step: RoPE of the new q and k, the (plain or
+    quantised) cache write and attention over rows [0, ctx) in one call.  The roofline times the attention
+    alone (attend_decode_dev on the same rows)."""
     import __graft_entry__
     pkg = __graft_entry__.load_package()
     torch.cuda.set_device(local_rank)
@@ -974,16 +975,19 @@ def run_decode(args, torch, dist, rank, world, local_rank):
     bytes_alg = decode_bytes(B, L, hkv, kv_name)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if bytes_alg < (1 << 30) else None
 
-    def step(ev=None):
-        kv.rope_append_dev(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), hq, q_rot.data_ptr())
-        if ev is not None:
-            ev[1].record()
+    def step():
+        kv.decode_step_dev(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), L - 1, hq, scale,
+                           out.data_ptr())
+
+    def attend():
         kv.attend_decode_dev(0, q_rot.data_ptr(), pos.data_ptr(), L - 1, hq, scale, out.data_ptr())
 
+    kv.rope_append_dev(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), hq, q_rot.data_ptr())
     for _ in range(args.warmup):
         step()
+        attend()
     torch.cuda.synchronize()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     clocks = ClockSampler(local_rank)
     if dist:
         dist.barrier()
@@ -994,38 +998,43 @@ def run_decode(args, torch, dist, rank, world, local_rank):
         if flush is not None:
             flush.zero_()  # caches smaller than 1 GiB: evict them from L2 between steps
         ev[s][0].record()
-        step(ev[s])
-        ev[s][2].record()
+        step()
+        ev[s][1].record()
     torch.cuda.synchronize()
     launches = ctx.launch_count - l0
+    for s in range(args.steps):  # the attention alone, for the roofline
+        if flush is not None:
+            flush.zero_()
+        ev[s][2].record()
+        attend()
+        ev[s][3].record()
+    torch.cuda.synchronize()
     clk = clocks.stop()
     ctx.synchronize()
-    ms = float(np.mean([e[0].elapsed_time(e[2]) for e in ev]))
-    att_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in ev]))
+    ms = float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
+    att_ms = float(np.mean([e[2].elapsed_time(e[3]) for e in ev]))
     ms = pkg.shard.max_over_ranks(dist, ms, "cuda")
-    # e2e through the host-pointer ABI: pinned fp32 q / k / v / pos in, rotated q and the output back
+    # e2e through the host-pointer ABI: pinned fp32 q / k / v / pos in, the output back
     hg = torch.Generator().manual_seed(5)
     qh = torch.randn(B, hq * DC_D, generator=hg).pin_memory().numpy()
     kh = torch.randn(B, hkv * DC_D, generator=hg).pin_memory().numpy()
     vh = torch.randn(B, hkv * DC_D, generator=hg).pin_memory().numpy()
     ph = torch.full((B,), L - 1, dtype=torch.int32).pin_memory().numpy()
-    qr = torch.empty(B, hq * DC_D).pin_memory().numpy()
     oh = torch.empty(B, hq * DC_D).pin_memory().numpy()
     ctx.set_stream(None)
-    n_e2e = max(3, args.steps)
-    kv.rope_append(0, qh, kh, vh, ph, hq, q_out=qr)
-    kv.attend_decode(0, qr, ph, hq, scale, out=oh)
+    n_e2e = max(3, args.steps) * (20 if bytes_alg < (64 << 20) else 1)  # short steps: enough of them to time
+    for _ in range(3):
+        kv.decode_step(0, qh, kh, vh, ph, hq, scale, out=oh)
     t0 = time.perf_counter()
     for _ in range(n_e2e):
-        kv.rope_append(0, qh, kh, vh, ph, hq, q_out=qr)
-        kv.attend_decode(0, qr, ph, hq, scale, out=oh)
+        kv.decode_step(0, qh, kh, vh, ph, hq, scale, out=oh)
     e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / n_e2e, "cuda")
     if rank != 0:
         return None
     hbm, _, src = peaks()
     ach = bytes_alg / (att_ms * 1e-3) / 1e9
-    h2d = (qh.nbytes + kh.nbytes + vh.nbytes + 2 * ph.nbytes + qr.nbytes) * world
-    d2h = (qr.nbytes + oh.nbytes) * world
+    h2d = (qh.nbytes + kh.nbytes + vh.nbytes + ph.nbytes) * world
+    d2h = oh.nbytes * world
     cfg_name = "BASELINE configs[0] exactly" if (GB, L, kv_name) == (1, 512, "f32") else \
         "BASELINE configs[0]'s heads, batched"
     line = {"metric": "tinyllm GQA decode tokens/s (one attention layer: RoPE + cache write + attention)",
@@ -1038,9 +1047,11 @@ def run_decode(args, torch, dist, rank, world, local_rank):
                        "parallelism": f"(sequence, kv group) units over {world} rank(s), no collective"},
             "e2e": {"value": GB / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "host-pointer C ABI eif_cuda_rope_append + eif_cuda_attend_decode (pinned)"},
+                    "path": "host-pointer C ABI eif_cuda_decode_step (pinned)"},
+            "step_path": "one launch (attn_decode_step_kernel, a cluster per (sequence, kv head))"
+                         if launches == args.steps else "rope_append_kernel + split-K decode + combine",
             "roofline": {"kernel": {"bf16": "attn_decode_tc_kernel", "int8": "attn_decode_i8_kernel"}.get(
-                             kv_name, "attn_decode_simt_kernel") + " + combine", "bound": "hbm", "achieved": ach,
+                             kv_name, "attn_decode_f32_kernel") + " + combine", "bound": "hbm", "achieved": ach,
                          "peak": hbm,
                          "unit": "GB/s", "frac": ach / hbm, "peak_source": src,
                          "algorithmic_bytes_per_launch": bytes_alg, "attention_ms": att_ms, "traffic": None},

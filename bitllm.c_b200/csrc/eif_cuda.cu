@@ -81,12 +81,9 @@ eif_status_t ensure_buffer(eif_cuda_ctx_t *ctx, void **buf, size_t *cap, size_t 
     return EIF_STATUS_OK;
 }
 
-// Wait for the context's stream with the deadline, then report any device-side error word.
-eif_status_t wait_stream(eif_cuda_ctx_t *ctx) {
-    *ctx->host_err = 0;
-    cudaError_t e = cudaMemcpyAsync(ctx->host_err, ctx->dev_err, sizeof(unsigned), cudaMemcpyDeviceToHost,
-                                    ctx->stream);
-    if (e == cudaSuccess) e = cudaEventRecord(ctx->done, ctx->stream);
+// Wait for the context's stream with the deadline (the work queued so far, copies included).
+static eif_status_t wait_done(eif_cuda_ctx_t *ctx) {
+    cudaError_t e = cudaEventRecord(ctx->done, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "queue completion event");
     const double t0 = now_ms();
     int spins = 0;
@@ -101,7 +98,11 @@ eif_status_t wait_stream(eif_cuda_ctx_t *ctx) {
         else
             usleep(50);
     }
-    const unsigned derr = *ctx->host_err;
+    return EIF_STATUS_OK;
+}
+
+// The device error word read back after the work: clears it and reports what it says.
+static eif_status_t check_err_word(eif_cuda_ctx_t *ctx, unsigned derr) {
     if (derr) {
         CK(cudaMemsetAsync(ctx->dev_err, 0, sizeof(unsigned), ctx->stream));
         if (derr & EIF_DEVERR_POS_RANGE)
@@ -110,6 +111,48 @@ eif_status_t wait_stream(eif_cuda_ctx_t *ctx) {
             return fail(ctx, EIF_STATUS_TIMEOUT, "a kernel pipeline wait ran out of iterations");
         return fail(ctx, EIF_STATUS_INTERNAL_ERROR, "device error word 0x%x", derr);
     }
+    return EIF_STATUS_OK;
+}
+
+// Wait for the context's stream with the deadline, then report any device-side error word.
+eif_status_t wait_stream(eif_cuda_ctx_t *ctx) {
+    *ctx->host_err = 0;
+    CK(cudaMemcpyAsync(ctx->host_err, ctx->dev_err, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx->stream));
+    const eif_status_t st = wait_done(ctx);
+    if (st != EIF_STATUS_OK) return st;
+    return check_err_word(ctx, *ctx->host_err);
+}
+
+// Small host-pointer calls.  send_packed copies n host arrays (total at most kSmallIo, each at a 16-byte
+// aligned offset off[i]) into the pinned block and sends them to dst in one copy; the call's kernels write
+// an output of at most kSmallIo bytes to small_out(ctx); finish_small brings back the error word and that
+// output in one copy, waits, and hands the output to the caller.  The pinned block is reused only after
+// the wait, so no copy still reads it.
+static size_t a16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+static float *small_out(eif_cuda_ctx_t *ctx) { return reinterpret_cast<float *>(static_cast<char *>(ctx->io) + 16); }
+
+static eif_status_t send_packed(eif_cuda_ctx_t *ctx, char *dst, int n, const void *const *src, const size_t *bytes,
+                                size_t *off) {
+    char *h = static_cast<char *>(ctx->pin);
+    size_t o = 0;
+    for (int i = 0; i < n; ++i) {
+        off[i] = o;
+        if (bytes[i]) memcpy(h + o, src[i], bytes[i]);
+        o += a16(bytes[i]);
+    }
+    CK(cudaMemcpyAsync(dst, h, o, cudaMemcpyHostToDevice, ctx->stream));
+    return EIF_STATUS_OK;
+}
+
+static eif_status_t finish_small(eif_cuda_ctx_t *ctx, void *out, size_t bytes) {
+    char *h = static_cast<char *>(ctx->pin) + kSmallIo;
+    CK(cudaMemcpyAsync(h, ctx->io, 16 + bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    eif_status_t st = wait_done(ctx);
+    if (st != EIF_STATUS_OK) return st;
+    st = check_err_word(ctx, *reinterpret_cast<const unsigned *>(h));
+    if (st != EIF_STATUS_OK) return st;
+    memcpy(out, h + 16, bytes);
     return EIF_STATUS_OK;
 }
 
@@ -214,9 +257,11 @@ EIF_API eif_status_t eif_cuda_init(eif_cuda_ctx_t **out, int device) {
     DeviceGuard g(ctx);
     cudaError_t e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->done, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaMalloc(&ctx->dev_err, sizeof(unsigned));
-    if (e == cudaSuccess) e = cudaMemset(ctx->dev_err, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->io, 16 + kSmallIo);
+    if (e == cudaSuccess) e = cudaMemset(ctx->io, 0, 16);
     if (e == cudaSuccess) e = cudaMallocHost(&ctx->host_err, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMallocHost(&ctx->pin, 2 * kSmallIo + 16);
+    ctx->dev_err = static_cast<unsigned *>(ctx->io);
     if (e != cudaSuccess) {
         eif_cuda_free(ctx);
         return e == cudaErrorMemoryAllocation ? EIF_STATUS_OUT_OF_MEMORY : EIF_STATUS_ERROR;
@@ -234,8 +279,9 @@ EIF_API void eif_cuda_free(eif_cuda_ctx_t *ctx) {
         if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
         if (ctx->ws) cudaFree(ctx->ws);
         if (ctx->stage) cudaFree(ctx->stage);
-        if (ctx->dev_err) cudaFree(ctx->dev_err);
+        if (ctx->io) cudaFree(ctx->io);
         if (ctx->host_err) cudaFreeHost(ctx->host_err);
+        if (ctx->pin) cudaFreeHost(ctx->pin);
         if (ctx->done) cudaEventDestroy(ctx->done);
         if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     }
@@ -631,26 +677,35 @@ EIF_API eif_status_t eif_cuda_attend_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *
     DeviceGuard g(ctx);
     const size_t row = (size_t)n_heads * kv->hd;
     const size_t nq = (size_t)kv->batch * row;
-    Carver cv;
-    const size_t o_q = cv.take(nq * 4), o_o = cv.take(nq * 4), o_p = cv.take((size_t)kv->batch * 4);
-    const size_t o_g = gate ? cv.take(nq * 4) : 0;
-    const size_t o_n = (subln == EIF_CUDA_SUBLN_WEIGHT) ? cv.take(row * 4) : 0;
-    st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    // inputs q, pos, gate, sub_norm (absent ones are empty), packed in one copy when small
+    const bool wn = subln == EIF_CUDA_SUBLN_WEIGHT;
+    const void *src[4] = {q, pos, gate, sub_norm};
+    const size_t bytes[4] = {nq * 4, (size_t)kv->batch * 4, gate ? nq * 4 : 0, wn ? row * 4 : 0};
+    size_t off[4], in_total = 0;
+    for (int i = 0; i < 4; ++i) {
+        off[i] = in_total;
+        in_total += a16(bytes[i]);
+    }
+    const bool small = in_total <= kSmallIo && nq * 4 <= kSmallIo;
+    st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, a256(in_total) + (small ? 0 : nq * 4));
     if (st != EIF_STATUS_OK) return st;
     char *s = static_cast<char *>(ctx->stage);
-    CK(cudaMemcpyAsync(s + o_q, q, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
-    CK(cudaMemcpyAsync(s + o_p, pos, (size_t)kv->batch * 4, cudaMemcpyHostToDevice, ctx->stream));
-    if (gate) CK(cudaMemcpyAsync(s + o_g, gate, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
-    if (subln == EIF_CUDA_SUBLN_WEIGHT)
-        CK(cudaMemcpyAsync(s + o_n, sub_norm, row * 4, cudaMemcpyHostToDevice, ctx->stream));
-    DecodeArgs a{kv->k[layer], kv->v[layer], kv->dtype, reinterpret_cast<float *>(s + o_q),
-                 reinterpret_cast<int *>(s + o_p), kv->batch, n_heads, kv->n_kv, kv->hd, kv->max_seq, max_pos + 1,
-                 scale, gate ? reinterpret_cast<float *>(s + o_g) : nullptr, (int)subln,
-                 subln == EIF_CUDA_SUBLN_WEIGHT ? reinterpret_cast<float *>(s + o_n) : nullptr,
-                 reinterpret_cast<float *>(s + o_o), ctx->dev_err};
+    if (small) {
+        st = send_packed(ctx, s, 4, src, bytes, off);
+        if (st != EIF_STATUS_OK) return st;
+    } else {
+        for (int i = 0; i < 4; ++i)
+            if (bytes[i]) CK(cudaMemcpyAsync(s + off[i], src[i], bytes[i], cudaMemcpyHostToDevice, ctx->stream));
+    }
+    float *dout = small ? small_out(ctx) : reinterpret_cast<float *>(s + a256(in_total));
+    DecodeArgs a{kv->k[layer], kv->v[layer], kv->dtype, reinterpret_cast<float *>(s + off[0]),
+                 reinterpret_cast<int *>(s + off[1]), kv->batch, n_heads, kv->n_kv, kv->hd, kv->max_seq, max_pos + 1,
+                 scale, gate ? reinterpret_cast<float *>(s + off[2]) : nullptr, (int)subln,
+                 wn ? reinterpret_cast<float *>(s + off[3]) : nullptr, dout, ctx->dev_err};
     st = decode_run(ctx, kv, layer, a);
     if (st != EIF_STATUS_OK) return st;
-    CK(cudaMemcpyAsync(out, s + o_o, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    if (small) return finish_small(ctx, out, nq * 4);
+    CK(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return wait_stream(ctx);
 }
 
@@ -1319,6 +1374,10 @@ EIF_API eif_status_t eif_cuda_rope_append_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t
     return rope_run(ctx, kv, layer, q_dev, k_dev, v_dev, pos_dev, 1, 0, n_heads, q_out_dev, nullptr);
 }
 
+static eif_status_t stage_step_inputs(eif_cuda_ctx_t *ctx, const float *q, const float *k, const float *v,
+                                      const int *pos, size_t nq, size_t nk, size_t B, char **s_out, size_t *off,
+                                      float **dout);
+
 EIF_API eif_status_t eif_cuda_rope_append(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
                                           const float *k, const float *v, const int *pos, int n_heads, float *q_out) {
     eif_status_t rs = rope_check(ctx, kv, layer, n_heads);
@@ -1329,22 +1388,119 @@ EIF_API eif_status_t eif_cuda_rope_append(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv
             return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "pos[%d] = %d outside [0, %d)", b, pos[b], kv->max_seq);
     DeviceGuard g(ctx);
     const size_t B = kv->batch, nq = B * n_heads * kv->hd, nk = B * kv->n_kv * kv->hd;
-    Carver cv;
-    const size_t o_q = cv.take(nq * 4), o_k = cv.take(nk * 4), o_v = cv.take(nk * 4), o_p = cv.take(B * 4),
-                 o_o = cv.take(nq * 4);
-    rs = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    char *s = nullptr;
+    size_t off[4];
+    float *dout = nullptr;
+    rs = stage_step_inputs(ctx, q, k, v, pos, nq, nk, B, &s, off, &dout);
     if (rs != EIF_STATUS_OK) return rs;
-    char *s = static_cast<char *>(ctx->stage);
-    CK(cudaMemcpyAsync(s + o_q, q, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
-    CK(cudaMemcpyAsync(s + o_k, k, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
-    CK(cudaMemcpyAsync(s + o_v, v, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
-    CK(cudaMemcpyAsync(s + o_p, pos, B * 4, cudaMemcpyHostToDevice, ctx->stream));
-    rs = rope_run(ctx, kv, layer, reinterpret_cast<float *>(s + o_q), reinterpret_cast<float *>(s + o_k),
-                  reinterpret_cast<float *>(s + o_v), reinterpret_cast<int *>(s + o_p), 1, 0, n_heads,
-                  reinterpret_cast<float *>(s + o_o), nullptr);
+    rs = rope_run(ctx, kv, layer, reinterpret_cast<float *>(s + off[0]), reinterpret_cast<float *>(s + off[1]),
+                  reinterpret_cast<float *>(s + off[2]), reinterpret_cast<int *>(s + off[3]), 1, 0, n_heads, dout,
+                  nullptr);
     if (rs != EIF_STATUS_OK) return rs;
-    CK(cudaMemcpyAsync(q_out, s + o_o, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    if (dout == small_out(ctx)) return finish_small(ctx, q_out, nq * 4);
+    CK(cudaMemcpyAsync(q_out, dout, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return wait_stream(ctx);
+}
+
+// ---- the whole decode step of a layer: RoPE, the new row, attention -------------------------------------
+
+// Host inputs q, k, v, pos of a decode step into the stage buffer (packed in one copy when small); *dout is
+// where the step's output [B][nq / B] goes: small_out(ctx) when it fits, else the stage after the inputs,
+// followed by nq floats of scratch.
+static eif_status_t stage_step_inputs(eif_cuda_ctx_t *ctx, const float *q, const float *k, const float *v,
+                                      const int *pos, size_t nq, size_t nk, size_t B, char **s_out, size_t *off,
+                                      float **dout) {
+    const void *src[4] = {q, k, v, pos};
+    const size_t bytes[4] = {nq * 4, nk * 4, nk * 4, B * 4};
+    size_t in_total = 0;
+    for (int i = 0; i < 4; ++i) {
+        off[i] = in_total;
+        in_total += a16(bytes[i]);
+    }
+    const bool small = in_total <= kSmallIo && nq * 4 <= kSmallIo;
+    eif_status_t st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, a256(in_total) + 2 * a256(nq * 4));
+    if (st != EIF_STATUS_OK) return st;
+    char *s = static_cast<char *>(ctx->stage);
+    if (small) {
+        st = send_packed(ctx, s, 4, src, bytes, off);
+        if (st != EIF_STATUS_OK) return st;
+    } else {
+        for (int i = 0; i < 4; ++i) CK(cudaMemcpyAsync(s + off[i], src[i], bytes[i], cudaMemcpyHostToDevice, ctx->stream));
+    }
+    *s_out = s;
+    *dout = small ? small_out(ctx) : reinterpret_cast<float *>(s + a256(in_total));
+    return EIF_STATUS_OK;
+}
+
+// The step on device arrays: one launch (attn_decode_step.cu) when the shape is small enough, else
+// rope_append's kernel (the rotated q into q_rot) and the split-K decode.
+static eif_status_t step_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q, const float *k,
+                             const float *v, const int *pos, int max_len, int n_heads, float scale, float *out,
+                             float *q_rot) {
+    const int nc = decode_step_chunks(kv->dtype, kv->hd, n_heads / kv->n_kv, kv->batch, kv->n_kv, max_len,
+                                      ctx->sm_count);
+    if (nc > 0) {
+        DecodeStepArgs a{q, k, v, pos, kv->tl_cos, kv->tl_sin, kv->k[layer], kv->v[layer], kv->dtype, out,
+                         kv->batch, n_heads, kv->n_kv, kv->hd, kv->max_seq, kv->tl_interleaved, nc, scale,
+                         ctx->dev_err};
+        CK(launch_attend_decode_step(ctx->stream, a));
+        ctx->launches += 1;
+        return EIF_STATUS_OK;
+    }
+    eif_status_t st = rope_run(ctx, kv, layer, q, k, v, pos, 1, 0, n_heads, q_rot, nullptr);
+    if (st != EIF_STATUS_OK) return st;
+    DecodeArgs a{kv->k[layer], kv->v[layer], kv->dtype, q_rot, pos, kv->batch, n_heads, kv->n_kv, kv->hd,
+                 kv->max_seq, max_len, scale, nullptr, (int)EIF_CUDA_SUBLN_NONE, nullptr, out, ctx->dev_err};
+    return decode_run(ctx, kv, layer, a);
+}
+
+EIF_API eif_status_t eif_cuda_decode_step(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
+                                          const float *k, const float *v, const int *pos, int n_heads, float scale,
+                                          float *out) {
+    eif_status_t rs = rope_check(ctx, kv, layer, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!q || !k || !v || !pos || !out) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "decode_step: NULL pointer");
+    int max_pos = 0;
+    for (int b = 0; b < kv->batch; ++b) {
+        if (pos[b] < 0 || pos[b] >= kv->max_seq)
+            return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "pos[%d] = %d outside [0, %d)", b, pos[b], kv->max_seq);
+        max_pos = std::max(max_pos, pos[b]);
+    }
+    DeviceGuard g(ctx);
+    const size_t B = kv->batch, nq = B * n_heads * kv->hd, nk = B * kv->n_kv * kv->hd;
+    char *s = nullptr;
+    size_t off[4];
+    float *dout = nullptr;
+    rs = stage_step_inputs(ctx, q, k, v, pos, nq, nk, B, &s, off, &dout);
+    if (rs != EIF_STATUS_OK) return rs;
+    const bool small = dout == small_out(ctx);
+    float *q_rot = small ? reinterpret_cast<float *>(s + a256(off[3] + B * 4))
+                         : reinterpret_cast<float *>(reinterpret_cast<char *>(dout) + a256(nq * 4));
+    rs = step_run(ctx, kv, layer, reinterpret_cast<float *>(s + off[0]), reinterpret_cast<float *>(s + off[1]),
+                  reinterpret_cast<float *>(s + off[2]), reinterpret_cast<int *>(s + off[3]), max_pos + 1, n_heads,
+                  scale, dout, q_rot);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (small) return finish_small(ctx, out, nq * 4);
+    CK(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+EIF_API eif_status_t eif_cuda_decode_step_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_dev,
+                                              const float *k_dev, const float *v_dev, const int *pos_dev, int max_pos,
+                                              int n_heads, float scale, float *out_dev) {
+    eif_status_t rs = rope_check(ctx, kv, layer, n_heads);
+    if (rs != EIF_STATUS_OK) return rs;
+    if (!q_dev || !k_dev || !v_dev || !pos_dev || !out_dev)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "decode_step_dev: NULL pointer");
+    if (max_pos < 0 || max_pos >= kv->max_seq)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "max_pos %d outside [0, %d)", max_pos, kv->max_seq);
+    DeviceGuard g(ctx);
+    // scratch for the rotated q of the two-launch form
+    const size_t nq = (size_t)kv->batch * n_heads * kv->hd;
+    rs = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, a256(nq * 4));
+    if (rs != EIF_STATUS_OK) return rs;
+    return step_run(ctx, kv, layer, q_dev, k_dev, v_dev, pos_dev, max_pos + 1, n_heads, scale, out_dev,
+                    static_cast<float *>(ctx->stage));
 }
 
 static eif_status_t rope_prefill_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int n_tok, int start_pos,

@@ -31,11 +31,19 @@ struct eif_cuda_ctx {
     // device staging for the host-pointer entry points, grown on demand
     void *stage = nullptr;
     size_t stage_bytes = 0;
-    // device error word
+    // device error word: the first 16 bytes of io, whose remaining kSmallIo bytes take the outputs of
+    // small host-pointer calls, so that the word and the output come back in one copy
+    void *io = nullptr;
     unsigned *dev_err = nullptr;
     // pinned host copy of the error word
     unsigned *host_err = nullptr;
+    // pinned host staging of small host-pointer calls: [inputs, packed | error word + output]
+    void *pin = nullptr;
 };
+
+// Host-pointer calls whose inputs (together) and output are at most this many bytes go through the pinned
+// staging block: one host-to-device copy of the packed inputs, one copy back of the error word + output.
+constexpr size_t kSmallIo = 256 << 10;
 
 struct eif_cuda_kv {
     eif_cuda_ctx_t *ctx = nullptr;
@@ -189,6 +197,23 @@ cudaError_t launch_attend_decode_tc(cudaStream_t st, const CUtensorMap &tk, cons
                                     const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,
                                     float2 *part_ml, int sm_count);
 // TMA-fed decode over an fp32 cache (attn_decode_f32.cu); tk / tv: 32-key x 32-float boxes, 128-byte swizzle.
+// One tinyllm decode step in one launch for small batches (attn_decode_step.cu): RoPE of q and k, the new
+// K / V row, GQA attention over [0, pos] split over a cluster of nc CTAs per (sequence, kv head).
+struct DecodeStepArgs {
+    const float *q, *k, *v;       // [B][Hq*D], [B][Hkv*D], [B][Hkv*D] fp32, un-rotated
+    const int *pos;               // [B]
+    const float *cos_t, *sin_t;   // [max_seq][D/2]
+    void *Kc, *Vc;                // the layer's cache
+    eif_cuda_dtype_t dtype;
+    float *out;                   // [B][Hq*D]
+    int B, Hq, Hkv, D, max_seq, interleaved, nc;
+    float scale;
+    unsigned *dev_err;
+};
+// Chunks per (sequence, kv head) of the one-launch step for this shape, or 0 when it does not take it.
+int decode_step_chunks(eif_cuda_dtype_t dtype, int D, int G, int B, int Hkv, int max_len, int sm_count);
+cudaError_t launch_attend_decode_step(cudaStream_t st, const DecodeStepArgs &a);
+
 bool decode_f32_supported(int D, int G);
 cudaError_t launch_attend_decode_f32(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
                                      const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,

@@ -7,9 +7,9 @@
 //   (:642-653).  One CTA per (sequence, head): it owns that head's q, k and v conv channels (so every
 //   conv-window row is updated by exactly one CTA) and all d_v columns of S (so the RMSNorm of the
 //   head's output row closes inside the CTA).  S crosses HBM once each way.
-//   S is read from global memory twice and never staged: the retrieve pass from HBM, the update pass
-//   from L2, where the first pass just left it (at four CTAs of 256 threads per SM at most 38 MB of
-//   state is in flight, well inside L2).  Without a shared-memory copy of S, four CTAs fit per SM and
+//   S is read from global memory twice and never staged: an L2 prefetch of the head's S starts with the
+//   CTA, the retrieve pass reads it after the conv and the norms, the update pass re-reads it from L2
+//   (at four CTAs of 256 threads per SM at most 38 MB of state is in flight, well inside L2).  Without a shared-memory copy of S, four CTAs fit per SM and
 //   up to 4 x SMs heads run in one wave (a copy of the head's S in shared memory allows three, and at
 //   small batches its second wave of a few CTAs set the time).
 //
@@ -51,6 +51,8 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
 
     float *Sh = a.S + bh * DK * DV;
     const int col0 = lc * 4;
+    // the head's S starts towards L2 now, so that the retrieve pass after the conv and the norms finds it there
+    if (tid < DK * DV * 4 / 16384) bulk_prefetch_l2(Sh + tid * 4096, 16384);
 
     // causal conv1d + SiLU on this head's channels: q [h*DK, +DK), k [key_dim + h*DK, +DK), v [2*key_dim + h*DV, +DV)
     const int ck = a.conv_k;

@@ -84,6 +84,33 @@ EIF_DEV void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t b
         : "memory");
 }
 
+// Thread-block clusters: this CTA's rank, a peer's copy of a shared-memory address, loads from it, and the
+// cluster-wide barrier (release / acquire: shared-memory writes before it are visible to the peers after it).
+EIF_DEV uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+EIF_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+EIF_DEV float ld_shared_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+EIF_DEV void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Starts a copy of [src, src + bytes) from global memory into L2 (16-byte aligned, a multiple of 16 bytes).
+EIF_DEV void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+                 : "memory");
+}
+
 EIF_DEV void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -77,6 +77,8 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_kv_set_rope": (_I, [_P, _P, _F, _I]),
         "eif_cuda_rope_append": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P]),
         "eif_cuda_rope_append_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P]),
+        "eif_cuda_decode_step": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, ctypes.c_float, _P]),
+        "eif_cuda_decode_step_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _I, ctypes.c_float, _P]),
         "eif_cuda_rope_append_prefill": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _P]),
         "eif_cuda_rope_append_prefill_dev": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _P]),
         "eif_cuda_attend_decode": (_I, [_P, _P, _I, _P, _P, _I, _F, _P, _I, _P, _P]),
@@ -116,10 +118,12 @@ def lib() -> ctypes.CDLL:
 
 
 def _ptr(a):
-    """Host numpy array -> void* (None passes NULL)."""
+    """Host numpy array -> its data address for a void* argument (None passes NULL).  The address comes from
+    the array interface rather than a.ctypes, whose per-call object costs microseconds on short calls; the
+    caller keeps the array alive across the call."""
     if a is None:
         return None
-    return a.ctypes.data_as(_P)
+    return a.__array_interface__["data"][0]
 
 
 def _f32(a):
@@ -297,6 +301,20 @@ class KVCache:
     def rope_append_dev(self, layer: int, q_dev, k_dev, v_dev, pos_dev, n_heads: int, q_out_dev):
         self.ctx.check(lib().eif_cuda_rope_append_dev(self.ctx.handle, self._h, layer, q_dev, k_dev, v_dev, pos_dev,
                                                       n_heads, q_out_dev), "rope_append_dev")
+
+    def decode_step(self, layer: int, q, k, v, pos, n_heads: int, scale: float, out=None):
+        """The whole decode step of the layer (RoPE, the new K / V row at pos[b], attention over [0, pos[b]]):
+        returns out [batch][n_heads*hd] (written into `out` when given)."""
+        qq, kk, vv, pp = _f32(q), _f32(k), _f32(v), _i32(pos)
+        o = _out(out, (self.batch, n_heads * self.head_dim))
+        self.ctx.check(lib().eif_cuda_decode_step(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv),
+                                                  _ptr(pp), n_heads, float(scale), _ptr(o)), "decode_step")
+        return o
+
+    def decode_step_dev(self, layer: int, q_dev, k_dev, v_dev, pos_dev, max_pos: int, n_heads: int, scale: float,
+                        out_dev):
+        self.ctx.check(lib().eif_cuda_decode_step_dev(self.ctx.handle, self._h, layer, q_dev, k_dev, v_dev, pos_dev,
+                                                      int(max_pos), n_heads, float(scale), out_dev), "decode_step_dev")
 
     def rope_append_prefill(self, layer: int, q, k, v, n_tok: int, start_pos: int, n_heads: int):
         """RoPE + cache write for n_tok tokens per sequence at start_pos + i: returns the rotated q."""

@@ -168,6 +168,22 @@ eif_status_t eif_cuda_rope_append_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t
                                               const float *k_dev, const float *v_dev, int n_tok, int start_pos,
                                               int n_heads, void *q_out_dev);
 
+/*
+ * A whole tinyllm decode step of one layer in one call: RoPE of the new q and k, the write of the new K / V row at
+ * pos[b], and GQA attention over rows [0, pos[b]] for every head -- src/eif_tinyllm.c:480-507 (rotation and cache
+ * write, :509-549 for an INT8 cache) then the head loop :555-656, i.e. eif_cuda_rope_append followed by
+ * eif_cuda_attend_decode (no gate, no SubLN) without the rotated q leaving the device.  Small batches (fp32 or bf16
+ * cache, head_dim 64 / 128, at most 8 q heads per kv head) run as ONE launch with a thread-block cluster per
+ * (sequence, kv head); other shapes run the two calls' kernels.  Needs eif_cuda_kv_set_rope.
+ *   q [batch][n_heads*head_dim], k, v [batch][n_kv*head_dim] fp32 (un-rotated); out [batch][n_heads*head_dim].
+ * _dev: device arrays, asynchronous; max_pos bounds every pos[b] (as in eif_cuda_attend_decode_dev).
+ */
+eif_status_t eif_cuda_decode_step(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q, const float *k,
+                                  const float *v, const int *pos, int n_heads, float scale, float *out);
+eif_status_t eif_cuda_decode_step_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_dev,
+                                      const float *k_dev, const float *v_dev, const int *pos_dev, int max_pos,
+                                      int n_heads, float scale, float *out_dev);
+
 /* ---------------------------------------------------------------------------------------------
  * Decode attention: one new query token per sequence over cache rows [0, pos[b]].
  * Replaces the head loop of fullatt_attend (src/eif_qwen35.c:741-790) and the inline tinyllm decode

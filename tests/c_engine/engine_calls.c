@@ -2,7 +2,7 @@
  * engine_calls.c -- the calls a C99 engine makes through include/eif_cuda.h, checked against plain C loops.
  *
  * The tinyllm decode step (src/eif_tinyllm.c:395-405 RoPE tables, :480-506 rotation, :509-549 INT8 cache
- * write, :551-656 attention) over an fp32 and an INT8 cache, and the DeltaNet delta rule (src/eif_qwen35.c:594-639),
+ * write, :551-656 attention) over an fp32 and an INT8 cache, as two calls and as one (eif_cuda_decode_step), and the DeltaNet delta rule (src/eif_qwen35.c:594-639),
  * run token by token through the host-pointer entry points; the reference loops below restate the same
  * arithmetic in C (RoPE tables in the form the reference's -ffast-math build evaluates, powf(theta, -e)).
  * Exit status 0 when every check passes (or when no CUDA device is present), 1 otherwise.
@@ -98,7 +98,9 @@ static int fail_status(eif_cuda_ctx_t *ctx, const char *what, eif_status_t st) {
     return 1;
 }
 
-static int tinyllm_decode(eif_cuda_ctx_t *ctx, eif_cuda_dtype_t dtype) {
+/* one_call: the step as eif_cuda_decode_step (RoPE, row write, attention in one call) instead of
+ * eif_cuda_rope_append + eif_cuda_attend_decode */
+static int tinyllm_decode(eif_cuda_ctx_t *ctx, eif_cuda_dtype_t dtype, int one_call) {
     eif_cuda_kv_t *kv = NULL;
     eif_status_t st = eif_cuda_kv_alloc(ctx, 1, 1, T, NKV, HD, dtype, &kv);
     if (st != EIF_STATUS_OK) return fail_status(ctx, "kv_alloc", st);
@@ -113,17 +115,23 @@ static int tinyllm_decode(eif_cuda_ctx_t *ctx, eif_cuda_dtype_t dtype) {
         for (int i = 0; i < NH * HD; i++) q[i] = 2.0f * rnd();
         for (int i = 0; i < NKV * HD; i++) { k[i] = 2.0f * rnd(); v[i] = 2.0f * rnd(); }
         /* the engine: RoPE + cache write of the new row, then the head loop */
-        if ((st = eif_cuda_rope_append(ctx, kv, 0, q, k, v, &pos, NH, qr)) != EIF_STATUS_OK)
-            return fail_status(ctx, "rope_append", st);
-        if ((st = eif_cuda_attend_decode(ctx, kv, 0, qr, &pos, NH, 1.0f / sqrtf((float)HD), NULL,
-                                         EIF_CUDA_SUBLN_NONE, NULL, out)) != EIF_STATUS_OK)
-            return fail_status(ctx, "attend_decode", st);
+        if (one_call) {
+            if ((st = eif_cuda_decode_step(ctx, kv, 0, q, k, v, &pos, NH, 1.0f / sqrtf((float)HD), out)) != EIF_STATUS_OK)
+                return fail_status(ctx, "decode_step", st);
+        } else {
+            if ((st = eif_cuda_rope_append(ctx, kv, 0, q, k, v, &pos, NH, qr)) != EIF_STATUS_OK)
+                return fail_status(ctx, "rope_append", st);
+            if ((st = eif_cuda_attend_decode(ctx, kv, 0, qr, &pos, NH, 1.0f / sqrtf((float)HD), NULL,
+                                             EIF_CUDA_SUBLN_NONE, NULL, out)) != EIF_STATUS_OK)
+                return fail_status(ctx, "attend_decode", st);
+        }
         /* the reference loops */
         float qh[NH * HD], kh[NKV * HD];
         memcpy(qh, q, sizeof qh);
         memcpy(kh, k, sizeof kh);
         rope(qh, NH, pos, theta);
         rope(kh, NKV, pos, theta);
+        if (one_call) memcpy(qr, qh, sizeof qh); /* q stays on the device: compare the reference with itself */
         memcpy(kc + pos * NKV * HD, kh, sizeof kh);
         memcpy(vc + pos * NKV * HD, v, sizeof v);
         if (dtype == EIF_CUDA_INT8) {
@@ -145,8 +153,9 @@ static int tinyllm_decode(eif_cuda_ctx_t *ctx, eif_cuda_dtype_t dtype) {
         worst = eq > worst ? eq : worst;
     }
     eif_cuda_kv_free(kv);
-    printf("tinyllm decode, %s cache: worst rel-L2 %.2e, rows with code / scale mismatches %d\n",
-           dtype == EIF_CUDA_INT8 ? "INT8" : "fp32", worst, code_mismatch);
+    printf("tinyllm decode, %s cache, %s: worst rel-L2 %.2e, rows with code / scale mismatches %d\n",
+           dtype == EIF_CUDA_INT8 ? "INT8" : "fp32", one_call ? "eif_cuda_decode_step" : "rope_append + attend_decode",
+           worst, code_mismatch);
     return worst <= 1e-5 && code_mismatch == 0 ? 0 : 1;
 }
 
@@ -211,8 +220,10 @@ int main(void) {
         return 1;
     }
     int bad = 0;
-    bad |= tinyllm_decode(ctx, EIF_CUDA_F32);
-    bad |= tinyllm_decode(ctx, EIF_CUDA_INT8);
+    bad |= tinyllm_decode(ctx, EIF_CUDA_F32, 0);
+    bad |= tinyllm_decode(ctx, EIF_CUDA_INT8, 0);
+    bad |= tinyllm_decode(ctx, EIF_CUDA_F32, 1);
+    bad |= tinyllm_decode(ctx, EIF_CUDA_INT8, 1);
     bad |= deltanet_rule(ctx);
     eif_cuda_free(ctx);
     printf(bad ? "FAILED\n" : "OK\n");
