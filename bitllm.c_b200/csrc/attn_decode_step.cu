@@ -7,11 +7,14 @@
 // with the same arithmetic, for the batches where launch latency rather than HBM sets the step time.
 //
 // One cluster of NC CTAs per (sequence b, kv head): every CTA rotates the G query heads of the group into
-// shared memory and takes one chunk of the key range; the CTA whose chunk holds pos rotates k, writes the
-// new K / V row to the cache and uses its own shared copy of that row for key pos (no CTA reads a row this
-// launch writes).  Each CTA merges its warps into a partial (m, l, o[G][D]) in shared memory; after a
-// cluster barrier every CTA combines a slice of the G x D outputs from all NC partials through distributed
-// shared memory, and a second barrier keeps the partials alive until the last peer has read them.
+// shared memory and takes one chunk of the key range, whose K and V rows it brings into shared memory with
+// bulk copies issued at the start (one round trip, rows padded by 16 bytes so that lanes reading one column
+// of consecutive rows hit different banks); the CTA whose chunk holds pos rotates k, writes the new K / V
+// row to the cache and places its own copy of that row in the chunk (no CTA reads a row this launch writes).
+// The chunk's keys are spread over the four warps.  Each CTA merges its warps into a partial
+// (m, l, o[G][D]) in shared memory; after a cluster barrier every CTA combines a slice of the G x D outputs
+// from all NC partials through distributed shared memory, and a second barrier keeps the partials alive
+// until the last peer has read them.
 // fp32 and bf16 caches, head_dim 64 / 128, G <= 8.
 #include <math.h>
 
@@ -23,6 +26,7 @@ namespace {
 
 constexpr int kStepThreads = 128;
 constexpr int kStepWarps = kStepThreads / 32;
+constexpr int kStepStageBytes = 100 * 1024;  // shared memory for a CTA's staged K / V rows
 
 template <typename KT>
 __device__ __forceinline__ KT to_cache(float x);
@@ -31,10 +35,15 @@ __device__ __forceinline__ float to_cache<float>(float x) { return x; }
 template <>
 __device__ __forceinline__ __nv_bfloat16 to_cache<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 
+// Shared-memory row stride of a staged K / V row: the row plus 16 bytes.
+template <typename KT, int D>
+constexpr int step_row_bytes() { return D * (int)sizeof(KT) + 16; }
+
 template <typename KT, int D, int G>
 __global__ void __launch_bounds__(kStepThreads) attn_decode_step_kernel(const DecodeStepArgs a) {
     constexpr int DL = D / 32, HALF = D / 2;
     constexpr int KV_VEC = 16 / (int)sizeof(KT);
+    constexpr int RB = step_row_bytes<KT, D>(), RS = RB / (int)sizeof(KT);  // row stride, bytes / elements
     static_assert(DL == 2 || DL == 4, "head_dim 64 / 128");
     const int nc = a.nc, rank = (int)cluster_ctarank();
     const int kvh = blockIdx.x / nc, b = blockIdx.y;
@@ -46,16 +55,42 @@ __global__ void __launch_bounds__(kStepThreads) attn_decode_step_kernel(const De
     __shared__ float wm[kStepWarps][G], wl[kStepWarps][G];
     __shared__ float wacc[kStepWarps][G][D];  // warp partials; the CTA partial is merged into wacc[0]
     __shared__ float pm[G], pl[G];
+    __shared__ __align__(8) uint64_t rows_bar;
+    extern __shared__ __align__(16) uint8_t kvs[];  // the chunk's K rows, then its V rows (stride RB)
 
     int p = a.pos[b];
-    const bool pos_ok = p >= 0 && p < a.max_seq;
+    // pos past the bound the launch was sized for (max_pos of the _dev call) is refused like one outside
+    // the cache: the staged chunk would not fit
+    const bool pos_ok = p >= 0 && p < a.max_seq && (p + nc) / nc <= a.chunk_cap;
     if (!pos_ok) {
         if (threadIdx.x == 0 && rank == 0 && kvh == 0) atomicOr(a.dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
         p = -1;  // no keys, no row written: the output is zeros
     }
     const int L = p + 1, chunk = (L + nc - 1) / nc;
     const int t_begin = min(L, rank * chunk), t_end = min(L, t_begin + chunk);
+    const int n_rows = t_end - t_begin;  // at most a.chunk_cap
     const bool owner = pos_ok && t_begin <= p && p < t_end;
+    const size_t row_stride = (size_t)a.Hkv * D;
+    KT *Kb = static_cast<KT *>(a.Kc) + ((size_t)b * a.max_seq * a.Hkv + kvh) * D;
+    KT *Vb = static_cast<KT *>(a.Vc) + ((size_t)b * a.max_seq * a.Hkv + kvh) * D;
+    KT *ks = reinterpret_cast<KT *>(kvs), *vs = reinterpret_cast<KT *>(kvs + (size_t)a.chunk_cap * RB);
+
+    // the chunk's rows (all but the new one) start towards shared memory
+    const uint32_t rbar = smem_u32(&rows_bar);
+    const int n_copy = n_rows - (owner ? 1 : 0);
+    if (threadIdx.x == 0) {
+        mbar_init(rbar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(rbar, (uint32_t)(2 * n_copy * D * (int)sizeof(KT)));
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < 2 * n_rows; r += kStepThreads) {
+        const int t = t_begin + (r >> 1);
+        if (t == p) continue;
+        const bool isv = r & 1;
+        bulk_load(smem_u32(kvs) + (uint32_t)((isv ? a.chunk_cap : 0) + (t - t_begin)) * RB,
+                  (isv ? Vb : Kb) + (size_t)t * row_stride, D * (uint32_t)sizeof(KT), rbar);
+    }
 
     // rotated q of the group's heads, and (owner) the rotated k: the rotation of rope_append_kernel
     const float *cs = a.cos_t + (size_t)(pos_ok ? p : 0) * HALF;
@@ -75,17 +110,19 @@ __global__ void __launch_bounds__(kStepThreads) attn_decode_step_kernel(const De
             sq[g][ib] = y1;
         }
     }
-    const size_t row_stride = (size_t)a.Hkv * D;
-    KT *Kb = static_cast<KT *>(a.Kc) + ((size_t)b * a.max_seq * a.Hkv + kvh) * D;
-    KT *Vb = static_cast<KT *>(a.Vc) + ((size_t)b * a.max_seq * a.Hkv + kvh) * D;
     if (owner)
         for (int d = threadIdx.x; d < D; d += kStepThreads) vrow[d] = to_cache<KT>(a.v[((size_t)b * a.Hkv + kvh) * D + d]);
     __syncthreads();
-    if (owner)
+    if (owner)  // the new row: into the cache, and into its place in the staged chunk
         for (int d = threadIdx.x; d < D; d += kStepThreads) {
             Kb[(size_t)p * row_stride + d] = krow[d];
             Vb[(size_t)p * row_stride + d] = vrow[d];
+            ks[(size_t)(p - t_begin) * RS + d] = krow[d];
+            vs[(size_t)(p - t_begin) * RS + d] = vrow[d];
         }
+    // a wait that gives up leaves the partial empty (the error word tells the host)
+    const bool rows_ok = mbar_wait(rbar, 0, a.dev_err);
+    __syncthreads();
 
     float m[G], l[G], acc[G][DL];
 #pragma unroll
@@ -95,14 +132,17 @@ __global__ void __launch_bounds__(kStepThreads) attn_decode_step_kernel(const De
 #pragma unroll
         for (int i = 0; i < DL; ++i) acc[h][i] = 0.f;
     }
-    for (int t0 = t_begin + warp * 32; t0 < t_end; t0 += kStepWarps * 32) {
+    // warp w takes keys [w0, w1) of the chunk, in blocks of 32 (lane = key for the scores)
+    const int per_warp = (n_rows + kStepWarps - 1) / kStepWarps;
+    const int w0 = rows_ok ? warp * per_warp : 0, w1 = rows_ok ? min(n_rows, w0 + per_warp) : 0;
+    for (int t0 = w0; t0 < w1; t0 += 32) {
         const int t = t0 + lane;
-        const bool valid = t < t_end;
+        const bool valid = t < w1;
         float s[G];
 #pragma unroll
         for (int h = 0; h < G; ++h) s[h] = 0.f;
         if (valid) {
-            const KT *kr = t == p ? krow : Kb + (size_t)t * row_stride;
+            const KT *kr = ks + (size_t)t * RS;
 #pragma unroll 4
             for (int d = 0; d < D; d += KV_VEC) {
                 float kv[KV_VEC];
@@ -126,10 +166,9 @@ __global__ void __launch_bounds__(kStepThreads) attn_decode_step_kernel(const De
             m[h] = m_new;
             s[h] = pr;
         }
-        const int nvalid = min(32, t_end - t0);
+        const int nvalid = min(32, w1 - t0);
         for (int j = 0; j < nvalid; ++j) {
-            const int tj = t0 + j;
-            const KT *vr = (tj == p ? vrow : Vb + (size_t)tj * row_stride) + lane * DL;
+            const KT *vr = vs + (size_t)(t0 + j) * RS + lane * DL;
             float vv[DL];
             KvLoad<KT, DL>::load(vr, vv);
 #pragma unroll
@@ -198,7 +237,7 @@ cudaError_t launch_g(cudaStream_t st, const DecodeStepArgs &a, int G) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nc * a.Hkv, a.B, 1);
     cfg.blockDim = dim3(kStepThreads, 1, 1);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = (size_t)2 * a.chunk_cap * step_row_bytes<KT, D>();
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -207,27 +246,45 @@ cudaError_t launch_g(cudaStream_t st, const DecodeStepArgs &a, int G) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    // the shared-memory opt-in is made once per kernel and device (for the whole staging budget), not per launch
+    static bool opted[64][9] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = -1;
+    auto go = [&](auto kernel) {
+        if (dev < 0 || !opted[dev][G]) {
+            const cudaError_t e =
+                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepStageBytes);
+            if (e != cudaSuccess) return e;
+            if (dev >= 0) opted[dev][G] = true;
+        }
+        return cudaLaunchKernelEx(&cfg, kernel, a);
+    };
     switch (G) {
-        case 1: return cudaLaunchKernelEx(&cfg, attn_decode_step_kernel<KT, D, 1>, a);
-        case 2: return cudaLaunchKernelEx(&cfg, attn_decode_step_kernel<KT, D, 2>, a);
-        case 3: return cudaLaunchKernelEx(&cfg, attn_decode_step_kernel<KT, D, 3>, a);
-        case 4: return cudaLaunchKernelEx(&cfg, attn_decode_step_kernel<KT, D, 4>, a);
-        case 5: return cudaLaunchKernelEx(&cfg, attn_decode_step_kernel<KT, D, 5>, a);
-        case 6: return cudaLaunchKernelEx(&cfg, attn_decode_step_kernel<KT, D, 6>, a);
-        case 7: return cudaLaunchKernelEx(&cfg, attn_decode_step_kernel<KT, D, 7>, a);
-        case 8: return cudaLaunchKernelEx(&cfg, attn_decode_step_kernel<KT, D, 8>, a);
+        case 1: return go(attn_decode_step_kernel<KT, D, 1>);
+        case 2: return go(attn_decode_step_kernel<KT, D, 2>);
+        case 3: return go(attn_decode_step_kernel<KT, D, 3>);
+        case 4: return go(attn_decode_step_kernel<KT, D, 4>);
+        case 5: return go(attn_decode_step_kernel<KT, D, 5>);
+        case 6: return go(attn_decode_step_kernel<KT, D, 6>);
+        case 7: return go(attn_decode_step_kernel<KT, D, 7>);
+        case 8: return go(attn_decode_step_kernel<KT, D, 8>);
         default: return cudaErrorInvalidValue;
     }
 }
 
 }  // namespace
 
-int decode_step_chunks(eif_cuda_dtype_t dtype, int D, int G, int B, int Hkv, int max_len, int sm_count) {
+int decode_step_chunks(eif_cuda_dtype_t dtype, int D, int G, int B, int Hkv, int max_len, int sm_count,
+                       int *chunk_cap) {
     if (dtype != EIF_CUDA_F32 && dtype != EIF_CUDA_BF16) return 0;
-    if ((D != 64 && D != 128) || G < 1 || G > 8 || max_len < 1 || max_len > 8192) return 0;
+    if ((D != 64 && D != 128) || G < 1 || G > 8 || max_len < 1) return 0;
+    // a chunk's K and V rows must fit the shared-memory budget of the staged copy
+    const int rb = D * (dtype == EIF_CUDA_F32 ? 4 : 2) + 16, cap = kStepStageBytes / (2 * rb);
     int nc = (max_len + 63) / 64;  // at least 64 keys a CTA
     if (nc > 8) nc = 8;            // the portable cluster size
+    if ((max_len + nc - 1) / nc > cap) return 0;
     if ((long)B * Hkv * nc > 2L * sm_count) return 0;
+    *chunk_cap = (max_len + nc - 1) / nc;
     return nc;
 }
 

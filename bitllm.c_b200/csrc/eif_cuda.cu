@@ -1437,12 +1437,13 @@ static eif_status_t stage_step_inputs(eif_cuda_ctx_t *ctx, const float *q, const
 static eif_status_t step_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q, const float *k,
                              const float *v, const int *pos, int max_len, int n_heads, float scale, float *out,
                              float *q_rot) {
+    int cap = 0;
     const int nc = decode_step_chunks(kv->dtype, kv->hd, n_heads / kv->n_kv, kv->batch, kv->n_kv, max_len,
-                                      ctx->sm_count);
+                                      ctx->sm_count, &cap);
     if (nc > 0) {
         DecodeStepArgs a{q, k, v, pos, kv->tl_cos, kv->tl_sin, kv->k[layer], kv->v[layer], kv->dtype, out,
                          kv->batch, n_heads, kv->n_kv, kv->hd, kv->max_seq, kv->tl_interleaved, nc, scale,
-                         ctx->dev_err};
+                         ctx->dev_err, cap};
         CK(launch_attend_decode_step(ctx->stream, a));
         ctx->launches += 1;
         return EIF_STATUS_OK;

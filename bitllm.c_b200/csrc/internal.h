@@ -209,9 +209,12 @@ struct DecodeStepArgs {
     int B, Hq, Hkv, D, max_seq, interleaved, nc;
     float scale;
     unsigned *dev_err;
+    int chunk_cap;                // keys of the largest chunk (sizes the staged rows)
 };
-// Chunks per (sequence, kv head) of the one-launch step for this shape, or 0 when it does not take it.
-int decode_step_chunks(eif_cuda_dtype_t dtype, int D, int G, int B, int Hkv, int max_len, int sm_count);
+// Chunks per (sequence, kv head) of the one-launch step for this shape (and the largest chunk in
+// *chunk_cap), or 0 when it does not take it.
+int decode_step_chunks(eif_cuda_dtype_t dtype, int D, int G, int B, int Hkv, int max_len, int sm_count,
+                       int *chunk_cap);
 cudaError_t launch_attend_decode_step(cudaStream_t st, const DecodeStepArgs &a);
 
 bool decode_f32_supported(int D, int G);

@@ -76,7 +76,8 @@ def test_decode_step_vs_port(pkg, ctx, orc, B, hd, nh, nkv, theta, inter, dtype)
 
 
 def test_decode_step_long_context(pkg, ctx, orc):
-    """One step at pos 4999 over rows uploaded before (fp32, 14 / 2 heads): 8 CTAs of 625 keys per kv head."""
+    """One step at pos 4999 over rows uploaded before (fp32, 14 / 2 heads): more keys than the one-launch
+    kernel stages, so rope_append's kernel and the split-K decode."""
     rng = np.random.default_rng(11)
     nh, nkv, hd, T, t = 14, 2, 64, 5008, 4999
     kv = pkg.KVCache(ctx, 1, 1, T, nkv, hd, pkg.F32)
