@@ -18,10 +18,11 @@
 //                        each, and G, per chunk.
 //   deltanet_chunked_kernel  one CTA per (sequence, head, 64-column slice of d_v): the columns of S
 //                        evolve independently (column j of u depends on column j of S only), so slices
-//                        need no communication.  Every chunk product runs on tcgen05 (bf16 operands in
-//                        shared memory, fp32 accumulators in tensor memory); the fp32 state stays in
-//                        registers; TMA brings q / k / v / T two chunks ahead (128-byte swizzle, no
-//                        multicast).  Warp roles are described above the kernel.
+//                        need no communication.  Every chunk product runs on tcgen05 (fp32 accumulators
+//                        in tensor memory; bf16 operands in shared memory, except the A operands of the
+//                        state chain's products, which the prep warps write into tensor memory); the fp32
+//                        state stays in registers; TMA brings q / k / v / T two chunks ahead (128-byte
+//                        swizzle, no multicast).  Warp roles are described above the kernel.
 #include <math.h>
 
 #include "internal.h"
@@ -203,33 +204,39 @@ __global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid
 // ==================================================================================================
 // Kernel B: the chunk products on tcgen05 and the state recurrence
 // ==================================================================================================
-// Products of chunk c (M = 128 TMEM lanes, fp32 accumulators; "lanes 0-63" are the chunk's tokens):
-//   Dq  = [Q ; *] K^T                         lanes 0-63: Q K^T                      (prep)
-//   Dp[:, 0:128]   = [T1 ; T2] K              lanes 0-63: -W                          (prep)
-//   Dp[:, 128:192] = [T2 ; 0] V               lanes 0-63: U'                          (prep)
-//   Dp[:, 128:192] += [-W ; Q~] S             lanes 0-63: U = U' - W S, lanes 64-127: Q~ S
-//   Dp[:, 128:192] += [* ; QKm] U             lanes 64-127: O (lanes 0-63 are dead by then)
-//   Ds  = Kt^T U                              S_next = e^{G_C} S + Ds
+// Products of chunk c (M = 128 TMEM lanes, fp32 accumulators; "lanes 0-63" are the chunk's tokens in the
+// upper half, "lanes 64-127" in the lower half).  Slot s = c & 1 of TMEM holds 192 columns:
+//   Dp[:, 0:128]   = [T2 ; T1] K            lanes 64-127: -W (prep MMA; lanes 0-63 dead)
+//   Dp[:, 128:192] = [0 ; T2] V             lanes 64-127: U'
+//   A1 = Dp[:, 0:64] as bf16 pairs          lanes 0-63: Q~ (prep warps 4-5), lanes 64-127: -W (prep warps 6-7,
+//                                           converted in place)
+//   A2 = Dp[:, 64:96] as bf16 pairs         lanes 0-63: QKm (prep warps 4-5); lanes 64-127 dead
+//   Dp[:, 128:192] += A1 S                  lanes 0-63: Q~ S, lanes 64-127: U = U' - W S    (tensor-memory A)
+//   Ds  = Kt^T U                            S_next = e^{G_C} S + Ds
+//   Dp[:, 128:192] += A2 U                  lanes 0-63: O (lanes 64-127 are dead by then)  (tensor-memory A)
+//   Dq  = [Q ; *] K^T                       lanes 0-63: Q K^T (prep)
 // with T1 = T diag(-b e^G), T2 = T diag(b) (from chunk_solve_kernel), Q~ = q_scale e^G Q,
 // Kt = e^{G_C - G} K and QKm = q_scale e^{G_i - G_j} Q K^T (j <= i); "*" rows only reach dead lanes.
+// The chain's A operands never touch shared memory: the tensor cores read them from TMEM, and shared memory
+// carries only the B operands (S, U), the TMA stages and Kt -- the kernel is bound by shared-memory traffic
+// and the chain's round trips, so this is what sets its speed.
 // Roles (352 threads):
-//   warps 0-3  state: thread r owns row r of the fp32 state slice (64 columns, registers) and TMEM
-//              lane r; warps 0-1 turn Dp into U (bf16), all four form the next S (bf16 copy for the
-//              MMA), warps 2-3 store O.
-//   warps 4-7  prep, one chunk ahead of the state: QKm and -W (from TMEM, warps 4-5, which own lanes
-//              0-63); Q~ and Kt (bf16x2 products from the TMA stage, warps 6-7).
+//   warps 0-3  state: thread r owns row r of the fp32 state slice (64 columns, registers) and TMEM lane r;
+//              all four form the next S (bf16 copy for the MMA); warps 2-3 turn U (lanes 64-127) into the bf16
+//              B operand; warps 0-1 store O (lanes 0-63).
+//   warps 4-7  prep, ahead of the state by up to two chunks: warps 4-5 (lanes 0-63) QKm from Dq and Q~ from the
+//              TMA stage into A1 / A2; warps 6-7 (lanes 64-127) -W into A1, Kt into its shared buffer (two).
 //   warp 8     MMA issuer of the state chain; owns the TMEM allocation.
 //   warp 9     MMA issuer of the prep products (Dq, Dp).
 //   warp 10    TMA producer (two stages); its lanes also copy the chunk's G into the stage.
 // Every wait is a bounded mbarrier wait; the prep warps agree on aborting through a barrier reduction.
 constexpr int kThreads = 352;
-// one stage: [Q box0 | K box0 | Q box1 | K box1] 32 KB, V 8 KB, T1 8 KB, T2 8 KB, zeros 8 KB, G 256 B
-constexpr int SL_V = 32768, SL_T1 = 40960, SL_T2 = 49152, SL_Z = 57344, SL_G = 65536, SLOT = 66560;
+// one stage: [Q box0 | K box0 | Q box1 | K box1] 32 KB, V 8 KB, zeros 8 KB, T2 8 KB, T1 8 KB, G 256 B
+// ([0 ; T2] and [T2 ; T1] are the A operands of U' and -W: 128 rows from one start)
+constexpr int SL_V = 32768, SL_Z = 40960, SL_T2 = 49152, SL_T1 = 57344, SL_G = 65536, SLOT = 66560;
 constexpr int STAGE_TX = 57344;               // bytes TMA brings per stage
-constexpr int OFF_WQ = 2 * SLOT;              // [-W box0 | Q~ box0 | -W box1 | Q~ box1]: A of the S product
-constexpr int OFF_QKM = OFF_WQ + 32768;       // QKm; the 8 KB before it stand in as the dead A rows 0-63
-constexpr int OFF_KT = OFF_QKM + 8192;        // Kt, 2 boxes
-constexpr int OFF_SB = OFF_KT + 16384;        // S slice, bf16 [128 key rows][64 columns]
+constexpr int OFF_KT = 2 * SLOT;              // Kt of chunks c & 1 = 0 / 1, 2 boxes each
+constexpr int OFF_SB = OFF_KT + 32768;        // S slice, bf16 [128 key rows][64 columns]
 constexpr int OFF_U = OFF_SB + 16384;         // U, bf16 [64 tokens][64 columns]
 constexpr int OFF_VEC = OFF_U + 8192;         // bf16x2 pairs q_scale e^G, e^{G_C - G}; fp32 e^{g} [64 each]; e^{G_C} ring [4]
 constexpr int OFF_BAR = OFF_VEC + 1024;
@@ -241,14 +248,15 @@ enum {
     B_EMPTY = 2,     // [2] stage consumed (prep MMAs + 128 prep threads)
     B_QDONE = 4,     // Dq ready
     B_DQFREE = 5,    // Dq read (warps 4-5)
-    B_PDONE = 6,     // [2] Dp of the slot ready (a ring: the prep issuer may run a chunk ahead of the reader)
-    B_DPFREE = 8,    // [2] O of the slot read (warps 2-3)
-    B_PREP = 10,     // [2] -W, Q~, QKm, Kt and the gates of the chunk written (prep)
-    B_M1 = 12,       // S product done: U in TMEM; -W / Q~ free
-    B_UREADY = 13,   // U written (warps 0-1)
-    B_M23 = 14,      // O and Ds done; U, QKm, Kt free
-    B_SREADY = 15,   // next S written (state)
-    B_COUNT = 16
+    B_PDONE = 6,     // [2] Dp of the slot ready; the slot's A1 / A2 and Kt buffer free to write
+    B_DPFREE = 8,    // [2] O of the slot read (warps 0-1)
+    B_PREP = 10,     // [2] A1, A2, Kt and the gates of the chunk written (prep)
+    B_M1 = 12,       // S product done: U in TMEM
+    B_UREADY = 13,   // U written (warps 2-3)
+    B_DS = 14,       // Ds done; U's first reader done
+    B_ODONE = 15,    // [2] O of the slot done
+    B_SREADY = 17,   // next S written (state)
+    B_COUNT = 18
 };
 
 struct ChunkArgs {
@@ -313,11 +321,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar(B_PDONE + 1), 1);
         mbar_init(bar(B_M1), 1);
         mbar_init(bar(B_UREADY), 64);
-        mbar_init(bar(B_M23), 1);
+        mbar_init(bar(B_DS), 1);
+        mbar_init(bar(B_ODONE), 1);
+        mbar_init(bar(B_ODONE + 1), 1);
         mbar_init(bar(B_SREADY), 128);
         fence_barrier_init();
     }
-    // zero rows 64-127 of the [T2 ; 0] operand of both stages (TMA never writes them)
+    // zero rows 0-63 of the [0 ; T2] operand of both stages (TMA never writes them)
     for (int e = tid; e < 2 * 512; e += kThreads)
         reinterpret_cast<uint4 *>(sm + (e >> 9) * SLOT + SL_Z)[e & 511] = make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem();
@@ -353,18 +363,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t dcol = tmem + lane_off + slot * 192 + 128;
             if (!mbar_wait(bar(B_PREP + slot), (c >> 1) & 1, p.dev_err)) { ok = false; break; }
             const float dC = dCv[c & 3];
-            if (warp < 2) {
+            if (warp >= 2) {  // U (lanes 64-127) -> the bf16 B operand of Ds and O
                 if (!mbar_wait(bar(B_M1), c & 1, p.dev_err)) { ok = false; break; }
                 tc_fence_after();
                 float u[64];
                 tmem_ld64(dcol, u);
                 tmem_wait_ld();
-                store_row64(sm + OFF_U, r, u, 1.f);
+                store_row64(sm + OFF_U, r - 64, u, 1.f);
                 fence_proxy_async_smem();
                 tc_fence_before();
                 mbar_arrive(bar(B_UREADY));
             }
-            if (!mbar_wait(bar(B_M23), c & 1, p.dev_err)) { ok = false; break; }
+            if (!mbar_wait(bar(B_DS), c & 1, p.dev_err)) { ok = false; break; }
             tc_fence_after();
             {
                 float d[64];
@@ -375,14 +385,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             store_row64(sm + OFF_SB, r, S, 1.f);
             fence_proxy_async_smem();
-            if (warp >= 2) {
+            tc_fence_before();
+            mbar_arrive(bar(B_SREADY));
+            if (warp < 2) {  // O (lanes 0-63)
+                if (!mbar_wait(bar(B_ODONE + slot), (c >> 1) & 1, p.dev_err)) { ok = false; break; }
+                tc_fence_after();
                 float o[64];
                 tmem_ld64(dcol, o);
                 tmem_wait_ld();
                 tc_fence_before();
-                mbar_arrive(bar(B_SREADY));
                 mbar_arrive(bar(B_DPFREE + slot));
-                const int t = c * C + r - 64;
+                const int t = c * C + r;
                 if (t < p.T) {
                     const size_t orow = (((size_t)b * p.T + t) * p.H + h) * p.dv + slice * DS;
                     store_scaled32(p.o + orow, p.o_f32 ? p.o_f32 + orow : nullptr, *reinterpret_cast<float(*)[32]>(o),
@@ -390,9 +403,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     store_scaled32(p.o + orow + 32, p.o_f32 ? p.o_f32 + orow + 32 : nullptr,
                                    *reinterpret_cast<float(*)[32]>(o + 32), 1.f);
                 }
-            } else {
-                tc_fence_before();
-                mbar_arrive(bar(B_SREADY));
             }
         }
         if (ok) {
@@ -419,6 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (pt == 0) dCv[c & 3] = expf(GC);
             }
             named_bar_sync(1, 128);
+            const uint32_t a1 = tmem + lane_off + s * 192;  // A1 = slot columns 0-63, A2 = 64-95
             if (pw < 2) {
                 const int i = pt;
                 // QKm row i from Dq
@@ -431,10 +442,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_before();
                 mbar_arrive(bar(B_DQFREE));
+                uint32_t qk[32];
                 {
-                    // q_scale e^{G_i - G_j} for j <= i as a running product of the per-token decays from j = i
-                    // down (e^{G_i - G_{j-1}} = e^{G_i - G_j} e^{g_j}): no exponentials, values only shrink.
-                    // Columns right of the warp's last row are all masked (a warp-uniform test).
                     const int jmax = pw * 32 + 31;
                     float e = p.q_scale;
 #pragma unroll
@@ -455,53 +464,67 @@ __global__ void __launch_bounds__(kThreads, 1)
                             e = in ? e * d[q] : e;
                         }
                     }
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) qk[q] = pack_bf16x2(a[2 * q], a[2 * q + 1]);
                 }
-                mbar_arrive(bar(B_EMPTY + s));  // last read of the stage by this thread
-                // QKm, -W and Q~ of chunk c - 1 are consumed once its O / Ds products completed
-                if (ok && c >= 1) ok = mbar_wait(bar(B_M23), (c - 1) & 1, p.dev_err);
-                if (ok) store_row64(sm + OFF_QKM, i, a, 1.f);
-                // -W row i from Dp
                 if (ok) ok = mbar_wait(bar(B_PDONE + s), (c >> 1) & 1, p.dev_err);
                 if (ok) {
                     tc_fence_after();
+                    tmem_st32u(a1 + 64, qk);
+                    // Q~ row i = q_scale e^{G_i} Q row i (bf16 products) from the stage's two Q boxes, one box
+                    // (32 columns of pairs) at a time
+                    const uint32_t f2 = fq2[i];
 #pragma unroll
-                    for (int kb = 0; kb < 2; ++kb) {
-                        tmem_ld64(tmem + lane_off + s * 192 + kb * 64, a);
-                        tmem_wait_ld();
-                        store_row64(sm + OFF_WQ + kb * 16384, i, a, 1.f);
+                    for (int bx = 0; bx < 2; ++bx) {
+                        uint32_t qt[32];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const uint4 v = scale8(*reinterpret_cast<const uint4 *>(stg + bx * 16384 + swz(i, u)), f2);
+                            qt[4 * u] = v.x;
+                            qt[4 * u + 1] = v.y;
+                            qt[4 * u + 2] = v.z;
+                            qt[4 * u + 3] = v.w;
+                        }
+                        tmem_st32u(a1 + 32 * bx, qt);
                     }
                 }
+                mbar_arrive(bar(B_EMPTY + s));  // last read of the stage by this thread
             } else {
                 // thread q handles 16-byte unit q & 7 of rows (q >> 3) + 8 m (m < 8) of both 64-column boxes:
                 // the swizzled offset is a per-thread constant plus 1024 m
                 const int q = pt - 64, j0 = q >> 3;
                 const uint32_t off0 = swz(j0, q & 7);
-                // each product is formed in registers (all loads first) before its buffer frees
                 uint4 t[16];
-#pragma unroll
-                for (int n = 0; n < 16; ++n)  // Q~ = q_scale e^G Q
-                    t[n] = *reinterpret_cast<const uint4 *>(stg + (n >> 3) * 16384 + off0 + (n & 7) * 1024);
-#pragma unroll
-                for (int n = 0; n < 16; ++n) t[n] = scale8(t[n], fq2[j0 + 8 * (n & 7)]);
-                if (ok && c >= 1) ok = mbar_wait(bar(B_M1), (c - 1) & 1, p.dev_err);  // Q~ rows free
-                if (ok) {
-#pragma unroll
-                    for (int n = 0; n < 16; ++n)  // into rows 64-127 of -W | Q~
-                        *reinterpret_cast<uint4 *>(sm + OFF_WQ + 8192 + (n >> 3) * 16384 + off0 + (n & 7) * 1024) = t[n];
-                }
 #pragma unroll
                 for (int n = 0; n < 16; ++n)  // Kt = e^{G_C - G} K
                     t[n] = *reinterpret_cast<const uint4 *>(stg + (n >> 3) * 16384 + 8192 + off0 + (n & 7) * 1024);
 #pragma unroll
                 for (int n = 0; n < 16; ++n) t[n] = scale8(t[n], fk2[j0 + 8 * (n & 7)]);
                 mbar_arrive(bar(B_EMPTY + s));
-                if (ok && c >= 1) ok = mbar_wait(bar(B_M23), (c - 1) & 1, p.dev_err);  // Kt free
+                // the slot's Dp has landed, and with it the Kt buffer of chunk c - 2 is free (its O product
+                // completed before the O read that let the prep issuer fill this slot)
+                if (ok) ok = mbar_wait(bar(B_PDONE + s), (c >> 1) & 1, p.dev_err);
                 if (ok) {
 #pragma unroll
                     for (int n = 0; n < 16; ++n)
-                        *reinterpret_cast<uint4 *>(sm + OFF_KT + (n >> 3) * 8192 + off0 + (n & 7) * 1024) = t[n];
+                        *reinterpret_cast<uint4 *>(sm + OFF_KT + s * 16384 + (n >> 3) * 8192 + off0 + (n & 7) * 1024) =
+                            t[n];
+                    // -W (lanes 64-127, fp32 columns 0-127) -> bf16 pairs in columns 0-63, in place: each half is
+                    // read completely before its pairs overwrite the columns it came from
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int hh = 0; hh < 2; ++hh) {
+                        float w[64];
+                        tmem_ld64(a1 + 64 * hh, w);
+                        tmem_wait_ld();
+                        uint32_t wp[32];
+#pragma unroll
+                        for (int k2 = 0; k2 < 32; ++k2) wp[k2] = pack_bf16x2(w[2 * k2], w[2 * k2 + 1]);
+                        tmem_st32u(a1 + 32 * hh, wp);
+                    }
                 }
             }
+            tmem_wait_st();
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(bar(B_PREP + s));
@@ -516,31 +539,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t last_par = 0;
             for (int c = 0; c < n_chunks; ++c) {
                 const int slot = c & 1;
-                const uint32_t dcol = tmem + slot * 192 + 128;
+                const uint32_t dcol = tmem + slot * 192 + 128, a1 = tmem + slot * 192;
                 if (!mbar_wait(bar(B_SREADY), c & 1, p.dev_err)) break;
                 if (!mbar_wait(bar(B_PREP + slot), (c >> 1) & 1, p.dev_err)) break;
                 tc_fence_after();
+                // [Q~ ; -W] S: A from tensor memory (8 columns of bf16 pairs per K step of 16)
 #pragma unroll
-                for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_bf16_ss(dcol, umma_desc_sw128(sb + OFF_WQ + kb * 16384 + kk * 32, 16, 1024),
-                                     umma_desc_sw128(sb + OFF_SB + (kb * 4 + kk) * 2048, 8192, 1024), id_kmn, 1);
+                for (int ks = 0; ks < 8; ++ks)
+                    umma_bf16_ts(dcol, a1 + ks * 8, umma_desc_sw128(sb + OFF_SB + ks * 2048, 8192, 1024), id_kmn, 1);
                 umma_commit(bar(B_M1));
                 last_bar = B_M1;
                 last_par = c & 1;
                 if (!mbar_wait(bar(B_UREADY), c & 1, p.dev_err)) break;
                 tc_fence_after();
+                // Ds = Kt^T U first (the state chain waits for it), then O += QKm U
+                const uint32_t kt = sb + OFF_KT + slot * 16384;
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16_ss(dcol, umma_desc_sw128(sb + OFF_QKM - 8192 + kk * 32, 16, 1024),
-                                 umma_desc_sw128(sb + OFF_U + kk * 2048, 8192, 1024), id_kmn, 1);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16_ss(tmem + TM_DS, umma_desc_sw128(sb + OFF_KT + kk * 2048, 8192, 1024),
+                    umma_bf16_ss(tmem + TM_DS, umma_desc_sw128(kt + kk * 2048, 8192, 1024),
                                  umma_desc_sw128(sb + OFF_U + kk * 2048, 8192, 1024), id_mnmn, kk > 0);
-                umma_commit(bar(B_M23));
-                last_bar = B_M23;
+                umma_commit(bar(B_DS));
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16_ts(dcol, a1 + 64 + kk * 8, umma_desc_sw128(sb + OFF_U + kk * 2048, 8192, 1024), id_kmn, 1);
+                umma_commit(bar(B_ODONE + slot));
+                last_bar = B_ODONE + slot;
+                last_par = (c >> 1) & 1;
             }
             if (last_bar >= 0) mbar_wait(bar(last_bar), last_par, p.dev_err);  // own MMAs drained
         }
@@ -569,14 +593,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 last_par = c & 1;
                 if (c >= 2 && !mbar_wait(bar(B_DPFREE + s), ((c - 2) >> 1) & 1, p.dev_err)) break;
                 tc_fence_after();
-                // -W = T1 K (B = K key-major: two 64-column groups 16 KB apart) and U' = T2 V
+                // -W = T1 K into lanes 64-127 (A = [T2 ; T1]; B = K key-major: two 64-column groups 16 KB apart)
+                // and U' = T2 V into lanes 64-127 (A = [0 ; T2])
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16_ss(tmem + s * 192, umma_desc_sw128(stg + SL_T1 + kk * 32, 16, 1024),
+                    umma_bf16_ss(tmem + s * 192, umma_desc_sw128(stg + SL_T2 + kk * 32, 16, 1024),
                                  umma_desc_sw128(stg + 8192 + kk * 2048, 16384, 1024), id_w, kk > 0);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16_ss(tmem + s * 192 + 128, umma_desc_sw128(stg + SL_T2 + kk * 32, 16, 1024),
+                    umma_bf16_ss(tmem + s * 192 + 128, umma_desc_sw128(stg + SL_Z + kk * 32, 16, 1024),
                                  umma_desc_sw128(stg + SL_V + kk * 2048, 8192, 1024), id_u, kk > 0);
                 umma_commit(bar(B_PDONE + s));
                 umma_commit(bar(B_EMPTY + s));
