@@ -1099,8 +1099,7 @@ def main():
 
         import torch.distributed as tdist
         torch.cuda.set_device(local_rank)
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                 device_id=torch.device("cuda", local_rank))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         dist = tdist
     if args.workload in ("prefill", "chunked", "decode", "recurrent"):
         run = {"prefill": run_prefill, "chunked": run_chunked, "decode": run_decode,
