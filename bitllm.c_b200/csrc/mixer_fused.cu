@@ -7,10 +7,11 @@
 //   (:642-653).  One CTA per (sequence, head): it owns that head's q, k and v conv channels (so every
 //   conv-window row is updated by exactly one CTA) and all d_v columns of S (so the RMSNorm of the
 //   head's output row closes inside the CTA).  S crosses HBM once each way.
-//   S is read from global memory twice and never staged: an L2 prefetch of the head's S starts with the
-//   CTA, the retrieve pass reads it after the conv and the norms, the update pass re-reads it from L2
-//   (at four CTAs of 256 threads per SM at most 38 MB of state is in flight, well inside L2).  Without a shared-memory copy of S, four CTAs fit per SM and
-//   up to 4 x SMs heads run in one wave (a copy of the head's S in shared memory allows three, and at
+//   The S reads are all issued when the CTA starts, before the conv: the first half of the head's rows
+//   by bulk copies into shared memory, the second half by each thread into registers (eight float4
+//   rows), so one memory round trip overlaps the conv and the norms, and both passes over S (retrieve,
+//   then update + output) read on-chip copies.  32 KB of shared memory and 64 registers per CTA: four CTAs
+//   fit per SM, so up to 4 x SMs heads run in one wave (a whole head in shared memory allows three, and at
 //   small batches its second wave of a few CTAs set the time).
 //
 // fullatt_prep_kernel: fullatt_prep (src/eif_qwen35.c:699-737) for one token of every sequence:
@@ -44,15 +45,31 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
     const size_t bh = (size_t)b * H + h;
     const int key_dim = H * DK, conv_dim = 2 * key_dim + H * DV;
 
+    constexpr int NH = NP / 2;  // passes over the rows staged in shared memory; the other NH in registers
     __shared__ float sq[DK], sk[DK], sv[DV];
     __shared__ float red[NW];
     __shared__ float4 cred[NW][LPR];
     __shared__ float gates[2];
+    __shared__ __align__(8) uint64_t s_bar;
+    extern __shared__ __align__(128) float Ssm[];  // S rows [0, DK/2)
 
     float *Sh = a.S + bh * DK * DV;
     const int col0 = lc * 4;
-    // the head's S starts towards L2 now, so that the retrieve pass after the conv and the norms finds it there
-    if (tid < DK * DV * 4 / 16384) bulk_prefetch_l2(Sh + tid * 4096, 16384);
+    const float4 *Srow = reinterpret_cast<const float4 *>(Sh) + col0 / 4;
+    const float4 *Smem = reinterpret_cast<const float4 *>(Ssm) + col0 / 4;
+    // S rows [0, DK/2) into shared memory (bulk copies completing on s_bar), rows [DK/2, DK) into registers
+    const uint32_t sbar = smem_u32(&s_bar);
+    if (tid == 0) {
+        constexpr uint32_t bytes = DK / 2 * DV * 4, piece = bytes < 16384 ? bytes : 16384;
+        mbar_init(sbar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(sbar, bytes);
+        for (uint32_t off = 0; off < bytes; off += piece)
+            bulk_load(smem_u32(Ssm) + off, reinterpret_cast<const char *>(Sh) + off, piece, sbar);
+    }
+    float4 sreg[NH];
+#pragma unroll
+    for (int u = 0; u < NH; ++u) sreg[u] = Srow[(rg + (NH + u) * RP) * (DV / 4)];
 
     // causal conv1d + SiLU on this head's channels: q [h*DK, +DK), k [key_dim + h*DK, +DK), v [2*key_dim + h*DV, +DV)
     const int ck = a.conv_k;
@@ -120,45 +137,31 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
 
     const float decay = expf(gates[1]), bet = gates[0];
     // a wait that gives up leaves S untouched (the error word tells the host)
-    const float4 *Srow = reinterpret_cast<const float4 *>(Sh) + col0 / 4;
-    // rows go in batches of SB loads before their arithmetic, so that the loads of a batch are in flight
-    // together (the update pass stores to the rows it reads, and the compiler would not move a later
-    // load above such a store)
-    constexpr int SB = NP < 8 ? NP : 8;
+    const bool s_ok = mbar_wait(sbar, 0, a.dev_err);
+    // pass p reads row rg + p * RP: from shared memory for p < NH, from registers after
+    auto row = [&](int p) -> float4 { return p < NH ? Smem[(rg + p * RP) * (DV / 4)] : sreg[p - NH]; };
     float4 e = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int p0 = 0; p0 < NP; p0 += SB) {
-        float4 sr[SB];
-#pragma unroll
-        for (int u = 0; u < SB; ++u) sr[u] = Srow[(rg + (p0 + u) * RP) * (DV / 4)];
-#pragma unroll
-        for (int u = 0; u < SB; ++u) {
-            const float ki = sk[rg + (p0 + u) * RP];
-            float4 s = sr[u];
-            s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;
-            e.x += s.x * ki; e.y += s.y * ki; e.z += s.z * ki; e.w += s.w * ki;
-        }
+    for (int p = 0; p < NP; ++p) {
+        const float ki = sk[rg + p * RP];
+        float4 s = row(p);
+        s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;
+        e.x += s.x * ki; e.y += s.y * ki; e.z += s.z * ki; e.w += s.w * ki;
     }
     e = colsum(e);
     const float4 vv = make_float4(sv[col0], sv[col0 + 1], sv[col0 + 2], sv[col0 + 3]);
     const float4 dlt = make_float4(vv.x - e.x, vv.y - e.y, vv.z - e.z, vv.w - e.w);
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int p0 = 0; p0 < NP; p0 += SB) {
-        float4 sr[SB];
-#pragma unroll
-        for (int u = 0; u < SB; ++u) sr[u] = Srow[(rg + (p0 + u) * RP) * (DV / 4)];
-#pragma unroll
-        for (int u = 0; u < SB; ++u) {
-            const int i = rg + (p0 + u) * RP;
-            const float ki = bet * sk[i];
-            float4 s = sr[u];
-            s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;  // as in the first pass
-            s.x += ki * dlt.x; s.y += ki * dlt.y; s.z += ki * dlt.z; s.w += ki * dlt.w;
-            __stcs(reinterpret_cast<float4 *>(Sh + (size_t)i * DV + col0), s);
-            const float qi = sq[i];
-            o.x += s.x * qi; o.y += s.y * qi; o.z += s.z * qi; o.w += s.w * qi;
-        }
+    for (int p = 0; p < NP; ++p) {
+        const int i = rg + p * RP;
+        const float ki = bet * sk[i];
+        float4 s = row(p);
+        s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;  // as in the first pass
+        s.x += ki * dlt.x; s.y += ki * dlt.y; s.z += ki * dlt.z; s.w += ki * dlt.w;
+        if (s_ok) __stcs(reinterpret_cast<float4 *>(Sh + (size_t)i * DV + col0), s);
+        const float qi = sq[i];
+        o.x += s.x * qi; o.y += s.y * qi; o.z += s.z * qi; o.w += s.w * qi;
     }
     o = colsum(o);
     // gated RMSNorm over the head's d_v outputs (threads of row group 0 hold the whole row)
@@ -357,13 +360,13 @@ __global__ void __launch_bounds__(256) fullatt_prep_warp_kernel(const AttnPrepAr
 cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *supported) {
     *supported = true;
     const dim3 grid(a.H, a.B);
-    auto run = [&](auto kernel, int threads) {
-        kernel<<<grid, threads, 0, st>>>(a);
+    auto run = [&](auto kernel, int threads, int smem) {  // smem: S rows [0, dk/2), at most 32 KB
+        kernel<<<grid, threads, smem, st>>>(a);
         return cudaGetLastError();
     };
-    if (a.dk == 128 && a.dv == 128) return run(deltanet_core_kernel<128, 128, 256>, 256);
-    if (a.dk == 128 && a.dv == 64) return run(deltanet_core_kernel<128, 64, 256>, 256);
-    if (a.dk == 64 && a.dv == 64) return run(deltanet_core_kernel<64, 64, 128>, 128);
+    if (a.dk == 128 && a.dv == 128) return run(deltanet_core_kernel<128, 128, 256>, 256, 64 * 128 * 4);
+    if (a.dk == 128 && a.dv == 64) return run(deltanet_core_kernel<128, 64, 256>, 256, 64 * 64 * 4);
+    if (a.dk == 64 && a.dv == 64) return run(deltanet_core_kernel<64, 64, 128>, 128, 32 * 64 * 4);
     *supported = false;
     return cudaSuccess;
 }
