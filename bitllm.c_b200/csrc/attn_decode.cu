@@ -263,11 +263,16 @@ struct Split {
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// Scratch bytes of the chunk partials: o [units][nchunk][G][D] and (m, l) [units][nchunk][G].
-size_t partials_bytes(const DecodeArgs &a, int nchunk) {
+// Partials each item leaves: the bf16 tensor-core kernel writes one per consumer warp (its four warps need
+// no merge in shared memory, and the combine weighs them like chunks); the other kernels one per item.
+int item_partials(const DecodeArgs &a, bool tc) { return tc && a.dtype == EIF_CUDA_BF16 ? 4 : 1; }
+
+// Scratch bytes of the chunk partials: o [units][nchunk * ip][G][D] and (m, l) [units][nchunk * ip][G].
+size_t partials_bytes(const DecodeArgs &a, int nchunk, int ip = 1) {
     const size_t units = (size_t)a.B * a.Hkv;
     const size_t G = (size_t)(a.Hq / a.Hkv);
-    return align256(units * nchunk * G * a.D * sizeof(float)) + align256(units * nchunk * G * sizeof(float2));
+    const size_t n = (size_t)nchunk * ip;
+    return align256(units * n * G * a.D * sizeof(float)) + align256(units * n * G * sizeof(float2));
 }
 
 // The TMA-fed persistent kernels: bf16 / INT8 caches on the tensor cores, fp32 caches in fp32 FMAs.
@@ -300,7 +305,7 @@ Split choose_split_tc(const DecodeArgs &a, int sm_count) {
         const long ct = (tpu + nc - 1) / nc;
         const long ncu = (tpu + ct - 1) / ct;  // chunks actually used
         const long items = units * ncu;
-        if (a.max_ws_bytes && ncu > 1 && partials_bytes(a, (int)ncu) > a.max_ws_bytes) break;
+        if (a.max_ws_bytes && ncu > 1 && partials_bytes(a, (int)ncu, item_partials(a, true)) > a.max_ws_bytes) break;
         const long per_cta = (items + sm_count - 1) / sm_count;
         const double busiest = per_cta * ct * tile_bytes;
         const double cost = (elastic ? fmax(fair, busiest / 1.5) : busiest) + per_cta * item_bytes;
@@ -367,9 +372,7 @@ cudaError_t dispatch_d(cudaStream_t st, const DecodeArgs &a, const Split &sp, fl
 
 size_t decode_workspace_bytes(const DecodeArgs &a, int sm_count) {
     const Split sp = choose_split(a, sm_count);
-    const size_t units = (size_t)a.B * a.Hkv;
-    const int G = a.Hq / a.Hkv;
-    return align256(units * sp.nchunk * G * a.D * sizeof(float)) + align256(units * sp.nchunk * G * sizeof(float2));
+    return partials_bytes(a, sp.nchunk, item_partials(a, sp.tc));
 }
 
 cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws, size_t ws_bytes, int sm_count,
@@ -379,8 +382,9 @@ cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws,
     const Split sp = choose_split(a, sm_count);
     const size_t units = (size_t)a.B * a.Hkv;
     const int G = a.Hq / a.Hkv;
-    const size_t o_bytes = align256(units * sp.nchunk * G * a.D * sizeof(float));
-    if (o_bytes + align256(units * sp.nchunk * G * sizeof(float2)) > ws_bytes) return cudaErrorInvalidValue;
+    const int n_part = sp.nchunk * item_partials(a, sp.tc);  // partials per unit, merged by the combine
+    const size_t o_bytes = align256(units * n_part * G * a.D * sizeof(float));
+    if (partials_bytes(a, sp.nchunk, item_partials(a, sp.tc)) > ws_bytes) return cudaErrorInvalidValue;
     float *part_o = static_cast<float *>(ws);
     float2 *part_ml = reinterpret_cast<float2 *>(static_cast<char *>(ws) + o_bytes);
     cudaError_t e;
@@ -398,12 +402,12 @@ cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws,
         e = dispatch_d<__nv_bfloat16>(st, a, sp, part_o, part_ml, supported);
     if (!*supported || e != cudaSuccess) return e;
     ++*n_launches;
-    const size_t smem = ((size_t)a.Hq * sp.nchunk + (size_t)a.Hq * a.D) * sizeof(float);
+    const size_t smem = ((size_t)a.Hq * n_part + (size_t)a.Hq * a.D) * sizeof(float);
     if (smem > 48 * 1024) {
         e = cudaFuncSetAttribute(attn_decode_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    attn_decode_combine_kernel<<<a.B, 256, smem, st>>>(part_o, part_ml, a.Hq, a.Hkv, a.D, sp.nchunk, a.gate,
+    attn_decode_combine_kernel<<<a.B, 256, smem, st>>>(part_o, part_ml, a.Hq, a.Hkv, a.D, n_part, a.gate,
                                                          a.subln, a.sub_norm, a.out);
     ++*n_launches;
     return cudaGetLastError();

@@ -2,7 +2,8 @@
 //
 // Same contract as the SIMT kernel of attn_decode.cu (fullatt_attend's head loop,
 // src/eif_qwen35.c:741-771; tinyllm decode, src/eif_tinyllm.c:555-656): every (sequence, kv head,
-// key chunk) item leaves an unnormalised partial (m, l, o[G][D]) that attn_decode_combine merges.
+// key chunk) item leaves unnormalised partials (m, l, o[G][D]) -- one per consumer warp, over the warp's
+// 16 keys of every tile -- that attn_decode_combine merges with the other chunks'.
 //
 // Structure (persistent, one CTA per SM, 5 warps):
 //   warp 4  producer: one lane streams K and V tiles of 64 keys x D through an NS-stage ring with
@@ -36,9 +37,7 @@ struct TcCfg {
     static constexpr int BOX = 64 * 128;              // one 64-key x 64-dim swizzled box, bytes
     static constexpr int TILE = (D / 64) * BOX;       // K (or V) tile bytes
     static constexpr int STAGE = 2 * TILE;
-    static constexpr int EXTRA = kConsumers * HS * D * 4      // merge buffer o
-                                 + 2 * kConsumers * HS * 4    // merge m, l
-                                 + kConsumers * 16 * HS * 4   // P transpose
+    static constexpr int EXTRA = kConsumers * 16 * HS * 4   // P transpose
                                  + 64 * 8                     // barriers
                                  + 1024;                      // alignment slack
     static constexpr int NS = ((kSmemLimit - EXTRA) / STAGE) > 8 ? 8 : ((kSmemLimit - EXTRA) / STAGE);
@@ -85,14 +84,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int NS = C::NS, HS = C::HS, MT = D / 16;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_align1024(smem_raw);
-    float *ow = reinterpret_cast<float *>(smem + NS * C::STAGE);   // [4][HS][D]
-    float *mw = ow + kConsumers * HS * D;                          // [4][HS]
-    float *lw = mw + kConsumers * HS;                              // [4][HS]
-    float *pbuf = lw + kConsumers * HS;                            // [4][16][HS]
+    float *pbuf = reinterpret_cast<float *>(smem + NS * C::STAGE);  // [4][16][HS]
     uint64_t *bars = reinterpret_cast<uint64_t *>(pbuf + kConsumers * 16 * HS);
-    // bars: full[NS], empty[NS], merged, drained
+    // bars: full[NS], empty[NS]
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NS);
-    const uint32_t merged = smem_u32(bars + 2 * NS), drained = smem_u32(bars + 2 * NS + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -100,8 +95,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, kConsumers);
         }
-        mbar_init(merged, kConsumers);
-        mbar_init(drained, kConsumers);
         fence_barrier_init();
     }
     __syncthreads();
@@ -134,8 +127,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------------- consumers
     const int g = lane >> 2, t = lane & 3;
     float *pw = pbuf + warp * 16 * HS;
-    uint32_t it = 0, item_no = 0;
-    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++item_no) {
+    uint32_t it = 0;
+    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
         const ItemInfo inf = item_info(p, item, warp == 0 && lane == 0);
 
         // Q^T fragments: column g of the 8 is head (g & 3) of the block, hi part for g < 4, lo for g >= 4
@@ -306,8 +299,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(empty0 + 8 * s);
         }
 
-        // ---- item epilogue: reduce l over the 8 key lanes, add lo columns onto hi, merge the 4 warps
-        float lsum[NB][2];
+        // ---- item epilogue: reduce l over the 8 key lanes, add the lo columns onto hi, and write this warp's
+        // partial (m in natural-log units, l, o) as partial 4 * item + warp: the combine weighs the four warps'
+        // partials like chunks, so the warps never wait for one another
+        const size_t pbase = ((size_t)item * kConsumers + warp) * p.G;
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
@@ -316,11 +311,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 l += __shfl_xor_sync(0xffffffffu, l, 4);
                 l += __shfl_xor_sync(0xffffffffu, l, 8);
                 l += __shfl_xor_sync(0xffffffffu, l, 16);
-                lsum[nb][e] = l;
+                const int h = nb * 4 + 2 * t + e;
+                if (g == 0 && t < 2 && h < p.G) {
+                    const float m = m_run[nb][e];
+                    p.part_ml[pbase + h] = make_float2(m == -INFINITY ? -INFINITY : m * 0.69314718055994531f, l);
+                }
             }
-        // the previous item's merge must be finished reading ow before it is overwritten
-        if (item_no > 0 && !mbar_wait(drained, (item_no - 1) & 1, p.dev_err)) return;
-        float *oww = ow + warp * HS * D;
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
@@ -329,40 +325,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int r = 0; r < 4; ++r) {
                     float o = oacc[nb][mt][r];
                     o += __shfl_xor_sync(0xffffffffu, o, 2);
-                    if (t < 2) oww[(nb * 4 + 2 * t + (r & 1)) * D + mt * 16 + g + (r >> 1) * 8] = o;
+                    const int h = nb * 4 + 2 * t + (r & 1);
+                    if (t < 2 && h < p.G) p.part_o[(pbase + h) * D + mt * 16 + g + (r >> 1) * 8] = o;
                 }
-        if (g == 0 && t < 2) {
-#pragma unroll
-            for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    mw[warp * HS + nb * 4 + 2 * t + e] = m_run[nb][e];
-                    lw[warp * HS + nb * 4 + 2 * t + e] = lsum[nb][e];
-                }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(merged);
-        if (!mbar_wait(merged, item_no & 1, p.dev_err)) return;
-        const size_t pbase = (size_t)item * p.G;
-        for (int idx = threadIdx.x; idx < p.G * D; idx += 32 * kConsumers) {
-            const int h = idx / D, d = idx - h * D;
-            float M = -INFINITY;
-#pragma unroll
-            for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, mw[w * HS + h]);
-            float O = 0.f, L = 0.f;
-            if (M != -INFINITY) {
-#pragma unroll
-                for (int w = 0; w < kConsumers; ++w) {
-                    const float f = fast_exp2(mw[w * HS + h] - M);
-                    O += ow[(w * HS + h) * D + d] * f;
-                    L += lw[w * HS + h] * f;
-                }
-            }
-            p.part_o[(pbase + h) * D + d] = O;
-            if (d == 0) p.part_ml[pbase + h] = make_float2(M == -INFINITY ? -INFINITY : M * 0.69314718055994531f, L);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(drained);
     }
 }
 
