@@ -263,9 +263,9 @@ struct Split {
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// Partials each item leaves: the bf16 tensor-core kernel writes one per consumer warp (its four warps need
-// no merge in shared memory, and the combine weighs them like chunks); the other kernels one per item.
-int item_partials(const DecodeArgs &a, bool tc) { return tc && a.dtype == EIF_CUDA_BF16 ? 4 : 1; }
+// Partials each item leaves: the bf16 tensor-core kernel writes one per consumer warp (its warps need no
+// merge in shared memory, and the combine weighs them like chunks); the other kernels one per item.
+int item_partials(const DecodeArgs &a, bool tc) { return tc && a.dtype == EIF_CUDA_BF16 ? decode_tc_partials(a.D) : 1; }
 
 // Scratch bytes of the chunk partials: o [units][nchunk * ip][G][D] and (m, l) [units][nchunk * ip][G].
 size_t partials_bytes(const DecodeArgs &a, int nchunk, int ip = 1) {

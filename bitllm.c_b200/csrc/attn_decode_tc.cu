@@ -3,15 +3,16 @@
 // Same contract as the SIMT kernel of attn_decode.cu (fullatt_attend's head loop,
 // src/eif_qwen35.c:741-771; tinyllm decode, src/eif_tinyllm.c:555-656): every (sequence, kv head,
 // key chunk) item leaves unnormalised partials (m, l, o[G][D]) -- one per consumer warp, over the warp's
-// 16 keys of every tile -- that attn_decode_combine merges with the other chunks'.
+// 16 keys of its group's tiles -- that attn_decode_combine merges with the other chunks'.
 //
-// Structure (persistent, one CTA per SM, 5 warps):
-//   warp 4  producer: one lane streams K and V tiles of 64 keys x D through an NS-stage ring with
+// Structure (persistent, one CTA per SM; NG groups of 4 consumer warps + 1 producer warp, NG = 2 at
+// head_dim 64 / 128 and 1 at 256):
+//   last warp  producer: one lane streams K and V tiles of 64 keys x D through an NS-stage ring with
 //           3-D TMA tile loads (128-byte swizzle, no multicast) completing on "full" mbarriers;
-//   warps 0-3 consumers: each takes 16 keys of every tile.  S^T = K Q^T and O^T += V^T P^T run on
-//           the tensor cores (mma.m16n8k16, bf16 in, fp32 accumulate), fed by ldmatrix from the
-//           swizzled tiles; online softmax in base 2 with warp shuffles; the tile is released
-//           through an "empty" mbarrier.
+//   consumer groups take the tiles round-robin; each warp of a group takes 16 keys of its tiles.
+//           S^T = K Q^T and O^T += V^T P^T run on the tensor cores (mma.m16n8k16, bf16 in, fp32
+//           accumulate), fed by ldmatrix from the swizzled tiles; online softmax in base 2 with warp
+//           shuffles; the tile is released through an "empty" mbarrier (four arrivals, its group's).
 // Each K/V byte crosses HBM once and serves all G query heads of its kv head.
 //
 // Exactness: the query (pre-scaled by scale*log2 e) and the probabilities are split into two
@@ -27,23 +28,31 @@
 namespace {
 
 constexpr int KT = 64;              // keys per tile
-constexpr int kConsumers = 4;       // consumer warps, 16 keys each
-constexpr int kThreads = 32 * (kConsumers + 1);
+constexpr int kConsumers = 4;       // consumer warps of a group, 16 keys of a tile each
 constexpr int kSmemLimit = 227 * 1024;
 
-template <int D, int NB>
+// NG groups of four consumer warps take the tiles round-robin (two warps per SM sub-partition hide each
+// other's MMA / shuffle latencies at head_dim 64 / 128; head_dim 256 has the registers for one group)
+template <int D, int NB, int NG>
 struct TcCfg {
+    static constexpr int CW = kConsumers * NG;       // consumer warps
+    static constexpr int THREADS = 32 * (CW + 1);
     static constexpr int HS = 4 * NB;                 // head slots (G <= HS)
     static constexpr int BOX = 64 * 128;              // one 64-key x 64-dim swizzled box, bytes
     static constexpr int TILE = (D / 64) * BOX;       // K (or V) tile bytes
     static constexpr int STAGE = 2 * TILE;
-    static constexpr int EXTRA = kConsumers * 16 * HS * 4   // P transpose
-                                 + 64 * 8                     // barriers
-                                 + 1024;                      // alignment slack
-    static constexpr int NS = ((kSmemLimit - EXTRA) / STAGE) > 8 ? 8 : ((kSmemLimit - EXTRA) / STAGE);
+    static constexpr int EXTRA = CW * 16 * HS * 4     // P transpose
+                                 + 64 * 8             // barriers
+                                 + 1024;              // alignment slack
+    static constexpr int FIT = ((kSmemLimit - EXTRA) / STAGE) > 8 ? 8 : ((kSmemLimit - EXTRA) / STAGE);
+    // a multiple of the groups: a stage is always consumed by the same group, so a barrier's phase parity
+    // cannot alias between two groups' uses (their TMA copies may land out of order)
+    static constexpr int NS = FIT / NG * NG;
     static constexpr int SMEM = NS * STAGE + EXTRA;
     static_assert(NS >= 2, "pipeline needs two stages");
 };
+
+constexpr int tc_groups(int D) { return D <= 128 ? 2 : 1; }
 
 struct TcParams {
     const float *q;
@@ -76,16 +85,16 @@ __device__ __forceinline__ ItemInfo item_info(const TcParams &p, int item, bool 
     return it;
 }
 
-template <int D, int NB>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int D, int NB, int NG>
+__global__ void __launch_bounds__(TcCfg<D, NB, NG>::THREADS, 1)
     attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                           const TcParams p) {
-    using C = TcCfg<D, NB>;
+    using C = TcCfg<D, NB, NG>;
     constexpr int NS = C::NS, HS = C::HS, MT = D / 16;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_align1024(smem_raw);
     float *pbuf = reinterpret_cast<float *>(smem + NS * C::STAGE);  // [4][16][HS]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(pbuf + kConsumers * 16 * HS);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(pbuf + C::CW * 16 * HS);
     // bars: full[NS], empty[NS]
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NS);
 
@@ -99,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
 
-    if (warp == kConsumers) {
+    if (warp == C::CW) {
         // ------------------------------------------------------------------ producer
         if (lane != 0) return;
         prefetch_tmap(&tmK);
@@ -126,6 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---------------------------------------------------------------------- consumers
     const int g = lane >> 2, t = lane & 3;
+    const int grp = warp / kConsumers, sl = warp % kConsumers;  // group, 16-key slice of the tile
     float *pw = pbuf + warp * 16 * HS;
     uint32_t it = 0;
     for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
@@ -164,10 +174,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 
         for (int i = 0; i < inf.ntiles; ++i, ++it) {
+            if ((int)(it % NG) != grp) continue;  // another group's tile
             const uint32_t s = it % NS, ph = (it / NS) & 1;
             if (!mbar_wait(full0 + 8 * s, ph, p.dev_err)) return;
             const uint32_t kbase = smem_u32(smem + s * C::STAGE), vbase = kbase + C::TILE;
-            const int key0 = inf.t_begin + i * KT + warp * 16;  // first key of this warp
+            const int key0 = inf.t_begin + i * KT + sl * 16;  // first key of this warp
             const int nvalid = inf.t_end - key0;                // keys of the warp below t_end (may be <= 0)
 
             // ---- S^T = K Q^T over the head dim (two accumulator chains)
@@ -177,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 sb[nb][2] = sb[nb][3] = 0.f;
             {
                 const int mi = lane >> 3, r = lane & 7;
-                const int key = warp * 16 + (mi & 1) * 8 + r;
+                const int key = sl * 16 + (mi & 1) * 8 + r;
                 const uint32_t rowaddr = kbase + key * 128;
 #pragma unroll
                 for (int kc = 0; kc < MT; ++kc) {
@@ -269,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             //      turn 0 * v into NaN (only the last tile of a chunk can hold such keys)
             if (nvalid < 16) {
                 for (int r = max(nvalid, 0); r < 16; ++r) {
-                    const int key = warp * 16 + r;
+                    const int key = sl * 16 + r;
                     for (int j = lane; j < (D / 64) * 8; j += 32) {
                         uint4 *dst = reinterpret_cast<uint4 *>(smem + s * C::STAGE + C::TILE + (j >> 3) * C::BOX +
                                                                 key * 128 + (j & 7) * 16);
@@ -282,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---- O^T += V^T P^T over this warp's 16 keys
             {
                 const int mi = lane >> 3, r = lane & 7;
-                const int key = warp * 16 + (mi >> 1) * 8 + r;
+                const int key = sl * 16 + (mi >> 1) * 8 + r;
                 const uint32_t rowaddr = vbase + key * 128;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
@@ -302,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---- item epilogue: reduce l over the 8 key lanes, add the lo columns onto hi, and write this warp's
         // partial (m in natural-log units, l, o) as partial 4 * item + warp: the combine weighs the four warps'
         // partials like chunks, so the warps never wait for one another
-        const size_t pbase = ((size_t)item * kConsumers + warp) * p.G;
+        const size_t pbase = ((size_t)item * C::CW + warp) * p.G;
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
@@ -334,18 +345,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D, int NB>
 cudaError_t launch_tc_t(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv, const TcParams &p,
                         int sm_count) {
-    using C = TcCfg<D, NB>;
-    cudaError_t e =
-        cudaFuncSetAttribute(attn_decode_tc_kernel<D, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    constexpr int NG = tc_groups(D);
+    using C = TcCfg<D, NB, NG>;
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_tc_kernel<D, NB, NG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM);
     if (e != cudaSuccess) return e;
     const int grid = p.n_items < sm_count ? p.n_items : sm_count;
-    attn_decode_tc_kernel<D, NB><<<grid, kThreads, C::SMEM, st>>>(tk, tv, p);
+    attn_decode_tc_kernel<D, NB, NG><<<grid, C::THREADS, C::SMEM, st>>>(tk, tv, p);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 bool decode_tc_supported(int D, int G) { return (D == 64 || D == 128 || D == 256) && G >= 1 && G <= 8; }
+
+int decode_tc_partials(int D) { return kConsumers * tc_groups(D); }
 
 cudaError_t launch_attend_decode_tc(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
                                     const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,

@@ -193,6 +193,7 @@ void decode_prepare(eif_cuda_kv_t *kv, int layer, DecodeArgs &a);
 
 // Tensor-core decode path (attn_decode_tc.cu).
 bool decode_tc_supported(int D, int G);
+int decode_tc_partials(int D);  // partials per item of the bf16 kernel (one per consumer warp)
 cudaError_t launch_attend_decode_tc(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
                                     const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,
                                     float2 *part_ml, int sm_count);
