@@ -49,6 +49,24 @@ METRIC = "attn+DeltaNet tokens/s (24-layer Qwen3.5-like token-mixer decode step)
 UNIT = "tokens/s"
 
 
+# DRAM traffic of each roofline kernel per algorithmic byte, from one ncu capture of a smaller case of the same
+# kernel (dram__bytes_read.sum + dram__bytes_write.sum over the algorithmic bytes of that launch; the summaries
+# under profiles/ give the commands).  The bench scales it to its own launch by the units processed, which is
+# valid where traffic grows in proportion to the units (every kernel here streams each unit's bytes once).
+TRAFFIC_PER_ALG_BYTE = {
+    # batch 8 of config 5's attention layer: 536.99 MB read + 7.37 MB written for 536.87 MB of K + V
+    "attn_decode_tc_hd256": ((536.99 + 7.37) / 536.87, "profiles/attn_decode_tc_qwen35_hybrid.md"),
+}
+
+
+def traffic(kernel, alg_bytes):
+    """(DRAM bytes per launch, where the figure comes from) for the roofline's `traffic` / `traffic_source`."""
+    r = TRAFFIC_PER_ALG_BYTE.get(kernel)
+    if r is None:
+        return None, None
+    return r[0] * alg_bytes, f"{r[1]}: ncu DRAM bytes of a smaller case, x {r[0]:.4f} per algorithmic byte"
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -236,8 +254,6 @@ class HybridHost:
         self.pos = pinned(np.full(B, CTX - 1), np.int32)
         # the results land in pinned host arrays too (an engine keeps its activations in such buffers)
         self.dn_out = pinned(np.zeros((B, DN_H * DN_D)))
-        self.q = pinned(np.zeros((B, AT_HQ * AT_D)))
-        self.gate = pinned(np.zeros((B, AT_HQ * AT_D)))
         self.out = pinned(np.zeros((B, AT_HQ * AT_D)))
         h = self.h
         self.h2d = 0
@@ -247,10 +263,8 @@ class HybridHost:
                 self.h2d += h["qkv"].nbytes + h["z"].nbytes + h["b"].nbytes + h["a"].nbytes
                 self.d2h += B * DN_H * DN_D * 4
             else:
-                # fullatt_prep: qg, k, v, pos in; q, gate out -- attend: q, gate, pos, sub_norm in; out out
-                self.h2d += h["qg"].nbytes + h["k"].nbytes + h["v"].nbytes + self.pos.nbytes
-                self.d2h += 2 * B * AT_HQ * AT_D * 4
-                self.h2d += 2 * B * AT_HQ * AT_D * 4 + self.pos.nbytes + self.sub_norm[0].nbytes
+                # fullatt_decode (prep + attention in one call): qg, k, v, pos, sub_norm in; out out
+                self.h2d += h["qg"].nbytes + h["k"].nbytes + h["v"].nbytes + self.pos.nbytes + self.sub_norm[0].nbytes
                 self.d2h += B * AT_HQ * AT_D * 4
 
     def step(self, hy: Hybrid):
@@ -261,10 +275,8 @@ class HybridHost:
                 hy.dn.core(d, h["qkv"], h["z"], h["b"], h["a"], out=self.dn_out)
                 d += 1
             else:
-                q, g = hy.kv.fullatt_prep(a, h["qg"], h["k"], h["v"], self.pos, AT_HQ, q_out=self.q,
-                                          gate_out=self.gate)
-                hy.kv.attend_decode(a, q, self.pos, AT_HQ, hy.scale, gate=g, subln=hy.pkg.SUBLN_WEIGHT,
-                                    sub_norm=self.sub_norm[a], out=self.out)
+                hy.kv.fullatt_decode(a, h["qg"], h["k"], h["v"], self.pos, AT_HQ, hy.scale, subln=hy.pkg.SUBLN_WEIGHT,
+                                     sub_norm=self.sub_norm[a], out=self.out)
                 a += 1
 
 
@@ -350,7 +362,7 @@ def run_ours(args, torch, dist, rank, world, local_rank):
             e2e_ms = float(t[0])
         e2e = {"value": GB / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": host.h2d * world, "d2h_bytes_per_step": host.d2h * world,
-               "path": "host-pointer C ABI (eif_cuda_kv_append / eif_cuda_attend_decode / eif_cuda_deltanet_step)"}
+               "path": "host-pointer C ABI (eif_cuda_deltanet_core x 18, eif_cuda_fullatt_decode x 6)"}
 
     if rank != 0:
         return None
@@ -371,7 +383,8 @@ def run_ours(args, torch, dist, rank, world, local_rank):
         "roofline": {"kernel": "decode attention (split-K kernel + chunk combine), one attention layer",
                      "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": src, "algorithmic_bytes_per_launch": bytes_att, "ms_per_launch": att_ms,
-                     "traffic": None},
+                     "traffic": traffic("attn_decode_tc_hd256", bytes_att)[0],
+                     "traffic_source": traffic("attn_decode_tc_hd256", bytes_att)[1]},
         "step_hbm_frac": world * step_bytes / (ms_all * 1e-3) / 1e9 / (hbm * world),
         "gpu_launches": launches,
         "clocks": clk,
@@ -519,7 +532,17 @@ def cpu_prefill_reference(seconds=20.0):
                              f"{PF_B} x {PF_S}")
 
 
+_CPU_MEMO = {}
+
+
 def cpu_chunked_reference(seconds=10.0):
+    """Memoised: the recurrent and the chunked workloads share this measurement within one run."""
+    if seconds not in _CPU_MEMO:
+        _CPU_MEMO[seconds] = _cpu_chunked_reference(seconds)
+    return _CPU_MEMO[seconds]
+
+
+def _cpu_chunked_reference(seconds):
     """What the engine's prefill_chunk runs for a DeltaNet layer: the reference's deltanet_core once per
     token (src/eif_qwen35.c:1104-1106; conv window, norms, gates, the rule, gated RMSNorm), 16 heads of
     d 128 from a zero state, one sequence per host thread for the time budget.  Returns tokens/s of all
@@ -879,53 +902,54 @@ def decode_bytes(B, L, hkv, kv):
 
 
 def cpu_decode_reference(kv_name, L, seconds=10.0):
-    """The reference's decode attention of one token at pos L-1, one sequence per host thread for the time
-    budget: fp32 / bf16 caches -> the reference's fullatt_attend on fp32 rows (gate +100 -> sigmoid 1, plain:
-    the tinyllm GQA core, src/eif_tinyllm.c:557-656 computes the same); INT8 -> the restatement of the
-    tinyllm INT8 loop (src/eif_tinyllm.c:563-571, 618-625; the reference has it inline only).  RoPE and the
-    cache write are not timed (O(D) next to O(L D))."""
+    """The reference's own tinyllm decode step at position L-1 (tinyllm_forward_embedding_ex on a one-layer fp32
+    model whose attention is observable, oracle/ref_shim.c: RoPE, the cache write -- quantised for an INT8
+    cache, src/eif_tinyllm.c:509-553 -- and the head loop :555-656 over a pre-filled cache), one sequence per
+    host thread for the time budget.  A bf16 cache is timed as the reference's fp32 cache (it has no bf16).
+    Without the reference build: the restatement's attention loop (fp32 / INT8) alone."""
     os.environ.setdefault("OMP_NUM_THREADS", "1")
     from concurrent.futures import ThreadPoolExecutor
 
     from oracle import oracle as orc
     ncpu = len(os.sched_getaffinity(0))
-    rng = np.random.default_rng(8)
-    kv_dim = DC_HKV * DC_D
-    q = rng.standard_normal(DC_HQ * DC_D).astype(np.float32)
-    gate = np.full(DC_HQ * DC_D, 100.0, np.float32)
-    if kv_name == "int8":
-        kind = "port"
-        kc = rng.integers(-127, 128, (L, kv_dim)).astype(np.int8)
-        vc = rng.integers(-127, 128, (L, kv_dim)).astype(np.int8)
-        ks = rng.uniform(0.005, 0.03, (L, DC_HKV)).astype(np.float32)
-        vs = rng.uniform(0.005, 0.03, (L, DC_HKV)).astype(np.float32)
-    else:
-        kind = "reference" if orc.ref_available() else "port"
-        kc = rng.standard_normal((L, kv_dim)).astype(np.float32)
-        vc = rng.standard_normal((L, kv_dim)).astype(np.float32)
+    kind = "reference" if orc.ref_available() else "port"
+    kv_type = 1 if kv_name == "int8" else 0
     if kind == "reference":
         orc.ref().ref_set_threads(1)
 
-    def run(_):
-        n, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            if kv_name == "int8":
-                orc.attend_decode_i8(q, kc, ks, vc, vs, L - 1, DC_HQ, DC_HKV, DC_D, 0.125)
-            elif kind == "reference":
-                orc.ref_fullatt_attend(q, gate, kc, vc, None, 1, L - 1, DC_HQ, DC_HKV, DC_D)
-            else:
-                orc.attend_decode(q, kc, vc, L - 1, DC_HQ, DC_HKV, DC_D, 0.125)
-            n += 1
-        return n, time.perf_counter() - t0
+        def run(_):
+            t1 = orc.ref_tinyllm_decode_time(DC_HQ, DC_HKV, DC_D, L, DC_THETA, kv_type, L - 1, 3) / 3
+            n = max(3, int(seconds / max(t1, 1e-6)))
+            return n, orc.ref_tinyllm_decode_time(DC_HQ, DC_HKV, DC_D, L, DC_THETA, kv_type, L - 1, n)
+        what = ("the reference's tinyllm forward (one fp32 layer; its zero q/k/v and identity o projections add "
+                "dim^2 matvecs to each step)")
+    else:
+        rng = np.random.default_rng(8)
+        kv_dim = DC_HKV * DC_D
+        q = rng.standard_normal(DC_HQ * DC_D).astype(np.float32)
+        kc = rng.standard_normal((L, kv_dim)).astype(np.float32)
+        vc = rng.standard_normal((L, kv_dim)).astype(np.float32)
+        kq, ks = orc.kv_quantize(kc, DC_HKV, DC_D) if kv_type else (None, None)
+        vq, vs = orc.kv_quantize(vc, DC_HKV, DC_D) if kv_type else (None, None)
 
+        def run(_):
+            n, t0 = 0, time.perf_counter()
+            while time.perf_counter() - t0 < seconds:
+                if kv_type:
+                    orc.attend_decode_i8(q, kq, ks, vq, vs, L - 1, DC_HQ, DC_HKV, DC_D, 0.125)
+                else:
+                    orc.attend_decode(q, kc, vc, L - 1, DC_HQ, DC_HKV, DC_D, 0.125)
+                n += 1
+            return n, time.perf_counter() - t0
+        what = "the restatement's attention loop"
     pool = ThreadPoolExecutor(max_workers=ncpu)
     res = list(pool.map(run, range(ncpu)))
     pool.shutdown()
     tokens = sum(n for n, _ in res)
     el = max(t for _, t in res)
-    return tokens / el, ncpu, kind, (f"{tokens} decode tokens at ctx {L} ({kv_name} cache as the reference holds "
-                                     f"it: {'int8 codes + scales' if kv_name == 'int8' else 'fp32'}), one sequence "
-                                     f"per host thread, {el:.1f} s")
+    return tokens / el, ncpu, kind, (f"{tokens} decode steps at ctx {L} through {what}, "
+                                     f"{'int8 codes + scales' if kv_type else 'fp32'} cache, one sequence per "
+                                     f"host thread, {el:.1f} s")
 
 
 def run_decode(args, torch, dist, rank, world, local_rank):
@@ -1062,6 +1086,37 @@ def run_decode(args, torch, dist, rank, world, local_rank):
     return line
 
 
+WORKLOADS = [  # (key, workload, overrides): BASELINE configs[0..3] and config 1's heads batched per cache type
+    ("config1_decode", "decode", dict(batch=1, ctx=512, kv="f32")),
+    ("config2_prefill", "prefill", {}),
+    ("config3_recurrent", "recurrent", {}),
+    ("config4_chunked", "chunked", {}),
+    ("decode_batched_f32", "decode", dict(batch=256, ctx=4096, kv="f32")),
+    ("decode_batched_bf16", "decode", dict(batch=256, ctx=4096, kv="bf16")),
+    ("decode_batched_int8", "decode", dict(batch=256, ctx=4096, kv="int8")),
+]
+_KEEP = ("metric", "value", "unit", "ms_per_step", "dtype", "config", "roofline", "e2e", "cpu_baseline", "gpu_launches",
+         "clocks", "step_path")
+
+
+def run_workloads(args, torch, local_rank):
+    """The other BASELINE configs on the same GPU after the headline, each through its own workload function
+    (same timing rules: warm-up, events on the library's stream, L2 flush or inputs > L2), one compact entry
+    each for the `workloads` object of the headline line."""
+    import gc
+    out = {}
+    for key, wl, over in WORKLOADS:
+        a = argparse.Namespace(**vars(args))
+        a.workload, a.batch, a.ctx, a.kv = wl, over.get("batch"), over.get("ctx"), over.get("kv", "f32")
+        fn = {"prefill": run_prefill, "chunked": run_chunked, "decode": run_decode, "recurrent": run_recurrent}[wl]
+        line = fn(a, torch, None, 0, 1, local_rank)
+        out[key] = {k: line[k] for k in _KEEP if k in line}
+        gc.collect()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--workload", default="hybrid", choices=["hybrid", "prefill", "chunked", "decode", "recurrent"],
@@ -1076,6 +1131,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-pointer end-to-end leg (profiling runs)")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="hybrid at N=1: skip the other configs' entries (the `workloads` object)")
     ap.add_argument("--batch", type=int, default=None,
                     help="global batch (default: the workload's config: 256 hybrid, 8 prefill, 4 chunked)")
     args = ap.parse_args()
@@ -1115,6 +1172,12 @@ def main():
     if line is not None and world == 1 and not args.no_cpu_baseline:
         tps, cores, kind, sample, _ = cpu_reference(3, per_round_cap_s=30)
         line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample}
+    if line is not None and world == 1 and not args.no_workloads and args.batch is None:
+        import gc
+        gc.collect()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        line["workloads"] = run_workloads(args, torch, local_rank)
     if line is not None:
         print(json.dumps(line), flush=True)
     if dist:

@@ -31,7 +31,7 @@ constexpr int kDecodeWarps = kDecodeThreads / 32;
 template <typename KT, int D, int G>
 __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
     const KT *__restrict__ Kc, const KT *__restrict__ Vc, const float *__restrict__ q, const int *__restrict__ pos,
-    int max_seq, int Hkv, int chunk, int nchunk, float scale, float *__restrict__ part_o,
+    int max_seq, int max_len, int Hkv, int chunk, int nchunk, float scale, float *__restrict__ part_o,
     float2 *__restrict__ part_ml, unsigned *__restrict__ dev_err, const float *__restrict__ k_scale,
     const float *__restrict__ v_scale, int sstride) {
     constexpr int DL = D / 32;  // head-dim elements per lane in P.V
@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
     __shared__ float wacc[kDecodeWarps][G][D];
 
     int p = pos[b];
-    if (p < 0 || p >= max_seq) {
+    if (p < 0 || p >= max_len) {  // max_len = the caller's bound + 1, never above max_seq
         if (threadIdx.x == 0 && c == 0 && kvh == 0) atomicOr(dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
         p = -1;  // no keys: the partial is empty and the combine writes zeros
     }
@@ -338,7 +338,7 @@ template <typename KT, int D, int G>
 cudaError_t launch_simt(cudaStream_t st, const DecodeArgs &a, const Split &sp, float *part_o, float2 *part_ml) {
     dim3 grid(sp.nchunk, a.Hkv, a.B);
     attn_decode_simt_kernel<KT, D, G><<<grid, kDecodeThreads, 0, st>>>(
-        static_cast<const KT *>(a.K), static_cast<const KT *>(a.V), a.q, a.pos, a.max_seq, a.Hkv, sp.chunk,
+        static_cast<const KT *>(a.K), static_cast<const KT *>(a.V), a.q, a.pos, a.max_seq, a.max_len, a.Hkv, sp.chunk,
         sp.nchunk, a.scale, part_o, part_ml, a.dev_err, a.k_scale, a.v_scale, a.scale_stride);
     return cudaGetLastError();
 }
@@ -373,6 +373,13 @@ cudaError_t dispatch_d(cudaStream_t st, const DecodeArgs &a, const Split &sp, fl
 size_t decode_workspace_bytes(const DecodeArgs &a, int sm_count) {
     const Split sp = choose_split(a, sm_count);
     return partials_bytes(a, sp.nchunk, item_partials(a, sp.tc));
+}
+
+void decode_plan(const DecodeArgs &a, int sm_count, int *nchunk, int *chunk_keys, size_t *ws_bytes) {
+    const Split sp = choose_split(a, sm_count);
+    *nchunk = sp.nchunk;
+    *chunk_keys = sp.chunk;
+    *ws_bytes = partials_bytes(a, sp.nchunk, item_partials(a, sp.tc));
 }
 
 cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws, size_t ws_bytes, int sm_count,

@@ -57,7 +57,7 @@ struct F32Cfg {
 struct F32Params {
     const float *q;
     const int *pos;
-    int max_seq, Hkv, Hq;
+    int max_seq, max_len, Hkv, Hq;
     int nchunk, chunk_keys, n_items;
     float qscale;  // scale * log2(e)
     float *part_o;
@@ -75,7 +75,7 @@ __device__ __forceinline__ ItemInfo item_info(const F32Params &p, int item, bool
     it.b = unit / p.Hkv;
     it.kvh = unit - it.b * p.Hkv;
     int pp = p.pos[it.b];
-    if (pp < 0 || pp >= p.max_seq) {
+    if (pp < 0 || pp >= p.max_len) {  // max_len = the caller's bound + 1, never above max_seq
         if (report) atomicOr(p.dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
         pp = -1;
     }
@@ -333,6 +333,7 @@ cudaError_t launch_attend_decode_f32(cudaStream_t st, const CUtensorMap &tk, con
     p.q = a.q;
     p.pos = a.pos;
     p.max_seq = a.max_seq;
+    p.max_len = a.max_len;
     p.Hkv = a.Hkv;
     p.Hq = a.Hq;
     p.nchunk = nchunk;

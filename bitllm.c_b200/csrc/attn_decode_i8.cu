@@ -71,7 +71,7 @@ struct I8Params {
     const float *q;
     const float *ks, *vs;  // [B][Hkv][sstride] scales
     const int *pos;
-    int max_seq, Hkv, G, Hq, sstride;
+    int max_seq, max_len, Hkv, G, Hq, sstride;
     int nchunk, chunk_keys, n_items;
     float qscale;  // scale * log2(e)
     float *part_o;
@@ -89,7 +89,7 @@ __device__ __forceinline__ ItemInfo item_info(const I8Params &p, int item, bool 
     it.b = unit / p.Hkv;
     it.kvh = unit - it.b * p.Hkv;
     int pp = p.pos[it.b];
-    if (pp < 0 || pp >= p.max_seq) {
+    if (pp < 0 || pp >= p.max_len) {  // max_len = the caller's bound + 1, never above max_seq
         if (report) atomicOr(p.dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
         pp = -1;
     }
@@ -402,6 +402,7 @@ cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, cons
     p.sstride = a.scale_stride;
     p.pos = a.pos;
     p.max_seq = a.max_seq;
+    p.max_len = a.max_len;
     p.Hkv = a.Hkv;
     p.G = a.Hq / a.Hkv;
     p.Hq = a.Hq;

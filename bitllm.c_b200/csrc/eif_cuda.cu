@@ -106,7 +106,7 @@ static eif_status_t check_err_word(eif_cuda_ctx_t *ctx, unsigned derr) {
     if (derr) {
         CK(cudaMemsetAsync(ctx->dev_err, 0, sizeof(unsigned), ctx->stream));
         if (derr & EIF_DEVERR_POS_RANGE)
-            return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "a kernel saw pos outside [0, max_seq_len)");
+            return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "a kernel saw pos outside [0, max_seq_len) or above the call's max_pos");
         if (derr & EIF_DEVERR_WAIT_LIMIT)
             return fail(ctx, EIF_STATUS_TIMEOUT, "a kernel pipeline wait ran out of iterations");
         return fail(ctx, EIF_STATUS_INTERNAL_ERROR, "device error word 0x%x", derr);
@@ -279,6 +279,7 @@ EIF_API void eif_cuda_free(eif_cuda_ctx_t *ctx) {
         if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
         if (ctx->ws) cudaFree(ctx->ws);
         if (ctx->stage) cudaFree(ctx->stage);
+        if (ctx->mix) cudaFree(ctx->mix);
         if (ctx->io) cudaFree(ctx->io);
         if (ctx->host_err) cudaFreeHost(ctx->host_err);
         if (ctx->pin) cudaFreeHost(ctx->pin);
@@ -707,6 +708,24 @@ EIF_API eif_status_t eif_cuda_attend_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *
     if (small) return finish_small(ctx, out, nq * 4);
     CK(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return wait_stream(ctx);
+}
+
+EIF_API eif_status_t eif_cuda_attend_decode_plan(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int n_heads,
+                                                 int max_pos, int noalloc, int *n_chunks, int *chunk_keys,
+                                                 size_t *scratch_bytes) {
+    eif_status_t st = decode_check(ctx, kv, layer, n_heads, EIF_CUDA_SUBLN_NONE);
+    if (st != EIF_STATUS_OK) return st;
+    if (!n_chunks || !chunk_keys || !scratch_bytes)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "attend_decode_plan: NULL pointer");
+    if (max_pos < 0 || max_pos >= kv->max_seq)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "max_pos %d outside [0, %d)", max_pos, kv->max_seq);
+    DeviceGuard g(ctx);
+    DecodeArgs a{kv->k[layer], kv->v[layer], kv->dtype, nullptr, nullptr, kv->batch, n_heads, kv->n_kv, kv->hd,
+                 kv->max_seq, max_pos + 1, 1.0f, nullptr, 0, nullptr, nullptr, ctx->dev_err};
+    if (noalloc) a.max_ws_bytes = noalloc_scratch_capacity();
+    decode_prepare(kv, layer, a);
+    decode_plan(a, ctx->sm_count, n_chunks, chunk_keys, scratch_bytes);
+    return EIF_STATUS_OK;
 }
 
 // =================================================================================================
@@ -1568,8 +1587,12 @@ EIF_API eif_status_t eif_cuda_kv_set_norms(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *k
     return wait_stream(ctx);
 }
 
-// cos / sin of rope_partial (src/eif_qwen35.c:502-535) for every cache row, by the reference's formula:
-// n_rot = head_dim * 0.25, inv_freq_i = 1 / powf(1e7, 2i / n_rot), angle = pos * inv_freq_i.
+// cos / sin of rope_partial (src/eif_qwen35.c:502-535) for every cache row: n_rot = head_dim * 0.25,
+// angle = pos * inv_freq_i.  The source reads inv_freq_i = 1.0f / powf(1e7f, 2i / n_rot); the reference's
+// build (-O3 -ffast-math, CMakeLists.txt:19) turns a power of the constant 1e7 into an exponential,
+// inv_freq_i = expf(-(2i / n_rot) * logf(1e7)), which differs from 1 / powf in the last bit for most i.
+// At positions in the tens of thousands one ulp of inv_freq moves the angle by ~1e-3 rad, so the table
+// takes the compiled form: the float product, then its exponential rounded to nearest from double.
 static eif_status_t ensure_rope_table(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv) {
     if (kv->rope_cos) return EIF_STATUS_OK;
     const int n_rot = (int)(kv->hd * 0.25f), half = n_rot / 2;
@@ -1578,7 +1601,11 @@ static eif_status_t ensure_rope_table(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv) {
     float *hc = (float *)malloc(2 * n * sizeof(float));
     if (!hc) return fail(ctx, EIF_STATUS_OUT_OF_MEMORY, "rope table");
     float inv[128];
-    for (int i = 0; i < half && i < 128; ++i) inv[i] = 1.0f / powf(10000000.0f, 2.0f * i / (float)n_rot);
+    const float ln_theta = (float)log(10000000.0);
+    for (int i = 0; i < half && i < 128; ++i) {
+        const float y = -(2.0f * i / (float)n_rot) * ln_theta;
+        inv[i] = (float)exp((double)y);
+    }
     for (int pos = 0; pos < kv->max_seq; ++pos)
         for (int i = 0; i < half; ++i) {
             const float theta = pos * inv[i];
@@ -1713,5 +1740,79 @@ EIF_API eif_status_t eif_cuda_fullatt_prep(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *k
     if (rs != EIF_STATUS_OK) return rs;
     CK(cudaMemcpyAsync(q_out, s + o_q, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
     CK(cudaMemcpyAsync(gate_out, s + o_g, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// =================================================================================================
+// The Qwen3.5 attention mixer of one token: fullatt_prep + fullatt_attend in one call
+// =================================================================================================
+
+static eif_status_t fullatt_decode_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg,
+                                       const float *k, const float *v, const int *pos, int max_pos, int n_heads,
+                                       float scale, eif_cuda_subln_t subln, const float *sub_norm, float *out,
+                                       float *q_buf, float *gate_buf) {
+    eif_status_t st = prep_run(ctx, kv, layer, qg, k, v, pos, n_heads, q_buf, gate_buf);
+    if (st != EIF_STATUS_OK) return st;
+    DecodeArgs a{kv->k[layer], kv->v[layer], kv->dtype, q_buf, pos, kv->batch, n_heads, kv->n_kv, kv->hd,
+                 kv->max_seq, max_pos + 1, scale, gate_buf, (int)subln, sub_norm, out, ctx->dev_err};
+    return decode_run(ctx, kv, layer, a);
+}
+
+EIF_API eif_status_t eif_cuda_fullatt_decode_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
+                                                 const float *qg_dev, const float *k_dev, const float *v_dev,
+                                                 const int *pos_dev, int max_pos, int n_heads, float scale,
+                                                 eif_cuda_subln_t subln, const float *sub_norm_dev, float *out_dev) {
+    eif_status_t st = prep_check(ctx, kv, layer, n_heads);
+    if (st == EIF_STATUS_OK) st = decode_check(ctx, kv, layer, n_heads, subln);
+    if (st != EIF_STATUS_OK) return st;
+    if (!qg_dev || !k_dev || !v_dev || !pos_dev || !out_dev || (subln == EIF_CUDA_SUBLN_WEIGHT && !sub_norm_dev))
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "fullatt_decode_dev: NULL pointer");
+    if (max_pos < 0 || max_pos >= kv->max_seq)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "max_pos %d outside [0, %d)", max_pos, kv->max_seq);
+    DeviceGuard g(ctx);
+    const size_t nq = (size_t)kv->batch * n_heads * kv->hd;
+    st = ensure_buffer(ctx, &ctx->mix, &ctx->mix_bytes, 2 * a256(nq * 4));
+    if (st != EIF_STATUS_OK) return st;
+    float *qb = static_cast<float *>(ctx->mix);
+    float *gb = reinterpret_cast<float *>(static_cast<char *>(ctx->mix) + a256(nq * 4));
+    return fullatt_decode_run(ctx, kv, layer, qg_dev, k_dev, v_dev, pos_dev, max_pos, n_heads, scale, subln,
+                              sub_norm_dev, out_dev, qb, gb);
+}
+
+EIF_API eif_status_t eif_cuda_fullatt_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg,
+                                             const float *k, const float *v, const int *pos, int n_heads, float scale,
+                                             eif_cuda_subln_t subln, const float *sub_norm, float *out) {
+    eif_status_t st = prep_check(ctx, kv, layer, n_heads);
+    if (st == EIF_STATUS_OK) st = decode_check(ctx, kv, layer, n_heads, subln);
+    if (st != EIF_STATUS_OK) return st;
+    if (!qg || !k || !v || !pos || !out || (subln == EIF_CUDA_SUBLN_WEIGHT && !sub_norm))
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "fullatt_decode: NULL pointer");
+    int max_pos = 0;
+    for (int b = 0; b < kv->batch; ++b) {
+        if (pos[b] < 0 || pos[b] >= kv->max_seq)
+            return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "pos[%d] = %d outside [0, %d)", b, pos[b], kv->max_seq);
+        max_pos = std::max(max_pos, pos[b]);
+    }
+    DeviceGuard g(ctx);
+    const size_t B = kv->batch, row = (size_t)n_heads * kv->hd, nq = B * row, nk = B * kv->n_kv * kv->hd;
+    const bool wn = subln == EIF_CUDA_SUBLN_WEIGHT;
+    Carver cv;
+    const size_t o_qg = cv.take(2 * nq * 4), o_k = cv.take(nk * 4), o_v = cv.take(nk * 4), o_p = cv.take(B * 4),
+                 o_n = cv.take(wn ? row * 4 : 0), o_q = cv.take(nq * 4), o_g = cv.take(nq * 4), o_o = cv.take(nq * 4);
+    st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (st != EIF_STATUS_OK) return st;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_qg, qg, 2 * nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_k, k, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_v, v, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_p, pos, B * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (wn) CK(cudaMemcpyAsync(s + o_n, sub_norm, row * 4, cudaMemcpyHostToDevice, ctx->stream));
+    st = fullatt_decode_run(ctx, kv, layer, reinterpret_cast<float *>(s + o_qg), reinterpret_cast<float *>(s + o_k),
+                            reinterpret_cast<float *>(s + o_v), reinterpret_cast<int *>(s + o_p), max_pos, n_heads,
+                            scale, subln, wn ? reinterpret_cast<float *>(s + o_n) : nullptr,
+                            reinterpret_cast<float *>(s + o_o), reinterpret_cast<float *>(s + o_q),
+                            reinterpret_cast<float *>(s + o_g));
+    if (st != EIF_STATUS_OK) return st;
+    CK(cudaMemcpyAsync(out, s + o_o, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return wait_stream(ctx);
 }

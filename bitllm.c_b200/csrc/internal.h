@@ -31,6 +31,9 @@ struct eif_cuda_ctx {
     // device staging for the host-pointer entry points, grown on demand
     void *stage = nullptr;
     size_t stage_bytes = 0;
+    // device q / gate between the two halves of eif_cuda_fullatt_decode_dev, grown on demand
+    void *mix = nullptr;
+    size_t mix_bytes = 0;
     // device error word: the first 16 bytes of io, whose remaining kSmallIo bytes take the outputs of
     // small host-pointer calls, so that the word and the output come back in one copy
     void *io = nullptr;
@@ -228,6 +231,10 @@ cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, cons
                                     float2 *part_ml, int sm_count);
 // Workspace bytes needed by launch_attend_decode for these args and the chosen split.
 size_t decode_workspace_bytes(const DecodeArgs &a, int sm_count);
+// The split launch_attend_decode would use: key chunks per (sequence, kv head), keys per chunk, scratch bytes.
+void decode_plan(const DecodeArgs &a, int sm_count, int *nchunk, int *chunk_keys, size_t *ws_bytes);
+// Bytes of the fixed scratch array of eif_cuda_attend_decode_noalloc_dev (noalloc.cu).
+size_t noalloc_scratch_capacity();
 cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws, size_t ws_bytes, int sm_count,
                                  bool *supported, int *n_launches);
 

@@ -12,7 +12,10 @@
 // library and held until the process exits.  Host code never dereferences its name (on the host the
 // symbol is only a stand-in, not a device address); the device address is fetched once per device
 // with cudaGetSymbolAddress, with that device current, and handed to the kernels.  The first call on a
-// device does that set-up, so make the first call on each device before any stream capture begins.
+// device does that set-up, so make the first call on each device before any stream capture begins.  The
+// address is kept per device ordinal and belongs to the device's primary context, the one the CUDA
+// runtime (and this library's contexts) use: a host that drives the library from another driver context,
+// or that reset the device (cudaDeviceReset) after the first call, must not use this entry point.
 //
 // All calls in the process share the array and find the previous call's contents in it.  The decode
 // kernels overwrite every partial they later read, so nothing has to be cleared between calls; calls
@@ -67,6 +70,8 @@ eif_status_t scratch_address(eif_cuda_ctx_t *ctx, void **addr) {
 }
 
 }  // namespace
+
+size_t noalloc_scratch_capacity() { return kNoallocScratchBytes; }
 
 EIF_API eif_status_t eif_cuda_attend_decode_noalloc_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
                                                         const float *q_dev, const int *pos_dev, int max_pos,

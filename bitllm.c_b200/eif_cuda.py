@@ -1,7 +1,7 @@
 """ctypes binding of include/eif_cuda.h (the C ABI of libeif_cuda.so).
 
 This is the host-side mirror a Python caller uses; a C99 engine calls the same entry points
-directly (see INTEGRATION.md).  Host arrays are numpy float32/int32; `_dev` methods take raw device
+directly.  Host arrays are numpy float32/int32; `_dev` methods take raw device
 addresses (ints), e.g. torch's tensor.data_ptr(), and run asynchronously on the context's stream.
 
 Errors come back as EifCudaError carrying the eif_status_t code and the library's message; there is
@@ -84,6 +84,10 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_attend_decode": (_I, [_P, _P, _I, _P, _P, _I, _F, _P, _I, _P, _P]),
         "eif_cuda_attend_decode_dev": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _P, _I, _P, _P]),
         "eif_cuda_attend_decode_noalloc_dev": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _P, _I, _P, _P]),
+        "eif_cuda_attend_decode_plan": (_I, [_P, _P, _I, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I),
+                                             ctypes.POINTER(ctypes.c_size_t)]),
+        "eif_cuda_fullatt_decode": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _F, _I, _P, _P]),
+        "eif_cuda_fullatt_decode_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _I, _F, _I, _P, _P]),
         "eif_cuda_attend_prefill": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P]),
         "eif_cuda_attend_prefill_dev": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P]),
         "eif_cuda_attend_prefill_gated": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P, _I, _P, _P]),
@@ -415,6 +419,31 @@ class KVCache:
         self.ctx.check(lib().eif_cuda_attend_prefill_gated_dev(self.ctx.handle, self._h, layer, q_dev, n_tok, start_pos,
                                                                n_heads, float(scale), gate_dev, int(subln),
                                                                sub_norm_dev, out_dev), "attend_prefill_gated_dev")
+
+    def decode_plan(self, layer: int, n_heads: int, max_pos: int, noalloc: bool = False):
+        """(key chunks per (sequence, kv head), keys per chunk, scratch bytes) of decode attention's split."""
+        nc, ck, wb = _I(), _I(), ctypes.c_size_t()
+        self.ctx.check(lib().eif_cuda_attend_decode_plan(self.ctx.handle, self._h, layer, n_heads, int(max_pos),
+                                                         int(bool(noalloc)), ctypes.byref(nc), ctypes.byref(ck),
+                                                         ctypes.byref(wb)), "attend_decode_plan")
+        return nc.value, ck.value, wb.value
+
+    def fullatt_decode(self, layer: int, qg, k, v, pos, n_heads: int, scale: float, subln: int = SUBLN_NONE,
+                       sub_norm=None, out=None):
+        """The Qwen3.5 attention mixer of one token (fullatt_prep + fullatt_attend) from host arrays."""
+        qq, kk, vv, pp = _f32(qg), _f32(k), _f32(v), _i32(pos)
+        nn = _f32(sub_norm) if sub_norm is not None else None
+        o = _out(out, (self.batch, n_heads * self.head_dim))
+        self.ctx.check(lib().eif_cuda_fullatt_decode(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv),
+                                                     _ptr(pp), n_heads, float(scale), int(subln), _ptr(nn), _ptr(o)),
+                       "fullatt_decode")
+        return o
+
+    def fullatt_decode_dev(self, layer: int, qg_dev, k_dev, v_dev, pos_dev, max_pos: int, n_heads: int,
+                           scale: float, out_dev, subln: int = SUBLN_NONE, sub_norm_dev=None):
+        self.ctx.check(lib().eif_cuda_fullatt_decode_dev(self.ctx.handle, self._h, layer, qg_dev, k_dev, v_dev,
+                                                         pos_dev, int(max_pos), n_heads, float(scale), int(subln),
+                                                         sub_norm_dev, out_dev), "fullatt_decode_dev")
 
     def attend_decode_dev(self, layer: int, q_dev: int, pos_dev: int, max_pos: int, n_heads: int, scale: float,
                           out_dev: int, gate_dev: int | None = None, subln: int = SUBLN_NONE,

@@ -201,11 +201,21 @@ eif_status_t eif_cuda_attend_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int 
                                     const int *pos, int n_heads, float scale, const float *gate,
                                     eif_cuda_subln_t subln, const float *sub_norm, float *out);
 /* Device-pointer variant; max_pos is an upper bound of pos_dev[] (used to size the split over the KV
- * length: rows beyond a sequence's own pos are never read). */
+ * length: rows beyond a sequence's own pos are never read).  A pos_dev[b] above max_pos (or outside the
+ * cache) is not computed: that sequence's output is zeros and the next synchronising call returns
+ * EIF_STATUS_INVALID_ARGUMENT. */
 eif_status_t eif_cuda_attend_decode_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_dev,
                                         const int *pos_dev, int max_pos, int n_heads, float scale,
                                         const float *gate_dev, eif_cuda_subln_t subln, const float *sub_norm_dev,
                                         float *out_dev);
+
+/* The split decode attention would use for this cache layer, n_heads and max_pos: key chunks per (sequence,
+ * kv head) in *n_chunks, keys per chunk in *chunk_keys, and the device scratch its partials need in
+ * *scratch_bytes.  noalloc != 0 answers for eif_cuda_attend_decode_noalloc_dev (split capped to its fixed
+ * array; *scratch_bytes above that array means the call would be refused).  Launches nothing.  No counterpart
+ * in the reference: it lets a caller size memory up front and lets tests pin the split regime. */
+eif_status_t eif_cuda_attend_decode_plan(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, int n_heads, int max_pos,
+                                         int noalloc, int *n_chunks, int *chunk_keys, size_t *scratch_bytes);
 
 /* ---------------------------------------------------------------------------------------------
  * Causal prefill attention: n_tok new tokens per sequence at positions start_pos .. start_pos+n_tok-1,
@@ -242,8 +252,10 @@ eif_status_t eif_cuda_attend_prefill_gated_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_
  * fixed memory budget).  No counterpart in the reference.  It calls no cudaMalloc / cudaFree: the split-K
  * partials go to one 16 MiB array compiled into the library (reserved on every GPU that loads it, until
  * exit); shapes whose partials do not fit even unsplit return EIF_STATUS_INVALID_ARGUMENT.  The first call
- * on a device looks the array's address up, so make it before any stream capture.  All calls share the
- * array: calls that overlap on the GPU race and must be serialised by the caller. */
+ * on a device looks the array's address up, so make it before any stream capture; the address belongs to
+ * the device's primary context (the CUDA runtime's), so do not use this entry from another driver context or
+ * after a cudaDeviceReset.  All calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller. */
 eif_status_t eif_cuda_attend_decode_noalloc_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
                                                 const float *q_dev, const int *pos_dev, int max_pos, int n_heads,
                                                 float scale, const float *gate_dev, eif_cuda_subln_t subln,
@@ -356,6 +368,21 @@ eif_status_t eif_cuda_fullatt_prep_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *k
 eif_status_t eif_cuda_fullatt_prep_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
                                                const float *qg_dev, const float *k_dev, const float *v_dev, int n_tok,
                                                int start_pos, int n_heads, void *q_out_dev, float *gate_out_dev);
+
+/* The whole Qwen3.5 attention mixer of one token per sequence in one call: fullatt_prep then fullatt_attend,
+ * as fullatt_fwd calls them (src/eif_qwen35.c:819-820 -> :699-737, :741-790) -- eif_cuda_fullatt_prep followed
+ * by eif_cuda_attend_decode with the gate and SubLN, with q and the gate kept on the device between the two.
+ *   qg [batch][n_heads][2*head_dim], k, v [batch][n_kv*head_dim] (the projections), pos [batch] (the new row;
+ *   the attention spans rows [0, pos[b]]), sub_norm [n_heads*head_dim] for EIF_CUDA_SUBLN_WEIGHT,
+ *   out [batch][n_heads*head_dim] (the input of o_proj).  Needs eif_cuda_kv_set_norms.
+ * _dev: device arrays, asynchronous; max_pos bounds every pos_dev[b] as in eif_cuda_attend_decode_dev. */
+eif_status_t eif_cuda_fullatt_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg, const float *k,
+                                     const float *v, const int *pos, int n_heads, float scale, eif_cuda_subln_t subln,
+                                     const float *sub_norm, float *out);
+eif_status_t eif_cuda_fullatt_decode_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg_dev,
+                                         const float *k_dev, const float *v_dev, const int *pos_dev, int max_pos,
+                                         int n_heads, float scale, eif_cuda_subln_t subln, const float *sub_norm_dev,
+                                         float *out_dev);
 
 #ifdef __cplusplus
 }

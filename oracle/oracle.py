@@ -83,6 +83,8 @@ def ref():
         _ref.ref_tinyllm_decode_steps.argtypes = [i, i, i, i, ctypes.c_float, i, i, i, _F, _F, _F, _F, _F, _F,
                                                   _I8, _I8, _F, _F, _F]
         _ref.ref_tinyllm_decode_steps.restype = i
+        _ref.ref_tinyllm_decode_time.argtypes = [i, i, i, i, ctypes.c_float, i, i, i]
+        _ref.ref_tinyllm_decode_time.restype = ctypes.c_double
         _ref.ref_set_threads.argtypes = [i]
     return _ref
 
@@ -226,6 +228,15 @@ def ref_tinyllm_decode_steps(q, k, v, nh, nkv, hd, seq_len, theta, interleaved, 
     if rc != 0:
         raise RuntimeError("the reference rejected the tinyllm configuration")
     return o
+
+
+def ref_tinyllm_decode_time(nh, nkv, hd, seq_len, theta, kv_type, pos, n_steps):
+    """Seconds the reference's own tinyllm forward takes for n_steps decode steps at position pos over a
+    pre-filled fp32 (kv_type 0) or INT8 (kv_type 1) cache (oracle/ref_shim.c); needs oracle/_ref."""
+    t = ref().ref_tinyllm_decode_time(nh, nkv, hd, seq_len, float(theta), int(kv_type), int(pos), int(n_steps))
+    if t < 0:
+        raise RuntimeError("the reference rejected the tinyllm configuration")
+    return t
 
 
 def round_bf16(x):

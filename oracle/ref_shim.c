@@ -10,6 +10,7 @@
  * and calls the reference function unchanged.
  */
 #include "eif_qwen35.c"
+#include <time.h>
 
 #define REF_EXPORT __attribute__((visibility("default")))
 
@@ -99,12 +100,42 @@ REF_EXPORT void ref_fullatt_attend(const float *q, const float *gate, float *o_i
  */
 #include "eif_tinyllm.h"
 
-REF_EXPORT int ref_tinyllm_decode_steps(int n_heads, int n_kv, int hd, int seq_len, float theta, int interleaved,
-                                        int kv_type, int n_steps, const float *q_in, const float *k_in,
-                                        const float *v_in, float *q_rot, float *k_row, float *v_row,
-                                        int8_t *k_i8, int8_t *v_i8, float *k_scale, float *v_scale, float *attn)
+/* A one-layer fp32 tinyllm model built so that its attention is observable: zero q / k / v projections whose
+ * Qwen biases carry the step's q / k / v (src/eif_tinyllm.c:467-479), an identity wo (s->xb2 is the attention
+ * output), a zero FFN. */
+typedef struct {
+    tinyllm_t *llm;
+    void *pool;
+    float *ones, *wq, *wkv, *wo, *wffn, *bq, *bk, *bv, *x0;
+    int dim, kv_dim;
+} tl_model_t;
+
+static void tl_model_free(tl_model_t *m)
 {
+    if (m->llm) {
+        tinyllm_free(m->llm);
+        free(m->llm);
+    }
+    free(m->pool);
+    free(m->ones);
+    free(m->wq);
+    free(m->wkv);
+    free(m->wo);
+    free(m->wffn);
+    free(m->bq);
+    free(m->bk);
+    free(m->bv);
+    free(m->x0);
+    memset(m, 0, sizeof *m);
+}
+
+static int tl_model_make(tl_model_t *m, int n_heads, int n_kv, int hd, int seq_len, float theta, int interleaved,
+                         int kv_type)
+{
+    memset(m, 0, sizeof *m);
     const int dim = n_heads * hd, kv_dim = n_kv * hd, hidden = 8;
+    m->dim = dim;
+    m->kv_dim = kv_dim;
     tinyllm_config_t cfg;
     memset(&cfg, 0, sizeof cfg);
     cfg.dim = dim;
@@ -119,48 +150,60 @@ REF_EXPORT int ref_tinyllm_decode_steps(int n_heads, int n_kv, int hd, int seq_l
     cfg.rope_theta = theta;
     cfg.kv_type = kv_type;
     const size_t pool_bytes = tinyllm_memory_size(&cfg);
-    void *pool = calloc(1, pool_bytes);
+    m->pool = calloc(1, pool_bytes);
     tinyllm_t *llm = (tinyllm_t *)calloc(1, sizeof(tinyllm_t));
-    if (!pool || !llm || tinyllm_init(llm, &cfg, pool, pool_bytes) != 0) {
-        free(pool);
+    if (!m->pool || !llm || tinyllm_init(llm, &cfg, m->pool, pool_bytes) != 0) {
         free(llm);
+        tl_model_free(m);
         return -1;
     }
-    float *ones = (float *)malloc(sizeof(float) * dim);
-    for (int i = 0; i < dim; i++) ones[i] = 1.0f;
-    float *wq = (float *)calloc((size_t)dim * dim, sizeof(float));
-    float *wkv = (float *)calloc((size_t)dim * kv_dim, sizeof(float));
-    float *wo = (float *)calloc((size_t)dim * dim, sizeof(float));
-    for (int i = 0; i < dim; i++) wo[(size_t)i * dim + i] = 1.0f;
-    float *wffn = (float *)calloc((size_t)dim * hidden, sizeof(float));
-    float *bq = (float *)malloc(sizeof(float) * dim);
-    float *bk = (float *)malloc(sizeof(float) * kv_dim);
-    float *bv = (float *)malloc(sizeof(float) * kv_dim);
-    float *x0 = (float *)calloc(dim, sizeof(float));
+    m->llm = llm;
+    m->ones = (float *)malloc(sizeof(float) * dim);
+    for (int i = 0; i < dim; i++) m->ones[i] = 1.0f;
+    m->wq = (float *)calloc((size_t)dim * dim, sizeof(float));
+    m->wkv = (float *)calloc((size_t)dim * kv_dim, sizeof(float));
+    m->wo = (float *)calloc((size_t)dim * dim, sizeof(float));
+    for (int i = 0; i < dim; i++) m->wo[(size_t)i * dim + i] = 1.0f;
+    m->wffn = (float *)calloc((size_t)dim * hidden, sizeof(float));
+    m->bq = (float *)malloc(sizeof(float) * dim);
+    m->bk = (float *)malloc(sizeof(float) * kv_dim);
+    m->bv = (float *)malloc(sizeof(float) * kv_dim);
+    m->x0 = (float *)calloc(dim, sizeof(float));
     tinyllm_weights_t *w = &llm->weights;
-    w->rms_att_weight = ones;
-    w->rms_ffn_weight = ones;
-    w->rms_final_weight = ones;
-    w->wq = wq;
-    w->wk = wkv;
-    w->wv = wkv;
-    w->wo = wo;
-    w->w1 = wffn;
-    w->w3 = wffn;
-    w->w2 = wffn;
-    w->bq = bq;
-    w->bk = bk;
-    w->bv = bv;
+    w->rms_att_weight = m->ones;
+    w->rms_ffn_weight = m->ones;
+    w->rms_final_weight = m->ones;
+    w->wq = m->wq;
+    w->wk = m->wkv;
+    w->wv = m->wkv;
+    w->wo = m->wo;
+    w->w1 = m->wffn;
+    w->w3 = m->wffn;
+    w->w2 = m->wffn;
+    w->bq = m->bq;
+    w->bk = m->bk;
+    w->bv = m->bv;
+    return 0;
+}
+
+REF_EXPORT int ref_tinyllm_decode_steps(int n_heads, int n_kv, int hd, int seq_len, float theta, int interleaved,
+                                        int kv_type, int n_steps, const float *q_in, const float *k_in,
+                                        const float *v_in, float *q_rot, float *k_row, float *v_row,
+                                        int8_t *k_i8, int8_t *v_i8, float *k_scale, float *v_scale, float *attn)
+{
+    tl_model_t m;
+    if (tl_model_make(&m, n_heads, n_kv, hd, seq_len, theta, interleaved, kv_type) != 0) return -1;
+    const int dim = m.dim, kv_dim = m.kv_dim;
     int rc = 0;
     for (int t = 0; t < n_steps && rc == 0; t++) {
-        memcpy(bq, q_in + (size_t)t * dim, sizeof(float) * dim);
-        memcpy(bk, k_in + (size_t)t * kv_dim, sizeof(float) * kv_dim);
-        memcpy(bv, v_in + (size_t)t * kv_dim, sizeof(float) * kv_dim);
-        if (!tinyllm_forward_embedding_ex(llm, x0, t, false)) {
+        memcpy(m.bq, q_in + (size_t)t * dim, sizeof(float) * dim);
+        memcpy(m.bk, k_in + (size_t)t * kv_dim, sizeof(float) * kv_dim);
+        memcpy(m.bv, v_in + (size_t)t * kv_dim, sizeof(float) * kv_dim);
+        if (!tinyllm_forward_embedding_ex(m.llm, m.x0, t, false)) {
             rc = -1;
             break;
         }
-        tinyllm_state_t *s = &llm->state;
+        tinyllm_state_t *s = &m.llm->state;
         memcpy(q_rot + (size_t)t * dim, s->q, sizeof(float) * dim);
         memcpy(k_row + (size_t)t * kv_dim, s->key_cache + (size_t)t * kv_dim, sizeof(float) * kv_dim);
         memcpy(v_row + (size_t)t * kv_dim, s->value_cache + (size_t)t * kv_dim, sizeof(float) * kv_dim);
@@ -172,19 +215,48 @@ REF_EXPORT int ref_tinyllm_decode_steps(int n_heads, int n_kv, int hd, int seq_l
         }
         memcpy(attn + (size_t)t * dim, s->xb2, sizeof(float) * dim);
     }
-    tinyllm_free(llm);
-    free(llm);
-    free(pool);
-    free(ones);
-    free(wq);
-    free(wkv);
-    free(wo);
-    free(wffn);
-    free(bq);
-    free(bk);
-    free(bv);
-    free(x0);
+    tl_model_free(&m);
     return rc;
+}
+
+/* Seconds the reference's own tinyllm forward takes for n_steps decode steps at position pos (each step writes
+ * row pos and attends over rows [0, pos]) of the model above, on a cache whose rows [0, pos) were filled with
+ * pseudo-random contents: fp32 rows in [-1, 1), or (kv_type 1) INT8 codes in [-127, 127] with scales in
+ * [0.005, 0.03).  For timing the CPU baseline; -1 on failure. */
+REF_EXPORT double ref_tinyllm_decode_time(int n_heads, int n_kv, int hd, int seq_len, float theta, int kv_type,
+                                          int pos, int n_steps)
+{
+    if (pos < 0 || pos >= seq_len || n_steps < 1) return -1.0;
+    tl_model_t m;
+    if (tl_model_make(&m, n_heads, n_kv, hd, seq_len, theta, 0, kv_type) != 0) return -1.0;
+    tinyllm_state_t *s = &m.llm->state;
+    uint32_t x = 12345u;
+    for (size_t i = 0; i < (size_t)pos * m.kv_dim; i++) {
+        x = x * 1664525u + 1013904223u;
+        if (kv_type == 1) {
+            s->key_cache_i8[i] = (int8_t)((int)((x >> 24) % 255u) - 127);
+            s->value_cache_i8[i] = (int8_t)((int)(((x >> 8) & 0xffu) % 255u) - 127);
+        } else {
+            s->key_cache[i] = (float)(x >> 8) * (2.0f / 16777216.0f) - 1.0f;
+            s->value_cache[i] = (float)((x * 747796405u) >> 8) * (2.0f / 16777216.0f) - 1.0f;
+        }
+    }
+    if (kv_type == 1)
+        for (size_t i = 0; i < (size_t)pos * n_kv; i++) {
+            x = x * 1664525u + 1013904223u;
+            s->key_scale[i] = 0.005f + 0.025f * (float)(x >> 8) / 16777216.0f;
+            s->value_scale[i] = 0.005f + 0.025f * (float)((x * 747796405u) >> 8) / 16777216.0f;
+        }
+    for (int i = 0; i < m.dim; i++) m.bq[i] = (float)((i * 37) % 11) * 0.1f - 0.5f;
+    for (int i = 0; i < m.kv_dim; i++) m.bk[i] = m.bv[i] = (float)((i * 13) % 7) * 0.1f - 0.3f;
+    struct timespec t0, t1;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    int ok = 1;
+    for (int t = 0; t < n_steps && ok; t++) ok = tinyllm_forward_embedding_ex(m.llm, m.x0, pos, false);
+    clock_gettime(CLOCK_MONOTONIC, &t1);
+    tl_model_free(&m);
+    if (!ok) return -1.0;
+    return (double)(t1.tv_sec - t0.tv_sec) + 1e-9 * (double)(t1.tv_nsec - t0.tv_nsec);
 }
 
 /* Number of OpenMP threads the reference code will use (for reporting the CPU baseline). */

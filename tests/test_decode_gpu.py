@@ -193,6 +193,41 @@ def test_device_pos_out_of_range_reported(pkg, ctx):
     assert torch.all(out[1] == 0)
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "int8", "simt"])
+def test_device_pos_above_max_pos_reported(pkg, ctx, orc, monkeypatch, dtype):
+    """A device-side pos inside the cache but above the call's max_pos (the bound the split was sized for)
+    is skipped and reported like one outside the cache, never answered from a truncated key range; the
+    other sequences of the batch are still computed."""
+    import torch
+    if dtype == "simt":
+        monkeypatch.setenv("BITLLM_DECODE_SIMT", "1")
+    dt = {"f32": pkg.F32, "bf16": pkg.BF16, "int8": pkg.INT8, "simt": pkg.BF16}[dtype]
+    rng = np.random.default_rng(31)
+    B, T, nh, nkv, hd = 3, 600, 8, 2, 128
+    kv, kc, vc = make_cache(pkg, ctx, orc, rng, B, T, nkv, hd, dt)  # an INT8 cache quantises on upload
+    qn = rng.standard_normal((B, nh * hd)).astype(np.float32)
+    q = torch.from_numpy(qn).cuda()
+    out = torch.full((B, nh * hd), 7.0, device="cuda")
+    pos_np = np.array([100, 599, 64], np.int32)
+    pos = torch.from_numpy(pos_np).cuda()
+    torch.cuda.synchronize()
+    kv.attend_decode_dev(0, q.data_ptr(), pos.data_ptr(), 128, nh, 0.1, out.data_ptr())  # bound 128 < 599
+    with pytest.raises(pkg.EifCudaError) as e:
+        ctx.synchronize()
+    assert e.value.name == "INVALID_ARGUMENT"
+    ctx.synchronize()
+    o = out.cpu().numpy()
+    assert np.all(o[1] == 0)
+    for b in (0, 2):
+        if dt == pkg.INT8:
+            kq, vq, ks, vs = kv.download_int8(0, b, 0, T)
+            ref = orc.attend_decode_i8(qn[b], kq, ks, vq, vs, int(pos_np[b]), nh, nkv, hd, 0.1)
+        else:
+            ref = orc.attend_decode(qn[b], kc[b], vc[b], int(pos_np[b]), nh, nkv, hd, 0.1)
+        assert rel_l2(o[b], ref) <= TOL, b
+    kv.free()
+
+
 @pytest.mark.parametrize("dtype", ["f32", "bf16", "int8"])
 @pytest.mark.parametrize("hd,nh,nkv", [(64, 14, 2), (128, 8, 2), (64, 2, 2)])
 def test_many_items_per_cta(pkg, ctx, orc, dtype, hd, nh, nkv):

@@ -77,6 +77,33 @@ def test_fullatt_prep_golden(pkg, ctx):
     assert np.array_equal(vd[0], d["v_row"])
 
 
+def test_fullatt_prep_large_positions(pkg, ctx, orc):
+    """Partial RoPE far into a long context (rows up to 32767): at such positions one ulp of an inverse
+    frequency moves the angle by ~1e-3 rad, so the device table must hold the compiled reference's own
+    inverse frequencies (its -ffast-math build evaluates 1/powf(1e7, x) as expf(-x * logf(1e7))).  q and the
+    written k row against the reference's fullatt_prep (the restatement, built the same way, where the
+    reference build is absent)."""
+    rng = np.random.default_rng(90)
+    B, nh, nkv, hd, T = 4, 8, 2, 256, 32768
+    lib = orc.ref() if orc.ref_available() else None
+    kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, pkg.F32)
+    qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kv.set_norms(0, qn, kn)
+    pos = np.array([4095, 20001, 32766, 32767], np.int32)
+    qg = rng.standard_normal((B, nh * 2 * hd)).astype(np.float32)
+    k = rng.standard_normal((B, nkv * hd)).astype(np.float32)
+    v = rng.standard_normal((B, nkv * hd)).astype(np.float32)
+    q, g = kv.fullatt_prep(0, qg, k, v, pos, nh)
+    for b in range(B):
+        kc = np.zeros((int(pos[b]) + 1, nkv * hd), np.float32)
+        rq, rg, rk = orc.fullatt_prep(qg[b], k[b], v[b], qn, kn, kc, kc.copy(), int(pos[b]), nh, nkv, hd, lib=lib)
+        assert rel_l2(q[b], rq) <= 1e-6, (b, rel_l2(q[b], rq))
+        kd, _ = kv.download(0, b, int(pos[b]), 1)
+        assert rel_l2(kd[0], rk) <= 1e-6, b
+    kv.free()
+
+
 def test_deltanet_core_batch_independent(pkg, ctx, orc):
     """40 sequences x 16 heads (more heads than one wave of CTAs) and the first 5 of them alone give the
     same bits (outputs and states), and the large batch matches the port."""
@@ -154,11 +181,12 @@ def test_fullatt_prep_head_dims(pkg, ctx, orc, hd):
         assert rel_l2(kd[0], rk) <= TOL and np.array_equal(vd[0], v[b])
 
 
+@pytest.mark.parametrize("api", ["two_calls", "one_call"])
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
-def test_qwen35_attention_layer_chain(pkg, ctx, orc, dtype):
+def test_qwen35_attention_layer_chain(pkg, ctx, orc, dtype, api):
     """Several decode steps of a Qwen3.5 full-attention layer for a batch with ragged positions:
-    fullatt_prep (norms, partial RoPE, append) then attend with the sigmoid gate and SubLN, against the
-    restatement of fullatt_prep + fullatt_attend."""
+    fullatt_prep (norms, partial RoPE, append) then attend with the sigmoid gate and SubLN -- as two calls, or
+    as the one call eif_cuda_fullatt_decode -- against the restatement of fullatt_prep + fullatt_attend."""
     rng = np.random.default_rng(88)
     B, nh, nkv, hd, T = 3, 8, 2, 256, 48
     dt = pkg.F32 if dtype == "f32" else pkg.BF16
@@ -174,14 +202,18 @@ def test_qwen35_attention_layer_chain(pkg, ctx, orc, dtype):
         qg = rng.standard_normal((B, nh * 2 * hd)).astype(np.float32)
         k = rng.standard_normal((B, nkv * hd)).astype(np.float32)
         v = rng.standard_normal((B, nkv * hd)).astype(np.float32)
-        q, g = kv.fullatt_prep(0, qg, k, v, pos, nh)
-        out = kv.attend_decode(0, q, pos, nh, 1.0 / 16, gate=g, subln=pkg.SUBLN_WEIGHT, sub_norm=sub)
+        if api == "two_calls":
+            q, g = kv.fullatt_prep(0, qg, k, v, pos, nh)
+            out = kv.attend_decode(0, q, pos, nh, 1.0 / 16, gate=g, subln=pkg.SUBLN_WEIGHT, sub_norm=sub)
+        else:
+            out = kv.fullatt_decode(0, qg, k, v, pos, nh, 1.0 / 16, subln=pkg.SUBLN_WEIGHT, sub_norm=sub)
         for b in range(B):
             rq, rg, _ = orc.fullatt_prep(qg[b], k[b], v[b], qn, kn, kc[b], vc[b], pos[b], nh, nkv, hd)
             if dt == pkg.BF16:
                 kc[b, pos[b]] = orc.round_bf16(kc[b, pos[b]])
                 vc[b, pos[b]] = orc.round_bf16(vc[b, pos[b]])
-            assert rel_l2(q[b], rq) <= TOL and np.array_equal(g[b], rg)
+            if api == "two_calls":
+                assert rel_l2(q[b], rq) <= TOL and np.array_equal(g[b], rg)
             ref = orc.subln(orc.attend_decode(rq, kc[b], vc[b], pos[b], nh, nkv, hd, 1.0 / 16, gate=rg), sub, 2)
             assert rel_l2(out[b], ref) <= TOL, (step, b)
         pos = pos + 1
