@@ -631,13 +631,15 @@ def run_prefill(args, torch, dist, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
     # e2e through the host-pointer ABI: fp32 q from pinned host memory, fp32 output read back
+    e2e_ms = None
     qh = torch.randn(B, PF_S, hq * PF_D, generator=torch.Generator().manual_seed(3)).pin_memory().numpy()
-    ctx.set_stream(None)
-    kv.attend_prefill(0, qh, PF_S, 0, hq, scale)
-    t0 = time.perf_counter()
-    for _ in range(max(1, args.steps // 4)):
+    if not args.no_e2e:
+        ctx.set_stream(None)
         kv.attend_prefill(0, qh, PF_S, 0, hq, scale)
-    e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / max(1, args.steps // 4), "cuda")
+        t0 = time.perf_counter()
+        for _ in range(max(1, args.steps // 4)):
+            kv.attend_prefill(0, qh, PF_S, 0, hq, scale)
+        e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / max(1, args.steps // 4), "cuda")
     if rank != 0:
         return None
     _, tflops_peak, src = peaks()
@@ -651,9 +653,10 @@ def run_prefill(args, torch, dist, rank, world, local_rank):
             "config": {"workload": "gqa_causal_prefill (BASELINE configs[1])", "global_batch": GB, "seq_len": PF_S,
                        "heads": "12 q / 2 kv", "head_dim": PF_D, "l2": "256 MiB flush between launches",
                        "parallelism": f"(sequence, kv head) units over {world} rank(s), no collective"},
-            "e2e": {"value": GB * PF_S / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": qh.nbytes * world, "d2h_bytes_per_step": qh.nbytes * world,
-                    "path": "host-pointer C ABI eif_cuda_attend_prefill (fp32 in/out)"},
+            "e2e": None if e2e_ms is None else {
+                "value": GB * PF_S / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": qh.nbytes * world, "d2h_bytes_per_step": qh.nbytes * world,
+                "path": "host-pointer C ABI eif_cuda_attend_prefill (fp32 in/out)"},
             "roofline": {"kernel": "attn_prefill_tc_kernel", "bound": "tensor", "achieved": ach,
                          "peak": tflops_peak, "unit": "TFLOP/s", "frac": ach / tflops_peak, "peak_source": src,
                          "algorithmic_flops_per_launch": flops, "traffic": None},
@@ -850,12 +853,14 @@ def run_recurrent(args, torch, dist, rank, world, local_rank):
     # reads o back (the state stays on the device, as the engine's does)
     hin = [tuple(x.cpu().pin_memory().numpy() for x in ins[i]) for i in range(RC_NIN)]
     oh = torch.empty(B, H * RC_D).pin_memory().numpy()
-    ctx.set_stream(None)
-    st.step(0, *hin[0], q_scale, out=oh)
-    t0 = time.perf_counter()
-    for i in range(RC_STEPS):
-        st.step(i % RC_LAYERS, *hin[i % RC_NIN], q_scale, out=oh)
-    e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3, "cuda")
+    e2e_ms = None
+    if not args.no_e2e:
+        ctx.set_stream(None)
+        st.step(0, *hin[0], q_scale, out=oh)
+        t0 = time.perf_counter()
+        for i in range(RC_STEPS):
+            st.step(i % RC_LAYERS, *hin[i % RC_NIN], q_scale, out=oh)
+        e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3, "cuda")
     if rank != 0:
         return None
     hbm, _, src = peaks()
@@ -873,9 +878,10 @@ def run_recurrent(args, torch, dist, rank, world, local_rank):
                        "l2": f"state streamed from HBM every step ({RC_LAYERS} layers' states alternated, as "
                              "the engine interleaves layers); inputs cycled",
                        "parallelism": f"(sequence, head) units over {world} rank(s), no collective"},
-            "e2e": {"value": GB * RC_STEPS / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": h2d * RC_STEPS, "d2h_bytes_per_step": d2h * RC_STEPS,
-                    "path": "host-pointer C ABI eif_cuda_deltanet_step (pinned), 1024 calls"},
+            "e2e": None if e2e_ms is None else {
+                "value": GB * RC_STEPS / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d * RC_STEPS, "d2h_bytes_per_step": d2h * RC_STEPS,
+                "path": "host-pointer C ABI eif_cuda_deltanet_step (pinned), 1024 calls"},
             "roofline": {"kernel": "delta_rule_kernel", "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
                          "frac": ach / hbm, "peak_source": src, "algorithmic_bytes_per_launch": sbytes + io_bytes,
                          "launch_ms": launch_ms, "traffic": None},
@@ -1045,14 +1051,16 @@ def run_decode(args, torch, dist, rank, world, local_rank):
     vh = torch.randn(B, hkv * DC_D, generator=hg).pin_memory().numpy()
     ph = torch.full((B,), L - 1, dtype=torch.int32).pin_memory().numpy()
     oh = torch.empty(B, hq * DC_D).pin_memory().numpy()
-    ctx.set_stream(None)
-    n_e2e = max(3, args.steps) * (20 if bytes_alg < (64 << 20) else 1)  # short steps: enough of them to time
-    for _ in range(3):
-        kv.decode_step(0, qh, kh, vh, ph, hq, scale, out=oh)
-    t0 = time.perf_counter()
-    for _ in range(n_e2e):
-        kv.decode_step(0, qh, kh, vh, ph, hq, scale, out=oh)
-    e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / n_e2e, "cuda")
+    e2e_ms = None
+    if not args.no_e2e:
+        ctx.set_stream(None)
+        n_e2e = max(3, args.steps) * (20 if bytes_alg < (64 << 20) else 1)  # short steps: enough of them to time
+        for _ in range(3):
+            kv.decode_step(0, qh, kh, vh, ph, hq, scale, out=oh)
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            kv.decode_step(0, qh, kh, vh, ph, hq, scale, out=oh)
+        e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / n_e2e, "cuda")
     if rank != 0:
         return None
     hbm, _, src = peaks()
@@ -1069,9 +1077,10 @@ def run_decode(args, torch, dist, rank, world, local_rank):
                        "heads": "14 q / 2 kv", "head_dim": DC_D, "kv_dtype": kv_name,
                        "l2": "256 MiB flush between steps" if flush is not None else "cache > L2",
                        "parallelism": f"(sequence, kv group) units over {world} rank(s), no collective"},
-            "e2e": {"value": GB / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "host-pointer C ABI eif_cuda_decode_step (pinned)"},
+            "e2e": None if e2e_ms is None else {
+                "value": GB / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "host-pointer C ABI eif_cuda_decode_step (pinned)"},
             "step_path": "one launch (attn_decode_step_kernel, a cluster per (sequence, kv head))"
                          if launches == args.steps else "rope_append_kernel + split-K decode + combine",
             "roofline": {"kernel": {"bf16": "attn_decode_tc_kernel", "int8": "attn_decode_i8_kernel"}.get(
