@@ -53,9 +53,23 @@ UNIT = "tokens/s"
 # kernel (dram__bytes_read.sum + dram__bytes_write.sum over the algorithmic bytes of that launch; the summaries
 # under profiles/ give the commands).  The bench scales it to its own launch by the units processed, which is
 # valid where traffic grows in proportion to the units (every kernel here streams each unit's bytes once).
+# ncu flushes L2 before a captured launch, so a kernel whose writes still fit in L2 when it ends shows fewer
+# DRAM write bytes than it eventually causes (the recurrent rule's state, the prefill outputs).
+_DRAM = "profiles/dram_traffic_bench_kernels.md"
 TRAFFIC_PER_ALG_BYTE = {
-    # batch 8 of config 5's attention layer: 536.99 MB read + 7.37 MB written for 536.87 MB of K + V
-    "attn_decode_tc_hd256": ((536.99 + 7.37) / 536.87, "profiles/attn_decode_tc_qwen35_hybrid.md"),
+    # config 5's attention layer at batch 8: 537,031,168 B read + 137,472 B written / 537,067,520 B algorithmic
+    "attn_decode_tc_hd256": (537168640 / 537067520, _DRAM),
+    # config 2 at full size: 137,945,600 B read + 61,187,840 B written / 234,881,024 B (q, K, V, o)
+    "attn_prefill_tc": (199133440 / 234881024, _DRAM),
+    # config 4 at batch 1, both kernels of the prefill (k is read by the solve and by the state walk):
+    # 185,881,344 B / 137,363,456 B
+    "deltanet_chunked": (185881344 / 137363456, _DRAM),
+    # config 3, one rule step over 64 x 16 heads: 68,700,160 B read + 7,954,176 B written / 136,323,072 B
+    "delta_rule": (76654336 / 136323072, _DRAM),
+    # config 1's heads batched (256 sequences, ctx 4096), attention launch
+    "attn_decode_f32": (1079984896 / 1073741824, _DRAM),
+    "attn_decode_tc": (552377088 / 536870912, _DRAM),
+    "attn_decode_i8": (291107584 / 285212672, _DRAM),
 }
 
 
@@ -644,6 +658,7 @@ def run_prefill(args, torch, dist, rank, world, local_rank):
         return None
     _, tflops_peak, src = peaks()
     flops = prefill_flops(B, PF_S) * hq / PF_HQ  # this rank's launch
+    pf_bytes = B * PF_S * (2 * hq + 2 * hkv) * PF_D * 2  # q, o (bf16) and the K / V rows, each once
     ach = flops / (ms * 1e-3) / 1e12
     GB = GBP
     line = {"metric": "causal prefill attention tokens/s (BASELINE configs[1])", "value": GB * PF_S / (ms * 1e-3),
@@ -659,7 +674,9 @@ def run_prefill(args, torch, dist, rank, world, local_rank):
                 "path": "host-pointer C ABI eif_cuda_attend_prefill (fp32 in/out)"},
             "roofline": {"kernel": "attn_prefill_tc_kernel", "bound": "tensor", "achieved": ach,
                          "peak": tflops_peak, "unit": "TFLOP/s", "frac": ach / tflops_peak, "peak_source": src,
-                         "algorithmic_flops_per_launch": flops, "traffic": None},
+                         "algorithmic_flops_per_launch": flops,
+                         "traffic": traffic("attn_prefill_tc", pf_bytes)[0],
+                         "traffic_source": traffic("attn_prefill_tc", pf_bytes)[1]},
             "gpu_launches": launches, "clocks": clk}
     if world == 1 and not args.no_cpu_baseline:
         tps, cores, kind, sample = cpu_prefill_reference()
@@ -768,7 +785,8 @@ def run_chunked(args, torch, dist, rank, world, local_rank):
             "roofline": {"kernel": "deltanet_chunked_kernel", "bound": "hbm", "achieved": ach, "peak": hbm,
                          "unit": "GB/s", "frac": ach / hbm, "peak_source": src, "algorithmic_bytes_per_launch":
                              bytes_alg, "recurrent_equivalent_tflops": flops_rec / (ms * 1e-3) / 1e12,
-                         "traffic": None},
+                         "traffic": traffic("deltanet_chunked", bytes_alg)[0],
+                         "traffic_source": traffic("deltanet_chunked", bytes_alg)[1]},
             "gpu_launches": launches, "clocks": clk}
     if e2e is not None:
         line["e2e"] = e2e
@@ -884,7 +902,8 @@ def run_recurrent(args, torch, dist, rank, world, local_rank):
                 "path": "host-pointer C ABI eif_cuda_deltanet_step (pinned), 1024 calls"},
             "roofline": {"kernel": "delta_rule_kernel", "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
                          "frac": ach / hbm, "peak_source": src, "algorithmic_bytes_per_launch": sbytes + io_bytes,
-                         "launch_ms": launch_ms, "traffic": None},
+                         "launch_ms": launch_ms, "traffic": traffic("delta_rule", sbytes + io_bytes)[0],
+                         "traffic_source": traffic("delta_rule", sbytes + io_bytes)[1]},
             "gpu_launches": launches, "clocks": clk}
     if world == 1 and not args.no_cpu_baseline:
         tps, cores, kind, sample = cpu_chunked_reference()
@@ -1065,6 +1084,7 @@ def run_decode(args, torch, dist, rank, world, local_rank):
         return None
     hbm, _, src = peaks()
     ach = bytes_alg / (att_ms * 1e-3) / 1e9
+    dec_kernel = {"bf16": "attn_decode_tc", "int8": "attn_decode_i8"}.get(kv_name, "attn_decode_f32")
     h2d = (qh.nbytes + kh.nbytes + vh.nbytes + ph.nbytes) * world
     d2h = oh.nbytes * world
     cfg_name = "BASELINE configs[0] exactly" if (GB, L, kv_name) == (1, 512, "f32") else \
@@ -1083,11 +1103,12 @@ def run_decode(args, torch, dist, rank, world, local_rank):
                 "path": "host-pointer C ABI eif_cuda_decode_step (pinned)"},
             "step_path": "one launch (attn_decode_step_kernel, a cluster per (sequence, kv head))"
                          if launches == args.steps else "rope_append_kernel + split-K decode + combine",
-            "roofline": {"kernel": {"bf16": "attn_decode_tc_kernel", "int8": "attn_decode_i8_kernel"}.get(
-                             kv_name, "attn_decode_f32_kernel") + " + combine", "bound": "hbm", "achieved": ach,
+            "roofline": {"kernel": dec_kernel + "_kernel + combine", "bound": "hbm", "achieved": ach,
                          "peak": hbm,
                          "unit": "GB/s", "frac": ach / hbm, "peak_source": src,
-                         "algorithmic_bytes_per_launch": bytes_alg, "attention_ms": att_ms, "traffic": None},
+                         "algorithmic_bytes_per_launch": bytes_alg, "attention_ms": att_ms,
+                         "traffic": traffic(dec_kernel, bytes_alg)[0] if GB > 1 else None,
+                         "traffic_source": traffic(dec_kernel, bytes_alg)[1] if GB > 1 else None},
             "gpu_launches": launches, "clocks": clk}
     if world == 1 and not args.no_cpu_baseline:
         tps, cores, kind, sample = cpu_decode_reference(kv_name, L)

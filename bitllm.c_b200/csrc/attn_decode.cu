@@ -33,7 +33,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
     const KT *__restrict__ Kc, const KT *__restrict__ Vc, const float *__restrict__ q, const int *__restrict__ pos,
     int max_seq, int max_len, int Hkv, int chunk, int nchunk, float scale, float *__restrict__ part_o,
     float2 *__restrict__ part_ml, unsigned *__restrict__ dev_err, const float *__restrict__ k_scale,
-    const float *__restrict__ v_scale, int sstride) {
+    const float *__restrict__ v_scale, int sstride, const int *__restrict__ row_seq) {
     constexpr int DL = D / 32;  // head-dim elements per lane in P.V
     static_assert(D % 32 == 0 && (DL == 2 || DL == 4 || DL == 8), "head_dim 64/128/256");
     constexpr bool kI8 = sizeof(KT) == 1;  // INT8 cache: codes, one K and one V scale per (row, kv head)
@@ -70,8 +70,9 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
     }
 
     const size_t row_stride = (size_t)Hkv * D;
-    const KT *Kb = Kc + ((size_t)b * max_seq * Hkv + kvh) * D;
-    const KT *Vb = Vc + ((size_t)b * max_seq * Hkv + kvh) * D;
+    const int cb = row_seq ? row_seq[b] : b;  // the cache sequence of query row b
+    const KT *Kb = Kc + ((size_t)cb * max_seq * Hkv + kvh) * D;
+    const KT *Vb = Vc + ((size_t)cb * max_seq * Hkv + kvh) * D;
 
     for (int t0 = t_begin + warp * 32; t0 < t_end; t0 += kDecodeWarps * 32) {
         const int t = t0 + lane;
@@ -82,7 +83,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
         float ksc = 1.f, vsc = 1.f;
         if constexpr (kI8) {
             if (valid) {
-                const size_t si = ((size_t)b * Hkv + kvh) * sstride + t;
+                const size_t si = ((size_t)cb * Hkv + kvh) * sstride + t;
                 ksc = k_scale[si];
                 vsc = v_scale[si];
             }
@@ -339,7 +340,7 @@ cudaError_t launch_simt(cudaStream_t st, const DecodeArgs &a, const Split &sp, f
     dim3 grid(sp.nchunk, a.Hkv, a.B);
     attn_decode_simt_kernel<KT, D, G><<<grid, kDecodeThreads, 0, st>>>(
         static_cast<const KT *>(a.K), static_cast<const KT *>(a.V), a.q, a.pos, a.max_seq, a.max_len, a.Hkv, sp.chunk,
-        sp.nchunk, a.scale, part_o, part_ml, a.dev_err, a.k_scale, a.v_scale, a.scale_stride);
+        sp.nchunk, a.scale, part_o, part_ml, a.dev_err, a.k_scale, a.v_scale, a.scale_stride, a.row_seq);
     return cudaGetLastError();
 }
 
@@ -369,6 +370,22 @@ cudaError_t dispatch_d(cudaStream_t st, const DecodeArgs &a, const Split &sp, fl
 }
 
 }  // namespace
+
+namespace {
+__global__ void prefill_rows_kernel(int *row_seq, int *pos, int rows, int n_tok, int start_pos) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < rows) {
+        row_seq[i] = i / n_tok;
+        pos[i] = start_pos + i % n_tok;
+    }
+}
+}  // namespace
+
+cudaError_t launch_prefill_rows(cudaStream_t st, int *row_seq, int *pos, int batch, int n_tok, int start_pos) {
+    const int rows = batch * n_tok;
+    prefill_rows_kernel<<<(rows + 255) / 256, 256, 0, st>>>(row_seq, pos, rows, n_tok, start_pos);
+    return cudaGetLastError();
+}
 
 size_t decode_workspace_bytes(const DecodeArgs &a, int sm_count) {
     const Split sp = choose_split(a, sm_count);

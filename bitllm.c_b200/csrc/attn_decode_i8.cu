@@ -71,6 +71,7 @@ struct I8Params {
     const float *q;
     const float *ks, *vs;  // [B][Hkv][sstride] scales
     const int *pos;
+    const int *row_seq;  // nullptr, or the cache sequence of each query row (prefill rows)
     int max_seq, max_len, Hkv, G, Hq, sstride;
     int nchunk, chunk_keys, n_items;
     float qscale;  // scale * log2(e)
@@ -80,7 +81,7 @@ struct I8Params {
 };
 
 struct ItemInfo {
-    int b, kvh, t_begin, t_end, ntiles;
+    int b, cb, kvh, t_begin, t_end, ntiles;  // b: query row, cb: its cache sequence
 };
 
 __device__ __forceinline__ ItemInfo item_info(const I8Params &p, int item, bool report) {
@@ -88,6 +89,7 @@ __device__ __forceinline__ ItemInfo item_info(const I8Params &p, int item, bool 
     const int unit = item / p.nchunk, c = item - unit * p.nchunk;
     it.b = unit / p.Hkv;
     it.kvh = unit - it.b * p.Hkv;
+    it.cb = p.row_seq ? p.row_seq[it.b] : it.b;
     int pp = p.pos[it.b];
     if (pp < 0 || pp >= p.max_len) {  // max_len = the caller's bound + 1, never above max_seq
         if (report) atomicOr(p.dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
@@ -183,7 +185,7 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
                 if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.dev_err)) return;
                 const uint32_t fb = full0 + 8 * s;
                 const int t0 = inf.t_begin + i * KT;
-                const int row = inf.b * p.max_seq + t0;
+                const int row = inf.cb * p.max_seq + t0;
                 mbar_arrive_expect_tx(fb, C::STAGE + C::SCALES);
                 const uint32_t kdst = smem_u32(smem + s * C::STAGE), vdst = kdst + C::TILE;
 #pragma unroll
@@ -191,7 +193,7 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
                     tma_load_3d(kdst + j * C::BOX, &tmK, j * C::BW, inf.kvh, row, fb);
                     tma_load_3d(vdst + j * C::BOX, &tmV, j * C::BW, inf.kvh, row, fb);
                 }
-                const size_t srow = ((size_t)inf.b * p.Hkv + inf.kvh) * p.sstride + t0;
+                const size_t srow = ((size_t)inf.cb * p.Hkv + inf.kvh) * p.sstride + t0;
                 const uint32_t sdst = smem_u32(sbuf + s * 2 * KT);
                 bulk_load(sdst, p.ks + srow, KT * 4, fb);
                 bulk_load(sdst + KT * 4, p.vs + srow, KT * 4, fb);
@@ -401,6 +403,7 @@ cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, cons
     p.vs = a.v_scale;
     p.sstride = a.scale_stride;
     p.pos = a.pos;
+    p.row_seq = a.row_seq;
     p.max_seq = a.max_seq;
     p.max_len = a.max_len;
     p.Hkv = a.Hkv;

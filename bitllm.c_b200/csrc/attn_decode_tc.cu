@@ -57,6 +57,7 @@ constexpr int tc_groups(int D) { return D <= 128 ? 2 : 1; }
 struct TcParams {
     const float *q;
     const int *pos;
+    const int *row_seq;  // nullptr, or the cache sequence of each query row (prefill rows)
     int max_seq, max_len, Hkv, G, Hq;
     int nchunk, chunk_keys, n_items;
     float qscale;  // scale * log2(e)
@@ -66,7 +67,7 @@ struct TcParams {
 };
 
 struct ItemInfo {
-    int b, kvh, t_begin, t_end, ntiles;
+    int b, cb, kvh, t_begin, t_end, ntiles;  // b: query row, cb: its cache sequence
 };
 
 __device__ __forceinline__ ItemInfo item_info(const TcParams &p, int item, bool report) {
@@ -74,6 +75,7 @@ __device__ __forceinline__ ItemInfo item_info(const TcParams &p, int item, bool 
     const int unit = item / p.nchunk, c = item - unit * p.nchunk;
     it.b = unit / p.Hkv;
     it.kvh = unit - it.b * p.Hkv;
+    it.cb = p.row_seq ? p.row_seq[it.b] : it.b;
     int pp = p.pos[it.b];
     if (pp < 0 || pp >= p.max_len) {  // max_len = the caller's bound + 1, never above max_seq
         if (report) atomicOr(p.dev_err, (unsigned)EIF_DEVERR_POS_RANGE);
@@ -121,7 +123,7 @@ __global__ void __launch_bounds__(TcCfg<D, NB, NG>::THREADS, 1)
                 if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.dev_err)) return;
                 const uint32_t fb = full0 + 8 * s;
                 mbar_arrive_expect_tx(fb, C::STAGE);
-                const int row = inf.b * p.max_seq + inf.t_begin + i * KT;
+                const int row = inf.cb * p.max_seq + inf.t_begin + i * KT;
                 const uint32_t kdst = smem_u32(smem + s * C::STAGE), vdst = kdst + C::TILE;
 #pragma unroll
                 for (int j = 0; j < D / 64; ++j) {
@@ -367,6 +369,7 @@ cudaError_t launch_attend_decode_tc(cudaStream_t st, const CUtensorMap &tk, cons
     TcParams p;
     p.q = a.q;
     p.pos = a.pos;
+    p.row_seq = a.row_seq;
     p.max_seq = a.max_seq;
     p.max_len = a.max_len;
     p.Hkv = a.Hkv;

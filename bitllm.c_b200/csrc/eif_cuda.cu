@@ -280,6 +280,7 @@ EIF_API void eif_cuda_free(eif_cuda_ctx_t *ctx) {
         if (ctx->ws) cudaFree(ctx->ws);
         if (ctx->stage) cudaFree(ctx->stage);
         if (ctx->mix) cudaFree(ctx->mix);
+        if (ctx->rowbuf) cudaFree(ctx->rowbuf);
         if (ctx->io) cudaFree(ctx->io);
         if (ctx->host_err) cudaFreeHost(ctx->host_err);
         if (ctx->pin) cudaFreeHost(ctx->pin);
@@ -741,12 +742,33 @@ static eif_status_t prefill_check(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int la
     if (n_tok < 1 || start_pos < 0 || start_pos + n_tok > kv->max_seq)
         return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rows [%d, %d) outside the cache [0, %d)", start_pos,
                     start_pos + n_tok, kv->max_seq);
-    if (kv->dtype != EIF_CUDA_BF16 || !prefill_tc_supported(kv->hd))
-        return fail(ctx, EIF_STATUS_NOT_SUPPORTED,
-                    "prefill attention needs a bf16 cache with head_dim 64, 128 or 256 (an INT8 cache is read by "
-                    "the decode attention)");
-    if ((size_t)kv->batch * n_tok > 0x7fffffffull) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "too many rows");
+    if (kv->hd != 64 && kv->hd != 128 && kv->hd != 256)
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "prefill attention: head_dim %d (64, 128 or 256)", kv->hd);
+    if ((size_t)kv->batch * n_tok * kv->n_kv > 0x3fffffffull)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "too many rows");
     return EIF_STATUS_OK;
+}
+
+// bf16 caches run the causal prefill on the tensor-core kernels (bf16 q / out); fp32 and INT8 caches run every
+// token of the chunk as one decode row at its own position on the decode kernels, in fp32 arithmetic over the
+// cache's own values (fp32 q / out) -- the reference's per-token loop (src/eif_tinyllm.c:1158-1268,
+// src/eif_qwen35.c:1122-1133), with the split-K work spread over (token, kv head, key chunk) items.
+static bool prefill_by_rows(const eif_cuda_kv_t *kv) { return kv->dtype != EIF_CUDA_BF16; }
+
+static eif_status_t prefill_rows_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_dev,
+                                     int n_tok, int start_pos, int n_heads, float scale, const float *gate_dev,
+                                     eif_cuda_subln_t subln, const float *sub_norm_dev, float *out_dev) {
+    const int rows = kv->batch * n_tok;
+    eif_status_t st = ensure_buffer(ctx, &ctx->rowbuf, &ctx->rowbuf_bytes, 2 * a256((size_t)rows * 4));
+    if (st != EIF_STATUS_OK) return st;
+    int *row_seq = static_cast<int *>(ctx->rowbuf);
+    int *pos = reinterpret_cast<int *>(static_cast<char *>(ctx->rowbuf) + a256((size_t)rows * 4));
+    CK(launch_prefill_rows(ctx->stream, row_seq, pos, kv->batch, n_tok, start_pos));
+    ctx->launches += 1;
+    DecodeArgs a{kv->k[layer], kv->v[layer], kv->dtype, q_dev, pos, rows, n_heads, kv->n_kv, kv->hd, kv->max_seq,
+                 start_pos + n_tok, scale, gate_dev, (int)subln, sub_norm_dev, out_dev, ctx->dev_err};
+    a.row_seq = row_seq;
+    return decode_run(ctx, kv, layer, a);
 }
 
 // TMA descriptor of the queries [B*n_tok][Hq][hd] bf16: boxes of 64 dims x 1 head x 128 tokens.
@@ -788,6 +810,9 @@ EIF_API eif_status_t eif_cuda_attend_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_k
     if (st != EIF_STATUS_OK) return st;
     if (!q_dev || !out_dev) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "attend_prefill_dev: NULL pointer");
     DeviceGuard g(ctx);
+    if (prefill_by_rows(kv))
+        return prefill_rows_run(ctx, kv, layer, static_cast<const float *>(q_dev), n_tok, start_pos, n_heads, scale,
+                                nullptr, EIF_CUDA_SUBLN_NONE, nullptr, static_cast<float *>(out_dev));
     return prefill_run(ctx, kv, layer, q_dev, n_tok, start_pos, n_heads, scale, out_dev);
 }
 
@@ -798,6 +823,19 @@ EIF_API eif_status_t eif_cuda_attend_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t 
     if (!q || !out) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "attend_prefill: NULL pointer");
     DeviceGuard g(ctx);
     const size_t n = (size_t)kv->batch * n_tok * n_heads * kv->hd;
+    if (prefill_by_rows(kv)) {
+        Carver cr;
+        const size_t o_q = cr.take(n * 4), o_o = cr.take(n * 4);
+        st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cr.off);
+        if (st != EIF_STATUS_OK) return st;
+        char *s = static_cast<char *>(ctx->stage);
+        CK(cudaMemcpyAsync(s + o_q, q, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        st = prefill_rows_run(ctx, kv, layer, reinterpret_cast<float *>(s + o_q), n_tok, start_pos, n_heads, scale,
+                              nullptr, EIF_CUDA_SUBLN_NONE, nullptr, reinterpret_cast<float *>(s + o_o));
+        if (st != EIF_STATUS_OK) return st;
+        CK(cudaMemcpyAsync(out, s + o_o, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        return wait_stream(ctx);
+    }
     Carver cv;
     const size_t o_f = cv.take(n * 4), o_q = cv.take(n * 2), o_o = cv.take(n * 2);
     st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
@@ -849,6 +887,9 @@ EIF_API eif_status_t eif_cuda_attend_prefill_gated_dev(eif_cuda_ctx_t *ctx, eif_
     if (st != EIF_STATUS_OK) return st;
     if (!q_dev || !out_dev) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "attend_prefill_gated_dev: NULL pointer");
     DeviceGuard g(ctx);
+    if (prefill_by_rows(kv))
+        return prefill_rows_run(ctx, kv, layer, static_cast<const float *>(q_dev), n_tok, start_pos, n_heads, scale,
+                                gate_dev, subln, sub_norm_dev, out_dev);
     return prefill_gated_run(ctx, kv, layer, q_dev, n_tok, start_pos, n_heads, scale, gate_dev, subln, sub_norm_dev,
                              out_dev);
 }
@@ -864,21 +905,30 @@ EIF_API eif_status_t eif_cuda_attend_prefill_gated(eif_cuda_ctx_t *ctx, eif_cuda
     if (!q || !out) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "attend_prefill_gated: NULL pointer");
     DeviceGuard g(ctx);
     const size_t row = (size_t)n_heads * kv->hd, n = (size_t)kv->batch * n_tok * row;
+    const bool rows = prefill_by_rows(kv);  // fp32 q on the decode kernels, else bf16 q on the prefill kernels
     Carver cv;
-    const size_t o_f = cv.take(n * 4), o_q = cv.take(n * 2), o_g = gate ? cv.take(n * 4) : 0,
+    const size_t o_f = cv.take(n * 4), o_q = cv.take(rows ? n * 4 : n * 2), o_g = gate ? cv.take(n * 4) : 0,
                  o_n = subln == EIF_CUDA_SUBLN_WEIGHT ? cv.take(row * 4) : 0;
     st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
     if (st != EIF_STATUS_OK) return st;
     char *s = static_cast<char *>(ctx->stage);
     float *f = reinterpret_cast<float *>(s + o_f);
-    CK(cudaMemcpyAsync(f, q, n * 4, cudaMemcpyHostToDevice, ctx->stream));
-    CK(launch_f32_to_bf16(ctx->stream, f, reinterpret_cast<__nv_bfloat16 *>(s + o_q), n));
-    ctx->launches += 1;
+    if (rows) {
+        CK(cudaMemcpyAsync(s + o_q, q, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    } else {
+        CK(cudaMemcpyAsync(f, q, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        CK(launch_f32_to_bf16(ctx->stream, f, reinterpret_cast<__nv_bfloat16 *>(s + o_q), n));
+        ctx->launches += 1;
+    }
     if (gate) CK(cudaMemcpyAsync(s + o_g, gate, n * 4, cudaMemcpyHostToDevice, ctx->stream));
     if (subln == EIF_CUDA_SUBLN_WEIGHT) CK(cudaMemcpyAsync(s + o_n, sub_norm, row * 4, cudaMemcpyHostToDevice, ctx->stream));
-    st = prefill_gated_run(ctx, kv, layer, s + o_q, n_tok, start_pos, n_heads, scale,
-                           gate ? reinterpret_cast<float *>(s + o_g) : nullptr, subln,
-                           subln == EIF_CUDA_SUBLN_WEIGHT ? reinterpret_cast<float *>(s + o_n) : nullptr, f);
+    const float *gd = gate ? reinterpret_cast<float *>(s + o_g) : nullptr;
+    const float *nd = subln == EIF_CUDA_SUBLN_WEIGHT ? reinterpret_cast<float *>(s + o_n) : nullptr;
+    if (rows)
+        st = prefill_rows_run(ctx, kv, layer, reinterpret_cast<float *>(s + o_q), n_tok, start_pos, n_heads, scale, gd,
+                              subln, nd, f);
+    else
+        st = prefill_gated_run(ctx, kv, layer, s + o_q, n_tok, start_pos, n_heads, scale, gd, subln, nd, f);
     if (st != EIF_STATUS_OK) return st;
     CK(cudaMemcpyAsync(out, f, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return wait_stream(ctx);
@@ -1541,6 +1591,9 @@ EIF_API eif_status_t eif_cuda_rope_append_prefill_dev(eif_cuda_ctx_t *ctx, eif_c
     if (!q_dev || !k_dev || !v_dev || !q_out_dev)
         return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "rope_append_prefill_dev: NULL pointer");
     DeviceGuard g(ctx);
+    if (prefill_by_rows(kv))  // fp32 / INT8 caches: the prefill attention reads fp32 queries
+        return rope_run(ctx, kv, layer, q_dev, k_dev, v_dev, nullptr, n_tok, start_pos, n_heads,
+                        static_cast<float *>(q_out_dev), nullptr);
     return rope_run(ctx, kv, layer, q_dev, k_dev, v_dev, nullptr, n_tok, start_pos, n_heads, nullptr,
                     static_cast<__nv_bfloat16 *>(q_out_dev));
 }
@@ -1670,6 +1723,9 @@ EIF_API eif_status_t eif_cuda_fullatt_prep_prefill_dev(eif_cuda_ctx_t *ctx, eif_
     if (!qg_dev || !k_dev || !v_dev || !q_out_dev || !gate_out_dev)
         return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "fullatt_prep_prefill_dev: NULL pointer");
     DeviceGuard g(ctx);
+    if (prefill_by_rows(kv))  // an fp32 cache: the prefill attention reads fp32 queries
+        return prep_run(ctx, kv, layer, qg_dev, k_dev, v_dev, nullptr, n_heads, static_cast<float *>(q_out_dev),
+                        gate_out_dev, n_tok, start_pos);
     return prep_run(ctx, kv, layer, qg_dev, k_dev, v_dev, nullptr, n_heads, nullptr, gate_out_dev, n_tok, start_pos,
                     static_cast<__nv_bfloat16 *>(q_out_dev));
 }
@@ -1812,6 +1868,133 @@ EIF_API eif_status_t eif_cuda_fullatt_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t 
                             scale, subln, wn ? reinterpret_cast<float *>(s + o_n) : nullptr,
                             reinterpret_cast<float *>(s + o_o), reinterpret_cast<float *>(s + o_q),
                             reinterpret_cast<float *>(s + o_g));
+    if (st != EIF_STATUS_OK) return st;
+    CK(cudaMemcpyAsync(out, s + o_o, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// =================================================================================================
+// Whole attention blocks of a prefill chunk in one call (queries stay on the device between the halves)
+// =================================================================================================
+
+// tinyllm: RoPE + cache write of the chunk, then causal attention; q_buf holds the rotated queries (bf16 for a
+// bf16 cache, fp32 otherwise), out is fp32.
+static eif_status_t prefill_step_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
+                                     const float *k, const float *v, int n_tok, int start_pos, int n_heads,
+                                     float scale, float *out, void *q_buf) {
+    const bool rows = prefill_by_rows(kv);
+    eif_status_t st = rope_run(ctx, kv, layer, q, k, v, nullptr, n_tok, start_pos, n_heads,
+                               rows ? static_cast<float *>(q_buf) : nullptr,
+                               rows ? nullptr : static_cast<__nv_bfloat16 *>(q_buf));
+    if (st != EIF_STATUS_OK) return st;
+    if (rows)
+        return prefill_rows_run(ctx, kv, layer, static_cast<float *>(q_buf), n_tok, start_pos, n_heads, scale, nullptr,
+                                EIF_CUDA_SUBLN_NONE, nullptr, out);
+    return prefill_run(ctx, kv, layer, q_buf, n_tok, start_pos, n_heads, scale, nullptr, out);
+}
+
+EIF_API eif_status_t eif_cuda_prefill_step_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_dev,
+                                               const float *k_dev, const float *v_dev, int n_tok, int start_pos,
+                                               int n_heads, float scale, float *out_dev) {
+    eif_status_t st = rope_prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st == EIF_STATUS_OK) st = prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st != EIF_STATUS_OK) return st;
+    if (!q_dev || !k_dev || !v_dev || !out_dev)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "prefill_step_dev: NULL pointer");
+    DeviceGuard g(ctx);
+    const size_t nq = (size_t)kv->batch * n_tok * n_heads * kv->hd;
+    st = ensure_buffer(ctx, &ctx->mix, &ctx->mix_bytes, a256(nq * 4));
+    if (st != EIF_STATUS_OK) return st;
+    return prefill_step_run(ctx, kv, layer, q_dev, k_dev, v_dev, n_tok, start_pos, n_heads, scale, out_dev, ctx->mix);
+}
+
+EIF_API eif_status_t eif_cuda_prefill_step(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
+                                           const float *k, const float *v, int n_tok, int start_pos, int n_heads,
+                                           float scale, float *out) {
+    eif_status_t st = rope_prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st == EIF_STATUS_OK) st = prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st != EIF_STATUS_OK) return st;
+    if (!q || !k || !v || !out) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "prefill_step: NULL pointer");
+    DeviceGuard g(ctx);
+    const size_t rows = (size_t)kv->batch * n_tok, nq = rows * n_heads * kv->hd, nk = rows * kv->n_kv * kv->hd;
+    Carver cv;
+    const size_t o_q = cv.take(nq * 4), o_k = cv.take(nk * 4), o_v = cv.take(nk * 4), o_r = cv.take(nq * 4),
+                 o_o = cv.take(nq * 4);
+    st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (st != EIF_STATUS_OK) return st;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_q, q, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_k, k, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_v, v, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    st = prefill_step_run(ctx, kv, layer, reinterpret_cast<float *>(s + o_q), reinterpret_cast<float *>(s + o_k),
+                          reinterpret_cast<float *>(s + o_v), n_tok, start_pos, n_heads, scale,
+                          reinterpret_cast<float *>(s + o_o), s + o_r);
+    if (st != EIF_STATUS_OK) return st;
+    CK(cudaMemcpyAsync(out, s + o_o, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// Qwen3.5: fullatt_prep of the chunk, then the gated causal attention; q_buf as above, gate_buf fp32.
+static eif_status_t fullatt_prefill_run(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg,
+                                        const float *k, const float *v, int n_tok, int start_pos, int n_heads,
+                                        float scale, eif_cuda_subln_t subln, const float *sub_norm, float *out,
+                                        void *q_buf, float *gate_buf) {
+    const bool rows = prefill_by_rows(kv);
+    eif_status_t st = prep_run(ctx, kv, layer, qg, k, v, nullptr, n_heads, rows ? static_cast<float *>(q_buf) : nullptr,
+                               gate_buf, n_tok, start_pos, rows ? nullptr : static_cast<__nv_bfloat16 *>(q_buf));
+    if (st != EIF_STATUS_OK) return st;
+    if (rows)
+        return prefill_rows_run(ctx, kv, layer, static_cast<float *>(q_buf), n_tok, start_pos, n_heads, scale, gate_buf,
+                                subln, sub_norm, out);
+    return prefill_gated_run(ctx, kv, layer, q_buf, n_tok, start_pos, n_heads, scale, gate_buf, subln, sub_norm, out);
+}
+
+EIF_API eif_status_t eif_cuda_fullatt_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer,
+                                                  const float *qg_dev, const float *k_dev, const float *v_dev,
+                                                  int n_tok, int start_pos, int n_heads, float scale,
+                                                  eif_cuda_subln_t subln, const float *sub_norm_dev, float *out_dev) {
+    eif_status_t st = prep_prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st == EIF_STATUS_OK) st = prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st == EIF_STATUS_OK) st = subln_check(ctx, subln, sub_norm_dev);
+    if (st != EIF_STATUS_OK) return st;
+    if (!qg_dev || !k_dev || !v_dev || !out_dev)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "fullatt_prefill_dev: NULL pointer");
+    DeviceGuard g(ctx);
+    const size_t nq = (size_t)kv->batch * n_tok * n_heads * kv->hd;
+    st = ensure_buffer(ctx, &ctx->mix, &ctx->mix_bytes, 2 * a256(nq * 4));
+    if (st != EIF_STATUS_OK) return st;
+    float *gb = reinterpret_cast<float *>(static_cast<char *>(ctx->mix) + a256(nq * 4));
+    return fullatt_prefill_run(ctx, kv, layer, qg_dev, k_dev, v_dev, n_tok, start_pos, n_heads, scale, subln,
+                               sub_norm_dev, out_dev, ctx->mix, gb);
+}
+
+EIF_API eif_status_t eif_cuda_fullatt_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg,
+                                              const float *k, const float *v, int n_tok, int start_pos, int n_heads,
+                                              float scale, eif_cuda_subln_t subln, const float *sub_norm,
+                                              float *out) {
+    eif_status_t st = prep_prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st == EIF_STATUS_OK) st = prefill_check(ctx, kv, layer, n_tok, start_pos, n_heads);
+    if (st == EIF_STATUS_OK) st = subln_check(ctx, subln, sub_norm);
+    if (st != EIF_STATUS_OK) return st;
+    if (!qg || !k || !v || !out) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "fullatt_prefill: NULL pointer");
+    DeviceGuard g(ctx);
+    const size_t rows = (size_t)kv->batch * n_tok, row = (size_t)n_heads * kv->hd, nq = rows * row,
+                 nk = rows * kv->n_kv * kv->hd;
+    const bool wn = subln == EIF_CUDA_SUBLN_WEIGHT;
+    Carver cv;
+    const size_t o_qg = cv.take(2 * nq * 4), o_k = cv.take(nk * 4), o_v = cv.take(nk * 4),
+                 o_n = cv.take(wn ? row * 4 : 0), o_q = cv.take(nq * 4), o_g = cv.take(nq * 4), o_o = cv.take(nq * 4);
+    st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, cv.off);
+    if (st != EIF_STATUS_OK) return st;
+    char *s = static_cast<char *>(ctx->stage);
+    CK(cudaMemcpyAsync(s + o_qg, qg, 2 * nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_k, k, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(s + o_v, v, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (wn) CK(cudaMemcpyAsync(s + o_n, sub_norm, row * 4, cudaMemcpyHostToDevice, ctx->stream));
+    st = fullatt_prefill_run(ctx, kv, layer, reinterpret_cast<float *>(s + o_qg), reinterpret_cast<float *>(s + o_k),
+                             reinterpret_cast<float *>(s + o_v), n_tok, start_pos, n_heads, scale, subln,
+                             wn ? reinterpret_cast<float *>(s + o_n) : nullptr, reinterpret_cast<float *>(s + o_o),
+                             s + o_q, reinterpret_cast<float *>(s + o_g));
     if (st != EIF_STATUS_OK) return st;
     CK(cudaMemcpyAsync(out, s + o_o, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return wait_stream(ctx);

@@ -34,6 +34,9 @@ struct eif_cuda_ctx {
     // device q / gate between the two halves of eif_cuda_fullatt_decode_dev, grown on demand
     void *mix = nullptr;
     size_t mix_bytes = 0;
+    // device (cache sequence, pos) of every query row of a prefill over an fp32 / INT8 cache, grown on demand
+    void *rowbuf = nullptr;
+    size_t rowbuf_bytes = 0;
     // device error word: the first 16 bytes of io, whose remaining kSmallIo bytes take the outputs of
     // small host-pointer calls, so that the word and the output come back in one copy
     void *io = nullptr;
@@ -107,6 +110,9 @@ struct DecodeArgs {
     const float *k_scale = nullptr;  // INT8 caches: [B][Hkv][scale_stride] scales of K and V
     const float *v_scale = nullptr;
     int scale_stride = 0;
+    // nullptr: query row b reads cache sequence b.  Else [B] cache sequence of each query row (prefill over
+    // fp32 / INT8 caches runs every token of a chunk as one decode row at its own pos)
+    const int *row_seq = nullptr;
 };
 
 // Fused per-token mixer bodies (mixer_fused.cu).
@@ -233,6 +239,8 @@ cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, cons
 size_t decode_workspace_bytes(const DecodeArgs &a, int sm_count);
 // The split launch_attend_decode would use: key chunks per (sequence, kv head), keys per chunk, scratch bytes.
 void decode_plan(const DecodeArgs &a, int sm_count, int *nchunk, int *chunk_keys, size_t *ws_bytes);
+// Query rows of a prefill chunk as decode rows: row i = token i % n_tok of sequence i / n_tok at start_pos + i % n_tok.
+cudaError_t launch_prefill_rows(cudaStream_t st, int *row_seq, int *pos, int batch, int n_tok, int start_pos);
 // Bytes of the fixed scratch array of eif_cuda_attend_decode_noalloc_dev (noalloc.cu).
 size_t noalloc_scratch_capacity();
 cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws, size_t ws_bytes, int sm_count,

@@ -88,6 +88,10 @@ def lib() -> ctypes.CDLL:
                                              ctypes.POINTER(ctypes.c_size_t)]),
         "eif_cuda_fullatt_decode": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _F, _I, _P, _P]),
         "eif_cuda_fullatt_decode_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _I, _F, _I, _P, _P]),
+        "eif_cuda_fullatt_prefill": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _F, _I, _P, _P]),
+        "eif_cuda_fullatt_prefill_dev": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _F, _I, _P, _P]),
+        "eif_cuda_prefill_step": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _F, _P]),
+        "eif_cuda_prefill_step_dev": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _F, _P]),
         "eif_cuda_attend_prefill": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P]),
         "eif_cuda_attend_prefill_dev": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P]),
         "eif_cuda_attend_prefill_gated": (_I, [_P, _P, _I, _P, _I, _I, _I, _F, _P, _I, _P, _P]),
@@ -438,6 +442,36 @@ class KVCache:
                                                      _ptr(pp), n_heads, float(scale), int(subln), _ptr(nn), _ptr(o)),
                        "fullatt_decode")
         return o
+
+    def fullatt_prefill(self, layer: int, qg, k, v, n_tok: int, start_pos: int, n_heads: int, scale: float,
+                        subln: int = SUBLN_NONE, sub_norm=None):
+        """The Qwen3.5 attention block of a prefill chunk (fullatt_prep + gated causal attention), host arrays."""
+        qq, kk, vv = _f32(qg), _f32(k), _f32(v)
+        nn = _f32(sub_norm) if sub_norm is not None else None
+        o = np.zeros((self.batch, n_tok, n_heads * self.head_dim), np.float32)
+        self.ctx.check(lib().eif_cuda_fullatt_prefill(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv),
+                                                      n_tok, start_pos, n_heads, float(scale), int(subln), _ptr(nn),
+                                                      _ptr(o)), "fullatt_prefill")
+        return o
+
+    def fullatt_prefill_dev(self, layer: int, qg_dev, k_dev, v_dev, n_tok: int, start_pos: int, n_heads: int,
+                            scale: float, out_dev, subln: int = SUBLN_NONE, sub_norm_dev=None):
+        self.ctx.check(lib().eif_cuda_fullatt_prefill_dev(self.ctx.handle, self._h, layer, qg_dev, k_dev, v_dev, n_tok,
+                                                          start_pos, n_heads, float(scale), int(subln), sub_norm_dev,
+                                                          out_dev), "fullatt_prefill_dev")
+
+    def prefill_step(self, layer: int, q, k, v, n_tok: int, start_pos: int, n_heads: int, scale: float):
+        """The tinyllm attention block of a prefill chunk (RoPE, cache writes, causal attention), host arrays."""
+        qq, kk, vv = _f32(q), _f32(k), _f32(v)
+        o = np.zeros((self.batch, n_tok, n_heads * self.head_dim), np.float32)
+        self.ctx.check(lib().eif_cuda_prefill_step(self.ctx.handle, self._h, layer, _ptr(qq), _ptr(kk), _ptr(vv), n_tok,
+                                                   start_pos, n_heads, float(scale), _ptr(o)), "prefill_step")
+        return o
+
+    def prefill_step_dev(self, layer: int, q_dev, k_dev, v_dev, n_tok: int, start_pos: int, n_heads: int,
+                         scale: float, out_dev):
+        self.ctx.check(lib().eif_cuda_prefill_step_dev(self.ctx.handle, self._h, layer, q_dev, k_dev, v_dev, n_tok,
+                                                       start_pos, n_heads, float(scale), out_dev), "prefill_step_dev")
 
     def fullatt_decode_dev(self, layer: int, qg_dev, k_dev, v_dev, pos_dev, max_pos: int, n_heads: int,
                            scale: float, out_dev, subln: int = SUBLN_NONE, sub_norm_dev=None):

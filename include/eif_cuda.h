@@ -159,8 +159,8 @@ eif_status_t eif_cuda_rope_append_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, in
 /* The same for a prefill chunk: token i of every sequence at position start_pos + i (the per-token tables of
  * the batched prefill, src/eif_tinyllm.c:994-1006).
  *   q, q_out [batch][n_tok][n_heads*head_dim]; k, v [batch][n_tok][n_kv_heads*head_dim]
- * _dev: q_out as bf16 (the input of eif_cuda_attend_prefill_dev), the rest fp32 device arrays, asynchronous.
- * Host variant: fp32 host arrays. */
+ * _dev: q_out in the input type of eif_cuda_attend_prefill_dev for this cache (bf16 for a bf16 cache, fp32 for
+ * fp32 and INT8 caches), the rest fp32 device arrays, asynchronous.  Host variant: fp32 host arrays. */
 eif_status_t eif_cuda_rope_append_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
                                           const float *k, const float *v, int n_tok, int start_pos, int n_heads,
                                           float *q_out);
@@ -222,10 +222,13 @@ eif_status_t eif_cuda_attend_decode_plan(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv,
  * token i attending to cache rows 0 .. start_pos+i.  Replaces the batched prefill attention of
  * tinyllm_forward_batch_embeddings (src/eif_tinyllm.c:1158-1268) and the per-token fullatt_attend of
  * Qwen3.5's prefill_chunk (src/eif_qwen35.c:1122-1133, without gate / SubLN).  The chunk's k / v rows must
- * already be in the cache (kv_upload, kv_append).  Needs a bf16 cache with head_dim 64, 128 or 256.
+ * already be in the cache (kv_upload, kv_append, rope_append_prefill).  head_dim 64, 128 or 256.
  *   q   [batch][n_tok][n_heads*head_dim], out the same shape
- * _dev: bf16 device arrays (16-byte aligned), asynchronous.  Host variant: fp32 host arrays (rounded to
- * bf16 on the device, the output widened back).
+ * A bf16 cache runs the tensor-core causal kernels: _dev takes bf16 device arrays (16-byte aligned) and the
+ * host variant rounds q to bf16 on the device and widens the output back.  An fp32 or INT8 cache (tinyllm's
+ * kv_type 1, read as src/eif_tinyllm.c:1172-1235 reads it) runs every token as one decode row at its own
+ * position, in fp32 arithmetic over the cache's own values: _dev takes fp32 device arrays.
+ * _dev calls are asynchronous; the host variant takes fp32 host arrays.
  * ------------------------------------------------------------------------------------------- */
 eif_status_t eif_cuda_attend_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q, int n_tok,
                                      int start_pos, int n_heads, float scale, float *out);
@@ -237,8 +240,8 @@ eif_status_t eif_cuda_attend_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv,
  * output gate and SubLN of eif_cuda_attend_decode (out = SubLN(o * sigmoid(gate))).
  *   gate  NULL, or [batch][n_tok][n_heads*head_dim] fp32; sub_norm [n_heads*head_dim] for EIF_CUDA_SUBLN_WEIGHT
  *   out   [batch][n_tok][n_heads*head_dim] fp32
- * _dev: q bf16 (16-byte aligned), gate / sub_norm / out fp32 device arrays, asynchronous.  Host variant: fp32
- * host arrays. */
+ * _dev: q bf16 (16-byte aligned) for a bf16 cache, fp32 for an fp32 cache; gate / sub_norm / out fp32 device
+ * arrays, asynchronous.  Host variant: fp32 host arrays. */
 eif_status_t eif_cuda_attend_prefill_gated(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q,
                                            int n_tok, int start_pos, int n_heads, float scale, const float *gate,
                                            eif_cuda_subln_t subln, const float *sub_norm, float *out);
@@ -360,8 +363,8 @@ eif_status_t eif_cuda_fullatt_prep_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, i
  * fullatt_prep calls of prefill_chunk, src/eif_qwen35.c:1122-1133), one launch.
  *   qg [batch][n_tok][n_heads*2*head_dim], k, v [batch][n_tok][n_kv_heads*head_dim];
  *   q_out, gate_out [batch][n_tok][n_heads*head_dim]
- * _dev: q_out as bf16 (the input of eif_cuda_attend_prefill_gated_dev), the rest fp32 device arrays,
- * asynchronous.  Host variant: fp32 host arrays. */
+ * _dev: q_out in the input type of eif_cuda_attend_prefill_gated_dev for this cache (bf16 for a bf16 cache, fp32
+ * for an fp32 cache), the rest fp32 device arrays, asynchronous.  Host variant: fp32 host arrays. */
 eif_status_t eif_cuda_fullatt_prep_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg,
                                            const float *k, const float *v, int n_tok, int start_pos, int n_heads,
                                            float *q_out, float *gate_out);
@@ -383,6 +386,32 @@ eif_status_t eif_cuda_fullatt_decode_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv,
                                          const float *k_dev, const float *v_dev, const int *pos_dev, int max_pos,
                                          int n_heads, float scale, eif_cuda_subln_t subln, const float *sub_norm_dev,
                                          float *out_dev);
+
+/* The whole Qwen3.5 attention block of a prefill chunk in one call: fullatt_prep of every token, then the gated
+ * causal attention -- prefill_chunk's attention layer (src/eif_qwen35.c:1118-1133) -- i.e.
+ * eif_cuda_fullatt_prep_prefill followed by eif_cuda_attend_prefill_gated with q and the gate kept on the device.
+ *   qg [batch][n_tok][n_heads*2*head_dim], k, v [batch][n_tok][n_kv*head_dim], out [batch][n_tok][n_heads*head_dim]
+ * A bf16 cache runs the tensor-core prefill (bf16 q, the prefill tolerance); an fp32 cache the exact per-token
+ * path.  _dev: fp32 device arrays, asynchronous.  Host variant: fp32 host arrays. */
+eif_status_t eif_cuda_fullatt_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg,
+                                      const float *k, const float *v, int n_tok, int start_pos, int n_heads,
+                                      float scale, eif_cuda_subln_t subln, const float *sub_norm, float *out);
+eif_status_t eif_cuda_fullatt_prefill_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *qg_dev,
+                                          const float *k_dev, const float *v_dev, int n_tok, int start_pos,
+                                          int n_heads, float scale, eif_cuda_subln_t subln, const float *sub_norm_dev,
+                                          float *out_dev);
+
+/* The whole tinyllm attention block of a prefill chunk in one call: RoPE of the chunk's q and k and the (plain or
+ * quantised) cache writes, then causal attention -- tinyllm_forward_batch_embeddings for one layer
+ * (src/eif_tinyllm.c:1086-1268) -- i.e. eif_cuda_rope_append_prefill then eif_cuda_attend_prefill with the
+ * rotated queries kept on the device.  Needs eif_cuda_kv_set_rope.
+ *   q [batch][n_tok][n_heads*head_dim], k, v [batch][n_tok][n_kv*head_dim] (un-rotated), out like q
+ * _dev: fp32 device arrays, asynchronous.  Host variant: fp32 host arrays. */
+eif_status_t eif_cuda_prefill_step(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q, const float *k,
+                                   const float *v, int n_tok, int start_pos, int n_heads, float scale, float *out);
+eif_status_t eif_cuda_prefill_step_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_dev,
+                                       const float *k_dev, const float *v_dev, int n_tok, int start_pos, int n_heads,
+                                       float scale, float *out_dev);
 
 #ifdef __cplusplus
 }

@@ -109,16 +109,54 @@ def test_decode_vs_oracle(pkg, ctx, orc, monkeypatch, simt, nh, nkv, hd, T):
 
 
 def test_int8_rejections(pkg, ctx):
-    """INT8 caches: head_dim 64/128/256 only; no prefill attention or Qwen3.5 prep over them; the raw download
+    """INT8 caches: head_dim 64/128/256 only; no Qwen3.5 prep over them (its cache is fp32); the raw download
     needs an INT8 cache."""
     with pytest.raises(pkg.EifCudaError) as e:
         pkg.KVCache(ctx, 1, 1, 8, 2, 96, pkg.INT8)
     assert e.value.name == "NOT_SUPPORTED"
     kv = pkg.KVCache(ctx, 1, 1, 64, 2, 64, pkg.INT8)
+    kv.set_norms(0, np.ones(64, np.float32), np.ones(64, np.float32))
     with pytest.raises(pkg.EifCudaError) as e:
-        kv.attend_prefill(0, np.zeros((1, 8, 4 * 64), np.float32), 8, 0, 4, 0.125)
+        kv.fullatt_prep(0, np.zeros((1, 4 * 128), np.float32), np.zeros((1, 128), np.float32),
+                        np.zeros((1, 128), np.float32), np.array([0]), 4)
     assert e.value.name == "NOT_SUPPORTED"
     f32 = pkg.KVCache(ctx, 1, 1, 8, 2, 64, pkg.F32)
     with pytest.raises(pkg.EifCudaError) as e:
         f32.download_int8(0, 0, 0, 1)
     assert e.value.name == "INVALID_ARGUMENT"
+
+
+@pytest.mark.parametrize("hd,nh,nkv", [(64, 14, 2), (128, 8, 2), (256, 8, 2)])
+def test_int8_prefill_chain(pkg, ctx, orc, hd, nh, nkv):
+    """The batched prefill over an INT8 cache (src/eif_tinyllm.c:1158-1268 with kv_type 1, :1172-1235): a chunk's
+    RoPE and quantised cache writes (rope_append_prefill: codes and scales bit-identical to per-token
+    rope_append), then causal attention of every chunk token over the codes and scales, against the
+    restatement of the INT8 loop token by token (rel-L2 <= 1e-5); a second chunk continues at start_pos > 0."""
+    rng = np.random.default_rng(hd + nh)
+    B, T = 2, 300
+    kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, pkg.INT8)
+    kv.set_rope(1e6)
+    one = pkg.KVCache(ctx, 1, B, T, nkv, hd, pkg.INT8)  # the same rows written one token at a time
+    one.set_rope(1e6)
+    scale = 1.0 / np.sqrt(hd)
+    start = 0
+    for n_tok in (130, 67):
+        q = rng.standard_normal((B, n_tok, nh * hd)).astype(np.float32)
+        k = rng.standard_normal((B, n_tok, nkv * hd)).astype(np.float32)
+        v = rng.standard_normal((B, n_tok, nkv * hd)).astype(np.float32)
+        qr = kv.rope_append_prefill(0, q, k, v, n_tok, start, nh)
+        for t in range(n_tok):
+            pos = np.full(B, start + t, np.int32)
+            qt = one.rope_append(0, q[:, t], k[:, t], v[:, t], pos, nh)
+            assert np.array_equal(qt, qr[:, t]), t
+        out = kv.attend_prefill(0, qr, n_tok, start, nh, scale)
+        for b in range(B):
+            got = kv.download_int8(0, b, 0, start + n_tok)
+            want = one.download_int8(0, b, 0, start + n_tok)
+            for g_, w_ in zip(got, want):
+                assert np.array_equal(g_, w_)
+            kc, vc, ks, vs = got
+            for t in range(n_tok):
+                ref = orc.attend_decode_i8(qr[b, t], kc, ks, vc, vs, start + t, nh, nkv, hd, scale)
+                assert rel_l2(out[b, t], ref) <= TOL, (b, t)
+        start += n_tok

@@ -261,6 +261,50 @@ def test_qwen35_attention_prefill_chain(pkg, ctx, orc):
         assert rel_l2(out[b], ref) <= 1e-2 and np.max(np.abs(out[b] - ref)) <= 2e-2
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_fullatt_prefill_one_call(pkg, ctx, orc, dtype):
+    """eif_cuda_fullatt_prefill (the chunk's fullatt_prep and the gated causal attention in one call) against
+    fullatt_prep_prefill + attend_prefill_gated on a second cache; over the reference's own fp32 cache, also
+    against fullatt_prep + fullatt_attend token by token at the fp32 tolerance (rel-L2 <= 1e-5)."""
+    rng = np.random.default_rng(92)
+    dt = pkg.F32 if dtype == "f32" else pkg.BF16
+    B, nh, nkv, hd, start, n = 2, 8, 2, 256, 20, 70
+    T = start + n + 4
+    qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    sub = (1 + 0.1 * rng.standard_normal(nh * hd)).astype(np.float32)
+    k0 = rng.standard_normal((B, start, nkv * hd)).astype(np.float32)
+    v0 = rng.standard_normal((B, start, nkv * hd)).astype(np.float32)
+    kvs = []
+    for _ in range(2):
+        kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, dt)
+        kv.set_norms(0, qn, kn)
+        for b in range(B):
+            kv.upload(0, b, 0, k0[b], v0[b])
+        kvs.append(kv)
+    qg = rng.standard_normal((B, n, nh * 2 * hd)).astype(np.float32)
+    k = rng.standard_normal((B, n, nkv * hd)).astype(np.float32)
+    v = rng.standard_normal((B, n, nkv * hd)).astype(np.float32)
+    q, g = kvs[0].fullatt_prep_prefill(0, qg, k, v, n, start, nh)
+    two = kvs[0].attend_prefill_gated(0, q, n, start, nh, 1.0 / 16, g, pkg.SUBLN_WEIGHT, sub)
+    one = kvs[1].fullatt_prefill(0, qg, k, v, n, start, nh, 1.0 / 16, subln=pkg.SUBLN_WEIGHT, sub_norm=sub)
+    for b in range(B):
+        for a_, b_ in zip(kvs[0].download(0, b, 0, T), kvs[1].download(0, b, 0, T)):
+            assert np.array_equal(a_, b_)
+        assert rel_l2(one[b], two[b]) <= (1e-5 if dt == pkg.F32 else 1e-2)
+    if dt == pkg.F32:
+        for b in range(B):
+            kc = np.zeros((T, nkv * hd), np.float32)
+            vc = np.zeros_like(kc)
+            kc[:start], vc[:start] = k0[b], v0[b]
+            for i in range(n):
+                rq, rg, _ = orc.fullatt_prep(qg[b, i], k[b, i], v[b, i], qn, kn, kc, vc, start + i, nh, nkv, hd)
+                ref = orc.subln(orc.attend_decode(rq, kc, vc, start + i, nh, nkv, hd, 1.0 / 16, gate=rg), sub, 2)
+                assert rel_l2(one[b, i], ref) <= 1e-5, (b, i)
+    for kv in kvs:
+        kv.free()
+
+
 def test_deltanet_core_host_matches_dev(pkg, ctx):
     """A host-pointer deltanet_core at a serving batch (160 sequences, 5.3 MB of inputs per call) against the
     device-pointer call on a twin state: the same bits, outputs and states."""

@@ -105,9 +105,9 @@ def test_prefill_gated_vs_oracle(pkg, ctx, orc, subln, hd, nh, nkv):
 
 
 def test_prefill_bad_arguments(pkg, ctx):
-    kv32 = pkg.KVCache(ctx, 1, 1, 64, 2, 128, pkg.F32)
+    kv96 = pkg.KVCache(ctx, 1, 1, 64, 2, 96, pkg.F32)  # head_dim outside 64 / 128 / 256
     with pytest.raises(pkg.EifCudaError) as e:
-        kv32.attend_prefill(0, np.zeros((1, 4, 256), np.float32), 4, 0, 2, 0.1)
+        kv96.attend_prefill(0, np.zeros((1, 4, 192), np.float32), 4, 0, 2, 0.1)
     assert e.value.name == "NOT_SUPPORTED"
     kv = pkg.KVCache(ctx, 1, 1, 64, 2, 128, pkg.BF16)
     with pytest.raises(pkg.EifCudaError) as e:
@@ -116,3 +116,38 @@ def test_prefill_bad_arguments(pkg, ctx):
     with pytest.raises(pkg.EifCudaError) as e:
         kv.attend_prefill(0, np.zeros((1, 8, 384), np.float32), 8, 0, 3, 0.1)
     assert e.value.name == "SHAPE_MISMATCH"
+
+
+@pytest.mark.parametrize("hd,nh,nkv", [(64, 14, 2), (128, 12, 2), (256, 8, 2)])
+def test_prefill_fp32_cache(pkg, ctx, orc, hd, nh, nkv):
+    """The reference's own cache type (fp32): every chunk token is one decode row at its own position, in fp32
+    arithmetic -- the fp32 tolerance (rel-L2 <= 1e-5) against the restatement of the prefill loop; host and
+    device-pointer entries, plain and gated (Qwen3.5's prefill_chunk path, src/eif_qwen35.c:1122-1133)."""
+    import torch
+    rng = np.random.default_rng(hd + 3 * nh)
+    B, start, n_tok = 2, 77, 150
+    rows = start + n_tok
+    kv = pkg.KVCache(ctx, 1, B, rows + 3, nkv, hd, pkg.F32)
+    kc = rng.standard_normal((B, rows, nkv * hd)).astype(np.float32)
+    vc = rng.standard_normal((B, rows, nkv * hd)).astype(np.float32)
+    for b in range(B):
+        kv.upload(0, b, 0, kc[b], vc[b])
+    q = rng.standard_normal((B, n_tok, nh * hd)).astype(np.float32)
+    gate = rng.standard_normal((B, n_tok, nh * hd)).astype(np.float32)
+    sub = (1 + 0.1 * rng.standard_normal(nh * hd)).astype(np.float32)
+    scale = 1.0 / np.sqrt(hd)
+    out = kv.attend_prefill(0, q, n_tok, start, nh, scale)
+    outg = kv.attend_prefill_gated(0, q, n_tok, start, nh, scale, gate=gate, subln=pkg.SUBLN_WEIGHT, sub_norm=sub)
+    qd, od = torch.from_numpy(q).cuda(), torch.zeros((B, n_tok, nh * hd), device="cuda")
+    torch.cuda.synchronize()
+    kv.attend_prefill_dev(0, qd.data_ptr(), n_tok, start, nh, scale, od.data_ptr())
+    ctx.synchronize()
+    outd = od.cpu().numpy()
+    for b in range(B):
+        ref = orc.attend_prefill(q[b], kc[b], vc[b], n_tok, start, nh, nkv, hd, scale)
+        assert rel_l2(out[b], ref) <= 1e-5 and rel_l2(outd[b], ref) <= 1e-5, b
+        for t in (0, 1, n_tok // 2, n_tok - 1):
+            rg = orc.subln(orc.attend_decode(q[b, t], kc[b], vc[b], start + t, nh, nkv, hd, scale, gate=gate[b, t]),
+                           sub, 2)
+            assert rel_l2(outg[b, t], rg) <= 1e-5, (b, t)
+    kv.free()

@@ -91,6 +91,50 @@ def test_rope_append_prefill_then_attention(pkg, ctx, orc):
         assert rel_l2(out[b], ref) <= 1e-2 and np.max(np.abs(out[b] - ref)) <= 2e-2
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "int8"])
+def test_prefill_step_one_call(pkg, ctx, orc, dtype):
+    """eif_cuda_prefill_step (RoPE, cache writes and causal attention of a chunk in one call) against the two
+    calls rope_append_prefill + attend_prefill on a second cache: the same cache rows, and the same attention
+    (fp32 / INT8 caches: rel-L2 <= 1e-5 and the fp32 cache also against the restatement; bf16: the prefill
+    tolerance, the two-call host path rounds its output to bf16)."""
+    rng = np.random.default_rng(17)
+    dt = {"f32": pkg.F32, "bf16": pkg.BF16, "int8": pkg.INT8}[dtype]
+    B, nh, nkv, hd, theta, start, n = 2, 14, 2, 64, 1e6, 40, 90
+    T = start + n + 2
+    kvs = []
+    for _ in range(2):
+        kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, dt)
+        kv.set_rope(theta, False)
+        kvs.append(kv)
+    k0 = rng.standard_normal((B, start, nkv * hd)).astype(np.float32)
+    v0 = rng.standard_normal((B, start, nkv * hd)).astype(np.float32)
+    for kv in kvs:
+        for b in range(B):
+            kv.upload(0, b, 0, k0[b], v0[b])
+    q = rng.standard_normal((B, n, nh * hd)).astype(np.float32)
+    k = rng.standard_normal((B, n, nkv * hd)).astype(np.float32)
+    v = rng.standard_normal((B, n, nkv * hd)).astype(np.float32)
+    qr = kvs[0].rope_append_prefill(0, q, k, v, n, start, nh)
+    two = kvs[0].attend_prefill(0, qr, n, start, nh, 1.0 / 8)
+    one = kvs[1].prefill_step(0, q, k, v, n, start, nh, 1.0 / 8)
+    for b in range(B):
+        if dt == pkg.INT8:
+            for a_, b_ in zip(kvs[0].download_int8(0, b, 0, T), kvs[1].download_int8(0, b, 0, T)):
+                assert np.array_equal(a_, b_)
+        else:
+            for a_, b_ in zip(kvs[0].download(0, b, 0, T), kvs[1].download(0, b, 0, T)):
+                assert np.array_equal(a_, b_)
+        if dt == pkg.BF16:
+            assert rel_l2(one[b], two[b]) <= 1e-2
+        else:
+            assert rel_l2(one[b], two[b]) <= 1e-5
+        if dt == pkg.F32:
+            kd, vd = kvs[1].download(0, b, 0, start + n)
+            assert rel_l2(one[b], orc.attend_prefill(qr[b], kd, vd, n, start, nh, nkv, hd, 1.0 / 8)) <= 1e-5
+    for kv in kvs:
+        kv.free()
+
+
 def test_rope_needs_table(pkg, ctx):
     kv = pkg.KVCache(ctx, 1, 1, 8, 2, 64, pkg.F32)
     with pytest.raises(pkg.EifCudaError) as e:
