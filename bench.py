@@ -915,12 +915,14 @@ def run_recurrent(args, torch, dist, rank, world, local_rank):
 DC_HQ, DC_HKV, DC_D, DC_THETA = 14, 2, 64, 1e6  # BASELINE configs[0]'s heads (Qwen2.5-0.5B), NeoX RoPE
 DC_B, DC_CTX = 256, 4096  # the batched variant; configs[0] itself is --batch 1 --ctx 512 --kv f32
 KV_ELT = {"f32": 4, "bf16": 2, "int8": 1}
+# --heads qwen35: the Qwen3.5 full-attention shape (8 q / 2 kv heads, head_dim 256), one attention mixer per step
+Q5_HQ, Q5_HKV, Q5_D = AT_HQ, AT_HKV, AT_D
 
 
-def decode_bytes(B, L, hkv, kv):
+def decode_bytes(B, L, hkv, kv, D=DC_D):
     """Algorithmic bytes of one decode-attention launch: K and V rows [0, L) of every (sequence, kv head),
     plus the per-(row, kv head) K and V scales of an INT8 cache (q and out are < 0.1 %)."""
-    b = 2.0 * B * hkv * L * DC_D * KV_ELT[kv]
+    b = 2.0 * B * hkv * L * D * KV_ELT[kv]
     if kv == "int8":
         b += 2.0 * B * hkv * L * 4
     return b
@@ -982,15 +984,20 @@ def run_decode(args, torch, dist, rank, world, local_rank):
     theta 1e6), batched: one decode step of one attention layer for `--batch` sequences at context `--ctx`
     over an fp32, bf16 or INT8 (`--kv`) cache -- eif_cuda_decode_step: RoPE of the new q and k, the (plain or
     quantised) cache write and attention over rows [0, ctx) in one call.  The roofline times the attention
-    alone (attend_decode_dev on the same rows)."""
+    alone (attend_decode_dev on the same rows).
+    `--heads qwen35`: the Qwen3.5 full-attention shape (8 q / 2 kv heads, head_dim 256, fp32 or bf16 cache) and
+    its whole attention mixer per step -- eif_cuda_fullatt_decode_dev: q / k norms, partial RoPE, the cache
+    write, attention with the sigmoid gate and SubLN."""
     import __graft_entry__
     pkg = __graft_entry__.load_package()
     torch.cuda.set_device(local_rank)
     kv_name = args.kv
+    q35 = getattr(args, "heads", "qwen2") == "qwen35"
+    HQ, HKV, D = (Q5_HQ, Q5_HKV, Q5_D) if q35 else (DC_HQ, DC_HKV, DC_D)
     GB, L = args.batch or DC_B, args.ctx or DC_CTX
-    sh = pkg.shard.shard(GB, DC_HKV, world, rank)  # (sequence, kv group) units
+    sh = pkg.shard.shard(GB, HKV, world, rank)  # (sequence, kv group) units
     B, hkv = sh.nb, sh.nh
-    hq = hkv * (DC_HQ // DC_HKV)
+    hq = hkv * (HQ // HKV)
     ctx = pkg.Context(local_rank)
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -999,9 +1006,13 @@ def run_decode(args, torch, dist, rank, world, local_rank):
     gen = torch.Generator(device=dev)
     gen.manual_seed(21 + rank)
     dt = {"f32": pkg.F32, "bf16": pkg.BF16, "int8": pkg.INT8}[kv_name]
-    kv = pkg.KVCache(ctx, 1, B, L, hkv, DC_D, dt)
+    kv = pkg.KVCache(ctx, 1, B, L, hkv, D, dt)
     kv.set_rope(DC_THETA)
-    n_el = B * L * hkv * DC_D
+    if q35:
+        w = Weights().at[0]
+        kv.set_norms(0, w["q_norm"], w["k_norm"])
+        sub = torch.from_numpy(w["sub_norm"][:hq * D]).to(dev)
+    n_el = B * L * hkv * D
     for p in kv.layer_ptrs(0):  # cache ~ N(0,1) (fp32 / bf16) or uniform codes with scales ~ U(0.005, 0.03)
         if kv_name == "f32":
             torch.as_tensor(CudaArray(p, (n_el,), "<f4"), device=dev).normal_(generator=gen)
@@ -1014,24 +1025,37 @@ def run_decode(args, torch, dist, rank, world, local_rank):
         for p in kv.layer_scales(0):
             torch.as_tensor(CudaArray(p, (B * hkv * ((L + 63) // 64 * 64),), "<f4"), device=dev).uniform_(
                 0.005, 0.03, generator=gen)
-    q = torch.randn(B, hq * DC_D, device=dev, generator=gen)
-    k = torch.randn(B, hkv * DC_D, device=dev, generator=gen)
-    v = torch.randn(B, hkv * DC_D, device=dev, generator=gen)
+    q = torch.randn(B, hq * D * (2 if q35 else 1), device=dev, generator=gen)  # Qwen3.5: [q | gate] per head
+    k = torch.randn(B, hkv * D, device=dev, generator=gen)
+    v = torch.randn(B, hkv * D, device=dev, generator=gen)
     pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
-    q_rot = torch.empty_like(q)
-    out = torch.empty_like(q)
-    scale = 1.0 / math.sqrt(DC_D)
-    bytes_alg = decode_bytes(B, L, hkv, kv_name)
+    q_rot = torch.empty(B, hq * D, device=dev)
+    gate = torch.empty(B, hq * D, device=dev)
+    out = torch.empty(B, hq * D, device=dev)
+    scale = 1.0 / math.sqrt(D)
+    bytes_alg = decode_bytes(B, L, hkv, kv_name, D)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if bytes_alg < (1 << 30) else None
 
     def step():
-        kv.decode_step_dev(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), L - 1, hq, scale,
-                           out.data_ptr())
+        if q35:
+            kv.fullatt_decode_dev(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), L - 1, hq, scale,
+                                  out.data_ptr(), subln=pkg.SUBLN_WEIGHT, sub_norm_dev=sub.data_ptr())
+        else:
+            kv.decode_step_dev(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), L - 1, hq, scale,
+                               out.data_ptr())
 
     def attend():
-        kv.attend_decode_dev(0, q_rot.data_ptr(), pos.data_ptr(), L - 1, hq, scale, out.data_ptr())
+        if q35:
+            kv.attend_decode_dev(0, q_rot.data_ptr(), pos.data_ptr(), L - 1, hq, scale, out.data_ptr(),
+                                 gate_dev=gate.data_ptr(), subln=pkg.SUBLN_WEIGHT, sub_norm_dev=sub.data_ptr())
+        else:
+            kv.attend_decode_dev(0, q_rot.data_ptr(), pos.data_ptr(), L - 1, hq, scale, out.data_ptr())
 
-    kv.rope_append_dev(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), hq, q_rot.data_ptr())
+    if q35:
+        kv.fullatt_prep_dev(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), hq, q_rot.data_ptr(),
+                            gate.data_ptr())
+    else:
+        kv.rope_append_dev(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), hq, q_rot.data_ptr())
     for _ in range(args.warmup):
         step()
         attend()
@@ -1065,20 +1089,27 @@ def run_decode(args, torch, dist, rank, world, local_rank):
     ms = pkg.shard.max_over_ranks(dist, ms, "cuda")
     # e2e through the host-pointer ABI: pinned fp32 q / k / v / pos in, the output back
     hg = torch.Generator().manual_seed(5)
-    qh = torch.randn(B, hq * DC_D, generator=hg).pin_memory().numpy()
-    kh = torch.randn(B, hkv * DC_D, generator=hg).pin_memory().numpy()
-    vh = torch.randn(B, hkv * DC_D, generator=hg).pin_memory().numpy()
+    qh = torch.randn(B, hq * D * (2 if q35 else 1), generator=hg).pin_memory().numpy()
+    kh = torch.randn(B, hkv * D, generator=hg).pin_memory().numpy()
+    vh = torch.randn(B, hkv * D, generator=hg).pin_memory().numpy()
+    subh = sub.cpu().pin_memory().numpy() if q35 else None
     ph = torch.full((B,), L - 1, dtype=torch.int32).pin_memory().numpy()
-    oh = torch.empty(B, hq * DC_D).pin_memory().numpy()
+    oh = torch.empty(B, hq * D).pin_memory().numpy()
+
+    def e2e_call():
+        if q35:
+            kv.fullatt_decode(0, qh, kh, vh, ph, hq, scale, subln=pkg.SUBLN_WEIGHT, sub_norm=subh, out=oh)
+        else:
+            kv.decode_step(0, qh, kh, vh, ph, hq, scale, out=oh)
     e2e_ms = None
     if not args.no_e2e:
         ctx.set_stream(None)
         n_e2e = max(3, args.steps) * (20 if bytes_alg < (64 << 20) else 1)  # short steps: enough of them to time
         for _ in range(3):
-            kv.decode_step(0, qh, kh, vh, ph, hq, scale, out=oh)
+            e2e_call()
         t0 = time.perf_counter()
         for _ in range(n_e2e):
-            kv.decode_step(0, qh, kh, vh, ph, hq, scale, out=oh)
+            e2e_call()
         e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / n_e2e, "cuda")
     if rank != 0:
         return None
@@ -1087,33 +1118,79 @@ def run_decode(args, torch, dist, rank, world, local_rank):
     dec_kernel = {"bf16": "attn_decode_tc", "int8": "attn_decode_i8"}.get(kv_name, "attn_decode_f32")
     h2d = (qh.nbytes + kh.nbytes + vh.nbytes + ph.nbytes) * world
     d2h = oh.nbytes * world
-    cfg_name = "BASELINE configs[0] exactly" if (GB, L, kv_name) == (1, 512, "f32") else \
-        "BASELINE configs[0]'s heads, batched"
-    line = {"metric": "tinyllm GQA decode tokens/s (one attention layer: RoPE + cache write + attention)",
+    cfg_name = "BASELINE configs[0] exactly" if (GB, L, kv_name, q35) == (1, 512, "f32", False) else \
+        "BASELINE configs[4]'s attention heads" if q35 else "BASELINE configs[0]'s heads, batched"
+    metric = ("Qwen3.5 attention mixer decode tokens/s (one layer: fullatt_prep + gated attention + SubLN)" if q35
+              else "tinyllm GQA decode tokens/s (one attention layer: RoPE + cache write + attention)")
+    line = {"metric": metric,
             "value": GB / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32 arithmetic over a " + kv_name + " cache", "data": "synthetic (seeded)",
-            "config": {"workload": f"tinyllm_decode ({cfg_name})", "global_batch": GB, "ctx": L,
-                       "heads": "14 q / 2 kv", "head_dim": DC_D, "kv_dtype": kv_name,
+            "config": {"workload": f"{'qwen35_attention' if q35 else 'tinyllm'}_decode ({cfg_name})",
+                       "global_batch": GB, "ctx": L, "heads": f"{HQ} q / {HKV} kv", "head_dim": D,
+                       "kv_dtype": kv_name,
                        "l2": "256 MiB flush between steps" if flush is not None else "cache > L2",
                        "parallelism": f"(sequence, kv group) units over {world} rank(s), no collective"},
             "e2e": None if e2e_ms is None else {
                 "value": GB / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "path": "host-pointer C ABI eif_cuda_decode_step (pinned)"},
-            "step_path": "one launch (attn_decode_step_kernel, a cluster per (sequence, kv head))"
+                "path": "host-pointer C ABI " + ("eif_cuda_fullatt_decode" if q35 else "eif_cuda_decode_step") +
+                        " (pinned)"},
+            "step_path": "fullatt_prep + split-K decode + combine" if q35 else
+                         "one launch (attn_decode_step_kernel, a cluster per (sequence, kv head))"
                          if launches == args.steps else "rope_append_kernel + split-K decode + combine",
             "roofline": {"kernel": dec_kernel + "_kernel + combine", "bound": "hbm", "achieved": ach,
                          "peak": hbm,
                          "unit": "GB/s", "frac": ach / hbm, "peak_source": src,
                          "algorithmic_bytes_per_launch": bytes_alg, "attention_ms": att_ms,
-                         "traffic": traffic(dec_kernel, bytes_alg)[0] if GB > 1 else None,
-                         "traffic_source": traffic(dec_kernel, bytes_alg)[1] if GB > 1 else None},
+                         "traffic": traffic(dec_kernel, bytes_alg)[0] if GB > 1 and not q35 else None,
+                         "traffic_source": traffic(dec_kernel, bytes_alg)[1] if GB > 1 and not q35 else None},
             "gpu_launches": launches, "clocks": clk}
     if world == 1 and not args.no_cpu_baseline:
-        tps, cores, kind, sample = cpu_decode_reference(kv_name, L)
+        tps, cores, kind, sample = cpu_qwen35_attention_reference(L) if q35 else cpu_decode_reference(kv_name, L)
         line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
     return line
+
+
+def cpu_qwen35_attention_reference(L, seconds=10.0):
+    """The reference's fullatt_prep + fullatt_attend (src/eif_qwen35.c:699-790) of one token at position L-1
+    over its fp32 cache (its only Qwen3.5 KV type), one sequence per host thread for the time budget."""
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as orc
+    ncpu = len(os.sched_getaffinity(0))
+    kind = "reference" if orc.ref_available() else "port"
+    lib = orc.ref() if kind == "reference" else None
+    if lib is not None:
+        lib.ref_set_threads(1)
+    w = Weights().at[0]
+    rng = np.random.default_rng(9)
+    qg = rng.standard_normal(Q5_HQ * 2 * Q5_D).astype(np.float32)
+    k = rng.standard_normal(Q5_HKV * Q5_D).astype(np.float32)
+    v = rng.standard_normal(Q5_HKV * Q5_D).astype(np.float32)
+    block = rng.standard_normal((min(L, 4096), Q5_HKV * Q5_D)).astype(np.float32)
+
+    def run(_):
+        kc = np.tile(block, ((L + len(block) - 1) // len(block), 1))[:L].copy()
+        vc = kc[::-1].copy()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            q, g, _ = orc.fullatt_prep(qg, k, v, w["q_norm"], w["k_norm"], kc, vc, L - 1, Q5_HQ, Q5_HKV, Q5_D, lib=lib)
+            if lib is not None:
+                orc.ref_fullatt_attend(q, g, kc, vc, w["sub_norm"], 0, L - 1, Q5_HQ, Q5_HKV, Q5_D)
+            else:
+                orc.subln(orc.attend_decode(q, kc, vc, L - 1, Q5_HQ, Q5_HKV, Q5_D, 1 / 16.0, gate=g), w["sub_norm"], 2)
+            n += 1
+        return n, time.perf_counter() - t0
+
+    pool = ThreadPoolExecutor(max_workers=ncpu)
+    res = list(pool.map(run, range(ncpu)))
+    pool.shutdown()
+    tokens = sum(n for n, _ in res)
+    el = max(t for _, t in res)
+    return tokens / el, ncpu, kind, (f"{tokens} tokens of fullatt_prep + fullatt_attend at ctx {L} (fp32 cache), one "
+                                     f"sequence per host thread, {el:.1f} s")
 
 
 WORKLOADS = [  # (key, workload, overrides): BASELINE configs[0..3] and config 1's heads batched per cache type
@@ -1124,6 +1201,9 @@ WORKLOADS = [  # (key, workload, overrides): BASELINE configs[0..3] and config 1
     ("decode_batched_f32", "decode", dict(batch=256, ctx=4096, kv="f32")),
     ("decode_batched_bf16", "decode", dict(batch=256, ctx=4096, kv="bf16")),
     ("decode_batched_int8", "decode", dict(batch=256, ctx=4096, kv="int8")),
+    # the Qwen3.5 attention mixer on the reference's own fp32 cache and on bf16 (config 5's heads)
+    ("qwen35_attention_f32", "decode", dict(batch=64, ctx=32768, kv="f32", heads="qwen35")),
+    ("qwen35_attention_bf16", "decode", dict(batch=64, ctx=32768, kv="bf16", heads="qwen35")),
 ]
 _KEEP = ("metric", "value", "unit", "ms_per_step", "dtype", "config", "roofline", "e2e", "cpu_baseline", "gpu_launches",
          "clocks", "step_path")
@@ -1138,6 +1218,7 @@ def run_workloads(args, torch, local_rank):
     for key, wl, over in WORKLOADS:
         a = argparse.Namespace(**vars(args))
         a.workload, a.batch, a.ctx, a.kv = wl, over.get("batch"), over.get("ctx"), over.get("kv", "f32")
+        a.heads = over.get("heads", "qwen2")
         fn = {"prefill": run_prefill, "chunked": run_chunked, "decode": run_decode, "recurrent": run_recurrent}[wl]
         line = fn(a, torch, None, 0, 1, local_rank)
         out[key] = {k: line[k] for k in _KEEP if k in line}
@@ -1155,6 +1236,9 @@ def main():
                          "int8, --ctx)")
     ap.add_argument("--kv", default="f32", choices=["f32", "bf16", "int8"], help="decode workload: cache dtype")
     ap.add_argument("--ctx", type=int, default=None, help="decode workload: context length (default 4096)")
+    ap.add_argument("--heads", default="qwen2", choices=["qwen2", "qwen35"],
+                    help="decode workload: 14 q / 2 kv heads at head_dim 64 (the tinyllm decode step), or the "
+                         "Qwen3.5 attention mixer at 8 q / 2 kv, head_dim 256")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)

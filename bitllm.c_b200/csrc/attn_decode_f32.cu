@@ -27,7 +27,6 @@
 
 namespace {
 
-constexpr int KT = 32;          // keys per tile (one consumer warp)
 constexpr int kSmemLimit = 227 * 1024;
 constexpr int HS = 8;           // head slots (G <= 8)
 
@@ -37,13 +36,16 @@ constexpr int HS = 8;           // head slots (G <= 8)
 // complete out of order).  Items are separated by the merge barrier.
 template <int D>
 struct F32Cfg {
+    // keys per tile (one consumer warp): 32, or 16 at head_dim 256, where a 32-key stage (64 KB) would leave
+    // room for too few stages; there the two half-warps take the two halves of every key's dims
+    static constexpr int KT = D == 256 ? 16 : 32;
     static constexpr int NW = 4;                     // consumer warps
     static constexpr int THREADS = 32 * (NW + 1);
-    static constexpr int BOX = KT * 128;              // 32 keys x 32 floats, 128-byte swizzle
+    static constexpr int BOX = KT * 128;              // KT keys x 32 floats, 128-byte swizzle
     static constexpr int TILE = (D / 32) * BOX;       // K (or V) tile bytes
     static constexpr int STAGE = 2 * TILE;
     static constexpr int EXTRA = NW * HS * D * 4      // per-warp query copies
-                                 + NW * KT * HS * 4   // per-warp probabilities
+                                 + NW * 32 * HS * 4   // per-warp probabilities
                                  + NW * HS * D * 4    // merge buffer o
                                  + 2 * NW * HS * 4    // merge m, l
                                  + 64 * 8             // barriers
@@ -70,7 +72,7 @@ struct ItemInfo {
     int b, cb, kvh, t_begin, t_end, ntiles;  // b: query row, cb: its cache sequence
 };
 
-__device__ __forceinline__ ItemInfo item_info(const F32Params &p, int item, bool report) {
+__device__ __forceinline__ ItemInfo item_info(const F32Params &p, int item, bool report, int KT) {
     ItemInfo it;
     const int unit = item / p.nchunk, c = item - unit * p.nchunk;
     it.b = unit / p.Hkv;
@@ -98,7 +100,7 @@ __device__ __forceinline__ float2 lds64(uint32_t a) {
     return v;
 }
 
-// Byte offset of floats [4c, 4c+4) of row `key` in one 32-key x 32-float box (128-byte swizzle: the 16-byte
+// Byte offset of floats [4c, 4c+4) of row `key` in one KT-key x 32-float box (128-byte swizzle: the 16-byte
 // chunk index XOR the row index mod 8).
 __device__ __forceinline__ uint32_t box_off(int key, int c) { return key * 128 + ((c ^ (key & 7)) << 4); }
 
@@ -107,8 +109,8 @@ __global__ void __launch_bounds__(F32Cfg<D>::THREADS, 1)
     attn_decode_f32_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            const F32Params p) {
     using C = F32Cfg<D>;
-    constexpr int NS = C::NS, DL = D / 32, NW = C::NW;
-    static_assert(DL == 2 || DL == 4, "head_dim 64 or 128");
+    constexpr int NS = C::NS, DL = D / 32, NW = C::NW, KT = C::KT;
+    static_assert(DL == 2 || DL == 4 || DL == 8, "head_dim 64, 128 or 256");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_align1024(smem_raw);
     float *sq = reinterpret_cast<float *>(smem + NS * C::STAGE);  // [NW][HS][D]
@@ -140,7 +142,7 @@ __global__ void __launch_bounds__(F32Cfg<D>::THREADS, 1)
         prefetch_tmap(&tmV);
         uint32_t it = 0;
         for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
-            const ItemInfo inf = item_info(p, item, false);
+            const ItemInfo inf = item_info(p, item, false, KT);
             for (int i = 0; i < inf.ntiles; ++i, ++it) {
                 const uint32_t s = it % NS, ph = (it / NS) & 1;
                 if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.dev_err)) return;
@@ -164,7 +166,7 @@ __global__ void __launch_bounds__(F32Cfg<D>::THREADS, 1)
     const uint32_t sqw_a = smem_u32(sqw), pww_a = smem_u32(pww);
     uint32_t it_base = 0, item_no = 0;
     for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++item_no) {
-        const ItemInfo inf = item_info(p, item, warp == 0 && lane == 0);
+        const ItemInfo inf = item_info(p, item, warp == 0 && lane == 0, KT);
         const float *qh = p.q + ((size_t)inf.b * p.Hq + (size_t)inf.kvh * G) * D;
         for (int i = lane; i < G * D; i += 32) sqw[i] = qh[i] * p.qscale;  // the G heads' rows, [h][D]
         __syncwarp();
@@ -186,18 +188,20 @@ __global__ void __launch_bounds__(F32Cfg<D>::THREADS, 1)
             if (!mbar_wait(full0 + 8 * s, ph, p.dev_err)) return;
             const uint32_t kbase = smem_u32(smem + s * C::STAGE), vbase = kbase + C::TILE;
 
-            // ---- scores: lane = key
+            // ---- scores: lane = key (KT 32); at KT 16 lane = key + 16 * half, each half over D / 2 dims
+            constexpr int JB = KT == 32 ? D / 32 : D / 64;  // boxes per lane
+            const int key = lane & (KT - 1), jb0 = KT == 32 ? 0 : (lane >> 4) * JB;
             float sc[G];
 #pragma unroll
             for (int h = 0; h < G; ++h) sc[h] = 0.f;
 #pragma unroll
-            for (int j = 0; j < D / 32; ++j) {
+            for (int j = 0; j < JB; ++j) {
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
-                    const float4 k4 = lds128(kbase + j * C::BOX + box_off(lane, c));
+                    const float4 k4 = lds128(kbase + (jb0 + j) * C::BOX + box_off(key, c));
 #pragma unroll
                     for (int h = 0; h < G; ++h) {
-                        const float4 q4 = lds128(sqw_a + (h * D + j * 32 + c * 4) * 4);
+                        const float4 q4 = lds128(sqw_a + (h * D + (jb0 + j) * 32 + c * 4) * 4);
                         sc[h] = fmaf(q4.x, k4.x, sc[h]);
                         sc[h] = fmaf(q4.y, k4.y, sc[h]);
                         sc[h] = fmaf(q4.z, k4.z, sc[h]);
@@ -205,9 +209,13 @@ __global__ void __launch_bounds__(F32Cfg<D>::THREADS, 1)
                     }
                 }
             }
+            if constexpr (KT == 16) {
+#pragma unroll
+                for (int h = 0; h < G; ++h) sc[h] += __shfl_xor_sync(0xffffffffu, sc[h], 16);
+            }
 
-            // ---- online softmax (base 2) per head over the 32 keys
-            const bool valid = lane < nvalid;
+            // ---- online softmax (base 2) per head over the tile's keys (at KT 16 both halves hold each key)
+            const bool valid = key < nvalid;
 #pragma unroll
             for (int h = 0; h < G; ++h) {
                 const float x = valid ? sc[h] : -INFINITY;
@@ -215,11 +223,11 @@ __global__ void __launch_bounds__(F32Cfg<D>::THREADS, 1)
                 const float m_use = m_new == -INFINITY ? 0.f : m_new;
                 const float corr = fast_exp2(m[h] - m_use);
                 const float pr = valid ? fast_exp2(x - m_use) : 0.f;
-                l[h] = l[h] * corr + warp_sum(pr);
+                l[h] = l[h] * corr + warp_sum(lane < KT ? pr : 0.f);
                 m[h] = m_new;
 #pragma unroll
                 for (int e = 0; e < DL; ++e) acc[h][e] *= corr;
-                pww[lane * HS + h] = pr;
+                if (lane < KT) pww[lane * HS + h] = pr;
             }
             __syncwarp();
 
@@ -236,6 +244,12 @@ __global__ void __launch_bounds__(F32Cfg<D>::THREADS, 1)
                 if constexpr (DL == 2) {
                     const float2 v2 = lds64(vbase + (lane >> 4) * C::BOX + box_off(r, (lane & 15) >> 1) + (lane & 1) * 8);
                     v[0] = v2.x; v[1] = v2.y;
+                } else if constexpr (DL == 8) {
+                    const uint32_t vb = vbase + (lane >> 2) * C::BOX;
+                    const float4 v0 = lds128(vb + box_off(r, (lane & 3) * 2));
+                    const float4 v1 = lds128(vb + box_off(r, (lane & 3) * 2 + 1));
+                    v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
+                    v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
                 } else {
                     const float4 v4 = lds128(vbase + (lane >> 3) * C::BOX + box_off(r, lane & 7));
                     v[0] = v4.x; v[1] = v4.y; v[2] = v4.z; v[3] = v4.w;
@@ -326,7 +340,7 @@ cudaError_t dispatch_g(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap
 
 }  // namespace
 
-bool decode_f32_supported(int D, int G) { return (D == 64 || D == 128) && G >= 1 && G <= 8; }
+bool decode_f32_supported(int D, int G) { return (D == 64 || D == 128 || D == 256) && G >= 1 && G <= 8; }
 
 cudaError_t launch_attend_decode_f32(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
                                      const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,
@@ -349,5 +363,6 @@ cudaError_t launch_attend_decode_f32(cudaStream_t st, const CUtensorMap &tk, con
     const int G = a.Hq / a.Hkv;
     if (a.D == 64) return dispatch_g<64>(st, tk, tv, p, G, sm_count);
     if (a.D == 128) return dispatch_g<128>(st, tk, tv, p, G, sm_count);
+    if (a.D == 256) return dispatch_g<256>(st, tk, tv, p, G, sm_count);
     return cudaErrorInvalidValue;
 }

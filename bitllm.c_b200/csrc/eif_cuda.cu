@@ -190,7 +190,8 @@ bool make_kv_tensor_map(CUtensorMap *map, void *base, const eif_cuda_kv_t *kv) {
     const cuuint64_t strides[2] = {(cuuint64_t)kv->hd * elt, (cuuint64_t)kv->n_kv * kv->hd * elt};
     // INT8: 128-byte rows (128 dims) from head_dim 128 up; 64-byte rows at head_dim 64
     const cuuint32_t box0 = f32 ? 32u : (i8 && kv->hd >= 128) ? 128u : 64u;
-    const cuuint32_t box[3] = {box0, 1, f32 ? 32u : 64u};
+    // fp32: 32-key boxes, 16 at head_dim 256 (the fp32 decode kernel's tile there)
+    const cuuint32_t box[3] = {box0, 1, f32 ? (kv->hd == 256 ? 16u : 32u) : 64u};
     const cuuint32_t es[3] = {1, 1, 1};
     // L2 promotion no wider than one kv head's row: the rows of the other kv heads in between belong to other
     // work items, and a wider promotion would fetch them from HBM with every tile

@@ -229,7 +229,7 @@ def test_device_pos_above_max_pos_reported(pkg, ctx, orc, monkeypatch, dtype):
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16", "int8"])
-@pytest.mark.parametrize("hd,nh,nkv", [(64, 14, 2), (128, 8, 2), (64, 2, 2)])
+@pytest.mark.parametrize("hd,nh,nkv", [(64, 14, 2), (128, 8, 2), (64, 2, 2), (256, 8, 2)])
 def test_many_items_per_cta(pkg, ctx, orc, dtype, hd, nh, nkv):
     """Batches whose (sequence, kv head, chunk) items outnumber the SMs, so every persistent CTA runs several
     items and its TMA ring is reused across them and across consumer warps (the regime of the benchmarks).
