@@ -358,6 +358,28 @@ def run_ours(args, torch, dist, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_all, att_ms = float(t[0]), float(t[1])
 
+    # the optional collective, timed on its own (not part of `value`): reassembling one attention layer's output
+    # [batch, 8 heads, 256] fp32 on every rank with the NCCL all-gather of shard.gather_outputs, as a caller
+    # feeding a replicated projection would
+    gather = None
+    if dist:
+        loc = hy.out.view(B, AT_HQ, AT_D)
+        for _ in range(3):
+            pkg.shard.gather_outputs(dist, loc, GB, AT_HQ, world)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(args.steps):
+            pkg.shard.gather_outputs(dist, loc, GB, AT_HQ, world)
+        g1.record()
+        torch.cuda.synchronize()
+        g_ms = pkg.shard.max_over_ranks(dist, g0.elapsed_time(g1) / args.steps, "cuda")
+        g_bytes = GB * AT_HQ * AT_D * 4
+        gather = {"op": "shard.gather_outputs: NCCL all-gather of one attention layer's output + placement",
+                  "bytes_gathered": g_bytes, "ms_per_call": g_ms, "algbw_GBs": g_bytes / (g_ms * 1e-3) / 1e9,
+                  "timed": "CUDA events on the collective's stream, max over ranks; not part of value"}
+
     # end to end through the host-pointer ABI (pinned host buffers, H2D + D2H inside every call)
     e2e = None
     if not args.no_e2e:
@@ -400,6 +422,7 @@ def run_ours(args, torch, dist, rank, world, local_rank):
                      "traffic": traffic("attn_decode_tc_hd256", bytes_att)[0],
                      "traffic_source": traffic("attn_decode_tc_hd256", bytes_att)[1]},
         "step_hbm_frac": world * step_bytes / (ms_all * 1e-3) / 1e9 / (hbm * world),
+        "gather": gather,
         "gpu_launches": launches,
         "clocks": clk,
     }
