@@ -47,8 +47,8 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
 
     constexpr int NH = NP / 2;  // passes over the rows staged in shared memory; the other NH in registers
     __shared__ float sq[DK], sk[DK], sv[DV];
-    __shared__ float red[NW];
-    __shared__ float4 cred[NW][LPR];
+    __shared__ float2 red[NW];
+    __shared__ float4 cred[2][NW][LPR];  // one buffer per column sum: no barrier between their uses
     __shared__ float gates[2];
     __shared__ __align__(8) uint64_t s_bar;
     extern __shared__ __align__(128) float Ssm[];  // S rows [0, DK/2)
@@ -70,6 +70,14 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
     float4 sreg[NH];
 #pragma unroll
     for (int u = 0; u < NH; ++u) sreg[u] = Srow[(rg + (NH + u) * RP) * (DV / 4)];
+    // the gates' inputs, loaded now so that their latency overlaps the conv
+    float braw = 0.f, araw = 0.f, dtb = 0.f, aex = 0.f;
+    if (tid == 0) {
+        braw = a.b_raw[bh];
+        araw = a.a_raw[bh];
+        dtb = a.dt_bias[h];
+        aex = a.a_exp[h];
+    }
 
     // causal conv1d + SiLU on this head's channels: q [h*DK, +DK), k [key_dim + h*DK, +DK), v [2*key_dim + h*DV, +DV)
     const int ck = a.conv_k;
@@ -92,29 +100,27 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
         else sv[i - 2 * DK] = y;
     }
     if (tid == 0) {
-        gates[0] = 1.0f / (1.0f + expf(-a.b_raw[bh]));
-        const float x = a.a_raw[bh] + a.dt_bias[h];
-        gates[1] = -a.a_exp[h] * logf(1.0f + expf(x));
+        gates[0] = 1.0f / (1.0f + expf(-braw));
+        gates[1] = -aex * logf(1.0f + expf(araw + dtb));
     }
     __syncthreads();
 
-    auto block_sum = [&](float x) -> float {
-        x = warp_sum(x);
-        if (lane == 0) red[warp] = x;
-        __syncthreads();
-        float t = 0.f;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) t += red[w];
-        __syncthreads();
-        return t;
-    };
-    // L2 norms (eps 1e-12 inside the root), q also scaled by 1/sqrt(d_k)
+    // L2 norms (eps 1e-12 inside the root), q also scaled by 1/sqrt(d_k): both sums in one block reduction
     float pq = 0.f, pk = 0.f;
     for (int i = tid; i < DK; i += THREADS) {
         pq += sq[i] * sq[i];
         pk += sk[i] * sk[i];
     }
-    const float ssq = block_sum(pq), ssk = block_sum(pk);
+    pq = warp_sum(pq);
+    pk = warp_sum(pk);
+    if (lane == 0) red[warp] = make_float2(pq, pk);
+    __syncthreads();
+    float ssq = 0.f, ssk = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        ssq += red[w].x;
+        ssk += red[w].y;
+    }
     const float iq = 1.0f / sqrtf(ssq + 1e-12f), ik = 1.0f / sqrtf(ssk + 1e-12f);
     const float q_scale = 1.0f / sqrtf((float)DK);
     for (int i = tid; i < DK; i += THREADS) {
@@ -123,15 +129,15 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
     }
     __syncthreads();
 
-    auto colsum = [&](float4 x) -> float4 {
+    // column sums over the row groups; every thread gets its columns' totals (buffer `cb`, used once)
+    auto colsum = [&](float4 x, int cb) -> float4 {
 #pragma unroll
         for (int off = LPR; off < 32; off <<= 1) x = f4_add(x, f4_shfl_xor(x, off));
-        if (lane < LPR) cred[warp][lc] = x;
+        if (lane < LPR) cred[cb][warp][lc] = x;
         __syncthreads();
-        float4 t = cred[0][lc];
+        float4 t = cred[cb][0][lc];
 #pragma unroll
-        for (int w = 1; w < NW; ++w) t = f4_add(t, cred[w][lc]);
-        __syncthreads();
+        for (int w = 1; w < NW; ++w) t = f4_add(t, cred[cb][w][lc]);
         return t;
     };
 
@@ -148,7 +154,7 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
         s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;
         e.x += s.x * ki; e.y += s.y * ki; e.z += s.z * ki; e.w += s.w * ki;
     }
-    e = colsum(e);
+    e = colsum(e, 0);
     const float4 vv = make_float4(sv[col0], sv[col0 + 1], sv[col0 + 2], sv[col0 + 3]);
     const float4 dlt = make_float4(vv.x - e.x, vv.y - e.y, vv.z - e.z, vv.w - e.w);
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -163,10 +169,12 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
         const float qi = sq[i];
         o.x += s.x * qi; o.y += s.y * qi; o.z += s.z * qi; o.w += s.w * qi;
     }
-    o = colsum(o);
-    // gated RMSNorm over the head's d_v outputs (threads of row group 0 hold the whole row)
-    float pss = rg == 0 ? o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w : 0.f;
-    const float ss = block_sum(pss);
+    o = colsum(o, 1);
+    // gated RMSNorm over the head's d_v outputs: the LPR lanes of a row group hold the whole row, so the sum
+    // of squares is a shuffle reduction (no block barrier); row group 0 writes
+    float ss = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
+#pragma unroll
+    for (int off = 1; off < LPR; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     if (rg == 0) {
         const float rms = 1.0f / sqrtf(ss / DV + 1e-6f);
         const float *z = a.z + bh * DV + col0;
