@@ -1216,6 +1216,189 @@ def cpu_qwen35_attention_reference(L, seconds=10.0):
                                      f"sequence per host thread, {el:.1f} s")
 
 
+# --workload projection: the quantised projections of one Qwen3.5-0.8B decode step (the reference's own model
+# config, include/eif_qwen35.h:58-72): dim 1024, FFN 3584, 24 layers (DeltaNet x 3, attention) x 6, 16 x 128
+# DeltaNet heads, 8 / 2 heads of 256 with the output gate, vocabulary 248320.  The projections that read the same
+# input are stacked by rows into one matrix (DeltaNet qkv + z + b + a, attention q + k + v, FFN gate + up), so a
+# step is 4 launches a layer plus the INT8 LM head (int8_gemv, the default tied embedding).
+PJ_DIM, PJ_HID, PJ_VOCAB = 1024, 3584, 248320
+
+
+def projection_step_shapes(qt=2):
+    """(rows, cols, quant_type) of the launches of one decode step, in the engine's order."""
+    out = []
+    for typ in LAYER_TYPES:
+        if typ == "A":  # q with its gate, k, v; o_proj
+            out += [(2 * AT_HQ * AT_D + 2 * AT_HKV * AT_D, PJ_DIM, qt), (PJ_DIM, AT_HQ * AT_D, qt)]
+        else:  # in_proj_qkv, in_proj_z, in_proj_b, in_proj_a; out_proj
+            out += [(DN_CONV + DN_H * DN_D + 2 * DN_H, PJ_DIM, qt), (PJ_DIM, DN_H * DN_D, qt)]
+        out += [(2 * PJ_HID, PJ_DIM, qt), (PJ_DIM, PJ_HID, qt)]  # FFN gate + up; down
+    out.append((PJ_VOCAB, PJ_DIM, 4))
+    return out
+
+
+def _packed_bytes(rows, cols, qt):
+    base = qt & 0xFF
+    return rows * {0: 4 * cols, 1: (cols + 1) // 2, 2: (cols + 3) // 4, 3: (cols + 4) // 5}.get(base, cols)
+
+
+def _linear_alg_bytes(rows, cols, qt, n):
+    """Algorithmic bytes of one launch: the packed weights and scales once, n input and output vectors."""
+    base, group = qt & 0xFF, qt >> 8
+    n_sc = 0 if base == 0 else rows * (cols // group if group else 1)
+    return _packed_bytes(rows, cols, qt) + 4 * n_sc + 4 * n * (cols + rows)
+
+
+def cpu_projection_reference(shapes, n, seconds=10.0):
+    """The reference's linear_gemv / linear_gemm / int8_gemv (oracle/_ref) over the step's projections with all
+    host threads (its OpenMP loops), on random weight bytes; the port where the reference build is absent."""
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as orc
+    rng = np.random.default_rng(7)
+    mats = []
+    for rows, cols, qt in shapes:
+        W = rng.integers(0, 256, _packed_bytes(rows, cols, qt), dtype=np.uint8)
+        sc = None if (qt & 0xFF) == 0 else (0.01 + rng.random(rows)).astype(np.float32)
+        mats.append((W, sc, rng.standard_normal((n, cols)).astype(np.float32), rows, cols, qt))
+    use_ref = orc.ref_available()
+    ncpu = os.cpu_count() or 1
+    if use_ref:
+        orc.ref().ref_set_threads(ncpu)
+    steps, t_total = 0, 0.0
+    while t_total < seconds:
+        for W, sc, x, rows, cols, qt in mats:
+            if use_ref:
+                t_total += orc.ref_linear_time(W, sc, x, rows, cols, qt, 1)
+            else:
+                t0 = time.perf_counter()
+                orc.linear(W, sc, x, rows, cols, qt)
+                t_total += time.perf_counter() - t0
+        steps += 1
+    kind = "reference" if use_ref else "port"
+    return n * steps / t_total, (ncpu if use_ref else 1), kind, (
+        f"{steps} decode steps' projections ({len(shapes)} launches each, batch {n}), {t_total:.1f} s")
+
+
+def run_projection(args, torch, dist, rank, world, local_rank):
+    """Row f4: every projection of a Qwen3.5-0.8B decode step on the GPU (2-bit ternary weights with a scale a
+    row, the INT8 LM head), `--batch` tokens a rank (default 1), replayed as one CUDA graph of the 97 launches.
+    Weights: random bytes (every byte is a valid code of each format), ~380 MB > L2, so each step streams them
+    from HBM.  Roofline: the ternary launches together (the dominant kernel), from a graph of those alone, and
+    the LM head from its own launches."""
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    torch.cuda.set_device(local_rank)
+    n = args.batch or 1
+    shapes = projection_step_shapes()
+    ctx = pkg.Context(local_rank)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    dev = torch.device("cuda", local_rank)
+    rng = np.random.default_rng(11)
+    lins, xs, outs = [], [], []
+    for rows, cols, qt in shapes:
+        W = rng.integers(0, 256, _packed_bytes(rows, cols, qt), dtype=np.uint8)
+        sc = (0.01 + rng.random(rows)).astype(np.float32)
+        lins.append(pkg.Linear(ctx, qt, rows, cols, W, sc))
+        xs.append(torch.randn(n, cols, device=dev))
+        outs.append(torch.empty(n, rows, device=dev))
+    tern = [i for i, (_, _, qt) in enumerate(shapes) if qt != 4]
+    head = len(shapes) - 1
+
+    def launch(idx):
+        for i in idx:
+            lins[i].forward_dev(xs[i].data_ptr(), n, outs[i].data_ptr())
+
+    every = list(range(len(shapes)))
+    for _ in range(args.warmup):
+        launch(every)
+    torch.cuda.synchronize()
+    graphs = {}
+    for key, idx in (("step", every), ("ternary", tern)):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            launch(idx)
+        graphs[key] = g
+    torch.cuda.synchronize()
+
+    def timed(fn, k):
+        ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(k)]
+        for j in range(k):
+            ev[j][0].record()
+            fn()
+            ev[j][1].record()
+        torch.cuda.synchronize()
+        return float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
+
+    for _ in range(args.warmup):
+        graphs["step"].replay()
+    clocks = ClockSampler(local_rank)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    ms = timed(graphs["step"].replay, args.steps)
+    clk = clocks.stop()
+    ms = pkg.shard.max_over_ranks(dist, ms, "cuda")
+    tern_ms = pkg.shard.max_over_ranks(dist, timed(graphs["ternary"].replay, args.steps), "cuda")
+    head_ms = pkg.shard.max_over_ranks(dist, timed(lambda: launch([head]), args.steps), "cuda")
+    # e2e: each step copies the token's input from pinned host memory, runs the step's graph and reads the logits
+    # back (the hidden states between projections stay on the device, as a device-resident decode step's do)
+    e2e_ms = None
+    xh = torch.randn(n, PJ_DIM).pin_memory()
+    lh = torch.empty(n, PJ_VOCAB).pin_memory()
+    if not args.no_e2e:
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            xs[0].copy_(xh, non_blocking=True)
+            graphs["step"].replay()
+            lh.copy_(outs[head], non_blocking=True)
+            stream.synchronize()
+        e2e_ms = pkg.shard.max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / args.steps, "cuda")
+    for g in graphs.values():
+        del g
+    graphs.clear()
+    for lin in lins:
+        lin.free()
+    if rank != 0:
+        return None
+    hbm, _, src = peaks()
+    tern_bytes = sum(_linear_alg_bytes(*shapes[i], n) for i in tern)
+    head_bytes = _linear_alg_bytes(*shapes[head], n)
+    step_bytes = tern_bytes + head_bytes
+    ach = tern_bytes / (tern_ms * 1e-3) / 1e9
+    head_ach = head_bytes / (head_ms * 1e-3) / 1e9
+    tr, tr_src = traffic("linear_ternary2", tern_bytes)
+    line = {"metric": "projection tokens/s (every quantised projection of a Qwen3.5-0.8B decode step)",
+            "value": n * world / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random weight bytes and inputs)",
+            "config": {"workload": "projection (row f4): Qwen3.5-0.8B decode-step projections", "tokens_per_rank": n,
+                       "launches_per_step": len(shapes), "weights": "2-bit ternary, a scale a row; INT8 LM head",
+                       "weight_bytes_per_step": sum(_packed_bytes(*s) for s in shapes),
+                       "l2": "weights (~380 MB) > L2: every step streams them from HBM",
+                       "graph": "the step's launches replayed as one CUDA graph",
+                       "parallelism": f"tokens over {world} rank(s), weights replicated, no collective"},
+            "step_hbm_frac": step_bytes / (ms * 1e-3) / 1e9 / hbm,
+            "e2e": None if e2e_ms is None else {
+                "value": n * world / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": xh.numel() * 4 * world, "d2h_bytes_per_step": lh.numel() * 4 * world,
+                "path": "pinned input copied in, the step's eif_cuda_linear_forward_dev graph, logits copied out"},
+            "roofline": {"kernel": "linear_kernel (2-bit ternary, the 96 layer launches)", "bound": "hbm",
+                         "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm, "peak_source": src,
+                         "algorithmic_bytes_per_launch": tern_bytes / len(tern), "launch_ms": tern_ms / len(tern),
+                         "traffic": None if tr is None else tr / len(tern), "traffic_source": tr_src},
+            "lm_head": {"kernel": "linear_kernel (INT8, 248320 x 1024)", "achieved": head_ach, "frac": head_ach / hbm,
+                        "launch_ms": head_ms, "algorithmic_bytes": head_bytes},
+            "gpu_launches": len(shapes) * args.steps, "clocks": clk}
+    if world == 1 and not args.no_cpu_baseline:
+        tps, cores, kind, sample = cpu_projection_reference(shapes, n)
+        line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
+    return line
+
+
 WORKLOADS = [  # (key, workload, overrides): BASELINE configs[0..3] and config 1's heads batched per cache type
     ("config1_decode", "decode", dict(batch=1, ctx=512, kv="f32")),
     ("config2_prefill", "prefill", {}),
@@ -1242,7 +1425,8 @@ def run_workloads(args, torch, local_rank):
         a = argparse.Namespace(**vars(args))
         a.workload, a.batch, a.ctx, a.kv = wl, over.get("batch"), over.get("ctx"), over.get("kv", "f32")
         a.heads = over.get("heads", "qwen2")
-        fn = {"prefill": run_prefill, "chunked": run_chunked, "decode": run_decode, "recurrent": run_recurrent}[wl]
+        fn = {"prefill": run_prefill, "chunked": run_chunked, "decode": run_decode, "recurrent": run_recurrent,
+              "projection": run_projection}[wl]
         line = fn(a, torch, None, 0, 1, local_rank)
         out[key] = {k: line[k] for k in _KEEP if k in line}
         gc.collect()
@@ -1253,10 +1437,12 @@ def run_workloads(args, torch, local_rank):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", default="hybrid", choices=["hybrid", "prefill", "chunked", "decode", "recurrent"],
+    ap.add_argument("--workload", default="hybrid",
+                    choices=["hybrid", "prefill", "chunked", "decode", "recurrent", "projection"],
                     help="hybrid = BASELINE configs[4] (the headline); prefill = configs[1]; chunked = configs[3]; "
                          "recurrent = configs[2]; decode = configs[0]'s tinyllm heads, batched (--kv f32 | bf16 | "
-                         "int8, --ctx)")
+                         "int8, --ctx); projection = the quantised projections of a Qwen3.5-0.8B decode step "
+                         "(--batch tokens, default 1)")
     ap.add_argument("--kv", default="f32", choices=["f32", "bf16", "int8"], help="decode workload: cache dtype")
     ap.add_argument("--ctx", type=int, default=None, help="decode workload: context length (default 4096)")
     ap.add_argument("--heads", default="qwen2", choices=["qwen2", "qwen35"],
@@ -1295,9 +1481,9 @@ def main():
         torch.cuda.set_device(local_rank)
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         dist = tdist
-    if args.workload in ("prefill", "chunked", "decode", "recurrent"):
+    if args.workload in ("prefill", "chunked", "decode", "recurrent", "projection"):
         run = {"prefill": run_prefill, "chunked": run_chunked, "decode": run_decode,
-               "recurrent": run_recurrent}[args.workload]
+               "recurrent": run_recurrent, "projection": run_projection}[args.workload]
         line = run(args, torch, dist, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)

@@ -14,6 +14,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <new>
 
 #include "internal.h"
 
@@ -1998,5 +1999,92 @@ EIF_API eif_status_t eif_cuda_fullatt_prefill(eif_cuda_ctx_t *ctx, eif_cuda_kv_t
                              s + o_q, reinterpret_cast<float *>(s + o_g));
     if (st != EIF_STATUS_OK) return st;
     CK(cudaMemcpyAsync(out, s + o_o, nq * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return wait_stream(ctx);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Projections: linear_gemv / linear_gemm / int8_gemv (src/eif_qwen35.c:384-443, 1033-1063) on resident weights.
+
+EIF_API eif_status_t eif_cuda_linear_upload(eif_cuda_ctx_t *ctx, int quant_type, int rows, int cols, const void *W,
+                                            const float *scales, eif_cuda_linear_t **out) {
+    if (!ctx || !out) return EIF_STATUS_INVALID_ARGUMENT;
+    *out = nullptr;
+    const int wt = quant_type & 0xff, group = quant_type >> 8;
+    if (wt < EIF_CUDA_W_F32 || wt > EIF_CUDA_W_INT8 || group < 0)
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "linear: unknown quant type %d", quant_type);
+    if (rows <= 0 || cols <= 0 || !W || (wt != EIF_CUDA_W_F32 && !scales))
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "linear_upload: rows %d cols %d or a NULL pointer", rows, cols);
+    if (group > 0 && (wt != EIF_CUDA_W_TERNARY2 || group % 16 || cols % group))
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED,
+                    "linear: scale group %d (2-bit ternary only, a multiple of 16 dividing cols %d)", group, cols);
+    const size_t row_bytes = linear_row_bytes(wt, cols), stride = (row_bytes + 15) & ~(size_t)15;
+    if (!linear_fits(wt, stride))
+        return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "linear: %d columns exceed the shared-memory token tile", cols);
+    DeviceGuard g(ctx);
+    if (!g.ok) return fail(ctx, EIF_STATUS_ERROR, "cannot select device %d", ctx->device);
+    eif_cuda_linear_t *lin = new (std::nothrow) eif_cuda_linear_t();
+    if (!lin) return fail(ctx, EIF_STATUS_OUT_OF_MEMORY, "linear_upload: host allocation");
+    lin->ctx = ctx;
+    lin->wtype = wt;
+    lin->group = group;
+    lin->rows = rows;
+    lin->cols = cols;
+    lin->row_bytes = row_bytes;
+    lin->stride = stride;
+    lin->n_scales_row = wt == EIF_CUDA_W_F32 ? 0 : (group ? cols / group : 1);
+    cudaError_t e = cudaMalloc(&lin->W, stride * (size_t)rows);
+    if (e == cudaSuccess && stride != row_bytes) e = cudaMemset(lin->W, 0, stride * (size_t)rows);
+    if (e == cudaSuccess) e = cudaMemcpy2D(lin->W, stride, W, row_bytes, row_bytes, rows, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && lin->n_scales_row) {
+        const size_t ns = (size_t)rows * lin->n_scales_row * sizeof(float);
+        e = cudaMalloc(&lin->scales, ns);
+        if (e == cudaSuccess) e = cudaMemcpy(lin->scales, scales, ns, cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) {
+        if (lin->W) cudaFree(lin->W);
+        if (lin->scales) cudaFree(lin->scales);
+        delete lin;
+        return cuda_fail(ctx, e, "linear_upload");
+    }
+    *out = lin;
+    return EIF_STATUS_OK;
+}
+
+EIF_API void eif_cuda_linear_free(eif_cuda_linear_t *lin) {
+    if (!lin) return;
+    DeviceGuard g(lin->ctx);
+    cudaStreamSynchronize(lin->ctx->stream);  // queued projections may still read the weights
+    if (lin->W) cudaFree(lin->W);
+    if (lin->scales) cudaFree(lin->scales);
+    delete lin;
+}
+
+EIF_API eif_status_t eif_cuda_linear_forward_dev(eif_cuda_ctx_t *ctx, const eif_cuda_linear_t *lin,
+                                                 const float *x_dev, int n, float *out_dev) {
+    if (!ctx || !lin) return EIF_STATUS_INVALID_ARGUMENT;
+    if (lin->ctx != ctx) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "linear: weights of another context");
+    if (n < 1 || !x_dev || !out_dev)
+        return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "linear_forward_dev: n %d or a NULL pointer", n);
+    DeviceGuard g(ctx);
+    CK(launch_linear(ctx->stream, *lin, x_dev, n, out_dev, ctx->sm_count));
+    ctx->launches += 1;
+    return EIF_STATUS_OK;
+}
+
+EIF_API eif_status_t eif_cuda_linear_forward(eif_cuda_ctx_t *ctx, const eif_cuda_linear_t *lin, const float *x,
+                                             int n, float *out) {
+    if (!ctx || !lin) return EIF_STATUS_INVALID_ARGUMENT;
+    if (lin->ctx != ctx) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "linear: weights of another context");
+    if (n < 1 || !x || !out) return fail(ctx, EIF_STATUS_INVALID_ARGUMENT, "linear_forward: n %d or a NULL pointer", n);
+    DeviceGuard g(ctx);
+    const size_t xb = (size_t)n * lin->cols * 4, ob = (size_t)n * lin->rows * 4;
+    eif_status_t st = ensure_buffer(ctx, &ctx->stage, &ctx->stage_bytes, a256(xb) + ob);
+    if (st != EIF_STATUS_OK) return st;
+    float *xd = static_cast<float *>(ctx->stage);
+    float *od = reinterpret_cast<float *>(static_cast<char *>(ctx->stage) + a256(xb));
+    CK(cudaMemcpyAsync(xd, x, xb, cudaMemcpyHostToDevice, ctx->stream));
+    CK(launch_linear(ctx->stream, *lin, xd, n, od, ctx->sm_count));
+    ctx->launches += 1;
+    CK(cudaMemcpyAsync(out, od, ob, cudaMemcpyDeviceToHost, ctx->stream));
     return wait_stream(ctx);
 }

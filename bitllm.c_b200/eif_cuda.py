@@ -24,6 +24,8 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "eif_cuda.h")
 STATUS = {0: "OK", -1: "ERROR", -2: "INVALID_ARGUMENT", -3: "OUT_OF_MEMORY", -4: "NOT_IMPLEMENTED",
           -5: "NOT_SUPPORTED", -6: "TIMEOUT", -7: "INTERNAL_ERROR", -8: "INVALID_LAYER", -9: "SHAPE_MISMATCH"}
 F32, BF16, INT8 = 0, 1, 2
+# projection weight formats (eif_cuda_wtype_t): the engine's quant types (include/eif_qwen35.h:83-86) + INT8 head
+W_F32, W_INT4, W_TERNARY2, W_TERNARY_DENSE, W_INT8 = 0, 1, 2, 3, 4
 SUBLN_NONE, SUBLN_RMS, SUBLN_WEIGHT = 0, 1, 2
 
 _P = ctypes.c_void_p
@@ -116,6 +118,10 @@ def lib() -> ctypes.CDLL:
         "eif_cuda_fullatt_prep_dev": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _P, _P]),
         "eif_cuda_fullatt_prep_prefill": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _P, _P]),
         "eif_cuda_fullatt_prep_prefill_dev": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _P, _P]),
+        "eif_cuda_linear_upload": (_I, [_P, _I, _I, _I, _P, _P, ctypes.POINTER(_P)]),
+        "eif_cuda_linear_free": (None, [_P]),
+        "eif_cuda_linear_forward": (_I, [_P, _P, _P, _I, _P]),
+        "eif_cuda_linear_forward_dev": (_I, [_P, _P, _P, _I, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -594,3 +600,51 @@ class DeltaState:
     def step_dev(self, layer: int, q_dev, k_dev, v_dev, beta_dev, g_dev, q_scale: float, o_dev):
         self.ctx.check(lib().eif_cuda_deltanet_step_dev(self.ctx.handle, self._h, layer, q_dev, k_dev, v_dev,
                                                         beta_dev, g_dev, float(q_scale), o_dev), "deltanet_step_dev")
+
+
+def packed_row_bytes(cols: int, wtype: int) -> int:
+    """Bytes of one packed weight row of the format (row_bytes, src/eif_qwen35.c:110-116; INT8 a byte a weight)."""
+    return {W_F32: 4 * cols, W_INT4: (cols + 1) // 2, W_TERNARY2: (cols + 3) // 4,
+            W_TERNARY_DENSE: (cols + 4) // 5}.get(wtype, cols)
+
+
+class Linear:
+    """A projection's weights resident on the device (eif_cuda_linear_t): linear_gemv / linear_gemm / int8_gemv
+    (src/eif_qwen35.c:384-443, 1033-1063) on the GPU.  `quant_type` is the engine's packed quant type (base in the
+    low byte, the 2-bit ternary scale group in the bits above); W is the engine's packed rows (uint8, rows x
+    row_bytes) and scales its fp32 scales (None for fp32 weights)."""
+
+    def __init__(self, ctx: Context, quant_type: int, rows: int, cols: int, W, scales=None):
+        self.ctx, self.quant_type, self.rows, self.cols = ctx, int(quant_type), int(rows), int(cols)
+        w = np.ascontiguousarray(W).view(np.uint8)
+        need = rows * packed_row_bytes(cols, quant_type & 0xFF)
+        if (quant_type & 0xFF) <= W_INT8 and w.size != need:  # an unknown format is the library's to reject
+            raise ValueError(f"W holds {w.size} bytes, the format needs {need}")
+        sc = _f32(scales) if scales is not None else None
+        self._h = _P()
+        ctx.check(lib().eif_cuda_linear_upload(ctx.handle, self.quant_type, self.rows, self.cols, _ptr(w), _ptr(sc),
+                                               ctypes.byref(self._h)), "linear_upload")
+        ctx._children.add(self)
+
+    def free(self):
+        if self._h and self.ctx.alive:
+            lib().eif_cuda_linear_free(self._h)
+        self._h = _P()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def forward(self, x, out=None):
+        """out [n][rows] = W x[t] for x [n][cols] (fp32 host arrays; a 1-D x is one token)."""
+        xx = _f32(x).reshape(-1, self.cols)
+        o = _out(out, (xx.shape[0], self.rows))
+        self.ctx.check(lib().eif_cuda_linear_forward(self.ctx.handle, self._h, _ptr(xx), xx.shape[0], _ptr(o)),
+                       "linear_forward")
+        return o
+
+    def forward_dev(self, x_dev, n: int, out_dev):
+        self.ctx.check(lib().eif_cuda_linear_forward_dev(self.ctx.handle, self._h, x_dev, int(n), out_dev),
+                       "linear_forward_dev")

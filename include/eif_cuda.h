@@ -413,6 +413,41 @@ eif_status_t eif_cuda_prefill_step_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, i
                                        const float *k_dev, const float *v_dev, int n_tok, int start_pos, int n_heads,
                                        float scale, float *out_dev);
 
+/* ---------------------------------------------------------------------------------------------
+ * Projections  (replace linear_gemv, src/eif_qwen35.c:422-443, its batched twin linear_gemm :1033-1063, and the
+ * INT8 LM head int8_gemv :384-420; the mixers' q/k/v/z/a/b/o and FFN projections and the logits)
+ * ------------------------------------------------------------------------------------------- */
+
+/* Weight formats: the engine's quant types (include/eif_qwen35.h:83-86) and the INT8 LM head.  The engine's
+ * packed quant type is passed unchanged: base = quant_type & 0xff, and for EIF_CUDA_W_TERNARY2 the scale group
+ * in the upper bits, group = quant_type >> 8 (0: one scale a row; src/eif_qwen35.c:100-101). */
+typedef enum {
+    EIF_CUDA_W_F32 = 0,           /* fp32 rows, no scale (f32_gemv, :355-382) */
+    EIF_CUDA_W_INT4 = 1,          /* two a byte, even column in the high nibble, value - 8; a scale a row (:293-352) */
+    EIF_CUDA_W_TERNARY2 = 2,      /* four a byte, column c at bits 2(c mod 4), code 1 = +1, 2 = -1, else 0; a scale a
+                                     row, or a scale per `group` columns (src/eif_quantize_bitnet.c:834-889, 1356-1420) */
+    EIF_CUDA_W_TERNARY_DENSE = 3, /* five base-3 digits a byte, least significant first, 1 = +1, 2 = -1; a scale a row
+                                     (bitnet_gemv_dense, src/eif_qwen35.c:148-180) */
+    EIF_CUDA_W_INT8 = 4           /* int8, a scale a row: the LM head (int8_gemv) */
+} eif_cuda_wtype_t;
+
+typedef struct eif_cuda_linear eif_cuda_linear_t; /* one weight matrix resident on the context's device */
+
+/* Upload a [rows][cols] weight matrix in the engine's packed row layout (row_bytes, src/eif_qwen35.c:110-116:
+ * fp32 4*cols, INT4 (cols+1)/2, ternary (cols+3)/4, dense (cols+4)/5, INT8 cols bytes a row) and its scales (rows
+ * floats; rows * cols/group for grouped ternary; NULL for fp32).  A group must be a multiple of 16 dividing cols
+ * (the engine's loader accepts multiples of 32, src/eif_qwen35.c:1265); cols up to 12288.  Synchronous. */
+eif_status_t eif_cuda_linear_upload(eif_cuda_ctx_t *ctx, int quant_type, int rows, int cols, const void *W,
+                                    const float *scales, eif_cuda_linear_t **out);
+void eif_cuda_linear_free(eif_cuda_linear_t *lin);
+
+/* out[t][rows] = W x[t] for n tokens x[n][cols] (n = 1: linear_gemv; n > 1: linear_gemm), fp32 arithmetic.
+ * _dev: device arrays, asynchronous.  Host variant: host arrays, returns when out is written. */
+eif_status_t eif_cuda_linear_forward(eif_cuda_ctx_t *ctx, const eif_cuda_linear_t *lin, const float *x, int n,
+                                     float *out);
+eif_status_t eif_cuda_linear_forward_dev(eif_cuda_ctx_t *ctx, const eif_cuda_linear_t *lin, const float *x_dev, int n,
+                                         float *out_dev);
+
 #ifdef __cplusplus
 }
 #endif

@@ -414,3 +414,72 @@ ORC_EXPORT void orc_round_bf16(float *x, size_t n)
         memcpy(&x[i], &u, 4);
     }
 }
+
+/* ------------------------------------------------------------------------------------------------
+ * Projections
+ * ---------------------------------------------------------------------------------------------- */
+
+/* Weight i of a packed row in the engine's formats (quant type base: 0 fp32, 1 INT4, 2 2-bit ternary,
+ * 3 dense ternary; 4 is the INT8 LM head):
+ *   INT4   byte i/2, even column in the high nibble, value - 8              (src/eif_qwen35.c:335-343)
+ *   2-bit  byte i/4, bits 2(i mod 4); code 1 = +1, 2 = -1, else 0           (src/eif_quantize_bitnet.c:52-64, 876-880)
+ *   dense  byte i/5, base-3 digit i mod 5 (least significant first); 1 = +1, 2 = -1 (src/eif_qwen35.c:78-92)
+ *   INT8   signed byte                                                      (src/eif_qwen35.c:384-420) */
+static float orc_weight(const uint8_t *row, int i, int base)
+{
+    switch (base) {
+    case 0: { float w; memcpy(&w, row + 4 * (size_t)i, 4); return w; }
+    case 1: { const uint8_t b = row[i >> 1]; return (float)(((i & 1) ? (b & 0x0F) : (b >> 4)) - 8); }
+    case 2: { const unsigned c = (row[i >> 2] >> (2 * (i & 3))) & 3u; return c == 1u ? 1.0f : (c == 2u ? -1.0f : 0.0f); }
+    case 3: {
+        unsigned b = row[i / 5];
+        for (int p = 0; p < i % 5; p++) b /= 3u;
+        const unsigned d = b % 3u;
+        return d == 1u ? 1.0f : (d == 2u ? -1.0f : 0.0f);
+    }
+    default: return (float)(int8_t)row[i];
+    }
+}
+
+static size_t orc_row_bytes(int cols, int base)  /* row_bytes, src/eif_qwen35.c:110-116 (+ INT8) */
+{
+    switch (base) {
+    case 0: return (size_t)cols * 4;
+    case 1: return (size_t)(cols + 1) / 2;
+    case 2: return (size_t)(cols + 3) / 4;
+    case 3: return (size_t)(cols + 4) / 5;
+    default: return (size_t)cols;
+    }
+}
+
+/*
+ * out[t][rows] = W x[t] for n tokens: linear_gemv (src/eif_qwen35.c:422-443) per token, each kernel's scalar
+ * form -- one fp32 sum a row in column order, then the row scale (fp32: none, f32_gemv :355-382); grouped
+ * 2-bit ternary (quant_type >> 8 = group > 0) sums each group of columns and adds block_sum * scale
+ * (eif_matmul_bitnet_block_f32, src/eif_quantize_bitnet.c:1376-1417).
+ */
+ORC_EXPORT void orc_linear(float *out, const uint8_t *W, const float *sc, const float *x, int n, int rows, int cols,
+                           int quant_type)
+{
+    const int base = quant_type & 0xff, group = quant_type >> 8;
+    const size_t rb = orc_row_bytes(cols, base);
+    for (int t = 0; t < n; t++) {
+        const float *xt = x + (size_t)t * cols;
+        for (int r = 0; r < rows; r++) {
+            const uint8_t *row = W + (size_t)r * rb;
+            float acc = 0.0f;
+            if (base == 2 && group > 0) {
+                const int nb = (cols + group - 1) / group;
+                for (int b = 0; b < nb; b++) {
+                    float bs = 0.0f;
+                    for (int c = b * group; c < cols && c < (b + 1) * group; c++) bs += orc_weight(row, c, base) * xt[c];
+                    acc += bs * sc[(size_t)r * nb + b];
+                }
+            } else {
+                for (int c = 0; c < cols; c++) acc += orc_weight(row, c, base) * xt[c];
+                if (base != 0) acc *= sc[r];
+            }
+            out[(size_t)t * rows + r] = acc;
+        }
+    }
+}

@@ -61,6 +61,7 @@ def port():
         _port.orc_round_bf16.argtypes = [_F, ctypes.c_size_t]
         _port.orc_kv_quantize.argtypes = [_F, i, i, _I8, _F]
         _port.orc_attend_decode_i8.argtypes = [_F, _I8, _F, _I8, _F, i, i, i, i, f, _F]
+        _port.orc_linear.argtypes = [_F, ctypes.c_void_p, _F, _F, i, i, i, i]
     return _port
 
 
@@ -86,6 +87,9 @@ def ref():
         _ref.ref_tinyllm_decode_time.argtypes = [i, i, i, i, ctypes.c_float, i, i, i]
         _ref.ref_tinyllm_decode_time.restype = ctypes.c_double
         _ref.ref_set_threads.argtypes = [i]
+        _ref.ref_linear.argtypes = [_F, ctypes.c_void_p, _F, _F, i, i, i, i]
+        _ref.ref_linear_time.argtypes = [_F, ctypes.c_void_p, _F, _F, i, i, i, i, i]
+        _ref.ref_linear_time.restype = ctypes.c_double
     return _ref
 
 
@@ -277,3 +281,80 @@ def deltanet_core_bf16_rule(qkv_raw, z, b_raw, a_raw, conv_state, S, conv_w, dt_
         o = o / np.sqrt((o * o).mean(-1, keepdims=True) + 1e-6) * np.asarray(norm_w, np.float64) * silu(zz[t])
         out[t] = o.ravel()
     return out
+
+
+# ------------------------------------------------------------------------------------------------
+# Projections: the engine's packed weight rows (src/eif_qwen35.c:110-116) and linear_gemv / linear_gemm /
+# int8_gemv (src/eif_qwen35.c:384-443, 1033-1063)
+# ------------------------------------------------------------------------------------------------
+
+W_F32, W_INT4, W_TERNARY2, W_TERNARY_DENSE, W_INT8 = 0, 1, 2, 3, 4
+
+
+def row_bytes(cols, base):
+    return {0: 4 * cols, 1: (cols + 1) // 2, 2: (cols + 3) // 4, 3: (cols + 4) // 5}.get(base, cols)
+
+
+def pack_weights(values, base, rng=None):
+    """Pack a [rows][cols] array of weight values into the engine's row layout of quant type `base`:
+    fp32 values as they are; INT4 values in [-8, 7] (even column in the high nibble, value + 8); 2-bit ternary
+    values in {-1, 0, 1} (column c at bits 2(c mod 4), +1 -> code 1, -1 -> code 2, 0 -> code 0, or code 3 at
+    random when `rng` is given: the reference reads code 3 as 0); dense ternary in {-1, 0, 1} (five base-3 digits
+    a byte, least significant first, +1 -> 1, -1 -> 2); INT8 values in [-128, 127]."""
+    v = np.asarray(values)
+    rows, cols = v.shape
+    if base == 0:
+        return np.ascontiguousarray(v, dtype=np.float32).view(np.uint8).reshape(rows, 4 * cols)
+    if base == 4:
+        return np.ascontiguousarray(v.astype(np.int8)).view(np.uint8)
+    out = np.zeros((rows, row_bytes(cols, base)), dtype=np.uint8)
+    vi = v.astype(np.int64)
+    if base == 1:
+        nib = (vi + 8).astype(np.uint8)
+        out[:, :] = 0
+        out[:, : (cols + 1) // 2] |= (nib[:, 0::2] << 4).astype(np.uint8)
+        out[:, : cols // 2] |= nib[:, 1::2]
+        return out
+    if base == 2:
+        code = np.where(vi == 1, 1, np.where(vi == -1, 2, 0)).astype(np.uint8)
+        if rng is not None:
+            code = np.where((vi == 0) & (rng.random(vi.shape) < 0.5), 3, code).astype(np.uint8)
+        for q in range(4):
+            part = code[:, q::4]
+            out[:, : part.shape[1]] |= (part << (2 * q)).astype(np.uint8)
+        return out
+    digit = np.where(vi == 1, 1, np.where(vi == -1, 2, 0)).astype(np.int64)
+    acc = np.zeros((rows, out.shape[1]), dtype=np.int64)
+    for p in range(5):
+        part = digit[:, p::5]
+        acc[:, : part.shape[1]] += part * 3 ** p
+    return acc.astype(np.uint8)
+
+
+def _linear_call(fn, W, scales, x, rows, cols, quant_type):
+    W = np.ascontiguousarray(W, dtype=np.uint8)
+    x = c32(x).reshape(-1, cols)
+    sc = None if scales is None else c32(scales)
+    out = np.zeros((x.shape[0], rows), dtype=np.float32)
+    fn(_fp(out), W.ctypes.data_as(ctypes.c_void_p), _fp(sc), _fp(x), x.shape[0], rows, cols, quant_type)
+    return out
+
+
+def linear(W, scales, x, rows, cols, quant_type):
+    """out[n][rows] = W x[t] (the port of linear_gemv / int8_gemv in each kernel's scalar order)."""
+    return _linear_call(port().orc_linear, W, scales, x, rows, cols, quant_type)
+
+
+def ref_linear(W, scales, x, rows, cols, quant_type):
+    """The reference's own linear_gemv (one token), linear_gemm (several) or int8_gemv (quant type 4)."""
+    return _linear_call(ref().ref_linear, W, scales, x, rows, cols, quant_type)
+
+
+def ref_linear_time(W, scales, x, rows, cols, quant_type, reps):
+    """Seconds the reference's projection takes for `reps` calls on these inputs."""
+    W = np.ascontiguousarray(W, dtype=np.uint8)
+    x = c32(x).reshape(-1, cols)
+    sc = None if scales is None else c32(scales)
+    out = np.zeros((x.shape[0], rows), dtype=np.float32)
+    return ref().ref_linear_time(_fp(out), W.ctypes.data_as(ctypes.c_void_p), _fp(sc), _fp(x), x.shape[0], rows,
+                                 cols, quant_type, reps)

@@ -278,3 +278,29 @@ REF_EXPORT void ref_set_threads(int n)
     (void)n;
 #endif
 }
+
+/* The projections as the engine runs them: linear_gemv (src/eif_qwen35.c:422-443) for one token, linear_gemm
+ * (:1033-1063) for n > 1, and the INT8 LM head int8_gemv (:384-420) token by token (quant type 4). */
+REF_EXPORT void ref_linear(float *out, const void *W, const float *sc, const float *x, int n, int rows, int cols,
+                           int quant_type)
+{
+    if (quant_type == 4) {
+        for (int t = 0; t < n; t++)
+            int8_gemv(out + (size_t)t * rows, (const int8_t *)W, sc, x + (size_t)t * cols, rows, cols);
+    } else if (n == 1) {
+        linear_gemv(out, W, sc, x, rows, cols, quant_type);
+    } else {
+        linear_gemm(out, W, sc, x, n, rows, cols, quant_type);
+    }
+}
+
+/* Seconds for `reps` calls of ref_linear (the CPU baseline of the projection workload). */
+REF_EXPORT double ref_linear_time(float *out, const void *W, const float *sc, const float *x, int n, int rows,
+                                  int cols, int quant_type, int reps)
+{
+    struct timespec a, b;
+    clock_gettime(CLOCK_MONOTONIC, &a);
+    for (int i = 0; i < reps; i++) ref_linear(out, W, sc, x, n, rows, cols, quant_type);
+    clock_gettime(CLOCK_MONOTONIC, &b);
+    return (double)(b.tv_sec - a.tv_sec) + 1e-9 * (double)(b.tv_nsec - a.tv_nsec);
+}

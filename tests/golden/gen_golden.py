@@ -22,6 +22,10 @@ reference without the reference being present.
                         steps of a one-layer model whose attention is observable (oracle/ref_shim.c,
                         ref_tinyllm_decode_steps): RoPE (:481-507), the cache write -- fp32, or INT8 codes
                         and scales (:509-553) -- and the attention output (:555-656)
+  linear_formats.npz    linear_gemv (one token) and linear_gemm (several) of src/eif_qwen35.c:422-443, 1033-1063
+                        for every weight format -- fp32, INT4, 2-bit ternary (a scale a row, and grouped
+                        scales; code-3 bytes included), dense base-3 ternary -- and int8_gemv (:384-420),
+                        at ragged widths (cols not a multiple of the weights a byte)
 
     python tests/golden/gen_golden.py [fixture-name ...]   # default: every fixture
 """
@@ -173,6 +177,49 @@ FIXTURES = {
     "tinyllm_int8_hd256.npz": lambda: gen_tinyllm("tinyllm_int8_hd256.npz", 1010, 2, 1, 256, 24, 5e5, 0, 1,
                                                   [0, 3, 9, 21, 23]),
 }
+
+
+LINEAR_CASES = [  # name, quant_type, rows, cols, n
+    ("f32", 0, 24, 96, 1), ("f32_n3", 0, 24, 96, 3),
+    ("int4", 1, 24, 97, 1), ("int4_n5", 1, 24, 97, 5),
+    ("tern2", 2, 24, 130, 1), ("tern2_n5", 2, 24, 130, 5),
+    ("tern2_g32", 2 | (32 << 8), 24, 128, 1), ("tern2_g32_n5", 2 | (32 << 8), 24, 128, 5),
+    ("dense", 3, 24, 101, 1), ("dense_n5", 3, 24, 101, 5),
+    ("int8", 4, 24, 96, 1), ("int8_n3", 4, 24, 96, 3),
+]
+
+
+def linear_case(rng, quant_type, rows, cols, n):
+    """Seeded weights of the format (values, packed rows, scales) and n input tokens."""
+    base, group = quant_type & 0xFF, quant_type >> 8
+    if base == 0:
+        v = (0.05 * rng.standard_normal((rows, cols))).astype(np.float32)
+    elif base == 1:
+        v = rng.integers(-8, 8, (rows, cols))
+    elif base == 4:
+        v = rng.integers(-128, 128, (rows, cols))
+    else:
+        v = rng.integers(-1, 2, (rows, cols))
+    W = orc.pack_weights(v, base, rng if base == 2 else None)
+    sc = None if base == 0 else (0.01 + 0.1 * rng.random((rows, cols // group) if group else rows)).astype(np.float32)
+    x = rng.standard_normal((n, cols)).astype(np.float32)
+    return v, W, sc, x
+
+
+def gen_linear(seed):
+    rng = np.random.default_rng(seed)
+    arrays = {}
+    for name, qt, rows, cols, n in LINEAR_CASES:
+        _, W, sc, x = linear_case(rng, qt, rows, cols, n)
+        arrays[f"{name}_W"] = W
+        arrays[f"{name}_sc"] = sc if sc is not None else np.zeros(0, np.float32)
+        arrays[f"{name}_x"] = x
+        arrays[f"{name}_out"] = orc.ref_linear(W, sc, x, rows, cols, qt)
+        arrays[f"{name}_shape"] = np.array([qt, rows, cols, n], np.int64)
+    np.savez(os.path.join(HERE, "linear_formats.npz"), **arrays)
+
+
+FIXTURES["linear_formats.npz"] = lambda: gen_linear(1100)
 
 
 def main():

@@ -179,3 +179,58 @@ def test_rope_table_folded_form(orc):
                 vals = [f32(pos) * f for f in freq]
                 assert np.array_equal(c, np.array([libm.cosf(v) for v in vals], f32)), (theta, hd, pos)
                 assert np.array_equal(s, np.array([libm.sinf(v) for v in vals], f32)), (theta, hd, pos)
+
+
+# ------------------------------------------------------------------------------------------------
+# Projections (linear_gemv / linear_gemm / int8_gemv, src/eif_qwen35.c:384-443, 1033-1063)
+# ------------------------------------------------------------------------------------------------
+
+LINEAR_NAMES = ["f32", "f32_n3", "int4", "int4_n5", "tern2", "tern2_n5", "tern2_g32", "tern2_g32_n5", "dense",
+                "dense_n5", "int8", "int8_n3"]
+
+
+def linear_golden(name):
+    d = golden("linear_formats.npz")
+    qt, rows, cols, n = (int(v) for v in d[f"{name}_shape"])
+    sc = d[f"{name}_sc"]
+    return qt, rows, cols, n, d[f"{name}_W"], (sc if sc.size else None), d[f"{name}_x"], d[f"{name}_out"]
+
+
+@pytest.mark.parametrize("name", LINEAR_NAMES)
+def test_linear_golden(orc, name):
+    """The restatement against the reference's own projections on every weight format (rel-L2 <= 1e-5: both
+    sum in fp32, in different orders; a decoding mistake is O(1))."""
+    qt, rows, cols, n, W, sc, x, out = linear_golden(name)
+    assert rel_l2(orc.linear(W, sc, x, rows, cols, qt), out) <= 1e-5
+
+
+@pytest.mark.parametrize("base", [0, 1, 2, 3, 4])
+def test_linear_pack_decode_exact(orc, base):
+    """Packing and the restatement's decoding are inverse: integer weights and inputs with a power-of-two scale
+    give the exact integer product (every partial sum is an integer below 2^24)."""
+    rng = np.random.default_rng(70 + base)
+    rows, cols = 19, 203
+    lo, hi = {0: (-8, 8), 1: (-8, 8), 4: (-128, 128)}.get(base, (-1, 2))
+    v = rng.integers(lo, hi, (rows, cols))
+    W = orc.pack_weights(v.astype(np.float32) if base == 0 else v, base, rng if base == 2 else None)
+    sc = None if base == 0 else np.full(rows, 0.5, np.float32)
+    x = rng.integers(-4, 5, (3, cols)).astype(np.float32)
+    want = (x.astype(np.int64) @ v.T.astype(np.int64)).astype(np.float64) * (1.0 if base == 0 else 0.5)
+    assert np.array_equal(orc.linear(W, sc, x, rows, cols, base).astype(np.float64), want)
+
+
+def test_port_vs_reference_linear_random(orc):
+    """Where the reference build is present: the restatement against it at a Qwen3.5 projection width."""
+    if not orc.ref_available():
+        pytest.skip("reference build absent")
+    rng = np.random.default_rng(71)
+    for qt, rows, cols in [(2, 96, 1024), (2 | (64 << 8), 96, 1024), (1, 64, 2048), (3, 64, 1024), (4, 128, 1024),
+                           (0, 64, 1024)]:
+        base, group = qt & 0xFF, qt >> 8
+        v = (rng.integers(-1, 2, (rows, cols)) if base in (2, 3) else rng.integers(-8, 8, (rows, cols)) if base == 1
+             else rng.integers(-128, 128, (rows, cols)) if base == 4 else rng.standard_normal((rows, cols)) * 0.05)
+        W = orc.pack_weights(v, base, rng if base == 2 else None)
+        sc = None if base == 0 else (0.01 + rng.random((rows, cols // group) if group else rows)).astype(np.float32)
+        for n in (1, 6):
+            x = rng.standard_normal((n, cols)).astype(np.float32)
+            assert rel_l2(orc.linear(W, sc, x, rows, cols, qt), orc.ref_linear(W, sc, x, rows, cols, qt)) <= 1e-5, qt
