@@ -2017,7 +2017,7 @@ EIF_API eif_status_t eif_cuda_linear_upload(eif_cuda_ctx_t *ctx, int quant_type,
     if (group > 0 && (wt != EIF_CUDA_W_TERNARY2 || group % 16 || cols % group))
         return fail(ctx, EIF_STATUS_NOT_SUPPORTED,
                     "linear: scale group %d (2-bit ternary only, a multiple of 16 dividing cols %d)", group, cols);
-    const size_t row_bytes = linear_row_bytes(wt, cols), stride = (row_bytes + 15) & ~(size_t)15;
+    const size_t row_bytes = linear_row_bytes(wt, cols), stride = (row_bytes + 63) & ~(size_t)63;
     if (!linear_fits(wt, stride))
         return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "linear: %d columns exceed the shared-memory token tile", cols);
     DeviceGuard g(ctx);

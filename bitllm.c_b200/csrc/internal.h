@@ -241,8 +241,8 @@ size_t decode_workspace_bytes(const DecodeArgs &a, int sm_count);
 void decode_plan(const DecodeArgs &a, int sm_count, int *nchunk, int *chunk_keys, size_t *ws_bytes);
 // Query rows of a prefill chunk as decode rows: row i = token i % n_tok of sequence i / n_tok at start_pos + i % n_tok.
 cudaError_t launch_prefill_rows(cudaStream_t st, int *row_seq, int *pos, int batch, int n_tok, int start_pos);
-// A projection's weights on the device (linear.cu): the engine's packed rows, each padded to `stride` bytes (a
-// multiple of 16), and the scales (rows x n_scales_row floats; none for fp32).
+// A projection's weights on the device (linear.cu): the engine's packed rows, each padded with zeros to `stride`
+// bytes (a multiple of 64), and the scales (rows x n_scales_row floats; none for fp32).
 struct eif_cuda_linear {
     eif_cuda_ctx_t *ctx = nullptr;
     int wtype = 0, group = 0, rows = 0, cols = 0;
@@ -255,9 +255,13 @@ struct eif_cuda_linear {
 size_t linear_row_bytes(int wtype, int cols);
 // Whether a row of `stride` bytes fits the kernel's shared-memory token tile.
 bool linear_fits(int wtype, size_t stride);
-// out[t][rows] = W x[t] for n tokens (fp32 device arrays).
+// out[t][rows] = W x[t] for n tokens (fp32 device arrays): the tensor-core kernel where it supports the format and
+// n >= 4 (linear_mma.cu), else the CUDA-core kernel (linear.cu).
 cudaError_t launch_linear(cudaStream_t st, const eif_cuda_linear &lin, const float *x, int n, float *out,
                           int sm_count);
+bool linear_mma_supported(const eif_cuda_linear &lin);
+cudaError_t launch_linear_mma(cudaStream_t st, const eif_cuda_linear &lin, const float *x, int n, float *out,
+                              int sm_count);
 // Bytes of the fixed scratch array of eif_cuda_attend_decode_noalloc_dev (noalloc.cu).
 size_t noalloc_scratch_capacity();
 cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws, size_t ws_bytes, int sm_count,

@@ -6,11 +6,14 @@
 // dense base-3 ternary (bitnet_gemv_dense, src/eif_qwen35.c:148-180) -- its batched twin linear_gemm (:1033-1063)
 // and the INT8 LM head int8_gemv (:384-420).
 //
-// Device layout: the engine's packed rows, each padded with zero bytes to a multiple of 16, so that a warp reads
-// a row as aligned 4-byte words, 128 contiguous bytes an instruction.
+// Device layout: the engine's packed rows, each padded with zero bytes to a multiple of 64, so that a warp reads
+// a row as aligned 4-byte words, 128 contiguous bytes an instruction.  This kernel serves the formats the
+// tensor-core kernel of linear_mma.cu does not: fp32 weights, grouped 2-bit scales and dense ternary.
 //
 // Kernel: one warp per group of R = 4 rows, lane l taking words l, l + 32, ... of the four rows (U words of each
-// row in flight per lane).  A tile of T tokens (1, 2, 4 or 8) sits in shared memory token-minor, [column][T] in
+// row a work item; the next item's words are in flight while the current one is computed).  Launched as a
+// programmatic dependent: each CTA fetches its first weights before waiting for the previous kernel, so a chain of
+// small projections overlaps one launch's tail with the next one's weight stream.  A tile of T tokens (1, 2, 4 or 8) sits in shared memory token-minor, [column][T] in
 // planes of up to four tokens, with one empty slot after each word's columns: lane l's column c = w * CPW + i
 // then lands in bank (w * (CPW + 1) + i) mod 32, distinct across the warp because CPW + 1 is odd.
 // Each weight is decoded once per tile and meets the T tokens with T FMAs.  Decoding builds the float directly:
@@ -51,8 +54,13 @@ __device__ __forceinline__ int xslot(int c) {
     return CPW == 1 ? c : c + c / CPW;
 }
 
+// floats of the staged token tile, rounded to 16 bytes
+__host__ __device__ constexpr int tile_floats(int wt, int n_words, int T) { return (x_slots(wt, n_words) * T + 3) / 4 * 4; }
+
+// the tile, the dense table and the slices' sums ([kWarps][4 T] floats)
 size_t tile_smem(int wt, int n_words, int T) {
-    return (size_t)x_slots(wt, n_words) * T * sizeof(float) + (wt == EIF_CUDA_W_TERNARY_DENSE ? kDenseLut : 0);
+    return (size_t)tile_floats(wt, n_words, T) * sizeof(float) + (wt == EIF_CUDA_W_TERNARY_DENSE ? kDenseLut : 0) +
+           (size_t)kWarps * kRows * T * sizeof(float);
 }
 
 // tokens a tile: the largest of 8, 4, 2, 1 not above n whose tile fits in shared memory (0: none fits)
@@ -61,6 +69,11 @@ int pick_tile(int wt, int n_words, int n) {
     while (T > 1 && tile_smem(wt, n_words, T) > kSmemCap) T >>= 1;
     return tile_smem(wt, n_words, T) <= kSmemCap ? T : 0;
 }
+
+// Programmatic dependent launch (sm_90+): let the next kernel on the stream begin launching its CTAs, and wait
+// until the previous kernel has completed with its memory visible (a no-op when launched without the attribute).
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // the float of the integer field in byte j of `bytes`, minus the bias (bias_2p23 = 2^23 + bias)
 __device__ __forceinline__ float field_float(uint32_t bytes, int j, float bias_2p23) {
@@ -162,10 +175,11 @@ struct LinArgs {
     size_t stride;   // bytes between padded rows
     int group;       // grouped ternary: columns a scale (a multiple of 16), else 0
     int n_scales_row;
+    int ks;          // column slices: the CTA's 8 warps are 8 / ks row-group lanes x ks slices of the words
 };
 
 template <int WT, int T, bool GROUPED>
-__global__ void __launch_bounds__(kThreads) linear_kernel(const LinArgs a) {
+__global__ void __launch_bounds__(kThreads, T == 1 ? 3 : 1) linear_kernel(const LinArgs a) {
     constexpr int CPW = cols_per_word(WT);
     constexpr int K = kRows * T;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -175,6 +189,29 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const LinArgs a) {
     const int n_groups = (a.rows + kRows - 1) / kRows;
     const int n_slots = x_slots(WT, a.n_words);
     const int n_cols = a.n_words * CPW;  // columns of the padded rows (those past `cols` meet zeros)
+    // The CTA's warps: RG row-group lanes x KS column slices.  A warp's work items: (row group g, word block it)
+    // for g = g0, g0 + gstride, ... and it over its slice's blocks of 32 * U words (the same count for every slice,
+    // so the slices of a row group meet at its end together).  Item j + 1's weights are loaded while item j is
+    // computed, across groups and tiles.
+    const int KS = a.ks, RG = kWarps / KS, rg = warp / KS, ks = warp - rg * KS;
+    const int wps = (a.n_words + KS - 1) / KS, w_begin = ks * wps, w_end = min(a.n_words, w_begin + wps);
+    const int g0 = blockIdx.x * RG + rg, gstride = gridDim.x * RG;
+    const int ipg = (wps + 32 * kUnroll - 1) / (32 * kUnroll);
+    const int n_items = g0 < n_groups ? (n_groups - g0 + gstride - 1) / gstride * ipg : 0;
+    auto load = [&](int j, uint32_t (&raw)[kUnroll][kRows]) {
+        const int g = g0 + (j / ipg) * gstride, w0 = w_begin + lane + (j % ipg) * 32 * kUnroll;
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            const uint32_t *wr = reinterpret_cast<const uint32_t *>(a.W + (size_t)min(g * kRows + r, a.rows - 1) * a.stride);
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) raw[u][r] = (w0 + 32 * u < w_end) ? __ldg(wr + w0 + 32 * u) : 0u;
+        }
+    };
+    float *red = xs + tile_floats(WT, a.n_words, T);  // [kWarps][K] the slices' sums
+    uint32_t raw[kUnroll][kRows];
+    if (n_items > 0) load(0, raw);  // the weights do not depend on the previous kernel: fetch before waiting
+    griddep_launch_dependents();
+    griddep_wait();  // x is the previous kernel's output
     if constexpr (WT == EIF_CUDA_W_TERNARY_DENSE) {
         for (int b = threadIdx.x; b < 256; b += kThreads) {
             uint32_t e = 0, v = b;
@@ -187,6 +224,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const LinArgs a) {
             dlut[b] = e;
         }
     }
+    float acc[K];
     for (int t0 = 0; t0 < a.n; t0 += T) {
         __syncthreads();  // the previous tile's readers are done
         for (int c = threadIdx.x; c < n_cols; c += kThreads) {
@@ -197,73 +235,83 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const LinArgs a) {
             store_tile<T>(xs, n_slots, xslot<CPW>(c), v);
         }
         __syncthreads();
-        for (int g = blockIdx.x * kWarps + warp; g < n_groups; g += gridDim.x * kWarps) {
-            const int r0 = g * kRows;
-            const uint32_t *wr[kRows];
+        const bool more_tiles = t0 + T < a.n;
+        for (int j = 0; j < n_items; ++j) {
+            const int it = j % ipg, g = g0 + (j / ipg) * gstride, r0 = g * kRows;
+            uint32_t nxt[kUnroll][kRows];
+            if (j + 1 < n_items)
+                load(j + 1, nxt);
+            else if (more_tiles)
+                load(0, nxt);
+            if (it == 0) {
 #pragma unroll
-            for (int r = 0; r < kRows; ++r)
-                wr[r] = reinterpret_cast<const uint32_t *>(a.W + (size_t)min(r0 + r, a.rows - 1) * a.stride);
-            float acc[K];
+                for (int k = 0; k < K; ++k) acc[k] = 0.f;
+            }
+            const int w0 = w_begin + lane + it * 32 * kUnroll;
 #pragma unroll
-            for (int k = 0; k < K; ++k) acc[k] = 0.f;
-            for (int w0 = lane; w0 < a.n_words; w0 += 32 * kUnroll) {
-                uint32_t raw[kUnroll][kRows];
+            for (int u = 0; u < kUnroll; ++u) {
+                const int w = w0 + 32 * u;
+                if (w >= w_end) break;
+                Word<WT> wd[kRows];
 #pragma unroll
-                for (int u = 0; u < kUnroll; ++u)
+                for (int r = 0; r < kRows; ++r) wd[r].prepare(raw[u][r], dlut);
+                float part[K];
 #pragma unroll
-                    for (int r = 0; r < kRows; ++r)
-                        raw[u][r] = (w0 + 32 * u < a.n_words) ? __ldg(wr[r] + w0 + 32 * u) : 0u;
+                for (int k = 0; k < K; ++k) part[k] = 0.f;
 #pragma unroll
-                for (int u = 0; u < kUnroll; ++u) {
-                    const int w = w0 + 32 * u;
-                    if (w >= a.n_words) break;
-                    Word<WT> wd[kRows];
+                for (int i = 0; i < CPW; ++i) {
+                    float xv[T];
+                    load_tile<T>(xs, n_slots, xslot<CPW>(w * CPW + i), xv);
 #pragma unroll
-                    for (int r = 0; r < kRows; ++r) wd[r].prepare(raw[u][r], dlut);
-                    float part[K];
+                    for (int r = 0; r < kRows; ++r) {
+                        const float wv = wd[r](i);
 #pragma unroll
-                    for (int k = 0; k < K; ++k) part[k] = 0.f;
-#pragma unroll
-                    for (int i = 0; i < CPW; ++i) {
-                        float xv[T];
-                        load_tile<T>(xs, n_slots, xslot<CPW>(w * CPW + i), xv);
-#pragma unroll
-                        for (int r = 0; r < kRows; ++r) {
-                            const float wv = wd[r](i);
-#pragma unroll
-                            for (int t = 0; t < T; ++t) {
-                                float &d = GROUPED ? part[r * T + t] : acc[r * T + t];
-                                d = fmaf(wv, xv[t], d);
-                            }
-                        }
-                    }
-                    if constexpr (GROUPED) {  // the word's 16 columns share one group's scale
-                        const int grp = (w * CPW) / a.group;
-#pragma unroll
-                        for (int r = 0; r < kRows; ++r) {
-                            const float s = (r0 + r < a.rows && grp < a.n_scales_row)
-                                                ? __ldg(a.scales + (size_t)(r0 + r) * a.n_scales_row + grp) : 0.f;
-#pragma unroll
-                            for (int t = 0; t < T; ++t) acc[r * T + t] = fmaf(s, part[r * T + t], acc[r * T + t]);
+                        for (int t = 0; t < T; ++t) {
+                            float &d = GROUPED ? part[r * T + t] : acc[r * T + t];
+                            d = fmaf(wv, xv[t], d);
                         }
                     }
                 }
-            }
-            const float tot = warp_transpose_sum<K>(acc, lane);
-            constexpr int per = 32 / K;  // lanes holding each total
-            if ((lane & (per - 1)) == 0) {
-                const int idx = lane / per, r = idx / T, t = idx % T, row = r0 + r;
-                if (row < a.rows && t0 + t < a.n) {
-                    const float s = (WT == EIF_CUDA_W_F32 || GROUPED) ? 1.f : __ldg(a.scales + row);
-                    a.out[(size_t)(t0 + t) * a.rows + row] = tot * s;
+                if constexpr (GROUPED) {  // the word's 16 columns share one group's scale
+                    const int grp = (w * CPW) / a.group;
+#pragma unroll
+                    for (int r = 0; r < kRows; ++r) {
+                        const float s = (r0 + r < a.rows && grp < a.n_scales_row)
+                                            ? __ldg(a.scales + (size_t)(r0 + r) * a.n_scales_row + grp) : 0.f;
+#pragma unroll
+                        for (int t = 0; t < T; ++t) acc[r * T + t] = fmaf(s, part[r * T + t], acc[r * T + t]);
+                    }
                 }
             }
+            if (it == ipg - 1) {
+                float tot = warp_transpose_sum<K>(acc, lane);
+                constexpr int per = 32 / K;  // lanes holding each total
+                const int idx = lane / per;
+                if (KS > 1) {  // the row group's slices meet in shared memory; slice 0 writes
+                    if ((lane & (per - 1)) == 0) red[warp * K + idx] = tot;
+                    asm volatile("bar.sync %0, %1;" ::"r"(1 + rg), "r"(32 * KS) : "memory");
+                    if (ks == 0)
+                        for (int k2 = 1; k2 < KS; ++k2) tot += red[(warp + k2) * K + idx];
+                }
+                if (ks == 0 && (lane & (per - 1)) == 0) {
+                    const int r = idx / T, t = idx % T, row = r0 + r;
+                    if (row < a.rows && t0 + t < a.n) {
+                        const float s = (WT == EIF_CUDA_W_F32 || GROUPED) ? 1.f : __ldg(a.scales + row);
+                        a.out[(size_t)(t0 + t) * a.rows + row] = tot * s;
+                    }
+                }
+                if (KS > 1) asm volatile("bar.sync %0, %1;" ::"r"(1 + rg), "r"(32 * KS) : "memory");
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+                for (int r = 0; r < kRows; ++r) raw[u][r] = nxt[u][r];
         }
     }
 }
 
 template <int WT, int T, bool G>
-cudaError_t go(cudaStream_t st, const LinArgs &a, size_t smem, int sm_count) {
+cudaError_t go(cudaStream_t st, LinArgs a, size_t smem, int sm_count) {
     auto kernel = linear_kernel<WT, T, G>;
     static unsigned long long raised = 0;  // devices on which the dynamic shared-memory limit is at the cap
     int dev = 0;
@@ -275,11 +323,28 @@ cudaError_t go(cudaStream_t st, const LinArgs &a, size_t smem, int sm_count) {
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem) != cudaSuccess || per_sm < 1)
         per_sm = 1;
+    // column slices: enough warps to fill the GPU twice over where the row groups alone do not, each slice
+    // at least 32 words (a word a lane)
     const int n_groups = (a.rows + kRows - 1) / kRows;
-    int grid = (n_groups + kWarps - 1) / kWarps;
+    int ks = 1;
+    while (ks < kWarps && n_groups * ks < 2 * kWarps * sm_count && a.n_words >= 32 * 2 * ks) ks *= 2;
+    a.ks = ks;
+    const int rg = kWarps / ks;
+    int grid = (n_groups + rg - 1) / rg;
     if (grid > per_sm * sm_count) grid = per_sm * sm_count;
-    kernel<<<grid, kThreads, smem, st>>>(a);
-    return cudaGetLastError();
+    // programmatic dependent launch: the CTAs may start while the previous kernel on the stream drains; each one
+    // loads its first weights and then waits for that kernel's completion (griddepcontrol.wait) before reading x
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, a);
 }
 
 template <int WT, bool G>
@@ -308,8 +373,11 @@ bool linear_fits(int wtype, size_t stride) { return pick_tile(wtype, (int)(strid
 
 cudaError_t launch_linear(cudaStream_t st, const eif_cuda_linear &lin, const float *x, int n, float *out,
                           int sm_count) {
+    // a few tokens: the CUDA-core kernel (its decode per weight is cheaper than the tensor-core kernel's x staging
+    // and hi / lo split); from four tokens on, the tensor cores
+    if (n >= 4 && linear_mma_supported(lin)) return launch_linear_mma(st, lin, x, n, out, sm_count);
     const LinArgs a{lin.W, lin.scales, x, out, lin.rows, lin.cols, n, (int)(lin.stride / 4), lin.stride,
-                    lin.group, lin.n_scales_row};
+                    lin.group, lin.n_scales_row, 1};
     const int T = pick_tile(lin.wtype, a.n_words, n);
     if (T == 0) return cudaErrorInvalidValue;
     const size_t smem = tile_smem(lin.wtype, a.n_words, T);
