@@ -1371,6 +1371,7 @@ def run_projection(args, torch, dist, rank, world, local_rank):
     ach = tern_bytes / (tern_ms * 1e-3) / 1e9
     head_ach = head_bytes / (head_ms * 1e-3) / 1e9
     tr, tr_src = traffic("linear_ternary2", tern_bytes)
+    kname = "linear_mma_kernel" if n >= 4 else "linear_kernel"  # the library's choice: tensor cores from 4 tokens
     line = {"metric": "projection tokens/s (every quantised projection of a Qwen3.5-0.8B decode step)",
             "value": n * world / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -1386,11 +1387,11 @@ def run_projection(args, torch, dist, rank, world, local_rank):
                 "value": n * world / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": xh.numel() * 4 * world, "d2h_bytes_per_step": lh.numel() * 4 * world,
                 "path": "pinned input copied in, the step's eif_cuda_linear_forward_dev graph, logits copied out"},
-            "roofline": {"kernel": "linear_kernel (2-bit ternary, the 96 layer launches)", "bound": "hbm",
+            "roofline": {"kernel": f"{kname} (2-bit ternary, the 96 layer launches)", "bound": "hbm",
                          "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm, "peak_source": src,
                          "algorithmic_bytes_per_launch": tern_bytes / len(tern), "launch_ms": tern_ms / len(tern),
                          "traffic": None if tr is None else tr / len(tern), "traffic_source": tr_src},
-            "lm_head": {"kernel": "linear_kernel (INT8, 248320 x 1024)", "achieved": head_ach, "frac": head_ach / hbm,
+            "lm_head": {"kernel": f"{kname} (INT8, 248320 x 1024)", "achieved": head_ach, "frac": head_ach / hbm,
                         "launch_ms": head_ms, "algorithmic_bytes": head_bytes},
             "gpu_launches": len(shapes) * args.steps, "clocks": clk}
     if world == 1 and not args.no_cpu_baseline:
@@ -1399,7 +1400,7 @@ def run_projection(args, torch, dist, rank, world, local_rank):
     return line
 
 
-WORKLOADS = [  # (key, workload, overrides): BASELINE configs[0..3] and config 1's heads batched per cache type
+WORKLOADS = [  # (key, workload, overrides): BASELINE configs[0..3], config 1's heads batched per cache type, f4
     ("config1_decode", "decode", dict(batch=1, ctx=512, kv="f32")),
     ("config2_prefill", "prefill", {}),
     ("config3_recurrent", "recurrent", {}),
@@ -1410,9 +1411,12 @@ WORKLOADS = [  # (key, workload, overrides): BASELINE configs[0..3] and config 1
     # the Qwen3.5 attention mixer on the reference's own fp32 cache and on bf16 (config 5's heads)
     ("qwen35_attention_f32", "decode", dict(batch=64, ctx=32768, kv="f32", heads="qwen35")),
     ("qwen35_attention_bf16", "decode", dict(batch=64, ctx=32768, kv="bf16", heads="qwen35")),
+    # row f4: every projection of a Qwen3.5-0.8B decode step, one token and sixteen
+    ("projection_decode_b1", "projection", dict(batch=1)),
+    ("projection_decode_b16", "projection", dict(batch=16)),
 ]
 _KEEP = ("metric", "value", "unit", "ms_per_step", "dtype", "config", "roofline", "e2e", "cpu_baseline", "gpu_launches",
-         "clocks", "step_path")
+         "clocks", "step_path", "lm_head", "step_hbm_frac")
 
 
 def run_workloads(args, torch, local_rank):
