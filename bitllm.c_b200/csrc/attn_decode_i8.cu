@@ -45,15 +45,20 @@ constexpr int HS = 8;           // head slots: MMA rows g (high part) and g + 8 
 constexpr float kPScale = 4096.f, kPUnscale = 1.f / 4096.f;
 
 // NG consumer groups take alternate tiles (more tiles in flight per SM where the registers allow).
-template <int D, int NG>
+// KH kv heads a stage: 2 ("pair" mode, head_dim 64 with an even kv-head count) puts both halves of every 128-byte
+// cache row in one stage, so a tile streams whole rows (a stage of one head's 64-byte halves leaves the other
+// halves of the same DRAM pages to another CTA later, which caps the stream near 0.57 of the copy peak); the
+// consumer groups then split by head.
+template <int D, int NG, int KH>
 struct I8Cfg {
     static constexpr int NW = kGroup * NG;            // consumer warps
+    static constexpr int TG = NG / KH;                // tiles in flight (consumer groups per tile: KH)
     static constexpr int THREADS = 32 * (NW + 1);
     static constexpr int BW = D >= 128 ? 128 : 64;    // box width in code bytes (= dims); the swizzle span
     static constexpr int BOX = 64 * BW;               // 64 keys x BW code bytes
-    static constexpr int TILE = (D / BW) * BOX;       // K (or V) tile bytes
-    static constexpr int STAGE = 2 * TILE;
-    static constexpr int SCALES = 2 * KT * 4;         // per stage: the K and V scales of the tile's keys
+    static constexpr int TILE = (D / BW) * BOX;       // K (or V) tile bytes of one head
+    static constexpr int STAGE = 2 * KH * TILE;       // [K head 0 .. KH-1][V head 0 .. KH-1]
+    static constexpr int SCALES = 2 * KH * KT * 4;    // per stage: [head][K, V][64 keys] scales
     static constexpr int EXTRA = NW * HS * D * 4              // merge buffer o
                                  + 2 * NW * HS * 4            // merge m, l
                                  + 64 * 8                     // barriers
@@ -62,9 +67,10 @@ struct I8Cfg {
     // a multiple of NG: consecutive uses of a stage within an item go to the same group, which has consumed
     // the previous use itself before it polls the next (a parity wait cannot tell use k from use k-2, and
     // TMA copies complete out of order)
-    static constexpr int NS = (NS_FIT > 16 ? 16 : NS_FIT) / NG * NG;
+    static constexpr int NS = (NS_FIT > 16 ? 16 : NS_FIT) / TG * TG;
     static constexpr int SMEM = NS * (STAGE + SCALES) + EXTRA;
-    static_assert(NS >= 2 && NS % NG == 0, "ring depth a multiple of the consumer groups");
+    static_assert(NS >= 2 && NS % TG == 0, "ring depth a multiple of the tiles in flight");
+    static_assert(NG % KH == 0, "consumer groups a multiple of the heads a stage");
 };
 
 struct I8Params {
@@ -81,14 +87,17 @@ struct I8Params {
 };
 
 struct ItemInfo {
-    int b, cb, kvh, t_begin, t_end, ntiles;  // b: query row, cb: its cache sequence
+    int b, cb, kvh, c, t_begin, t_end, ntiles;  // b: query row, cb: its cache sequence, kvh: first kv head, c: chunk
 };
 
+// item = ((row * (Hkv / KH)) + head group) * nchunk + chunk
+template <int KH>
 __device__ __forceinline__ ItemInfo item_info(const I8Params &p, int item, bool report) {
     ItemInfo it;
-    const int unit = item / p.nchunk, c = item - unit * p.nchunk;
-    it.b = unit / p.Hkv;
-    it.kvh = unit - it.b * p.Hkv;
+    const int unit = item / p.nchunk, c = item - unit * p.nchunk, hg = p.Hkv / KH;
+    it.b = unit / hg;
+    it.kvh = (unit - it.b * hg) * KH;
+    it.c = c;
     it.cb = p.row_seq ? p.row_seq[it.b] : it.b;
     int pp = p.pos[it.b];
     if (pp < 0 || pp >= p.max_len) {  // max_len = the caller's bound + 1, never above max_seq
@@ -141,16 +150,17 @@ __device__ __forceinline__ uint32_t tile_addr(uint32_t base, int key, int chunk)
         return base + (chunk >> 2) * 4096 + key * 64 + (((chunk & 3) ^ ((key >> 1) & 3)) << 4);
 }
 
-template <int D, int NG>
-__global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
+template <int D, int NG, int KH>
+__global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
     attn_decode_i8_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                           const I8Params p) {
-    using C = I8Cfg<D, NG>;
+    using C = I8Cfg<D, NG, KH>;
+    constexpr int TG = C::TG;
     constexpr int NS = C::NS, KS = D / 16, NT = D / 8, NW = C::NW;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_align1024(smem_raw);
-    float *sbuf = reinterpret_cast<float *>(smem + NS * C::STAGE);  // [NS][2][64] K, V scales per stage
-    float *ow = sbuf + NS * 2 * KT;                                 // [4][HS][D]
+    float *sbuf = reinterpret_cast<float *>(smem + NS * C::STAGE);  // [NS][KH][2][64] K, V scales per stage
+    float *ow = sbuf + NS * KH * 2 * KT;                            // [NW][HS][D]
     float *mw = ow + NW * HS * D;                                   // [NW][HS]
     float *lw = mw + NW * HS;                                       // [NW][HS]
     uint64_t *bars = reinterpret_cast<uint64_t *>(lw + NW * HS);
@@ -162,7 +172,7 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(full0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, kGroup);  // the 4 warps of the group that takes the tile
+            mbar_init(empty0 + 8 * s, kGroup * KH);  // the warps of the KH groups that take the tile
         }
         mbar_init(merged, NW);
         mbar_init(drained, NW);
@@ -179,7 +189,7 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
         prefetch_tmap(&tmV);
         uint32_t it = 0;
         for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
-            const ItemInfo inf = item_info(p, item, false);
+            const ItemInfo inf = item_info<KH>(p, item, false);
             for (int i = 0; i < inf.ntiles; ++i, ++it) {
                 const uint32_t s = it % NS, ph = (it / NS) & 1;
                 if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.dev_err)) return;
@@ -187,16 +197,19 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
                 const int t0 = inf.t_begin + i * KT;
                 const int row = inf.cb * p.max_seq + t0;
                 mbar_arrive_expect_tx(fb, C::STAGE + C::SCALES);
-                const uint32_t kdst = smem_u32(smem + s * C::STAGE), vdst = kdst + C::TILE;
+                const uint32_t kdst = smem_u32(smem + s * C::STAGE), vdst = kdst + KH * C::TILE;
 #pragma unroll
-                for (int j = 0; j < D / C::BW; ++j) {
-                    tma_load_3d(kdst + j * C::BOX, &tmK, j * C::BW, inf.kvh, row, fb);
-                    tma_load_3d(vdst + j * C::BOX, &tmV, j * C::BW, inf.kvh, row, fb);
+                for (int h = 0; h < KH; ++h) {
+#pragma unroll
+                    for (int j = 0; j < D / C::BW; ++j) {
+                        tma_load_3d(kdst + h * C::TILE + j * C::BOX, &tmK, j * C::BW, inf.kvh + h, row, fb);
+                        tma_load_3d(vdst + h * C::TILE + j * C::BOX, &tmV, j * C::BW, inf.kvh + h, row, fb);
+                    }
+                    const size_t srow = ((size_t)inf.cb * p.Hkv + inf.kvh + h) * p.sstride + t0;
+                    const uint32_t sdst = smem_u32(sbuf + (s * KH + h) * 2 * KT);
+                    bulk_load(sdst, p.ks + srow, KT * 4, fb);
+                    bulk_load(sdst + KT * 4, p.vs + srow, KT * 4, fb);
                 }
-                const size_t srow = ((size_t)inf.cb * p.Hkv + inf.kvh) * p.sstride + t0;
-                const uint32_t sdst = smem_u32(sbuf + s * 2 * KT);
-                bulk_load(sdst, p.ks + srow, KT * 4, fb);
-                bulk_load(sdst + KT * 4, p.vs + srow, KT * 4, fb);
             }
         }
         return;
@@ -206,15 +219,16 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
     const int g = lane >> 2, t = lane & 3;
     const int mi = lane >> 3, mr = lane & 7;               // ldmatrix: matrix / row this lane addresses
     const int grp = warp / kGroup, wk = (warp % kGroup) * 16;  // group; first tile row of this warp's keys
+    const int tg = grp / KH, hh = grp - tg * KH;                 // the group's tile slot and head within the stage
     const int my_key = wk + (mi & 1) * 8 + mr;             // tile row (key) of this lane's ldmatrix rows
     uint32_t it_base = 0, item_no = 0;
     for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++item_no) {
-        const ItemInfo inf = item_info(p, item, warp == 0 && lane == 0);
+        const ItemInfo inf = item_info<KH>(p, item, warp == 0 && lane == 0);
 
         // ---- query fragments: head g of the kv group, dims (4t .. 4t+3) of every 16-dim chunk, scaled by
         //      2^e so that the head's largest |q * qscale| lies in [2^13, 2^14), split into f16 hi / lo
         const bool on = g < p.G;
-        const float *qh = p.q + ((size_t)inf.b * p.Hq + (size_t)inf.kvh * p.G + (on ? g : 0)) * D;
+        const float *qh = p.q + ((size_t)inf.b * p.Hq + (size_t)(inf.kvh + hh) * p.G + (on ? g : 0)) * D;
         float qv[KS][4];
         float amax = 0.f;
 #pragma unroll
@@ -244,14 +258,14 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
         for (int n = 0; n < NT; ++n) oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.f;
         float m_run = -INFINITY, l_run = 0.f;
 
-        for (int i = grp; i < inf.ntiles; i += NG) {  // this group's tiles of the item
+        for (int i = tg; i < inf.ntiles; i += TG) {  // this group's tiles of the item (its head of each)
             const uint32_t it = it_base + i;
             const uint32_t s = it % NS, ph = (it / NS) & 1;
             const int key0 = inf.t_begin + i * KT + wk;         // first key of this warp
             const int nvalid = inf.t_end - key0;                // keys of the warp below t_end (may be <= 0)
             if (!mbar_wait(full0 + 8 * s, ph, p.dev_err)) return;
-            const float *scs = sbuf + s * 2 * KT + wk;          // this warp's keys: K scales, V scales at +64
-            const uint32_t kbase = smem_u32(smem + s * C::STAGE), vbase = kbase + C::TILE;
+            const float *scs = sbuf + (s * KH + hh) * 2 * KT + wk;  // this warp's keys: K scales, V scales at +64
+            const uint32_t kbase = smem_u32(smem + s * C::STAGE) + hh * C::TILE, vbase = kbase + KH * C::TILE;
 
             // ---- S = Q K^T: n-tiles of keys 0-7 and 8-15 of the warp
             float sacc[2][4];
@@ -357,20 +371,27 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(merged);
         if (!mbar_wait(merged, item_no & 1, p.dev_err)) return;
-        const size_t pbase = (size_t)item * p.G;
-        for (int idx = threadIdx.x; idx < p.G * D; idx += 32 * NW) {
-            const int h = idx / D, d = idx - h * D;
+        // per kv head h2 of the stage: merge the warps of its groups (w = (tile slot * KH + h2) * 4 + k) into the
+        // partial of (row, kv head, chunk)
+        for (int idx = threadIdx.x; idx < KH * p.G * D; idx += 32 * NW) {
+            const int h2 = idx / (p.G * D), hd = idx - h2 * p.G * D, h = hd / D, d = hd - h * D;
+            const size_t pbase = (((size_t)inf.b * p.Hkv + inf.kvh + h2) * p.nchunk + inf.c) * p.G;
             float M = -INFINITY;
 #pragma unroll
-            for (int w = 0; w < NW; ++w) M = fmaxf(M, mw[w * HS + h]);
+            for (int t2 = 0; t2 < TG; ++t2)
+#pragma unroll
+                for (int k = 0; k < kGroup; ++k) M = fmaxf(M, mw[((t2 * KH + h2) * kGroup + k) * HS + h]);
             float O = 0.f, L = 0.f;
             if (M != -INFINITY) {
 #pragma unroll
-                for (int w = 0; w < NW; ++w) {
-                    const float f = fast_exp2(mw[w * HS + h] - M);
-                    O += ow[(w * HS + h) * D + d] * f;
-                    L += lw[w * HS + h] * f;
-                }
+                for (int t2 = 0; t2 < TG; ++t2)
+#pragma unroll
+                    for (int k = 0; k < kGroup; ++k) {
+                        const int w = (t2 * KH + h2) * kGroup + k;
+                        const float f = fast_exp2(mw[w * HS + h] - M);
+                        O += ow[(w * HS + h) * D + d] * f;
+                        L += lw[w * HS + h] * f;
+                    }
             }
             p.part_o[(pbase + h) * D + d] = O;
             if (d == 0) p.part_ml[pbase + h] = make_float2(M == -INFINITY ? -INFINITY : M * 0.69314718055994531f, L);
@@ -380,15 +401,15 @@ __global__ void __launch_bounds__(I8Cfg<D, NG>::THREADS, 1)
     }
 }
 
-template <int D, int NG>
-cudaError_t launch_i8_t(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv, const I8Params &p,
-                        int sm_count) {
-    using C = I8Cfg<D, NG>;
+template <int D, int NG, int KH>
+cudaError_t launch_i8_t(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv, I8Params p, int sm_count) {
+    using C = I8Cfg<D, NG, KH>;
     cudaError_t e =
-        cudaFuncSetAttribute(attn_decode_i8_kernel<D, NG>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        cudaFuncSetAttribute(attn_decode_i8_kernel<D, NG, KH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
+    p.n_items /= KH;  // items of KH kv heads each
     const int grid = p.n_items < sm_count ? p.n_items : sm_count;
-    attn_decode_i8_kernel<D, NG><<<grid, C::THREADS, C::SMEM, st>>>(tk, tv, p);
+    attn_decode_i8_kernel<D, NG, KH><<<grid, C::THREADS, C::SMEM, st>>>(tk, tv, p);
     return cudaGetLastError();
 }
 
@@ -417,9 +438,11 @@ cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, cons
     p.part_ml = part_ml;
     p.dev_err = a.dev_err;
     switch (a.D) {
-        case 64: return launch_i8_t<64, 4>(st, tk, tv, p, sm_count);   // 105 registers: four groups
-        case 128: return launch_i8_t<128, 2>(st, tk, tv, p, sm_count);
-        case 256: return launch_i8_t<256, 1>(st, tk, tv, p, sm_count);  // 249 registers: one group
+        case 64:  // four groups; with an even kv-head count both heads of a 128-byte cache row a stage
+            return p.Hkv % 2 == 0 ? launch_i8_t<64, 4, 2>(st, tk, tv, p, sm_count)
+                                  : launch_i8_t<64, 4, 1>(st, tk, tv, p, sm_count);
+        case 128: return launch_i8_t<128, 2, 1>(st, tk, tv, p, sm_count);
+        case 256: return launch_i8_t<256, 1, 1>(st, tk, tv, p, sm_count);  // 249 registers: one group
         default: return cudaErrorInvalidValue;
     }
 }

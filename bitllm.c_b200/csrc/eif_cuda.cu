@@ -194,9 +194,10 @@ bool make_kv_tensor_map(CUtensorMap *map, void *base, const eif_cuda_kv_t *kv) {
     // fp32: 32-key boxes, 16 at head_dim 256 (the fp32 decode kernel's tile there)
     const cuuint32_t box[3] = {box0, 1, f32 ? (kv->hd == 256 ? 16u : 32u) : 64u};
     const cuuint32_t es[3] = {1, 1, 1};
-    // L2 promotion no wider than one kv head's row: the rows of the other kv heads in between belong to other
-    // work items, and a wider promotion would fetch them from HBM with every tile
-    const size_t head_row = (size_t)kv->hd * elt;
+    // L2 promotion no wider than what a tile reads of a cache row: one kv head's row, or two heads' at INT8 head_dim
+    // 64 with an even kv-head count (the INT8 decode kernel's stages then hold both halves of each 128-byte row);
+    // a wider promotion would fetch rows of other work items from HBM with every tile
+    const size_t head_row = (size_t)kv->hd * elt * ((i8 && kv->hd == 64 && kv->n_kv % 2 == 0) ? 2 : 1);
     const CUtensorMapL2promotion promo = head_row >= 256   ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
                                          : head_row >= 128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
                                                            : CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
