@@ -286,11 +286,13 @@ bool use_tc(const DecodeArgs &a) {
 // Tensor-core path: persistent CTAs (one per SM) take items round-robin, so pick the chunk count that
 // minimises the busiest CTA's tiles plus the partials it writes and the combine reads back.
 Split choose_split_tc(const DecodeArgs &a, int sm_count) {
-    const long units = (long)a.B * a.Hkv;
+    // an item is (row, kh kv heads, chunk): the INT8 kernel takes both heads of a 128-byte row at head_dim 64
+    const int kh = a.dtype == EIF_CUDA_INT8 ? decode_i8_heads_per_item(a.D, a.Hkv) : 1;
+    const long units = (long)a.B * a.Hkv / kh;
     const long tpu = (a.max_len + 63) / 64;  // 64-key tiles per unit
-    // K + V bytes of a 64-key tile (INT8: codes plus the two scales of every key)
-    const double tile_bytes = a.dtype == EIF_CUDA_INT8 ? 64.0 * (a.D * 2 + 8)
-                              : 64.0 * a.D * 2 * (a.dtype == EIF_CUDA_F32 ? 4 : 2);
+    // K + V bytes of a 64-key tile of the unit's kh heads (INT8: codes plus the two scales of every key)
+    const double tile_bytes = kh * (a.dtype == EIF_CUDA_INT8 ? 64.0 * (a.D * 2 + 8)
+                                                              : 64.0 * a.D * 2 * (a.dtype == EIF_CUDA_F32 ? 4 : 2));
     // Cost of a split, in bytes streamed by the busiest CTA (items go round-robin over the persistent
     // CTAs): its tiles plus a fixed cost per item.  The bf16 kernel at head_dim 256 (three 64 KB stages
     // per CTA) was measured elastic: a CTA with more items than the others streams up to half again its
@@ -298,7 +300,7 @@ Split choose_split_tc(const DecodeArgs &a, int sm_count) {
     // item (q load, merge of the four warps, its share of the combine) costs about 64 KB of streaming;
     // the others were measured best at the most even split, with the partial's bytes as the item cost.
     const bool elastic = a.dtype == EIF_CUDA_BF16 && a.D >= 256;
-    const double item_bytes = elastic ? 65536.0 : 2.0 * (a.Hq / a.Hkv) * a.D * 4;
+    const double item_bytes = elastic ? 65536.0 : 2.0 * kh * (a.Hq / a.Hkv) * a.D * 4;
     const double fair = (double)units * tpu * tile_bytes / sm_count;
     int best = 1;
     double best_cost = 1e300;

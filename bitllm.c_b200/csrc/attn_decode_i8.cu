@@ -439,8 +439,8 @@ cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, cons
     p.dev_err = a.dev_err;
     switch (a.D) {
         case 64:  // four groups; with an even kv-head count both heads of a 128-byte cache row a stage
-            return p.Hkv % 2 == 0 ? launch_i8_t<64, 4, 2>(st, tk, tv, p, sm_count)
-                                  : launch_i8_t<64, 4, 1>(st, tk, tv, p, sm_count);
+            return decode_i8_heads_per_item(64, p.Hkv) == 2 ? launch_i8_t<64, 4, 2>(st, tk, tv, p, sm_count)
+                                                             : launch_i8_t<64, 4, 1>(st, tk, tv, p, sm_count);
         case 128: return launch_i8_t<128, 2, 1>(st, tk, tv, p, sm_count);
         case 256: return launch_i8_t<256, 1, 1>(st, tk, tv, p, sm_count);  // 249 registers: one group
         default: return cudaErrorInvalidValue;

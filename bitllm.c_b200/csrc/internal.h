@@ -235,6 +235,9 @@ cudaError_t launch_attend_decode_f32(cudaStream_t st, const CUtensorMap &tk, con
 cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
                                     const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,
                                     float2 *part_ml, int sm_count);
+// KV heads a work item of the INT8 tensor-core decode covers: both heads of a 128-byte cache row at head_dim 64
+// with an even kv-head count (attn_decode_i8.cu), else one.
+inline int decode_i8_heads_per_item(int D, int Hkv) { return D == 64 && Hkv % 2 == 0 ? 2 : 1; }
 // Workspace bytes needed by launch_attend_decode for these args and the chosen split.
 size_t decode_workspace_bytes(const DecodeArgs &a, int sm_count);
 // The split launch_attend_decode would use: key chunks per (sequence, kv head), keys per chunk, scratch bytes.
