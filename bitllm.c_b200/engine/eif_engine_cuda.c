@@ -15,12 +15,23 @@
  * Qwen3.5
  * ============================================================================================== */
 
+#define MAX_MATRICES 512  /* a Qwen3.5 model has 5 / 4 mixer projections a layer, 3 FFN ones and the head */
+
+typedef struct {
+    const void *W;  /* the engine's weight pointer (inside the model image) */
+    int quant_type, rows, cols;
+    eif_cuda_linear_t *lin;
+} q35_matrix_t;
+
 typedef struct {
     qwen35_t *m;
     eif_cuda_ctx_t *ctx;
     eif_cuda_kv_t *kv;       /* n_full layers, batch 1 */
     eif_cuda_delta_t *dn;    /* n_delta layers, batch 1 */
     int prefill_mode;
+    int projections;         /* linear_gemv / linear_gemm / int8_gemv on the device too */
+    int n_mat;
+    q35_matrix_t mat[MAX_MATRICES];
     int failed;
     char err[256];
 } q35_dev_t;
@@ -66,6 +77,44 @@ static int q35_status(q35_dev_t *d, eif_status_t st, const char *what) {
     return 1;
 }
 
+int eif_q35_cuda_set_projections(qwen35_t *m, int on) {
+    q35_dev_t *d = q35_of_model(m);
+    if (!d) return EIF_STATUS_INVALID_ARGUMENT;
+    d->projections = on != 0;
+    return EIF_STATUS_OK;
+}
+
+/* The projection hook: the attachment whose model image holds W (with projections on) runs out = W x for n
+ * tokens on its device, uploading the matrix on first use; 0 when no attachment owns W. */
+int eif_q35_cuda_linear(const void *W, const float *sc, int quant_type, int rows, int cols, const float *x, int n,
+                        float *out) {
+    q35_dev_t *d = NULL;
+    for (int i = 0; i < MAX_ATTACHED && !d; i++) {
+        const qwen35_t *m = g_q35[i].m;
+        if (m && g_q35[i].projections && m->file_data && (const uint8_t *)W >= (const uint8_t *)m->file_data &&
+            (const uint8_t *)W < (const uint8_t *)m->file_data + m->file_size)
+            d = &g_q35[i];
+    }
+    if (!d) return 0;
+    if (d->failed) return 1;
+    q35_matrix_t *e = NULL;
+    for (int i = 0; i < d->n_mat && !e; i++)
+        if (d->mat[i].W == W && d->mat[i].quant_type == quant_type && d->mat[i].rows == rows && d->mat[i].cols == cols)
+            e = &d->mat[i];
+    if (!e) {
+        if (d->n_mat == MAX_MATRICES) return q35_status(d, EIF_STATUS_OUT_OF_MEMORY, "projection table full");
+        e = &d->mat[d->n_mat];
+        eif_status_t st = eif_cuda_linear_upload(d->ctx, quant_type, rows, cols, W, sc, &e->lin);
+        if (st != EIF_STATUS_OK) return q35_status(d, st, "linear_upload");
+        e->W = W;
+        e->quant_type = quant_type;
+        e->rows = rows;
+        e->cols = cols;
+        d->n_mat++;
+    }
+    return q35_status(d, eif_cuda_linear_forward(d->ctx, e->lin, x, n, out), "linear_forward");
+}
+
 static eif_cuda_subln_t q35_subln(const qwen35_t *m, int fa) {
     /* fullatt_attend's epilogue (src/eif_qwen35.c:779-789) */
     if (m->weights.full[fa].sub_norm) return EIF_CUDA_SUBLN_WEIGHT;
@@ -75,6 +124,7 @@ static eif_cuda_subln_t q35_subln(const qwen35_t *m, int fa) {
 void eif_q35_cuda_detach(qwen35_t *m) {
     q35_dev_t *d = q35_of_model(m);
     if (!d) return;
+    for (int i = 0; i < d->n_mat; i++) eif_cuda_linear_free(d->mat[i].lin);
     if (d->kv) eif_cuda_kv_free(d->kv);
     if (d->dn) eif_cuda_delta_free(d->dn);
     if (d->ctx) eif_cuda_free(d->ctx);

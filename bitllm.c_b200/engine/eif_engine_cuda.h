@@ -11,8 +11,8 @@
  *
  * From then on the engine's deltanet_core / fullatt_prep / fullatt_attend calls (src/eif_qwen35.c:690, 819-820),
  * its prefill_chunk loops (:1104-1106, :1118-1133), tinyllm's per-token attention block (src/eif_tinyllm.c:481-657)
- * and its batched prefill attention (:1088-1268) run on the device through eif_cuda.h; the projections, norms
- * and FFN stay on the host.  The device copies of the recurrent states and KV caches are authoritative while a
+ * and its batched prefill attention (:1088-1268) run on the device through eif_cuda.h; the projections stay on
+ * the host unless eif_q35_cuda_set_projections turns them on, the norms and the FFN's activations always do.  The device copies of the recurrent states and KV caches are authoritative while a
  * model is attached (the host copies are no longer updated).  A device failure is sticky: the forward functions
  * return NULL (prefill_chunk -1) from then on, and eif_*_cuda_error() says why; there is no silent CPU fallback.
  *
@@ -48,7 +48,15 @@ const char *eif_q35_cuda_error(const qwen35_t *m);
 /* Zero the device states (called by qwen35_reset). */
 void eif_q35_cuda_reset(qwen35_t *m);
 
+/* Also run the model's projections on the device (on != 0): linear_gemv, linear_gemm and the INT8 LM head
+ * int8_gemv (src/eif_qwen35.c:384-443, 1033-1063).  Each weight matrix is recognised by its address inside the
+ * model's image and uploaded in the engine's packed layout on first use (eif_cuda_linear_upload); every call then
+ * copies x in and the output back.  Off by default: the attachment moves only the token mixers. */
+int eif_q35_cuda_set_projections(qwen35_t *m, int on);
+
 /* Hooks at the engine's call sites. */
+int eif_q35_cuda_linear(const void *W, const float *sc, int quant_type, int rows, int cols, const float *x, int n,
+                        float *out);
 int eif_q35_cuda_deltanet(const qwen35_delta_state_t *st, const float *qkv, const float *z, const float *b,
                           const float *a, float *out);
 int eif_q35_cuda_fullatt(const qwen35_attn_state_t *st, const float *qg, const float *k, const float *v, int pos,

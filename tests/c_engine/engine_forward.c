@@ -188,8 +188,11 @@ static int run_qwen35(const char *kv, const char *mode, double tol) {
     }
     remove(path);
     const eif_cuda_dtype_t dt = strcmp(kv, "bf16") == 0 ? EIF_CUDA_BF16 : EIF_CUDA_F32;
-    const int pm = strcmp(mode, "chunked") == 0 ? EIF_ENGINE_PREFILL_CHUNKED : EIF_ENGINE_PREFILL_TOKENWISE;
-    const int rc = getenv("ENGINE_FORWARD_HOST_ONLY") ? 0 : eif_q35_cuda_attach(&gpu, 0, dt, pm);
+    /* mode: "tokenwise" | "chunked", with "-proj" the projections (INT4 linears, the INT8 head) on the GPU too */
+    const int pm = strncmp(mode, "chunked", 7) == 0 ? EIF_ENGINE_PREFILL_CHUNKED : EIF_ENGINE_PREFILL_TOKENWISE;
+    const int proj = strstr(mode, "-proj") != NULL;
+    int rc = getenv("ENGINE_FORWARD_HOST_ONLY") ? 0 : eif_q35_cuda_attach(&gpu, 0, dt, pm);
+    if (rc == 0 && proj && !getenv("ENGINE_FORWARD_HOST_ONLY")) rc = eif_q35_cuda_set_projections(&gpu, 1);
     if (rc != 0) {
         fprintf(stderr, "attach failed: %d %s\n", rc, eif_q35_cuda_error(&gpu));
         return 2;

@@ -7,7 +7,8 @@ reference's; unattached, the patched engines give the host logits exactly.
 
 Logit tolerances (rel-L2 over the vocabulary), with what one B200 measured:
 * fp32 paths (fp32 KV cache; Qwen3.5 prefill with deltanet_core per token): Qwen3.5 1e-4 (measured <= 1.1e-5
-  over 24 layers), tinyllm 1e-5 (measured <= 5e-7, fp32 and INT8 caches);
+  over 24 layers; the same bound with the projections -- linear_gemv / linear_gemm / int8_gemv -- on the GPU too,
+  `-proj`), tinyllm 1e-5 (measured <= 5e-7, fp32 and INT8 caches);
 * bf16 paths (the chunked DeltaNet prefill's bf16 q / k / v, or a bf16 KV cache): 6e-2 (measured <= 4.5e-2 for
   Qwen3.5, whose 18 DeltaNet layers each carry a ~2e-3 input rounding into the residual stream; 1e-3 for
   tinyllm's bf16 cache).  The per-mixer prefill tolerance (rel-L2 <= 1e-2) is checked in the kernel tests."""
@@ -23,7 +24,9 @@ PATCH = os.path.join(ENGINE, "bitllm_cuda.patch")
 REF = os.environ.get("BITLLM_REF_DIR", "/root/reference")
 
 CASES = [("qwen35", "f32", "tokenwise", 1e-4), ("qwen35", "f32", "chunked", 6e-2), ("qwen35", "bf16", "chunked", 6e-2),
-         ("tinyllm", "f32", None, 1e-5), ("tinyllm", "int8", None, 1e-5), ("tinyllm", "bf16", None, 6e-2)]
+         ("tinyllm", "f32", None, 1e-5), ("tinyllm", "int8", None, 1e-5), ("tinyllm", "bf16", None, 6e-2),
+         # the Qwen3.5 projections (INT4 linears, the INT8 tied head) on the GPU as well (row f4)
+         ("qwen35", "f32", "tokenwise-proj", 1e-4), ("qwen35", "f32", "chunked-proj", 6e-2)]
 
 
 def _binary(build=True):
