@@ -150,17 +150,21 @@ __global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid
     // (m >> 2) & 1 == hf in registers (local index 4 (m >> 3) + (m & 3)) and sums its half of each row
     // from float4 broadcasts of A; a lane shuffle joins the halves.  Entries not yet formed are 0 and A is
     // 0 on and above the diagonal, so no masking is needed; rows above the diagonal come out exactly 0.
+    // Warp w holds columns 16w .. 16w + 15: its rows above 16w and its entries below 16w are exactly 0, so it
+    // starts at row 16w and skips the float4 groups of columns below 16w (warp-uniform; 54 % less work).
     {
-        const int cidx = tid >> 1, hf = tid & 1;
+        const int cidx = tid >> 1, hf = tid & 1, r0 = 16 * warp, g0 = 2 * warp;
         float tl[C / 2];
 #pragma unroll
         for (int k = 0; k < C / 2; ++k) tl[k] = 0.f;
 #pragma unroll
         for (int r = 0; r < C; ++r) {
+            if (r < r0) continue;  // warp-uniform
             const float *arow = Af + r * FP + 4 * hf;
             float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
             for (int g = 0; 8 * g < r; ++g) {
+                if (g < g0) continue;  // warp-uniform: columns below 16w meet zero entries
                 const float4 a4 = *reinterpret_cast<const float4 *>(arow + 8 * g);
                 s0 = fmaf(a4.x, tl[4 * g], s0);
                 s1 = fmaf(a4.y, tl[4 * g + 1], s1);

@@ -35,6 +35,10 @@ constexpr int kWarps = 8;
 constexpr int kThreads = 32 * kWarps;
 constexpr size_t kSmemCap = 200 * 1024;
 constexpr int kDenseLut = 256 * 4;  // bytes of the dense-ternary digit table at the front of shared memory
+#ifndef EIF_LINEAR_MMA_MIN_TOKENS
+#define EIF_LINEAR_MMA_MIN_TOKENS 4
+#endif
+constexpr int kMmaMinTokens = EIF_LINEAR_MMA_MIN_TOKENS;  // tokens from which the tensor-core kernel runs
 
 __host__ __device__ constexpr int cols_per_word(int wt) {
     return wt == EIF_CUDA_W_F32 ? 1
@@ -373,9 +377,8 @@ bool linear_fits(int wtype, size_t stride) { return pick_tile(wtype, (int)(strid
 
 cudaError_t launch_linear(cudaStream_t st, const eif_cuda_linear &lin, const float *x, int n, float *out,
                           int sm_count) {
-    // a few tokens: the CUDA-core kernel (its decode per weight is cheaper than the tensor-core kernel's x staging
-    // and hi / lo split); from four tokens on, the tensor cores
-    if (n >= 4 && linear_mma_supported(lin)) return launch_linear_mma(st, lin, x, n, out, sm_count);
+    // below kMmaMinTokens tokens the CUDA-core kernel, from there on the tensor cores (where the format allows)
+    if (n >= kMmaMinTokens && linear_mma_supported(lin)) return launch_linear_mma(st, lin, x, n, out, sm_count);
     const LinArgs a{lin.W, lin.scales, x, out, lin.rows, lin.cols, n, (int)(lin.stride / 4), lin.stride,
                     lin.group, lin.n_scales_row, 1};
     const int T = pick_tile(lin.wtype, a.n_words, n);
