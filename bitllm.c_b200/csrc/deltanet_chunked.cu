@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid
     if (tid < C) Xv[tid] = -Bv[tid] * expf(Gv[tid]);  // read after the solve's barriers
 
     // K K^T: warp w owns rows 16w..16w+15 and needs the columns j < 16 (w + 1) only (16-column groups
-    // np <= w); A_ij = b_i e^{G_i - G_j} k_i.k_j for j < i, 0 elsewhere
+    // np <= w); A_ij = b_i e^{G_i - G_j} k_i.k_j for j < i, 0 elsewhere, kept as its transpose
     {
         float acc[8][4];
 #pragma unroll
@@ -134,51 +134,41 @@ __global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid
             const int j = nt * 8 + 2 * t4;
             const float2 gj = *reinterpret_cast<const float2 *>(Gv + j);
             const float gj0 = gj.x * kLog2e, gj1 = gj.y * kLog2e;
-            // e^{G_i - G_j} <= 1 on the SFU (ex2.approx, relative error ~2^-22)
-            *reinterpret_cast<float2 *>(Af + i0 * FP + j) =
-                make_float2(j < i0 ? bi0 * fast_exp2(gi0 - gj0) * acc[nt][0] : 0.f,
-                            j + 1 < i0 ? bi0 * fast_exp2(gi0 - gj1) * acc[nt][1] : 0.f);
-            *reinterpret_cast<float2 *>(Af + (i0 + 8) * FP + j) =
-                make_float2(j < i0 + 8 ? bi1 * fast_exp2(gi1 - gj0) * acc[nt][2] : 0.f,
-                            j + 1 < i0 + 8 ? bi1 * fast_exp2(gi1 - gj1) * acc[nt][3] : 0.f);
+            // e^{G_i - G_j} <= 1 on the SFU (ex2.approx, relative error ~2^-22); stored transposed, Af[j][i] = A_ij
+            Af[j * FP + i0] = j < i0 ? bi0 * fast_exp2(gi0 - gj0) * acc[nt][0] : 0.f;
+            Af[(j + 1) * FP + i0] = j + 1 < i0 ? bi0 * fast_exp2(gi0 - gj1) * acc[nt][1] : 0.f;
+            Af[j * FP + i0 + 8] = j < i0 + 8 ? bi1 * fast_exp2(gi1 - gj0) * acc[nt][2] : 0.f;
+            Af[(j + 1) * FP + i0 + 8] = j + 1 < i0 + 8 ? bi1 * fast_exp2(gi1 - gj1) * acc[nt][3] : 0.f;
         }
     }
     __syncthreads();  // A complete; the K tile is dead from here on (its space holds T)
 
-    // T = (I + A)^-1 by forward substitution in fp32: t_r = [r == c] - sum_{m < r} A_rm t_m per column c.
-    // Two threads per column (lanes 2c, 2c + 1 of a warp): thread hf keeps the column entries m with
-    // (m >> 2) & 1 == hf in registers (local index 4 (m >> 3) + (m & 3)) and sums its half of each row
-    // from float4 broadcasts of A; a lane shuffle joins the halves.  Entries not yet formed are 0 and A is
-    // 0 on and above the diagonal, so no masking is needed; rows above the diagonal come out exactly 0.
-    // Warp w holds columns 16w .. 16w + 15: its rows above 16w and its entries below 16w are exactly 0, so it
-    // starts at row 16w and skips the float4 groups of columns below 16w (warp-uniform; 54 % less work).
-    {
-        const int cidx = tid >> 1, hf = tid & 1, r0 = 16 * warp, g0 = 2 * warp;
-        float tl[C / 2];
+    // T = (I + A)^-1 by right-looking forward substitution in fp32, one column c of T per thread of warps 0-1:
+    // u = e_c in registers; at step r, t_r = u_r is final and every later row takes its share,
+    // u_i -= A_ir t_r (i > r), from float4 broadcasts of row r of A^T.  No reduction or shuffle per step: the
+    // dependency chain is one FMA a step.  Warp w's columns are >= 32 w, so its first 32 w steps are skipped
+    // (exactly zero); rows above the diagonal come out exactly 0.
+    if (warp < 2) {
+        const int c = tid, r0 = 32 * warp;
+        float u[C];
 #pragma unroll
-        for (int k = 0; k < C / 2; ++k) tl[k] = 0.f;
+        for (int i = 0; i < C; ++i) u[i] = i == c ? 1.f : 0.f;
 #pragma unroll
-        for (int r = 0; r < C; ++r) {
+        for (int r = 0; r < C - 1; ++r) {
             if (r < r0) continue;  // warp-uniform
-            const float *arow = Af + r * FP + 4 * hf;
-            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+            const float t = u[r];
+            const float *arow = Af + r * FP;  // A^T row r: A_ir for i = 0 .. 63
 #pragma unroll
-            for (int g = 0; 8 * g < r; ++g) {
-                if (g < g0) continue;  // warp-uniform: columns below 16w meet zero entries
-                const float4 a4 = *reinterpret_cast<const float4 *>(arow + 8 * g);
-                s0 = fmaf(a4.x, tl[4 * g], s0);
-                s1 = fmaf(a4.y, tl[4 * g + 1], s1);
-                s2 = fmaf(a4.z, tl[4 * g + 2], s2);
-                s3 = fmaf(a4.w, tl[4 * g + 3], s3);
+            for (int g = (r + 1) / 4; g < C / 4; ++g) {
+                const float4 a4 = *reinterpret_cast<const float4 *>(arow + 4 * g);
+                if (4 * g > r) u[4 * g] = fmaf(-a4.x, t, u[4 * g]);
+                if (4 * g + 1 > r) u[4 * g + 1] = fmaf(-a4.y, t, u[4 * g + 1]);
+                if (4 * g + 2 > r) u[4 * g + 2] = fmaf(-a4.z, t, u[4 * g + 2]);
+                u[4 * g + 3] = fmaf(-a4.w, t, u[4 * g + 3]);
             }
-            float s = (s0 + s1) + (s2 + s3);
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            const float tr = (r == cidx ? 1.f : 0.f) - s;
-            const int k = 4 * (r >> 3) + (r & 3);
-            tl[k] = ((r >> 2) & 1) == hf ? tr : tl[k];
         }
 #pragma unroll
-        for (int k = 0; k < C / 2; ++k) Tf[(8 * (k >> 2) + 4 * hf + (k & 3)) * C + cidx] = tl[k];
+        for (int i = 0; i < C; ++i) Tf[i * C + c] = u[i];
     }
     __syncthreads();
     // T diag(-b e^G) ; T diag(b) (T lower triangular) -> bf16 rows of 64 for the state kernel's TMA; G
