@@ -164,3 +164,38 @@ def test_linear_rejections(pkg, ctx):
             lin.forward(np.zeros((2, 256), np.float32), out=np.zeros((3, 4), np.float32))
     finally:
         other.close()
+
+
+@pytest.mark.parametrize("n", [1, 6])
+def test_linear_dependent_chain(pkg, ctx, orc, n):
+    """Projections launched back to back as programmatic dependents, each reading the previous one's output
+    (no synchronisation between them), on both kernels (one token: CUDA cores, six: tensor cores): every
+    launch waits for its predecessor before it reads x, so the chain equals the reference applied in turn."""
+    import torch
+    rng = np.random.default_rng(20 + n)
+    dims = [1024, 768, 1536, 512, 1024]
+    mats = []
+    for i in range(len(dims) - 1):
+        rows, cols = dims[i + 1], dims[i]
+        qt = 2 if i % 2 == 0 else 1
+        v = _values(rng, qt, rows, cols)
+        W = orc.pack_weights(v, qt, rng if qt == 2 else None)
+        sc = (0.5 + rng.random(rows)).astype(np.float32) / np.sqrt(cols)
+        mats.append((qt, rows, cols, W, sc, pkg.Linear(ctx, qt, rows, cols, W, sc)))
+    stream = torch.cuda.Stream()
+    try:
+        x = rng.standard_normal((n, dims[0])).astype(np.float32)
+        bufs = [torch.from_numpy(x).cuda()] + [torch.full((n, d), float("nan"), device="cuda") for d in dims[1:]]
+        torch.cuda.synchronize()
+        ctx.set_stream(stream.cuda_stream)
+        for i, (_, _, _, _, _, lin) in enumerate(mats):
+            lin.forward_dev(bufs[i].data_ptr(), n, bufs[i + 1].data_ptr())
+        ctx.synchronize()
+        ref = x
+        for qt, rows, cols, W, sc, _ in mats:
+            ref = _reference(orc, W, sc, ref, rows, cols, qt)
+        assert rel_l2(bufs[-1].cpu().numpy(), ref) <= 4 * TOL
+    finally:
+        ctx.set_stream(None)
+        for *_, lin in mats:
+            lin.free()
