@@ -70,6 +70,10 @@ TRAFFIC_PER_ALG_BYTE = {
     "attn_decode_f32": (1079984896 / 1073741824, _DRAM),
     "attn_decode_tc": (552377088 / 536870912, _DRAM),
     "attn_decode_i8": (291107584 / 285212672, _DRAM),
+    # row f4 at one token (linear_kernel): the 8224 x 1024 2-bit launch read 2,178,304 B / 2,175,232 B algorithmic;
+    # the INT8 LM head 255,299,072 B read + 4,149,248 B written / 256,270,336 B
+    "linear_ternary2": (2178304 / 2175232, "profiles/linear_projection_decode.md"),
+    "linear_int8_head": ((255299072 + 4149248) / 256270336, "profiles/linear_projection_decode.md"),
 }
 
 
@@ -1465,8 +1469,10 @@ def run_projection(args, torch, dist, rank, world, local_rank):
     step_bytes = tern_bytes + head_bytes
     ach = tern_bytes / (tern_ms * 1e-3) / 1e9
     head_ach = head_bytes / (head_ms * 1e-3) / 1e9
-    tr, tr_src = traffic("linear_ternary2", tern_bytes)
     kname = "linear_mma_kernel" if n >= 4 else "linear_kernel"  # the library's choice: tensor cores from 4 tokens
+    # DRAM bytes per algorithmic byte were captured for the one-token kernel only
+    tr, tr_src = traffic("linear_ternary2", tern_bytes) if n < 4 else (None, None)
+    htr, htr_src = traffic("linear_int8_head", head_bytes) if n < 4 else (None, None)
     line = {"metric": "projection tokens/s (every quantised projection of a Qwen3.5-0.8B decode step)",
             "value": n * world / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -1487,7 +1493,8 @@ def run_projection(args, torch, dist, rank, world, local_rank):
                          "algorithmic_bytes_per_launch": tern_bytes / len(tern), "launch_ms": tern_ms / len(tern),
                          "traffic": None if tr is None else tr / len(tern), "traffic_source": tr_src},
             "lm_head": {"kernel": f"{kname} (INT8, 248320 x 1024)", "achieved": head_ach, "frac": head_ach / hbm,
-                        "launch_ms": head_ms, "algorithmic_bytes": head_bytes},
+                        "launch_ms": head_ms, "algorithmic_bytes": head_bytes, "traffic": htr,
+                        "traffic_source": htr_src},
             "gpu_launches": len(shapes) * args.steps, "clocks": clk}
     if world == 1 and not args.no_cpu_baseline:
         tps, cores, kind, sample = cpu_projection_reference(shapes, n)
