@@ -79,7 +79,7 @@ int eif_cuda_device_count(void);
 /* Create a context on `device`.  Returns EIF_STATUS_NOT_SUPPORTED when there is no device, the device
  * is not sm_100 (B200) or BITLLM_NO_CUDA=1 is set. */
 eif_status_t eif_cuda_init(eif_cuda_ctx_t **ctx, int device);
-/* Free every KV cache and DeltaNet state made on the context before the context itself. */
+/* Free every KV cache, DeltaNet state and projection matrix made on the context before the context itself. */
 void eif_cuda_free(eif_cuda_ctx_t *ctx);
 
 /* Message of the last failure on this context ("" if none).  Valid until the next call. */
@@ -439,9 +439,13 @@ typedef struct eif_cuda_linear eif_cuda_linear_t; /* one weight matrix resident 
  * (the engine's loader accepts multiples of 32, src/eif_qwen35.c:1265); cols up to 12288.  Synchronous. */
 eif_status_t eif_cuda_linear_upload(eif_cuda_ctx_t *ctx, int quant_type, int rows, int cols, const void *W,
                                     const float *scales, eif_cuda_linear_t **out);
+/* Waits for the context's queued work, then frees the matrix; call it before eif_cuda_free of its context. */
 void eif_cuda_linear_free(eif_cuda_linear_t *lin);
 
-/* out[t][rows] = W x[t] for n tokens x[n][cols] (n = 1: linear_gemv; n > 1: linear_gemm), fp32 arithmetic.
+/* out[t][rows] = W x[t] for n tokens x[n][cols] (n = 1: linear_gemv; n > 1: linear_gemm), fp32 arithmetic: CUDA
+ * cores below four tokens, tensor cores from four on for INT8 / INT4 / ungrouped 2-bit weights (exact integer
+ * weights, x split into two f16 parts, fp32 accumulation).  The kernels are launched as programmatic dependents
+ * of the previous kernel on the stream: they fetch weights early and wait for that kernel before reading x.
  * _dev: device arrays, asynchronous.  Host variant: host arrays, returns when out is written. */
 eif_status_t eif_cuda_linear_forward(eif_cuda_ctx_t *ctx, const eif_cuda_linear_t *lin, const float *x, int n,
                                      float *out);
