@@ -34,6 +34,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
     int max_seq, int max_len, int Hkv, int chunk, int nchunk, float scale, float *__restrict__ part_o,
     float2 *__restrict__ part_ml, unsigned *__restrict__ dev_err, const float *__restrict__ k_scale,
     const float *__restrict__ v_scale, int sstride, const int *__restrict__ row_seq) {
+    griddep_launch_dependents();  // the chunk combine may launch now and wait for this grid's results
     constexpr int DL = D / 32;  // head-dim elements per lane in P.V
     static_assert(D % 32 == 0 && (DL == 2 || DL == 4 || DL == 8), "head_dim 64/128/256");
     constexpr bool kI8 = sizeof(KT) == 1;  // INT8 cache: codes, one K and one V scale per (row, kv head)
@@ -178,6 +179,9 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
 __global__ void __launch_bounds__(256) attn_decode_combine_kernel(
     const float *__restrict__ part_o, const float2 *__restrict__ part_ml, int Hq, int Hkv, int D, int nchunk,
     const float *__restrict__ gate, int subln, const float *__restrict__ sub_norm, float *__restrict__ out) {
+    // launched as a programmatic dependent of the decode kernel: resident early, it waits here for that grid's
+    // partials (and, through it, for the gate written before it)
+    griddep_wait();
     extern __shared__ float smem[];
     const int b = blockIdx.x;
     const int G = Hq / Hkv;
@@ -433,8 +437,18 @@ cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws,
         e = cudaFuncSetAttribute(attn_decode_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    attn_decode_combine_kernel<<<a.B, 256, smem, st>>>(part_o, part_ml, a.Hq, a.Hkv, a.D, n_part, a.gate,
-                                                         a.subln, a.sub_norm, a.out);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.B);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, attn_decode_combine_kernel, (const float *)part_o, (const float2 *)part_ml, a.Hq,
+                           a.Hkv, a.D, n_part, a.gate, (int)a.subln, a.sub_norm, a.out);
     ++*n_launches;
-    return cudaGetLastError();
+    return e;
 }

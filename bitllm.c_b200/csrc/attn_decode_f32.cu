@@ -134,6 +134,7 @@ __global__ void __launch_bounds__(F32Cfg<D>::THREADS, 1)
         fence_barrier_init();
     }
     __syncthreads();
+    griddep_launch_dependents();  // the chunk combine may launch now and wait for this grid's results
 
     if (warp == NW) {
         // ------------------------------------------------------------------ producer

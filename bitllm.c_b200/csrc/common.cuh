@@ -7,6 +7,12 @@
 
 #define EIF_DEV __device__ __forceinline__
 
+// Programmatic dependent launch (sm_90+): let the next kernel on the stream begin launching its CTAs, and wait
+// until the previous kernel has completed with its memory visible (no-ops for a kernel launched without the
+// programmatic-serialization attribute, or with no kernel before it).
+EIF_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+EIF_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 EIF_DEV float warp_sum(float x) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);

@@ -26,6 +26,7 @@
 // The 4 x T accumulators of a warp are summed across lanes by a transposed butterfly (R*T - 1 shuffles instead of
 // 5 R T); the scale is applied as the reference applies it (per row after the sum, or per group inside it).
 #include "internal.h"
+#include "common.cuh"
 
 namespace {
 
@@ -73,11 +74,6 @@ int pick_tile(int wt, int n_words, int n) {
     while (T > 1 && tile_smem(wt, n_words, T) > kSmemCap) T >>= 1;
     return tile_smem(wt, n_words, T) <= kSmemCap ? T : 0;
 }
-
-// Programmatic dependent launch (sm_90+): let the next kernel on the stream begin launching its CTAs, and wait
-// until the previous kernel has completed with its memory visible (a no-op when launched without the attribute).
-__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // the float of the integer field in byte j of `bytes`, minus the bias (bias_2p23 = 2^23 + bias)
 __device__ __forceinline__ float field_float(uint32_t bytes, int j, float bias_2p23) {

@@ -28,6 +28,7 @@
 #include <cuda_fp16.h>
 
 #include "internal.h"
+#include "common.cuh"
 
 namespace {
 
@@ -41,8 +42,6 @@ __host__ __device__ constexpr int mma_cpw(int wt) {
     return wt == EIF_CUDA_W_INT8 ? 4 : wt == EIF_CUDA_W_INT4 ? 8 : 16;
 }
 
-__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 // 16-byte asynchronous global -> shared copy, L2 only (the weights are streamed once)
