@@ -35,6 +35,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
     float2 *__restrict__ part_ml, unsigned *__restrict__ dev_err, const float *__restrict__ k_scale,
     const float *__restrict__ v_scale, int sstride, const int *__restrict__ row_seq) {
     griddep_launch_dependents();  // the chunk combine may launch now and wait for this grid's results
+    griddep_wait();  // launched as a programmatic dependent: wait for the previous kernels' writes
     constexpr int DL = D / 32;  // head-dim elements per lane in P.V
     static_assert(D % 32 == 0 && (DL == 2 || DL == 4 || DL == 8), "head_dim 64/128/256");
     constexpr bool kI8 = sizeof(KT) == 1;  // INT8 cache: codes, one K and one V scale per (row, kv head)
@@ -283,6 +284,8 @@ size_t partials_bytes(const DecodeArgs &a, int nchunk, int ip = 1) {
 // The TMA-fed persistent kernels: bf16 / INT8 caches on the tensor cores, fp32 caches in fp32 FMAs.
 bool use_tc(const DecodeArgs &a) {
     if (!a.tmk || !a.tmv || a.force_simt) return false;
+    // the kernels stage each item's query rows with a bulk copy (16-byte aligned source)
+    if ((reinterpret_cast<uintptr_t>(a.q) & 15) != 0) return false;
     if (a.dtype == EIF_CUDA_F32) return decode_f32_supported(a.D, a.Hq / a.Hkv);
     return decode_tc_supported(a.D, a.Hq / a.Hkv);
 }
@@ -344,9 +347,9 @@ Split choose_split(const DecodeArgs &a, int sm_count) {
 template <typename KT, int D, int G>
 cudaError_t launch_simt(cudaStream_t st, const DecodeArgs &a, const Split &sp, float *part_o, float2 *part_ml) {
     dim3 grid(sp.nchunk, a.Hkv, a.B);
-    attn_decode_simt_kernel<KT, D, G><<<grid, kDecodeThreads, 0, st>>>(
-        static_cast<const KT *>(a.K), static_cast<const KT *>(a.V), a.q, a.pos, a.max_seq, a.max_len, a.Hkv, sp.chunk,
-        sp.nchunk, a.scale, part_o, part_ml, a.dev_err, a.k_scale, a.v_scale, a.scale_stride, a.row_seq);
+    launch_pdl(attn_decode_simt_kernel<KT, D, G>, grid, dim3(kDecodeThreads), 0, st, static_cast<const KT *>(a.K),
+               static_cast<const KT *>(a.V), a.q, a.pos, a.max_seq, a.max_len, a.Hkv, sp.chunk, sp.nchunk, a.scale,
+               part_o, part_ml, a.dev_err, a.k_scale, a.v_scale, a.scale_stride, a.row_seq);
     return cudaGetLastError();
 }
 
@@ -437,18 +440,8 @@ cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws,
         e = cudaFuncSetAttribute(attn_decode_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.B);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, attn_decode_combine_kernel, (const float *)part_o, (const float2 *)part_ml, a.Hq,
-                           a.Hkv, a.D, n_part, a.gate, (int)a.subln, a.sub_norm, a.out);
+    e = launch_pdl(attn_decode_combine_kernel, dim3(a.B), dim3(256), smem, st, (const float *)part_o,
+                   (const float2 *)part_ml, a.Hq, a.Hkv, a.D, n_part, a.gate, (int)a.subln, a.sub_norm, a.out);
     ++*n_launches;
     return e;
 }

@@ -59,7 +59,9 @@ struct I8Cfg {
     static constexpr int TILE = (D / BW) * BOX;       // K (or V) tile bytes of one head
     static constexpr int STAGE = 2 * KH * TILE;       // [K head 0 .. KH-1][V head 0 .. KH-1]
     static constexpr int SCALES = 2 * KH * KT * 4;    // per stage: [head][K, V][64 keys] scales
-    static constexpr int EXTRA = NW * HS * D * 4              // merge buffer o
+    static constexpr int QSLOT = KH * HS * D * 4;     // the query rows of an item (KH x G heads)
+    static constexpr int EXTRA = 2 * QSLOT                    // two query slots
+                                 + NW * HS * D * 4            // merge buffer o
                                  + 2 * NW * HS * 4            // merge m, l
                                  + 64 * 8                     // barriers
                                  + 1024;                      // alignment slack
@@ -160,13 +162,15 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_align1024(smem_raw);
     float *sbuf = reinterpret_cast<float *>(smem + NS * C::STAGE);  // [NS][KH][2][64] K, V scales per stage
-    float *ow = sbuf + NS * KH * 2 * KT;                            // [NW][HS][D]
+    float *qbuf = sbuf + NS * KH * 2 * KT;                          // [2][KH * G][D] query rows of an item
+    float *ow = qbuf + 2 * KH * HS * D;                             // [NW][HS][D]
     float *mw = ow + NW * HS * D;                                   // [NW][HS]
     float *lw = mw + NW * HS;                                       // [NW][HS]
     uint64_t *bars = reinterpret_cast<uint64_t *>(lw + NW * HS);
-    // bars: full[NS], empty[NS], merged, drained
+    // bars: full[NS], empty[NS], merged, drained, qfull[2], qempty[2]
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NS);
     const uint32_t merged = smem_u32(bars + 2 * NS), drained = smem_u32(bars + 2 * NS + 1);
+    const uint32_t qfull0 = smem_u32(bars + 2 * NS + 2), qempty0 = smem_u32(bars + 2 * NS + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -176,21 +180,34 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
         }
         mbar_init(merged, NW);
         mbar_init(drained, NW);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(qfull0 + 8 * s, 1);
+            mbar_init(qempty0 + 8 * s, NW);
+        }
         fence_barrier_init();
     }
     __syncthreads();
     griddep_launch_dependents();  // the chunk combine may launch now and wait for this grid's results
+    griddep_wait();  // launched as a programmatic dependent: wait for the previous kernels' writes
 
     if (warp == NW) {
         // ------------------------------------------------------------------ producer
-        // one lane: per tile the TMA loads of the K / V codes and two bulk copies of their 64 K / V scales
-        // (256-byte runs of the head-major scale rows; keys past t_end come along and are masked)
+        // one lane: per item a bulk copy of its query rows into one of two slots, so the consumers never wait
+        // on a global load between items; per tile the TMA loads of the K / V codes and two bulk copies of
+        // their 64 K / V scales (256-byte runs of the head-major scale rows; keys past t_end come along and
+        // are masked)
         if (lane != 0) return;
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
-        uint32_t it = 0;
-        for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+        const uint32_t qbytes = (uint32_t)(KH * p.G * D * 4);
+        uint32_t it = 0, qn = 0;
+        for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++qn) {
             const ItemInfo inf = item_info<KH>(p, item, false);
+            const uint32_t qs = qn & 1;  // slot use qn >> 1 waits for the consumers' release of the previous use
+            if (!mbar_wait(qempty0 + 8 * qs, ((qn >> 1) & 1) ^ 1, p.dev_err)) return;
+            mbar_arrive_expect_tx(qfull0 + 8 * qs, qbytes);
+            bulk_load(smem_u32(qbuf + qs * KH * HS * D), p.q + ((size_t)inf.b * p.Hq + (size_t)inf.kvh * p.G) * D,
+                      qbytes, qfull0 + 8 * qs);
             for (int i = 0; i < inf.ntiles; ++i, ++it) {
                 const uint32_t s = it % NS, ph = (it / NS) & 1;
                 if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.dev_err)) return;
@@ -229,15 +246,22 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
         // ---- query fragments: head g of the kv group, dims (4t .. 4t+3) of every 16-dim chunk, scaled by
         //      2^e so that the head's largest |q * qscale| lies in [2^13, 2^14), split into f16 hi / lo
         const bool on = g < p.G;
-        const float *qh = p.q + ((size_t)inf.b * p.Hq + (size_t)(inf.kvh + hh) * p.G + (on ? g : 0)) * D;
+        const uint32_t qs = item_no & 1;
+        if (!mbar_wait(qfull0 + 8 * qs, (item_no >> 1) & 1, p.dev_err)) return;
+        const float *qh = qbuf + qs * KH * HS * D + (hh * p.G + (on ? g : 0)) * D;
         float qv[KS][4];
         float amax = 0.f;
 #pragma unroll
         for (int kc = 0; kc < KS; ++kc) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) qv[kc][e] = on ? qh[kc * 16 + 4 * t + e] * p.qscale : 0.f;
+            const float4 q4 = *reinterpret_cast<const float4 *>(qh + kc * 16 + 4 * t);
+            qv[kc][0] = on ? q4.x * p.qscale : 0.f;
+            qv[kc][1] = on ? q4.y * p.qscale : 0.f;
+            qv[kc][2] = on ? q4.z * p.qscale : 0.f;
+            qv[kc][3] = on ? q4.w * p.qscale : 0.f;
             amax = fmax3(amax, fmaxf(fabsf(qv[kc][0]), fabsf(qv[kc][1])), fmaxf(fabsf(qv[kc][2]), fabsf(qv[kc][3])));
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(qempty0 + 8 * qs);
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
         int e2 = 0;
@@ -410,7 +434,7 @@ cudaError_t launch_i8_t(cudaStream_t st, const CUtensorMap &tk, const CUtensorMa
     if (e != cudaSuccess) return e;
     p.n_items /= KH;  // items of KH kv heads each
     const int grid = p.n_items < sm_count ? p.n_items : sm_count;
-    attn_decode_i8_kernel<D, NG, KH><<<grid, C::THREADS, C::SMEM, st>>>(tk, tv, p);
+    launch_pdl(attn_decode_i8_kernel<D, NG, KH>, grid, dim3(C::THREADS), C::SMEM, st, tk, tv, p);
     return cudaGetLastError();
 }
 

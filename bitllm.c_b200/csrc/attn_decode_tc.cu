@@ -41,7 +41,9 @@ struct TcCfg {
     static constexpr int BOX = 64 * 128;              // one 64-key x 64-dim swizzled box, bytes
     static constexpr int TILE = (D / 64) * BOX;       // K (or V) tile bytes
     static constexpr int STAGE = 2 * TILE;
+    static constexpr int QSLOT = HS * D * 4;          // the query rows of an item (G heads)
     static constexpr int EXTRA = CW * 16 * HS * 4     // P transpose
+                                 + 2 * QSLOT          // two query slots
                                  + 64 * 8             // barriers
                                  + 1024;              // alignment slack
     static constexpr int FIT = ((kSmemLimit - EXTRA) / STAGE) > 8 ? 8 : ((kSmemLimit - EXTRA) / STAGE);
@@ -96,9 +98,11 @@ __global__ void __launch_bounds__(TcCfg<D, NB, NG>::THREADS, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_align1024(smem_raw);
     float *pbuf = reinterpret_cast<float *>(smem + NS * C::STAGE);  // [4][16][HS]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(pbuf + C::CW * 16 * HS);
-    // bars: full[NS], empty[NS]
+    float *qbuf = pbuf + C::CW * 16 * HS;                           // [2][G][D] query rows of an item
+    uint64_t *bars = reinterpret_cast<uint64_t *>(qbuf + 2 * HS * D);
+    // bars: full[NS], empty[NS], qfull[2], qempty[2]
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NS);
+    const uint32_t qfull0 = smem_u32(bars + 2 * NS), qempty0 = smem_u32(bars + 2 * NS + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -106,19 +110,32 @@ __global__ void __launch_bounds__(TcCfg<D, NB, NG>::THREADS, 1)
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, kConsumers);
         }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(qfull0 + 8 * s, 1);
+            mbar_init(qempty0 + 8 * s, C::CW);
+        }
         fence_barrier_init();
     }
     __syncthreads();
     griddep_launch_dependents();  // the chunk combine may launch now and wait for this grid's results
+    griddep_wait();  // launched as a programmatic dependent: wait for the previous kernels' writes
 
     if (warp == C::CW) {
         // ------------------------------------------------------------------ producer
+        // one lane: per item a bulk copy of its query rows into one of two slots (the consumers never wait on
+        // a global load between items), then the item's K / V tiles
         if (lane != 0) return;
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
-        uint32_t it = 0;
-        for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+        const uint32_t qbytes = (uint32_t)(p.G * D * 4);
+        uint32_t it = 0, qn = 0;
+        for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++qn) {
             const ItemInfo inf = item_info(p, item, false);
+            const uint32_t qs = qn & 1;  // slot use qn >> 1 waits for the consumers' release of the previous use
+            if (!mbar_wait(qempty0 + 8 * qs, ((qn >> 1) & 1) ^ 1, p.dev_err)) return;
+            mbar_arrive_expect_tx(qfull0 + 8 * qs, qbytes);
+            bulk_load(smem_u32(qbuf + qs * HS * D), p.q + ((size_t)inf.b * p.Hq + (size_t)inf.kvh * p.G) * D, qbytes,
+                      qfull0 + 8 * qs);
             for (int i = 0; i < inf.ntiles; ++i, ++it) {
                 const uint32_t s = it % NS, ph = (it / NS) & 1;
                 if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.dev_err)) return;
@@ -140,31 +157,37 @@ __global__ void __launch_bounds__(TcCfg<D, NB, NG>::THREADS, 1)
     const int g = lane >> 2, t = lane & 3;
     const int grp = warp / kConsumers, sl = warp % kConsumers;  // group, 16-key slice of the tile
     float *pw = pbuf + warp * 16 * HS;
-    uint32_t it = 0;
-    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+    uint32_t it = 0, item_no = 0;
+    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++item_no) {
         const ItemInfo inf = item_info(p, item, warp == 0 && lane == 0);
 
         // Q^T fragments: column g of the 8 is head (g & 3) of the block, hi part for g < 4, lo for g >= 4
+        const uint32_t qs = item_no & 1;
+        if (!mbar_wait(qfull0 + 8 * qs, (item_no >> 1) & 1, p.dev_err)) return;
         uint32_t qf[NB][MT][2];
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb) {
             const int j = nb * 4 + (g & 3);
             const bool on = j < p.G;
-            const float *qh = p.q + (size_t)inf.b * p.Hq * D + (size_t)(inf.kvh * p.G + (on ? j : 0)) * D;
+            const float *qh = qbuf + qs * HS * D + (on ? j : 0) * D;
 #pragma unroll
             for (int kc = 0; kc < MT; ++kc) {
                 float v[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int d = kc * 16 + 2 * t + (e & 1) + (e >> 1) * 8;
+                for (int e2 = 0; e2 < 2; ++e2) {  // dims (2t, 2t+1) and (2t+8, 2t+9) of the 16-dim chunk
+                    const float2 q2 = *reinterpret_cast<const float2 *>(qh + kc * 16 + 2 * t + 8 * e2);
                     float hi, lo;
-                    split_bf16(on ? qh[d] * p.qscale : 0.f, hi, lo);
-                    v[e] = g < 4 ? hi : lo;
+                    split_bf16(on ? q2.x * p.qscale : 0.f, hi, lo);
+                    v[2 * e2] = g < 4 ? hi : lo;
+                    split_bf16(on ? q2.y * p.qscale : 0.f, hi, lo);
+                    v[2 * e2 + 1] = g < 4 ? hi : lo;
                 }
                 qf[nb][kc][0] = pack_bf16x2(v[0], v[1]);
                 qf[nb][kc][1] = pack_bf16x2(v[2], v[3]);
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(qempty0 + 8 * qs);
 
         float oacc[NB][MT][4];
         float m_run[NB][2], l_run[NB][2];
@@ -354,7 +377,7 @@ cudaError_t launch_tc_t(cudaStream_t st, const CUtensorMap &tk, const CUtensorMa
                                          C::SMEM);
     if (e != cudaSuccess) return e;
     const int grid = p.n_items < sm_count ? p.n_items : sm_count;
-    attn_decode_tc_kernel<D, NB, NG><<<grid, C::THREADS, C::SMEM, st>>>(tk, tv, p);
+    launch_pdl(attn_decode_tc_kernel<D, NB, NG>, grid, dim3(C::THREADS), C::SMEM, st, tk, tv, p);
     return cudaGetLastError();
 }
 

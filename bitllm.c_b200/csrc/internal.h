@@ -235,6 +235,24 @@ cudaError_t launch_attend_decode_f32(cudaStream_t st, const CUtensorMap &tk, con
 cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv,
                                     const DecodeArgs &a, int nchunk, int chunk_keys, float *part_o,
                                     float2 *part_ml, int sm_count);
+// Launch `kernel` as a programmatic dependent of the previous kernel on `st`: its CTAs may start while that kernel
+// drains, so the kernel must call griddepcontrol.wait (griddep_wait) before it reads anything the previous kernels
+// wrote, and may call griddepcontrol.launch_dependents to let the next one do the same.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // KV heads a work item of the INT8 tensor-core decode covers: both heads of a 128-byte cache row at head_dim 64
 // with an even kv-head count (attn_decode_i8.cu), else one.
 inline int decode_i8_heads_per_item(int D, int Hkv) { return D == 64 && Hkv % 2 == 0 ? 2 : 1; }

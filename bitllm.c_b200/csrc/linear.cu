@@ -334,17 +334,7 @@ cudaError_t go(cudaStream_t st, LinArgs a, size_t smem, int sm_count) {
     if (grid > per_sm * sm_count) grid = per_sm * sm_count;
     // programmatic dependent launch: the CTAs may start while the previous kernel on the stream drains; each one
     // loads its first weights and then waits for that kernel's completion (griddepcontrol.wait) before reading x
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, a);
+    return launch_pdl(kernel, dim3(grid), dim3(kThreads), smem, st, a);
 }
 
 template <int WT, bool G>

@@ -435,17 +435,7 @@ cudaError_t go(cudaStream_t st, MmaArgs a, size_t smem, int sm_count) {
     const int rg = kWarps / ks;
     int grid = (n_rt + rg - 1) / rg;
     if (grid > per_sm * sm_count) grid = per_sm * sm_count;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, a);
+    return launch_pdl(kernel, dim3(grid), dim3(kThreads), smem, st, a);
 }
 
 template <int WT>

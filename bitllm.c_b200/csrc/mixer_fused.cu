@@ -38,6 +38,8 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
     constexpr int NP = DK / RP;        // passes
     constexpr int NW = THREADS / 32;
     static_assert(LPR <= 32 && 32 % LPR == 0 && DK % RP == 0, "tile shape");
+    griddep_launch_dependents();
+    griddep_wait();  // launched as a programmatic dependent: the previous kernels' writes (S included) are visible
     const int h = blockIdx.x, b = blockIdx.y;
     const int H = a.H;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -291,6 +293,8 @@ __global__ void __launch_bounds__(256) fullatt_prep_warp_kernel(const AttnPrepAr
     const int hd = a.hd, nh = a.nh, nkv = a.nkv, half = a.n_rot / 2;
     const int per_row = nh + nkv + 1;
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    griddep_launch_dependents();
+    griddep_wait();  // launched as a programmatic dependent: wait for the previous kernels' writes
     if (gw >= a.B * a.n_tok * per_row) return;  // warp-uniform; the kernel has no block barrier
     const int r = gw / per_row, hh = gw % per_row, b = r / a.n_tok;
     const int p = a.pos ? a.pos[b] : a.start_pos + r % a.n_tok;
@@ -369,7 +373,7 @@ cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *
     *supported = true;
     const dim3 grid(a.H, a.B);
     auto run = [&](auto kernel, int threads, int smem) {  // smem: S rows [0, dk/2), at most 32 KB
-        kernel<<<grid, threads, smem, st>>>(a);
+        launch_pdl(kernel, grid, dim3(threads), smem, st, a);
         return cudaGetLastError();
     };
     if (a.dk == 128 && a.dv == 128) return run(deltanet_core_kernel<128, 128, 256>, 256, 64 * 128 * 4);
@@ -392,8 +396,8 @@ cudaError_t launch_fullatt_prep(cudaStream_t st, const AttnPrepArgs &a) {
     }
     const long warps = (long)a.B * a.n_tok * (a.nh + a.nkv + 1);
     const unsigned blocks = (unsigned)((warps + 7) / 8);
-    if (vpl == 2) fullatt_prep_warp_kernel<2><<<blocks, 256, 0, st>>>(a);
-    else if (vpl == 4) fullatt_prep_warp_kernel<4><<<blocks, 256, 0, st>>>(a);
-    else fullatt_prep_warp_kernel<8><<<blocks, 256, 0, st>>>(a);
+    if (vpl == 2) launch_pdl(fullatt_prep_warp_kernel<2>, dim3(blocks), dim3(256), 0, st, a);
+    else if (vpl == 4) launch_pdl(fullatt_prep_warp_kernel<4>, dim3(blocks), dim3(256), 0, st, a);
+    else launch_pdl(fullatt_prep_warp_kernel<8>, dim3(blocks), dim3(256), 0, st, a);
     return cudaGetLastError();
 }

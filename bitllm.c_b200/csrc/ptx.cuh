@@ -41,14 +41,18 @@ EIF_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
         : "memory");
 }
 
+// The waiting thread may be suspended until the phase completes, for up to kMbarSuspendNs per call (a hint),
+// so a warp that waits for a tile or a free stage takes no issue slots from the warps that compute.
+constexpr uint32_t kMbarSuspendNs = 1000000;
+
 EIF_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "n"(kMbarSuspendNs)
         : "memory");
     return ok != 0;
 }
