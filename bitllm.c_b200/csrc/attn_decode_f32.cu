@@ -44,7 +44,8 @@ struct F32Cfg {
     static constexpr int BOX = KT * 128;              // KT keys x 32 floats, 128-byte swizzle
     static constexpr int TILE = (D / 32) * BOX;       // K (or V) tile bytes
     static constexpr int STAGE = 2 * TILE;
-    static constexpr int EXTRA = NW * HS * D * 4      // per-warp query copies
+    static constexpr int EXTRA = 2 * HS * D * 4       // two query slots (an item's rows, bulk-copied)
+                                 + NW * HS * D * 4    // per-warp scaled query copies
                                  + NW * 32 * HS * 4   // per-warp probabilities
                                  + NW * HS * D * 4    // merge buffer o
                                  + 2 * NW * HS * 4    // merge m, l
@@ -113,15 +114,17 @@ __global__ void __launch_bounds__(F32Cfg<D>::THREADS, 1)
     static_assert(DL == 2 || DL == 4 || DL == 8, "head_dim 64, 128 or 256");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_align1024(smem_raw);
-    float *sq = reinterpret_cast<float *>(smem + NS * C::STAGE);  // [NW][HS][D]
-    float *pw = sq + NW * HS * D;                                  // [NW][KT][HS]
+    float *qbuf = reinterpret_cast<float *>(smem + NS * C::STAGE);  // [2][G][D] query rows of an item
+    float *sq = qbuf + 2 * HS * D;                                   // [NW][HS][D]
+    float *pw = sq + NW * HS * D;                                    // [NW][KT][HS]
     float *ow = pw + NW * KT * HS;                                 // [NW][HS][D]
     float *mw = ow + NW * HS * D;                                  // [NW][HS]
     float *lw = mw + NW * HS;                                      // [NW][HS]
     uint64_t *bars = reinterpret_cast<uint64_t *>(lw + NW * HS);
-    // bars: full[NS], empty[NS], merged, drained
+    // bars: full[NS], empty[NS], merged, drained, qfull[2], qempty[2]
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NS);
     const uint32_t merged = smem_u32(bars + 2 * NS), drained = smem_u32(bars + 2 * NS + 1);
+    const uint32_t qfull0 = smem_u32(bars + 2 * NS + 2), qempty0 = smem_u32(bars + 2 * NS + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -131,19 +134,32 @@ __global__ void __launch_bounds__(F32Cfg<D>::THREADS, 1)
         }
         mbar_init(merged, NW);
         mbar_init(drained, NW);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(qfull0 + 8 * s, 1);
+            mbar_init(qempty0 + 8 * s, NW);
+        }
         fence_barrier_init();
     }
     __syncthreads();
     griddep_launch_dependents();  // the chunk combine may launch now and wait for this grid's results
+    griddep_wait();  // launched as a programmatic dependent: wait for the previous kernels' writes
 
     if (warp == NW) {
         // ------------------------------------------------------------------ producer
+        // one lane: per item a bulk copy of its query rows into one of two slots (the consumers never wait on
+        // a global load between items), then the item's K / V tiles
         if (lane != 0) return;
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
-        uint32_t it = 0;
-        for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+        constexpr uint32_t qbytes = (uint32_t)(G * D * 4);
+        uint32_t it = 0, qn = 0;
+        for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++qn) {
             const ItemInfo inf = item_info(p, item, false, KT);
+            const uint32_t qs = qn & 1;  // slot use qn >> 1 waits for the consumers' release of the previous use
+            if (!mbar_wait(qempty0 + 8 * qs, ((qn >> 1) & 1) ^ 1, p.dev_err)) return;
+            mbar_arrive_expect_tx(qfull0 + 8 * qs, qbytes);
+            bulk_load(smem_u32(qbuf + qs * HS * D), p.q + ((size_t)inf.b * p.Hq + (size_t)inf.kvh * G) * D, qbytes,
+                      qfull0 + 8 * qs);
             for (int i = 0; i < inf.ntiles; ++i, ++it) {
                 const uint32_t s = it % NS, ph = (it / NS) & 1;
                 if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.dev_err)) return;
@@ -168,9 +184,12 @@ __global__ void __launch_bounds__(F32Cfg<D>::THREADS, 1)
     uint32_t it_base = 0, item_no = 0;
     for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++item_no) {
         const ItemInfo inf = item_info(p, item, warp == 0 && lane == 0, KT);
-        const float *qh = p.q + ((size_t)inf.b * p.Hq + (size_t)inf.kvh * G) * D;
+        const uint32_t qs = item_no & 1;
+        if (!mbar_wait(qfull0 + 8 * qs, (item_no >> 1) & 1, p.dev_err)) return;
+        const float *qh = qbuf + qs * HS * D;
         for (int i = lane; i < G * D; i += 32) sqw[i] = qh[i] * p.qscale;  // the G heads' rows, [h][D]
         __syncwarp();
+        if (lane == 0) mbar_arrive(qempty0 + 8 * qs);
 
         float m[G], l[G], acc[G][DL];
 #pragma unroll
@@ -319,7 +338,7 @@ cudaError_t launch_f32_t(cudaStream_t st, const CUtensorMap &tk, const CUtensorM
         cudaFuncSetAttribute(attn_decode_f32_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     const int grid = p.n_items < sm_count ? p.n_items : sm_count;
-    attn_decode_f32_kernel<D, G><<<grid, C::THREADS, C::SMEM, st>>>(tk, tv, p);
+    launch_pdl(attn_decode_f32_kernel<D, G>, grid, dim3(C::THREADS), C::SMEM, st, tk, tv, p);
     return cudaGetLastError();
 }
 

@@ -123,6 +123,7 @@ struct DeltaCoreArgs {
     float *out;  // [B][H*dv]
     int B, H, dk, dv, conv_k;
     unsigned *dev_err;
+    int stage_inputs;  // set by launch_deltanet_core: the conv windows, weights, inputs, z and norm_w come by bulk copies
 };
 cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *supported);
 

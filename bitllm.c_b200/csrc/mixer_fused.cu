@@ -48,12 +48,18 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
     const int key_dim = H * DK, conv_dim = 2 * key_dim + H * DV;
 
     constexpr int NH = NP / 2;  // passes over the rows staged in shared memory; the other NH in registers
+    constexpr int NC = 2 * DK + DV;  // the head's conv channels: q, k, v
     __shared__ float sq[DK], sk[DK], sv[DV];
     __shared__ float2 red[NW];
-    __shared__ float4 cred[2][NW][LPR];  // one buffer per column sum: no barrier between their uses
     __shared__ float gates[2];
     __shared__ __align__(8) uint64_t s_bar;
-    extern __shared__ __align__(128) float Ssm[];  // S rows [0, DK/2)
+    // dynamic: S rows [0, DK/2) | z, norm_w [2][DV] | staging: conv windows [NC][ck], conv weights [NC][ck],
+    // inputs [NC] (stage_inputs), dead after the conv and then reused for the two column-sum buffers
+    extern __shared__ __align__(128) float Ssm[];
+    float *zn = Ssm + DK / 2 * DV;
+    float *stg = zn + 2 * DV;
+    float4(*cred)[NW][LPR] = reinterpret_cast<float4(*)[NW][LPR]>(stg);  // [2][NW][LPR]: no barrier between uses
+    const bool staged = a.stage_inputs != 0;
 
     float *Sh = a.S + bh * DK * DV;
     const int col0 = lc * 4;
@@ -61,13 +67,29 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
     const float4 *Smem = reinterpret_cast<const float4 *>(Ssm) + col0 / 4;
     // S rows [0, DK/2) into shared memory (bulk copies completing on s_bar), rows [DK/2, DK) into registers
     const uint32_t sbar = smem_u32(&s_bar);
+    const int ck = a.conv_k;
     if (tid == 0) {
         constexpr uint32_t bytes = DK / 2 * DV * 4, piece = bytes < 16384 ? bytes : 16384;
         mbar_init(sbar, 1);
         fence_barrier_init();
-        mbar_arrive_expect_tx(sbar, bytes);
+        // staged: everything else the CTA reads rides on the same barrier, so its inputs cost one round trip
+        // (the conv windows of the q, k and v channel blocks, their weights, the raw inputs, z and norm_w)
+        const uint32_t wbytes = (uint32_t)(NC * ck * 4);
+        mbar_arrive_expect_tx(sbar, bytes + (staged ? 2 * DV * 4 + 2 * wbytes + NC * 4 : 0));
         for (uint32_t off = 0; off < bytes; off += piece)
             bulk_load(smem_u32(Ssm) + off, reinterpret_cast<const char *>(Sh) + off, piece, sbar);
+        if (staged) {
+            bulk_load(smem_u32(zn), a.z + bh * DV, DV * 4, sbar);
+            bulk_load(smem_u32(zn + DV), a.norm_w, DV * 4, sbar);
+#pragma unroll
+            for (int blk = 0; blk < 3; ++blk) {  // local channels [i0, i0 + n) = global channels [c0, c0 + n)
+                const int i0 = blk * DK, n = blk < 2 ? DK : DV;
+                const int c0 = blk == 0 ? h * DK : (blk == 1 ? key_dim + h * DK : 2 * key_dim + h * DV);
+                bulk_load(smem_u32(stg + i0 * ck), a.conv + ((size_t)b * conv_dim + c0) * ck, n * ck * 4, sbar);
+                bulk_load(smem_u32(stg + (NC + i0) * ck), a.conv_w + (size_t)c0 * ck, n * ck * 4, sbar);
+                bulk_load(smem_u32(stg + 2 * NC * ck + i0), a.qkv + (size_t)b * conv_dim + c0, n * 4, sbar);
+            }
+        }
     }
     float4 sreg[NH];
 #pragma unroll
@@ -82,24 +104,47 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
     }
 
     // causal conv1d + SiLU on this head's channels: q [h*DK, +DK), k [key_dim + h*DK, +DK), v [2*key_dim + h*DV, +DV)
-    const int ck = a.conv_k;
-    for (int i = tid; i < 2 * DK + DV; i += THREADS) {
-        const int c = i < DK ? h * DK + i : (i < 2 * DK ? key_dim + h * DK + (i - DK) : 2 * key_dim + h * DV + (i - 2 * DK));
-        float *row = a.conv + ((size_t)b * conv_dim + c) * ck;
-        const float *w = a.conv_w + (size_t)c * ck;
-        const float xin = a.qkv[(size_t)b * conv_dim + c];
-        float acc = 0.f;
-        for (int j = 0; j < ck - 1; ++j) {
-            const float v = row[j + 1];
-            row[j] = v;
-            acc += v * w[j];
+    __syncthreads();  // the barrier's initialisation is visible to every thread
+    // a wait that gives up leaves S and the conv windows untouched (the error word tells the host)
+    const bool s_ok0 = staged ? mbar_wait(sbar, 0, a.dev_err) : true;
+    if (staged) {
+        const float *cwin = stg, *cwt = stg + NC * ck, *cx = stg + 2 * NC * ck;
+        for (int i = tid; i < NC; i += THREADS) {
+            const int c = i < DK ? h * DK + i : (i < 2 * DK ? key_dim + h * DK + (i - DK) : 2 * key_dim + h * DV + (i - 2 * DK));
+            const float *wr = cwin + i * ck, *w = cwt + i * ck;
+            const float xin = cx[i];
+            float acc = 0.f;
+            for (int j = 0; j < ck - 1; ++j) acc += wr[j + 1] * w[j];
+            acc += xin * w[ck - 1];
+            if (s_ok0) {
+                float *row = a.conv + ((size_t)b * conv_dim + c) * ck;
+                for (int j = 0; j < ck - 1; ++j) row[j] = wr[j + 1];
+                row[ck - 1] = xin;
+            }
+            const float y = silu_f(acc);
+            if (i < DK) sq[i] = y;
+            else if (i < 2 * DK) sk[i - DK] = y;
+            else sv[i - 2 * DK] = y;
         }
-        row[ck - 1] = xin;
-        acc += xin * w[ck - 1];
-        const float y = silu_f(acc);
-        if (i < DK) sq[i] = y;
-        else if (i < 2 * DK) sk[i - DK] = y;
-        else sv[i - 2 * DK] = y;
+    } else {  // conv state arrays not staged: read in place
+        for (int i = tid; i < 2 * DK + DV; i += THREADS) {
+            const int c = i < DK ? h * DK + i : (i < 2 * DK ? key_dim + h * DK + (i - DK) : 2 * key_dim + h * DV + (i - 2 * DK));
+            float *row = a.conv + ((size_t)b * conv_dim + c) * ck;
+            const float *w = a.conv_w + (size_t)c * ck;
+            const float xin = a.qkv[(size_t)b * conv_dim + c];
+            float acc = 0.f;
+            for (int j = 0; j < ck - 1; ++j) {
+                const float v = row[j + 1];
+                row[j] = v;
+                acc += v * w[j];
+            }
+            row[ck - 1] = xin;
+            acc += xin * w[ck - 1];
+            const float y = silu_f(acc);
+            if (i < DK) sq[i] = y;
+            else if (i < 2 * DK) sk[i - DK] = y;
+            else sv[i - 2 * DK] = y;
+        }
     }
     if (tid == 0) {
         gates[0] = 1.0f / (1.0f + expf(-braw));
@@ -144,8 +189,7 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
     };
 
     const float decay = expf(gates[1]), bet = gates[0];
-    // a wait that gives up leaves S untouched (the error word tells the host)
-    const bool s_ok = mbar_wait(sbar, 0, a.dev_err);
+    const bool s_ok = staged ? s_ok0 : mbar_wait(sbar, 0, a.dev_err);
     // pass p reads row rg + p * RP: from shared memory for p < NH, from registers after
     auto row = [&](int p) -> float4 { return p < NH ? Smem[(rg + p * RP) * (DV / 4)] : sreg[p - NH]; };
     float4 e = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -179,8 +223,8 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
     for (int off = 1; off < LPR; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     if (rg == 0) {
         const float rms = 1.0f / sqrtf(ss / DV + 1e-6f);
-        const float *z = a.z + bh * DV + col0;
-        const float *nw = a.norm_w + col0;
+        const float *z = (staged ? zn : a.z + bh * DV) + col0;
+        const float *nw = (staged ? zn + DV : a.norm_w) + col0;
         float4 y;
         y.x = o.x * rms * nw[0] * silu_f(z[0]);
         y.y = o.y * rms * nw[1] * silu_f(z[1]);
@@ -369,16 +413,32 @@ __global__ void __launch_bounds__(256) fullatt_prep_warp_kernel(const AttnPrepAr
 
 }  // namespace
 
-cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *supported) {
+cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a0, bool *supported) {
     *supported = true;
-    const dim3 grid(a.H, a.B);
-    auto run = [&](auto kernel, int threads, int smem) {  // smem: S rows [0, dk/2), at most 32 KB
+    const dim3 grid(a0.H, a0.B);
+    // the inputs ride on the S barrier as bulk copies when every array is 16-byte aligned (the channel blocks'
+    // offsets then are too: d_k and d_v are multiples of 4) and the windows are short enough to stage
+    DeltaCoreArgs a = a0;
+    auto al = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    a.stage_inputs = a.conv_k >= 1 && a.conv_k <= 4 && al(a.conv) && al(a.conv_w) && al(a.qkv) && al(a.z) &&
+                     al(a.norm_w);
+    auto run = [&](auto kernel, int threads) {
+        // dynamic shared memory: S rows [0, dk/2) | z, norm_w | the larger of the staged inputs and the two
+        // column-sum buffers (one float4 per thread each)
+        const size_t nc = 2 * (size_t)a.dk + a.dv;
+        const size_t csum = 2 * (size_t)threads * 16, staging = a.stage_inputs ? nc * (2 * a.conv_k + 1) * 4 : 0;
+        const size_t smem = (size_t)a.dk / 2 * a.dv * 4 + 2 * (size_t)a.dv * 4 + (staging > csum ? staging : csum);
+        // static + dynamic shared memory above 48 KB needs the opt-in (the static part is under 8 KB)
+        if (smem > 40 * 1024) {
+            const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+        }
         launch_pdl(kernel, grid, dim3(threads), smem, st, a);
         return cudaGetLastError();
     };
-    if (a.dk == 128 && a.dv == 128) return run(deltanet_core_kernel<128, 128, 256>, 256, 64 * 128 * 4);
-    if (a.dk == 128 && a.dv == 64) return run(deltanet_core_kernel<128, 64, 256>, 256, 64 * 64 * 4);
-    if (a.dk == 64 && a.dv == 64) return run(deltanet_core_kernel<64, 64, 128>, 128, 32 * 64 * 4);
+    if (a.dk == 128 && a.dv == 128) return run(deltanet_core_kernel<128, 128, 256>, 256);
+    if (a.dk == 128 && a.dv == 64) return run(deltanet_core_kernel<128, 64, 256>, 256);
+    if (a.dk == 64 && a.dv == 64) return run(deltanet_core_kernel<64, 64, 128>, 128);
     *supported = false;
     return cudaSuccess;
 }
