@@ -14,21 +14,23 @@
 //   warps 0 .. 4NG-1 consumers in NG groups of 4 that take tiles round-robin, so NG tiles are in flight
 //           per SM: NG = 4 at head_dim 64, 2 at 128, 1 at 256, as many as the registers allow; within a
 //           group each warp takes 16 keys of the tile:
-//     S = Q K^T   A = the query, MMA rows 0-7 = heads (high f16 part), rows 8-15 = the same heads (low part),
-//                 so all G <= 8 heads of the kv head ride in one m16n8k16; B = the K codes, loaded with
-//                 ldmatrix from the int8 tile viewed as 16-bit pairs and widened in registers to exact f16
-//                 (byte permute into 0x64uu = 1024 + (x + 128), one f16x2 subtract).  ldmatrix hands each
-//                 thread 4 consecutive dims; the MMA's k slots (2t, 2t+1, 2t+8, 2t+9) are mapped to dims
-//                 (4t .. 4t+3) for both operands, a permutation of the reduction that leaves the sum alone;
+//     S = Q K^T   in exact integer arithmetic (mma.m16n8k32 on 8-bit operands, int32 accumulators): the
+//                 query of each head, scaled by a power of two so that its largest |q| lies in [2^21, 2^22),
+//                 is rounded to integers and split into bytes q = hi * 2^16 + mid * 2^8 + lo; one u8 x s8
+//                 MMA takes mid (rows 0-7 = the G <= 8 heads) and lo (rows 8-15), one s8 x s8 MMA takes hi;
+//                 B = the K codes exactly as ldmatrix delivers them from the int8 tile viewed as 16-bit pairs
+//                 (key g, dims 4t .. 4t+3 = the MMA's k slots 4t .. 4t+3): no widening of K at all;
 //     softmax     online in base 2; the S accumulator of a thread (head g, keys 2t, 2t+1, 2t+8, 2t+9) is
 //                 already the A-fragment layout of P, so no transpose;
 //     O += P V    A = p * v_scale (f16 high / low rows as for q); B = the V codes from ldmatrix.trans of
 //                 the 16-bit view, which gives each thread two keys of two adjacent dims: the even dims
 //                 and the odd dims of a 16-dim chunk form two n-tiles.
-// Exactness: codes are exact in f16, products are exact in the fp32 accumulator; the query and the
-// probabilities are split as hi + lo (22 significant bits) after scaling by powers of two into f16's
-// normal range (q: per head to a maximum in [2^13, 2^14); p * v_scale: by 2^12); both scalings are undone
-// exactly.  Results match fp32 arithmetic on the codes to ~1e-7.
+// Exactness: the score sums are exact integers (the query quantised to 22 bits of its head's largest
+// element), combined with one rounding; in P V codes are exact in f16, products are exact in the fp32
+// accumulator and p * v_scale is split as hi + lo (22 significant bits) after scaling by a power of two that
+// keeps the largest v_scale seen times 2^k below 2^14 (adapted tile by tile, never raised, so no f16 part
+// overflows whatever the values' magnitude); the scalings are undone exactly.  Results match fp32 arithmetic
+// on the codes to ~1e-7.
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -42,7 +44,6 @@ constexpr int KT = 64;          // keys per tile
 constexpr int kGroup = 4;       // consumer warps per group, 16 keys of a tile each
 constexpr int kSmemLimit = 227 * 1024;
 constexpr int HS = 8;           // head slots: MMA rows g (high part) and g + 8 (low part)
-constexpr float kPScale = 4096.f, kPUnscale = 1.f / 4096.f;
 
 // NG consumer groups take alternate tiles (more tiles in flight per SM where the registers allow).
 // KH kv heads a stage: 2 ("pair" mode, head_dim 64 with an even kv-head count) puts both halves of every 128-byte
@@ -120,7 +121,6 @@ __device__ __forceinline__ uint32_t codes_f16x2(uint32_t u, uint32_t sel) {
     asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
     return r;
 }
-constexpr uint32_t kSelB01 = 0x5140, kSelB23 = 0x5342;  // bytes (0, 1) / (2, 3)
 constexpr uint32_t kSelB02 = 0x5240, kSelB13 = 0x5341;  // bytes (0, 2) / (1, 3)
 
 // (x0, x1) = hi + lo with hi = f16(x), lo = f16(x - hi); x0 in the low halves.
@@ -130,6 +130,31 @@ __device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t &hi, ui
     const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
     hi = *reinterpret_cast<const uint32_t *>(&h);
     lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+// Byte b of each of x0 .. x3, packed in that order (the 4 k-slots of one 8-bit MMA fragment register).
+__device__ __forceinline__ uint32_t byte_column(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3, uint32_t b) {
+    const uint32_t sel = b | ((b + 4) << 4);
+    return __byte_perm(__byte_perm(x0, x1, sel), __byte_perm(x2, x3, sel), 0x5410);
+}
+
+// D = A(16x32, row) * B(32x8, col) + D in exact integer arithmetic: A unsigned bytes (u8) or signed (s8), B the
+// signed int8 codes.
+__device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_s8s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -243,8 +268,8 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
     for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++item_no) {
         const ItemInfo inf = item_info<KH>(p, item, warp == 0 && lane == 0);
 
-        // ---- query fragments: head g of the kv group, dims (4t .. 4t+3) of every 16-dim chunk, scaled by
-        //      2^e so that the head's largest |q * qscale| lies in [2^13, 2^14), split into f16 hi / lo
+        // ---- query fragments: head g of the kv group, dims (4t .. 4t+3) of every 16-dim chunk (the k slots
+        //      4t .. 4t+3 of the 8-bit MMA's A fragment)
         const bool on = g < p.G;
         const uint32_t qs = item_no & 1;
         if (!mbar_wait(qfull0 + 8 * qs, (item_no >> 1) & 1, p.dev_err)) return;
@@ -268,20 +293,30 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
         if (amax > 0.f && isfinite(amax)) {
             int ex;
             frexpf(amax, &ex);  // amax in [2^(ex-1), 2^ex)
-            e2 = max(-126, min(126, 14 - ex));
+            e2 = max(-126, min(126, 22 - ex));
         }
+        // the head's q as integers of at most 22 bits (its largest |q| scaled into [2^21, 2^22)), split into
+        // bytes q = hi * 2^16 + mid * 2^8 + lo: mid and lo unsigned, hi (|hi| <= 64) signed
         const float qmul = __int_as_float((127 + e2) << 23), qdiv = __int_as_float((127 - e2) << 23);
-        uint32_t qf[KS][4];
+        uint32_t qlo[KS], qmid[KS], qhi[KS];
 #pragma unroll
         for (int kc = 0; kc < KS; ++kc) {
-            split_f16x2(qv[kc][0] * qmul, qv[kc][1] * qmul, qf[kc][0], qf[kc][1]);
-            split_f16x2(qv[kc][2] * qmul, qv[kc][3] * qmul, qf[kc][2], qf[kc][3]);
+            const uint32_t x0 = (uint32_t)__float2int_rn(qv[kc][0] * qmul), x1 = (uint32_t)__float2int_rn(qv[kc][1] * qmul);
+            const uint32_t x2 = (uint32_t)__float2int_rn(qv[kc][2] * qmul), x3 = (uint32_t)__float2int_rn(qv[kc][3] * qmul);
+            qlo[kc] = byte_column(x0, x1, x2, x3, 0);
+            qmid[kc] = byte_column(x0, x1, x2, x3, 1);
+            qhi[kc] = byte_column(x0, x1, x2, x3, 2);
         }
 
         float oacc[NT][4];
 #pragma unroll
         for (int n = 0; n < NT; ++n) oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.f;
         float m_run = -INFINITY, l_run = 0.f;
+        // p * v_scale enters the f16 P operand multiplied by pmul (a power of two, uniform over the warp): p <= 1,
+        // so the largest v_scale seen times pmul below 2^14 keeps every f16 part finite; pmul is set from the
+        // first tile and only ever lowered (the accumulators are rescaled with it, exactly), whatever the
+        // magnitude of the values
+        float pmul = 0.f;
 
         for (int i = tg; i < inf.ntiles; i += TG) {  // this group's tiles of the item (its head of each)
             const uint32_t it = it_base + i;
@@ -292,32 +327,32 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
             const float *scs = sbuf + (s * KH + hh) * 2 * KT + wk;  // this warp's keys: K scales, V scales at +64
             const uint32_t kbase = smem_u32(smem + s * C::STAGE) + hh * C::TILE, vbase = kbase + KH * C::TILE;
 
-            // ---- S = Q K^T: n-tiles of keys 0-7 and 8-15 of the warp
-            float sacc[2][4];
+            // ---- S = Q K^T in integers: n-tiles of keys 0-7 and 8-15 of the warp; the K codes from ldmatrix
+            //      are the B fragments as they are (key g, dims 4t .. 4t+3 of a 16-dim chunk).  A u8 MMA takes
+            //      mid (rows g) and lo (rows g + 8), an s8 MMA hi (rows g); sums of 256 products stay in int32
+            int aml[2][4], ah[2][4];
 #pragma unroll
-            for (int n = 0; n < 2; ++n) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
+            for (int n = 0; n < 2; ++n) aml[n][0] = aml[n][1] = aml[n][2] = aml[n][3] = ah[n][0] = ah[n][1] = ah[n][2] = ah[n][3] = 0;
 #pragma unroll
             for (int kp = 0; kp < KS / 2; ++kp) {
                 uint32_t r0, r1, r2, r3;  // (keys 0-7 | 8-15) x (chunk 2kp | 2kp+1)
                 ldsm_x4(tile_addr<C::BW>(kbase, my_key, 2 * kp + (mi >> 1)), r0, r1, r2, r3);
-                r0 ^= 0x80808080u;
-                r1 ^= 0x80808080u;
-                r2 ^= 0x80808080u;
-                r3 ^= 0x80808080u;
-                const uint32_t *qa = qf[2 * kp], *qb = qf[2 * kp + 1];
-                mma_f16_16816(sacc[0], qa[0], qa[1], qa[2], qa[3], codes_f16x2(r0, kSelB01), codes_f16x2(r0, kSelB23));
-                mma_f16_16816(sacc[1], qa[0], qa[1], qa[2], qa[3], codes_f16x2(r1, kSelB01), codes_f16x2(r1, kSelB23));
-                mma_f16_16816(sacc[0], qb[0], qb[1], qb[2], qb[3], codes_f16x2(r2, kSelB01), codes_f16x2(r2, kSelB23));
-                mma_f16_16816(sacc[1], qb[0], qb[1], qb[2], qb[3], codes_f16x2(r3, kSelB01), codes_f16x2(r3, kSelB23));
+                const int c0 = 2 * kp, c1 = 2 * kp + 1;
+                mma_u8s8_16832(aml[0], qmid[c0], qlo[c0], qmid[c1], qlo[c1], r0, r2);
+                mma_u8s8_16832(aml[1], qmid[c0], qlo[c0], qmid[c1], qlo[c1], r1, r3);
+                mma_s8s8_16832(ah[0], qhi[c0], 0u, qhi[c1], 0u, r0, r2);
+                mma_s8s8_16832(ah[1], qhi[c0], 0u, qhi[c1], 0u, r1, r3);
             }
 
-            // ---- online softmax (base 2) for head g over keys 2t, 2t+1, 8+2t, 9+2t
+            // ---- online softmax (base 2) for head g over keys 2t, 2t+1, 8+2t, 9+2t; the score of a key is
+            //      hi * 2^16 + (mid * 2^8 + lo) (the bracket exact in int32), rounded once in the FMA
             const int kk[4] = {2 * t, 2 * t + 1, 8 + 2 * t, 9 + 2 * t};
             float sv[4], vsc[4];
-            sv[0] = sacc[0][0] + sacc[0][2];
-            sv[1] = sacc[0][1] + sacc[0][3];
-            sv[2] = sacc[1][0] + sacc[1][2];
-            sv[3] = sacc[1][1] + sacc[1][3];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int n = e >> 1, j = e & 1;
+                sv[e] = fmaf((float)ah[n][j], 65536.f, (float)(aml[n][j] * 256 + aml[n][2 + j]));
+            }
             float mx = -INFINITY;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {  // keys past t_end: masked (their scale slots hold stale values)
@@ -328,27 +363,46 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
             }
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            // this lane's largest V scale: p <= 1, so p * v_scale * pmul stays below 2^14 (f16 parts finite) while
+            // vmx * pmul < 2^14; checked in the rescale vote below
+            const float vmx = fmaxf(fmaxf(vsc[0], vsc[1]), fmaxf(vsc[2], vsc[3]));
+            const bool need = vmx * pmul >= 16384.f || (pmul == 0.f && vmx > 0.f);
             const float m_new = fmaxf(m_run, mx);
             const float m_use = m_new == -INFINITY ? 0.f : m_new;
             const float corr = fast_exp2(m_run - m_use);
-            float pv[4], psum = 0.f;
+            float pe[4], psum = 0.f;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float pe = fast_exp2(sv[e] - m_use);
-                psum += pe;
-                pv[e] = pe * vsc[e] * kPScale;
+                pe[e] = fast_exp2(sv[e] - m_use);
+                psum += pe[e];
             }
             l_run = l_run * corr + psum;
             m_run = m_new;
-            if (__any_sync(0xffffffffu, corr != 1.f)) {
+            if (__any_sync(0xffffffffu, corr != 1.f || need)) {  // a new running max, or a new P scale
+                float ocorr = corr;
+                if (__any_sync(0xffffffffu, need)) {  // rare: the warp's 16 keys (lanes t) agree on pmul
+                    float w = vmx;
+                    w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, 1));
+                    w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, 2));
+                    if (w * pmul >= 16384.f || pmul == 0.f) {
+                        int ex;
+                        frexpf(w, &ex);  // w in [2^(ex-1), 2^ex): w * np in [2^13, 2^14)
+                        const float np = __int_as_float((127 + max(-126, min(126, 14 - ex))) << 23);
+                        if (pmul != 0.f) ocorr *= np / pmul;  // a power of two: exact
+                        pmul = np;
+                    }
+                }
 #pragma unroll
                 for (int n = 0; n < NT; ++n) {
-                    oacc[n][0] *= corr;
-                    oacc[n][1] *= corr;
-                    oacc[n][2] *= corr;
-                    oacc[n][3] *= corr;
+                    oacc[n][0] *= ocorr;
+                    oacc[n][1] *= ocorr;
+                    oacc[n][2] *= ocorr;
+                    oacc[n][3] *= ocorr;
                 }
             }
+            float pv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) pv[e] = pe[e] * vsc[e] * pmul;
             uint32_t pa0, pa1, pa2, pa3;  // rows g (hi) / g+8 (lo); k slots = keys (2t, 2t+1) and (8+2t, 9+2t)
             split_f16x2(pv[0], pv[1], pa0, pa1);
             split_f16x2(pv[2], pv[3], pa2, pa3);
@@ -382,11 +436,12 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
         if (item_no > 0 && !mbar_wait(drained, (item_no - 1) & 1, p.dev_err)) return;
         if (on) {
             float *oh = ow + (warp * HS + g) * D;
+            const float unscale = __int_as_float(max(0, 254 - ((__float_as_int(pmul) >> 23) & 0xff)) << 23);
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
                 const int d = (n >> 1) * 16 + 4 * t + (n & 1);  // n-tile n, column 2t -> dim d; 2t+1 -> d + 2
-                oh[d] = (oacc[n][0] + oacc[n][2]) * kPUnscale;
-                oh[d + 2] = (oacc[n][1] + oacc[n][3]) * kPUnscale;
+                oh[d] = (oacc[n][0] + oacc[n][2]) * unscale;
+                oh[d + 2] = (oacc[n][1] + oacc[n][3]) * unscale;
             }
             if (t == 0) {
                 mw[warp * HS + g] = m_run;

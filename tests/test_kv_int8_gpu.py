@@ -108,6 +108,32 @@ def test_decode_vs_oracle(pkg, ctx, orc, monkeypatch, simt, nh, nkv, hd, T):
         assert rel_l2(out[b], ref) <= TOL, b
 
 
+@pytest.mark.parametrize("vmag", [1e-7, 1.0, 3e3, 1e6], ids=["v1e-7", "v1", "v3e3", "v1e6"])
+@pytest.mark.parametrize("nh,nkv,hd", [(14, 2, 64), (8, 2, 128)])
+def test_decode_value_range(pkg, ctx, orc, nh, nkv, hd, vmag):
+    """V rows whose INT8 scales are tiny or far above 16 (p * v_scale then leaves f16's range unless the kernel
+    rescales its P operand), and rows of one sequence spanning four orders of magnitude, through the tensor-core
+    kernel against the restatement's INT8 attention on the same codes."""
+    rng = np.random.default_rng(int(hd + nh + np.log10(vmag) * 7 + 100))
+    B, T = 2, 900
+    kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, pkg.INT8)
+    pos = np.array([T - 1, T // 3], np.int32)
+    codes = []
+    for b in range(B):
+        k = (rng.standard_normal((T, nkv * hd)) * rng.uniform(0.2, 4, (T, 1))).astype(np.float32)
+        v = (rng.standard_normal((T, nkv * hd)) * vmag * 10.0 ** rng.uniform(-2, 2, (T, 1))).astype(np.float32)
+        kv.upload(0, b, 0, k, v)
+        codes.append(kv.download_int8(0, b, 0, T))
+    q = rng.standard_normal((B, nh * hd)).astype(np.float32)
+    scale = 1.0 / np.sqrt(hd)
+    out = kv.attend_decode(0, q, pos, nh, scale)
+    assert np.isfinite(out).all()
+    for b in range(B):
+        kc, vc, ks, vs = codes[b]
+        ref = orc.attend_decode_i8(q[b], kc, ks, vc, vs, int(pos[b]), nh, nkv, hd, scale)
+        assert rel_l2(out[b], ref) <= TOL, b
+
+
 def test_int8_rejections(pkg, ctx):
     """INT8 caches: head_dim 64/128/256 only; no Qwen3.5 prep over them (its cache is fp32); the raw download
     needs an INT8 cache."""
