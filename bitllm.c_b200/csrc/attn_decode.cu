@@ -34,8 +34,8 @@ __global__ void __launch_bounds__(kDecodeThreads) attn_decode_simt_kernel(
     int max_seq, int max_len, int Hkv, int chunk, int nchunk, float scale, float *__restrict__ part_o,
     float2 *__restrict__ part_ml, unsigned *__restrict__ dev_err, const float *__restrict__ k_scale,
     const float *__restrict__ v_scale, int sstride, const int *__restrict__ row_seq) {
-    griddep_launch_dependents();  // the chunk combine may launch now and wait for this grid's results
     griddep_wait();  // launched as a programmatic dependent: wait for the previous kernels' writes
+    griddep_launch_dependents();  // after the wait: a dependent that starts early finds every earlier grid complete
     constexpr int DL = D / 32;  // head-dim elements per lane in P.V
     static_assert(D % 32 == 0 && (DL == 2 || DL == 4 || DL == 8), "head_dim 64/128/256");
     constexpr bool kI8 = sizeof(KT) == 1;  // INT8 cache: codes, one K and one V scale per (row, kv head)

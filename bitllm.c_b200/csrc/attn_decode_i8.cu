@@ -212,8 +212,8 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
         fence_barrier_init();
     }
     __syncthreads();
-    griddep_launch_dependents();  // the chunk combine may launch now and wait for this grid's results
     griddep_wait();  // launched as a programmatic dependent: wait for the previous kernels' writes
+    griddep_launch_dependents();  // after the wait: a dependent that starts early finds every earlier grid complete
 
     if (warp == NW) {
         // ------------------------------------------------------------------ producer

@@ -1141,11 +1141,17 @@ static eif_status_t core_run(eif_cuda_ctx_t *ctx, eif_cuda_delta_t *st, int laye
     const float *w = st->weights[layer];
     DeltaCoreArgs a{st->S[layer], st->conv[layer], qkv, z, b_raw, a_raw, w, w + ncw, w + ncw + st->H,
                     w + ncw + 2 * st->H, out, st->batch, st->H, st->dk, st->dv, st->conv_k, ctx->dev_err};
+    // every library kernel launched as a programmatic dependent triggers its own dependents only after its
+    // grid-dependency wait, so when this kernel starts early only the launch just before it can still be running:
+    // the state may be read ahead of the wait unless that launch wrote it
+    a.prefetch = !(ctx->last_state == st->S[layer] && ctx->last_state_launches == ctx->launches);
     bool ok = true;
     cudaError_t e = launch_deltanet_core(ctx->stream, a, &ok);
     if (!ok) return fail(ctx, EIF_STATUS_NOT_SUPPORTED, "deltanet_core: d_k %d / d_v %d not supported", st->dk, st->dv);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "deltanet_core launch");
     ctx->launches += 1;
+    ctx->last_state = st->S[layer];
+    ctx->last_state_launches = ctx->launches;
     return EIF_STATUS_OK;
 }
 

@@ -45,6 +45,11 @@ struct eif_cuda_ctx {
     unsigned *host_err = nullptr;
     // pinned host staging of small host-pointer calls: [inputs, packed | error word + output]
     void *pin = nullptr;
+    // the DeltaNet state written by the most recent deltanet_core launch, and `launches` right after it: the next
+    // deltanet_core may read its own state before its grid-dependency wait unless it is that state and no other
+    // launch came in between
+    const void *last_state = nullptr;
+    uint64_t last_state_launches = 0;
 };
 
 // Host-pointer calls whose inputs (together) and output are at most this many bytes go through the pinned
@@ -124,6 +129,7 @@ struct DeltaCoreArgs {
     int B, H, dk, dv, conv_k;
     unsigned *dev_err;
     int stage_inputs;  // set by launch_deltanet_core: the conv windows, weights, inputs, z and norm_w come by bulk copies
+    int prefetch;      // the kernel launched just before this one on the stream does not write this layer's state
 };
 cudaError_t launch_deltanet_core(cudaStream_t st, const DeltaCoreArgs &a, bool *supported);
 

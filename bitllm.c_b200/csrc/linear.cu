@@ -210,8 +210,8 @@ __global__ void __launch_bounds__(kThreads, T == 1 ? 3 : 1) linear_kernel(const 
     float *red = xs + tile_floats(WT, a.n_words, T);  // [kWarps][K] the slices' sums
     uint32_t raw[kUnroll][kRows];
     if (n_items > 0) load(0, raw);  // the weights do not depend on the previous kernel: fetch before waiting
-    griddep_launch_dependents();
     griddep_wait();  // x is the previous kernel's output
+    griddep_launch_dependents();  // after the wait: a dependent that starts early finds every earlier grid complete
     if constexpr (WT == EIF_CUDA_W_TERNARY_DENSE) {
         for (int b = threadIdx.x; b < 256; b += kThreads) {
             uint32_t e = 0, v = b;

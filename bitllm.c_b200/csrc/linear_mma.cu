@@ -152,8 +152,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_mma_kernel(const MmaArgs a
     };
 #pragma unroll
     for (int j = 0; j < kStages - 1; ++j) issue(j);  // weights do not depend on the previous kernel
-    griddep_launch_dependents();
     griddep_wait();  // x is the previous kernel's output
+    griddep_launch_dependents();  // after the wait: a dependent that starts early finds every earlier grid complete
 
     uint32_t *tmax = reinterpret_cast<uint32_t *>(red);  // per-token largest |x| (bits), before the sums use red
     const int n_cols = a.n_blocks * 4 * CPL;  // columns of the padded rows (those past `cols` stage as zeros)

@@ -38,8 +38,15 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
     constexpr int NP = DK / RP;        // passes
     constexpr int NW = THREADS / 32;
     static_assert(LPR <= 32 && 32 % LPR == 0 && DK % RP == 0, "tile shape");
-    griddep_launch_dependents();
-    griddep_wait();  // launched as a programmatic dependent: the previous kernels' writes (S included) are visible
+    // launched as a programmatic dependent.  prefetch (set by the host when the kernel launched just before this one
+    // on the stream does not write this layer's state): the state (S, conv windows) and the layer's weights are
+    // read before griddepcontrol.wait -- every grid before that kernel has completed, since each of the library's
+    // grids triggers its dependents only after its own wait -- and only the inputs after it
+    const bool pre = a.prefetch != 0;
+    if (!pre) {
+        griddep_wait();
+        griddep_launch_dependents();  // after the wait: a dependent that starts early finds every earlier grid complete
+    }
     const int h = blockIdx.x, b = blockIdx.y;
     const int H = a.H;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -79,7 +86,6 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
         for (uint32_t off = 0; off < bytes; off += piece)
             bulk_load(smem_u32(Ssm) + off, reinterpret_cast<const char *>(Sh) + off, piece, sbar);
         if (staged) {
-            bulk_load(smem_u32(zn), a.z + bh * DV, DV * 4, sbar);
             bulk_load(smem_u32(zn + DV), a.norm_w, DV * 4, sbar);
 #pragma unroll
             for (int blk = 0; blk < 3; ++blk) {  // local channels [i0, i0 + n) = global channels [c0, c0 + n)
@@ -87,13 +93,25 @@ __global__ void __launch_bounds__(THREADS, 4) deltanet_core_kernel(const DeltaCo
                 const int c0 = blk == 0 ? h * DK : (blk == 1 ? key_dim + h * DK : 2 * key_dim + h * DV);
                 bulk_load(smem_u32(stg + i0 * ck), a.conv + ((size_t)b * conv_dim + c0) * ck, n * ck * 4, sbar);
                 bulk_load(smem_u32(stg + (NC + i0) * ck), a.conv_w + (size_t)c0 * ck, n * ck * 4, sbar);
-                bulk_load(smem_u32(stg + 2 * NC * ck + i0), a.qkv + (size_t)b * conv_dim + c0, n * 4, sbar);
             }
         }
     }
     float4 sreg[NH];
 #pragma unroll
     for (int u = 0; u < NH; ++u) sreg[u] = Srow[(rg + (NH + u) * RP) * (DV / 4)];
+    if (pre) {
+        griddep_wait();  // the inputs (qkv, z, the gates' inputs) may be the previous kernel's output
+        griddep_launch_dependents();
+    }
+    if (tid == 0 && staged) {  // the inputs, on the same barrier
+        bulk_load(smem_u32(zn), a.z + bh * DV, DV * 4, sbar);
+#pragma unroll
+        for (int blk = 0; blk < 3; ++blk) {
+            const int i0 = blk * DK, n = blk < 2 ? DK : DV;
+            const int c0 = blk == 0 ? h * DK : (blk == 1 ? key_dim + h * DK : 2 * key_dim + h * DV);
+            bulk_load(smem_u32(stg + 2 * NC * ck + i0), a.qkv + (size_t)b * conv_dim + c0, n * 4, sbar);
+        }
+    }
     // the gates' inputs, loaded now so that their latency overlaps the conv
     float braw = 0.f, araw = 0.f, dtb = 0.f, aex = 0.f;
     if (tid == 0) {
@@ -337,8 +355,8 @@ __global__ void __launch_bounds__(256) fullatt_prep_warp_kernel(const AttnPrepAr
     const int hd = a.hd, nh = a.nh, nkv = a.nkv, half = a.n_rot / 2;
     const int per_row = nh + nkv + 1;
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    griddep_launch_dependents();
     griddep_wait();  // launched as a programmatic dependent: wait for the previous kernels' writes
+    griddep_launch_dependents();  // after the wait: a dependent that starts early finds every earlier grid complete
     if (gw >= a.B * a.n_tok * per_row) return;  // warp-uniform; the kernel has no block barrier
     const int r = gw / per_row, hh = gw % per_row, b = r / a.n_tok;
     const int p = a.pos ? a.pos[b] : a.start_pos + r % a.n_tok;
