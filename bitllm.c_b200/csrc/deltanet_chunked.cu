@@ -79,7 +79,7 @@ constexpr int kSolveSmem = SOL_BAR + 16 + 1024;  // ~35 KB: six CTAs per SM
 
 // Outputs per (sequence, head, chunk): Tout [128][64] bf16 = T diag(-b e^G) ; T diag(b) (the A operands
 // of W and U' in the state kernel, with the minus sign of U = U' - W S folded in) and Gout [64] fp32 = G.
-__global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid_constant__ CUtensorMap tmK,
+__global__ void __launch_bounds__(kSolveThreads, 5) chunk_solve_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                     const float *__restrict__ beta,
                                                                     const float *__restrict__ g,
                                                                     __nv_bfloat16 *__restrict__ Tout,
@@ -157,14 +157,20 @@ __global__ void __launch_bounds__(kSolveThreads) chunk_solve_kernel(const __grid
         for (int r = 0; r < C - 1; ++r) {
             if (r < r0) continue;  // warp-uniform
             const float t = u[r];
+            const unsigned long long nt2 = f2_pack(-t, -t);
             const float *arow = Af + r * FP;  // A^T row r: A_ir for i = 0 .. 63
 #pragma unroll
             for (int g = (r + 1) / 4; g < C / 4; ++g) {
                 const float4 a4 = *reinterpret_cast<const float4 *>(arow + 4 * g);
-                if (4 * g > r) u[4 * g] = fmaf(-a4.x, t, u[4 * g]);
-                if (4 * g + 1 > r) u[4 * g + 1] = fmaf(-a4.y, t, u[4 * g + 1]);
-                if (4 * g + 2 > r) u[4 * g + 2] = fmaf(-a4.z, t, u[4 * g + 2]);
-                u[4 * g + 3] = fmaf(-a4.w, t, u[4 * g + 3]);
+                if (4 * g > r) {  // a whole group: two packed FMAs (fma.rn.f32x2, the same rounding as fmaf)
+                    f2_unpack(ffma2(f2_pack(a4.x, a4.y), nt2, f2_pack(u[4 * g], u[4 * g + 1])), u[4 * g], u[4 * g + 1]);
+                    f2_unpack(ffma2(f2_pack(a4.z, a4.w), nt2, f2_pack(u[4 * g + 2], u[4 * g + 3])), u[4 * g + 2],
+                              u[4 * g + 3]);
+                } else {
+                    if (4 * g + 1 > r) u[4 * g + 1] = fmaf(a4.y, -t, u[4 * g + 1]);
+                    if (4 * g + 2 > r) u[4 * g + 2] = fmaf(a4.z, -t, u[4 * g + 2]);
+                    u[4 * g + 3] = fmaf(a4.w, -t, u[4 * g + 3]);
+                }
             }
         }
 #pragma unroll
