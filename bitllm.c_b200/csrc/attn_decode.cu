@@ -211,9 +211,10 @@ __global__ void __launch_bounds__(256) attn_decode_combine_kernel(
     }
     __syncthreads();
 
-    // weighted sum over the chunks, kCombineRun row elements per thread at once (their loads of a chunk are
-    // independent, so they are in flight together)
-    constexpr int kCombineRun = 8;
+    // weighted sum over the chunks, kCombineRun row elements per thread at once and kChunkRun chunks of them
+    // loaded before they are added (in chunk order): 32 independent loads in flight, so a split into many
+    // chunks (small batches) is not a chain of round trips to L2
+    constexpr int kCombineRun = 8, kChunkRun = 4;
     float ss = 0.f;
     for (int i0 = threadIdx.x; i0 < row; i0 += kCombineRun * blockDim.x) {
         const float *po[kCombineRun];
@@ -228,7 +229,19 @@ __global__ void __launch_bounds__(256) attn_decode_combine_kernel(
             wh[k] = w + h * nchunk;
             o[k] = 0.f;
         }
-        for (int c = 0; c < nchunk; ++c)
+        int c = 0;
+        for (; c + kChunkRun <= nchunk; c += kChunkRun) {
+            float v[kChunkRun][kCombineRun];
+#pragma unroll
+            for (int u = 0; u < kChunkRun; ++u)
+#pragma unroll
+                for (int k = 0; k < kCombineRun; ++k) v[u][k] = po[k][(size_t)(c + u) * G * D];
+#pragma unroll
+            for (int u = 0; u < kChunkRun; ++u)
+#pragma unroll
+                for (int k = 0; k < kCombineRun; ++k) o[k] += v[u][k] * wh[k][c + u];
+        }
+        for (; c < nchunk; ++c)
 #pragma unroll
             for (int k = 0; k < kCombineRun; ++k) o[k] += po[k][(size_t)c * G * D] * wh[k][c];
 #pragma unroll
