@@ -253,11 +253,12 @@ class Hybrid:
 
 class HybridPipe:
     """End to end with the copies overlapped: every layer's inputs come from pinned host memory (H2D on one copy
-    stream into double-buffered device inputs), every layer's output goes back to pinned host memory (D2H on a
-    second copy stream), and the compute stream runs the layers through the `_dev` entry points
-    (eif_cuda_deltanet_core_dev, eif_cuda_fullatt_decode_dev) as soon as their inputs have landed, so the PCIe
-    transfers of one layer overlap the kernels of its neighbours.  A step ends when its last output is on the
-    host."""
+    stream into that layer's own device input buffers), every layer's output goes back to pinned host memory (D2H
+    on a second copy stream), and the compute stream runs the layers through the `_dev` entry points
+    (eif_cuda_deltanet_core_dev, eif_cuda_fullatt_decode_dev) as soon as their inputs have landed.  One input
+    buffer set per layer (~230 MB at batch 256) lets the copy stream run ahead through a run of short DeltaNet
+    layers, whose 8.4 MB of inputs take longer over PCIe than their 0.12 ms kernels, while an attention layer
+    computes.  A step ends when its last output is on the host."""
 
     def __init__(self, torch, hy: Hybrid, seed):
         self.torch, self.hy = torch, hy
@@ -271,14 +272,14 @@ class HybridPipe:
         self.h_pos = torch.full((B,), CTX - 1, dtype=torch.int32).pin_memory()
         self.h_dn_out = torch.zeros(B, DN_H * DN_D).pin_memory()
         self.h_out = torch.zeros(B, AT_HQ * AT_D).pin_memory()
-        self.d_dn = [{k: torch.empty_like(v, device=dev) for k, v in self.h_dn.items()} for _ in range(2)]
-        self.d_at = [{k: torch.empty_like(v, device=dev) for k, v in self.h_at.items()} for _ in range(2)]
-        self.d_pos = [torch.empty_like(self.h_pos, device=dev) for _ in range(2)]
-        self.d_dn_out = [torch.empty(B, DN_H * DN_D, device=dev) for _ in range(2)]
-        self.d_out = [torch.empty(B, AT_HQ * AT_D, device=dev) for _ in range(2)]
+        n = len(LAYER_TYPES)
+        self.d_in = [{k: torch.empty_like(v, device=dev) for k, v in (self.h_dn if typ == "D" else self.h_at).items()}
+                     for typ in LAYER_TYPES]
+        self.d_pos = [torch.empty_like(self.h_pos, device=dev) if typ == "A" else None for typ in LAYER_TYPES]
+        self.d_out = [torch.empty(B, (DN_H * DN_D) if typ == "D" else (AT_HQ * AT_D), device=dev) for typ in LAYER_TYPES]
         self.cp_in, self.cp_out = torch.cuda.Stream(), torch.cuda.Stream()
         E = torch.cuda.Event
-        self.ev_in, self.ev_done, self.ev_out = [E(), E()], [E(), E()], [E(), E()]
+        self.ev_in, self.ev_done = [E() for _ in range(n)], [E() for _ in range(n)]
         self.h2d = self.d2h = 0
         for typ in LAYER_TYPES:
             if typ == "D":
@@ -291,39 +292,34 @@ class HybridPipe:
     def step(self):
         torch, hy = self.torch, self.hy
         comp = torch.cuda.current_stream()  # the library context's stream
+        # the whole step's inputs, in layer order, on the copy stream (a layer's buffers are its own, and the
+        # previous step ended with everything complete)
+        with torch.cuda.stream(self.cp_in):
+            for i, typ in enumerate(LAYER_TYPES):
+                for k, t in (self.h_dn if typ == "D" else self.h_at).items():
+                    self.d_in[i][k].copy_(t, non_blocking=True)
+                if typ == "A":
+                    self.d_pos[i].copy_(self.h_pos, non_blocking=True)
+                self.ev_in[i].record(self.cp_in)
         a = d = 0
         for i, typ in enumerate(LAYER_TYPES):
-            s = i % 2
-            self.cp_in.wait_event(self.ev_done[s])  # layer i - 2 has finished reading slot s
-            with torch.cuda.stream(self.cp_in):
-                if typ == "D":
-                    for k, t in self.h_dn.items():
-                        self.d_dn[s][k].copy_(t, non_blocking=True)
-                else:
-                    for k, t in self.h_at.items():
-                        self.d_at[s][k].copy_(t, non_blocking=True)
-                    self.d_pos[s].copy_(self.h_pos, non_blocking=True)
-                self.ev_in[s].record(self.cp_in)
-            comp.wait_event(self.ev_in[s])
-            comp.wait_event(self.ev_out[s])  # layer i - 2's output has left slot s
+            comp.wait_event(self.ev_in[i])
+            x = self.d_in[i]
             if typ == "D":
-                x = self.d_dn[s]
                 hy.dn.core_dev(d, x["qkv"].data_ptr(), x["z"].data_ptr(), x["b"].data_ptr(), x["a"].data_ptr(),
-                               self.d_dn_out[s].data_ptr())
+                               self.d_out[i].data_ptr())
                 d += 1
-                out_d, out_h = self.d_dn_out[s], self.h_dn_out
+                out_h = self.h_dn_out
             else:
-                x = self.d_at[s]
                 hy.kv.fullatt_decode_dev(a, x["qg"].data_ptr(), x["k"].data_ptr(), x["v"].data_ptr(),
-                                         self.d_pos[s].data_ptr(), CTX - 1, AT_HQ, hy.scale, self.d_out[s].data_ptr(),
+                                         self.d_pos[i].data_ptr(), CTX - 1, AT_HQ, hy.scale, self.d_out[i].data_ptr(),
                                          subln=hy.pkg.SUBLN_WEIGHT, sub_norm_dev=hy.sub_norm[a].data_ptr())
                 a += 1
-                out_d, out_h = self.d_out[s], self.h_out
-            self.ev_done[s].record(comp)
-            self.cp_out.wait_event(self.ev_done[s])
+                out_h = self.h_out
+            self.ev_done[i].record(comp)
+            self.cp_out.wait_event(self.ev_done[i])
             with torch.cuda.stream(self.cp_out):
-                out_h.copy_(out_d, non_blocking=True)
-                self.ev_out[s].record(self.cp_out)
+                out_h.copy_(self.d_out[i], non_blocking=True)
         self.cp_out.synchronize()  # the step's results are on the host
         comp.synchronize()
 
