@@ -203,7 +203,8 @@ eif_status_t eif_cuda_attend_decode(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int 
 /* Device-pointer variant; max_pos is an upper bound of pos_dev[] (used to size the split over the KV
  * length: rows beyond a sequence's own pos are never read).  A pos_dev[b] above max_pos (or outside the
  * cache) is not computed: that sequence's output is zeros and the next synchronising call returns
- * EIF_STATUS_INVALID_ARGUMENT. */
+ * EIF_STATUS_INVALID_ARGUMENT.  The TMA-fed kernels bulk-copy each item's query rows, so they need q_dev
+ * 16-byte aligned; an unaligned q_dev runs the (slower) SIMT kernel with the same results. */
 eif_status_t eif_cuda_attend_decode_dev(eif_cuda_ctx_t *ctx, eif_cuda_kv_t *kv, int layer, const float *q_dev,
                                         const int *pos_dev, int max_pos, int n_heads, float scale,
                                         const float *gate_dev, eif_cuda_subln_t subln, const float *sub_norm_dev,
