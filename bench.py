@@ -260,6 +260,8 @@ class HybridPipe:
     layers, whose 8.4 MB of inputs take longer over PCIe than their 0.12 ms kernels, while an attention layer
     computes.  A step ends when its last output is on the host."""
 
+    LOOKAHEAD = 6  # layers whose input copies are issued ahead of the current kernel (more than a D-D-D-A run)
+
     def __init__(self, torch, hy: Hybrid, seed):
         self.torch, self.hy = torch, hy
         B, dev = hy.B, torch.device("cuda", torch.cuda.current_device())
@@ -292,17 +294,24 @@ class HybridPipe:
     def step(self):
         torch, hy = self.torch, self.hy
         comp = torch.cuda.current_stream()  # the library context's stream
-        # the whole step's inputs, in layer order, on the copy stream (a layer's buffers are its own, and the
-        # previous step ended with everything complete)
-        with torch.cuda.stream(self.cp_in):
-            for i, typ in enumerate(LAYER_TYPES):
-                for k, t in (self.h_dn if typ == "D" else self.h_at).items():
+        # the inputs, in layer order on the copy stream, issued LOOKAHEAD layers ahead of the kernels (a layer's
+        # buffers are its own, and the previous step ended with everything complete), so the first kernels do not
+        # wait for the host to issue every copy of the step
+        n = len(LAYER_TYPES)
+
+        def copy_in(i):
+            with torch.cuda.stream(self.cp_in):
+                for k, t in (self.h_dn if LAYER_TYPES[i] == "D" else self.h_at).items():
                     self.d_in[i][k].copy_(t, non_blocking=True)
-                if typ == "A":
+                if LAYER_TYPES[i] == "A":
                     self.d_pos[i].copy_(self.h_pos, non_blocking=True)
                 self.ev_in[i].record(self.cp_in)
+        for i in range(min(self.LOOKAHEAD, n)):
+            copy_in(i)
         a = d = 0
         for i, typ in enumerate(LAYER_TYPES):
+            if i + self.LOOKAHEAD < n:
+                copy_in(i + self.LOOKAHEAD)
             comp.wait_event(self.ev_in[i])
             x = self.d_in[i]
             if typ == "D":
