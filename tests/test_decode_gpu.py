@@ -262,3 +262,31 @@ def test_many_items_per_cta(pkg, ctx, orc, dtype, hd, nh, nkv):
                 k, v = orc.round_bf16(k).reshape(k.shape), orc.round_bf16(v).reshape(v.shape)
             ref = orc.attend_decode(q[b], k, v, int(pos[b]), nh, nkv, hd, scale)
         assert rel_l2(out[b], ref) <= TOL, (b, int(pos[b]))
+
+
+@pytest.mark.parametrize("dtype", ["F32", "BF16", "INT8"])
+def test_device_q_unaligned(pkg, ctx, dtype):
+    """A q_dev that is 4- but not 16-byte aligned (a view one float into a buffer): the TMA-fed kernels bulk-copy
+    each item's query rows and need 16-byte alignment, so such a call runs the SIMT kernel, with the results of
+    the aligned (host-pointer) call."""
+    import torch
+    B, nh, nkv, hd, T = 3, 8, 2, 128, 300
+    rng = np.random.default_rng(91)
+    kv = pkg.KVCache(ctx, 1, B, T, nkv, hd, getattr(pkg, dtype))
+    for b in range(B):
+        kv.upload(0, b, 0, rng.standard_normal((T, nkv * hd)).astype(np.float32),
+                  rng.standard_normal((T, nkv * hd)).astype(np.float32))
+    q = rng.standard_normal((B, nh * hd)).astype(np.float32)
+    pos = np.array([T - 1, T // 2, 7], np.int32)
+    scale = 1.0 / np.sqrt(hd)
+    ref = kv.attend_decode(0, q, pos, nh, scale)
+    buf = torch.zeros(B * nh * hd + 1, device="cuda")
+    qd = buf[1:].view(B, nh * hd)
+    qd.copy_(torch.from_numpy(q))
+    assert qd.data_ptr() % 16 == 4
+    posd = torch.from_numpy(pos).cuda()
+    out = torch.zeros((B, nh * hd), device="cuda")
+    torch.cuda.synchronize()
+    kv.attend_decode_dev(0, qd.data_ptr(), posd.data_ptr(), T - 1, nh, scale, out.data_ptr())
+    ctx.synchronize()
+    assert rel_l2(out.cpu().numpy(), ref) <= TOL
