@@ -345,3 +345,52 @@ def test_deltanet_core_host_matches_dev(pkg, ctx):
         ctx.synchronize()
         assert np.array_equal(out_host, out_dev.cpu().numpy()), t
     assert torch.equal(views[0][0], views[1][0]) and torch.equal(views[0][1], views[1][1])
+
+
+def test_deltanet_core_back_to_back_launches(pkg, ctx):
+    """deltanet_core launches as a programmatic dependent and, when the launch just before it wrote another
+    layer's state, reads its own state before its grid-dependency wait.  A run of device-pointer calls with
+    nothing between them (the same layer twice in a row, then alternating layers) must leave the same bits as
+    the same calls with a synchronisation after each, where no launch can overlap another."""
+    import torch
+
+    class CudaArray:
+        def __init__(self, ptr, shape, typestr):
+            self.__cuda_array_interface__ = {"data": (ptr, False), "shape": shape, "typestr": typestr, "version": 3}
+    rng = np.random.default_rng(97)
+    B, H, d, ck = 24, 16, 128, 4
+    conv_dim = 3 * H * d
+    order = [0, 0, 1, 0, 1, 1, 0, 1]
+    sts = [pkg.DeltaState(ctx, 2, B, H, d, d, ck) for _ in range(2)]
+    views = []
+    # the same weights for both twins
+    wts = [dict(conv_w=(0.5 * rng.standard_normal((conv_dim, ck))).astype(np.float32),
+                dt_bias=rng.standard_normal(H).astype(np.float32),
+                A_log=(0.5 * rng.standard_normal(H)).astype(np.float32),
+                norm_w=(1 + 0.1 * rng.standard_normal(d)).astype(np.float32)) for _ in range(2)]
+    for st in sts:
+        for layer in range(2):
+            st.set_weights(layer, **wts[layer])
+            s_ptr, c_ptr = st.layer_ptrs(layer)
+            views.append((torch.as_tensor(CudaArray(s_ptr, (B * H * d * d,), "<f4"), device="cuda"),
+                          torch.as_tensor(CudaArray(c_ptr, (B * conv_dim * ck,), "<f4"), device="cuda")))
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    for layer in range(2):  # views: [twin 0 layer 0, twin 0 layer 1, twin 1 layer 0, twin 1 layer 1]
+        views[layer][0].normal_(0, 0.02, generator=gen)
+        views[layer][1].normal_(generator=gen)
+        views[2 + layer][0].copy_(views[layer][0])
+        views[2 + layer][1].copy_(views[layer][1])
+    ins = [[torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).cuda()
+            for shape in ((B, conv_dim), (B, H * d), (B, H), (B, H))] for _ in order]
+    outs = [[torch.zeros((B, H * d), device="cuda") for _ in order] for _ in range(2)]
+    torch.cuda.synchronize()
+    for k, layer in enumerate(order):  # twin 0: back to back
+        sts[0].core_dev(layer, *(x.data_ptr() for x in ins[k]), outs[0][k].data_ptr())
+    ctx.synchronize()
+    for k, layer in enumerate(order):  # twin 1: one call at a time
+        sts[1].core_dev(layer, *(x.data_ptr() for x in ins[k]), outs[1][k].data_ptr())
+        ctx.synchronize()
+    for k in range(len(order)):
+        assert torch.equal(outs[0][k], outs[1][k]), k
+    for layer in range(2):
+        assert torch.equal(views[layer][0], views[2 + layer][0]) and torch.equal(views[layer][1], views[2 + layer][1])
