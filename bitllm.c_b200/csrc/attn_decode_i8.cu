@@ -11,9 +11,10 @@
 //           64 keys x 64 bytes with the 64-byte swizzle at head_dim 64; no multicast) and copies
 //           the tile's 64 K and 64 V scales (aligned 256-byte runs of the head-major scale rows) into the
 //           same stage with bulk asynchronous copies on the same "full" mbarrier;
-//   warps 0 .. 4NG-1 consumers in NG groups of 4 that take tiles round-robin, so NG tiles are in flight
-//           per SM: NG = 4 at head_dim 64, 2 at 128, 1 at 256, as many as the registers allow; within a
-//           group each warp takes 16 keys of the tile:
+//   warps 0 .. NW-1 consumers in NG groups of KG = 64 / KPW warps that take tiles round-robin: at head_dim 64
+//           eight groups of two, each warp 32 keys of a tile (two 16-key halves, independent work for the
+//           scheduler); at 128 two groups and at 256 one group of four, 16 keys a warp (as the registers
+//           allow).  Per 16 keys:
 //     S = Q K^T   in exact integer arithmetic (mma.m16n8k32 on 8-bit operands, int32 accumulators): the
 //                 query of each head, scaled by a power of two so that its largest |q| lies in [2^21, 2^22),
 //                 is rounded to integers and split into bytes q = hi * 2^16 + mid * 2^8 + lo; one u8 x s8
@@ -41,7 +42,6 @@
 namespace {
 
 constexpr int KT = 64;          // keys per tile
-constexpr int kGroup = 4;       // consumer warps per group, 16 keys of a tile each
 constexpr int kSmemLimit = 227 * 1024;
 constexpr int HS = 8;           // head slots: MMA rows g (high part) and g + 8 (low part)
 
@@ -50,9 +50,10 @@ constexpr int HS = 8;           // head slots: MMA rows g (high part) and g + 8 
 // cache row in one stage, so a tile streams whole rows (a stage of one head's 64-byte halves leaves the other
 // halves of the same DRAM pages to another CTA later, which caps the stream near 0.57 of the copy peak); the
 // consumer groups then split by head.
-template <int D, int NG, int KH>
+template <int D, int NG, int KH, int KPW>
 struct I8Cfg {
-    static constexpr int NW = kGroup * NG;            // consumer warps
+    static constexpr int KG = KT / KPW;               // consumer warps per group: KPW keys of a tile each
+    static constexpr int NW = KG * NG;                // consumer warps
     static constexpr int TG = NG / KH;                // tiles in flight (consumer groups per tile: KH)
     static constexpr int THREADS = 32 * (NW + 1);
     static constexpr int BW = D >= 128 ? 128 : 64;    // box width in code bytes (= dims); the swizzle span
@@ -177,11 +178,12 @@ __device__ __forceinline__ uint32_t tile_addr(uint32_t base, int key, int chunk)
         return base + (chunk >> 2) * 4096 + key * 64 + (((chunk & 3) ^ ((key >> 1) & 3)) << 4);
 }
 
-template <int D, int NG, int KH>
-__global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
+template <int D, int NG, int KH, int KPW>
+__global__ void __launch_bounds__(I8Cfg<D, NG, KH, KPW>::THREADS, 1)
     attn_decode_i8_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                           const I8Params p) {
-    using C = I8Cfg<D, NG, KH>;
+    using C = I8Cfg<D, NG, KH, KPW>;
+    constexpr int kGroup = C::KG, NH = KPW / 16;  // warps per group; 16-key halves a warp takes per tile
     constexpr int TG = C::TG;
     constexpr int NS = C::NS, KS = D / 16, NT = D / 8, NW = C::NW;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -261,7 +263,7 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
     // ---------------------------------------------------------------------- consumers
     const int g = lane >> 2, t = lane & 3;
     const int mi = lane >> 3, mr = lane & 7;               // ldmatrix: matrix / row this lane addresses
-    const int grp = warp / kGroup, wk = (warp % kGroup) * 16;  // group; first tile row of this warp's keys
+    const int grp = warp / kGroup, wk = (warp % kGroup) * KPW;  // group; first tile row of this warp's keys
     const int tg = grp / KH, hh = grp - tg * KH;                 // the group's tile slot and head within the stage
     const int my_key = wk + (mi & 1) * 8 + mr;             // tile row (key) of this lane's ldmatrix rows
     uint32_t it_base = 0, item_no = 0;
@@ -327,52 +329,55 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
             const float *scs = sbuf + (s * KH + hh) * 2 * KT + wk;  // this warp's keys: K scales, V scales at +64
             const uint32_t kbase = smem_u32(smem + s * C::STAGE) + hh * C::TILE, vbase = kbase + KH * C::TILE;
 
-            // ---- S = Q K^T in integers: n-tiles of keys 0-7 and 8-15 of the warp; the K codes from ldmatrix
-            //      are the B fragments as they are (key g, dims 4t .. 4t+3 of a 16-dim chunk).  A u8 MMA takes
-            //      mid (rows g) and lo (rows g + 8), an s8 MMA hi (rows g); sums of 256 products stay in int32
-            int aml[2][4], ah[2][4];
-#pragma unroll
-            for (int n = 0; n < 2; ++n) aml[n][0] = aml[n][1] = aml[n][2] = aml[n][3] = ah[n][0] = ah[n][1] = ah[n][2] = ah[n][3] = 0;
-#pragma unroll
-            for (int kp = 0; kp < KS / 2; ++kp) {
-                uint32_t r0, r1, r2, r3;  // (keys 0-7 | 8-15) x (chunk 2kp | 2kp+1)
-                ldsm_x4(tile_addr<C::BW>(kbase, my_key, 2 * kp + (mi >> 1)), r0, r1, r2, r3);
-                const int c0 = 2 * kp, c1 = 2 * kp + 1;
-                mma_u8s8_16832(aml[0], qmid[c0], qlo[c0], qmid[c1], qlo[c1], r0, r2);
-                mma_u8s8_16832(aml[1], qmid[c0], qlo[c0], qmid[c1], qlo[c1], r1, r3);
-                mma_s8s8_16832(ah[0], qhi[c0], 0u, qhi[c1], 0u, r0, r2);
-                mma_s8s8_16832(ah[1], qhi[c0], 0u, qhi[c1], 0u, r1, r3);
-            }
-
-            // ---- online softmax (base 2) for head g over keys 2t, 2t+1, 8+2t, 9+2t; the score of a key is
-            //      hi * 2^16 + (mid * 2^8 + lo) (the bracket exact in int32), rounded once in the FMA
-            const int kk[4] = {2 * t, 2 * t + 1, 8 + 2 * t, 9 + 2 * t};
-            float sv[4], vsc[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int n = e >> 1, j = e & 1;
-                sv[e] = fmaf((float)ah[n][j], 65536.f, (float)(aml[n][j] * 256 + aml[n][2 + j]));
-            }
+            // ---- S = Q K^T in integers, per 16-key half h: n-tiles of keys 0-7 and 8-15 of the half; the K codes
+            //      from ldmatrix are the B fragments as they are (key g, dims 4t .. 4t+3 of a 16-dim chunk).  A u8
+            //      MMA takes mid (rows g) and lo (rows g + 8), an s8 MMA hi (rows g); sums of 256 products stay in
+            //      int32.  A half's sums become scores before the next half starts (fewer live registers).
+            //      Online softmax (base 2) for head g over keys 16h + (2t, 2t+1, 8+2t, 9+2t); the score of a key
+            //      is hi * 2^16 + (mid * 2^8 + lo) (the bracket exact in int32), rounded once in the FMA.
+            float sv[4 * NH], vsc[4 * NH];
             float mx = -INFINITY;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {  // keys past t_end: masked (their scale slots hold stale values)
-                const bool ok = kk[e] < nvalid;
-                vsc[e] = ok ? scs[KT + kk[e]] : 0.f;
-                sv[e] = ok ? (sv[e] * qdiv) * scs[kk[e]] : -INFINITY;
-                mx = fmaxf(mx, sv[e]);
+            for (int hf = 0; hf < NH; ++hf) {
+                int aml[2][4], ah[2][4];
+#pragma unroll
+                for (int n = 0; n < 2; ++n)
+                    aml[n][0] = aml[n][1] = aml[n][2] = aml[n][3] = ah[n][0] = ah[n][1] = ah[n][2] = ah[n][3] = 0;
+#pragma unroll
+                for (int kp = 0; kp < KS / 2; ++kp) {
+                    uint32_t r0, r1, r2, r3;  // (keys 0-7 | 8-15 of the half) x (chunk 2kp | 2kp+1)
+                    ldsm_x4(tile_addr<C::BW>(kbase, my_key + 16 * hf, 2 * kp + (mi >> 1)), r0, r1, r2, r3);
+                    const int c0 = 2 * kp, c1 = 2 * kp + 1;
+                    mma_u8s8_16832(aml[0], qmid[c0], qlo[c0], qmid[c1], qlo[c1], r0, r2);
+                    mma_u8s8_16832(aml[1], qmid[c0], qlo[c0], qmid[c1], qlo[c1], r1, r3);
+                    mma_s8s8_16832(ah[0], qhi[c0], 0u, qhi[c1], 0u, r0, r2);
+                    mma_s8s8_16832(ah[1], qhi[c0], 0u, qhi[c1], 0u, r1, r3);
+                }
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {  // keys past t_end: masked (their scale slots hold stale values)
+                    const int e = 4 * hf + q4, n = q4 >> 1, j = q4 & 1;
+                    const int kk = 16 * hf + 8 * n + 2 * t + j;
+                    const bool ok = kk < nvalid;
+                    const float raw = fmaf((float)ah[n][j], 65536.f, (float)(aml[n][j] * 256 + aml[n][2 + j]));
+                    vsc[e] = ok ? scs[KT + kk] : 0.f;
+                    sv[e] = ok ? (raw * qdiv) * scs[kk] : -INFINITY;
+                    mx = fmaxf(mx, sv[e]);
+                }
             }
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
             // this lane's largest V scale: p <= 1, so p * v_scale * pmul stays below 2^14 (f16 parts finite) while
             // vmx * pmul < 2^14; checked in the rescale vote below
-            const float vmx = fmaxf(fmaxf(vsc[0], vsc[1]), fmaxf(vsc[2], vsc[3]));
+            float vmx = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4 * NH; ++e) vmx = fmaxf(vmx, vsc[e]);
             const bool need = vmx * pmul >= 16384.f || (pmul == 0.f && vmx > 0.f);
             const float m_new = fmaxf(m_run, mx);
             const float m_use = m_new == -INFINITY ? 0.f : m_new;
             const float corr = fast_exp2(m_run - m_use);
-            float pe[4], psum = 0.f;
+            float pe[4 * NH], psum = 0.f;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
+            for (int e = 0; e < 4 * NH; ++e) {
                 pe[e] = fast_exp2(sv[e] - m_use);
                 psum += pe[e];
             }
@@ -380,7 +385,7 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
             m_run = m_new;
             if (__any_sync(0xffffffffu, corr != 1.f || need)) {  // a new running max, or a new P scale
                 float ocorr = corr;
-                if (__any_sync(0xffffffffu, need)) {  // rare: the warp's 16 keys (lanes t) agree on pmul
+                if (__any_sync(0xffffffffu, need)) {  // rare: the warp's keys (lanes t) agree on pmul
                     float w = vmx;
                     w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, 1));
                     w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, 2));
@@ -400,27 +405,28 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
                     oacc[n][3] *= ocorr;
                 }
             }
-            float pv[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) pv[e] = pe[e] * vsc[e] * pmul;
-            uint32_t pa0, pa1, pa2, pa3;  // rows g (hi) / g+8 (lo); k slots = keys (2t, 2t+1) and (8+2t, 9+2t)
-            split_f16x2(pv[0], pv[1], pa0, pa1);
-            split_f16x2(pv[2], pv[3], pa2, pa3);
 
-            // ---- O += P V: ldmatrix.trans of (keys 0-7 | 8-15) x (chunk 2cp | 2cp+1); even / odd dims of a
+            // ---- O += P V per half: rows g (hi) / g+8 (lo) of P, k slots = the half's keys (2t, 2t+1) and
+            //      (8+2t, 9+2t); ldmatrix.trans of (keys 0-7 | 8-15) x (chunk 2cp | 2cp+1); even / odd dims of a
             //      chunk are n-tiles 2c and 2c+1
 #pragma unroll
-            for (int cp = 0; cp < D / 32; ++cp) {
-                uint32_t r0, r1, r2, r3;
-                ldsm_x4_t(tile_addr<C::BW>(vbase, my_key, 2 * cp + (mi >> 1)), r0, r1, r2, r3);
-                r0 ^= 0x80808080u;
-                r1 ^= 0x80808080u;
-                r2 ^= 0x80808080u;
-                r3 ^= 0x80808080u;
-                mma_f16_16816(oacc[4 * cp + 0], pa0, pa1, pa2, pa3, codes_f16x2(r0, kSelB02), codes_f16x2(r1, kSelB02));
-                mma_f16_16816(oacc[4 * cp + 1], pa0, pa1, pa2, pa3, codes_f16x2(r0, kSelB13), codes_f16x2(r1, kSelB13));
-                mma_f16_16816(oacc[4 * cp + 2], pa0, pa1, pa2, pa3, codes_f16x2(r2, kSelB02), codes_f16x2(r3, kSelB02));
-                mma_f16_16816(oacc[4 * cp + 3], pa0, pa1, pa2, pa3, codes_f16x2(r2, kSelB13), codes_f16x2(r3, kSelB13));
+            for (int hf = 0; hf < NH; ++hf) {
+                uint32_t pa0, pa1, pa2, pa3;
+                split_f16x2(pe[4 * hf] * vsc[4 * hf] * pmul, pe[4 * hf + 1] * vsc[4 * hf + 1] * pmul, pa0, pa1);
+                split_f16x2(pe[4 * hf + 2] * vsc[4 * hf + 2] * pmul, pe[4 * hf + 3] * vsc[4 * hf + 3] * pmul, pa2, pa3);
+#pragma unroll
+                for (int cp = 0; cp < D / 32; ++cp) {
+                    uint32_t r0, r1, r2, r3;
+                    ldsm_x4_t(tile_addr<C::BW>(vbase, my_key + 16 * hf, 2 * cp + (mi >> 1)), r0, r1, r2, r3);
+                    r0 ^= 0x80808080u;
+                    r1 ^= 0x80808080u;
+                    r2 ^= 0x80808080u;
+                    r3 ^= 0x80808080u;
+                    mma_f16_16816(oacc[4 * cp + 0], pa0, pa1, pa2, pa3, codes_f16x2(r0, kSelB02), codes_f16x2(r1, kSelB02));
+                    mma_f16_16816(oacc[4 * cp + 1], pa0, pa1, pa2, pa3, codes_f16x2(r0, kSelB13), codes_f16x2(r1, kSelB13));
+                    mma_f16_16816(oacc[4 * cp + 2], pa0, pa1, pa2, pa3, codes_f16x2(r2, kSelB02), codes_f16x2(r3, kSelB02));
+                    mma_f16_16816(oacc[4 * cp + 3], pa0, pa1, pa2, pa3, codes_f16x2(r2, kSelB13), codes_f16x2(r3, kSelB13));
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(empty0 + 8 * s);
@@ -481,15 +487,15 @@ __global__ void __launch_bounds__(I8Cfg<D, NG, KH>::THREADS, 1)
     }
 }
 
-template <int D, int NG, int KH>
+template <int D, int NG, int KH, int KPW>
 cudaError_t launch_i8_t(cudaStream_t st, const CUtensorMap &tk, const CUtensorMap &tv, I8Params p, int sm_count) {
-    using C = I8Cfg<D, NG, KH>;
+    using C = I8Cfg<D, NG, KH, KPW>;
     cudaError_t e =
-        cudaFuncSetAttribute(attn_decode_i8_kernel<D, NG, KH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        cudaFuncSetAttribute(attn_decode_i8_kernel<D, NG, KH, KPW>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     p.n_items /= KH;  // items of KH kv heads each
     const int grid = p.n_items < sm_count ? p.n_items : sm_count;
-    launch_pdl(attn_decode_i8_kernel<D, NG, KH>, grid, dim3(C::THREADS), C::SMEM, st, tk, tv, p);
+    launch_pdl(attn_decode_i8_kernel<D, NG, KH, KPW>, grid, dim3(C::THREADS), C::SMEM, st, tk, tv, p);
     return cudaGetLastError();
 }
 
@@ -519,10 +525,10 @@ cudaError_t launch_attend_decode_i8(cudaStream_t st, const CUtensorMap &tk, cons
     p.dev_err = a.dev_err;
     switch (a.D) {
         case 64:  // four groups; with an even kv-head count both heads of a 128-byte cache row a stage
-            return decode_i8_heads_per_item(64, p.Hkv) == 2 ? launch_i8_t<64, 4, 2>(st, tk, tv, p, sm_count)
-                                                             : launch_i8_t<64, 4, 1>(st, tk, tv, p, sm_count);
-        case 128: return launch_i8_t<128, 2, 1>(st, tk, tv, p, sm_count);
-        case 256: return launch_i8_t<256, 1, 1>(st, tk, tv, p, sm_count);  // 249 registers: one group
+            return decode_i8_heads_per_item(64, p.Hkv) == 2 ? launch_i8_t<64, 8, 2, 32>(st, tk, tv, p, sm_count)
+                                                             : launch_i8_t<64, 8, 1, 32>(st, tk, tv, p, sm_count);
+        case 128: return launch_i8_t<128, 2, 1, 16>(st, tk, tv, p, sm_count);
+        case 256: return launch_i8_t<256, 1, 1, 16>(st, tk, tv, p, sm_count);  // 249 registers: one group
         default: return cudaErrorInvalidValue;
     }
 }
