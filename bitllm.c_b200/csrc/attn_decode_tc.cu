@@ -117,8 +117,8 @@ __global__ void __launch_bounds__(TcCfg<D, NB, NG>::THREADS, 1)
         fence_barrier_init();
     }
     __syncthreads();
-    griddep_wait();  // launched as a programmatic dependent: wait for the previous kernels' writes
-    griddep_launch_dependents();  // after the wait: a dependent that starts early finds every earlier grid complete
+    griddep_wait();  // a no-op unless launched as a programmatic dependent (these kernels are ordinary launches)
+    griddep_launch_dependents();  // the chunk combine may launch now; it waits for this grid's results
 
     if (warp == C::CW) {
         // ------------------------------------------------------------------ producer
@@ -377,7 +377,7 @@ cudaError_t launch_tc_t(cudaStream_t st, const CUtensorMap &tk, const CUtensorMa
                                          C::SMEM);
     if (e != cudaSuccess) return e;
     const int grid = p.n_items < sm_count ? p.n_items : sm_count;
-    launch_pdl(attn_decode_tc_kernel<D, NB, NG>, grid, dim3(C::THREADS), C::SMEM, st, tk, tv, p);
+    attn_decode_tc_kernel<D, NB, NG><<<grid, C::THREADS, C::SMEM, st>>>(tk, tv, p);  // not a programmatic dependent (see launch_attend_decode)
     return cudaGetLastError();
 }
 
