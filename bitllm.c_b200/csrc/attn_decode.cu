@@ -422,7 +422,7 @@ void decode_plan(const DecodeArgs &a, int sm_count, int *nchunk, int *chunk_keys
 }
 
 // The decode kernels are ordinary launches: as programmatic dependents (starting while the kernel before them
-// drains) the config-5 step measured 0.4 % slower at batch 256 and 1.4 % at batch 32 (A/B on one box).  Their
+// drains) the config-5 step measured 0.4-2.2 % slower at batch 256 and 1.4-2.5 % at batch 32 (A/B on two boxes).  Their
 // griddepcontrol calls are no-ops then.  The chunk combine after them is a programmatic dependent.
 cudaError_t launch_attend_decode(cudaStream_t st, const DecodeArgs &a, void *ws, size_t ws_bytes, int sm_count,
                                  bool *supported, int *n_launches) {
